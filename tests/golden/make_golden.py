@@ -1,0 +1,308 @@
+"""Generate golden vectors by running the reference renderer itself.
+
+This script imports the *reference* ``manbo`` package (TileLang kernels) from
+an installed copy (default ``baseline/_ref``, made with ``pip install --target``
+from the reference checkout) and runs it on a CUDA GPU on seeded inputs from
+``repo_b200.scenes``.  Every stage output of the cubic fill / stroke pipelines,
+the ring-segment conversion and the metric kernels is saved as a compressed
+``.npz`` next to this file.  The fixtures pin the CPU oracle (``oracle/``) and
+the CUDA path to the reference's own outputs; they are committed so that the
+tests never need the reference or TileLang at run time.
+
+It can also time the reference's training step on the 768x512 / 512-path
+configuration (``--time``), which is the GPU baseline of the benchmark.
+
+Usage (on a machine with a GPU and TileLang)::
+
+    python tests/golden/make_golden.py --ref baseline/_ref --out tests/golden
+    python tests/golden/make_golden.py --ref baseline/_ref --time --json out.json
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+import time
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, ROOT)
+
+from repo_b200 import scenes  # noqa: E402
+
+
+def _np(t):
+    if t is None:
+        return None
+    return t.detach().cpu().contiguous().numpy()
+
+
+def _save(out_dir, name, arrays):
+    arrays = {k: v for k, v in arrays.items() if v is not None}
+    path = os.path.join(out_dir, f"{name}.npz")
+    np.savez_compressed(path, **arrays)
+    print(f"wrote {path}: {len(arrays)} arrays", flush=True)
+
+
+def fill_case(cs, tb, scene, grad_seed, dev):
+    """Run every stage of the reference fill pipeline on ``scene``."""
+    h, w, s = scene.height, scene.width, scene.samples
+    cubics_norm = scene.cubics_norm().to(dev)
+    offs = scene.seg_offsets().to(dev)
+    colors = scene.colors.to(dev)
+    opac = scene.opacities.to(dev)
+    depths = scene.depths.to(dev)
+    rules = scene.fill_rules.to(dev)
+    aa = scene.aa_widths.to(dev)
+    bg = scene.background.to(dev)
+    bx = by = 16
+    tile_bounds = ((w + bx - 1) // bx, (h + by - 1) // by, 1)
+    g = int(cubics_norm.shape[0])
+
+    widths = torch.clamp(aa, min=1e-4)
+    inv_s2 = (1.0 / torch.clamp(widths * widths, min=1e-6)).contiguous()
+    seg_counts = (offs[1:] - offs[:-1]).to(torch.int64)
+    support_seg = torch.repeat_interleave(widths * 3.0, seg_counts).contiguous()
+    stroke_zeros = torch.zeros((g,), dtype=torch.float32, device=dev)
+    cubics_px, seg_ranges, seg_hits = cs.project_cubics_2d_forward_tilelang(
+        cubics_norm, stroke_zeros, support_seg, h, w, tile_bounds)
+    edges_px, prim_edge_offs, _, _, _ = cs._flatten_cubics_to_edges(
+        cubics_px, offs, distance_samples=s)
+    prim_ranges, num_hit = cs._primitive_tile_ranges_from_segment_tile_ranges(
+        seg_ranges, offs, tile_bounds)
+    cum = torch.cumsum(num_hit, dim=0, dtype=torch.int32)
+    isect_ids, prim_ids = cs.map_cubic_to_intersects_tilelang(prim_ranges, depths, cum, tile_bounds)
+    isect_sorted, order = torch.sort(isect_ids)
+    prim_sorted = torch.gather(prim_ids, 0, order)
+    ranges = cs._build_fill_isect_edge_ranges(prim_sorted, prim_edge_offs, num_edges=int(edges_px.shape[0]))
+    tile_bins = tb.get_tile_bin_edges_tilelang(int(cum[-1].item()), isect_sorted,
+                                               num_tiles=tile_bounds[0] * tile_bounds[1], compact=True)
+    img, final_ts, final_idx = cs.rasterize_cubic_fill_forward_tilelang(
+        tile_bounds, (bx, by, 1), (w, h, 1), prim_sorted, tile_bins, cubics_px, offs,
+        colors, opac, rules, bg, inv_sigma2s=inv_s2, edges_px=edges_px,
+        isect_edge_ranges=ranges, distance_samples=s)
+
+    v_out = scenes.seeded_grad(grad_seed, h, w).to(dev)
+    v_edges = torch.zeros_like(edges_px)
+    v_colors = torch.zeros_like(colors)
+    v_opac = torch.zeros_like(opac)
+    v_inv = torch.zeros_like(opac)
+    contrib = torch.zeros_like(colors)
+    isect_contrib = torch.zeros((int(prim_sorted.numel()),), dtype=torch.float32, device=dev)
+    kern = cs.rasterize_cubic_fill_backward_kernel(block_x=bx, block_y=by, dtype="float32")
+    kern(prim_sorted, tile_bins, edges_px, ranges, colors, opac, inv_s2, rules, bg,
+         final_ts, final_idx, v_out, v_edges, v_colors, v_opac, v_inv, 1, contrib, 1, isect_contrib)
+    v_cubics_px = cs._accumulate_edge_grads_to_cubics(v_edges, g, distance_samples=s)
+
+    # end-to-end autograd through the public entry point
+    cn = cubics_norm.clone().requires_grad_(True)
+    col = colors.clone().requires_grad_(True)
+    op = opac.clone().requires_grad_(True)
+    aw = aa.clone().requires_grad_(True)
+    out = cs.render_cubic_fill_splat_tilelang(cn, offs, col, op, depths, h, w, bx, by, bg,
+                                              fill_rules=rules, aa_widths=aw, distance_samples=s)
+    (out * v_out).sum().backward()
+
+    return {
+        "cubics_norm": _np(cubics_norm), "offs": _np(offs), "colors": _np(colors),
+        "opacities": _np(opac), "depths": _np(depths), "fill_rules": _np(rules),
+        "aa_widths": _np(aa), "background": _np(bg), "hw_s": np.array([h, w, s], np.int32),
+        "cubics_px": _np(cubics_px), "seg_tile_ranges": _np(seg_ranges),
+        "seg_num_tiles": _np(seg_hits), "edges_px": _np(edges_px),
+        "prim_edge_offsets": _np(prim_edge_offs), "prim_tile_ranges": _np(prim_ranges),
+        "num_tiles_hit": _np(num_hit), "isect_ids": _np(isect_ids), "prim_ids": _np(prim_ids),
+        "isect_ids_sorted": _np(isect_sorted), "prim_ids_sorted": _np(prim_sorted),
+        "isect_edge_ranges": _np(ranges), "tile_bins": _np(tile_bins),
+        "image": _np(img), "final_Ts": _np(final_ts), "final_idx": _np(final_idx),
+        "v_output": _np(v_out), "v_edges": _np(v_edges), "v_colors": _np(v_colors),
+        "v_opacities": _np(v_opac), "v_inv_sigma2s": _np(v_inv),
+        "curve_contrib_rgb": _np(contrib), "curve_isect_contrib": _np(isect_contrib),
+        "v_cubics_px": _np(v_cubics_px),
+        "api_image": _np(out), "api_v_cubics_norm": _np(cn.grad), "api_v_colors": _np(col.grad),
+        "api_v_opacities": _np(op.grad), "api_v_aa_widths": _np(aw.grad),
+    }
+
+
+def stroke_case(cs, ps, tb, scene, grad_seed, dev):
+    h, w, s = scene.height, scene.width, scene.samples
+    cubics_norm = scene.cubics_norm().to(dev)
+    offs = scene.seg_offsets().to(dev)
+    colors = scene.colors.to(dev)
+    opac = scene.opacities.to(dev)
+    sw = scene.stroke_widths.to(dev)
+    depths = scene.depths.to(dev)
+    aa = scene.aa_widths.to(dev)
+    bg = scene.background.to(dev)
+    bx = by = 16
+    tile_bounds = ((w + bx - 1) // bx, (h + by - 1) // by, 1)
+    g = int(cubics_norm.shape[0])
+    widths = torch.clamp(aa, min=1e-4)
+    inv_s2 = (1.0 / torch.clamp(widths * widths, min=1e-6)).contiguous()
+    seg_counts = (offs[1:] - offs[:-1]).to(torch.int64)
+    support_seg = torch.repeat_interleave(widths * 3.0, seg_counts).contiguous()
+    stroke_seg = torch.repeat_interleave(sw, seg_counts).contiguous()
+    cubics_px, seg_ranges, seg_hits = cs.project_cubics_2d_forward_tilelang(
+        cubics_norm, stroke_seg, support_seg, h, w, tile_bounds)
+    edges_px, prim_edge_offs, _, _, _ = cs._flatten_cubics_to_edges(cubics_px, offs, distance_samples=s)
+    prim_ranges, num_hit = cs._primitive_tile_ranges_from_segment_tile_ranges(seg_ranges, offs, tile_bounds)
+    cum = torch.cumsum(num_hit, dim=0, dtype=torch.int32)
+    isect_ids, prim_ids = cs.map_cubic_to_intersects_tilelang(prim_ranges, depths, cum, tile_bounds)
+    isect_sorted, order = torch.sort(isect_ids)
+    prim_sorted = torch.gather(prim_ids, 0, order)
+    ranges = cs._build_fill_isect_edge_ranges(prim_sorted, prim_edge_offs, num_edges=int(edges_px.shape[0]))
+    tile_bins = tb.get_tile_bin_edges_tilelang(int(cum[-1].item()), isect_sorted,
+                                               num_tiles=tile_bounds[0] * tile_bounds[1], compact=True)
+    img, final_ts, final_idx = ps.rasterize_cubic_polyline_forward_tilelang(
+        tile_bounds, (bx, by, 1), (w, h, 1), prim_sorted, tile_bins, colors, opac, sw, bg,
+        inv_sigma2s=inv_s2, edges_px=edges_px, isect_edge_ranges=ranges)
+    v_out = scenes.seeded_grad(grad_seed, h, w).to(dev)
+    v_edges = torch.zeros_like(edges_px)
+    v_colors = torch.zeros_like(colors)
+    v_opac = torch.zeros_like(opac)
+    v_sw = torch.zeros_like(sw)
+    v_inv = torch.zeros_like(opac)
+    contrib = torch.zeros_like(colors)
+    isect_contrib = torch.zeros((int(prim_sorted.numel()),), dtype=torch.float32, device=dev)
+    kern = ps.rasterize_cubic_polyline_backward_kernel(block_x=bx, block_y=by, dtype="float32")
+    kern(prim_sorted, tile_bins, edges_px, ranges, colors, opac, sw, inv_s2, bg, final_ts,
+         final_idx, v_out, v_edges, v_colors, v_opac, v_sw, v_inv, 1, contrib, 1, isect_contrib)
+    v_cubics_px = cs._accumulate_edge_grads_to_cubics(v_edges, g, distance_samples=s)
+
+    cn = cubics_norm.clone().requires_grad_(True)
+    col = colors.clone().requires_grad_(True)
+    op = opac.clone().requires_grad_(True)
+    swr = sw.clone().requires_grad_(True)
+    aw = aa.clone().requires_grad_(True)
+    out = ps.render_cubic_polyline_splat_tilelang(cn, offs, col, op, swr, depths, h, w, bx, by, bg,
+                                                  aa_widths=aw, distance_samples=s)
+    (out * v_out).sum().backward()
+    return {
+        "cubics_norm": _np(cubics_norm), "offs": _np(offs), "colors": _np(colors),
+        "opacities": _np(opac), "stroke_widths": _np(sw), "depths": _np(depths),
+        "aa_widths": _np(aa), "background": _np(bg), "hw_s": np.array([h, w, s], np.int32),
+        "cubics_px": _np(cubics_px), "seg_tile_ranges": _np(seg_ranges),
+        "edges_px": _np(edges_px), "prim_tile_ranges": _np(prim_ranges),
+        "isect_ids_sorted": _np(isect_sorted), "prim_ids_sorted": _np(prim_sorted),
+        "tile_bins": _np(tile_bins), "image": _np(img), "final_Ts": _np(final_ts),
+        "final_idx": _np(final_idx), "v_output": _np(v_out), "v_edges": _np(v_edges),
+        "v_colors": _np(v_colors), "v_opacities": _np(v_opac), "v_stroke_widths": _np(v_sw),
+        "v_inv_sigma2s": _np(v_inv), "curve_contrib_rgb": _np(contrib),
+        "curve_isect_contrib": _np(isect_contrib), "v_cubics_px": _np(v_cubics_px),
+        "api_image": _np(out), "api_v_cubics_norm": _np(cn.grad), "api_v_colors": _np(col.grad),
+        "api_v_opacities": _np(op.grad), "api_v_stroke_widths": _np(swr.grad),
+        "api_v_aa_widths": _np(aw.grad),
+    }
+
+
+def ring_case(cs, dev):
+    gen = torch.Generator().manual_seed(7)
+    cp = (torch.rand(5, 10, 2, generator=gen) * 2.0 - 1.0).to(dev)
+    cpg = cp.clone().requires_grad_(True)
+    segs, offs = cs.closed_cubic_fill_segments_tilelang(cpg, subdiv=4)
+    gs = (torch.rand(segs.shape, generator=gen) - 0.5).to(dev)
+    (segs * gs).sum().backward()
+    return {"control_points": _np(cp), "segments": _np(segs), "offsets": _np(offs),
+            "grad_segments": _np(gs), "grad_control_points": _np(cpg.grad)}
+
+
+def metric_case(metric, dev):
+    gen = torch.Generator().manual_seed(11)
+    x = torch.rand(2, 3, 40, 52, generator=gen).to(dev)
+    y = torch.clamp(x + 0.1 * (torch.rand(x.shape, generator=gen) - 0.5).to(dev), 0, 1)
+    xg = x.clone().requires_grad_(True)
+    loss = metric.mse_loss_tilelang(xg, y)
+    loss.backward()
+    return {
+        "x": _np(x), "y": _np(y), "mse": _np(loss.detach()), "mse_grad": _np(xg.grad),
+        "psnr": _np(metric.psnr(x, y)), "ssim": _np(metric.ssim(x, y)),
+        "ssim_per_image": _np(metric.ssim(x, y, size_average=False)),
+    }
+
+
+def time_config2(manbo, cs, dev, iters: int, warmup: int):
+    """Reference training step at config 2: render + MSE + SSIM + backward + Adam."""
+    sc = scenes.config2()
+    h, w = sc.height, sc.width
+    ring = sc.ring.to(dev).clone().requires_grad_(True)
+    colors = sc.colors.to(dev).clone().requires_grad_(True)
+    opac, depths = sc.opacities.to(dev), sc.depths.to(dev)
+    rules, aa, bg = sc.fill_rules.to(dev), sc.aa_widths.to(dev), sc.background.to(dev)
+    offs = sc.seg_offsets().to(dev)
+    target = sc.target.to(dev)
+    gidx = scenes.ring_gather_index(sc.segs_per_path).to(dev)
+    half = torch.tensor([0.5 * w, 0.5 * h], device=dev)
+    opt = torch.optim.Adam([{"params": [ring], "lr": 0.5}, {"params": [colors], "lr": 0.01}])
+
+    def step():
+        opt.zero_grad(set_to_none=True)
+        cub = ring[:, gidx, :].reshape(-1, 4, 2)
+        cn = cub / half - 1.0
+        out = cs.render_cubic_fill_splat_tilelang(cn, offs, colors, opac, depths, h, w, 16, 16, bg,
+                                                  fill_rules=rules, aa_widths=aa,
+                                                  distance_samples=sc.samples)
+        img = torch.clamp(out, 0, 1).permute(2, 0, 1).unsqueeze(0).contiguous()
+        loss = manbo.mse_loss_tilelang(img, target)
+        with torch.no_grad():
+            s = manbo.ssim(img.detach(), target)
+        loss.backward()
+        opt.step()
+        return loss, s
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(iters):
+        loss, s = step()
+    torch.cuda.synchronize()
+    dt = time.perf_counter() - t0
+    return {"iters": iters, "seconds": dt, "iters_per_s": iters / dt,
+            "final_loss": float(loss.item()), "final_ssim": float(s.item())}
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref", default=os.path.join(ROOT, "baseline", "_ref"))
+    ap.add_argument("--out", default=HERE)
+    ap.add_argument("--time", action="store_true")
+    ap.add_argument("--no-golden", action="store_true")
+    ap.add_argument("--iters", type=int, default=100)
+    ap.add_argument("--json", default=None)
+    args = ap.parse_args(argv)
+
+    sys.path.insert(0, os.path.abspath(args.ref))
+    import tilelang  # noqa: F401
+    import manbo
+    from manbo import metric
+    from manbo.ops import cubic_polyline_splatting as ps
+    from manbo.ops import cubic_splatting as cs
+    from manbo.ops import tile_bins as tb
+
+    dev = torch.device("cuda")
+    info = {"torch": torch.__version__, "tilelang": getattr(tilelang, "__version__", "?"),
+            "gpu": torch.cuda.get_device_name(0)}
+    print(info, flush=True)
+    if not args.no_golden:
+        _save(args.out, "fill_small_a", fill_case(cs, tb, scenes.small_fill_scene(21), 31, dev))
+        _save(args.out, "fill_small_b", fill_case(cs, tb, scenes.small_fill_scene(22, h=40, w=72, paths=9, samples=5), 32, dev))
+        ties = scenes.small_fill_scene(23, paths=7, mixed=False)
+        ties.depths = torch.full_like(ties.depths, 0.5)
+        _save(args.out, "fill_ties", fill_case(cs, tb, ties, 33, dev))
+        _save(args.out, "fill_config1", fill_case(cs, tb, scenes.config1(), 34, dev))
+        _save(args.out, "stroke_small", stroke_case(cs, ps, tb, scenes.small_stroke_scene(41), 42, dev))
+        _save(args.out, "ring_segments", ring_case(cs, dev))
+        _save(args.out, "metrics", metric_case(metric, dev))
+    if args.time:
+        info["config2_reference_tilelang"] = time_config2(manbo, cs, dev, args.iters, 5)
+        print(json.dumps(info), flush=True)
+    if args.json:
+        with open(args.json, "w") as f:
+            json.dump(info, f, indent=1)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,259 @@
+/*
+ * cubicsplat_b200.h -- C ABI of the B200 (sm_100a) CubicSplat hot path.
+ *
+ * Every entry point takes raw device pointers, element counts and a
+ * cudaStream_t passed as void* (the caller's current stream), launches its
+ * kernels on that stream and returns a status code.  No entry point allocates
+ * device memory; the ones that need scratch take a caller-provided workspace
+ * whose size is reported by a *_workspace_size function.  Nothing is
+ * synchronised: results are ready when the stream reaches them.
+ *
+ * Reference interfaces are cited by file:line inside the reference project
+ * (manbo/ops/cubic_splatting.py, manbo/ops/cubic_polyline_splatting.py,
+ * manbo/ops/tile_bins.py, manbo/ops/metric.py, manbo/metric.py).  Tiles are
+ * 16x16 pixels as in the reference default (BLOCK_X = BLOCK_Y = 16); other
+ * block sizes return CS_ERR_UNSUPPORTED.  Images are [H, W, 3] float32
+ * (HWC) as the reference renderer returns them; metric inputs are [N, C, H, W].
+ */
+#ifndef CUBICSPLAT_B200_H
+#define CUBICSPLAT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define CS_API __attribute__((visibility("default")))
+#else
+#define CS_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CS_OK 0
+#define CS_ERR_ARG 1          /* bad size, null pointer or unsupported tile size */
+#define CS_ERR_CAPACITY 2     /* intersect count exceeded the caller's capacity */
+#define CS_ERR_CUDA 3         /* a kernel launch failed */
+#define CS_ERR_UNSUPPORTED 4  /* valid but unsupported configuration */
+
+/* Library version string and the list of exported entry points (for checks). */
+CS_API const char *cs_version(void);
+
+/* --------------------------------------------------------------------------
+ * Projection, flattening and binning
+ * ------------------------------------------------------------------------ */
+
+/* Normalised cubic -> pixel space (p = fma(n, W/2, W/2)), exact cubic AABB from
+ * the roots of B'(t), padded by max(aabb_pad, support) + half stroke width (or
+ * the chord-anisotropic pad), tile rectangle [min, max) clamped to the grid.
+ * Replaces project_cubics_2d_forward_kernel, cubic_splatting.py:546-747.
+ * cubics_norm/cubics_px: [n, 4, 2]; stroke_widths, support_radii: [n];
+ * tile_ranges: [n, 4]; num_tiles_hit: [n]. */
+CS_API int cs_project_cubics(const float *cubics_norm, const float *stroke_widths,
+                      const float *support_radii, float *cubics_px, int32_t *tile_ranges,
+                      int32_t *num_tiles_hit, int64_t num_curves, int32_t img_height,
+                      int32_t img_width, int32_t block_x, int32_t block_y, float aabb_pad,
+                      int32_t aniso, void *stream);
+
+/* Uniform S-point Bernstein flattening of each cubic into S-1 straight edges.
+ * basis: [4, S] cubic Bernstein weights at linspace(0, 1, S).
+ * Replaces _flatten_cubics_to_edges (bernstein), cubic_splatting.py:1709-1728.
+ * cubics_px: [n, 4, 2] -> edges_px: [n*(S-1), 2, 2]. */
+CS_API int cs_flatten_bernstein(const float *cubics_px, const float *basis, float *edges_px,
+                         int64_t num_segments, int32_t samples, void *stream);
+
+/* Union of segment tile rectangles per primitive (CSR offsets over segments).
+ * Replaces primitive_tile_ranges_from_segment_ranges_kernel,
+ * cubic_splatting.py:2071-2137. */
+CS_API int cs_primitive_tile_ranges(const int32_t *seg_tile_ranges, const int32_t *prim_seg_offsets,
+                             int32_t *prim_tile_ranges, int32_t *num_tiles_hit,
+                             int64_t num_primitives, int32_t tile_bound_x, int32_t tile_bound_y,
+                             void *stream);
+
+/* Intersect keys (tile << 32 | sortable depth bits) and primitive ids,
+ * primitive-major and row-major over each primitive's tile rectangle;
+ * cum_tiles_hit is the inclusive prefix sum of num_tiles_hit.
+ * Replaces map_cubic_to_intersects_kernel, cubic_splatting.py:750-819. */
+CS_API int cs_map_cubic_to_intersects(const int32_t *tile_ranges, const float *depths,
+                               const int32_t *cum_tiles_hit, int64_t *isect_ids,
+                               int32_t *prim_ids, int64_t num_primitives, int32_t tile_bound_x,
+                               void *stream);
+
+/* Per-tile [start, end) of sorted keys; tile_bins [num_tiles, 2] is zeroed
+ * first, so empty tiles read [0, 0].
+ * Replaces get_tile_bin_edges_kernel, tile_bins.py:10-60 (compact=True). */
+CS_API int cs_tile_bin_edges(const int64_t *isect_ids_sorted, int64_t num_intersects,
+                      int32_t *tile_bins, int64_t num_tiles, void *stream);
+
+/* ranges[i] = (edge_offsets[pid], edge_offsets[pid + 1]) for pid = prim_ids[i].
+ * Replaces _build_fill_isect_edge_ranges, cubic_splatting.py:1849-1860. */
+CS_API int cs_isect_edge_ranges(const int32_t *prim_ids_sorted, const int32_t *prim_edge_offsets,
+                         int32_t *isect_edge_ranges, int64_t num_intersects, void *stream);
+
+/* Fused B200 binning, stage 1 of 2: projection + AABB + flattening of every
+ * segment, per-primitive tile rectangles, per-tile intersect counts restricted
+ * to tile rows [tile_row_begin, tile_row_end), and their exclusive scan into
+ * tile_bins [num_tiles, 2].  *num_intersects (device) receives the total.
+ * stroke_widths may be NULL (fill mode: zero stroke width); aniso selects the
+ * chord-anisotropic padding of the reference's aniso_intersects.  If the total
+ * exceeds capacity (pass INT64_MAX when the caller sizes the intersect buffers
+ * from *num_intersects afterwards), every tile range is written empty and
+ * *status (device int, may be NULL) is set to CS_ERR_CAPACITY, so no later
+ * kernel reads past the caller's buffers.  Offsets that do not start at 0,
+ * end at num_segments and increase set *status to CS_ERR_ARG (the primitive is
+ * treated as empty).
+ * The stage-2 call below produces the sorted intersect list; together they
+ * replace project (K3) + flatten + K4 + cumsum + K5 + torch.sort + K6 of
+ * _CubicFillSplatFunction.forward, cubic_splatting.py:2815-2908.
+ * Workspace: cs_bin_workspace_size(num_tiles). */
+CS_API size_t cs_bin_workspace_size(int64_t num_tiles);
+CS_API int cs_bin_count(const float *cubics_norm, const int32_t *prim_seg_offsets,
+                 const float *aa_widths, const float *stroke_widths, const float *basis,
+                 float *cubics_px, float *edges_px, int32_t *prim_tile_ranges,
+                 int32_t *num_tiles_hit, int32_t *tile_bins, int32_t *num_intersects,
+                 int32_t *status, void *workspace, int64_t num_primitives,
+                 int64_t num_segments, int64_t capacity, int32_t samples, int32_t img_height,
+                 int32_t img_width, int32_t tile_row_begin, int32_t tile_row_end, float aabb_pad,
+                 int32_t aniso, void *stream);
+
+/* Fused B200 binning, stage 2 of 2: scatter each (primitive, tile) pair into
+ * its tile's range and sort every tile's pairs by (depth key, primitive id),
+ * i.e. the order of a stable sort of the reference's keys.  Writes
+ * prim_ids_sorted [capacity] and isect_ids_sorted [capacity] (may be NULL).
+ * If the total exceeds capacity nothing is written out of bounds, *status
+ * (device int, may be NULL) is set to CS_ERR_CAPACITY and the call returns
+ * CS_OK (the check is on the device). */
+CS_API int cs_bin_sort(const int32_t *prim_tile_ranges, const float *depths,
+                const int32_t *tile_bins, const int32_t *num_intersects, int32_t *prim_ids_sorted,
+                int64_t *isect_ids_sorted, int32_t *status, void *workspace,
+                int64_t num_primitives, int64_t capacity, int32_t img_height, int32_t img_width,
+                int32_t tile_row_begin, int32_t tile_row_end, void *stream);
+
+/* --------------------------------------------------------------------------
+ * Rasterisation (one CTA per 16x16 tile, front-to-back compositing)
+ * ------------------------------------------------------------------------ */
+
+/* Closed-fill forward: per pixel, winding number / crossing parity and the
+ * minimum distance to the primitive's polyline, sigmoid soft coverage, then
+ * front-to-back alpha compositing with early termination.
+ * Replaces rasterize_cubic_fill_forward_kernel, cubic_splatting.py:918-1194.
+ * isect_edge_ranges [I, 2] may be NULL when prim_edge_offsets [P + 1] is given.
+ * Tile rows outside [tile_row_begin, tile_row_end) are not touched. */
+CS_API int cs_fill_forward(const int32_t *prim_ids_sorted, const int32_t *tile_bins,
+                    const float *edges_px, const int32_t *isect_edge_ranges,
+                    const int32_t *prim_edge_offsets, const float *colors,
+                    const float *opacities, const float *inv_sigma2s, const int32_t *fill_rules,
+                    const float *background, float *out_img, float *final_Ts, int32_t *final_idx,
+                    int32_t img_height, int32_t img_width, int32_t tile_row_begin,
+                    int32_t tile_row_end, void *stream);
+
+/* Closed-fill backward: reverse compositing from final_idx, gradients of the
+ * colours, opacities, 1/sigma^2 and edge endpoints (closest edge only).
+ * Outputs are accumulated (+=) into caller-zeroed buffers.  curve_contrib_rgb
+ * [P, 3] and curve_isect_contrib [I] are optional (NULL = not collected).
+ * v_output [H, W, 3] is the upstream image gradient; when it is NULL the MSE
+ * gradient is computed in the kernel instead: v = scale * (clamp(out) - target)
+ * masked to 0 <= out <= 1, with out_img [H, W, 3], target_chw [3, H, W] and
+ * *mse_scale (device scalar, e.g. 2/N * dLoss).
+ * Replaces rasterize_cubic_fill_backward_kernel, cubic_splatting.py:1197-1651. */
+CS_API int cs_fill_backward(const int32_t *prim_ids_sorted, const int32_t *tile_bins,
+                     const float *edges_px, const int32_t *isect_edge_ranges,
+                     const int32_t *prim_edge_offsets, const float *colors,
+                     const float *opacities, const float *inv_sigma2s, const int32_t *fill_rules,
+                     const float *background, const float *final_Ts, const int32_t *final_idx,
+                     const float *v_output, const float *out_img, const float *target_chw,
+                     const float *mse_scale, float *v_edges, float *v_colors, float *v_opacities,
+                     float *v_inv_sigma2s, float *curve_contrib_rgb, float *curve_isect_contrib,
+                     int32_t img_height, int32_t img_width, int32_t tile_row_begin,
+                     int32_t tile_row_end, void *stream);
+
+/* Stroke forward: coverage exp(-1/2 max(0, d - w/2)^2 / sigma^2).
+ * Replaces rasterize_cubic_polyline_forward_kernel,
+ * cubic_polyline_splatting.py:33-249. */
+CS_API int cs_stroke_forward(const int32_t *prim_ids_sorted, const int32_t *tile_bins,
+                      const float *edges_px, const int32_t *isect_edge_ranges,
+                      const int32_t *prim_edge_offsets, const float *colors,
+                      const float *opacities, const float *stroke_widths,
+                      const float *inv_sigma2s, const float *background, float *out_img,
+                      float *final_Ts, int32_t *final_idx, int32_t img_height, int32_t img_width,
+                      int32_t tile_row_begin, int32_t tile_row_end, void *stream);
+
+/* Stroke backward (adds d/d stroke width).
+ * Replaces rasterize_cubic_polyline_backward_kernel,
+ * cubic_polyline_splatting.py:252-660. */
+CS_API int cs_stroke_backward(const int32_t *prim_ids_sorted, const int32_t *tile_bins,
+                       const float *edges_px, const int32_t *isect_edge_ranges,
+                       const int32_t *prim_edge_offsets, const float *colors,
+                       const float *opacities, const float *stroke_widths,
+                       const float *inv_sigma2s, const float *background, const float *final_Ts,
+                       const int32_t *final_idx, const float *v_output, const float *out_img,
+                       const float *target_chw, const float *mse_scale, float *v_edges,
+                       float *v_colors, float *v_opacities, float *v_stroke_widths,
+                       float *v_inv_sigma2s, float *curve_contrib_rgb,
+                       float *curve_isect_contrib, int32_t img_height, int32_t img_width,
+                       int32_t tile_row_begin, int32_t tile_row_end, void *stream);
+
+/* Edge endpoint gradients -> cubic control-point gradients with the Bernstein
+ * weights at t = e / (S-1); optional scale (sx, sy) applied to the result
+ * (pass 1, 1 for pixel space, W/2, H/2 for normalised space).
+ * Replaces _accumulate_edge_grads_to_cubics_kernel, cubic_splatting.py:2308-2396
+ * and the epilogue scaling of cubic_splatting.py:3096-3100. */
+CS_API int cs_edge_grads_to_cubics(const float *v_edges, float *v_cubics, int64_t num_segments,
+                            int32_t edges_per_segment, float scale_x, float scale_y,
+                            void *stream);
+
+/* --------------------------------------------------------------------------
+ * Closed control polygon -> ring of piecewise-Hermite cubics
+ * ------------------------------------------------------------------------ */
+
+/* control_points [N, K, 2] -> segments [N*2*subdiv, 4, 2]; basis [subdiv+1, Kb],
+ * deriv_basis [subdiv+1, Kb-1], dt [subdiv] with Kb = (K+2)/2.
+ * Replaces closed_cubic_fill_segments_forward_kernel, cubic_splatting.py:137-268. */
+CS_API int cs_ring_segments_forward(const float *control_points, const float *basis,
+                             const float *deriv_basis, const float *dt, float *segments,
+                             int64_t num_curves, int32_t k, int32_t subdiv, void *stream);
+
+/* Adjoint of the above, accumulated (+=) into grad_control_points.
+ * Replaces closed_cubic_fill_segments_backward_kernel, cubic_splatting.py:271-397. */
+CS_API int cs_ring_segments_backward(const float *grad_segments, const float *basis,
+                              const float *deriv_basis, const float *dt,
+                              float *grad_control_points, int64_t num_curves, int32_t k,
+                              int32_t subdiv, void *stream);
+
+/* --------------------------------------------------------------------------
+ * Metrics
+ * ------------------------------------------------------------------------ */
+
+/* Sum of squared differences in one launch (block partials, last block
+ * reduces them in a fixed order).  Writes *out_sse and *out_mse = sse / n
+ * (device scalars; either may be NULL).  Workspace: cs_mse_workspace_size(n).
+ * Replaces mse_partial_sum_kernel + the reduce_sum_partial_kernel loop,
+ * manbo/ops/metric.py:18-163, 344-382 and _mse_forward_tilelang,
+ * manbo/metric.py:102-130. */
+CS_API size_t cs_mse_workspace_size(int64_t n);
+CS_API int cs_mse_forward(const float *x, const float *y, int64_t n, float *out_sse, float *out_mse,
+                   void *workspace, void *stream);
+
+/* grad = (*scale) * (lhs - rhs), scale read on the device (no host sync).
+ * Replaces mse_backward_diff_kernel, manbo/ops/metric.py:166-202. */
+CS_API int cs_mse_backward(const float *lhs, const float *rhs, const float *scale, float *grad,
+                    int64_t n, void *stream);
+
+/* SSIM with a separable Gaussian window g [win] (win odd, win2d = outer(g, g)),
+ * valid-window semantics, per plane (N*C planes of H x W).  Writes the mean
+ * SSIM of every plane to plane_means [planes] and, when ssim_map is not NULL,
+ * the map [planes, H-win+1, W-win+1].
+ * Workspace: cs_ssim_workspace_size(planes, h, w, win).
+ * Replaces ssim_map_kernel + the mean of manbo/metric.py:215-273
+ * (manbo/ops/metric.py:205-341). */
+CS_API size_t cs_ssim_workspace_size(int64_t planes, int32_t h, int32_t w, int32_t win);
+CS_API int cs_ssim(const float *x, const float *y, const float *gauss, int64_t planes, int32_t h,
+            int32_t w, int32_t win, float c1, float c2, float *plane_means, float *ssim_map,
+            void *workspace, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CUBICSPLAT_B200_H */

@@ -1,0 +1,597 @@
+// Projection, flattening and tile binning for the cubic renderer (sm_100a).
+//
+// Two families of entry points live here:
+//  * stage kernels with the reference's signatures (project, flatten,
+//    primitive ranges, intersect keys, tile bins, edge ranges) used by the
+//    drop-in per-stage API;
+//  * the fused B200 pipeline (cs_bin_count + cs_bin_sort): one warp per
+//    primitive projects, bounds and flattens its segments and counts its
+//    tiles; one CTA scans the per-tile counts into tile ranges; one warp per
+//    primitive scatters its (depth, id) pairs into its tiles' ranges; one CTA
+//    per tile sorts its pairs.  This replaces the reference's global 64-bit
+//    key sort with per-tile sorts of (depth key, primitive id), which yields
+//    exactly the order of a stable sort of the reference's keys.
+#include "cs_common.cuh"
+
+namespace cs {
+
+// ---------------------------------------------------------------------------
+// projection + exact cubic AABB + padded tile rectangle
+// (manbo/ops/cubic_splatting.py:588-745).  Arithmetic is the reference's, in
+// its written order; the pixel projection is one fused multiply-add, which is
+// what the reference's compiled kernel does (pinned by golden vectors).
+
+__device__ __forceinline__ void axis_extrema(float a, float b, float c, float d, float& mn,
+                                             float& mx) {
+  const float eps = kEps;
+  float q2 = 3.0f * a;
+  float q1 = 2.0f * b;
+  float q0 = c;
+  if ((q2 > eps) | (q2 < -eps)) {
+    float disc = q1 * q1 - 4.0f * q2 * q0;
+    if (disc >= -eps) {
+      float sq = sqrtf(fmaxf(disc, 0.0f));
+      float inv2q2 = 1.0f / (2.0f * q2);
+      float t0 = (-q1 - sq) * inv2q2;
+      float t1 = (-q1 + sq) * inv2q2;
+      if ((t0 > 0.0f) & (t0 < 1.0f)) {
+        float v = ((a * t0 + b) * t0 + c) * t0 + d;
+        mn = fminf(mn, v);
+        mx = fmaxf(mx, v);
+      }
+      if ((t1 > 0.0f) & (t1 < 1.0f)) {
+        float v = ((a * t1 + b) * t1 + c) * t1 + d;
+        mn = fminf(mn, v);
+        mx = fmaxf(mx, v);
+      }
+    }
+  } else if ((q1 > eps) | (q1 < -eps)) {
+    float t = -q0 / q1;
+    if ((t > 0.0f) & (t < 1.0f)) {
+      float v = ((a * t + b) * t + c) * t + d;
+      mn = fminf(mn, v);
+      mx = fmaxf(mx, v);
+    }
+  }
+}
+
+__device__ __forceinline__ void project_points(const float* __restrict__ cn, float half_w,
+                                               float half_h, float p[8]) {
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    p[2 * k] = __fmaf_rn(cn[2 * k], half_w, half_w);
+    p[2 * k + 1] = __fmaf_rn(cn[2 * k + 1], half_h, half_h);
+  }
+}
+
+__device__ __forceinline__ void segment_rect(const float p[8], float stroke_w, float support_r,
+                                             float aabb_pad, int aniso, int tbx, int tby,
+                                             int rect[4]) {
+  float p0x = p[0], p0y = p[1], p1x = p[2], p1y = p[3], p2x = p[4], p2y = p[5], p3x = p[6],
+        p3y = p[7];
+  float ax = -p0x + 3.0f * p1x - 3.0f * p2x + p3x;
+  float bx = 3.0f * p0x - 6.0f * p1x + 3.0f * p2x;
+  float cx = -3.0f * p0x + 3.0f * p1x;
+  float ay = -p0y + 3.0f * p1y - 3.0f * p2y + p3y;
+  float by = 3.0f * p0y - 6.0f * p1y + 3.0f * p2y;
+  float cy = -3.0f * p0y + 3.0f * p1y;
+  float min_x = fminf(p0x, p3x), max_x = fmaxf(p0x, p3x);
+  float min_y = fminf(p0y, p3y), max_y = fmaxf(p0y, p3y);
+  axis_extrema(ax, bx, cx, p0x, min_x, max_x);
+  axis_extrema(ay, by, cy, p0y, min_y, max_y);
+  float half_sw = fmaxf(0.0f, stroke_w) * 0.5f;
+  float support = fmaxf(0.0f, support_r);
+  if (aniso) {
+    float chx = p3x - p0x, chy = p3y - p0y;
+    float chord2 = chx * chx + chy * chy;
+    float inv_chord = 1.0f / sqrtf(fmaxf(chord2, kEps));
+    float nx = fmaxf(0.20f, fabsf(chy) * inv_chord);
+    float ny = fmaxf(0.20f, fabsf(chx) * inv_chord);
+    float radial = half_sw + support;
+    float pad_x = aabb_pad + radial * nx;
+    float pad_y = aabb_pad + radial * ny;
+    min_x = min_x - pad_x;
+    max_x = max_x + pad_x;
+    min_y = min_y - pad_y;
+    max_y = max_y + pad_y;
+  } else {
+    float pad_i = fmaxf(aabb_pad, support);
+    min_x = min_x - half_sw - pad_i;
+    min_y = min_y - half_sw - pad_i;
+    max_x = max_x + half_sw + pad_i;
+    max_y = max_y + half_sw + pad_i;
+  }
+  rect[0] = min(max(f2i_trunc_sat(min_x / 16.0f), 0), tbx);
+  rect[1] = min(max(f2i_trunc_sat(min_y / 16.0f), 0), tby);
+  rect[2] = min(max(f2i_trunc_sat(max_x / 16.0f + 1.0f), 0), tbx);
+  rect[3] = min(max(f2i_trunc_sat(max_y / 16.0f + 1.0f), 0), tby);
+}
+
+// Bernstein point s of a pixel-space cubic: ((c0 b0 + c1 b1) + c2 b2) + c3 b3
+// per coordinate (the summation order of torch's sum over the 4 control
+// points, manbo/ops/cubic_splatting.py:1717).
+__device__ __forceinline__ void bernstein_point(const float p[8], const float* __restrict__ basis,
+                                                int S, int s, float& x, float& y) {
+  float b0 = __ldg(basis + s), b1 = __ldg(basis + S + s), b2 = __ldg(basis + 2 * S + s),
+        b3 = __ldg(basis + 3 * S + s);
+  x = p[0] * b0 + p[2] * b1;
+  x = x + p[4] * b2;
+  x = x + p[6] * b3;
+  y = p[1] * b0 + p[3] * b1;
+  y = y + p[5] * b2;
+  y = y + p[7] * b3;
+}
+
+__device__ __forceinline__ void store_point(float* __restrict__ edges, long long seg, int S, int s,
+                                            float x, float y) {
+  const long long E = S - 1;
+  if (s > 0) *reinterpret_cast<float2*>(edges + (seg * E + s - 1) * 4 + 2) = make_float2(x, y);
+  if (s < S - 1) *reinterpret_cast<float2*>(edges + (seg * E + s) * 4) = make_float2(x, y);
+}
+
+// ---------------------------------------------------------------------------
+// stage kernels with reference signatures
+
+__global__ void project_kernel(const float* __restrict__ cn, const float* __restrict__ sw,
+                               const float* __restrict__ sr, float* __restrict__ cpx,
+                               int* __restrict__ ranges, int* __restrict__ hits, long long n,
+                               float half_w, float half_h, float pad, int aniso, int tbx, int tby) {
+  long long g = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (g >= n) return;
+  float c[8], p[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) c[i] = cn[g * 8 + i];
+  project_points(c, half_w, half_h, p);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) cpx[g * 8 + i] = p[i];
+  int r[4];
+  segment_rect(p, sw[g], sr[g], pad, aniso, tbx, tby, r);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) ranges[g * 4 + i] = r[i];
+  hits[g] = max(0, (r[2] - r[0]) * (r[3] - r[1]));
+}
+
+__global__ void flatten_kernel(const float* __restrict__ cpx, const float* __restrict__ basis,
+                               float* __restrict__ edges, long long nseg, int S) {
+  long long q = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (q >= nseg * S) return;
+  long long seg = q / S;
+  int s = (int)(q - seg * S);
+  float p[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) p[i] = cpx[seg * 8 + i];
+  float x, y;
+  bernstein_point(p, basis, S, s, x, y);
+  store_point(edges, seg, S, s, x, y);
+}
+
+__global__ void prim_ranges_kernel(const int* __restrict__ seg_ranges, const int* __restrict__ offs,
+                                   int* __restrict__ pr, int* __restrict__ hits, long long np,
+                                   int tbx, int tby) {
+  long long p = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (p >= np) return;
+  int s0 = offs[p], s1 = offs[p + 1];
+  int r0 = 0, r1 = 0, r2 = 0, r3 = 0, h = 0;
+  if (s1 > s0) {
+    r0 = tbx; r1 = tby;
+    for (int s = s0; s < s1; ++s) {
+      r0 = min(r0, seg_ranges[s * 4 + 0]);
+      r1 = min(r1, seg_ranges[s * 4 + 1]);
+      r2 = max(r2, seg_ranges[s * 4 + 2]);
+      r3 = max(r3, seg_ranges[s * 4 + 3]);
+    }
+    h = max(0, r2 - r0) * max(0, r3 - r1);
+  }
+  pr[p * 4 + 0] = r0; pr[p * 4 + 1] = r1; pr[p * 4 + 2] = r2; pr[p * 4 + 3] = r3;
+  hits[p] = h;
+}
+
+__global__ void map_kernel(const int* __restrict__ ranges, const float* __restrict__ depths,
+                           const int* __restrict__ cum, long long* __restrict__ ids,
+                           int* __restrict__ pids, long long np, int tbx) {
+  long long p = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  int lane = threadIdx.x & 31;
+  if (p >= np) return;
+  int x0 = ranges[p * 4], y0 = ranges[p * 4 + 1], x1 = ranges[p * 4 + 2], y1 = ranges[p * 4 + 3];
+  int w = x1 - x0, h = y1 - y0;
+  if (w * h <= 0) return;
+  long long base = p == 0 ? 0 : cum[p - 1];
+  unsigned long long dk = depth_sort_key(depths[p]);
+  for (int q = lane; q < w * h; q += 32) {
+    int r = q / w, c = q - r * w;
+    long long tile = (long long)(y0 + r) * tbx + x0 + c;
+    ids[base + q] = (long long)(((unsigned long long)tile << 32) | dk);
+    pids[base + q] = (int)p;
+  }
+}
+
+__global__ void tile_bins_kernel(const long long* __restrict__ ids, long long n,
+                                 int* __restrict__ bins) {
+  long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  int cur = (int)(ids[i] >> 32);
+  if (i == 0) bins[cur * 2] = 0;
+  if (i == n - 1) bins[cur * 2 + 1] = (int)n;
+  if (i > 0) {
+    int prev = (int)(ids[i - 1] >> 32);
+    if (prev != cur) {
+      bins[prev * 2 + 1] = (int)i;
+      bins[cur * 2] = (int)i;
+    }
+  }
+}
+
+__global__ void edge_ranges_kernel(const int* __restrict__ pids, const int* __restrict__ eoffs,
+                                   int* __restrict__ out, long long n) {
+  long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  int p = pids[i];
+  out[i * 2] = eoffs[p];
+  out[i * 2 + 1] = eoffs[p + 1];
+}
+
+// ---------------------------------------------------------------------------
+// fused pipeline
+
+struct BinWorkspace {
+  int* tile_counts;  // [T]
+  int* cursor;       // [T]
+};
+
+__host__ __device__ inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+inline BinWorkspace bin_ws(void* base, long long ntiles) {
+  BinWorkspace w;
+  char* b = static_cast<char*>(base);
+  w.tile_counts = reinterpret_cast<int*>(b);
+  w.cursor = reinterpret_cast<int*>(b + align256(sizeof(int) * ntiles));
+  return w;
+}
+
+// One warp per primitive: project + bound every segment, union the rects,
+// flatten all segments into edges and count the primitive's tiles within the
+// band of tile rows [r0, r1).
+__global__ void __launch_bounds__(256) bin_prep_kernel(
+    const float* __restrict__ cn, const int* __restrict__ offs, const float* __restrict__ aa,
+    const float* __restrict__ sw, const float* __restrict__ basis, float* __restrict__ cpx,
+    float* __restrict__ edges, int* __restrict__ pr, int* __restrict__ hits,
+    int* __restrict__ tile_counts, int* __restrict__ status, long long np, long long nseg_total,
+    int S, float half_w, float half_h, int tbx, int tby, int r0, int r1, float pad, int aniso) {
+  long long p = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  int lane = threadIdx.x & 31;
+  if (p >= np) return;
+  int s0 = offs[p], s1 = offs[p + 1];
+  // CSR offsets must start at 0, end at the segment count and not decrease;
+  // a bad primitive is reported and treated as empty (no out-of-bounds reads).
+  const bool bad = s0 < 0 || s1 < s0 || s1 > nseg_total || (p == 0 && s0 != 0) ||
+                   (p == np - 1 && s1 != nseg_total);
+  if (bad) {
+    if (lane == 0 && status) atomicExch(status, CS_ERR_ARG);
+    s1 = s0 = max(0, min(s0, (int)nseg_total));
+  }
+  float w = fmaxf(aa[p], 1e-4f);
+  float support = w * 3.0f;
+  float stroke = sw ? sw[p] : 0.0f;
+  int mnx = tbx, mny = tby, mxx = 0, mxy = 0;
+  for (int i = s0 + lane; i < s1; i += 32) {
+    float c[8], q[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) c[k] = cn[(long long)i * 8 + k];
+    project_points(c, half_w, half_h, q);
+    float4* dst = reinterpret_cast<float4*>(cpx + (long long)i * 8);
+    dst[0] = make_float4(q[0], q[1], q[2], q[3]);
+    dst[1] = make_float4(q[4], q[5], q[6], q[7]);
+    int r[4];
+    segment_rect(q, stroke, support, pad, aniso, tbx, tby, r);
+    mnx = min(mnx, r[0]); mny = min(mny, r[1]); mxx = max(mxx, r[2]); mxy = max(mxy, r[3]);
+  }
+  mnx = warp_min_i(mnx); mny = warp_min_i(mny); mxx = warp_max_i(mxx); mxy = warp_max_i(mxy);
+  int nseg = s1 - s0;
+  if (nseg <= 0) { mnx = mny = mxx = mxy = 0; }
+  int count = nseg > 0 ? max(0, mxx - mnx) * max(0, mxy - mny) : 0;
+  if (lane == 0) {
+    *reinterpret_cast<int4*>(pr + p * 4) = make_int4(mnx, mny, mxx, mxy);
+    hits[p] = count;
+  }
+  // flatten
+  const int npts = nseg * S;
+  for (int q = lane; q < npts; q += 32) {
+    int si = q / S;
+    int s = q - si * S;
+    long long seg = s0 + si;
+    float c[8], pp[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) c[k] = cn[seg * 8 + k];
+    project_points(c, half_w, half_h, pp);
+    float x, y;
+    bernstein_point(pp, basis, S, s, x, y);
+    store_point(edges, seg, S, s, x, y);
+  }
+  // per-tile counts inside the band
+  int y0 = max(mny, r0), y1 = min(mxy, r1);
+  int wdt = mxx - mnx, hgt = y1 - y0;
+  if (wdt > 0 && hgt > 0) {
+    for (int q = lane; q < wdt * hgt; q += 32) {
+      int rr = q / wdt, cc = q - rr * wdt;
+      atomicAdd(tile_counts + (long long)(y0 + rr) * tbx + mnx + cc, 1);
+    }
+  }
+}
+
+// Exclusive scan of per-tile counts into tile ranges; one CTA of 1024.
+__global__ void __launch_bounds__(1024) bin_scan_kernel(const int* __restrict__ counts,
+                                                        int* __restrict__ bins,
+                                                        int* __restrict__ cursor,
+                                                        int* __restrict__ total,
+                                                        int* __restrict__ status, long long nt,
+                                                        long long capacity) {
+  __shared__ int warp_tot[32];
+  __shared__ long long s_total;
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const long long chunk = (nt + 1023) / 1024;
+  const long long b = tid * chunk, e = min(nt, b + chunk);
+  int local = 0;
+  for (long long i = b; i < e; ++i) local += counts[i];
+  int incl = warp_incl_scan(local, lane);
+  if (lane == 31) warp_tot[wid] = incl;
+  __syncthreads();
+  if (wid == 0) {
+    int v = warp_tot[lane];
+    int vi = warp_incl_scan(v, lane);
+    warp_tot[lane] = vi - v;
+    if (lane == 31) {
+      s_total = vi;
+      *total = vi;
+      if (vi > capacity && status) *status = CS_ERR_CAPACITY;
+    }
+  }
+  __syncthreads();
+  const bool overflow = s_total > capacity;
+  int run = warp_tot[wid] + incl - local;
+  for (long long i = b; i < e; ++i) {
+    int c = overflow ? 0 : counts[i];
+    cursor[i] = run;
+    if (c > 0) {
+      bins[2 * i] = run;
+      bins[2 * i + 1] = run + c;
+    } else {
+      bins[2 * i] = 0;
+      bins[2 * i + 1] = 0;
+    }
+    run += c;
+  }
+}
+
+// One warp per primitive: scatter (depth key << 32 | primitive id) into the
+// primitive's tiles' ranges (unordered within a tile).
+__global__ void __launch_bounds__(256) bin_scatter_kernel(
+    const int* __restrict__ pr, const float* __restrict__ depths, int* __restrict__ cursor,
+    unsigned long long* __restrict__ pairs, int* __restrict__ status, long long np, int tbx,
+    long long capacity, int r0, int r1) {
+  long long p = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  int lane = threadIdx.x & 31;
+  if (p >= np) return;
+  int4 r = *reinterpret_cast<const int4*>(pr + p * 4);
+  int y0 = max(r.y, r0), y1 = min(r.w, r1);
+  int wdt = r.z - r.x, hgt = y1 - y0;
+  if (wdt <= 0 || hgt <= 0) return;
+  unsigned long long v = ((unsigned long long)depth_sort_key(depths[p]) << 32) | (unsigned)p;
+  for (int q = lane; q < wdt * hgt; q += 32) {
+    int rr = q / wdt, cc = q - rr * wdt;
+    int slot = atomicAdd(cursor + (long long)(y0 + rr) * tbx + r.x + cc, 1);
+    if (slot < capacity) {
+      pairs[slot] = v;
+    } else if (status) {
+      *status = CS_ERR_CAPACITY;
+    }
+  }
+}
+
+constexpr int kSortThreads = 128;
+constexpr int kSortSmem = 4096;
+
+__device__ __forceinline__ void emit_sorted(unsigned long long v, long long tile, long long pos,
+                                            int* __restrict__ pids, long long* __restrict__ ids) {
+  pids[pos] = (int)(v & 0xffffffffull);
+  if (ids) ids[pos] = (long long)(((unsigned long long)tile << 32) | (v >> 32));
+}
+
+// One CTA per tile: sort the tile's pairs ascending and emit primitive ids and
+// reference-format intersect ids.  Pairs are unique (one per primitive), so
+// the order is total.
+__global__ void __launch_bounds__(kSortThreads) bin_tile_sort_kernel(
+    const int* __restrict__ bins, const float* __restrict__ depths,
+    unsigned long long* __restrict__ pairs, int* __restrict__ pids, long long* __restrict__ ids,
+    const int* __restrict__ total, long long capacity, int tbx, int r0) {
+  __shared__ unsigned long long s[kSortSmem];
+  const long long tile = (long long)(r0 + blockIdx.y) * tbx + blockIdx.x;
+  const int start = bins[2 * tile], end = bins[2 * tile + 1];
+  const int n = end - start;
+  if (n <= 0) return;
+  if (*total > capacity) return;  // overflow: the pairs were not all written
+  const int tid = threadIdx.x, lane = tid & 31;
+  if (n <= 32) {
+    if (tid >= 32) return;
+    unsigned long long v = lane < n ? pairs[start + lane] : ~0ull;
+#pragma unroll
+    for (int k = 2; k <= 32; k <<= 1) {
+#pragma unroll
+      for (int j = k >> 1; j > 0; j >>= 1) {
+        unsigned long long o = __shfl_xor_sync(0xffffffffu, v, j);
+        bool up = (lane & k) == 0;
+        bool lower = (lane & j) == 0;
+        v = (lower == up) ? min(v, o) : max(v, o);
+      }
+    }
+    if (lane < n) emit_sorted(v, tile, start + lane, pids, ids);
+    return;
+  }
+  if (n <= kSortSmem) {
+    int m = 64;
+    while (m < n) m <<= 1;
+    for (int i = tid; i < m; i += kSortThreads) s[i] = i < n ? pairs[start + i] : ~0ull;
+    __syncthreads();
+    for (int k = 2; k <= m; k <<= 1) {
+      for (int j = k >> 1; j > 0; j >>= 1) {
+        for (int i = tid; i < m; i += kSortThreads) {
+          int ixj = i ^ j;
+          if (ixj > i) {
+            unsigned long long a = s[i], b = s[ixj];
+            bool asc = (i & k) == 0;
+            if ((a > b) == asc) { s[i] = b; s[ixj] = a; }
+          }
+        }
+        __syncthreads();
+      }
+    }
+    for (int i = tid; i < n; i += kSortThreads) emit_sorted(s[i], tile, start + i, pids, ids);
+    return;
+  }
+  // Large tile: rank each pair by counting smaller pairs (all distinct), then
+  // rebuild the keys from the depths.
+  for (int i = tid; i < n; i += kSortThreads) {
+    unsigned long long v = pairs[start + i];
+    int rank = 0;
+    for (int j = 0; j < n; ++j) rank += pairs[start + j] < v;
+    pids[start + rank] = (int)(v & 0xffffffffull);
+  }
+  __syncthreads();
+  if (ids) {
+    for (int i = tid; i < n; i += kSortThreads) {
+      int p = pids[start + i];
+      ids[start + i] =
+          (long long)(((unsigned long long)tile << 32) | (unsigned long long)depth_sort_key(depths[p]));
+    }
+  }
+}
+
+}  // namespace cs
+
+using namespace cs;
+
+extern "C" {
+
+const char* cs_version(void) { return "cubicsplat_b200 0.1.0 sm_100a"; }
+
+int cs_project_cubics(const float* cubics_norm, const float* stroke_widths,
+                      const float* support_radii, float* cubics_px, int32_t* tile_ranges,
+                      int32_t* num_tiles_hit, int64_t num_curves, int32_t img_height,
+                      int32_t img_width, int32_t block_x, int32_t block_y, float aabb_pad,
+                      int32_t aniso, void* stream) {
+  if (block_x != kTile || block_y != kTile) return CS_ERR_UNSUPPORTED;
+  if (num_curves < 0 || img_height <= 0 || img_width <= 0) return CS_ERR_ARG;
+  if (num_curves == 0) return CS_OK;
+  int tbx = (img_width + kTile - 1) / kTile, tby = (img_height + kTile - 1) / kTile;
+  project_kernel<<<ceil_div(num_curves, 256), 256, 0, (cudaStream_t)stream>>>(
+      cubics_norm, stroke_widths, support_radii, cubics_px, tile_ranges, num_tiles_hit,
+      num_curves, 0.5f * (float)img_width, 0.5f * (float)img_height, aabb_pad, aniso, tbx, tby);
+  return launch_status();
+}
+
+int cs_flatten_bernstein(const float* cubics_px, const float* basis, float* edges_px,
+                         int64_t num_segments, int32_t samples, void* stream) {
+  if (samples < 2 || num_segments < 0) return CS_ERR_ARG;
+  if (num_segments == 0) return CS_OK;
+  long long n = num_segments * samples;
+  flatten_kernel<<<ceil_div(n, 256), 256, 0, (cudaStream_t)stream>>>(cubics_px, basis, edges_px,
+                                                                     num_segments, samples);
+  return launch_status();
+}
+
+int cs_primitive_tile_ranges(const int32_t* seg_tile_ranges, const int32_t* prim_seg_offsets,
+                             int32_t* prim_tile_ranges, int32_t* num_tiles_hit,
+                             int64_t num_primitives, int32_t tile_bound_x, int32_t tile_bound_y,
+                             void* stream) {
+  if (num_primitives < 0) return CS_ERR_ARG;
+  if (num_primitives == 0) return CS_OK;
+  prim_ranges_kernel<<<ceil_div(num_primitives, 256), 256, 0, (cudaStream_t)stream>>>(
+      seg_tile_ranges, prim_seg_offsets, prim_tile_ranges, num_tiles_hit, num_primitives,
+      tile_bound_x, tile_bound_y);
+  return launch_status();
+}
+
+int cs_map_cubic_to_intersects(const int32_t* tile_ranges, const float* depths,
+                               const int32_t* cum_tiles_hit, int64_t* isect_ids,
+                               int32_t* prim_ids, int64_t num_primitives, int32_t tile_bound_x,
+                               void* stream) {
+  if (num_primitives < 0) return CS_ERR_ARG;
+  if (num_primitives == 0) return CS_OK;
+  map_kernel<<<ceil_div(num_primitives * 32, 256), 256, 0, (cudaStream_t)stream>>>(
+      tile_ranges, depths, cum_tiles_hit, reinterpret_cast<long long*>(isect_ids), prim_ids,
+      num_primitives, tile_bound_x);
+  return launch_status();
+}
+
+int cs_tile_bin_edges(const int64_t* isect_ids_sorted, int64_t num_intersects,
+                      int32_t* tile_bins, int64_t num_tiles, void* stream) {
+  if (num_intersects < 0 || num_tiles <= 0) return CS_ERR_ARG;
+  cudaMemsetAsync(tile_bins, 0, sizeof(int32_t) * 2 * num_tiles, (cudaStream_t)stream);
+  if (num_intersects == 0) return launch_status();
+  tile_bins_kernel<<<ceil_div(num_intersects, 256), 256, 0, (cudaStream_t)stream>>>(
+      reinterpret_cast<const long long*>(isect_ids_sorted), num_intersects, tile_bins);
+  return launch_status();
+}
+
+int cs_isect_edge_ranges(const int32_t* prim_ids_sorted, const int32_t* prim_edge_offsets,
+                         int32_t* isect_edge_ranges, int64_t num_intersects, void* stream) {
+  if (num_intersects < 0) return CS_ERR_ARG;
+  if (num_intersects == 0) return CS_OK;
+  edge_ranges_kernel<<<ceil_div(num_intersects, 256), 256, 0, (cudaStream_t)stream>>>(
+      prim_ids_sorted, prim_edge_offsets, isect_edge_ranges, num_intersects);
+  return launch_status();
+}
+
+size_t cs_bin_workspace_size(int64_t num_tiles) {
+  return align256(sizeof(int) * num_tiles) * 2;
+}
+
+int cs_bin_count(const float* cubics_norm, const int32_t* prim_seg_offsets, const float* aa_widths,
+                 const float* stroke_widths, const float* basis, float* cubics_px,
+                 float* edges_px, int32_t* prim_tile_ranges, int32_t* num_tiles_hit,
+                 int32_t* tile_bins, int32_t* num_intersects, int32_t* status, void* workspace,
+                 int64_t num_primitives, int64_t num_segments, int64_t capacity, int32_t samples,
+                 int32_t img_height, int32_t img_width, int32_t tile_row_begin,
+                 int32_t tile_row_end, float aabb_pad, int32_t aniso, void* stream) {
+  if (num_primitives < 0 || samples < 2 || img_height <= 0 || img_width <= 0 || !workspace)
+    return CS_ERR_ARG;
+  cudaStream_t st = (cudaStream_t)stream;
+  const int tbx = (img_width + kTile - 1) / kTile, tby = (img_height + kTile - 1) / kTile;
+  const long long nt = (long long)tbx * tby;
+  const int r0 = max(0, tile_row_begin), r1 = min(tby, tile_row_end);
+  BinWorkspace ws = bin_ws(workspace, nt);
+  cudaMemsetAsync(ws.tile_counts, 0, sizeof(int) * nt, st);
+  if (num_primitives > 0) {
+    bin_prep_kernel<<<ceil_div(num_primitives * 32, 256), 256, 0, st>>>(
+        cubics_norm, prim_seg_offsets, aa_widths, stroke_widths, basis, cubics_px, edges_px,
+        prim_tile_ranges, num_tiles_hit, ws.tile_counts, status, num_primitives, num_segments,
+        samples,
+        0.5f * (float)img_width, 0.5f * (float)img_height, tbx, tby, r0, r1, aabb_pad, aniso);
+  }
+  bin_scan_kernel<<<1, 1024, 0, st>>>(ws.tile_counts, tile_bins, ws.cursor, num_intersects,
+                                      status, nt, capacity < 0 ? 0 : capacity);
+  return launch_status();
+}
+
+int cs_bin_sort(const int32_t* prim_tile_ranges, const float* depths, const int32_t* tile_bins,
+                const int32_t* num_intersects, int32_t* prim_ids_sorted, int64_t* isect_ids_sorted,
+                int32_t* status, void* workspace, int64_t num_primitives, int64_t capacity,
+                int32_t img_height, int32_t img_width, int32_t tile_row_begin,
+                int32_t tile_row_end, void* stream) {
+  if (num_primitives < 0 || capacity < 0 || !workspace || !isect_ids_sorted) return CS_ERR_ARG;
+  cudaStream_t st = (cudaStream_t)stream;
+  const int tbx = (img_width + kTile - 1) / kTile, tby = (img_height + kTile - 1) / kTile;
+  const long long nt = (long long)tbx * tby;
+  const int r0 = max(0, tile_row_begin), r1 = min(tby, tile_row_end);
+  if (r1 <= r0 || num_primitives == 0 || capacity == 0) return CS_OK;
+  BinWorkspace ws = bin_ws(workspace, nt);
+  unsigned long long* pairs = reinterpret_cast<unsigned long long*>(isect_ids_sorted);
+  bin_scatter_kernel<<<ceil_div(num_primitives * 32, 256), 256, 0, st>>>(
+      prim_tile_ranges, depths, ws.cursor, pairs, status, num_primitives, tbx, capacity, r0, r1);
+  dim3 grid(tbx, r1 - r0);
+  bin_tile_sort_kernel<<<grid, kSortThreads, 0, st>>>(tile_bins, depths, pairs, prim_ids_sorted,
+                                                     reinterpret_cast<long long*>(isect_ids_sorted),
+                                                     num_intersects, capacity, tbx, r0);
+  return launch_status();
+}
+
+}  // extern "C"

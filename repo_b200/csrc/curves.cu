@@ -1,0 +1,163 @@
+// Cubic-domain kernels: edge-gradient accumulation onto cubic control points
+// and the closed control-polygon -> ring-of-cubics conversion (sm_100a).
+#include "cs_common.cuh"
+
+namespace cs {
+
+// v_P_k = sum_e gs_e B_k(e/E) + ge_e B_k((e+1)/E), in the reference's
+// summation order (manbo/ops/cubic_splatting.py:2338-2394), then an optional
+// per-axis scale (the normalised-space epilogue, :3096-3100).
+__global__ void edge_grads_kernel(const float4* __restrict__ v_edges, float* __restrict__ v_cubics,
+                                  long long nseg, int E, float sx, float sy) {
+  long long sid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (sid >= nseg) return;
+  const float inv_e = 1.0f / (float)E;
+  float a00 = 0.f, a01 = 0.f, a10 = 0.f, a11 = 0.f, a20 = 0.f, a21 = 0.f, a30 = 0.f, a31 = 0.f;
+  for (int e = 0; e < E; ++e) {
+    float t0 = (float)e * inv_e, t1 = (float)(e + 1) * inv_e;
+    float o0 = 1.0f - t0, o1 = 1.0f - t1;
+    float o0s = o0 * o0, o1s = o1 * o1, t0s = t0 * t0, t1s = t1 * t1;
+    float b00 = o0s * o0, b01 = 3.0f * o0s * t0, b02 = 3.0f * o0 * t0s, b03 = t0s * t0;
+    float b10 = o1s * o1, b11 = 3.0f * o1s * t1, b12 = 3.0f * o1 * t1s, b13 = t1s * t1;
+    float4 g = v_edges[sid * E + e];
+    a00 = a00 + g.x * b00 + g.z * b10;
+    a01 = a01 + g.y * b00 + g.w * b10;
+    a10 = a10 + g.x * b01 + g.z * b11;
+    a11 = a11 + g.y * b01 + g.w * b11;
+    a20 = a20 + g.x * b02 + g.z * b12;
+    a21 = a21 + g.y * b02 + g.w * b12;
+    a30 = a30 + g.x * b03 + g.z * b13;
+    a31 = a31 + g.y * b03 + g.w * b13;
+  }
+  float4* out = reinterpret_cast<float4*>(v_cubics + sid * 8);
+  if (sx == 1.0f && sy == 1.0f) {
+    out[0] = make_float4(a00, a01, a10, a11);
+    out[1] = make_float4(a20, a21, a30, a31);
+  } else {
+    out[0] = make_float4(a00 * sx, a01 * sy, a10 * sx, a11 * sy);
+    out[1] = make_float4(a20 * sx, a21 * sy, a30 * sx, a31 * sy);
+  }
+}
+
+// Closed K-point control polygon -> two degree-(K/2) Bernstein branches ->
+// `subdiv` Hermite cubics per branch (manbo/ops/cubic_splatting.py:190-266).
+__global__ void ring_forward_kernel(const float* __restrict__ cp, const float* __restrict__ basis,
+                                    const float* __restrict__ dbasis, const float* __restrict__ dt,
+                                    float* __restrict__ out, long long nseg, int K, int sub) {
+  long long sid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (sid >= nseg) return;
+  const int kb = (K + 2) / 2, spc = 2 * sub;
+  const float degree = (float)(kb - 1), third = (float)(1.0 / 3.0);
+  long long curve = sid / spc;
+  int local = (int)(sid - curve * spc);
+  int branch = local / sub, s = local - branch * sub, sn = s + 1;
+  int base = branch * (kb - 1);
+  const float* c = cp + curve * K * 2;
+  float p0x = 0.f, p0y = 0.f, p3x = 0.f, p3y = 0.f, d0x = 0.f, d0y = 0.f, d1x = 0.f, d1y = 0.f;
+  for (int i = 0; i < kb; ++i) {
+    int idx = base + i;
+    if (idx >= K) idx -= K;
+    float w0 = basis[s * kb + i], w1 = basis[sn * kb + i];
+    float x = c[2 * idx], y = c[2 * idx + 1];
+    p0x = p0x + w0 * x; p0y = p0y + w0 * y;
+    p3x = p3x + w1 * x; p3y = p3y + w1 * y;
+  }
+  for (int i = 0; i < kb - 1; ++i) {
+    int ic = base + i, in = ic + 1;
+    if (ic >= K) ic -= K;
+    if (in >= K) in -= K;
+    float dx = c[2 * in] - c[2 * ic], dy = c[2 * in + 1] - c[2 * ic + 1];
+    float db0 = dbasis[s * (kb - 1) + i], db1 = dbasis[sn * (kb - 1) + i];
+    d0x = d0x + db0 * dx; d0y = d0y + db0 * dy;
+    d1x = d1x + db1 * dx; d1y = d1y + db1 * dy;
+  }
+  d0x = d0x * degree; d0y = d0y * degree; d1x = d1x * degree; d1y = d1y * degree;
+  float dts = dt[s] * third;
+  float* o = out + sid * 8;
+  o[0] = p0x; o[1] = p0y; o[6] = p3x; o[7] = p3y;
+  o[2] = p0x + d0x * dts; o[3] = p0y + d0y * dts;
+  o[4] = p3x - d1x * dts; o[5] = p3y - d1y * dts;
+}
+
+// Adjoint of ring_forward_kernel with atomics into the control points
+// (manbo/ops/cubic_splatting.py:321-395).
+__global__ void ring_backward_kernel(const float* __restrict__ gseg, const float* __restrict__ basis,
+                                     const float* __restrict__ dbasis, const float* __restrict__ dt,
+                                     float* __restrict__ gcp, long long nseg, int K, int sub) {
+  long long sid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (sid >= nseg) return;
+  const int kb = (K + 2) / 2, spc = 2 * sub;
+  const float degree = (float)(kb - 1), third = (float)(1.0 / 3.0);
+  long long curve = sid / spc;
+  int local = (int)(sid - curve * spc);
+  int branch = local / sub, s = local - branch * sub, sn = s + 1;
+  int base = branch * (kb - 1);
+  float dts = dt[s] * third;
+  const float* g = gseg + sid * 8;
+  float g0x = g[0] + g[2], g0y = g[1] + g[3];
+  float g3x = g[6] + g[4], g3y = g[7] + g[5];
+  float gd0x = g[2] * dts, gd0y = g[3] * dts;
+  float gd1x = -g[4] * dts, gd1y = -g[5] * dts;
+  float* gc = gcp + curve * K * 2;
+  for (int i = 0; i < kb; ++i) {
+    int idx = base + i;
+    if (idx >= K) idx -= K;
+    float w0 = basis[s * kb + i], w1 = basis[sn * kb + i];
+    atomicAdd(gc + 2 * idx, g0x * w0 + g3x * w1);
+    atomicAdd(gc + 2 * idx + 1, g0y * w0 + g3y * w1);
+  }
+  for (int i = 0; i < kb - 1; ++i) {
+    int ic = base + i, in = ic + 1;
+    if (ic >= K) ic -= K;
+    if (in >= K) in -= K;
+    float db0 = dbasis[s * (kb - 1) + i], db1 = dbasis[sn * (kb - 1) + i];
+    float dcx = degree * (gd0x * db0 + gd1x * db1);
+    float dcy = degree * (gd0y * db0 + gd1y * db1);
+    atomicAdd(gc + 2 * ic, -dcx);
+    atomicAdd(gc + 2 * ic + 1, -dcy);
+    atomicAdd(gc + 2 * in, dcx);
+    atomicAdd(gc + 2 * in + 1, dcy);
+  }
+}
+
+}  // namespace cs
+
+using namespace cs;
+
+extern "C" {
+
+int cs_edge_grads_to_cubics(const float* v_edges, float* v_cubics, int64_t num_segments,
+                            int32_t edges_per_segment, float scale_x, float scale_y,
+                            void* stream) {
+  if (num_segments < 0 || edges_per_segment <= 0) return CS_ERR_ARG;
+  if (num_segments == 0) return CS_OK;
+  edge_grads_kernel<<<ceil_div(num_segments, 128), 128, 0, (cudaStream_t)stream>>>(
+      reinterpret_cast<const float4*>(v_edges), v_cubics, num_segments, edges_per_segment,
+      scale_x, scale_y);
+  return launch_status();
+}
+
+int cs_ring_segments_forward(const float* control_points, const float* basis,
+                             const float* deriv_basis, const float* dt, float* segments,
+                             int64_t num_curves, int32_t k, int32_t subdiv, void* stream) {
+  if (num_curves < 0 || k < 4 || (k - 2) % 2 != 0 || subdiv <= 0) return CS_ERR_ARG;
+  long long n = num_curves * 2LL * subdiv;
+  if (n == 0) return CS_OK;
+  ring_forward_kernel<<<ceil_div(n, 256), 256, 0, (cudaStream_t)stream>>>(
+      control_points, basis, deriv_basis, dt, segments, n, k, subdiv);
+  return launch_status();
+}
+
+int cs_ring_segments_backward(const float* grad_segments, const float* basis,
+                              const float* deriv_basis, const float* dt,
+                              float* grad_control_points, int64_t num_curves, int32_t k,
+                              int32_t subdiv, void* stream) {
+  if (num_curves < 0 || k < 4 || (k - 2) % 2 != 0 || subdiv <= 0) return CS_ERR_ARG;
+  long long n = num_curves * 2LL * subdiv;
+  if (n == 0) return CS_OK;
+  ring_backward_kernel<<<ceil_div(n, 256), 256, 0, (cudaStream_t)stream>>>(
+      grad_segments, basis, deriv_basis, dt, grad_control_points, n, k, subdiv);
+  return launch_status();
+}
+
+}  // extern "C"

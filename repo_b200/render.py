@@ -1,0 +1,587 @@
+"""Host side of the B200 cubic renderer: binning, autograd functions, entry points.
+
+Mirrors the reference's operator API for the hot path
+(``render_cubic_fill_splat_tilelang``, manbo/ops/cubic_splatting.py:3128-3229;
+``render_cubic_polyline_splat_tilelang``, manbo/ops/cubic_polyline_splatting.py:1341-1432)
+with the same argument meaning, validation messages, empty-scene behaviour and
+``process_fn`` hook stages.  All device work runs in the sm_100a kernels behind
+the C ABI (``repo_b200._native``); there is no CPU path.
+
+Differences from the reference, by design:
+  * binning is the fused count -> scan -> scatter -> per-tile sort pipeline,
+    which costs one host synchronisation per forward (to size the intersect
+    list) instead of the reference's three or more;
+  * ties in depth are ordered by primitive id (the order of a stable sort of
+    the reference's keys).
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Any, Callable, Mapping, MutableMapping, Optional
+
+import torch
+
+from . import _native as nat
+
+BLOCK_X = 16
+BLOCK_Y = 16
+DEFAULT_THREADS = 256
+DEFAULT_AABB_PAD = 1.0
+DEFAULT_AA_WIDTH = 1.0
+DEFAULT_DISTANCE_SAMPLES = 24
+CUBIC_FLATTEN_METHOD_BERNSTEIN = "bernstein"
+CUBIC_FLATTEN_METHOD_DE_CASTELJAU = "de_casteljau"
+DEFAULT_CUBIC_FLATTEN_METHOD = CUBIC_FLATTEN_METHOD_BERNSTEIN
+_FLATTEN_ALIASES = {
+    "bernstein": CUBIC_FLATTEN_METHOD_BERNSTEIN,
+    "de_casteljau": CUBIC_FLATTEN_METHOD_DE_CASTELJAU,
+    "decasteljau": CUBIC_FLATTEN_METHOD_DE_CASTELJAU,
+    "de-casteljau": CUBIC_FLATTEN_METHOD_DE_CASTELJAU,
+}
+INT64_MAX = (1 << 63) - 1
+
+CubicProcessPayload = MutableMapping[str, Any]
+CubicProcessFn = Callable[[str, CubicProcessPayload], Optional[Mapping[str, Any]]]
+
+
+def normalize_cubic_flatten_method(method: object) -> str:
+    raw = str(method).strip().lower()
+    key = _FLATTEN_ALIASES.get(raw, raw)
+    if key not in (CUBIC_FLATTEN_METHOD_BERNSTEIN, CUBIC_FLATTEN_METHOD_DE_CASTELJAU):
+        raise ValueError(
+            "flatten_method must be one of "
+            f"{sorted(_FLATTEN_ALIASES.keys())}, got {method!r}")
+    return key
+
+
+def _run_process_fn(process_fn, stage, payload):
+    if process_fn is None:
+        return payload
+    updates = process_fn(stage, payload)
+    if updates:
+        payload.update(updates)
+    return payload
+
+
+def _f32(t: torch.Tensor) -> torch.Tensor:
+    if t.dtype == torch.float32:
+        return t if t.is_contiguous() else t.contiguous()
+    return t.contiguous().to(torch.float32)
+
+
+def _i32(t: torch.Tensor) -> torch.Tensor:
+    if t.dtype == torch.int32:
+        return t if t.is_contiguous() else t.contiguous()
+    return t.contiguous().to(torch.int32)
+
+
+_BASIS_CACHE: dict = {}
+
+
+def bernstein_basis(samples: int, device: torch.device) -> torch.Tensor:
+    """[4, S] cubic Bernstein weights at linspace(0, 1, S), computed with torch on
+    the host exactly as the reference writes them (cubic_splatting.py:1710-1716)."""
+    s = max(2, int(samples))
+    key = (s, str(device))
+    b = _BASIS_CACHE.get(key)
+    if b is None:
+        t = torch.linspace(0.0, 1.0, s, dtype=torch.float32)
+        omt = 1.0 - t
+        b = torch.stack([omt * omt * omt, 3.0 * omt * omt * t, 3.0 * omt * t * t, t * t * t], 0)
+        b = b.contiguous().to(device)
+        _BASIS_CACHE[key] = b
+    return b
+
+
+def tile_bounds_for(img_h: int, img_w: int) -> tuple[int, int, int]:
+    return ((int(img_w) + BLOCK_X - 1) // BLOCK_X, (int(img_h) + BLOCK_Y - 1) // BLOCK_Y, 1)
+
+
+def _check_block(block_x: int, block_y: int) -> None:
+    if int(block_x) != BLOCK_X or int(block_y) != BLOCK_Y:
+        raise ValueError(f"the B200 renderer uses 16x16 tiles, got block {block_x}x{block_y}")
+
+
+@dataclass
+class Binning:
+    cubics_px: torch.Tensor
+    edges_px: torch.Tensor
+    prim_edge_offsets: torch.Tensor
+    prim_tile_ranges: torch.Tensor
+    num_tiles_hit: torch.Tensor
+    tile_bins: torch.Tensor
+    prim_ids_sorted: torch.Tensor
+    isect_ids_sorted: torch.Tensor
+    num_intersects: int
+    tile_bounds: tuple
+    samples: int
+    tile_rows: tuple
+
+
+def bin_primitives(cubics_norm: torch.Tensor, offs: torch.Tensor, depths: torch.Tensor,
+                   aa_widths: torch.Tensor, img_h: int, img_w: int, samples: int, *,
+                   stroke_widths: Optional[torch.Tensor] = None, aabb_pad: float = DEFAULT_AABB_PAD,
+                   aniso: bool = False, tile_rows: Optional[tuple] = None) -> Binning:
+    """Project, bound, flatten and bin all primitives (fused B200 pipeline).
+
+    Output semantics equal the reference's K3 + flatten + K4 + cumsum + K5 +
+    sort + K6 (cubic_splatting.py:2815-2908): tile_bins [T, 2] of [start, end)
+    ranges into prim_ids_sorted / isect_ids_sorted, front (small depth) first.
+    """
+    dev = cubics_norm.device
+    s = max(2, int(samples))
+    g = int(cubics_norm.shape[0])
+    p = int(offs.numel()) - 1
+    tbx, tby, _ = tile_bounds_for(img_h, img_w)
+    nt = tbx * tby
+    r0, r1 = (0, tby) if tile_rows is None else (int(tile_rows[0]), int(tile_rows[1]))
+    cubics_px = torch.empty((g, 4, 2), dtype=torch.float32, device=dev)
+    edges = torch.empty((g * (s - 1), 2, 2), dtype=torch.float32, device=dev)
+    prim_ranges = torch.empty((p, 4), dtype=torch.int32, device=dev)
+    num_hit = torch.empty((p,), dtype=torch.int32, device=dev)
+    tile_bins = torch.empty((nt, 2), dtype=torch.int32, device=dev)
+    counters = torch.zeros((2,), dtype=torch.int32, device=dev)  # [num_intersects, status]
+    ws = torch.empty((int(nat.call("cs_bin_workspace_size", nt)),), dtype=torch.uint8, device=dev)
+    st = nat.stream(dev)
+    cn = _f32(cubics_norm)
+    aw = _f32(aa_widths)
+    sw = None if stroke_widths is None else _f32(stroke_widths)
+    basis = bernstein_basis(s, dev)
+    nat.check(nat.call("cs_bin_count", nat.ptr(cn), nat.ptr(offs), nat.ptr(aw), nat.ptr(sw),
+                       nat.ptr(basis), nat.ptr(cubics_px), nat.ptr(edges), nat.ptr(prim_ranges),
+                       nat.ptr(num_hit), nat.ptr(tile_bins), counters.data_ptr(),
+                       counters.data_ptr() + 4, ws.data_ptr(), p, g, INT64_MAX, s, int(img_h),
+                       int(img_w), r0, r1, float(aabb_pad), int(bool(aniso)), st), "cs_bin_count")
+    # the one host synchronisation of the forward: intersect count + status
+    n_isect, status = (int(v) for v in counters.tolist())
+    if status == nat.CS_ERR_ARG:
+        o = offs.detach().to("cpu")
+        raise ValueError(
+            "primitive_seg_offsets must start at 0 and end at num_segments "
+            f"(got start={int(o[0])}, end={int(o[-1])}, num_segments={g}) and be non-decreasing")
+    nat.check(status, "cs_bin_count")
+    prim_sorted = torch.empty((n_isect,), dtype=torch.int32, device=dev)
+    isect_sorted = torch.empty((n_isect,), dtype=torch.int64, device=dev)
+    if n_isect > 0:
+        nat.check(nat.call("cs_bin_sort", nat.ptr(prim_ranges), nat.ptr(_f32(depths)),
+                           nat.ptr(tile_bins), counters.data_ptr(), nat.ptr(prim_sorted),
+                           nat.ptr(isect_sorted), counters.data_ptr() + 4, ws.data_ptr(), p,
+                           n_isect, int(img_h), int(img_w), r0, r1, st), "cs_bin_sort")
+    edge_offs = (offs.to(torch.int64) * (s - 1)).to(torch.int32)
+    return Binning(cubics_px, edges, edge_offs, prim_ranges, num_hit, tile_bins, prim_sorted,
+                   isect_sorted, n_isect, (tbx, tby, 1), s, (r0, r1))
+
+
+def _inv_sigma2(widths: torch.Tensor) -> torch.Tensor:
+    return (1.0 / torch.clamp(widths * widths, min=1e-6)).contiguous()
+
+
+def _zeros_views(dev, *shapes):
+    total = sum(math.prod(sh) for sh in shapes)
+    buf = torch.zeros((max(total, 1),), dtype=torch.float32, device=dev)
+    out, o = [], 0
+    for sh in shapes:
+        n = math.prod(sh)
+        out.append(buf[o:o + n].view(sh))
+        o += n
+    return out
+
+
+def fill_forward_raster(b: Binning, colors, opacities, inv_sigma2s, fill_rules, background,
+                        img_h: int, img_w: int):
+    dev = colors.device
+    out = torch.empty((img_h, img_w, 3), dtype=torch.float32, device=dev)
+    fts = torch.empty((img_h, img_w), dtype=torch.float32, device=dev)
+    fidx = torch.empty((img_h, img_w), dtype=torch.int32, device=dev)
+    if b.num_intersects <= 0:
+        out.copy_(background.view(1, 1, 3).expand(img_h, img_w, 3))
+        fts.fill_(1.0)
+        fidx.fill_(0)
+        return out, fts, fidx
+    nat.check(nat.call("cs_fill_forward", nat.ptr(b.prim_ids_sorted), nat.ptr(b.tile_bins),
+                       nat.ptr(b.edges_px), None, nat.ptr(b.prim_edge_offsets), nat.ptr(colors),
+                       nat.ptr(opacities), nat.ptr(inv_sigma2s), nat.ptr(fill_rules),
+                       nat.ptr(background), nat.ptr(out), nat.ptr(fts), nat.ptr(fidx), img_h,
+                       img_w, b.tile_rows[0], b.tile_rows[1], nat.stream(dev)), "cs_fill_forward")
+    return out, fts, fidx
+
+
+def stroke_forward_raster(b: Binning, colors, opacities, stroke_widths, inv_sigma2s, background,
+                          img_h: int, img_w: int):
+    dev = colors.device
+    out = torch.empty((img_h, img_w, 3), dtype=torch.float32, device=dev)
+    fts = torch.empty((img_h, img_w), dtype=torch.float32, device=dev)
+    fidx = torch.empty((img_h, img_w), dtype=torch.int32, device=dev)
+    if b.num_intersects <= 0:
+        out.copy_(background.view(1, 1, 3).expand(img_h, img_w, 3))
+        fts.fill_(1.0)
+        fidx.fill_(0)
+        return out, fts, fidx
+    nat.check(nat.call("cs_stroke_forward", nat.ptr(b.prim_ids_sorted), nat.ptr(b.tile_bins),
+                       nat.ptr(b.edges_px), None, nat.ptr(b.prim_edge_offsets), nat.ptr(colors),
+                       nat.ptr(opacities), nat.ptr(stroke_widths), nat.ptr(inv_sigma2s),
+                       nat.ptr(background), nat.ptr(out), nat.ptr(fts), nat.ptr(fidx), img_h,
+                       img_w, b.tile_rows[0], b.tile_rows[1], nat.stream(dev)),
+              "cs_stroke_forward")
+    return out, fts, fidx
+
+
+def raster_backward(b: Binning, colors, opacities, inv_sigma2s, fill_rules, stroke_widths,
+                    background, final_ts, final_idx, v_output, img_h, img_w, *,
+                    collect_contrib: bool = False, collect_isect_contrib: bool = False,
+                    out_img=None, target_chw=None, mse_scale=None):
+    """Backward rasteriser.  Returns v_edges, v_colors, v_opacities, v_inv_sigma2s,
+    v_stroke_widths (stroke only), curve_contrib_rgb, curve_isect_contrib."""
+    dev = colors.device
+    p = int(colors.shape[0])
+    ne = int(b.edges_px.shape[0])
+    ni = int(b.num_intersects)
+    stroke = stroke_widths is not None
+    shapes = [(ne, 2, 2), (p, 3), (p,), (p,)]
+    if stroke:
+        shapes.append((p,))
+    if collect_contrib:
+        shapes.append((p, 3))
+    if collect_isect_contrib:
+        shapes.append((ni,))
+    views = _zeros_views(dev, *shapes)
+    v_edges, v_colors, v_opac, v_inv = views[:4]
+    i = 4
+    v_sw = None
+    if stroke:
+        v_sw = views[i]
+        i += 1
+    contrib = None
+    if collect_contrib:
+        contrib = views[i]
+        i += 1
+    icontrib = views[i] if collect_isect_contrib else None
+    if ni > 0 and ne > 0:
+        st = nat.stream(dev)
+        vo = None if v_output is None else _f32(v_output)
+        if not stroke:
+            nat.check(nat.call("cs_fill_backward", nat.ptr(b.prim_ids_sorted), nat.ptr(b.tile_bins),
+                               nat.ptr(b.edges_px), None, nat.ptr(b.prim_edge_offsets),
+                               nat.ptr(colors), nat.ptr(opacities), nat.ptr(inv_sigma2s),
+                               nat.ptr(fill_rules), nat.ptr(background), nat.ptr(final_ts),
+                               nat.ptr(final_idx), nat.ptr(vo), nat.ptr(out_img),
+                               nat.ptr(target_chw), nat.ptr(mse_scale), nat.ptr(v_edges),
+                               nat.ptr(v_colors), nat.ptr(v_opac), nat.ptr(v_inv),
+                               nat.ptr(contrib), nat.ptr(icontrib), img_h, img_w,
+                               b.tile_rows[0], b.tile_rows[1], st), "cs_fill_backward")
+        else:
+            nat.check(nat.call("cs_stroke_backward", nat.ptr(b.prim_ids_sorted),
+                               nat.ptr(b.tile_bins), nat.ptr(b.edges_px), None,
+                               nat.ptr(b.prim_edge_offsets), nat.ptr(colors), nat.ptr(opacities),
+                               nat.ptr(stroke_widths), nat.ptr(inv_sigma2s), nat.ptr(background),
+                               nat.ptr(final_ts), nat.ptr(final_idx), nat.ptr(vo),
+                               nat.ptr(out_img), nat.ptr(target_chw), nat.ptr(mse_scale),
+                               nat.ptr(v_edges), nat.ptr(v_colors), nat.ptr(v_opac),
+                               nat.ptr(v_sw), nat.ptr(v_inv), nat.ptr(contrib),
+                               nat.ptr(icontrib), img_h, img_w, b.tile_rows[0], b.tile_rows[1],
+                               st), "cs_stroke_backward")
+    return v_edges, v_colors, v_opac, v_inv, v_sw, contrib, icontrib
+
+
+def edge_grads_to_cubics(v_edges: torch.Tensor, num_segments: int, samples: int,
+                         scale=(1.0, 1.0)) -> torch.Tensor:
+    dev = v_edges.device
+    e = max(2, int(samples)) - 1
+    out = torch.empty((num_segments, 4, 2), dtype=torch.float32, device=dev)
+    if num_segments > 0:
+        nat.check(nat.call("cs_edge_grads_to_cubics", nat.ptr(v_edges), nat.ptr(out),
+                           int(num_segments), e, float(scale[0]), float(scale[1]),
+                           nat.stream(dev)), "cs_edge_grads_to_cubics")
+    return out
+
+
+# --------------------------------------------------------------------------
+# autograd functions
+
+def _empty_image(bg: torch.Tensor, img_h: int, img_w: int) -> torch.Tensor:
+    return bg.view(1, 1, 3).expand(int(img_h), int(img_w), 3).clone()
+
+
+def _validate_common(num_primitives, num_segments, offs, colors, opacities, depths):
+    if int(colors.shape[0]) != num_primitives:
+        raise ValueError(
+            f"colors first dim must match primitive count ({num_primitives}), got {int(colors.shape[0])}")
+    if int(opacities.reshape(-1).shape[0]) != num_primitives:
+        raise ValueError(
+            f"opacities size must match primitive count ({num_primitives}), got {int(opacities.reshape(-1).shape[0])}")
+    if int(depths.reshape(-1).shape[0]) != num_primitives:
+        raise ValueError(
+            f"depths size must match primitive count ({num_primitives}), got {int(depths.reshape(-1).shape[0])}")
+
+
+class CubicFillSplatFunction(torch.autograd.Function):
+    """Closed-fill renderer (mirrors _CubicFillSplatFunction, cubic_splatting.py:2750-3125)."""
+
+    @staticmethod
+    def forward(ctx, cubics_norm, primitive_seg_offsets, colors, opacities, depths, fill_rules,
+                img_h, img_w, block_x, block_y, background, project_threads, map_threads,
+                aabb_pad, aniso_intersects, aa_widths, distance_samples,
+                flatten_method=DEFAULT_CUBIC_FLATTEN_METHOD, process_fn=None, tile_rows=None):
+        nat.require_cuda(cubics_norm, "cubics_norm")
+        method = normalize_cubic_flatten_method(flatten_method)
+        if method != CUBIC_FLATTEN_METHOD_BERNSTEIN:
+            raise NotImplementedError("de_casteljau flattening is not implemented in the B200 path")
+        _check_block(block_x, block_y)
+        num_segments = int(cubics_norm.shape[0])
+        offs = _i32(primitive_seg_offsets).view(-1)
+        num_primitives = max(0, int(offs.numel()) - 1)
+        bg = background.to(device=cubics_norm.device, dtype=torch.float32).view(3).contiguous()
+        ctx.img_h, ctx.img_w = int(img_h), int(img_w)
+        if num_primitives <= 0:
+            ctx.empty = True
+            return _empty_image(bg, img_h, img_w)
+        _validate_common(num_primitives, num_segments, offs, colors, opacities, depths)
+        if int(fill_rules.reshape(-1).shape[0]) != num_primitives:
+            raise ValueError(
+                f"fill_rules size must match primitive count ({num_primitives}), got {int(fill_rules.reshape(-1).shape[0])}")
+        widths = aa_widths.to(device=cubics_norm.device, dtype=torch.float32).reshape(-1)
+        if int(widths.numel()) != num_primitives:
+            raise ValueError(
+                f"aa_widths size must match primitive count ({num_primitives}), got {int(widths.numel())}")
+        widths = torch.clamp(_f32(widths), min=1e-4)
+        inv_s2 = _inv_sigma2(widths)
+        b = bin_primitives(cubics_norm, offs, depths.reshape(-1), widths, int(img_h), int(img_w),
+                           int(distance_samples), aabb_pad=float(aabb_pad),
+                           aniso=bool(aniso_intersects), tile_rows=tile_rows)
+        if b.num_intersects <= 0:
+            ctx.empty = True
+            return _empty_image(bg, img_h, img_w)
+        col = _f32(colors)
+        op = _f32(opacities).view(-1)
+        rules = _i32(fill_rules).view(-1)
+        out, fts, fidx = fill_forward_raster(b, col, op, inv_s2, rules, bg, int(img_h), int(img_w))
+        ctx.empty = False
+        ctx.binning = b
+        ctx.process_fn = process_fn
+        ctx.num_segments = num_segments
+        ctx.save_for_backward(cubics_norm, offs, col, op, rules, widths, inv_s2, bg, fts, fidx)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        nones = (None,) * 20
+        if getattr(ctx, "empty", False):
+            return nones
+        cubics_norm, offs, colors, opac, rules, widths, inv_s2, bg, fts, fidx = ctx.saved_tensors
+        b: Binning = ctx.binning
+        process_fn = ctx.process_fn
+        pre = _run_process_fn(process_fn, "pre_backward_rasterize", {
+            "collect_curve_contrib_rgb": False,
+            "collect_curve_isect_contrib": False,
+            "num_primitives": int(colors.shape[0]),
+            "colors": colors,
+        })
+        cc = bool(pre.get("collect_curve_contrib_rgb", False))
+        ci = bool(pre.get("collect_curve_isect_contrib", False))
+        v_edges, v_colors, v_opac, v_inv, _, contrib, icontrib = raster_backward(
+            b, colors, opac, inv_s2, rules, None, bg, fts, fidx, grad_out, ctx.img_h, ctx.img_w,
+            collect_contrib=cc, collect_isect_contrib=ci)
+        half_w, half_h = 0.5 * float(ctx.img_w), 0.5 * float(ctx.img_h)
+        if process_fn is None:
+            v_cubics_norm = edge_grads_to_cubics(v_edges, ctx.num_segments, b.samples,
+                                                 (half_w, half_h))
+        else:
+            v_cubics_px = edge_grads_to_cubics(v_edges, ctx.num_segments, b.samples)
+            post = _run_process_fn(process_fn, "post_backward_rasterize", {
+                "v_cubics_px": v_cubics_px, "v_colors": v_colors, "v_opacity": v_opac,
+                "curve_contrib_rgb": contrib, "curve_isect_contrib": icontrib,
+                "primitive_ids_sorted": b.prim_ids_sorted, "tile_bins": b.tile_bins,
+                "colors": colors, "opacities": opac, "primitive_seg_offsets": offs,
+            })
+            v_cubics_px = post["v_cubics_px"]
+            v_colors = post["v_colors"]
+            v_opac = post["v_opacity"]
+            v_cubics_norm = torch.empty_like(cubics_norm, dtype=torch.float32)
+            v_cubics_norm[..., 0] = v_cubics_px[..., 0] * half_w
+            v_cubics_norm[..., 1] = v_cubics_px[..., 1] * half_h
+        denom = torch.clamp(widths * widths * widths, min=1e-12)
+        v_aa = (-2.0 * v_inv / denom).contiguous()
+        out = [None] * 20
+        out[0] = v_cubics_norm
+        out[2] = v_colors
+        out[3] = v_opac.view_as(opac)
+        out[4] = torch.zeros_like(opac) if ctx.needs_input_grad[4] else None
+        out[15] = v_aa
+        return tuple(out)
+
+
+class CubicPolylineSplatFunction(torch.autograd.Function):
+    """Open-stroke renderer (mirrors _CubicPolylineSplatFunction,
+    cubic_polyline_splatting.py:962-1338)."""
+
+    @staticmethod
+    def forward(ctx, cubics_norm, primitive_seg_offsets, colors, opacities, stroke_widths, depths,
+                img_h, img_w, block_x, block_y, background, project_threads, map_threads,
+                aabb_pad, aniso_intersects, aa_widths, distance_samples,
+                flatten_method=DEFAULT_CUBIC_FLATTEN_METHOD, process_fn=None, tile_rows=None):
+        nat.require_cuda(cubics_norm, "cubics_norm")
+        method = normalize_cubic_flatten_method(flatten_method)
+        if method != CUBIC_FLATTEN_METHOD_BERNSTEIN:
+            raise NotImplementedError("de_casteljau flattening is not implemented in the B200 path")
+        _check_block(block_x, block_y)
+        num_segments = int(cubics_norm.shape[0])
+        offs = _i32(primitive_seg_offsets).view(-1)
+        num_primitives = max(0, int(offs.numel()) - 1)
+        bg = background.to(device=cubics_norm.device, dtype=torch.float32).view(3).contiguous()
+        ctx.img_h, ctx.img_w = int(img_h), int(img_w)
+        if num_primitives <= 0:
+            ctx.empty = True
+            return _empty_image(bg, img_h, img_w)
+        _validate_common(num_primitives, num_segments, offs, colors, opacities, depths)
+        if int(stroke_widths.reshape(-1).shape[0]) != num_primitives:
+            raise ValueError(
+                f"stroke_widths size must match primitive count ({num_primitives}), got {int(stroke_widths.reshape(-1).shape[0])}")
+        widths = aa_widths.to(device=cubics_norm.device, dtype=torch.float32).reshape(-1)
+        if int(widths.numel()) != num_primitives:
+            raise ValueError(
+                f"aa_widths size must match primitive count ({num_primitives}), got {int(widths.numel())}")
+        widths = torch.clamp(_f32(widths), min=1e-4)
+        inv_s2 = _inv_sigma2(widths)
+        sw = _f32(stroke_widths).view(-1)
+        b = bin_primitives(cubics_norm, offs, depths.reshape(-1), widths, int(img_h), int(img_w),
+                           int(distance_samples), stroke_widths=sw, aabb_pad=float(aabb_pad),
+                           aniso=bool(aniso_intersects), tile_rows=tile_rows)
+        if b.num_intersects <= 0:
+            ctx.empty = True
+            return _empty_image(bg, img_h, img_w)
+        col = _f32(colors)
+        op = _f32(opacities).view(-1)
+        out, fts, fidx = stroke_forward_raster(b, col, op, sw, inv_s2, bg, int(img_h), int(img_w))
+        ctx.empty = False
+        ctx.binning = b
+        ctx.process_fn = process_fn
+        ctx.num_segments = num_segments
+        ctx.save_for_backward(cubics_norm, offs, col, op, sw, widths, inv_s2, bg, fts, fidx)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        nones = (None,) * 20
+        if getattr(ctx, "empty", False):
+            return nones
+        cubics_norm, offs, colors, opac, sw, widths, inv_s2, bg, fts, fidx = ctx.saved_tensors
+        b: Binning = ctx.binning
+        process_fn = ctx.process_fn
+        pre = _run_process_fn(process_fn, "pre_backward_rasterize", {
+            "collect_curve_contrib_rgb": False,
+            "collect_curve_isect_contrib": False,
+            "num_primitives": int(colors.shape[0]),
+            "colors": colors,
+        })
+        cc = bool(pre.get("collect_curve_contrib_rgb", False))
+        ci = bool(pre.get("collect_curve_isect_contrib", False))
+        v_edges, v_colors, v_opac, v_inv, v_sw, contrib, icontrib = raster_backward(
+            b, colors, opac, inv_s2, None, sw, bg, fts, fidx, grad_out, ctx.img_h, ctx.img_w,
+            collect_contrib=cc, collect_isect_contrib=ci)
+        half_w, half_h = 0.5 * float(ctx.img_w), 0.5 * float(ctx.img_h)
+        if process_fn is None:
+            v_cubics_norm = edge_grads_to_cubics(v_edges, ctx.num_segments, b.samples,
+                                                 (half_w, half_h))
+        else:
+            v_cubics_px = edge_grads_to_cubics(v_edges, ctx.num_segments, b.samples)
+            post = _run_process_fn(process_fn, "post_backward_rasterize", {
+                "v_cubics_px": v_cubics_px, "v_colors": v_colors, "v_opacity": v_opac,
+                "v_stroke": v_sw, "curve_contrib_rgb": contrib, "curve_isect_contrib": icontrib,
+                "primitive_ids_sorted": b.prim_ids_sorted, "tile_bins": b.tile_bins,
+                "colors": colors, "opacities": opac, "stroke_widths": sw,
+                "primitive_seg_offsets": offs,
+            })
+            v_cubics_px = post["v_cubics_px"]
+            v_colors = post["v_colors"]
+            v_opac = post["v_opacity"]
+            v_sw = post["v_stroke"]
+            v_cubics_norm = torch.empty_like(cubics_norm, dtype=torch.float32)
+            v_cubics_norm[..., 0] = v_cubics_px[..., 0] * half_w
+            v_cubics_norm[..., 1] = v_cubics_px[..., 1] * half_h
+        denom = torch.clamp(widths * widths * widths, min=1e-12)
+        v_aa = (-2.0 * v_inv / denom).contiguous()
+        out = [None] * 20
+        out[0] = v_cubics_norm
+        out[2] = v_colors
+        out[3] = v_opac.view_as(opac)
+        out[4] = v_sw.view_as(sw)
+        out[5] = torch.zeros_like(opac) if ctx.needs_input_grad[5] else None
+        out[15] = v_aa
+        return tuple(out)
+
+
+# --------------------------------------------------------------------------
+# public entry points (reference signatures)
+
+def _prim_param(value, default, num_primitives, device, dtype, name):
+    if value is None:
+        return torch.full((num_primitives,), float(default), device=device, dtype=dtype)
+    t = value.to(device=device, dtype=dtype).reshape(-1)
+    if int(t.numel()) == 1 and num_primitives > 1:
+        t = t.expand(num_primitives)
+    if int(t.numel()) != num_primitives:
+        raise ValueError(
+            f"{name} size must match primitive count ({num_primitives}), got {int(t.numel())}")
+    return t
+
+
+def render_cubic_fill_splat(cubics_norm, primitive_seg_offsets, colors, opacities, depths, img_h,
+                            img_w, block_x, block_y, background, *, fill_rules=None,
+                            project_threads=DEFAULT_THREADS, map_threads=DEFAULT_THREADS,
+                            aabb_pad=DEFAULT_AABB_PAD, aniso_intersects=False, aa_widths=None,
+                            aa_width=DEFAULT_AA_WIDTH, distance_samples=DEFAULT_DISTANCE_SAMPLES,
+                            flatten_method=DEFAULT_CUBIC_FLATTEN_METHOD, process_fn=None,
+                            tile_rows=None):
+    """Render closed cubic fills, [H, W, 3] float32 (render_cubic_fill_splat_tilelang,
+    cubic_splatting.py:3128-3229).  ``tile_rows`` restricts rendering to a band of
+    tile rows (multi-GPU partition); rows outside it are left unwritten."""
+    num_segments = int(cubics_norm.shape[0])
+    offs = _i32(primitive_seg_offsets).view(-1)
+    num_primitives = max(0, int(offs.numel()) - 1)
+    if num_primitives <= 0:
+        bg = background.to(device=cubics_norm.device, dtype=torch.float32).view(1, 1, 3)
+        return bg.expand(int(img_h), int(img_w), 3).clone()
+    _validate_common(num_primitives, num_segments, offs, colors, opacities, depths)
+    dev = cubics_norm.device
+    rules = _prim_param(fill_rules, 1, num_primitives, dev, torch.int32, "fill_rules")
+    widths = _prim_param(aa_widths, aa_width, num_primitives, dev, torch.float32, "aa_widths")
+    widths = torch.clamp(_f32(widths), min=1e-4)
+    method = normalize_cubic_flatten_method(flatten_method)
+    return CubicFillSplatFunction.apply(
+        cubics_norm, offs.contiguous(), colors.contiguous(), opacities.reshape(-1).contiguous(),
+        depths.reshape(-1).contiguous(), rules.contiguous(), int(img_h), int(img_w), int(block_x),
+        int(block_y), background, int(project_threads), int(map_threads), float(aabb_pad),
+        bool(aniso_intersects), widths, int(distance_samples), method, process_fn, tile_rows)
+
+
+def render_cubic_polyline_splat(cubics_norm, primitive_seg_offsets, colors, opacities,
+                                stroke_widths, depths, img_h, img_w, block_x, block_y, background,
+                                *, project_threads=DEFAULT_THREADS, map_threads=DEFAULT_THREADS,
+                                aabb_pad=DEFAULT_AABB_PAD, aniso_intersects=False, aa_widths=None,
+                                aa_width=DEFAULT_AA_WIDTH,
+                                distance_samples=DEFAULT_DISTANCE_SAMPLES,
+                                flatten_method=DEFAULT_CUBIC_FLATTEN_METHOD, process_fn=None,
+                                tile_rows=None):
+    """Render open cubic strokes, [H, W, 3] float32 (render_cubic_polyline_splat_tilelang,
+    cubic_polyline_splatting.py:1341-1432)."""
+    num_segments = int(cubics_norm.shape[0])
+    offs = _i32(primitive_seg_offsets).view(-1)
+    num_primitives = max(0, int(offs.numel()) - 1)
+    if num_primitives <= 0:
+        bg = background.to(device=cubics_norm.device, dtype=torch.float32).view(1, 1, 3)
+        return bg.expand(int(img_h), int(img_w), 3).clone()
+    _validate_common(num_primitives, num_segments, offs, colors, opacities, depths)
+    if int(stroke_widths.reshape(-1).shape[0]) != num_primitives:
+        raise ValueError(
+            f"stroke_widths size must match primitive count ({num_primitives}), got {int(stroke_widths.reshape(-1).shape[0])}")
+    dev = cubics_norm.device
+    widths = _prim_param(aa_widths, aa_width, num_primitives, dev, torch.float32, "aa_widths")
+    widths = torch.clamp(_f32(widths), min=1e-4)
+    method = normalize_cubic_flatten_method(flatten_method)
+    return CubicPolylineSplatFunction.apply(
+        cubics_norm, offs.contiguous(), colors.contiguous(), opacities.reshape(-1).contiguous(),
+        stroke_widths.reshape(-1).contiguous(), depths.reshape(-1).contiguous(), int(img_h),
+        int(img_w), int(block_x), int(block_y), background, int(project_threads),
+        int(map_threads), float(aabb_pad), bool(aniso_intersects), widths,
+        int(distance_samples), method, process_fn, tile_rows)

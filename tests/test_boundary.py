@@ -1,0 +1,96 @@
+"""The C-ABI library and the drop-in Python surface (no GPU needed)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import ROOT
+
+HEADER = os.path.join(ROOT, "include", "cubicsplat_b200.h")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^CS_API [^;]*?\b(cs_\w+)\(", text, flags=re.M)))
+
+
+def test_header_declares_entry_points():
+    syms = declared_symbols()
+    assert len(syms) >= 20
+    for required in ["cs_project_cubics", "cs_bin_count", "cs_bin_sort", "cs_fill_forward",
+                     "cs_fill_backward", "cs_stroke_forward", "cs_stroke_backward",
+                     "cs_mse_forward", "cs_ssim", "cs_ring_segments_forward"]:
+        assert required in syms
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    from repo_b200 import _native
+    if not os.path.exists(_native.LIB_PATH):
+        from repo_b200 import build
+        build.build()
+    lib = ctypes.CDLL(_native.LIB_PATH)
+    for name in declared_symbols():
+        assert hasattr(lib, name), name
+    assert set(declared_symbols()) == set(_native.SIGNATURES), "ctypes table out of sync"
+    lib.cs_version.restype = ctypes.c_char_p
+    assert b"sm_100a" in lib.cs_version()
+
+
+def test_workspace_size_queries_need_no_gpu():
+    from repo_b200 import _native
+    assert _native.call("cs_bin_workspace_size", 1536) >= 2 * 4 * 1536
+    assert _native.call("cs_mse_workspace_size", 1 << 20) > 0
+    assert _native.call("cs_ssim_workspace_size", 3, 512, 768, 11) > 0
+
+
+def test_manbo_surface_imports():
+    import manbo
+    import manbo.ops as ops
+    for name in ["mse_loss_tilelang", "psnr", "ssim", "Adan", "gs_render",
+                 "regularization_loss_tilelang", "set_gs_profile_ctx_factory"]:
+        assert hasattr(manbo, name)
+    for name in ops.__all__:
+        assert hasattr(ops, name), name
+    from manbo.ops.cubic_polyline_splatting import render_cubic_polyline_splat_tilelang  # noqa
+    from manbo.ops.cubic_splatting import _flatten_cubics_to_edges  # noqa
+    from manbo.ops.tile_bins import get_tile_bin_edges_tilelang  # noqa
+
+
+def test_out_of_scope_names_raise():
+    import manbo
+    import manbo.ops as ops
+    with pytest.raises(NotImplementedError):
+        ops.rasterize_forward_tilelang()
+    with pytest.raises(NotImplementedError):
+        manbo.gs_render()
+    with pytest.raises(NotImplementedError):
+        manbo.Adan([])
+
+
+def test_cpu_tensors_are_rejected_without_fallback():
+    import torch
+    import manbo
+    x = torch.rand(1, 3, 16, 16)
+    with pytest.raises(ValueError):
+        manbo.psnr(x, x)
+    with pytest.raises(ValueError):
+        manbo.ops.render_cubic_fill_splat_tilelang(
+            torch.zeros(4, 4, 2), torch.tensor([0, 4], dtype=torch.int32), torch.rand(1, 3),
+            torch.ones(1), torch.rand(1), 32, 32, 16, 16, torch.ones(3))
+
+
+def test_flatten_method_validation():
+    from repo_b200.render import normalize_cubic_flatten_method
+    assert normalize_cubic_flatten_method("De-Casteljau") == "de_casteljau"
+    with pytest.raises(ValueError):
+        normalize_cubic_flatten_method("spline")
+
+
+def test_scenes_are_deterministic():
+    from repo_b200 import scenes
+    a, b = scenes.config2(), scenes.config2()
+    assert (a.ring == b.ring).all() and (a.target == b.target).all()
+    assert a.num_paths == 512 and a.cubics_norm().shape == (2048, 4, 2)
+    assert scenes.config3().cubics_norm().shape == (4096 * 6, 4, 2)
+    assert len(set(a.depths.tolist())) == 512

@@ -1,0 +1,470 @@
+"""Benchmark of the CubicSplat render/optimise hot path on B200.
+
+Metric: fwd+bwd training iterations/s at 768x512 with 512
+closed cubic paths x 4 segments, S=16 (config 2): each step renders, computes
+MSE and SSIM (11x11, sigma 1.5), back-propagates and takes an Adam step
+(lr 0.5 on points, 0.01 on colours).
+
+  value  -- device-resident throughput of the fused B200 step (one CUDA graph
+            per step, inputs already in HBM), timed per step with CUDA events;
+  e2e    -- the same step through the drop-in ``manbo`` API a user calls, with
+            the target image copied from pinned host memory and the loss read
+            back every step, inside the timed region.
+L2 is flushed (256 MiB write) before every timed step, outside its events.
+
+Multi-GPU (torchrun, N>1): every rank optimises its own config-2 scene
+(different seed), no collective on the data path; value = all ranks'
+iterations / max over ranks of the device time ("scaling": "weak").
+
+--impl reference times the reference algorithm's CPU implementation (the C
+oracle restating manbo/ops/cubic_splatting.py, all host threads) on the same
+workload; the reference has no CPU renderer of its own.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "fwd+bwd iters/s at 768x512, 512 paths"
+UNIT = "iters/s"
+L2_FLUSH_BYTES = 256 << 20
+
+
+def parse_args(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=20.0)
+    return ap.parse_args(argv)
+
+
+# --------------------------------------------------------------------------
+# clocks
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu_index = gpu_index
+        self.proc = None
+        self.path = os.path.join("/tmp", f"cs_clocks_{os.getpid()}_{gpu_index}.csv")
+
+    def __enter__(self):
+        try:
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.gpu_index)], stdout=self.fh,
+                stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.fh.close()
+
+    def summary(self):
+        rows = []
+        try:
+            for line in open(self.path):
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        except Exception:
+            pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
+                "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit()),
+                "reasons": reasons, "samples": len(rows)}
+
+
+# --------------------------------------------------------------------------
+# B200 arm
+
+def time_steps(step_fn, steps, flush, stream):
+    import torch
+    durs = []
+    for _ in range(steps):
+        flush()
+        s = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        step_fn()
+        e.record(stream)
+        durs.append((s, e))
+    torch.cuda.synchronize()
+    return [s.elapsed_time(e) for s, e in durs]
+
+
+def kernel_times(tr, reps, flush, stream):
+    """CUDA-event durations of the forward and backward raster launches, taken
+    inside eager training steps on the launching stream."""
+    import torch
+    from repo_b200 import _native as nat
+    fwd, bwd = [], []
+    orig = nat.call
+
+    def timed_call(name, *args):
+        if name in ("cs_fill_forward", "cs_fill_backward"):
+            s = torch.cuda.Event(enable_timing=True)
+            e = torch.cuda.Event(enable_timing=True)
+            s.record(stream)
+            r = orig(name, *args)
+            e.record(stream)
+            (fwd if name == "cs_fill_forward" else bwd).append((s, e))
+            return r
+        return orig(name, *args)
+
+    nat.call = timed_call
+    try:
+        for _ in range(reps):
+            flush()
+            tr.step_eager()
+        torch.cuda.synchronize()
+    finally:
+        nat.call = orig
+    f = [s.elapsed_time(e) for s, e in fwd]
+    b = [s.elapsed_time(e) for s, e in bwd]
+    return statistics.mean(f), statistics.mean(b)
+
+
+def raster_work(tr):
+    """Pixel-edge pairs and pixel-intersect visits of the reference algorithm
+    (SURVEY 8d definitions) for the current state, computed on the host from
+    tile_bins, per-intersect edge counts and the forward outputs."""
+    import numpy as np
+    n = int(tr.counters[0].item())
+    bins = tr.tile_bins.cpu().numpy()
+    pids = tr.prim_sorted[:n].cpu().numpy()
+    eoffs = tr.edge_offs.cpu().numpy()
+    ne = (eoffs[pids + 1] - eoffs[pids]).astype(np.int64)
+    cum = np.concatenate([[0], np.cumsum(ne)])
+    fidx = tr.fidx.cpu().numpy().astype(np.int64)
+    fts = tr.fts.cpu().numpy()
+    h, w = tr.h, tr.w
+    ty = np.arange(h)[:, None] // 16
+    tx = np.arange(w)[None, :] // 16
+    tile = ty * tr.tbx + tx
+    start = bins[tile, 0].astype(np.int64)
+    end = bins[tile, 1].astype(np.int64)
+    has = end > start
+    stop = np.where(fts <= 1e-4, fidx, end - 1)
+    pe_fwd = np.where(has, cum[np.clip(stop + 1, 0, n)] - cum[start], 0).sum()
+    vis_fwd = np.where(has, stop + 1 - start, 0).sum()
+    valid_b = has & (fidx >= start)
+    pe_bwd = np.where(valid_b, cum[np.clip(fidx + 1, 0, n)] - cum[start], 0).sum()
+    vis_bwd = np.where(valid_b, fidx + 1 - start, 0).sum()
+    return int(pe_fwd), int(vis_fwd), int(pe_bwd), int(vis_bwd), n
+
+
+def run_b200(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    from repo_b200 import scenes
+    from repo_b200.train import FillTrainer
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream(dev)
+    scene = scenes.config2() if rank == 0 else scenes.circles_scene(1 + 7919 * rank, 512, 768,
+                                                                     512, 4, 16, 32)
+    flush_buf = torch.empty((L2_FLUSH_BYTES // 4,), dtype=torch.float32, device=dev)
+
+    def flush():
+        flush_buf.zero_()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    tr = FillTrainer(scene, dev, lr_points=0.5, lr_colors=0.01, with_ssim=True)
+    tr.capture(warmup=max(3, args.warmup))
+    for _ in range(args.warmup):
+        tr.step()
+    torch.cuda.synchronize()
+    gpu_index = int(os.environ.get("LOCAL_RANK", "0"))
+    visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if visible:
+        try:
+            gpu_index = int(visible.split(",")[local_rank])
+        except ValueError:
+            pass
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(gpu_index) as clk:
+        t0 = time.perf_counter()
+        durs = time_steps(tr.step, args.steps, flush, stream)
+        wall = time.perf_counter() - t0
+    barrier()
+    torch.cuda.synchronize()
+    n_isect, status = tr.check_status()
+    if status != 0:
+        raise RuntimeError(f"device status {status} (intersect capacity {tr.capacity}, needed {n_isect})")
+    total_ms = sum(durs)
+    t_max = torch.tensor([total_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
+    total_ms = float(t_max.item())
+    value = world * args.steps / (total_ms / 1e3)
+    loss_final, ssim_final = tr.loss_value(), tr.ssim_value()
+
+    # dominant kernels, timed live with CUDA events on the launching stream
+    t_fwd, t_bwd = kernel_times(tr, 10, flush, stream)
+    pe_fwd, vis_fwd, pe_bwd, vis_bwd, n_now = raster_work(tr)
+
+    # e2e through the drop-in API with host buffers
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(scene, dev, args, flush, stream, world)
+
+    result = None
+    if rank == 0:
+        clocks = clk.summary()
+        sm_mhz = clocks.get("sm_mhz") or 1965.0
+        fp32_peak = 148 * 128 * 2 * sm_mhz * 1e6 / 1e12   # TFLOP/s at the sampled clock
+        flop_bwd = 24 * pe_bwd + 30 * vis_bwd
+        flop_fwd = 20 * pe_fwd + 12 * vis_fwd
+        achieved_bwd = flop_bwd / (t_bwd * 1e-3) / 1e12
+        result = {
+            "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "config2: 768x512 RGB, 512 closed cubic paths x 4 segs, S=16, "
+                                   "fwd+MSE+SSIM+bwd+Adam (lr 0.5 pts / 0.01 colours)",
+                       "scene": "seed-1 value noise + 32 ellipses target, circles r 5-40 px",
+                       "parallelism": f"one scene per rank x{world}" if world > 1 else "single GPU",
+                       "l2": "flushed before every step (256 MiB write), outside the step events",
+                       "step": "one CUDA graph of the fused B200 step",
+                       "intersects": n_now, "intersect_capacity": tr.capacity},
+            "final_loss": loss_final, "final_ssim": ssim_final,
+            "gpu_launches": args.steps * tr.launches_per_step,
+            "wall_s_timed_region": round(wall, 4),
+            "clocks": clocks,
+            "roofline": {
+                "kernel": "raster_backward (fill)", "bound": "fp32",
+                "achieved": round(achieved_bwd, 3), "peak": round(fp32_peak, 2),
+                "unit": "TFLOP/s", "frac": round(achieved_bwd / fp32_peak, 4),
+                "traffic": None,
+                "peak_note": "SIMT FP32 FMA peak 148 SM x 128 lanes x 2 at the sampled median SM "
+                             "clock; MEASURED_PEAKS.json holds only HBM and bf16 tensor peaks",
+                "flop_per_launch": flop_bwd,
+                "flop_model": "reference-algorithm work: 24 FLOP per pixel-edge pair up to "
+                              "final_idx + 30 per pixel-intersect visit",
+                "launch_ms": round(t_bwd, 4),
+                "forward": {"launch_ms": round(t_fwd, 4), "flop_per_launch": flop_fwd,
+                            "achieved": round(flop_fwd / (t_fwd * 1e-3) / 1e12, 3)},
+            },
+        }
+        if e2e is not None:
+            result["e2e"] = e2e
+    return result, tr
+
+
+def run_e2e(scene, dev, args, flush, stream, world):
+    """Training steps through the manbo API: target H2D from pinned memory and
+    loss D2H every step, timed with CUDA events."""
+    import torch
+
+    import manbo
+    from repo_b200 import scenes as sc_mod
+
+    h, w, s = scene.height, scene.width, scene.samples
+    ring = scene.ring.to(dev).clone().requires_grad_(True)
+    colors = scene.colors.to(dev).clone().requires_grad_(True)
+    opac, depths = scene.opacities.to(dev), scene.depths.to(dev)
+    rules, aa, bg = scene.fill_rules.to(dev), scene.aa_widths.to(dev), scene.background.to(dev)
+    offs = scene.seg_offsets().to(dev)
+    gidx = sc_mod.ring_gather_index(scene.segs_per_path).to(dev)
+    half = torch.tensor([0.5 * w, 0.5 * h], device=dev)
+    target_host = scene.target.clone().pin_memory()
+    target_dev = torch.empty_like(target_host, device=dev)
+    loss_host = torch.empty((2,), dtype=torch.float32).pin_memory()
+    opt = torch.optim.Adam([{"params": [ring], "lr": 0.5}, {"params": [colors], "lr": 0.01}],
+                           fused=True)
+
+    def step():
+        target_dev.copy_(target_host, non_blocking=True)
+        opt.zero_grad(set_to_none=True)
+        cn = ring[:, gidx, :].reshape(-1, 4, 2) / half - 1.0
+        out = manbo.ops.render_cubic_fill_splat_tilelang(
+            cn, offs, colors, opac, depths, h, w, 16, 16, bg, fill_rules=rules, aa_widths=aa,
+            distance_samples=s)
+        img = torch.clamp(out, 0, 1).permute(2, 0, 1).unsqueeze(0).contiguous()
+        loss = manbo.mse_loss_tilelang(img, target_dev)
+        with torch.no_grad():
+            sv = manbo.ssim(img.detach(), target_dev)
+        loss.backward()
+        opt.step()
+        loss_host[0:1].copy_(loss.detach().view(1), non_blocking=True)
+        loss_host[1:2].copy_(sv.view(1), non_blocking=True)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    durs = time_steps(step, args.steps, flush, stream)
+    total_ms = sum(durs)
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    return {"value": round(world * args.steps / (total_ms / 1e3), 3), "unit": UNIT,
+            "h2d_bytes_per_step": int(target_host.numel() * 4),
+            "d2h_bytes_per_step": 8, "path": "manbo.ops.render_cubic_fill_splat_tilelang + "
+            "manbo.mse_loss_tilelang + manbo.ssim + autograd + torch Adam",
+            "ms_per_step": round(total_ms / args.steps, 4)}
+
+
+# --------------------------------------------------------------------------
+# CPU reference arm (the C oracle restating the reference algorithm)
+
+def cpu_iteration(state, scene):
+    """One config-2 training iteration on the host: render, MSE, SSIM, backward,
+    Adam.  Returns the loss."""
+    import numpy as np
+
+    import oracle
+    from repo_b200 import scenes as sc_mod
+    ring, colors, m, v, t = state["ring"], state["colors"], state["m"], state["v"], state["t"]
+    h, w, s = scene.height, scene.width, scene.samples
+    gi = sc_mod.ring_gather_index(scene.segs_per_path).numpy()
+    cub = ring[:, gi, :].reshape(-1, 4, 2)
+    half = np.array([0.5 * w, 0.5 * h], np.float32)
+    cn = (cub / half - np.float32(1.0)).astype(np.float32)
+    st = oracle.render_fill(cn, scene.seg_offsets().numpy(), colors, scene.opacities.numpy(),
+                            scene.depths.numpy(), h, w, scene.background.numpy(),
+                            fill_rules=scene.fill_rules.numpy(), aa_widths=scene.aa_widths.numpy(),
+                            samples=s)
+    out = st["image"]
+    img = np.clip(out, 0.0, 1.0).transpose(2, 0, 1)[None]
+    tgt = state["target"]
+    loss = oracle.mse(img, tgt)
+    oracle.ssim(img, tgt)
+    g_img = oracle.mse_grad(img, tgt)[0].transpose(1, 2, 0)
+    g_out = np.where((out >= 0) & (out <= 1), g_img, 0).astype(np.float32)
+    gr = oracle.fill_backward(st, g_out)
+    v_cub = (gr["v_cubics_norm"] / half).reshape(ring.shape[0], -1, 2)
+    g_ring = np.zeros_like(ring)
+    np.add.at(g_ring, (slice(None), gi), v_cub)
+    t += 1
+    for key, p, g, lr in (("ring", ring, g_ring, 0.5), ("colors", colors, gr["v_colors"], 0.01)):
+        m[key] = 0.9 * m[key] + 0.1 * g
+        v[key] = 0.999 * v[key] + 0.001 * g * g
+        mh = m[key] / (1 - 0.9 ** t)
+        vh = v[key] / (1 - 0.999 ** t)
+        p -= (lr * mh / (np.sqrt(vh) + 1e-8)).astype(np.float32)
+    state["t"] = t
+    return loss
+
+
+def run_cpu(seconds_budget: float, max_iters: int):
+    import numpy as np
+
+    import oracle
+    from repo_b200 import scenes
+    scene = scenes.config2()
+    state = {"ring": scene.ring.numpy().copy(), "colors": scene.colors.numpy().copy(),
+             "target": scene.target.numpy(), "t": 0,
+             "m": {"ring": np.zeros_like(scene.ring.numpy()), "colors": np.zeros_like(scene.colors.numpy())},
+             "v": {"ring": np.zeros_like(scene.ring.numpy()), "colors": np.zeros_like(scene.colors.numpy())}}
+    cpu_iteration(state, scene)  # warm-up (library load, first touch)
+    t0 = time.perf_counter()
+    iters = 0
+    while iters < max_iters:
+        cpu_iteration(state, scene)
+        iters += 1
+        if time.perf_counter() - t0 > seconds_budget:
+            break
+    dt = time.perf_counter() - t0
+    return iters / dt, iters, dt, oracle.num_threads()
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return None
+    budget = min(120.0, max(10.0, 1.5 * args.cpu_seconds))
+    value, iters, dt, cores = run_cpu(budget, max(1, args.steps))
+    sample = (f"{iters} full config-2 training iterations (render fwd, MSE, SSIM, bwd, Adam) "
+              f"in {dt:.1f} s; each --steps step is one iteration, capped to ~{budget:.0f} s")
+    return {"metric": METRIC, "value": round(value, 5), "unit": UNIT, "n_gpus": world,
+            "steps": iters, "warmup": 1, "ms_per_step": round(1e3 * dt / iters, 2),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "impl": "reference",
+            "config": {"workload": "config2: 768x512 RGB, 512 closed cubic paths x 4 segs, S=16, "
+                                   "fwd+MSE+SSIM+bwd+Adam", "device": "host CPU"},
+            "cpu_baseline": {"value": round(value, 5), "unit": UNIT, "cores": cores,
+                             "kind": "port", "sample": sample},
+            "e2e": {"value": round(value, 5), "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
+# --------------------------------------------------------------------------
+
+def main(argv=None):
+    args = parse_args(argv)
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        res = run_reference(args, rank, world)
+        if res is not None:
+            print(json.dumps(res), flush=True)
+        return 0
+    import torch
+    import torch.distributed as dist
+    if world > 1:
+        from datetime import timedelta
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        res, tr = run_b200(args, rank, world, local_rank)
+        if rank == 0 and not args.no_cpu_baseline:
+            value, iters, dt, cores = run_cpu(args.cpu_seconds, 1000)
+            res["cpu_baseline"] = {
+                "value": round(value, 5), "unit": UNIT, "cores": cores, "kind": "port",
+                "sample": f"{iters} full config-2 training iterations on the host in {dt:.1f} s "
+                          f"(C oracle, {cores} threads)"}
+        if rank == 0:
+            print(json.dumps(res), flush=True)
+        del tr
+    finally:
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -139,14 +139,17 @@ CS_API int cs_bin_sort(const int32_t *prim_tile_ranges, const float *depths,
  * front-to-back alpha compositing with early termination.
  * Replaces rasterize_cubic_fill_forward_kernel, cubic_splatting.py:918-1194.
  * isect_edge_ranges [I, 2] may be NULL when prim_edge_offsets [P + 1] is given.
+ * out_chw_clamped [3, H, W] (may be NULL) additionally receives clamp(out, 0, 1)
+ * in channel-major layout, the image the training loss sees (the reference
+ * does torch.clamp + permute, manbo/gaussian_trace/render.py:1309-1310).
  * Tile rows outside [tile_row_begin, tile_row_end) are not touched. */
 CS_API int cs_fill_forward(const int32_t *prim_ids_sorted, const int32_t *tile_bins,
                     const float *edges_px, const int32_t *isect_edge_ranges,
                     const int32_t *prim_edge_offsets, const float *colors,
                     const float *opacities, const float *inv_sigma2s, const int32_t *fill_rules,
                     const float *background, float *out_img, float *final_Ts, int32_t *final_idx,
-                    int32_t img_height, int32_t img_width, int32_t tile_row_begin,
-                    int32_t tile_row_end, void *stream);
+                    float *out_chw_clamped, int32_t img_height, int32_t img_width,
+                    int32_t tile_row_begin, int32_t tile_row_end, void *stream);
 
 /* Closed-fill backward: reverse compositing from final_idx, gradients of the
  * colours, opacities, 1/sigma^2 and edge endpoints (closest edge only).
@@ -176,8 +179,9 @@ CS_API int cs_stroke_forward(const int32_t *prim_ids_sorted, const int32_t *tile
                       const int32_t *prim_edge_offsets, const float *colors,
                       const float *opacities, const float *stroke_widths,
                       const float *inv_sigma2s, const float *background, float *out_img,
-                      float *final_Ts, int32_t *final_idx, int32_t img_height, int32_t img_width,
-                      int32_t tile_row_begin, int32_t tile_row_end, void *stream);
+                      float *final_Ts, int32_t *final_idx, float *out_chw_clamped,
+                      int32_t img_height, int32_t img_width, int32_t tile_row_begin,
+                      int32_t tile_row_end, void *stream);
 
 /* Stroke backward (adds d/d stroke width).
  * Replaces rasterize_cubic_polyline_backward_kernel,

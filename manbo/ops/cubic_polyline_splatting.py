@@ -43,7 +43,7 @@ def rasterize_cubic_polyline_forward_kernel(block_x: int = BLOCK_X, block_y: int
                            nat.ptr(edges_px), nat.ptr(isect_edge_ranges), None, nat.ptr(colors),
                            nat.ptr(opacities), nat.ptr(stroke_widths), nat.ptr(inv_sigma2s),
                            nat.ptr(background), nat.ptr(out_img), nat.ptr(final_Ts),
-                           nat.ptr(final_idx), h, w, 0, (h + BLOCK_Y - 1) // BLOCK_Y,
+                           nat.ptr(final_idx), None, h, w, 0, (h + BLOCK_Y - 1) // BLOCK_Y,
                            nat.stream(out_img.device)), "cs_stroke_forward")
     return kernel
 

@@ -44,11 +44,9 @@ SIGNATURES = {
                                     _I64, _I64, _I32, _I32, _I32, _I32, _I32, _F32, _I32, _P]),
     "cs_bin_sort": (ctypes.c_int, [_P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I32, _I32, _I32,
                                    _I32, _P]),
-    "cs_fill_forward": (ctypes.c_int, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I32,
-                                       _I32, _I32, _I32, _P]),
+    "cs_fill_forward": (ctypes.c_int, [_P] * 14 + [_I32, _I32, _I32, _I32, _P]),
     "cs_fill_backward": (ctypes.c_int, [_P] * 22 + [_I32, _I32, _I32, _I32, _P]),
-    "cs_stroke_forward": (ctypes.c_int, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
-                                         _I32, _I32, _I32, _I32, _P]),
+    "cs_stroke_forward": (ctypes.c_int, [_P] * 14 + [_I32, _I32, _I32, _I32, _P]),
     "cs_stroke_backward": (ctypes.c_int, [_P] * 23 + [_I32, _I32, _I32, _I32, _P]),
     "cs_edge_grads_to_cubics": (ctypes.c_int, [_P, _P, _I64, _I32, _F32, _F32, _P]),
     "cs_ring_segments_forward": (ctypes.c_int, [_P, _P, _P, _P, _P, _I64, _I32, _I32, _P]),

@@ -85,6 +85,7 @@ struct RasterArgs {
   float* out;
   float* fts;
   int* fidx;
+  float* out_chw;  // optional clamp(out, 0, 1) in [3, H, W]
   // backward inputs / outputs
   const float* fts_in;
   const int* fidx_in;
@@ -459,21 +460,34 @@ __global__ void __launch_bounds__(kRT) raster_forward_kernel(const RasterArgs A)
     }
   }
   const float bg0 = A.bg[0], bg1 = A.bg[1], bg2 = A.bg[2];
+  const long long hw = (long long)A.H * A.W;
   if (in0) {
     const long long pix = (long long)i * A.W + j0;
+    const float o0 = a00 + T0 * bg0, o1 = a01 + T0 * bg1, o2 = a02 + T0 * bg2;
     A.fts[pix] = T0;
     A.fidx[pix] = cur0;
-    A.out[pix * 3] = a00 + T0 * bg0;
-    A.out[pix * 3 + 1] = a01 + T0 * bg1;
-    A.out[pix * 3 + 2] = a02 + T0 * bg2;
+    A.out[pix * 3] = o0;
+    A.out[pix * 3 + 1] = o1;
+    A.out[pix * 3 + 2] = o2;
+    if (A.out_chw) {
+      A.out_chw[pix] = fminf(fmaxf(o0, 0.0f), 1.0f);
+      A.out_chw[hw + pix] = fminf(fmaxf(o1, 0.0f), 1.0f);
+      A.out_chw[2 * hw + pix] = fminf(fmaxf(o2, 0.0f), 1.0f);
+    }
   }
   if (in1) {
     const long long pix = (long long)i * A.W + j0 + 1;
+    const float o0 = a10 + T1 * bg0, o1 = a11 + T1 * bg1, o2 = a12 + T1 * bg2;
     A.fts[pix] = T1;
     A.fidx[pix] = cur1;
-    A.out[pix * 3] = a10 + T1 * bg0;
-    A.out[pix * 3 + 1] = a11 + T1 * bg1;
-    A.out[pix * 3 + 2] = a12 + T1 * bg2;
+    A.out[pix * 3] = o0;
+    A.out[pix * 3 + 1] = o1;
+    A.out[pix * 3 + 2] = o2;
+    if (A.out_chw) {
+      A.out_chw[pix] = fminf(fmaxf(o0, 0.0f), 1.0f);
+      A.out_chw[hw + pix] = fminf(fmaxf(o1, 0.0f), 1.0f);
+      A.out_chw[2 * hw + pix] = fminf(fmaxf(o2, 0.0f), 1.0f);
+    }
   }
 }
 
@@ -789,8 +803,8 @@ int cs_fill_forward(const int32_t* prim_ids_sorted, const int32_t* tile_bins,
                     const int32_t* prim_edge_offsets, const float* colors,
                     const float* opacities, const float* inv_sigma2s, const int32_t* fill_rules,
                     const float* background, float* out_img, float* final_Ts, int32_t* final_idx,
-                    int32_t img_height, int32_t img_width, int32_t tile_row_begin,
-                    int32_t tile_row_end, void* stream) {
+                    float* out_chw_clamped, int32_t img_height, int32_t img_width,
+                    int32_t tile_row_begin, int32_t tile_row_end, void* stream) {
   if (img_height <= 0 || img_width <= 0 || !tile_bins || !out_img || !final_Ts || !final_idx ||
       (!isect_edge_ranges && !prim_edge_offsets))
     return CS_ERR_ARG;
@@ -808,6 +822,7 @@ int cs_fill_forward(const int32_t* prim_ids_sorted, const int32_t* tile_bins,
   a.out = out_img;
   a.fts = final_Ts;
   a.fidx = final_idx;
+  a.out_chw = out_chw_clamped;
   return launch_raster(false, false, a, img_height, img_width, tile_row_begin, tile_row_end,
                        (cudaStream_t)stream);
 }
@@ -858,8 +873,9 @@ int cs_stroke_forward(const int32_t* prim_ids_sorted, const int32_t* tile_bins,
                       const int32_t* prim_edge_offsets, const float* colors,
                       const float* opacities, const float* stroke_widths,
                       const float* inv_sigma2s, const float* background, float* out_img,
-                      float* final_Ts, int32_t* final_idx, int32_t img_height, int32_t img_width,
-                      int32_t tile_row_begin, int32_t tile_row_end, void* stream) {
+                      float* final_Ts, int32_t* final_idx, float* out_chw_clamped,
+                      int32_t img_height, int32_t img_width, int32_t tile_row_begin,
+                      int32_t tile_row_end, void* stream) {
   if (img_height <= 0 || img_width <= 0 || !tile_bins || !out_img || !final_Ts || !final_idx ||
       (!isect_edge_ranges && !prim_edge_offsets))
     return CS_ERR_ARG;
@@ -877,6 +893,7 @@ int cs_stroke_forward(const int32_t* prim_ids_sorted, const int32_t* tile_bins,
   a.out = out_img;
   a.fts = final_Ts;
   a.fidx = final_idx;
+  a.out_chw = out_chw_clamped;
   return launch_raster(true, false, a, img_height, img_width, tile_row_begin, tile_row_end,
                        (cudaStream_t)stream);
 }

@@ -189,7 +189,7 @@ def _zeros_views(dev, *shapes):
 
 
 def fill_forward_raster(b: Binning, colors, opacities, inv_sigma2s, fill_rules, background,
-                        img_h: int, img_w: int):
+                        img_h: int, img_w: int, out_chw=None):
     dev = colors.device
     out = torch.empty((img_h, img_w, 3), dtype=torch.float32, device=dev)
     fts = torch.empty((img_h, img_w), dtype=torch.float32, device=dev)
@@ -202,8 +202,9 @@ def fill_forward_raster(b: Binning, colors, opacities, inv_sigma2s, fill_rules, 
     nat.check(nat.call("cs_fill_forward", nat.ptr(b.prim_ids_sorted), nat.ptr(b.tile_bins),
                        nat.ptr(b.edges_px), None, nat.ptr(b.prim_edge_offsets), nat.ptr(colors),
                        nat.ptr(opacities), nat.ptr(inv_sigma2s), nat.ptr(fill_rules),
-                       nat.ptr(background), nat.ptr(out), nat.ptr(fts), nat.ptr(fidx), img_h,
-                       img_w, b.tile_rows[0], b.tile_rows[1], nat.stream(dev)), "cs_fill_forward")
+                       nat.ptr(background), nat.ptr(out), nat.ptr(fts), nat.ptr(fidx),
+                       nat.ptr(out_chw), img_h, img_w, b.tile_rows[0], b.tile_rows[1],
+                       nat.stream(dev)), "cs_fill_forward")
     return out, fts, fidx
 
 
@@ -221,8 +222,8 @@ def stroke_forward_raster(b: Binning, colors, opacities, stroke_widths, inv_sigm
     nat.check(nat.call("cs_stroke_forward", nat.ptr(b.prim_ids_sorted), nat.ptr(b.tile_bins),
                        nat.ptr(b.edges_px), None, nat.ptr(b.prim_edge_offsets), nat.ptr(colors),
                        nat.ptr(opacities), nat.ptr(stroke_widths), nat.ptr(inv_sigma2s),
-                       nat.ptr(background), nat.ptr(out), nat.ptr(fts), nat.ptr(fidx), img_h,
-                       img_w, b.tile_rows[0], b.tile_rows[1], nat.stream(dev)),
+                       nat.ptr(background), nat.ptr(out), nat.ptr(fts), nat.ptr(fidx), None,
+                       img_h, img_w, b.tile_rows[0], b.tile_rows[1], nat.stream(dev)),
               "cs_stroke_forward")
     return out, fts, fidx
 

@@ -266,7 +266,8 @@ def run_b200(args, rank, world, local_rank):
                        "parallelism": f"one scene per rank x{world}" if world > 1 else "single GPU",
                        "l2": "flushed before every step (256 MiB write), outside the step events",
                        "step": "one CUDA graph of the fused B200 step",
-                       "intersects": n_now, "intersect_capacity": tr.capacity},
+                       "intersects": n_now, "intersect_capacity": tr.capacity,
+                       "staged_record_capacity": tr.dcapacity},
             "final_loss": loss_final, "final_ssim": ssim_final,
             "gpu_launches": args.steps * tr.launches_per_step,
             "wall_s_timed_region": round(wall, 4),

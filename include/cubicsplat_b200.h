@@ -36,6 +36,7 @@ extern "C" {
 #define CS_ERR_CAPACITY 2     /* intersect count exceeded the caller's capacity */
 #define CS_ERR_CUDA 3         /* a kernel launch failed */
 #define CS_ERR_UNSUPPORTED 4  /* valid but unsupported configuration */
+#define CS_ERR_TIMEOUT 5      /* a bounded device-side wait gave up (reported on the device) */
 
 /* Library version string and the list of exported entry points (for checks). */
 CS_API const char *cs_version(void);
@@ -92,43 +93,65 @@ CS_API int cs_isect_edge_ranges(const int32_t *prim_ids_sorted, const int32_t *p
                          int32_t *isect_edge_ranges, int64_t num_intersects, void *stream);
 
 /* Fused B200 binning, stage 1 of 2: projection + AABB + flattening of every
- * segment, per-primitive tile rectangles, per-tile intersect counts restricted
- * to tile rows [tile_row_begin, tile_row_end), and their exclusive scan into
- * tile_bins [num_tiles, 2].  *num_intersects (device) receives the total.
+ * segment, per-primitive tile rectangles, per-tile intersect and edge-slot
+ * counts restricted to tile rows [tile_row_begin, tile_row_end), and their
+ * exclusive scans: tile_bins [T, 2] (intersect [start, end)) and tile_dlist
+ * [T, 2] (first staged record, record bound).  counters is a device int32[4]:
+ * [0] intersect total, [1] status, [2] staged-record bound, [3] unused.
  * stroke_widths may be NULL (fill mode: zero stroke width); aniso selects the
- * chord-anisotropic padding of the reference's aniso_intersects.  If the total
- * exceeds capacity (pass INT64_MAX when the caller sizes the intersect buffers
- * from *num_intersects afterwards), every tile range is written empty and
- * *status (device int, may be NULL) is set to CS_ERR_CAPACITY, so no later
- * kernel reads past the caller's buffers.  Offsets that do not start at 0,
- * end at num_segments and increase set *status to CS_ERR_ARG (the primitive is
- * treated as empty).
- * The stage-2 call below produces the sorted intersect list; together they
- * replace project (K3) + flatten + K4 + cumsum + K5 + torch.sort + K6 of
- * _CubicFillSplatFunction.forward, cubic_splatting.py:2815-2908.
+ * chord-anisotropic padding of the reference's aniso_intersects.  If a total
+ * exceeds its capacity (pass INT64_MAX to size buffers from the counters
+ * afterwards) every tile range is written empty and counters[1] is set to
+ * CS_ERR_CAPACITY, so no later kernel reads past the caller's buffers.
+ * Offsets that do not start at 0, end at num_segments and increase set
+ * counters[1] to CS_ERR_ARG (the primitive is treated as empty).
+ * With cs_bin_sort this replaces project (K3) + flatten + K4 + cumsum + K5 +
+ * torch.sort + K6 of _CubicFillSplatFunction.forward, cubic_splatting.py:2815-2908.
  * Workspace: cs_bin_workspace_size(num_tiles). */
 CS_API size_t cs_bin_workspace_size(int64_t num_tiles);
 CS_API int cs_bin_count(const float *cubics_norm, const int32_t *prim_seg_offsets,
                  const float *aa_widths, const float *stroke_widths, const float *basis,
                  float *cubics_px, float *edges_px, int32_t *prim_tile_ranges,
-                 int32_t *num_tiles_hit, int32_t *tile_bins, int32_t *num_intersects,
-                 int32_t *status, void *workspace, int64_t num_primitives,
-                 int64_t num_segments, int64_t capacity, int32_t samples, int32_t img_height,
-                 int32_t img_width, int32_t tile_row_begin, int32_t tile_row_end, float aabb_pad,
-                 int32_t aniso, void *stream);
+                 int32_t *num_tiles_hit, int32_t *tile_bins, int32_t *tile_dlist,
+                 int32_t *counters, void *workspace, int64_t num_primitives,
+                 int64_t num_segments, int64_t isect_capacity, int64_t dlist_capacity,
+                 int32_t samples, int32_t img_height, int32_t img_width, int32_t tile_row_begin,
+                 int32_t tile_row_end, float aabb_pad, int32_t aniso, void *stream);
 
 /* Fused B200 binning, stage 2 of 2: scatter each (primitive, tile) pair into
  * its tile's range and sort every tile's pairs by (depth key, primitive id),
- * i.e. the order of a stable sort of the reference's keys.  Writes
- * prim_ids_sorted [capacity] and isect_ids_sorted [capacity] (may be NULL).
- * If the total exceeds capacity nothing is written out of bounds, *status
- * (device int, may be NULL) is set to CS_ERR_CAPACITY and the call returns
- * CS_OK (the check is on the device). */
+ * the order of a stable sort of the reference's keys.  Writes prim_ids_sorted
+ * and isect_ids_sorted (reference key format; also used as scratch) [capacity].
+ * When imeta is not NULL the same per-tile pass also stages the raster input:
+ * per intersect a 48-byte record (imeta [I]) and, in fill mode, packed per-row
+ * winding offsets (rowoff [I, 16]); per tile the near-edge records (dlist
+ * [dlist_capacity] of 32 bytes; tile_dlist[t].y receives the record count).
+ * stroke_widths non-NULL selects stroke mode (fill_rules, rowoff unused).
+ * Work stops at the device when counters report an overflow. */
 CS_API int cs_bin_sort(const int32_t *prim_tile_ranges, const float *depths,
-                const int32_t *tile_bins, const int32_t *num_intersects, int32_t *prim_ids_sorted,
-                int64_t *isect_ids_sorted, int32_t *status, void *workspace,
-                int64_t num_primitives, int64_t capacity, int32_t img_height, int32_t img_width,
-                int32_t tile_row_begin, int32_t tile_row_end, void *stream);
+                const int32_t *tile_bins, int32_t *prim_ids_sorted, int64_t *isect_ids_sorted,
+                int32_t *counters, void *workspace, int64_t num_primitives,
+                int64_t isect_capacity, int32_t img_height, int32_t img_width,
+                int32_t tile_row_begin, int32_t tile_row_end, const float *edges_px,
+                const int32_t *prim_edge_offsets, const float *colors, const float *opacities,
+                const float *inv_sigma2s, const int32_t *fill_rules, const float *stroke_widths,
+                int32_t *tile_dlist, void *imeta, int32_t *rowoff, void *dlist,
+                int64_t dlist_capacity, void *stream);
+
+/* Staging of a reference-format sorted intersect list (primitive_ids_sorted,
+ * tile_bins and isect_edge_ranges [I, 2] or prim_edge_offsets [P + 1]) into
+ * the raster input described for cs_bin_sort; used by the per-stage API.
+ * counters: device int32[4] as for cs_bin_count ([2] receives the record
+ * bound; CS_ERR_CAPACITY in [1] if it exceeds dlist_capacity).
+ * Workspace: cs_stage_workspace_size(num_tiles). */
+CS_API size_t cs_stage_workspace_size(int64_t num_tiles);
+CS_API int cs_tile_stage(const int32_t *prim_ids_sorted, const int32_t *tile_bins,
+                  const float *edges_px, const int32_t *isect_edge_ranges,
+                  const int32_t *prim_edge_offsets, const float *colors, const float *opacities,
+                  const float *inv_sigma2s, const int32_t *fill_rules, const float *stroke_widths,
+                  int32_t *tile_dlist, void *imeta, int32_t *rowoff, void *dlist,
+                  int32_t *counters, void *workspace, int64_t dlist_capacity, int32_t img_height,
+                  int32_t img_width, void *stream);
 
 /* --------------------------------------------------------------------------
  * Rasterisation (one CTA per 16x16 tile, front-to-back compositing)
@@ -136,19 +159,19 @@ CS_API int cs_bin_sort(const int32_t *prim_tile_ranges, const float *depths,
 
 /* Closed-fill forward: per pixel, winding number / crossing parity and the
  * minimum distance to the primitive's polyline, sigmoid soft coverage, then
- * front-to-back alpha compositing with early termination.
- * Replaces rasterize_cubic_fill_forward_kernel, cubic_splatting.py:918-1194.
- * isect_edge_ranges [I, 2] may be NULL when prim_edge_offsets [P + 1] is given.
- * out_chw_clamped [3, H, W] (may be NULL) additionally receives clamp(out, 0, 1)
- * in channel-major layout, the image the training loss sees (the reference
- * does torch.clamp + permute, manbo/gaussian_trace/render.py:1309-1310).
- * Tile rows outside [tile_row_begin, tile_row_end) are not touched. */
+ * front-to-back alpha compositing with early termination.  Input is the
+ * staged tile data of cs_bin_sort / cs_tile_stage.  out_chw_clamped
+ * [3, H, W] (may be NULL) also receives clamp(out, 0, 1) channel-major, the
+ * image the training loss sees (the reference does torch.clamp + permute,
+ * manbo/gaussian_trace/render.py:1309-1310).  status (device int, may be NULL)
+ * receives CS_ERR_TIMEOUT if a bounded wait gave up.  Tile rows outside
+ * [tile_row_begin, tile_row_end) are not touched.
+ * Replaces rasterize_cubic_fill_forward_kernel, cubic_splatting.py:918-1194. */
 CS_API int cs_fill_forward(const int32_t *prim_ids_sorted, const int32_t *tile_bins,
-                    const float *edges_px, const int32_t *isect_edge_ranges,
-                    const int32_t *prim_edge_offsets, const float *colors,
-                    const float *opacities, const float *inv_sigma2s, const int32_t *fill_rules,
-                    const float *background, float *out_img, float *final_Ts, int32_t *final_idx,
-                    float *out_chw_clamped, int32_t img_height, int32_t img_width,
+                    const int32_t *tile_dlist, const void *imeta, const int32_t *rowoff,
+                    const void *dlist, const float *background, float *out_img,
+                    float *final_Ts, int32_t *final_idx, float *out_chw_clamped,
+                    int32_t *status, int32_t img_height, int32_t img_width,
                     int32_t tile_row_begin, int32_t tile_row_end, void *stream);
 
 /* Closed-fill backward: reverse compositing from final_idx, gradients of the
@@ -161,13 +184,12 @@ CS_API int cs_fill_forward(const int32_t *prim_ids_sorted, const int32_t *tile_b
  * *mse_scale (device scalar, e.g. 2/N * dLoss).
  * Replaces rasterize_cubic_fill_backward_kernel, cubic_splatting.py:1197-1651. */
 CS_API int cs_fill_backward(const int32_t *prim_ids_sorted, const int32_t *tile_bins,
-                     const float *edges_px, const int32_t *isect_edge_ranges,
-                     const int32_t *prim_edge_offsets, const float *colors,
-                     const float *opacities, const float *inv_sigma2s, const int32_t *fill_rules,
-                     const float *background, const float *final_Ts, const int32_t *final_idx,
-                     const float *v_output, const float *out_img, const float *target_chw,
-                     const float *mse_scale, float *v_edges, float *v_colors, float *v_opacities,
-                     float *v_inv_sigma2s, float *curve_contrib_rgb, float *curve_isect_contrib,
+                     const int32_t *tile_dlist, const void *imeta, const int32_t *rowoff,
+                     const void *dlist, const float *background, const float *final_Ts,
+                     const int32_t *final_idx, const float *v_output, const float *out_img,
+                     const float *target_chw, const float *mse_scale, float *v_edges,
+                     float *v_colors, float *v_opacities, float *v_inv_sigma2s,
+                     float *curve_contrib_rgb, float *curve_isect_contrib, int32_t *status,
                      int32_t img_height, int32_t img_width, int32_t tile_row_begin,
                      int32_t tile_row_end, void *stream);
 
@@ -175,11 +197,9 @@ CS_API int cs_fill_backward(const int32_t *prim_ids_sorted, const int32_t *tile_
  * Replaces rasterize_cubic_polyline_forward_kernel,
  * cubic_polyline_splatting.py:33-249. */
 CS_API int cs_stroke_forward(const int32_t *prim_ids_sorted, const int32_t *tile_bins,
-                      const float *edges_px, const int32_t *isect_edge_ranges,
-                      const int32_t *prim_edge_offsets, const float *colors,
-                      const float *opacities, const float *stroke_widths,
-                      const float *inv_sigma2s, const float *background, float *out_img,
-                      float *final_Ts, int32_t *final_idx, float *out_chw_clamped,
+                      const int32_t *tile_dlist, const void *imeta, const void *dlist,
+                      const float *background, float *out_img, float *final_Ts,
+                      int32_t *final_idx, float *out_chw_clamped, int32_t *status,
                       int32_t img_height, int32_t img_width, int32_t tile_row_begin,
                       int32_t tile_row_end, void *stream);
 
@@ -187,16 +207,15 @@ CS_API int cs_stroke_forward(const int32_t *prim_ids_sorted, const int32_t *tile
  * Replaces rasterize_cubic_polyline_backward_kernel,
  * cubic_polyline_splatting.py:252-660. */
 CS_API int cs_stroke_backward(const int32_t *prim_ids_sorted, const int32_t *tile_bins,
-                       const float *edges_px, const int32_t *isect_edge_ranges,
-                       const int32_t *prim_edge_offsets, const float *colors,
-                       const float *opacities, const float *stroke_widths,
-                       const float *inv_sigma2s, const float *background, const float *final_Ts,
+                       const int32_t *tile_dlist, const void *imeta, const void *dlist,
+                       const float *background, const float *final_Ts,
                        const int32_t *final_idx, const float *v_output, const float *out_img,
                        const float *target_chw, const float *mse_scale, float *v_edges,
                        float *v_colors, float *v_opacities, float *v_stroke_widths,
                        float *v_inv_sigma2s, float *curve_contrib_rgb,
-                       float *curve_isect_contrib, int32_t img_height, int32_t img_width,
-                       int32_t tile_row_begin, int32_t tile_row_end, void *stream);
+                       float *curve_isect_contrib, int32_t *status, int32_t img_height,
+                       int32_t img_width, int32_t tile_row_begin, int32_t tile_row_end,
+                       void *stream);
 
 /* Edge endpoint gradients -> cubic control-point gradients with the Bernstein
  * weights at t = e / (S-1); optional scale (sx, sy) applied to the result

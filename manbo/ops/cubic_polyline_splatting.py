@@ -4,7 +4,6 @@ from __future__ import annotations
 
 import torch
 
-from repo_b200 import _native as nat
 from repo_b200 import render as _r
 
 from .cubic_splatting import (  # noqa: F401  (re-exported like the reference module)
@@ -39,12 +38,9 @@ def rasterize_cubic_polyline_forward_kernel(block_x: int = BLOCK_X, block_y: int
     def kernel(primitive_ids_sorted, tile_bins, edges_px, isect_edge_ranges, colors, opacities,
                stroke_widths, inv_sigma2s, background, out_img, final_Ts, final_idx):
         h, w = int(out_img.shape[0]), int(out_img.shape[1])
-        nat.check(nat.call("cs_stroke_forward", nat.ptr(primitive_ids_sorted), nat.ptr(tile_bins),
-                           nat.ptr(edges_px), nat.ptr(isect_edge_ranges), None, nat.ptr(colors),
-                           nat.ptr(opacities), nat.ptr(stroke_widths), nat.ptr(inv_sigma2s),
-                           nat.ptr(background), nat.ptr(out_img), nat.ptr(final_Ts),
-                           nat.ptr(final_idx), None, h, w, 0, (h + BLOCK_Y - 1) // BLOCK_Y,
-                           nat.stream(out_img.device)), "cs_stroke_forward")
+        b = _r.stage_reference_lists(primitive_ids_sorted, tile_bins, edges_px, isect_edge_ranges,
+                                     colors, opacities, inv_sigma2s, None, stroke_widths, h, w)
+        _r.forward_raster(b, background, h, w, outputs=(out_img, final_Ts, final_idx))
     return kernel
 
 
@@ -59,17 +55,21 @@ def rasterize_cubic_polyline_backward_kernel(block_x: int = BLOCK_X, block_y: in
                v_colors, v_opacities, v_stroke_widths, v_inv_sigma2s, collect_curve_contrib_i32,
                curve_contrib_rgb, collect_curve_isect_contrib_i32, curve_isect_contrib):
         h, w = int(final_Ts.shape[0]), int(final_Ts.shape[1])
-        nat.check(nat.call("cs_stroke_backward", nat.ptr(primitive_ids_sorted), nat.ptr(tile_bins),
-                           nat.ptr(edges_px), nat.ptr(isect_edge_ranges), None, nat.ptr(colors),
-                           nat.ptr(opacities), nat.ptr(stroke_widths), nat.ptr(inv_sigma2s),
-                           nat.ptr(background), nat.ptr(final_Ts), nat.ptr(final_idx),
-                           nat.ptr(v_output), None, None, None, nat.ptr(v_edges),
-                           nat.ptr(v_colors), nat.ptr(v_opacities), nat.ptr(v_stroke_widths),
-                           nat.ptr(v_inv_sigma2s),
-                           nat.ptr(curve_contrib_rgb) if int(collect_curve_contrib_i32) else None,
-                           nat.ptr(curve_isect_contrib) if int(collect_curve_isect_contrib_i32) else None,
-                           h, w, 0, (h + BLOCK_Y - 1) // BLOCK_Y, nat.stream(final_Ts.device)),
-                  "cs_stroke_backward")
+        b = _r.stage_reference_lists(primitive_ids_sorted, tile_bins, edges_px, isect_edge_ranges,
+                                     colors, opacities, inv_sigma2s, None, stroke_widths, h, w)
+        ve, vc, vo, vi, vs, cc, ci = _r.raster_backward(
+            b, int(colors.shape[0]), background, final_Ts, final_idx, v_output, h, w,
+            collect_contrib=bool(int(collect_curve_contrib_i32)),
+            collect_isect_contrib=bool(int(collect_curve_isect_contrib_i32)))
+        v_edges.add_(ve)
+        v_colors.add_(vc)
+        v_opacities.add_(vo)
+        v_stroke_widths.add_(vs)
+        v_inv_sigma2s.add_(vi)
+        if cc is not None:
+            curve_contrib_rgb.add_(cc)
+        if ci is not None:
+            curve_isect_contrib.add_(ci)
     return kernel
 
 

@@ -256,17 +256,16 @@ def _check_ranges(isect_edge_ranges, num_intersects):
 def rasterize_cubic_fill_forward_kernel(block_x: int = BLOCK_X, block_y: int = BLOCK_Y,
                                         distance_samples: int = DEFAULT_DISTANCE_SAMPLES,
                                         dtype: str = "float32"):
+    """Callable(primitive_ids_sorted, tile_bins, edges_px, isect_edge_ranges, colors,
+    opacities, inv_sigma2s, fill_rules, background, out_img, final_Ts, final_idx)."""
     _r._check_block(block_x, block_y)
 
     def kernel(primitive_ids_sorted, tile_bins, edges_px, isect_edge_ranges, colors, opacities,
                inv_sigma2s, fill_rules, background, out_img, final_Ts, final_idx):
         h, w = int(out_img.shape[0]), int(out_img.shape[1])
-        nat.check(nat.call("cs_fill_forward", nat.ptr(primitive_ids_sorted), nat.ptr(tile_bins),
-                           nat.ptr(edges_px), nat.ptr(isect_edge_ranges), None, nat.ptr(colors),
-                           nat.ptr(opacities), nat.ptr(inv_sigma2s), nat.ptr(fill_rules),
-                           nat.ptr(background), nat.ptr(out_img), nat.ptr(final_Ts),
-                           nat.ptr(final_idx), None, h, w, 0, (h + BLOCK_Y - 1) // BLOCK_Y,
-                           _stream(out_img)), "cs_fill_forward")
+        b = _r.stage_reference_lists(primitive_ids_sorted, tile_bins, edges_px, isect_edge_ranges,
+                                     colors, opacities, inv_sigma2s, fill_rules, None, h, w)
+        _r.forward_raster(b, background, h, w, outputs=(out_img, final_Ts, final_idx))
     return kernel
 
 
@@ -303,6 +302,8 @@ def rasterize_cubic_fill_forward_tilelang(tile_bounds, block, img_size, primitiv
 def rasterize_cubic_fill_backward_kernel(block_x: int = BLOCK_X, block_y: int = BLOCK_Y,
                                          distance_samples: int = DEFAULT_DISTANCE_SAMPLES,
                                          dtype: str = "float32"):
+    """Callable with the argument order of the reference backward kernel; gradients
+    are accumulated into the given buffers."""
     _r._check_block(block_x, block_y)
 
     def kernel(primitive_ids_sorted, tile_bins, edges_px, isect_edge_ranges, colors, opacities,
@@ -310,16 +311,20 @@ def rasterize_cubic_fill_backward_kernel(block_x: int = BLOCK_X, block_y: int = 
                v_colors, v_opacities, v_inv_sigma2s, collect_curve_contrib, curve_contrib_rgb,
                collect_curve_isect_contrib, curve_isect_contrib):
         h, w = int(final_Ts.shape[0]), int(final_Ts.shape[1])
-        nat.check(nat.call("cs_fill_backward", nat.ptr(primitive_ids_sorted), nat.ptr(tile_bins),
-                           nat.ptr(edges_px), nat.ptr(isect_edge_ranges), None, nat.ptr(colors),
-                           nat.ptr(opacities), nat.ptr(inv_sigma2s), nat.ptr(fill_rules),
-                           nat.ptr(background), nat.ptr(final_Ts), nat.ptr(final_idx),
-                           nat.ptr(v_output), None, None, None, nat.ptr(v_edges),
-                           nat.ptr(v_colors), nat.ptr(v_opacities), nat.ptr(v_inv_sigma2s),
-                           nat.ptr(curve_contrib_rgb) if int(collect_curve_contrib) else None,
-                           nat.ptr(curve_isect_contrib) if int(collect_curve_isect_contrib) else None,
-                           h, w, 0, (h + BLOCK_Y - 1) // BLOCK_Y, _stream(final_Ts)),
-                  "cs_fill_backward")
+        b = _r.stage_reference_lists(primitive_ids_sorted, tile_bins, edges_px, isect_edge_ranges,
+                                     colors, opacities, inv_sigma2s, fill_rules, None, h, w)
+        ve, vc, vo, vi, _, cc, ci = _r.raster_backward(
+            b, int(colors.shape[0]), background, final_Ts, final_idx, v_output, h, w,
+            collect_contrib=bool(int(collect_curve_contrib)),
+            collect_isect_contrib=bool(int(collect_curve_isect_contrib)))
+        v_edges.add_(ve)
+        v_colors.add_(vc)
+        v_opacities.add_(vo)
+        v_inv_sigma2s.add_(vi)
+        if cc is not None:
+            curve_contrib_rgb.add_(cc)
+        if ci is not None:
+            curve_isect_contrib.add_(ci)
     return kernel
 
 

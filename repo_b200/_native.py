@@ -20,8 +20,9 @@ CS_ERR_ARG = 1
 CS_ERR_CAPACITY = 2
 CS_ERR_CUDA = 3
 CS_ERR_UNSUPPORTED = 4
+CS_ERR_TIMEOUT = 5
 _ERR_NAMES = {1: "invalid argument", 2: "intersect capacity exceeded", 3: "CUDA launch failed",
-              4: "unsupported configuration"}
+              4: "unsupported configuration", 5: "device-side wait timed out"}
 
 _P = ctypes.c_void_p
 _I64 = ctypes.c_int64
@@ -40,14 +41,16 @@ SIGNATURES = {
     "cs_tile_bin_edges": (ctypes.c_int, [_P, _I64, _P, _I64, _P]),
     "cs_isect_edge_ranges": (ctypes.c_int, [_P, _P, _P, _I64, _P]),
     "cs_bin_workspace_size": (_SZ, [_I64]),
-    "cs_bin_count": (ctypes.c_int, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64,
-                                    _I64, _I64, _I32, _I32, _I32, _I32, _I32, _F32, _I32, _P]),
-    "cs_bin_sort": (ctypes.c_int, [_P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I32, _I32, _I32,
-                                   _I32, _P]),
-    "cs_fill_forward": (ctypes.c_int, [_P] * 14 + [_I32, _I32, _I32, _I32, _P]),
-    "cs_fill_backward": (ctypes.c_int, [_P] * 22 + [_I32, _I32, _I32, _I32, _P]),
-    "cs_stroke_forward": (ctypes.c_int, [_P] * 14 + [_I32, _I32, _I32, _I32, _P]),
-    "cs_stroke_backward": (ctypes.c_int, [_P] * 23 + [_I32, _I32, _I32, _I32, _P]),
+    "cs_bin_count": (ctypes.c_int, [_P] * 13 + [_I64, _I64, _I64, _I64, _I32, _I32, _I32, _I32,
+                                                _I32, _F32, _I32, _P]),
+    "cs_bin_sort": (ctypes.c_int, [_P] * 7 + [_I64, _I64, _I32, _I32, _I32, _I32] + [_P] * 11
+                    + [_I64, _P]),
+    "cs_stage_workspace_size": (_SZ, [_I64]),
+    "cs_tile_stage": (ctypes.c_int, [_P] * 16 + [_I64, _I32, _I32, _P]),
+    "cs_fill_forward": (ctypes.c_int, [_P] * 12 + [_I32, _I32, _I32, _I32, _P]),
+    "cs_fill_backward": (ctypes.c_int, [_P] * 20 + [_I32, _I32, _I32, _I32, _P]),
+    "cs_stroke_forward": (ctypes.c_int, [_P] * 11 + [_I32, _I32, _I32, _I32, _P]),
+    "cs_stroke_backward": (ctypes.c_int, [_P] * 20 + [_I32, _I32, _I32, _I32, _P]),
     "cs_edge_grads_to_cubics": (ctypes.c_int, [_P, _P, _I64, _I32, _F32, _F32, _P]),
     "cs_ring_segments_forward": (ctypes.c_int, [_P, _P, _P, _P, _P, _I64, _I32, _I32, _P]),
     "cs_ring_segments_backward": (ctypes.c_int, [_P, _P, _P, _P, _P, _I64, _I32, _I32, _P]),

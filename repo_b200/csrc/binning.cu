@@ -11,7 +11,7 @@
 //    per tile sorts its pairs.  This replaces the reference's global 64-bit
 //    key sort with per-tile sorts of (depth key, primitive id), which yields
 //    exactly the order of a stable sort of the reference's keys.
-#include "cs_common.cuh"
+#include "stage.cuh"
 
 namespace cs {
 
@@ -234,8 +234,9 @@ __global__ void edge_ranges_kernel(const int* __restrict__ pids, const int* __re
 // fused pipeline
 
 struct BinWorkspace {
-  int* tile_counts;  // [T]
-  int* cursor;       // [T]
+  int* tile_counts;   // [T] intersects per tile
+  int* tile_ecounts;  // [T] edge slots per tile (upper bound of staged records)
+  int* cursor;        // [T] scatter cursors
 };
 
 __host__ __device__ inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
@@ -243,20 +244,23 @@ __host__ __device__ inline size_t align256(size_t v) { return (v + 255) & ~size_
 inline BinWorkspace bin_ws(void* base, long long ntiles) {
   BinWorkspace w;
   char* b = static_cast<char*>(base);
+  const size_t a = align256(sizeof(int) * ntiles);
   w.tile_counts = reinterpret_cast<int*>(b);
-  w.cursor = reinterpret_cast<int*>(b + align256(sizeof(int) * ntiles));
+  w.tile_ecounts = reinterpret_cast<int*>(b + a);
+  w.cursor = reinterpret_cast<int*>(b + 2 * a);
   return w;
 }
 
 // One warp per primitive: project + bound every segment, union the rects,
-// flatten all segments into edges and count the primitive's tiles within the
-// band of tile rows [r0, r1).
+// flatten all segments into edges, and add the primitive to the intersect and
+// edge-slot counts of its tiles within the band of tile rows [r0, r1).
 __global__ void __launch_bounds__(256) bin_prep_kernel(
     const float* __restrict__ cn, const int* __restrict__ offs, const float* __restrict__ aa,
     const float* __restrict__ sw, const float* __restrict__ basis, float* __restrict__ cpx,
     float* __restrict__ edges, int* __restrict__ pr, int* __restrict__ hits,
-    int* __restrict__ tile_counts, int* __restrict__ status, long long np, long long nseg_total,
-    int S, float half_w, float half_h, int tbx, int tby, int r0, int r1, float pad, int aniso) {
+    int* __restrict__ tile_counts, int* __restrict__ tile_ecounts, int* __restrict__ status,
+    long long np, long long nseg_total, int S, float half_w, float half_h, int tbx, int tby,
+    int r0, int r1, float pad, int aniso) {
   long long p = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   int lane = threadIdx.x & 31;
   if (p >= np) return;
@@ -293,7 +297,6 @@ __global__ void __launch_bounds__(256) bin_prep_kernel(
     *reinterpret_cast<int4*>(pr + p * 4) = make_int4(mnx, mny, mxx, mxy);
     hits[p] = count;
   }
-  // flatten
   const int npts = nseg * S;
   for (int q = lane; q < npts; q += 32) {
     int si = q / S;
@@ -307,58 +310,76 @@ __global__ void __launch_bounds__(256) bin_prep_kernel(
     bernstein_point(pp, basis, S, s, x, y);
     store_point(edges, seg, S, s, x, y);
   }
-  // per-tile counts inside the band
+  const int nedge = nseg * (S - 1);
   int y0 = max(mny, r0), y1 = min(mxy, r1);
   int wdt = mxx - mnx, hgt = y1 - y0;
   if (wdt > 0 && hgt > 0) {
     for (int q = lane; q < wdt * hgt; q += 32) {
       int rr = q / wdt, cc = q - rr * wdt;
-      atomicAdd(tile_counts + (long long)(y0 + rr) * tbx + mnx + cc, 1);
+      const long long t = (long long)(y0 + rr) * tbx + mnx + cc;
+      atomicAdd(tile_counts + t, 1);
+      atomicAdd(tile_ecounts + t, nedge);
     }
   }
 }
 
-// Exclusive scan of per-tile counts into tile ranges; one CTA of 1024.
+// Exclusive scan of per-tile intersect counts into tile ranges [start, end)
+// and of per-tile edge-slot counts into staged-record ranges [base, bound);
+// one CTA of 1024.  Either input may be NULL.  If a total exceeds its
+// capacity every range is written empty and the status is set.
 __global__ void __launch_bounds__(1024) bin_scan_kernel(const int* __restrict__ counts,
+                                                        const int* __restrict__ ecounts,
                                                         int* __restrict__ bins,
+                                                        int* __restrict__ dlr,
                                                         int* __restrict__ cursor,
-                                                        int* __restrict__ total,
-                                                        int* __restrict__ status, long long nt,
-                                                        long long capacity) {
-  __shared__ int warp_tot[32];
-  __shared__ long long s_total;
+                                                        int* __restrict__ counters, long long nt,
+                                                        long long icap, long long dcap) {
+  __shared__ int wa[32], wb[32];
+  __shared__ long long s_ta, s_tb;
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   const long long chunk = (nt + 1023) / 1024;
   const long long b = tid * chunk, e = min(nt, b + chunk);
-  int local = 0;
-  for (long long i = b; i < e; ++i) local += counts[i];
-  int incl = warp_incl_scan(local, lane);
-  if (lane == 31) warp_tot[wid] = incl;
+  int la = 0, lb = 0;
+  for (long long i = b; i < e; ++i) {
+    if (counts) la += counts[i];
+    if (ecounts) lb += ecounts[i];
+  }
+  int ia = warp_incl_scan(la, lane), ib = warp_incl_scan(lb, lane);
+  if (lane == 31) {
+    wa[wid] = ia;
+    wb[wid] = ib;
+  }
   __syncthreads();
   if (wid == 0) {
-    int v = warp_tot[lane];
-    int vi = warp_incl_scan(v, lane);
-    warp_tot[lane] = vi - v;
+    int va = wa[lane], vb = wb[lane];
+    int xa = warp_incl_scan(va, lane), xb = warp_incl_scan(vb, lane);
+    wa[lane] = xa - va;
+    wb[lane] = xb - vb;
     if (lane == 31) {
-      s_total = vi;
-      *total = vi;
-      if (vi > capacity && status) *status = CS_ERR_CAPACITY;
+      s_ta = xa;
+      s_tb = xb;
+      if (counts) counters[0] = xa;
+      if (ecounts) counters[2] = xb;
+      if ((counts && xa > icap) || (ecounts && xb > dcap)) counters[1] = CS_ERR_CAPACITY;
     }
   }
   __syncthreads();
-  const bool overflow = s_total > capacity;
-  int run = warp_tot[wid] + incl - local;
+  const bool overflow = (counts && s_ta > icap) || (ecounts && s_tb > dcap);
+  int ra = wa[wid] + ia - la, rb = wb[wid] + ib - lb;
   for (long long i = b; i < e; ++i) {
-    int c = overflow ? 0 : counts[i];
-    cursor[i] = run;
-    if (c > 0) {
-      bins[2 * i] = run;
-      bins[2 * i + 1] = run + c;
-    } else {
-      bins[2 * i] = 0;
-      bins[2 * i + 1] = 0;
+    if (counts) {
+      const int c = overflow ? 0 : counts[i];
+      cursor[i] = ra;
+      bins[2 * i] = c > 0 ? ra : 0;
+      bins[2 * i + 1] = c > 0 ? ra + c : 0;
+      ra += c;
     }
-    run += c;
+    if (ecounts) {
+      const int c = overflow ? 0 : ecounts[i];
+      dlr[2 * i] = c > 0 ? rb : 0;
+      dlr[2 * i + 1] = c > 0 ? c : 0;
+      rb += c;
+    }
   }
 }
 
@@ -366,11 +387,12 @@ __global__ void __launch_bounds__(1024) bin_scan_kernel(const int* __restrict__ 
 // primitive's tiles' ranges (unordered within a tile).
 __global__ void __launch_bounds__(256) bin_scatter_kernel(
     const int* __restrict__ pr, const float* __restrict__ depths, int* __restrict__ cursor,
-    unsigned long long* __restrict__ pairs, int* __restrict__ status, long long np, int tbx,
-    long long capacity, int r0, int r1) {
+    unsigned long long* __restrict__ pairs, const int* __restrict__ counters, long long np,
+    int tbx, long long capacity, int r0, int r1) {
   long long p = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   int lane = threadIdx.x & 31;
   if (p >= np) return;
+  if (counters[0] > capacity) return;  // overflow reported by the scan
   int4 r = *reinterpret_cast<const int4*>(pr + p * 4);
   int y0 = max(r.y, r0), y1 = min(r.w, r1);
   int wdt = r.z - r.x, hgt = y1 - y0;
@@ -379,16 +401,13 @@ __global__ void __launch_bounds__(256) bin_scatter_kernel(
   for (int q = lane; q < wdt * hgt; q += 32) {
     int rr = q / wdt, cc = q - rr * wdt;
     int slot = atomicAdd(cursor + (long long)(y0 + rr) * tbx + r.x + cc, 1);
-    if (slot < capacity) {
-      pairs[slot] = v;
-    } else if (status) {
-      *status = CS_ERR_CAPACITY;
-    }
+    if (slot < capacity) pairs[slot] = v;
   }
 }
 
 constexpr int kSortThreads = 128;
 constexpr int kSortSmem = 4096;
+constexpr int kStageChunk = 1024;
 
 __device__ __forceinline__ void emit_sorted(unsigned long long v, long long tile, long long pos,
                                             int* __restrict__ pids, long long* __restrict__ ids) {
@@ -396,34 +415,26 @@ __device__ __forceinline__ void emit_sorted(unsigned long long v, long long tile
   if (ids) ids[pos] = (long long)(((unsigned long long)tile << 32) | (v >> 32));
 }
 
-// One CTA per tile: sort the tile's pairs ascending and emit primitive ids and
-// reference-format intersect ids.  Pairs are unique (one per primitive), so
-// the order is total.
-__global__ void __launch_bounds__(kSortThreads) bin_tile_sort_kernel(
-    const int* __restrict__ bins, const float* __restrict__ depths,
-    unsigned long long* __restrict__ pairs, int* __restrict__ pids, long long* __restrict__ ids,
-    const int* __restrict__ total, long long capacity, int tbx, int r0) {
-  __shared__ unsigned long long s[kSortSmem];
-  const long long tile = (long long)(r0 + blockIdx.y) * tbx + blockIdx.x;
-  const int start = bins[2 * tile], end = bins[2 * tile + 1];
-  const int n = end - start;
-  if (n <= 0) return;
-  if (*total > capacity) return;  // overflow: the pairs were not all written
+// Sort one tile's pairs ascending (CTA of kSortThreads); pairs are unique.
+__device__ void sort_tile(unsigned long long* __restrict__ pairs, int start, int n, long long tile,
+                          const float* __restrict__ depths, int* __restrict__ pids,
+                          long long* __restrict__ ids, unsigned long long* s) {
   const int tid = threadIdx.x, lane = tid & 31;
   if (n <= 32) {
-    if (tid >= 32) return;
-    unsigned long long v = lane < n ? pairs[start + lane] : ~0ull;
+    if (tid < 32) {
+      unsigned long long v = lane < n ? pairs[start + lane] : ~0ull;
 #pragma unroll
-    for (int k = 2; k <= 32; k <<= 1) {
+      for (int k = 2; k <= 32; k <<= 1) {
 #pragma unroll
-      for (int j = k >> 1; j > 0; j >>= 1) {
-        unsigned long long o = __shfl_xor_sync(0xffffffffu, v, j);
-        bool up = (lane & k) == 0;
-        bool lower = (lane & j) == 0;
-        v = (lower == up) ? min(v, o) : max(v, o);
+        for (int j = k >> 1; j > 0; j >>= 1) {
+          unsigned long long o = __shfl_xor_sync(0xffffffffu, v, j);
+          bool up = (lane & k) == 0;
+          bool lower = (lane & j) == 0;
+          v = (lower == up) ? min(v, o) : max(v, o);
+        }
       }
+      if (lane < n) emit_sorted(v, tile, start + lane, pids, ids);
     }
-    if (lane < n) emit_sorted(v, tile, start + lane, pids, ids);
     return;
   }
   if (n <= kSortSmem) {
@@ -447,8 +458,7 @@ __global__ void __launch_bounds__(kSortThreads) bin_tile_sort_kernel(
     for (int i = tid; i < n; i += kSortThreads) emit_sorted(s[i], tile, start + i, pids, ids);
     return;
   }
-  // Large tile: rank each pair by counting smaller pairs (all distinct), then
-  // rebuild the keys from the depths.
+  // Large tile: rank each pair by counting smaller pairs, then rebuild keys.
   for (int i = tid; i < n; i += kSortThreads) {
     unsigned long long v = pairs[start + i];
     int rank = 0;
@@ -459,10 +469,211 @@ __global__ void __launch_bounds__(kSortThreads) bin_tile_sort_kernel(
   if (ids) {
     for (int i = tid; i < n; i += kSortThreads) {
       int p = pids[start + i];
-      ids[start + i] =
-          (long long)(((unsigned long long)tile << 32) | (unsigned long long)depth_sort_key(depths[p]));
+      ids[start + i] = (long long)(((unsigned long long)tile << 32) |
+                                   (unsigned long long)depth_sort_key(depths[p]));
     }
   }
+}
+
+struct StageIO {
+  const int* pids;
+  const float4* edges;
+  const int2* ranges;   // per intersect [eb, ee) or NULL
+  const int* eoffs;     // per primitive edge offsets (when ranges is NULL)
+  const float* colors;
+  const float* opac;
+  const float* inv_s2;
+  const int* rules;
+  const float* sw;      // stroke widths: non-NULL selects stroke mode
+  int2* dlr;
+  IMeta* imeta;
+  int* rowoff;
+  DEntry* dl;
+  int tbx;
+};
+
+__device__ __forceinline__ void isect_edges(const StageIO& io, int k, int pid, int& eb, int& ee) {
+  if (io.ranges) {
+    const int2 r = io.ranges[k];
+    eb = r.x;
+    ee = r.y;
+  } else {
+    eb = io.eoffs[pid];
+    ee = io.eoffs[pid + 1];
+  }
+}
+
+// Classify the edges of intersects [rs, re) of one tile and write its staged
+// records (CTA of kSortThreads; see stage.cuh).  Intersects are processed in
+// chunks of kStageChunk: pass 1 counts near edges per intersect (one warp per
+// intersect) and writes the far-edge row offsets; a block scan gives every
+// intersect its record range; pass 2 writes the records in edge order.
+template <bool STROKE>
+__device__ void stage_tile(const StageIO& io, long long tile, int rs, int re, int dbase,
+                           int* s_cnt, int (*s_row)[32], int* s_wt) {
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  constexpr int nw = kSortThreads / 32;
+  const float bx0 = (float)((tile % io.tbx) * kTile) + 0.5f;
+  const float by0 = (float)((tile / io.tbx) * kTile) + 0.5f;
+  const unsigned lt = (1u << lane) - 1u;
+  int base = 0;
+  for (int c0 = rs; c0 < re; c0 += kStageChunk) {
+    const int m = min(kStageChunk, re - c0);
+    for (int i = wid; i < m; i += nw) {
+      const int k = c0 + i;
+      const int pid = io.pids[k];
+      int eb, ee;
+      isect_edges(io, k, pid, eb, ee);
+      IMeta im;
+      intersect_attrs<STROKE>(pid, io.colors, io.opac, io.inv_s2, io.rules, io.sw, im);
+      if (!STROKE) s_row[wid][lane] = 0;
+      __syncwarp();
+      int cnt = 0;
+      for (int e0 = eb; e0 < ee; e0 += 32) {
+        const int e = e0 + lane;
+        bool near = false;
+        unsigned rows = 0u;
+        float4 E = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (e < ee) {
+          E = __ldg(io.edges + e);
+          near = edge_is_near(E, im.dthr, bx0, by0);
+          if (!STROKE && !near) rows = far_right_rows(E, bx0, by0);
+        }
+        cnt += __popc(__ballot_sync(0xffffffffu, near));
+        if (!STROKE && rows) {
+          const int dir = (E.w - E.y) > 0.0f ? 1 : -1;
+          while (rows) {
+            const int r = __ffs(rows) - 1;
+            rows &= rows - 1u;
+            atomicAdd(&s_row[wid][r], dir);
+            atomicAdd(&s_row[wid][16 + r], 1);
+          }
+        }
+      }
+      if (!STROKE) {
+        __syncwarp();
+        if (lane < 16) io.rowoff[(long long)k * 16 + lane] = pack_row(s_row[wid][lane], s_row[wid][16 + lane]);
+        __syncwarp();
+      }
+      if (lane == 0) s_cnt[i] = cnt;
+    }
+    __syncthreads();
+    // exclusive scan of s_cnt[0, m) in place
+    const int per = (m + kSortThreads - 1) / kSortThreads;
+    const int b0 = tid * per, b1 = min(m, b0 + per);
+    int local = 0;
+    for (int q = b0; q < b1; ++q) local += s_cnt[q];
+    const int incl = warp_incl_scan(local, lane);
+    if (lane == 31) s_wt[wid] = incl;
+    __syncthreads();
+    int run = incl - local;
+    for (int w2 = 0; w2 < wid; ++w2) run += s_wt[w2];
+    int total = 0;
+    for (int w2 = 0; w2 < nw; ++w2) total += s_wt[w2];
+    for (int q = b0; q < b1; ++q) {
+      const int c = s_cnt[q];
+      s_cnt[q] = run;
+      run += c;
+    }
+    __syncthreads();
+    for (int i = wid; i < m; i += nw) {
+      const int k = c0 + i;
+      const int pid = io.pids[k];
+      int eb, ee;
+      isect_edges(io, k, pid, eb, ee);
+      IMeta im;
+      intersect_attrs<STROKE>(pid, io.colors, io.opac, io.inv_s2, io.rules, io.sw, im);
+      const int dstart = base + s_cnt[i];
+      int pos = dstart;
+      for (int e0 = eb; e0 < ee; e0 += 32) {
+        const int e = e0 + lane;
+        bool near = false;
+        float4 E = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (e < ee) {
+          E = __ldg(io.edges + e);
+          near = edge_is_near(E, im.dthr, bx0, by0);
+        }
+        const unsigned bal = __ballot_sync(0xffffffffu, near);
+        if (near) io.dl[dbase + pos + __popc(bal & lt)] = make_entry(E, e);
+        pos += __popc(bal);
+      }
+      if (lane == 0) {
+        im.dstart = dstart;
+        im.dcount = pos - dstart;
+        int4* dst = reinterpret_cast<int4*>(io.imeta + k);
+        dst[0] = make_int4(im.dstart, im.dcount, im.pid, im.rule);
+        dst[1] = make_int4(__float_as_int(im.c0), __float_as_int(im.c1), __float_as_int(im.c2),
+                           __float_as_int(im.op));
+        dst[2] = make_int4(__float_as_int(im.a), __float_as_int(im.b), __float_as_int(im.dthr), 0);
+      }
+    }
+    base += total;
+    __syncthreads();
+  }
+  if (tid == 0) io.dlr[tile].y = base;
+}
+
+// One CTA per tile: sort the tile's pairs and emit primitive ids and
+// reference-format intersect ids; then, when staging outputs are given,
+// classify the tile's edges into its staged records.
+template <bool STROKE>
+__global__ void __launch_bounds__(kSortThreads) bin_tile_kernel(
+    const int* __restrict__ bins, const float* __restrict__ depths,
+    unsigned long long* __restrict__ pairs, int* __restrict__ pids, long long* __restrict__ ids,
+    const int* __restrict__ counters, long long icap, long long dcap, int r0, StageIO io) {
+  __shared__ unsigned long long s[kSortSmem];
+  __shared__ int s_cnt[kStageChunk];
+  __shared__ int s_row[kSortThreads / 32][32];
+  __shared__ int s_wt[kSortThreads / 32];
+  const long long tile = (long long)(r0 + blockIdx.y) * io.tbx + blockIdx.x;
+  const int start = bins[2 * tile], end = bins[2 * tile + 1];
+  const int n = end - start;
+  if (n <= 0) return;
+  if (counters[0] > icap) return;  // overflow: the pairs were not all written
+  sort_tile(pairs, start, n, tile, depths, pids, ids, s);
+  if (!io.imeta) return;
+  if (counters[2] > dcap) return;
+  __syncthreads();
+  stage_tile<STROKE>(io, tile, start, end, io.dlr[tile].x, s_cnt, s_row, s_wt);
+}
+
+// Standalone staging for a reference-format intersect list: per-tile edge-slot
+// bound (one warp per tile) ...
+__global__ void tile_esum_kernel(const int* __restrict__ bins, const int* __restrict__ pids,
+                                 const int2* __restrict__ ranges, const int* __restrict__ eoffs,
+                                 int* __restrict__ ecounts, long long nt) {
+  const long long t = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (t >= nt) return;
+  const int rs = bins[2 * t], re = bins[2 * t + 1];
+  int acc = 0;
+  for (int k = rs + lane; k < re; k += 32) {
+    if (ranges) {
+      const int2 r = ranges[k];
+      acc += max(0, r.y - r.x);
+    } else {
+      const int p = pids[k];
+      acc += max(0, eoffs[p + 1] - eoffs[p]);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (lane == 0) ecounts[t] = acc;
+}
+
+// ... and the staging pass itself (one CTA per tile).
+template <bool STROKE>
+__global__ void __launch_bounds__(kSortThreads) tile_stage_kernel(const int* __restrict__ bins,
+                                                                  const int* __restrict__ counters,
+                                                                  long long dcap, StageIO io) {
+  __shared__ int s_cnt[kStageChunk];
+  __shared__ int s_row[kSortThreads / 32][32];
+  __shared__ int s_wt[kSortThreads / 32];
+  const long long tile = (long long)blockIdx.y * io.tbx + blockIdx.x;
+  const int rs = bins[2 * tile], re = bins[2 * tile + 1];
+  if (re <= rs) return;
+  if (counters[2] > dcap) return;
+  stage_tile<STROKE>(io, tile, rs, re, io.dlr[tile].x, s_cnt, s_row, s_wt);
 }
 
 }  // namespace cs
@@ -542,55 +753,134 @@ int cs_isect_edge_ranges(const int32_t* prim_ids_sorted, const int32_t* prim_edg
 }
 
 size_t cs_bin_workspace_size(int64_t num_tiles) {
-  return align256(sizeof(int) * num_tiles) * 2;
+  return align256(sizeof(int) * num_tiles) * 3;
 }
 
 int cs_bin_count(const float* cubics_norm, const int32_t* prim_seg_offsets, const float* aa_widths,
                  const float* stroke_widths, const float* basis, float* cubics_px,
                  float* edges_px, int32_t* prim_tile_ranges, int32_t* num_tiles_hit,
-                 int32_t* tile_bins, int32_t* num_intersects, int32_t* status, void* workspace,
-                 int64_t num_primitives, int64_t num_segments, int64_t capacity, int32_t samples,
-                 int32_t img_height, int32_t img_width, int32_t tile_row_begin,
-                 int32_t tile_row_end, float aabb_pad, int32_t aniso, void* stream) {
-  if (num_primitives < 0 || samples < 2 || img_height <= 0 || img_width <= 0 || !workspace)
+                 int32_t* tile_bins, int32_t* tile_dlist, int32_t* counters, void* workspace,
+                 int64_t num_primitives, int64_t num_segments, int64_t isect_capacity,
+                 int64_t dlist_capacity, int32_t samples, int32_t img_height, int32_t img_width,
+                 int32_t tile_row_begin, int32_t tile_row_end, float aabb_pad, int32_t aniso,
+                 void* stream) {
+  if (num_primitives < 0 || samples < 2 || img_height <= 0 || img_width <= 0 || !workspace ||
+      !counters || !tile_bins || !tile_dlist)
     return CS_ERR_ARG;
   cudaStream_t st = (cudaStream_t)stream;
   const int tbx = (img_width + kTile - 1) / kTile, tby = (img_height + kTile - 1) / kTile;
   const long long nt = (long long)tbx * tby;
   const int r0 = max(0, tile_row_begin), r1 = min(tby, tile_row_end);
   BinWorkspace ws = bin_ws(workspace, nt);
-  cudaMemsetAsync(ws.tile_counts, 0, sizeof(int) * nt, st);
+  cudaMemsetAsync(ws.tile_counts, 0, align256(sizeof(int) * nt) * 2, st);
   if (num_primitives > 0) {
     bin_prep_kernel<<<ceil_div(num_primitives * 32, 256), 256, 0, st>>>(
         cubics_norm, prim_seg_offsets, aa_widths, stroke_widths, basis, cubics_px, edges_px,
-        prim_tile_ranges, num_tiles_hit, ws.tile_counts, status, num_primitives, num_segments,
-        samples,
-        0.5f * (float)img_width, 0.5f * (float)img_height, tbx, tby, r0, r1, aabb_pad, aniso);
+        prim_tile_ranges, num_tiles_hit, ws.tile_counts, ws.tile_ecounts, counters + 1,
+        num_primitives, num_segments, samples, 0.5f * (float)img_width,
+        0.5f * (float)img_height, tbx, tby, r0, r1, aabb_pad, aniso);
   }
-  bin_scan_kernel<<<1, 1024, 0, st>>>(ws.tile_counts, tile_bins, ws.cursor, num_intersects,
-                                      status, nt, capacity < 0 ? 0 : capacity);
+  bin_scan_kernel<<<1, 1024, 0, st>>>(ws.tile_counts, ws.tile_ecounts, tile_bins, tile_dlist,
+                                      ws.cursor, counters, nt, (isect_capacity > 0 ? isect_capacity : 0),
+                                      (dlist_capacity > 0 ? dlist_capacity : 0));
   return launch_status();
 }
 
+static StageIO stage_io(const int32_t* pids, const float* edges_px, const int32_t* ranges,
+                        const int32_t* eoffs, const float* colors, const float* opacities,
+                        const float* inv_sigma2s, const int32_t* fill_rules,
+                        const float* stroke_widths, int32_t* tile_dlist, void* imeta,
+                        int32_t* rowoff, void* dlist, int tbx) {
+  StageIO io;
+  io.pids = pids;
+  io.edges = reinterpret_cast<const float4*>(edges_px);
+  io.ranges = reinterpret_cast<const int2*>(ranges);
+  io.eoffs = eoffs;
+  io.colors = colors;
+  io.opac = opacities;
+  io.inv_s2 = inv_sigma2s;
+  io.rules = fill_rules;
+  io.sw = stroke_widths;
+  io.dlr = reinterpret_cast<int2*>(tile_dlist);
+  io.imeta = reinterpret_cast<IMeta*>(imeta);
+  io.rowoff = rowoff;
+  io.dl = reinterpret_cast<DEntry*>(dlist);
+  io.tbx = tbx;
+  return io;
+}
+
 int cs_bin_sort(const int32_t* prim_tile_ranges, const float* depths, const int32_t* tile_bins,
-                const int32_t* num_intersects, int32_t* prim_ids_sorted, int64_t* isect_ids_sorted,
-                int32_t* status, void* workspace, int64_t num_primitives, int64_t capacity,
+                int32_t* prim_ids_sorted, int64_t* isect_ids_sorted, int32_t* counters,
+                void* workspace, int64_t num_primitives, int64_t isect_capacity,
                 int32_t img_height, int32_t img_width, int32_t tile_row_begin,
-                int32_t tile_row_end, void* stream) {
-  if (num_primitives < 0 || capacity < 0 || !workspace || !isect_ids_sorted) return CS_ERR_ARG;
+                int32_t tile_row_end, const float* edges_px, const int32_t* prim_edge_offsets,
+                const float* colors, const float* opacities, const float* inv_sigma2s,
+                const int32_t* fill_rules, const float* stroke_widths, int32_t* tile_dlist,
+                void* imeta, int32_t* rowoff, void* dlist, int64_t dlist_capacity,
+                void* stream) {
+  if (num_primitives < 0 || isect_capacity < 0 || !workspace || !isect_ids_sorted || !counters)
+    return CS_ERR_ARG;
+  const bool stage = imeta != nullptr;
+  if (stage && (!edges_px || !prim_edge_offsets || !colors || !opacities || !inv_sigma2s ||
+                !tile_dlist || !dlist || (!stroke_widths && (!fill_rules || !rowoff))))
+    return CS_ERR_ARG;
   cudaStream_t st = (cudaStream_t)stream;
   const int tbx = (img_width + kTile - 1) / kTile, tby = (img_height + kTile - 1) / kTile;
   const long long nt = (long long)tbx * tby;
   const int r0 = max(0, tile_row_begin), r1 = min(tby, tile_row_end);
-  if (r1 <= r0 || num_primitives == 0 || capacity == 0) return CS_OK;
+  if (r1 <= r0 || num_primitives == 0 || isect_capacity == 0) return CS_OK;
   BinWorkspace ws = bin_ws(workspace, nt);
   unsigned long long* pairs = reinterpret_cast<unsigned long long*>(isect_ids_sorted);
   bin_scatter_kernel<<<ceil_div(num_primitives * 32, 256), 256, 0, st>>>(
-      prim_tile_ranges, depths, ws.cursor, pairs, status, num_primitives, tbx, capacity, r0, r1);
+      prim_tile_ranges, depths, ws.cursor, pairs, counters, num_primitives, tbx, isect_capacity,
+      r0, r1);
+  StageIO io = stage_io(prim_ids_sorted, edges_px, nullptr, prim_edge_offsets, colors, opacities,
+                        inv_sigma2s, fill_rules, stroke_widths, tile_dlist, imeta, rowoff, dlist,
+                        tbx);
   dim3 grid(tbx, r1 - r0);
-  bin_tile_sort_kernel<<<grid, kSortThreads, 0, st>>>(tile_bins, depths, pairs, prim_ids_sorted,
-                                                     reinterpret_cast<long long*>(isect_ids_sorted),
-                                                     num_intersects, capacity, tbx, r0);
+  if (stroke_widths)
+    bin_tile_kernel<true><<<grid, kSortThreads, 0, st>>>(
+        tile_bins, depths, pairs, prim_ids_sorted, reinterpret_cast<long long*>(isect_ids_sorted),
+        counters, isect_capacity, (dlist_capacity > 0 ? dlist_capacity : 0), r0, io);
+  else
+    bin_tile_kernel<false><<<grid, kSortThreads, 0, st>>>(
+        tile_bins, depths, pairs, prim_ids_sorted, reinterpret_cast<long long*>(isect_ids_sorted),
+        counters, isect_capacity, (dlist_capacity > 0 ? dlist_capacity : 0), r0, io);
+  return launch_status();
+}
+
+size_t cs_stage_workspace_size(int64_t num_tiles) { return align256(sizeof(int) * num_tiles); }
+
+int cs_tile_stage(const int32_t* prim_ids_sorted, const int32_t* tile_bins, const float* edges_px,
+                  const int32_t* isect_edge_ranges, const int32_t* prim_edge_offsets,
+                  const float* colors, const float* opacities, const float* inv_sigma2s,
+                  const int32_t* fill_rules, const float* stroke_widths, int32_t* tile_dlist,
+                  void* imeta, int32_t* rowoff, void* dlist, int32_t* counters, void* workspace,
+                  int64_t dlist_capacity, int32_t img_height, int32_t img_width, void* stream) {
+  if (!prim_ids_sorted || !tile_bins || !edges_px || (!isect_edge_ranges && !prim_edge_offsets) ||
+      !colors || !opacities || !inv_sigma2s || !tile_dlist || !imeta || !dlist || !counters ||
+      !workspace || (!stroke_widths && (!fill_rules || !rowoff)) || img_height <= 0 ||
+      img_width <= 0)
+    return CS_ERR_ARG;
+  cudaStream_t st = (cudaStream_t)stream;
+  const int tbx = (img_width + kTile - 1) / kTile, tby = (img_height + kTile - 1) / kTile;
+  const long long nt = (long long)tbx * tby;
+  int* ecounts = static_cast<int*>(workspace);
+  tile_esum_kernel<<<ceil_div(nt * 32, 256), 256, 0, st>>>(
+      tile_bins, prim_ids_sorted, reinterpret_cast<const int2*>(isect_edge_ranges),
+      prim_edge_offsets, ecounts, nt);
+  bin_scan_kernel<<<1, 1024, 0, st>>>(nullptr, ecounts, nullptr, tile_dlist, nullptr, counters,
+                                      nt, 0, (dlist_capacity > 0 ? dlist_capacity : 0));
+  StageIO io = stage_io(prim_ids_sorted, edges_px, isect_edge_ranges, prim_edge_offsets, colors,
+                        opacities, inv_sigma2s, fill_rules, stroke_widths, tile_dlist, imeta,
+                        rowoff, dlist, tbx);
+  dim3 grid(tbx, tby);
+  if (stroke_widths)
+    tile_stage_kernel<true><<<grid, kSortThreads, 0, st>>>(tile_bins, counters,
+                                                           (dlist_capacity > 0 ? dlist_capacity : 0), io);
+  else
+    tile_stage_kernel<false><<<grid, kSortThreads, 0, st>>>(tile_bins, counters,
+                                                            (dlist_capacity > 0 ? dlist_capacity : 0), io);
   return launch_status();
 }
 

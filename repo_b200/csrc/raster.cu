@@ -2,91 +2,59 @@
 // backward (sm_100a).
 //
 // One CTA per 16x16 tile, 128 threads, two horizontally adjacent pixels per
-// thread.  The tile's intersects (front-to-back in the forward, back-to-front
-// in the backward) are staged in batches: warp 0 gathers up to 32 intersects
-// ("pieces"; a primitive with more than kDCap edges is split into several
-// pieces) and the CTA classifies every edge of the batch against the tile:
+// thread (a warp owns four pixel rows).  The tile's geometry was staged once
+// per frame by the binning pass (stage.cuh): a compact list of the edges that
+// come within d_thr of the tile, per intersect, plus per-row winding offsets
+// for far edges right of the tile.  The CTA brings that list into shared
+// memory with cp.async.bulk copies of up to kChunk records, double-buffered
+// and completed on an mbarrier; after that every warp walks the intersects on
+// its own, with no CTA barrier until the next chunk.
 //
-//  * near edges -- the edge's bounding box comes within d_thr of the tile's
-//    pixel-centre box -- are compacted, in edge order, into a shared-memory
-//    list with their per-frame constants (direction, 1/|d|^2, x0*dy);
-//  * far edges whose y-span crosses tile rows and that lie entirely to the
-//    right of the tile add +-1 to per-row winding offsets (every pixel of such
-//    a row is crossed by them, far beyond rounding error);
-//  * all other edges cannot touch any pixel of the tile and are dropped.
+// Why visiting only near edges is exact: d_thr is the distance beyond which a
+// pixel's coverage is saturated for the primitive (fill: exactly 1.0f inside
+// and below alpha_min outside; stroke: below alpha_min).  A pixel closer than
+// d_thr to the polyline has its closest edge in the near list, so its minimum
+// distance is the exact one; a farther pixel gets a saturated coverage from
+// whatever edges it sees, identical to visiting every edge.  The crossing
+// test needs all edges that span the pixel's row and lie right of it: near
+// ones are tested per pixel, far ones are the per-row offsets.  This is the
+// reference's per-pixel loop over every edge of every intersect
+// (manbo/ops/cubic_splatting.py:1070-1136 forward, :1429-1501 backward;
+// cubic_polyline_splatting.py:175-216, :480-529) with the same arithmetic in
+// the same order (-fmad=false) and exp = cs_expf.
 //
-// d_thr is the distance beyond which a pixel's coverage is saturated for the
-// primitive: fill coverage is exactly 1.0f inside (logit <= -20) and below
-// alpha_min outside; stroke coverage is below alpha_min.  A pixel closer than
-// d_thr to the polyline has its closest edge in the near list, so its
-// distance is the exact minimum; a farther pixel gets a saturated coverage
-// whichever edges are visited.  Results are therefore those of visiting every
-// edge, which is what the reference does
-// (manbo/ops/cubic_splatting.py:1070-1136 and :1429-1501).
-//
-// Per-pixel arithmetic follows the reference formulas in their written order
-// (-fmad=false); exp is cs_expf.  The backward recomputes the geometry with
-// the first-minimum closest edge (lexicographic on (d^2, edge id)), walks the
-// intersects in reverse with T <- T / (1 - alpha), reduces per-primitive
-// gradients over the warp and the CTA in shared memory, and accumulates edge
-// gradients per near edge in shared memory before one global atomic per edge.
-#include <math_constants.h>
-
-#include "cs_common.cuh"
+// The backward walks the intersects in reverse from each warp's largest
+// final_idx with T <- T / (1 - alpha), takes the first-minimum closest edge
+// (lexicographic on (d^2, edge id), the reference's strict-< rule), reduces
+// per-primitive gradients over the warp into shared memory, and accumulates
+// edge gradients per staged edge in shared memory before one global atomic
+// per edge and chunk.
+#include "stage.cuh"
 
 namespace cs {
 
-constexpr int kRT = 128;     // threads per CTA: 16 rows x 8 pixel pairs
-constexpr int kDCap = 512;   // near-edge entries per batch (4 edges per thread)
-constexpr int kNP = 32;      // pieces per batch (one per lane of warp 0)
-constexpr int kFirst = 1;    // piece holds the first edge of its intersect
-constexpr int kLast = 2;     // piece holds the last edge of its intersect
-constexpr int kAcc = 10;     // per-piece gradient accumulators
-
-struct __align__(16) Piece {
-  int k, pid, ebeg, eend;
-  int flat, dstart, dcount, flags;
-  float c0, c1, c2, op;
-  float a;     // fill: inv_sigma = sqrt(max(inv_sigma2, eps)); stroke: max(inv_sigma2, eps)
-  float b;     // stroke: half stroke width
-  float dthr;  // culling distance
-  int rule;    // fill rule (0 even-odd, else nonzero)
-};
-
-template <bool BWD>
-struct Smem {
-  Piece piece[kNP];
-  float4 dA[kDCap];  // x0, y0, vx, vy
-  float4 dB[kDCap];  // 1/max(|v|^2, eps), y1, x0*vy, edge id (bits)
-  int rowwind[kNP][16];
-  int rowcnt[kNP][16];
-  int pcount[kNP];
-  int warp_tot[kRT / 32];
-  int npieces, total, ndl;
-  int next_k, next_e;
-  float pacc[BWD ? kNP : 1][kAcc];
-  float4 dgrad[BWD ? kDCap : 1];
-};
+constexpr int kRT = 128;              // threads per CTA: 16 rows x 8 pixel pairs
+constexpr int kChunk = 256;           // staged edge records per shared-memory buffer
+constexpr int kPaccCap = 64;          // intersects per tile with shared accumulators
+constexpr int kAcc = 10;              // per-intersect gradient accumulators
+constexpr int kSpinLimit = 1 << 22;   // mbarrier polls before reporting a timeout
 
 struct RasterArgs {
   const int* pids;
   const int* bins;
-  const float4* edges;
-  const int2* ranges;
-  const int* eoffs;
-  const float* colors;
-  const float* opac;
-  const float* inv_s2;
-  const int* rules;
-  const float* sw;
+  const int2* dlr;      // per tile: first staged record, record count
+  const IMeta* meta;
+  const int* rowoff;    // [I][16] packed row winding offsets (fill)
+  const DEntry* dl;
   const float* bg;
   int H, W, tbx, r0;
+  int* status;
   // forward outputs
   float* out;
   float* fts;
   int* fidx;
-  float* out_chw;  // optional clamp(out, 0, 1) in [3, H, W]
-  // backward inputs / outputs
+  float* out_chw;
+  // backward
   const float* fts_in;
   const int* fidx_in;
   const float* v_out;
@@ -103,226 +71,65 @@ struct RasterArgs {
 };
 
 // ---------------------------------------------------------------------------
-// batch construction (warp 0)
+// bulk copies into shared memory (non-multicast cp.async.bulk + mbarrier)
 
-template <bool STROKE>
-__device__ __forceinline__ void fill_piece_attrs(Piece& pc, const RasterArgs& A) {
-  const int pid = pc.pid;
-  pc.c0 = A.colors[pid * 3];
-  pc.c1 = A.colors[pid * 3 + 1];
-  pc.c2 = A.colors[pid * 3 + 2];
-  const float op = A.opac[pid];
-  pc.op = op;
-  const float is2 = A.inv_s2[pid];
-  const float lg = logf(fmaxf(255.0f * op, 1.0f)) + 1.0f;
-  if (!STROKE) {
-    pc.a = sqrtf(fmaxf(is2, kEps));
-    pc.b = 0.0f;
-    pc.rule = A.rules[pid];
-    const float L = fmaxf(20.0f, lg);
-    pc.dthr = (L <= 59.0f && pc.a > 0.0f) ? 0.5f * L / pc.a + 0.5f : CUDART_INF_F;
-  } else {
-    pc.a = fmaxf(is2, kEps);
-    pc.b = fmaxf(0.0f, A.sw[pid]) * 0.5f;
-    pc.rule = 1;
-    pc.dthr = pc.b + sqrtf(2.0f * lg / pc.a) + 0.5f;
-  }
-  if (!(pc.dthr == pc.dthr)) pc.dthr = CUDART_INF_F;
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
-// Fills piece[0..npieces) for the next batch.  Forward (REV = false) walks
-// intersects upward from next_k; next_e counts edges of next_k already
-// consumed.  Backward walks downward; next_e is the absolute end of the edges
-// of next_k still to visit (-1 = all).  Sets npieces = 0 when done.
-template <bool STROKE, bool REV, bool BWD>
-__device__ void build_batch(Smem<BWD>& sm, const RasterArgs& A, int rs, int re, int lane) {
-  const int nk = sm.next_k, ne = sm.next_e;
-  const int k = REV ? nk - lane : nk + lane;
-  const bool valid = REV ? (k >= rs) : (k < re);
-  int pid = 0, eb = 0, ee = 0;
-  if (valid) {
-    pid = A.pids[k];
-    if (A.ranges) {
-      int2 r = A.ranges[k];
-      eb = r.x;
-      ee = r.y;
-    } else {
-      eb = A.eoffs[pid];
-      ee = A.eoffs[pid + 1];
+__device__ __forceinline__ void mbar_init(uint64_t* bar) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Issued by one thread: arrive on `bar` expecting `bytes`, then copy.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+               "r"(bytes)
+               : "memory");
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait; the outcome is agreed by the whole CTA so that nobody is left
+// at a later barrier.  On timeout the device status is set and the CTA stops.
+__device__ __forceinline__ bool wait_chunk(uint64_t* bar, uint32_t parity, int* status) {
+  bool ok = false;
+  for (int i = 0; i < kSpinLimit; ++i) {
+    if (mbar_try_wait(bar, parity)) {
+      ok = true;
+      break;
     }
-    if (!REV && lane == 0) eb += ne;
-    if (REV && lane == 0 && ne >= 0) ee = ne;
   }
-  const int n = valid ? max(0, ee - eb) : 0;
-  const int incl = warp_incl_scan(n, lane);
-  const unsigned vmask = __ballot_sync(0xffffffffu, valid);
-  const unsigned fmask = __ballot_sync(0xffffffffu, valid && incl <= kDCap);
-  const int nvalid = __popc(vmask);
-  const int cnt = __popc(fmask);
-  __syncwarp();
-  if (nvalid == 0) {
-    if (lane == 0) sm.npieces = 0;
-    return;
-  }
-  if (cnt == 0) {
-    // The first intersect alone exceeds the staging capacity: one piece.
-    if (lane == 0) {
-      Piece pc;
-      pc.k = k;
-      pc.pid = pid;
-      pc.flat = 0;
-      if (!REV) {
-        pc.ebeg = eb;
-        pc.eend = eb + kDCap;
-        pc.flags = (ne == 0) ? kFirst : 0;
-        sm.next_e = ne + kDCap;
-      } else {
-        pc.eend = ee;
-        pc.ebeg = ee - kDCap;
-        pc.flags = (ne < 0) ? kLast : 0;
-        sm.next_e = pc.ebeg;
-      }
-      fill_piece_attrs<STROKE>(pc, A);
-      sm.piece[0] = pc;
-      sm.npieces = 1;
-      sm.total = kDCap;
-    }
-    return;
-  }
-  if (lane < cnt) {
-    Piece pc;
-    pc.k = k;
-    pc.pid = pid;
-    pc.ebeg = eb;
-    pc.eend = ee;
-    pc.flat = incl - n;
-    if (!REV)
-      pc.flags = kLast | ((lane > 0 || ne == 0) ? kFirst : 0);
-    else
-      pc.flags = kFirst | ((lane > 0 || ne < 0) ? kLast : 0);
-    fill_piece_attrs<STROKE>(pc, A);
-    sm.piece[lane] = pc;
-  }
-  if (lane == cnt - 1) {
-    sm.npieces = cnt;
-    sm.total = incl;
-    sm.next_k = REV ? nk - cnt : nk + cnt;
-    sm.next_e = REV ? -1 : 0;
-  }
+  const bool all = __syncthreads_and(ok);
+  if (!all && threadIdx.x == 0 && status) atomicExch(status, CS_ERR_TIMEOUT);
+  return all;
 }
 
 // ---------------------------------------------------------------------------
-// edge classification and near-list compaction (all threads)
-
-template <bool STROKE, bool BWD>
-__device__ void stage_batch(Smem<BWD>& sm, const RasterArgs& A, int tx, int ty, int tid) {
-  const int lane = tid & 31, wid = tid >> 5;
-  const int tot = sm.total, np = sm.npieces;
-  const float bx0 = (float)(tx * kTile) + 0.5f, bx1 = bx0 + 15.0f;
-  const float by0 = (float)(ty * kTile) + 0.5f, by1 = by0 + 15.0f;
-  const int q0 = tid * 4;
-  float4 ev[4];
-  int eidv[4];
-  unsigned nearbits = 0;
-  int mycount = 0;
-  if (q0 < tot) {
-    // piece containing q0: last piece whose flat <= q0
-    int lo = 0, hi = np - 1;
-    while (lo < hi) {
-      int mid = (lo + hi + 1) >> 1;
-      if (sm.piece[mid].flat <= q0) lo = mid; else hi = mid - 1;
-    }
-    int pc = lo;
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int q = q0 + u;
-      if (q >= tot) break;
-      while (pc + 1 < np && sm.piece[pc + 1].flat <= q) ++pc;
-      const Piece& P = sm.piece[pc];
-      const int eid = P.ebeg + (q - P.flat);
-      const float4 e = A.edges[eid];
-      ev[u] = e;
-      eidv[u] = eid;
-      const float d = P.dthr;
-      const float xmin = fminf(e.x, e.z), xmax = fmaxf(e.x, e.z);
-      const float ymin = fminf(e.y, e.w), ymax = fmaxf(e.y, e.w);
-      const bool moderate = fabsf(e.x) < 4.0e6f && fabsf(e.y) < 4.0e6f && fabsf(e.z) < 4.0e6f &&
-                            fabsf(e.w) < 4.0e6f;
-      const bool near = !moderate || (xmax >= bx0 - d && xmin <= bx1 + d && ymax >= by0 - d &&
-                                      ymin <= by1 + d);
-      if (near) {
-        nearbits |= 1u << u;
-        ++mycount;
-        atomicAdd(&sm.pcount[pc], 1);
-      } else if (!STROKE && xmin > bx1 && ymax >= by0 && ymin <= by1) {
-        // entirely right of the tile: crosses every pixel of the rows it spans
-        const float vy = e.w - e.y;
-        const int dir = vy > 0.0f ? 1 : -1;
-#pragma unroll 4
-        for (int r = 0; r < 16; ++r) {
-          const float py = by0 + (float)r;
-          if (((e.y <= py) & (e.w > py)) | ((e.y > py) & (e.w <= py))) {
-            atomicAdd(&sm.rowwind[pc][r], dir);
-            atomicAdd(&sm.rowcnt[pc][r], 1);
-          }
-        }
-      }
-    }
-  }
-  // block exclusive scan of the per-thread near counts (edge order preserved)
-  const int incl = warp_incl_scan(mycount, lane);
-  if (lane == 31) sm.warp_tot[wid] = incl;
-  __syncthreads();
-  int base = 0;
-#pragma unroll
-  for (int w = 0; w < kRT / 32; ++w) base += (w < wid) ? sm.warp_tot[w] : 0;
-  int pos = base + incl - mycount;
-  if (tid == kRT - 1) sm.ndl = base + incl;
-#pragma unroll
-  for (int u = 0; u < 4; ++u) {
-    if (nearbits & (1u << u)) {
-      const float4 e = ev[u];
-      const float vx = e.z - e.x, vy = e.w - e.y;
-      const float vv = vx * vx + vy * vy;
-      const float inv_vv = 1.0f / fmaxf(vv, kEps);
-      sm.dA[pos] = make_float4(e.x, e.y, vx, vy);
-      sm.dB[pos] = make_float4(inv_vv, e.w, e.x * vy, __int_as_float(eidv[u]));
-      ++pos;
-    }
-  }
-  if (wid == 0) {
-    const int c = lane < np ? sm.pcount[lane] : 0;
-    const int ci = warp_incl_scan(c, lane);
-    if (lane < np) {
-      sm.piece[lane].dstart = ci - c;
-      sm.piece[lane].dcount = c;
-    }
-  }
-}
-
-template <bool BWD>
-__device__ __forceinline__ void zero_batch_smem(Smem<BWD>& sm, int tid) {
-  int* rw = &sm.rowwind[0][0];
-  int* rc = &sm.rowcnt[0][0];
-  for (int i = tid; i < kNP * 16; i += kRT) {
-    rw[i] = 0;
-    rc[i] = 0;
-  }
-  if (tid < kNP) sm.pcount[tid] = 0;
-  if (BWD) {
-    float* pa = &sm.pacc[0][0];
-    for (int i = tid; i < kNP * kAcc; i += kRT) pa[i] = 0.0f;
-    for (int i = tid; i < kDCap; i += kRT) sm.dgrad[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-  }
-}
-
-// ---------------------------------------------------------------------------
-// per-pixel geometry
-
-struct FwdGeom {
-  float md;
-  int w, n;
-};
+// per-pixel arithmetic (reference formulas, written order)
 
 __device__ __forceinline__ float seg_d2(float px, float py, float wy, const float4& A,
                                         const float4& B, float& proj, float& cx, float& cy) {
@@ -354,118 +161,155 @@ __device__ __forceinline__ float stroke_coverage(float md, float half_sw, float 
   return cs_expf(-sigma);
 }
 
+__device__ __forceinline__ void load_meta(const IMeta* __restrict__ p, IMeta& m) {
+  const int4* q = reinterpret_cast<const int4*>(p);
+  int4 x = __ldg(q), y = __ldg(q + 1), z = __ldg(q + 2);
+  m.dstart = x.x; m.dcount = x.y; m.pid = x.z; m.rule = x.w;
+  m.c0 = __int_as_float(y.x); m.c1 = __int_as_float(y.y);
+  m.c2 = __int_as_float(y.z); m.op = __int_as_float(y.w);
+  m.a = __int_as_float(z.x); m.b = __int_as_float(z.y); m.dthr = __int_as_float(z.z);
+  m.spare = 0.0f;
+}
+
 // ---------------------------------------------------------------------------
 // forward
 
+struct FwdPix {
+  float T, a0, a1, a2, md;
+  int cur, w, n;
+  bool done;
+};
+
+template <bool STROKE>
+__device__ __forceinline__ void fwd_entries(const DEntry* __restrict__ buf, int c0, int lo, int hi,
+                                            float px0, float px1, float py, FwdPix& p0,
+                                            FwdPix& p1) {
+  for (int d = lo; d < hi; ++d) {
+    const float4 EA = buf[d - c0].a;
+    const float4 EB = buf[d - c0].b;
+    const float wy = py - EA.y;
+    float pr, cx, cy;
+    p0.md = fminf(p0.md, seg_d2(px0, py, wy, EA, EB, pr, cx, cy));
+    p1.md = fminf(p1.md, seg_d2(px1, py, wy, EA, EB, pr, cx, cy));
+    if (!STROKE) {
+      if (((EA.y <= py) & (EB.y > py)) | ((EA.y > py) & (EB.y <= py))) {
+        const float lhs = EB.z + wy * EA.z;
+        const float rhs0 = px0 * EA.w, rhs1 = px1 * EA.w;
+        const bool pos = EA.w > 0.0f;
+        const int h0 = pos ? (lhs > rhs0) : (lhs < rhs0);
+        const int h1 = pos ? (lhs > rhs1) : (lhs < rhs1);
+        const int sg = pos ? 1 : -1;
+        p0.n += h0;
+        p1.n += h1;
+        p0.w += h0 * sg;
+        p1.w += h1 * sg;
+      }
+    }
+  }
+}
+
+template <bool STROKE>
+__device__ __forceinline__ void fwd_composite(FwdPix& p, const IMeta& m, int k) {
+  if (p.done) return;
+  float cov;
+  if (!STROKE) {
+    float sign, dist;
+    cov = fill_coverage(p.md, p.w, p.n, m.rule, m.a, sign, dist);
+  } else {
+    float dist, edge_d;
+    cov = stroke_coverage(p.md, m.b, m.a, dist, edge_d);
+  }
+  const float alpha = fminf(kAlphaCap, m.op * cov);
+  if (alpha < kAlphaMin) return;
+  const float nT = p.T * (1.0f - alpha);
+  const float vis = alpha * p.T;
+  p.a0 += m.c0 * vis;
+  p.a1 += m.c1 * vis;
+  p.a2 += m.c2 * vis;
+  p.T = nT;
+  p.cur = k;
+  if (nT <= kTransStop) p.done = true;
+}
+
 template <bool STROKE>
 __global__ void __launch_bounds__(kRT) raster_forward_kernel(const RasterArgs A) {
-  __shared__ Smem<false> sm;
+  __shared__ __align__(128) DEntry buf[2][kChunk];
+  __shared__ __align__(8) uint64_t bars[2];
   const int tid = threadIdx.x, lane = tid & 31;
   const int tx = blockIdx.x, ty = A.r0 + blockIdx.y;
   const long long tile = (long long)ty * A.tbx + tx;
   const int rs = A.bins[2 * tile], re = A.bins[2 * tile + 1];
+  const int2 dr = A.dlr[tile];
+  const int nd = re > rs ? dr.y : 0;
+  const int nchunks = max(1, (nd + kChunk - 1) / kChunk);
   const int ly = tid >> 3, lx = (tid & 7) * 2;
   const int i = ty * kTile + ly, j0 = tx * kTile + lx;
   const bool in0 = i < A.H && j0 < A.W, in1 = i < A.H && j0 + 1 < A.W;
   const float py = (float)i + 0.5f;
   const float px0 = (float)j0 + 0.5f, px1 = (float)(j0 + 1) + 0.5f;
-  float T0 = 1.0f, T1 = 1.0f;
-  float a00 = 0.f, a01 = 0.f, a02 = 0.f, a10 = 0.f, a11 = 0.f, a12 = 0.f;
-  int cur0 = 0, cur1 = 0;
-  bool d0 = !in0, d1 = !in1;
-  FwdGeom g0{1e30f, 0, 0}, g1{1e30f, 0, 0};
-  if (tid == 0) {
-    sm.next_k = rs;
-    sm.next_e = 0;
+  FwdPix p0{1.0f, 0.f, 0.f, 0.f, 1e30f, 0, 0, 0, !in0};
+  FwdPix p1{1.0f, 0.f, 0.f, 0.f, 1e30f, 0, 0, 0, !in1};
+  if (tid == 0 && nd > 0) {
+    mbar_init(&bars[0]);
+    mbar_init(&bars[1]);
+    fence_barrier_init();
+    bulk_load(buf[0], A.dl + dr.x, (uint32_t)min(nd, kChunk) * sizeof(DEntry), &bars[0]);
   }
-  __syncthreads();
-  while (true) {
-    if (__syncthreads_count(!(d0 && d1)) == 0) break;
-    zero_batch_smem<false>(sm, tid);
-    if (tid < 32) build_batch<STROKE, false, false>(sm, A, rs, re, lane);
-    __syncthreads();
-    const int np = sm.npieces;
-    if (np == 0) break;
-    stage_batch<STROKE, false>(sm, A, tx, ty, tid);
-    __syncthreads();
-    for (int pc = 0; pc < np; ++pc) {
-      const bool act = !(d0 && d1);
-      if (!__any_sync(0xffffffffu, act)) continue;
-      const Piece& P = sm.piece[pc];
-      const int flags = P.flags, ds = P.dstart, de = P.dstart + P.dcount;
-      if (flags & kFirst) {
-        g0 = FwdGeom{1e30f, 0, 0};
-        g1 = FwdGeom{1e30f, 0, 0};
+  __syncthreads();  // barriers initialised before anyone waits on them
+  int k = rs;          // next intersect of this warp
+  bool mid = false;    // k partially visited (split across chunks)
+  bool ok = true;
+  for (int c = 0; c < nchunks; ++c) {
+    const int c0 = c * kChunk, c1 = min(nd, c0 + kChunk);
+    if (nd > 0) {
+      if (tid == 0 && c + 1 < nchunks) {
+        fence_proxy_async();
+        const int n1 = min(nd - c1, kChunk);
+        bulk_load(buf[(c + 1) & 1], A.dl + dr.x + c1, (uint32_t)n1 * sizeof(DEntry),
+                  &bars[(c + 1) & 1]);
       }
-      for (int d = ds; d < de; ++d) {
-        const float4 EA = sm.dA[d];
-        const float4 EB = sm.dB[d];
-        const float wy = py - EA.y;
-        float pr, cx, cy;
-        g0.md = fminf(g0.md, seg_d2(px0, py, wy, EA, EB, pr, cx, cy));
-        g1.md = fminf(g1.md, seg_d2(px1, py, wy, EA, EB, pr, cx, cy));
-        if (!STROKE) {
-          if (((EA.y <= py) & (EB.y > py)) | ((EA.y > py) & (EB.y <= py))) {
-            const float lhs = EB.z + wy * EA.z;
-            const float rhs0 = px0 * EA.w, rhs1 = px1 * EA.w;
-            const bool pos = EA.w > 0.0f;
-            const int h0 = pos ? (lhs > rhs0) : (lhs < rhs0);
-            const int h1 = pos ? (lhs > rhs1) : (lhs < rhs1);
-            const int sg = pos ? 1 : -1;
-            g0.n += h0;
-            g1.n += h1;
-            g0.w += h0 * sg;
-            g1.w += h1 * sg;
-          }
-        }
+      if (!wait_chunk(&bars[c & 1], (uint32_t)((c >> 1) & 1), A.status)) {
+        ok = false;
+        break;
+      }
+    }
+    const DEntry* cb = buf[c & 1];  // record d of the tile is cb[d - c0]
+    while (k < re && __any_sync(0xffffffffu, !(p0.done && p1.done))) {
+      IMeta m;
+      load_meta(A.meta + k, m);
+      const int ds = m.dstart, de = m.dstart + m.dcount;
+      if (!mid) {
+        p0.md = p1.md = 1e30f;
+        p0.w = p0.n = p1.w = p1.n = 0;
+      }
+      fwd_entries<STROKE>(cb, c0, max(ds, c0), min(de, c1), px0, px1, py, p0, p1);
+      if (de > c1) {
+        mid = true;
+        break;
       }
       if (!STROKE) {
-        const int rw = sm.rowwind[pc][ly], rc = sm.rowcnt[pc][ly];
-        g0.w += rw;
-        g1.w += rw;
-        g0.n += rc;
-        g1.n += rc;
+        const int ro = __ldg(A.rowoff + (long long)k * 16 + ly);
+        const int rw = row_wind(ro), rc = row_cnt(ro);
+        p0.w += rw; p1.w += rw; p0.n += rc; p1.n += rc;
       }
-      if (flags & kLast) {
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          const bool dn = u ? d1 : d0;
-          if (dn) continue;
-          const FwdGeom& g = u ? g1 : g0;
-          float cov;
-          if (!STROKE) {
-            float sign, dist;
-            cov = fill_coverage(g.md, g.w, g.n, P.rule, P.a, sign, dist);
-          } else {
-            float dist, edge_d;
-            cov = stroke_coverage(g.md, P.b, P.a, dist, edge_d);
-          }
-          const float alpha = fminf(kAlphaCap, P.op * cov);
-          if (alpha < kAlphaMin) continue;
-          float& T = u ? T1 : T0;
-          const float nT = T * (1.0f - alpha);
-          const float vis = alpha * T;
-          if (u) {
-            a10 += P.c0 * vis; a11 += P.c1 * vis; a12 += P.c2 * vis;
-            cur1 = P.k;
-            if (nT <= kTransStop) d1 = true;
-          } else {
-            a00 += P.c0 * vis; a01 += P.c1 * vis; a02 += P.c2 * vis;
-            cur0 = P.k;
-            if (nT <= kTransStop) d0 = true;
-          }
-          T = nT;
-        }
-      }
+      fwd_composite<STROKE>(p0, m, k);
+      fwd_composite<STROKE>(p1, m, k);
+      mid = false;
+      ++k;
     }
+    __syncthreads();  // this chunk's buffer may be refilled
   }
+  if (!ok) return;
   const float bg0 = A.bg[0], bg1 = A.bg[1], bg2 = A.bg[2];
   const long long hw = (long long)A.H * A.W;
-  if (in0) {
-    const long long pix = (long long)i * A.W + j0;
-    const float o0 = a00 + T0 * bg0, o1 = a01 + T0 * bg1, o2 = a02 + T0 * bg2;
-    A.fts[pix] = T0;
-    A.fidx[pix] = cur0;
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const FwdPix& p = u ? p1 : p0;
+    if (!(u ? in1 : in0)) continue;
+    const long long pix = (long long)i * A.W + j0 + u;
+    const float o0 = p.a0 + p.T * bg0, o1 = p.a1 + p.T * bg1, o2 = p.a2 + p.T * bg2;
+    A.fts[pix] = p.T;
+    A.fidx[pix] = p.cur;
     A.out[pix * 3] = o0;
     A.out[pix * 3 + 1] = o1;
     A.out[pix * 3 + 2] = o2;
@@ -475,20 +319,7 @@ __global__ void __launch_bounds__(kRT) raster_forward_kernel(const RasterArgs A)
       A.out_chw[2 * hw + pix] = fminf(fmaxf(o2, 0.0f), 1.0f);
     }
   }
-  if (in1) {
-    const long long pix = (long long)i * A.W + j0 + 1;
-    const float o0 = a10 + T1 * bg0, o1 = a11 + T1 * bg1, o2 = a12 + T1 * bg2;
-    A.fts[pix] = T1;
-    A.fidx[pix] = cur1;
-    A.out[pix * 3] = o0;
-    A.out[pix * 3 + 1] = o1;
-    A.out[pix * 3 + 2] = o2;
-    if (A.out_chw) {
-      A.out_chw[pix] = fminf(fmaxf(o0, 0.0f), 1.0f);
-      A.out_chw[hw + pix] = fminf(fmaxf(o1, 0.0f), 1.0f);
-      A.out_chw[2 * hw + pix] = fminf(fmaxf(o2, 0.0f), 1.0f);
-    }
-  }
+  (void)lane;
 }
 
 // ---------------------------------------------------------------------------
@@ -498,25 +329,61 @@ struct BwdPix {
   float T, Tf, b0, b1, b2, v0, v1, v2, bgd;
   int fidx;
   bool in;
-  // geometry of the current intersect
   float md, bp, bcx, bcy;
-  int be, bl, w, n;
+  int be, bl, w, n;  // bl: staged record of the closest edge in the current chunk, or -1
 };
 
 template <bool STROKE>
-__device__ __forceinline__ void bwd_pixel(BwdPix& s, const Piece& P, float px, float py, bool valid,
-                                          float acc[kAcc], bool collect, float4& eg, int& eg_loc,
-                                          int& eg_eid, bool& contributed) {
-  eg_loc = -1;
-  eg_eid = -1;
+__device__ __forceinline__ void bwd_entries(const DEntry* __restrict__ buf, int c0, int lo, int hi,
+                                            const float px[2], float py, BwdPix s[2]) {
+  for (int d = lo; d < hi; ++d) {
+    const float4 EA = buf[d - c0].a;
+    const float4 EB = buf[d - c0].b;
+    const int eid = __float_as_int(EB.w);
+    const float wy = py - EA.y;
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      float pr, cx, cy;
+      const float d2 = seg_d2(px[u], py, wy, EA, EB, pr, cx, cy);
+      if (d2 < s[u].md || (d2 == s[u].md && eid < s[u].be)) {
+        s[u].md = d2;
+        s[u].be = eid;
+        s[u].bl = d;
+        s[u].bp = pr;
+        s[u].bcx = cx;
+        s[u].bcy = cy;
+      }
+    }
+    if (!STROKE) {
+      if (((EA.y <= py) & (EB.y > py)) | ((EA.y > py) & (EB.y <= py))) {
+        const float lhs = EB.z + wy * EA.z;
+        const bool pos = EA.w > 0.0f;
+        const int sg = pos ? 1 : -1;
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const float rhs = px[u] * EA.w;
+          const int h = pos ? (lhs > rhs) : (lhs < rhs);
+          s[u].n += h;
+          s[u].w += h * sg;
+        }
+      }
+    }
+  }
+}
+
+template <bool STROKE>
+__device__ __forceinline__ void bwd_pixel(BwdPix& s, const IMeta& m, float px, float py, bool valid,
+                                          float acc[kAcc], bool collect, float4& eg,
+                                          bool& has_eg, bool& contributed) {
+  has_eg = false;
   if (!valid) return;
   float cov, sign = 1.0f, dist, edge_d = 0.0f;
   if (!STROKE) {
-    cov = fill_coverage(s.md, s.w, s.n, P.rule, P.a, sign, dist);
+    cov = fill_coverage(s.md, s.w, s.n, m.rule, m.a, sign, dist);
   } else {
-    cov = stroke_coverage(s.md, P.b, P.a, dist, edge_d);
+    cov = stroke_coverage(s.md, m.b, m.a, dist, edge_d);
   }
-  const float op = P.op;
+  const float op = m.op;
   const float alpha = fminf(kAlphaCap, op * cov);
   if (!(alpha >= kAlphaMin)) return;
   contributed = true;
@@ -527,38 +394,36 @@ __device__ __forceinline__ void bwd_pixel(BwdPix& s, const Piece& P, float px, f
   acc[1] += fac * s.v1;
   acc[2] += fac * s.v2;
   if (collect) {
-    const float c0 = fac * P.c0, c1 = fac * P.c1, c2 = fac * P.c2;
+    const float c0 = fac * m.c0, c1 = fac * m.c1, c2 = fac * m.c2;
     acc[6] += c0;
     acc[7] += c1;
     acc[8] += c2;
     acc[9] += c0 + c1 + c2;
   }
   float v_alpha = 0.0f;
-  v_alpha = v_alpha + (P.c0 * s.T - s.b0 * ra) * s.v0;
-  v_alpha = v_alpha + (P.c1 * s.T - s.b1 * ra) * s.v1;
-  v_alpha = v_alpha + (P.c2 * s.T - s.b2 * ra) * s.v2;
+  v_alpha = v_alpha + (m.c0 * s.T - s.b0 * ra) * s.v0;
+  v_alpha = v_alpha + (m.c1 * s.T - s.b1 * ra) * s.v1;
+  v_alpha = v_alpha + (m.c2 * s.T - s.b2 * ra) * s.v2;
   v_alpha = v_alpha + s.Tf * ra * (0.0f - s.bgd);
-  s.b0 = s.b0 + P.c0 * fac;
-  s.b1 = s.b1 + P.c1 * fac;
-  s.b2 = s.b2 + P.c2 * fac;
+  s.b0 = s.b0 + m.c0 * fac;
+  s.b1 = s.b1 + m.c1 * fac;
+  s.b2 = s.b2 + m.c2 * fac;
   if (!(alpha < kAlphaCap)) return;
   acc[3] += cov * v_alpha;
-  float gscale;  // d loss / d dist along (closest - pixel) / dist
-  bool geom;
+  float gscale = 0.0f;
+  bool geom = false;
   if (!STROKE) {
     const float v_cov = op * v_alpha;
     const float v_logit = -v_cov * cov * (1.0f - cov);
     const float v_inv_sigma = v_logit * sign * dist * 2.0f;
-    acc[4] += v_inv_sigma * 0.5f / fmaxf(P.a, kEps);
-    gscale = v_logit * sign * P.a * 2.0f;
+    acc[4] += v_inv_sigma * 0.5f / fmaxf(m.a, kEps);
+    gscale = v_logit * sign * m.a * 2.0f;
     geom = (dist > kEps) & (s.be >= 0);
   } else {
     const float v_sigma = -op * cov * v_alpha;
     acc[4] += 0.5f * edge_d * edge_d * v_sigma;
-    geom = false;
-    gscale = 0.0f;
     if (edge_d > 0.0f) {
-      const float v_edge = v_sigma * edge_d * P.a;
+      const float v_edge = v_sigma * edge_d * m.a;
       acc[5] += -0.5f * v_edge;
       gscale = v_edge;
       geom = (dist > kEps) & (s.be >= 0);
@@ -568,19 +433,34 @@ __device__ __forceinline__ void bwd_pixel(BwdPix& s, const Piece& P, float px, f
     const float gx = gscale * (s.bcx - px) / dist;
     const float gy = gscale * (s.bcy - py) / dist;
     eg = make_float4((1.0f - s.bp) * gx, (1.0f - s.bp) * gy, s.bp * gx, s.bp * gy);
-    eg_loc = s.bl;
-    eg_eid = s.be;
+    has_eg = true;
   }
+}
+
+__device__ __forceinline__ void flush_acc(const RasterArgs& A, int pid, int k, int c, float v) {
+  if (v == 0.0f) return;
+  if (c < 3) atomicAdd(A.v_colors + pid * 3 + c, v);
+  else if (c == 3) atomicAdd(A.v_opac + pid, v);
+  else if (c == 4) atomicAdd(A.v_inv + pid, v);
+  else if (c == 5) atomicAdd(A.v_sw + pid, v);
+  else if (c < 9) { if (A.contrib) atomicAdd(A.contrib + pid * 3 + (c - 6), v); }
+  else if (A.icontrib) atomicAdd(A.icontrib + k, v);
 }
 
 template <bool STROKE>
 __global__ void __launch_bounds__(kRT) raster_backward_kernel(const RasterArgs A) {
-  __shared__ Smem<true> sm;
+  __shared__ __align__(128) DEntry buf[2][kChunk];
+  __shared__ __align__(16) float4 dgrad[kChunk];
+  __shared__ float pacc[kPaccCap][kAcc];
+  __shared__ __align__(8) uint64_t bars[2];
   const int tid = threadIdx.x, lane = tid & 31;
   const int tx = blockIdx.x, ty = A.r0 + blockIdx.y;
   const long long tile = (long long)ty * A.tbx + tx;
   const int rs = A.bins[2 * tile], re = A.bins[2 * tile + 1];
   if (re <= rs) return;
+  const int2 dr = A.dlr[tile];
+  const int nd = dr.y;
+  const int nchunks = max(1, (nd + kChunk - 1) / kChunk);
   const int ly = tid >> 3, lx = (tid & 7) * 2;
   const int i = ty * kTile + ly, j0 = tx * kTile + lx;
   const float py = (float)i + 0.5f;
@@ -629,35 +509,48 @@ __global__ void __launch_bounds__(kRT) raster_backward_kernel(const RasterArgs A
     }
     s[u].Tf = s[u].T;
   }
-  // highest intersect any pixel of the tile needs
-  kmax = warp_max_i(kmax);
-  if (lane == 0) sm.warp_tot[tid >> 5] = kmax;
-  __syncthreads();
-  if (tid == 0) {
-    int m = sm.warp_tot[0];
-    for (int w = 1; w < kRT / 32; ++w) m = max(m, sm.warp_tot[w]);
-    sm.next_k = min(m, re - 1);
-    sm.next_e = -1;
+  kmax = min(warp_max_i(kmax), re - 1);  // this warp's last needed intersect
+  for (int q = tid; q < kPaccCap * kAcc; q += kRT) (&pacc[0][0])[q] = 0.0f;
+  for (int q = tid; q < kChunk; q += kRT) dgrad[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+  const int last = nchunks - 1;
+  if (tid == 0 && nd > 0) {
+    mbar_init(&bars[0]);
+    mbar_init(&bars[1]);
+    fence_barrier_init();
+    const int c0 = last * kChunk;
+    bulk_load(buf[last & 1], A.dl + dr.x + c0, (uint32_t)(nd - c0) * sizeof(DEntry),
+              &bars[last & 1]);
   }
   __syncthreads();
-  if (sm.next_k < rs) return;
-  while (true) {
-    zero_batch_smem<true>(sm, tid);
-    if (tid < 32) build_batch<STROKE, true, true>(sm, A, rs, re, lane);
-    __syncthreads();
-    const int np = sm.npieces;
-    if (np == 0) break;
-    stage_batch<STROKE, true>(sm, A, tx, ty, tid);
-    __syncthreads();
-    s[0].bl = -1;  // near lists are rebuilt every batch
+  int k = kmax;       // next intersect of this warp (walking down)
+  bool mid = false;   // k partially visited
+  for (int c = last; c >= 0; --c) {
+    const int c0 = c * kChunk, c1 = min(nd, c0 + kChunk);
+    if (nd > 0) {
+      if (tid == 0 && c > 0) {
+        fence_proxy_async();
+        bulk_load(buf[(c - 1) & 1], A.dl + dr.x + (c - 1) * kChunk,
+                  (uint32_t)kChunk * sizeof(DEntry), &bars[(c - 1) & 1]);
+      }
+      // buffer b is used by chunks b, b+2, ...; walking down from `last`, this
+      // is use number (last - c) / 2 of buffer c & 1
+      if (!wait_chunk(&bars[c & 1], (uint32_t)(((last - c) >> 1) & 1), A.status)) return;
+    }
+    const DEntry* cb = buf[c & 1];  // record d of the tile is cb[d - c0]
+    s[0].bl = -1;  // records of other chunks are flushed / not resident
     s[1].bl = -1;
-    for (int pc = 0; pc < np; ++pc) {
-      const Piece& P = sm.piece[pc];
-      const bool v0 = s[0].in && P.k <= s[0].fidx;
-      const bool v1 = s[1].in && P.k <= s[1].fidx;
-      if (!__any_sync(0xffffffffu, v0 || v1)) continue;
-      const int flags = P.flags, ds = P.dstart, de = P.dstart + P.dcount;
-      if (flags & kLast) {
+    while (k >= rs) {
+      const bool v0 = s[0].in && k <= s[0].fidx;
+      const bool v1 = s[1].in && k <= s[1].fidx;
+      if (!__any_sync(0xffffffffu, v0 || v1)) {
+        --k;
+        mid = false;
+        continue;
+      }
+      IMeta m;
+      load_meta(A.meta + k, m);
+      const int ds = m.dstart, de = m.dstart + m.dcount;
+      if (!mid) {
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
           s[u].md = 1e30f;
@@ -667,66 +560,35 @@ __global__ void __launch_bounds__(kRT) raster_backward_kernel(const RasterArgs A
           s[u].w = s[u].n = 0;
         }
       }
-      for (int d = ds; d < de; ++d) {
-        const float4 EA = sm.dA[d];
-        const float4 EB = sm.dB[d];
-        const int eid = __float_as_int(EB.w);
-        const float wy = py - EA.y;
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          float pr, cx, cy;
-          const float d2 = seg_d2(px[u], py, wy, EA, EB, pr, cx, cy);
-          if (d2 < s[u].md || (d2 == s[u].md && eid < s[u].be)) {
-            s[u].md = d2;
-            s[u].be = eid;
-            s[u].bl = d;
-            s[u].bp = pr;
-            s[u].bcx = cx;
-            s[u].bcy = cy;
-          }
-        }
-        if (!STROKE) {
-          if (((EA.y <= py) & (EB.y > py)) | ((EA.y > py) & (EB.y <= py))) {
-            const float lhs = EB.z + wy * EA.z;
-            const bool pos = EA.w > 0.0f;
-            const int sg = pos ? 1 : -1;
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-              const float rhs = px[u] * EA.w;
-              const int h = pos ? (lhs > rhs) : (lhs < rhs);
-              s[u].n += h;
-              s[u].w += h * sg;
-            }
-          }
-        }
+      if (de > ds && de <= c0) break;  // its records lie in a lower chunk
+      bwd_entries<STROKE>(cb, c0, max(ds, c0), min(de, c1), px, py, s);
+      if (ds < c0) {
+        mid = true;
+        break;
       }
       if (!STROKE) {
-        const int rw = sm.rowwind[pc][ly], rc = sm.rowcnt[pc][ly];
-        s[0].w += rw;
-        s[1].w += rw;
-        s[0].n += rc;
-        s[1].n += rc;
+        const int ro = __ldg(A.rowoff + (long long)k * 16 + ly);
+        const int rw = row_wind(ro), rc = row_cnt(ro);
+        s[0].w += rw; s[1].w += rw; s[0].n += rc; s[1].n += rc;
       }
-      if (!(flags & kFirst)) continue;
       float acc[kAcc];
 #pragma unroll
-      for (int c = 0; c < kAcc; ++c) acc[c] = 0.0f;
+      for (int q = 0; q < kAcc; ++q) acc[q] = 0.0f;
       bool contributed = false;
 #pragma unroll
       for (int u = 0; u < 2; ++u) {
         float4 eg;
-        int eg_loc, eg_eid;
-        bwd_pixel<STROKE>(s[u], P, px[u], py, u ? v1 : v0, acc, collect, eg, eg_loc, eg_eid,
-                          contributed);
-        if (eg_eid >= 0) {
-          if (eg_loc >= 0) {
-            float4* g = &sm.dgrad[eg_loc];
+        bool has_eg;
+        bwd_pixel<STROKE>(s[u], m, px[u], py, u ? v1 : v0, acc, collect, eg, has_eg, contributed);
+        if (has_eg) {
+          if (s[u].bl >= 0) {
+            float4* g = &dgrad[s[u].bl - c0];
             atomicAdd(&g->x, eg.x);
             atomicAdd(&g->y, eg.y);
             atomicAdd(&g->z, eg.z);
             atomicAdd(&g->w, eg.w);
           } else {
-            float* g = A.v_edges + (long long)eg_eid * 4;
+            float* g = A.v_edges + (long long)s[u].be * 4;
             atomicAdd(g, eg.x);
             atomicAdd(g + 1, eg.y);
             atomicAdd(g + 2, eg.z);
@@ -734,45 +596,46 @@ __global__ void __launch_bounds__(kRT) raster_backward_kernel(const RasterArgs A
           }
         }
       }
-      if (!__any_sync(0xffffffffu, contributed)) continue;
+      if (__any_sync(0xffffffffu, contributed)) {
+        const int kl = k - rs;
 #pragma unroll
-      for (int c = 0; c < kAcc; ++c) {
-        if (c == 5 && !STROKE) continue;
-        if (c >= 6 && !collect) continue;
-        const float v = warp_sum(acc[c]);
-        if (lane == 0 && v != 0.0f) atomicAdd(&sm.pacc[pc][c], v);
+        for (int q = 0; q < kAcc; ++q) {
+          if (q == 5 && !STROKE) continue;
+          if (q >= 6 && !collect) continue;
+          const float v = warp_sum(acc[q]);
+          if (lane == 0 && v != 0.0f) {
+            if (kl < kPaccCap) atomicAdd(&pacc[kl][q], v);
+            else flush_acc(A, m.pid, k, q, v);
+          }
+        }
       }
+      mid = false;
+      --k;
     }
     __syncthreads();
-    // flush per-piece and per-edge accumulators
-    for (int idx = tid; idx < np * kAcc; idx += kRT) {
-      const int pc = idx / kAcc, c = idx - pc * kAcc;
-      const float v = sm.pacc[pc][c];
-      if (v == 0.0f) continue;
-      const int pid = sm.piece[pc].pid;
-      if (c < 3) atomicAdd(A.v_colors + pid * 3 + c, v);
-      else if (c == 3) atomicAdd(A.v_opac + pid, v);
-      else if (c == 4) atomicAdd(A.v_inv + pid, v);
-      else if (c == 5) atomicAdd(A.v_sw + pid, v);
-      else if (c < 9) { if (A.contrib) atomicAdd(A.contrib + pid * 3 + (c - 6), v); }
-      else if (A.icontrib) atomicAdd(A.icontrib + sm.piece[pc].k, v);
-    }
-    const int ndl = sm.ndl;
-    for (int d = tid; d < ndl; d += kRT) {
-      const float4 g = sm.dgrad[d];
+    // flush this chunk's edge gradients while its records are still resident
+    for (int d = c0 + tid; d < c1; d += kRT) {
+      const float4 g = dgrad[d - c0];
       if (g.x == 0.0f && g.y == 0.0f && g.z == 0.0f && g.w == 0.0f) continue;
-      float* dst = A.v_edges + (long long)__float_as_int(sm.dB[d].w) * 4;
+      float* dst = A.v_edges + (long long)__float_as_int(cb[d - c0].b.w) * 4;
       atomicAdd(dst, g.x);
       atomicAdd(dst + 1, g.y);
       atomicAdd(dst + 2, g.z);
       atomicAdd(dst + 3, g.w);
+      dgrad[d - c0] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
     __syncthreads();
+  }
+  const int np = min(re - rs, kPaccCap);
+  for (int q = tid; q < np * kAcc; q += kRT) {
+    const int kl = q / kAcc, c = q - kl * kAcc;
+    const float v = pacc[kl][c];
+    if (v != 0.0f) flush_acc(A, A.pids[rs + kl], rs + kl, c, v);
   }
 }
 
 // ---------------------------------------------------------------------------
-// host launch helpers
+// host launch helper
 
 inline int launch_raster(bool stroke, bool bwd, const RasterArgs& a, int H, int W, int r_begin,
                          int r_end, cudaStream_t st) {
@@ -792,138 +655,83 @@ inline int launch_raster(bool stroke, bool bwd, const RasterArgs& a, int H, int 
   return launch_status();
 }
 
+inline void stage_args(RasterArgs& a, const int32_t* prim_ids_sorted, const int32_t* tile_bins,
+                       const int32_t* tile_dlist, const void* imeta, const int32_t* rowoff,
+                       const void* dlist, const float* background, int32_t* status) {
+  a.pids = prim_ids_sorted;
+  a.bins = tile_bins;
+  a.dlr = reinterpret_cast<const int2*>(tile_dlist);
+  a.meta = reinterpret_cast<const IMeta*>(imeta);
+  a.rowoff = rowoff;
+  a.dl = reinterpret_cast<const DEntry*>(dlist);
+  a.bg = background;
+  a.status = status;
+}
+
 }  // namespace cs
 
 using namespace cs;
 
 extern "C" {
 
-int cs_fill_forward(const int32_t* prim_ids_sorted, const int32_t* tile_bins,
-                    const float* edges_px, const int32_t* isect_edge_ranges,
-                    const int32_t* prim_edge_offsets, const float* colors,
-                    const float* opacities, const float* inv_sigma2s, const int32_t* fill_rules,
-                    const float* background, float* out_img, float* final_Ts, int32_t* final_idx,
-                    float* out_chw_clamped, int32_t img_height, int32_t img_width,
-                    int32_t tile_row_begin, int32_t tile_row_end, void* stream) {
-  if (img_height <= 0 || img_width <= 0 || !tile_bins || !out_img || !final_Ts || !final_idx ||
-      (!isect_edge_ranges && !prim_edge_offsets))
+static int raster_forward(bool stroke, const int32_t* prim_ids_sorted, const int32_t* tile_bins,
+                          const int32_t* tile_dlist, const void* imeta, const int32_t* rowoff,
+                          const void* dlist, const float* background, float* out_img,
+                          float* final_Ts, int32_t* final_idx, float* out_chw_clamped,
+                          int32_t* status, int32_t img_height, int32_t img_width,
+                          int32_t tile_row_begin, int32_t tile_row_end, void* stream) {
+  if (img_height <= 0 || img_width <= 0 || !tile_bins || !tile_dlist || !imeta || !dlist ||
+      !background || !out_img || !final_Ts || !final_idx || (!stroke && !rowoff))
     return CS_ERR_ARG;
   RasterArgs a{};
-  a.pids = prim_ids_sorted;
-  a.bins = tile_bins;
-  a.edges = reinterpret_cast<const float4*>(edges_px);
-  a.ranges = reinterpret_cast<const int2*>(isect_edge_ranges);
-  a.eoffs = prim_edge_offsets;
-  a.colors = colors;
-  a.opac = opacities;
-  a.inv_s2 = inv_sigma2s;
-  a.rules = fill_rules;
-  a.bg = background;
+  stage_args(a, prim_ids_sorted, tile_bins, tile_dlist, imeta, rowoff, dlist, background, status);
   a.out = out_img;
   a.fts = final_Ts;
   a.fidx = final_idx;
   a.out_chw = out_chw_clamped;
-  return launch_raster(false, false, a, img_height, img_width, tile_row_begin, tile_row_end,
+  return launch_raster(stroke, false, a, img_height, img_width, tile_row_begin, tile_row_end,
                        (cudaStream_t)stream);
 }
 
-int cs_fill_backward(const int32_t* prim_ids_sorted, const int32_t* tile_bins,
-                     const float* edges_px, const int32_t* isect_edge_ranges,
-                     const int32_t* prim_edge_offsets, const float* colors,
-                     const float* opacities, const float* inv_sigma2s, const int32_t* fill_rules,
-                     const float* background, const float* final_Ts, const int32_t* final_idx,
-                     const float* v_output, const float* out_img, const float* target_chw,
-                     const float* mse_scale, float* v_edges, float* v_colors, float* v_opacities,
-                     float* v_inv_sigma2s, float* curve_contrib_rgb, float* curve_isect_contrib,
-                     int32_t img_height, int32_t img_width, int32_t tile_row_begin,
-                     int32_t tile_row_end, void* stream) {
-  if (img_height <= 0 || img_width <= 0 || !tile_bins ||
-      (!isect_edge_ranges && !prim_edge_offsets))
-    return CS_ERR_ARG;
-  if (!v_output && (!out_img || !target_chw || !mse_scale)) return CS_ERR_ARG;
-  RasterArgs a{};
-  a.pids = prim_ids_sorted;
-  a.bins = tile_bins;
-  a.edges = reinterpret_cast<const float4*>(edges_px);
-  a.ranges = reinterpret_cast<const int2*>(isect_edge_ranges);
-  a.eoffs = prim_edge_offsets;
-  a.colors = colors;
-  a.opac = opacities;
-  a.inv_s2 = inv_sigma2s;
-  a.rules = fill_rules;
-  a.bg = background;
-  a.fts_in = final_Ts;
-  a.fidx_in = final_idx;
-  a.v_out = v_output;
-  a.out_img = out_img;
-  a.tgt = target_chw;
-  a.mse_scale = mse_scale;
-  a.v_edges = v_edges;
-  a.v_colors = v_colors;
-  a.v_opac = v_opacities;
-  a.v_inv = v_inv_sigma2s;
-  a.contrib = curve_contrib_rgb;
-  a.icontrib = curve_isect_contrib;
-  return launch_raster(false, true, a, img_height, img_width, tile_row_begin, tile_row_end,
-                       (cudaStream_t)stream);
+int cs_fill_forward(const int32_t* prim_ids_sorted, const int32_t* tile_bins,
+                    const int32_t* tile_dlist, const void* imeta, const int32_t* rowoff,
+                    const void* dlist, const float* background, float* out_img, float* final_Ts,
+                    int32_t* final_idx, float* out_chw_clamped, int32_t* status,
+                    int32_t img_height, int32_t img_width, int32_t tile_row_begin,
+                    int32_t tile_row_end, void* stream) {
+  return raster_forward(false, prim_ids_sorted, tile_bins, tile_dlist, imeta, rowoff, dlist,
+                        background, out_img, final_Ts, final_idx, out_chw_clamped, status,
+                        img_height, img_width, tile_row_begin, tile_row_end, stream);
 }
 
 int cs_stroke_forward(const int32_t* prim_ids_sorted, const int32_t* tile_bins,
-                      const float* edges_px, const int32_t* isect_edge_ranges,
-                      const int32_t* prim_edge_offsets, const float* colors,
-                      const float* opacities, const float* stroke_widths,
-                      const float* inv_sigma2s, const float* background, float* out_img,
-                      float* final_Ts, int32_t* final_idx, float* out_chw_clamped,
+                      const int32_t* tile_dlist, const void* imeta, const void* dlist,
+                      const float* background, float* out_img, float* final_Ts,
+                      int32_t* final_idx, float* out_chw_clamped, int32_t* status,
                       int32_t img_height, int32_t img_width, int32_t tile_row_begin,
                       int32_t tile_row_end, void* stream) {
-  if (img_height <= 0 || img_width <= 0 || !tile_bins || !out_img || !final_Ts || !final_idx ||
-      (!isect_edge_ranges && !prim_edge_offsets))
-    return CS_ERR_ARG;
-  RasterArgs a{};
-  a.pids = prim_ids_sorted;
-  a.bins = tile_bins;
-  a.edges = reinterpret_cast<const float4*>(edges_px);
-  a.ranges = reinterpret_cast<const int2*>(isect_edge_ranges);
-  a.eoffs = prim_edge_offsets;
-  a.colors = colors;
-  a.opac = opacities;
-  a.inv_s2 = inv_sigma2s;
-  a.sw = stroke_widths;
-  a.bg = background;
-  a.out = out_img;
-  a.fts = final_Ts;
-  a.fidx = final_idx;
-  a.out_chw = out_chw_clamped;
-  return launch_raster(true, false, a, img_height, img_width, tile_row_begin, tile_row_end,
-                       (cudaStream_t)stream);
+  return raster_forward(true, prim_ids_sorted, tile_bins, tile_dlist, imeta, nullptr, dlist,
+                        background, out_img, final_Ts, final_idx, out_chw_clamped, status,
+                        img_height, img_width, tile_row_begin, tile_row_end, stream);
 }
 
-int cs_stroke_backward(const int32_t* prim_ids_sorted, const int32_t* tile_bins,
-                       const float* edges_px, const int32_t* isect_edge_ranges,
-                       const int32_t* prim_edge_offsets, const float* colors,
-                       const float* opacities, const float* stroke_widths,
-                       const float* inv_sigma2s, const float* background, const float* final_Ts,
-                       const int32_t* final_idx, const float* v_output, const float* out_img,
-                       const float* target_chw, const float* mse_scale, float* v_edges,
-                       float* v_colors, float* v_opacities, float* v_stroke_widths,
-                       float* v_inv_sigma2s, float* curve_contrib_rgb,
-                       float* curve_isect_contrib, int32_t img_height, int32_t img_width,
-                       int32_t tile_row_begin, int32_t tile_row_end, void* stream) {
-  if (img_height <= 0 || img_width <= 0 || !tile_bins ||
-      (!isect_edge_ranges && !prim_edge_offsets))
+static int raster_backward(bool stroke, const int32_t* prim_ids_sorted, const int32_t* tile_bins,
+                           const int32_t* tile_dlist, const void* imeta, const int32_t* rowoff,
+                           const void* dlist, const float* background, const float* final_Ts,
+                           const int32_t* final_idx, const float* v_output, const float* out_img,
+                           const float* target_chw, const float* mse_scale, float* v_edges,
+                           float* v_colors, float* v_opacities, float* v_stroke_widths,
+                           float* v_inv_sigma2s, float* curve_contrib_rgb,
+                           float* curve_isect_contrib, int32_t* status, int32_t img_height,
+                           int32_t img_width, int32_t tile_row_begin, int32_t tile_row_end,
+                           void* stream) {
+  if (img_height <= 0 || img_width <= 0 || !prim_ids_sorted || !tile_bins || !tile_dlist ||
+      !imeta || !dlist || !background || !final_Ts || !final_idx || !v_edges || !v_colors ||
+      !v_opacities || !v_inv_sigma2s || (!stroke && !rowoff) || (stroke && !v_stroke_widths))
     return CS_ERR_ARG;
   if (!v_output && (!out_img || !target_chw || !mse_scale)) return CS_ERR_ARG;
   RasterArgs a{};
-  a.pids = prim_ids_sorted;
-  a.bins = tile_bins;
-  a.edges = reinterpret_cast<const float4*>(edges_px);
-  a.ranges = reinterpret_cast<const int2*>(isect_edge_ranges);
-  a.eoffs = prim_edge_offsets;
-  a.colors = colors;
-  a.opac = opacities;
-  a.inv_s2 = inv_sigma2s;
-  a.sw = stroke_widths;
-  a.bg = background;
+  stage_args(a, prim_ids_sorted, tile_bins, tile_dlist, imeta, rowoff, dlist, background, status);
   a.fts_in = final_Ts;
   a.fidx_in = final_idx;
   a.v_out = v_output;
@@ -937,8 +745,40 @@ int cs_stroke_backward(const int32_t* prim_ids_sorted, const int32_t* tile_bins,
   a.v_inv = v_inv_sigma2s;
   a.contrib = curve_contrib_rgb;
   a.icontrib = curve_isect_contrib;
-  return launch_raster(true, true, a, img_height, img_width, tile_row_begin, tile_row_end,
+  return launch_raster(stroke, true, a, img_height, img_width, tile_row_begin, tile_row_end,
                        (cudaStream_t)stream);
+}
+
+int cs_fill_backward(const int32_t* prim_ids_sorted, const int32_t* tile_bins,
+                     const int32_t* tile_dlist, const void* imeta, const int32_t* rowoff,
+                     const void* dlist, const float* background, const float* final_Ts,
+                     const int32_t* final_idx, const float* v_output, const float* out_img,
+                     const float* target_chw, const float* mse_scale, float* v_edges,
+                     float* v_colors, float* v_opacities, float* v_inv_sigma2s,
+                     float* curve_contrib_rgb, float* curve_isect_contrib, int32_t* status,
+                     int32_t img_height, int32_t img_width, int32_t tile_row_begin,
+                     int32_t tile_row_end, void* stream) {
+  return raster_backward(false, prim_ids_sorted, tile_bins, tile_dlist, imeta, rowoff, dlist,
+                         background, final_Ts, final_idx, v_output, out_img, target_chw,
+                         mse_scale, v_edges, v_colors, v_opacities, nullptr, v_inv_sigma2s,
+                         curve_contrib_rgb, curve_isect_contrib, status, img_height, img_width,
+                         tile_row_begin, tile_row_end, stream);
+}
+
+int cs_stroke_backward(const int32_t* prim_ids_sorted, const int32_t* tile_bins,
+                       const int32_t* tile_dlist, const void* imeta, const void* dlist,
+                       const float* background, const float* final_Ts, const int32_t* final_idx,
+                       const float* v_output, const float* out_img, const float* target_chw,
+                       const float* mse_scale, float* v_edges, float* v_colors,
+                       float* v_opacities, float* v_stroke_widths, float* v_inv_sigma2s,
+                       float* curve_contrib_rgb, float* curve_isect_contrib, int32_t* status,
+                       int32_t img_height, int32_t img_width, int32_t tile_row_begin,
+                       int32_t tile_row_end, void* stream) {
+  return raster_backward(true, prim_ids_sorted, tile_bins, tile_dlist, imeta, nullptr, dlist,
+                         background, final_Ts, final_idx, v_output, out_img, target_chw,
+                         mse_scale, v_edges, v_colors, v_opacities, v_stroke_widths,
+                         v_inv_sigma2s, curve_contrib_rgb, curve_isect_contrib, status,
+                         img_height, img_width, tile_row_begin, tile_row_end, stream);
 }
 
 }  // extern "C"

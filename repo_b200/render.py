@@ -105,6 +105,8 @@ def _check_block(block_x: int, block_y: int) -> None:
 
 @dataclass
 class Binning:
+    """Binned and staged frame: reference-format intersect list plus the per-tile
+    raster input (near-edge records, per-intersect records, row offsets)."""
     cubics_px: torch.Tensor
     edges_px: torch.Tensor
     prim_edge_offsets: torch.Tensor
@@ -117,17 +119,35 @@ class Binning:
     tile_bounds: tuple
     samples: int
     tile_rows: tuple
+    tile_dlist: torch.Tensor
+    imeta: torch.Tensor
+    rowoff: Optional[torch.Tensor]
+    dlist: torch.Tensor
+    counters: torch.Tensor
+    stroke: bool
+
+
+def _offsets_error(offs: torch.Tensor, num_segments: int) -> ValueError:
+    o = offs.detach().to("cpu")
+    return ValueError(
+        "primitive_seg_offsets must start at 0 and end at num_segments "
+        f"(got start={int(o[0])}, end={int(o[-1])}, num_segments={num_segments})")
 
 
 def bin_primitives(cubics_norm: torch.Tensor, offs: torch.Tensor, depths: torch.Tensor,
                    aa_widths: torch.Tensor, img_h: int, img_w: int, samples: int, *,
-                   stroke_widths: Optional[torch.Tensor] = None, aabb_pad: float = DEFAULT_AABB_PAD,
-                   aniso: bool = False, tile_rows: Optional[tuple] = None) -> Binning:
-    """Project, bound, flatten and bin all primitives (fused B200 pipeline).
+                   colors: torch.Tensor, opacities: torch.Tensor, inv_sigma2s: torch.Tensor,
+                   fill_rules: Optional[torch.Tensor] = None,
+                   stroke_widths: Optional[torch.Tensor] = None,
+                   aabb_pad: float = DEFAULT_AABB_PAD, aniso: bool = False,
+                   tile_rows: Optional[tuple] = None) -> Binning:
+    """Project, bound, flatten, bin, sort and stage all primitives (fused B200
+    pipeline, one host synchronisation to size the intersect list).
 
-    Output semantics equal the reference's K3 + flatten + K4 + cumsum + K5 +
+    The intersect list equals the reference's K3 + flatten + K4 + cumsum + K5 +
     sort + K6 (cubic_splatting.py:2815-2908): tile_bins [T, 2] of [start, end)
-    ranges into prim_ids_sorted / isect_ids_sorted, front (small depth) first.
+    into prim_ids_sorted / isect_ids_sorted, front (small depth) first.
+    stroke_widths selects stroke mode.
     """
     dev = cubics_norm.device
     s = max(2, int(samples))
@@ -136,12 +156,14 @@ def bin_primitives(cubics_norm: torch.Tensor, offs: torch.Tensor, depths: torch.
     tbx, tby, _ = tile_bounds_for(img_h, img_w)
     nt = tbx * tby
     r0, r1 = (0, tby) if tile_rows is None else (int(tile_rows[0]), int(tile_rows[1]))
+    stroke = stroke_widths is not None
     cubics_px = torch.empty((g, 4, 2), dtype=torch.float32, device=dev)
     edges = torch.empty((g * (s - 1), 2, 2), dtype=torch.float32, device=dev)
     prim_ranges = torch.empty((p, 4), dtype=torch.int32, device=dev)
     num_hit = torch.empty((p,), dtype=torch.int32, device=dev)
     tile_bins = torch.empty((nt, 2), dtype=torch.int32, device=dev)
-    counters = torch.zeros((2,), dtype=torch.int32, device=dev)  # [num_intersects, status]
+    tile_dlist = torch.empty((nt, 2), dtype=torch.int32, device=dev)
+    counters = torch.zeros((4,), dtype=torch.int32, device=dev)
     ws = torch.empty((int(nat.call("cs_bin_workspace_size", nt)),), dtype=torch.uint8, device=dev)
     st = nat.stream(dev)
     cn = _f32(cubics_norm)
@@ -150,27 +172,67 @@ def bin_primitives(cubics_norm: torch.Tensor, offs: torch.Tensor, depths: torch.
     basis = bernstein_basis(s, dev)
     nat.check(nat.call("cs_bin_count", nat.ptr(cn), nat.ptr(offs), nat.ptr(aw), nat.ptr(sw),
                        nat.ptr(basis), nat.ptr(cubics_px), nat.ptr(edges), nat.ptr(prim_ranges),
-                       nat.ptr(num_hit), nat.ptr(tile_bins), counters.data_ptr(),
-                       counters.data_ptr() + 4, ws.data_ptr(), p, g, INT64_MAX, s, int(img_h),
-                       int(img_w), r0, r1, float(aabb_pad), int(bool(aniso)), st), "cs_bin_count")
-    # the one host synchronisation of the forward: intersect count + status
-    n_isect, status = (int(v) for v in counters.tolist())
+                       nat.ptr(num_hit), nat.ptr(tile_bins), nat.ptr(tile_dlist),
+                       nat.ptr(counters), ws.data_ptr(), p, g, INT64_MAX, INT64_MAX, s,
+                       int(img_h), int(img_w), r0, r1, float(aabb_pad), int(bool(aniso)), st),
+              "cs_bin_count")
+    # the one host synchronisation of the forward: sizes + status
+    n_isect, status, n_dbound, _ = (int(v) for v in counters.tolist())
     if status == nat.CS_ERR_ARG:
-        o = offs.detach().to("cpu")
-        raise ValueError(
-            "primitive_seg_offsets must start at 0 and end at num_segments "
-            f"(got start={int(o[0])}, end={int(o[-1])}, num_segments={g}) and be non-decreasing")
+        raise _offsets_error(offs, g)
     nat.check(status, "cs_bin_count")
+    edge_offs = (offs.to(torch.int64) * (s - 1)).to(torch.int32)
     prim_sorted = torch.empty((n_isect,), dtype=torch.int32, device=dev)
     isect_sorted = torch.empty((n_isect,), dtype=torch.int64, device=dev)
+    imeta = torch.empty((max(n_isect, 1), 12), dtype=torch.int32, device=dev)
+    rowoff = None if stroke else torch.empty((max(n_isect, 1), 16), dtype=torch.int32, device=dev)
+    dlist = torch.empty((max(n_dbound, 1), 8), dtype=torch.float32, device=dev)
     if n_isect > 0:
         nat.check(nat.call("cs_bin_sort", nat.ptr(prim_ranges), nat.ptr(_f32(depths)),
-                           nat.ptr(tile_bins), counters.data_ptr(), nat.ptr(prim_sorted),
-                           nat.ptr(isect_sorted), counters.data_ptr() + 4, ws.data_ptr(), p,
-                           n_isect, int(img_h), int(img_w), r0, r1, st), "cs_bin_sort")
-    edge_offs = (offs.to(torch.int64) * (s - 1)).to(torch.int32)
+                           nat.ptr(tile_bins), nat.ptr(prim_sorted), nat.ptr(isect_sorted),
+                           nat.ptr(counters), ws.data_ptr(), p, n_isect, int(img_h), int(img_w),
+                           r0, r1, nat.ptr(edges), nat.ptr(edge_offs), nat.ptr(colors),
+                           nat.ptr(opacities), nat.ptr(inv_sigma2s), nat.ptr(fill_rules),
+                           nat.ptr(sw), nat.ptr(tile_dlist), nat.ptr(imeta), nat.ptr(rowoff),
+                           nat.ptr(dlist), max(n_dbound, 1), st), "cs_bin_sort")
     return Binning(cubics_px, edges, edge_offs, prim_ranges, num_hit, tile_bins, prim_sorted,
-                   isect_sorted, n_isect, (tbx, tby, 1), s, (r0, r1))
+                   isect_sorted, n_isect, (tbx, tby, 1), s, (r0, r1), tile_dlist, imeta, rowoff,
+                   dlist, counters, stroke)
+
+
+def stage_reference_lists(prim_ids_sorted, tile_bins, edges_px, isect_edge_ranges, colors,
+                          opacities, inv_sigma2s, fill_rules, stroke_widths, img_h, img_w,
+                          prim_edge_offsets=None) -> Binning:
+    """Stage a reference-format sorted intersect list for the raster kernels
+    (per-stage API).  Costs one host synchronisation to size the records."""
+    dev = edges_px.device
+    tbx, tby, _ = tile_bounds_for(img_h, img_w)
+    nt = tbx * tby
+    n = int(prim_ids_sorted.numel())
+    stroke = stroke_widths is not None
+    if isect_edge_ranges is not None:
+        bound = int((isect_edge_ranges[:, 1] - isect_edge_ranges[:, 0]).clamp_min(0).sum().item())
+    else:
+        eo = prim_edge_offsets.to(torch.int64)
+        pid = prim_ids_sorted.to(torch.int64)
+        bound = int((eo[pid + 1] - eo[pid]).clamp_min(0).sum().item())
+    tile_dlist = torch.empty((nt, 2), dtype=torch.int32, device=dev)
+    counters = torch.zeros((4,), dtype=torch.int32, device=dev)
+    imeta = torch.empty((max(n, 1), 12), dtype=torch.int32, device=dev)
+    rowoff = None if stroke else torch.empty((max(n, 1), 16), dtype=torch.int32, device=dev)
+    dlist = torch.empty((max(bound, 1), 8), dtype=torch.float32, device=dev)
+    ws = torch.empty((int(nat.call("cs_stage_workspace_size", nt)),), dtype=torch.uint8,
+                     device=dev)
+    nat.check(nat.call("cs_tile_stage", nat.ptr(prim_ids_sorted), nat.ptr(tile_bins),
+                       nat.ptr(edges_px), nat.ptr(isect_edge_ranges), nat.ptr(prim_edge_offsets),
+                       nat.ptr(colors), nat.ptr(opacities), nat.ptr(inv_sigma2s),
+                       nat.ptr(fill_rules), nat.ptr(stroke_widths), nat.ptr(tile_dlist),
+                       nat.ptr(imeta), nat.ptr(rowoff), nat.ptr(dlist), nat.ptr(counters),
+                       ws.data_ptr(), max(bound, 1), int(img_h), int(img_w), nat.stream(dev)),
+              "cs_tile_stage")
+    return Binning(None, edges_px, prim_edge_offsets, None, None, tile_bins, prim_ids_sorted,
+                   None, n, (tbx, tby, 1), 0, (0, tby), tile_dlist, imeta, rowoff, dlist, counters,
+                   stroke)
 
 
 def _inv_sigma2(widths: torch.Tensor) -> torch.Tensor:
@@ -188,59 +250,50 @@ def _zeros_views(dev, *shapes):
     return out
 
 
-def fill_forward_raster(b: Binning, colors, opacities, inv_sigma2s, fill_rules, background,
-                        img_h: int, img_w: int, out_chw=None):
-    dev = colors.device
-    out = torch.empty((img_h, img_w, 3), dtype=torch.float32, device=dev)
-    fts = torch.empty((img_h, img_w), dtype=torch.float32, device=dev)
-    fidx = torch.empty((img_h, img_w), dtype=torch.int32, device=dev)
+def forward_raster(b: Binning, background, img_h: int, img_w: int, out_chw=None, outputs=None):
+    """Forward rasteriser over staged tiles: image [H, W, 3], final_Ts, final_idx
+    (written into ``outputs`` when given)."""
+    dev = b.tile_bins.device
+    if outputs is None:
+        out = torch.empty((img_h, img_w, 3), dtype=torch.float32, device=dev)
+        fts = torch.empty((img_h, img_w), dtype=torch.float32, device=dev)
+        fidx = torch.empty((img_h, img_w), dtype=torch.int32, device=dev)
+    else:
+        out, fts, fidx = outputs
     if b.num_intersects <= 0:
         out.copy_(background.view(1, 1, 3).expand(img_h, img_w, 3))
         fts.fill_(1.0)
         fidx.fill_(0)
         return out, fts, fidx
-    nat.check(nat.call("cs_fill_forward", nat.ptr(b.prim_ids_sorted), nat.ptr(b.tile_bins),
-                       nat.ptr(b.edges_px), None, nat.ptr(b.prim_edge_offsets), nat.ptr(colors),
-                       nat.ptr(opacities), nat.ptr(inv_sigma2s), nat.ptr(fill_rules),
-                       nat.ptr(background), nat.ptr(out), nat.ptr(fts), nat.ptr(fidx),
-                       nat.ptr(out_chw), img_h, img_w, b.tile_rows[0], b.tile_rows[1],
-                       nat.stream(dev)), "cs_fill_forward")
+    st = nat.stream(dev)
+    status = b.counters[1:2]
+    if not b.stroke:
+        nat.check(nat.call("cs_fill_forward", nat.ptr(b.prim_ids_sorted), nat.ptr(b.tile_bins),
+                           nat.ptr(b.tile_dlist), nat.ptr(b.imeta), nat.ptr(b.rowoff),
+                           nat.ptr(b.dlist), nat.ptr(background), nat.ptr(out), nat.ptr(fts),
+                           nat.ptr(fidx), nat.ptr(out_chw), nat.ptr(status), img_h, img_w,
+                           b.tile_rows[0], b.tile_rows[1], st), "cs_fill_forward")
+    else:
+        nat.check(nat.call("cs_stroke_forward", nat.ptr(b.prim_ids_sorted), nat.ptr(b.tile_bins),
+                           nat.ptr(b.tile_dlist), nat.ptr(b.imeta), nat.ptr(b.dlist),
+                           nat.ptr(background), nat.ptr(out), nat.ptr(fts), nat.ptr(fidx),
+                           nat.ptr(out_chw), nat.ptr(status), img_h, img_w, b.tile_rows[0],
+                           b.tile_rows[1], st), "cs_stroke_forward")
     return out, fts, fidx
 
 
-def stroke_forward_raster(b: Binning, colors, opacities, stroke_widths, inv_sigma2s, background,
-                          img_h: int, img_w: int):
-    dev = colors.device
-    out = torch.empty((img_h, img_w, 3), dtype=torch.float32, device=dev)
-    fts = torch.empty((img_h, img_w), dtype=torch.float32, device=dev)
-    fidx = torch.empty((img_h, img_w), dtype=torch.int32, device=dev)
-    if b.num_intersects <= 0:
-        out.copy_(background.view(1, 1, 3).expand(img_h, img_w, 3))
-        fts.fill_(1.0)
-        fidx.fill_(0)
-        return out, fts, fidx
-    nat.check(nat.call("cs_stroke_forward", nat.ptr(b.prim_ids_sorted), nat.ptr(b.tile_bins),
-                       nat.ptr(b.edges_px), None, nat.ptr(b.prim_edge_offsets), nat.ptr(colors),
-                       nat.ptr(opacities), nat.ptr(stroke_widths), nat.ptr(inv_sigma2s),
-                       nat.ptr(background), nat.ptr(out), nat.ptr(fts), nat.ptr(fidx), None,
-                       img_h, img_w, b.tile_rows[0], b.tile_rows[1], nat.stream(dev)),
-              "cs_stroke_forward")
-    return out, fts, fidx
-
-
-def raster_backward(b: Binning, colors, opacities, inv_sigma2s, fill_rules, stroke_widths,
-                    background, final_ts, final_idx, v_output, img_h, img_w, *,
-                    collect_contrib: bool = False, collect_isect_contrib: bool = False,
-                    out_img=None, target_chw=None, mse_scale=None):
+def raster_backward(b: Binning, num_primitives: int, background, final_ts, final_idx, v_output,
+                    img_h, img_w, *, collect_contrib: bool = False,
+                    collect_isect_contrib: bool = False, out_img=None, target_chw=None,
+                    mse_scale=None):
     """Backward rasteriser.  Returns v_edges, v_colors, v_opacities, v_inv_sigma2s,
     v_stroke_widths (stroke only), curve_contrib_rgb, curve_isect_contrib."""
-    dev = colors.device
-    p = int(colors.shape[0])
+    dev = b.tile_bins.device
+    p = int(num_primitives)
     ne = int(b.edges_px.shape[0])
     ni = int(b.num_intersects)
-    stroke = stroke_widths is not None
     shapes = [(ne, 2, 2), (p, 3), (p,), (p,)]
-    if stroke:
+    if b.stroke:
         shapes.append((p,))
     if collect_contrib:
         shapes.append((p, 3))
@@ -250,7 +303,7 @@ def raster_backward(b: Binning, colors, opacities, inv_sigma2s, fill_rules, stro
     v_edges, v_colors, v_opac, v_inv = views[:4]
     i = 4
     v_sw = None
-    if stroke:
+    if b.stroke:
         v_sw = views[i]
         i += 1
     contrib = None
@@ -261,27 +314,25 @@ def raster_backward(b: Binning, colors, opacities, inv_sigma2s, fill_rules, stro
     if ni > 0 and ne > 0:
         st = nat.stream(dev)
         vo = None if v_output is None else _f32(v_output)
-        if not stroke:
+        status = b.counters[1:2]
+        if not b.stroke:
             nat.check(nat.call("cs_fill_backward", nat.ptr(b.prim_ids_sorted), nat.ptr(b.tile_bins),
-                               nat.ptr(b.edges_px), None, nat.ptr(b.prim_edge_offsets),
-                               nat.ptr(colors), nat.ptr(opacities), nat.ptr(inv_sigma2s),
-                               nat.ptr(fill_rules), nat.ptr(background), nat.ptr(final_ts),
+                               nat.ptr(b.tile_dlist), nat.ptr(b.imeta), nat.ptr(b.rowoff),
+                               nat.ptr(b.dlist), nat.ptr(background), nat.ptr(final_ts),
                                nat.ptr(final_idx), nat.ptr(vo), nat.ptr(out_img),
                                nat.ptr(target_chw), nat.ptr(mse_scale), nat.ptr(v_edges),
                                nat.ptr(v_colors), nat.ptr(v_opac), nat.ptr(v_inv),
-                               nat.ptr(contrib), nat.ptr(icontrib), img_h, img_w,
+                               nat.ptr(contrib), nat.ptr(icontrib), nat.ptr(status), img_h, img_w,
                                b.tile_rows[0], b.tile_rows[1], st), "cs_fill_backward")
         else:
             nat.check(nat.call("cs_stroke_backward", nat.ptr(b.prim_ids_sorted),
-                               nat.ptr(b.tile_bins), nat.ptr(b.edges_px), None,
-                               nat.ptr(b.prim_edge_offsets), nat.ptr(colors), nat.ptr(opacities),
-                               nat.ptr(stroke_widths), nat.ptr(inv_sigma2s), nat.ptr(background),
-                               nat.ptr(final_ts), nat.ptr(final_idx), nat.ptr(vo),
-                               nat.ptr(out_img), nat.ptr(target_chw), nat.ptr(mse_scale),
-                               nat.ptr(v_edges), nat.ptr(v_colors), nat.ptr(v_opac),
-                               nat.ptr(v_sw), nat.ptr(v_inv), nat.ptr(contrib),
-                               nat.ptr(icontrib), img_h, img_w, b.tile_rows[0], b.tile_rows[1],
-                               st), "cs_stroke_backward")
+                               nat.ptr(b.tile_bins), nat.ptr(b.tile_dlist), nat.ptr(b.imeta),
+                               nat.ptr(b.dlist), nat.ptr(background), nat.ptr(final_ts),
+                               nat.ptr(final_idx), nat.ptr(vo), nat.ptr(out_img),
+                               nat.ptr(target_chw), nat.ptr(mse_scale), nat.ptr(v_edges),
+                               nat.ptr(v_colors), nat.ptr(v_opac), nat.ptr(v_sw), nat.ptr(v_inv),
+                               nat.ptr(contrib), nat.ptr(icontrib), nat.ptr(status), img_h,
+                               img_w, b.tile_rows[0], b.tile_rows[1], st), "cs_stroke_backward")
     return v_edges, v_colors, v_opac, v_inv, v_sw, contrib, icontrib
 
 
@@ -347,16 +398,17 @@ class CubicFillSplatFunction(torch.autograd.Function):
                 f"aa_widths size must match primitive count ({num_primitives}), got {int(widths.numel())}")
         widths = torch.clamp(_f32(widths), min=1e-4)
         inv_s2 = _inv_sigma2(widths)
+        col = _f32(colors)
+        op = _f32(opacities).view(-1)
+        rules = _i32(fill_rules).view(-1)
         b = bin_primitives(cubics_norm, offs, depths.reshape(-1), widths, int(img_h), int(img_w),
-                           int(distance_samples), aabb_pad=float(aabb_pad),
+                           int(distance_samples), colors=col, opacities=op, inv_sigma2s=inv_s2,
+                           fill_rules=rules, aabb_pad=float(aabb_pad),
                            aniso=bool(aniso_intersects), tile_rows=tile_rows)
         if b.num_intersects <= 0:
             ctx.empty = True
             return _empty_image(bg, img_h, img_w)
-        col = _f32(colors)
-        op = _f32(opacities).view(-1)
-        rules = _i32(fill_rules).view(-1)
-        out, fts, fidx = fill_forward_raster(b, col, op, inv_s2, rules, bg, int(img_h), int(img_w))
+        out, fts, fidx = forward_raster(b, bg, int(img_h), int(img_w))
         ctx.empty = False
         ctx.binning = b
         ctx.process_fn = process_fn
@@ -381,7 +433,7 @@ class CubicFillSplatFunction(torch.autograd.Function):
         cc = bool(pre.get("collect_curve_contrib_rgb", False))
         ci = bool(pre.get("collect_curve_isect_contrib", False))
         v_edges, v_colors, v_opac, v_inv, _, contrib, icontrib = raster_backward(
-            b, colors, opac, inv_s2, rules, None, bg, fts, fidx, grad_out, ctx.img_h, ctx.img_w,
+            b, int(colors.shape[0]), bg, fts, fidx, grad_out, ctx.img_h, ctx.img_w,
             collect_contrib=cc, collect_isect_contrib=ci)
         half_w, half_h = 0.5 * float(ctx.img_w), 0.5 * float(ctx.img_h)
         if process_fn is None:
@@ -445,15 +497,16 @@ class CubicPolylineSplatFunction(torch.autograd.Function):
         widths = torch.clamp(_f32(widths), min=1e-4)
         inv_s2 = _inv_sigma2(widths)
         sw = _f32(stroke_widths).view(-1)
+        col = _f32(colors)
+        op = _f32(opacities).view(-1)
         b = bin_primitives(cubics_norm, offs, depths.reshape(-1), widths, int(img_h), int(img_w),
-                           int(distance_samples), stroke_widths=sw, aabb_pad=float(aabb_pad),
+                           int(distance_samples), colors=col, opacities=op, inv_sigma2s=inv_s2,
+                           stroke_widths=sw, aabb_pad=float(aabb_pad),
                            aniso=bool(aniso_intersects), tile_rows=tile_rows)
         if b.num_intersects <= 0:
             ctx.empty = True
             return _empty_image(bg, img_h, img_w)
-        col = _f32(colors)
-        op = _f32(opacities).view(-1)
-        out, fts, fidx = stroke_forward_raster(b, col, op, sw, inv_s2, bg, int(img_h), int(img_w))
+        out, fts, fidx = forward_raster(b, bg, int(img_h), int(img_w))
         ctx.empty = False
         ctx.binning = b
         ctx.process_fn = process_fn
@@ -478,7 +531,7 @@ class CubicPolylineSplatFunction(torch.autograd.Function):
         cc = bool(pre.get("collect_curve_contrib_rgb", False))
         ci = bool(pre.get("collect_curve_isect_contrib", False))
         v_edges, v_colors, v_opac, v_inv, v_sw, contrib, icontrib = raster_backward(
-            b, colors, opac, inv_s2, None, sw, bg, fts, fidx, grad_out, ctx.img_h, ctx.img_w,
+            b, int(colors.shape[0]), bg, fts, fidx, grad_out, ctx.img_h, ctx.img_w,
             collect_contrib=cc, collect_isect_contrib=ci)
         half_w, half_h = 0.5 * float(ctx.img_w), 0.5 * float(ctx.img_h)
         if process_fn is None:

@@ -73,7 +73,9 @@ class FillTrainer:
         self.prim_ranges = torch.empty((p, 4), device=dev, dtype=i32)
         self.num_hit = torch.empty((p,), device=dev, dtype=i32)
         self.tile_bins = torch.empty((self.num_tiles, 2), device=dev, dtype=i32)
-        self.counters = torch.zeros((2,), device=dev, dtype=i32)    # intersects, status
+        self.tile_dlist = torch.empty((self.num_tiles, 2), device=dev, dtype=i32)
+        # intersects, status, staged-record bound, unused
+        self.counters = torch.zeros((4,), device=dev, dtype=i32)
         self.bin_ws = torch.empty((int(nat.call("cs_bin_workspace_size", self.num_tiles)),),
                                   device=dev, dtype=torch.uint8)
         self.out = torch.empty((self.h, self.w, 3), device=dev, dtype=f32)
@@ -113,9 +115,12 @@ class FillTrainer:
                                     fused=True, capturable=True)
         if capacity is None:
             capacity = self.probe_capacity()
-        self.capacity = int(capacity)
+        self.capacity, self.dcapacity = (int(c) for c in capacity)
         self.prim_sorted = torch.empty((self.capacity,), device=dev, dtype=i32)
         self.isect_sorted = torch.empty((self.capacity,), device=dev, dtype=torch.int64)
+        self.imeta = torch.empty((self.capacity, 12), device=dev, dtype=i32)
+        self.rowoff = torch.empty((self.capacity, 16), device=dev, dtype=i32)
+        self.dlist = torch.empty((self.dcapacity, 8), device=dev, dtype=f32)
         self.graph: Optional[torch.cuda.CUDAGraph] = None
         self.launches_per_step = 0
 
@@ -126,7 +131,7 @@ class FillTrainer:
             torch.div(self.cub.view(-1, 4, 2), self.half, out=self.cn)
             self.cn.sub_(1.0)
 
-    def _bin(self, capacity: int):
+    def _bin(self, capacity: int, dcapacity: int):
         st = nat.stream(self.device)
         r0, r1 = self.tile_rows
         self.counters.zero_()
@@ -134,48 +139,52 @@ class FillTrainer:
                            self.widths.data_ptr(), None, self.basis.data_ptr(),
                            self.cubics_px.data_ptr(), self.edges.data_ptr(),
                            self.prim_ranges.data_ptr(), self.num_hit.data_ptr(),
-                           self.tile_bins.data_ptr(), self.counters.data_ptr(),
-                           self.counters.data_ptr() + 4, self.bin_ws.data_ptr(), self.num_paths,
-                           self.num_segments, capacity, self.s, self.h, self.w, r0, r1,
+                           self.tile_bins.data_ptr(), self.tile_dlist.data_ptr(),
+                           self.counters.data_ptr(), self.bin_ws.data_ptr(), self.num_paths,
+                           self.num_segments, capacity, dcapacity, self.s, self.h, self.w, r0, r1,
                            float(_render.DEFAULT_AABB_PAD), 0, st), "cs_bin_count")
 
-    def probe_capacity(self, slack: float = 1.5, extra: int = 4096) -> int:
-        """Intersect capacity from one counting pass (one host sync, at set-up)."""
+    def probe_capacity(self, slack: float = 1.5, extra: int = 4096) -> tuple[int, int]:
+        """Intersect and staged-record capacities from one counting pass (one
+        host sync, at set-up), with slack for the parameters to move."""
         self._params_to_cubics()
-        self._bin(INT64_MAX)
-        n = int(self.counters[0].item())
-        return int(math.ceil(n * slack)) + extra
+        self._bin(INT64_MAX, INT64_MAX)
+        n, _, nd, _ = (int(v) for v in self.counters.tolist())
+        return int(math.ceil(n * slack)) + extra, int(math.ceil(nd * slack)) + 16 * extra
 
     def forward_backward(self):
         """Enqueue one forward + loss + backward; no host synchronisation."""
         st = nat.stream(self.device)
         r0, r1 = self.tile_rows
         self._params_to_cubics()
-        self._bin(self.capacity)
+        self._bin(self.capacity, self.dcapacity)
+        status = self.counters.data_ptr() + 4
         nat.check(nat.call("cs_bin_sort", self.prim_ranges.data_ptr(), self.depths.data_ptr(),
-                           self.tile_bins.data_ptr(), self.counters.data_ptr(),
-                           self.prim_sorted.data_ptr(), self.isect_sorted.data_ptr(),
-                           self.counters.data_ptr() + 4, self.bin_ws.data_ptr(), self.num_paths,
-                           self.capacity, self.h, self.w, r0, r1, st), "cs_bin_sort")
+                           self.tile_bins.data_ptr(), self.prim_sorted.data_ptr(),
+                           self.isect_sorted.data_ptr(), self.counters.data_ptr(),
+                           self.bin_ws.data_ptr(), self.num_paths, self.capacity, self.h, self.w,
+                           r0, r1, self.edges.data_ptr(), self.edge_offs.data_ptr(),
+                           self.colors.data_ptr(), self.opac.data_ptr(), self.inv_s2.data_ptr(),
+                           self.rules.data_ptr(), None, self.tile_dlist.data_ptr(),
+                           self.imeta.data_ptr(), self.rowoff.data_ptr(), self.dlist.data_ptr(),
+                           self.dcapacity, st), "cs_bin_sort")
         nat.check(nat.call("cs_fill_forward", self.prim_sorted.data_ptr(),
-                           self.tile_bins.data_ptr(), self.edges.data_ptr(), None,
-                           self.edge_offs.data_ptr(), self.colors.data_ptr(),
-                           self.opac.data_ptr(), self.inv_s2.data_ptr(), self.rules.data_ptr(),
+                           self.tile_bins.data_ptr(), self.tile_dlist.data_ptr(),
+                           self.imeta.data_ptr(), self.rowoff.data_ptr(), self.dlist.data_ptr(),
                            self.bg.data_ptr(), self.out.data_ptr(), self.fts.data_ptr(),
-                           self.fidx.data_ptr(), self.img_chw.data_ptr(), self.h, self.w, r0, r1,
-                           st), "cs_fill_forward")
+                           self.fidx.data_ptr(), self.img_chw.data_ptr(), status, self.h, self.w,
+                           r0, r1, st), "cs_fill_forward")
         self._loss(st)
         self.scratch.zero_()
         self.flat_grad.zero_()
         nat.check(nat.call("cs_fill_backward", self.prim_sorted.data_ptr(),
-                           self.tile_bins.data_ptr(), self.edges.data_ptr(), None,
-                           self.edge_offs.data_ptr(), self.colors.data_ptr(),
-                           self.opac.data_ptr(), self.inv_s2.data_ptr(), self.rules.data_ptr(),
+                           self.tile_bins.data_ptr(), self.tile_dlist.data_ptr(),
+                           self.imeta.data_ptr(), self.rowoff.data_ptr(), self.dlist.data_ptr(),
                            self.bg.data_ptr(), self.fts.data_ptr(), self.fidx.data_ptr(), None,
                            self.out.data_ptr(), self.target.data_ptr(),
                            self.mse_scale.data_ptr(), self.v_edges.data_ptr(),
                            self.colors.grad.data_ptr(), self.v_opac.data_ptr(),
-                           self.v_inv.data_ptr(), None, None, self.h, self.w, r0, r1, st),
+                           self.v_inv.data_ptr(), None, None, status, self.h, self.w, r0, r1, st),
                   "cs_fill_backward")
         nat.check(nat.call("cs_edge_grads_to_cubics", self.v_edges.data_ptr(),
                            self.v_cn.data_ptr(), self.num_segments, self.s - 1,
@@ -243,7 +252,7 @@ class FillTrainer:
     # ------------------------------------------------------------------
     def check_status(self) -> tuple[int, int]:
         """(intersect count of the last step, device status); syncs."""
-        n, status = (int(v) for v in self.counters.tolist())
+        n, status, _, _ = (int(v) for v in self.counters.tolist())
         return n, status
 
     def loss_value(self) -> float:

@@ -48,20 +48,19 @@ def assert_grad_close(got, want, name):
 
 def gpu_fill(cubics_norm, offs, colors, opac, depths, h, w, bg, rules, aa, s, tile_rows=None):
     widths = torch.clamp(_t(aa, torch.float32), min=1e-4)
-    b = render.bin_primitives(_t(cubics_norm, torch.float32), _t(offs, torch.int32),
-                              _t(depths, torch.float32), widths, h, w, s, tile_rows=tile_rows)
     inv = render._inv_sigma2(widths)
-    out, fts, fidx = render.fill_forward_raster(b, _t(colors, torch.float32),
-                                                _t(opac, torch.float32), inv,
-                                                _t(rules, torch.int32), _t(bg, torch.float32), h, w)
+    col, op, rl = _t(colors, torch.float32), _t(opac, torch.float32), _t(rules, torch.int32)
+    b = render.bin_primitives(_t(cubics_norm, torch.float32), _t(offs, torch.int32),
+                              _t(depths, torch.float32), widths, h, w, s, colors=col,
+                              opacities=op, inv_sigma2s=inv, fill_rules=rl, tile_rows=tile_rows)
+    out, fts, fidx = render.forward_raster(b, _t(bg, torch.float32), h, w)
     return b, inv, out, fts, fidx
 
 
 def gpu_fill_backward(b, colors, opac, inv, rules, bg, fts, fidx, v_out, h, w):
     v_edges, v_colors, v_opac, v_inv, _, contrib, icontrib = render.raster_backward(
-        b, _t(colors, torch.float32), _t(opac, torch.float32), inv, _t(rules, torch.int32), None,
-        _t(bg, torch.float32), fts, fidx, _t(v_out, torch.float32), h, w,
-        collect_contrib=True, collect_isect_contrib=True)
+        b, int(np.asarray(colors).shape[0]), _t(bg, torch.float32), fts, fidx,
+        _t(v_out, torch.float32), h, w, collect_contrib=True, collect_isect_contrib=True)
     v_cpx = render.edge_grads_to_cubics(v_edges, int(b.cubics_px.shape[0]), b.samples)
     return {"v_edges": _np(v_edges), "v_colors": _np(v_colors), "v_opacities": _np(v_opac),
             "v_inv_sigma2s": _np(v_inv), "v_cubics_px": _np(v_cpx),

@@ -134,7 +134,7 @@ def kernel_times(tr, reps, flush, stream):
     orig = nat.call
 
     def timed_call(name, *args):
-        if name in ("cs_fill_forward", "cs_fill_backward"):
+        if name in ("cs_fill_forward", "cs_fill_backward"):  # the two raster kernels
             s = torch.cuda.Event(enable_timing=True)
             e = torch.cuda.Event(enable_timing=True)
             s.record(stream)

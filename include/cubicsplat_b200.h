@@ -164,15 +164,23 @@ CS_API int cs_tile_stage(const int32_t *prim_ids_sorted, const int32_t *tile_bin
  * [3, H, W] (may be NULL) also receives clamp(out, 0, 1) channel-major, the
  * image the training loss sees (the reference does torch.clamp + permute,
  * manbo/gaussian_trace/render.py:1309-1310).  status (device int, may be NULL)
- * receives CS_ERR_TIMEOUT if a bounded wait gave up.  Tile rows outside
- * [tile_row_begin, tile_row_end) are not touched.
- * Replaces rasterize_cubic_fill_forward_kernel, cubic_splatting.py:918-1194. */
+ * receives CS_ERR_TIMEOUT if a bounded wait gave up.  When target_chw
+ * [3, H, W] is given the same launch also computes the MSE loss of the
+ * clamped image: loss_out[0] = sum of squared differences over the launched
+ * tiles, loss_out[1] = that / (3 H W), reduced in a fixed order by the last
+ * CTA (workspace loss_ws: cs_loss_workspace_size(num_tiles) bytes, zeroed
+ * once).  Tile rows outside [tile_row_begin, tile_row_end) are not touched.
+ * Replaces rasterize_cubic_fill_forward_kernel, cubic_splatting.py:918-1194,
+ * and (with target_chw) mse_partial_sum_kernel + reduce_sum_partial_kernel,
+ * manbo/ops/metric.py:18-163. */
+CS_API size_t cs_loss_workspace_size(int64_t num_tiles);
 CS_API int cs_fill_forward(const int32_t *prim_ids_sorted, const int32_t *tile_bins,
                     const int32_t *tile_dlist, const void *imeta, const int32_t *rowoff,
                     const void *dlist, const float *background, float *out_img,
                     float *final_Ts, int32_t *final_idx, float *out_chw_clamped,
-                    int32_t *status, int32_t img_height, int32_t img_width,
-                    int32_t tile_row_begin, int32_t tile_row_end, void *stream);
+                    const float *target_chw, float *loss_out, void *loss_ws, int32_t *status,
+                    int32_t img_height, int32_t img_width, int32_t tile_row_begin,
+                    int32_t tile_row_end, void *stream);
 
 /* Closed-fill backward: reverse compositing from final_idx, gradients of the
  * colours, opacities, 1/sigma^2 and edge endpoints (closest edge only).
@@ -181,7 +189,8 @@ CS_API int cs_fill_forward(const int32_t *prim_ids_sorted, const int32_t *tile_b
  * v_output [H, W, 3] is the upstream image gradient; when it is NULL the MSE
  * gradient is computed in the kernel instead: v = scale * (clamp(out) - target)
  * masked to 0 <= out <= 1, with out_img [H, W, 3], target_chw [3, H, W] and
- * *mse_scale (device scalar, e.g. 2/N * dLoss).
+ * *mse_scale (device scalar, e.g. 2/N * dLoss).  v_opacities and
+ * v_inv_sigma2s may be NULL (not accumulated).
  * Replaces rasterize_cubic_fill_backward_kernel, cubic_splatting.py:1197-1651. */
 CS_API int cs_fill_backward(const int32_t *prim_ids_sorted, const int32_t *tile_bins,
                      const int32_t *tile_dlist, const void *imeta, const int32_t *rowoff,
@@ -199,9 +208,10 @@ CS_API int cs_fill_backward(const int32_t *prim_ids_sorted, const int32_t *tile_
 CS_API int cs_stroke_forward(const int32_t *prim_ids_sorted, const int32_t *tile_bins,
                       const int32_t *tile_dlist, const void *imeta, const void *dlist,
                       const float *background, float *out_img, float *final_Ts,
-                      int32_t *final_idx, float *out_chw_clamped, int32_t *status,
-                      int32_t img_height, int32_t img_width, int32_t tile_row_begin,
-                      int32_t tile_row_end, void *stream);
+                      int32_t *final_idx, float *out_chw_clamped, const float *target_chw,
+                      float *loss_out, void *loss_ws, int32_t *status, int32_t img_height,
+                      int32_t img_width, int32_t tile_row_begin, int32_t tile_row_end,
+                      void *stream);
 
 /* Stroke backward (adds d/d stroke width).
  * Replaces rasterize_cubic_polyline_backward_kernel,
@@ -225,6 +235,32 @@ CS_API int cs_stroke_backward(const int32_t *prim_ids_sorted, const int32_t *til
 CS_API int cs_edge_grads_to_cubics(const float *v_edges, float *v_cubics, int64_t num_segments,
                             int32_t edges_per_segment, float scale_x, float scale_y,
                             void *stream);
+
+/* Ring parameterisation of closed paths (the B200 training step's
+ * parameters): ring [P, 3G, 2] pixel-space points; segment k of a path is
+ * (r[3k], r[3k+1], r[3k+2], r[3k+3 mod 3G]).  cubics_norm [P*G, 4, 2] =
+ * point / (W/2, H/2) - 1, the normalisation the reference's renderer inverts
+ * (cubic_splatting.py:588-595). */
+CS_API int cs_ring_to_cubics(const float *ring, float *cubics_norm, int64_t num_paths,
+                      int32_t segs_per_path, int32_t img_height, int32_t img_width, void *stream);
+
+/* Edge endpoint gradients [P*G*E, 2, 2] -> ring point gradients [P, 3G, 2]
+ * (written, not accumulated): the per-segment Bernstein accumulation of
+ * cs_edge_grads_to_cubics in normalised space, then the derivative of the
+ * normalisation, summed over the control points that share a ring point.
+ * clear_edges != 0 zeroes v_edges after reading it.  G <= 128. */
+CS_API int cs_edge_grads_to_ring(float *v_edges, float *v_ring, int64_t num_paths,
+                          int32_t segs_per_path, int32_t edges_per_segment, int32_t img_height,
+                          int32_t img_width, int32_t clear_edges, void *stream);
+
+/* Adam step over one flat fp32 parameter buffer, elements [0, n_first) with
+ * lr_first and the rest with lr_rest; step (device int32) holds the number of
+ * steps taken and is advanced on the device.  clear_grads != 0 zeroes the
+ * gradient after use.  Workspace: cs_adam_workspace_size() bytes, zeroed once. */
+CS_API size_t cs_adam_workspace_size(void);
+CS_API int cs_adam_step(float *params, float *grads, float *exp_avg, float *exp_avg_sq, int64_t n,
+                 int64_t n_first, float lr_first, float lr_rest, float beta1, float beta2,
+                 float eps, int32_t *step, void *workspace, int32_t clear_grads, void *stream);
 
 /* --------------------------------------------------------------------------
  * Closed control polygon -> ring of piecewise-Hermite cubics
@@ -266,8 +302,9 @@ CS_API int cs_mse_backward(const float *lhs, const float *rhs, const float *scal
 /* SSIM with a separable Gaussian window g [win] (win odd, win2d = outer(g, g)),
  * valid-window semantics, per plane (N*C planes of H x W).  Writes the mean
  * SSIM of every plane to plane_means [planes] and, when ssim_map is not NULL,
- * the map [planes, H-win+1, W-win+1].
- * Workspace: cs_ssim_workspace_size(planes, h, w, win).
+ * the map [planes, H-win+1, W-win+1].  One launch; per-block sums are
+ * reduced by the last block.  win <= 15.
+ * Workspace: cs_ssim_workspace_size(planes, h, w, win) bytes, zeroed once.
  * Replaces ssim_map_kernel + the mean of manbo/metric.py:215-273
  * (manbo/ops/metric.py:205-341). */
 CS_API size_t cs_ssim_workspace_size(int64_t planes, int32_t h, int32_t w, int32_t win);

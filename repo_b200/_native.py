@@ -47,11 +47,17 @@ SIGNATURES = {
                     + [_I64, _P]),
     "cs_stage_workspace_size": (_SZ, [_I64]),
     "cs_tile_stage": (ctypes.c_int, [_P] * 16 + [_I64, _I32, _I32, _P]),
-    "cs_fill_forward": (ctypes.c_int, [_P] * 12 + [_I32, _I32, _I32, _I32, _P]),
+    "cs_loss_workspace_size": (_SZ, [_I64]),
+    "cs_fill_forward": (ctypes.c_int, [_P] * 15 + [_I32, _I32, _I32, _I32, _P]),
     "cs_fill_backward": (ctypes.c_int, [_P] * 20 + [_I32, _I32, _I32, _I32, _P]),
-    "cs_stroke_forward": (ctypes.c_int, [_P] * 11 + [_I32, _I32, _I32, _I32, _P]),
+    "cs_stroke_forward": (ctypes.c_int, [_P] * 14 + [_I32, _I32, _I32, _I32, _P]),
     "cs_stroke_backward": (ctypes.c_int, [_P] * 20 + [_I32, _I32, _I32, _I32, _P]),
     "cs_edge_grads_to_cubics": (ctypes.c_int, [_P, _P, _I64, _I32, _F32, _F32, _P]),
+    "cs_ring_to_cubics": (ctypes.c_int, [_P, _P, _I64, _I32, _I32, _I32, _P]),
+    "cs_edge_grads_to_ring": (ctypes.c_int, [_P, _P, _I64, _I32, _I32, _I32, _I32, _I32, _P]),
+    "cs_adam_workspace_size": (_SZ, []),
+    "cs_adam_step": (ctypes.c_int, [_P, _P, _P, _P, _I64, _I64, _F32, _F32, _F32, _F32, _F32, _P,
+                                    _P, _I32, _P]),
     "cs_ring_segments_forward": (ctypes.c_int, [_P, _P, _P, _P, _P, _I64, _I32, _I32, _P]),
     "cs_ring_segments_backward": (ctypes.c_int, [_P, _P, _P, _P, _P, _I64, _I32, _I32, _P]),
     "cs_mse_workspace_size": (_SZ, [_I64]),

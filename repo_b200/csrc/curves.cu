@@ -120,6 +120,119 @@ __global__ void ring_backward_kernel(const float* __restrict__ gseg, const float
   }
 }
 
+// ---------------------------------------------------------------------------
+// ring parameterisation of closed paths: ring [P, 3G, 2] pixel-space points,
+// segment k of a path = (r[3k], r[3k+1], r[3k+2], r[3k+3 mod 3G])
+
+// cubics_norm = ring point / (W/2, H/2) - 1 (IEEE division, then subtraction)
+__global__ void ring_to_cubics_kernel(const float* __restrict__ ring, float* __restrict__ cn,
+                                      long long npaths, int G, float half_w, float half_h) {
+  const long long q = (long long)blockIdx.x * blockDim.x + threadIdx.x;  // control point
+  const long long total = npaths * G * 4;
+  if (q >= total) return;
+  const long long path = q / (4 * G);
+  const int local = (int)(q - path * 4 * G);
+  const int k = local >> 2, j = local & 3;
+  int r = 3 * k + j;
+  if (r >= 3 * G) r -= 3 * G;
+  const float2 v = reinterpret_cast<const float2*>(ring)[path * 3 * G + r];
+  reinterpret_cast<float2*>(cn)[q] = make_float2(v.x / half_w - 1.0f, v.y / half_h - 1.0f);
+}
+
+// Edge endpoint gradients -> ring point gradients.  Each segment's control
+// point gradient is the reference's Bernstein accumulation scaled to
+// normalised space (x W/2, H/2); the ring gradient is that divided by
+// (W/2, H/2) (the derivative of the normalisation), summed over the one or
+// two control points that share the ring point.  One CTA handles whole
+// paths; optionally v_edges is cleared after it is read.
+constexpr int kRingThreads = 128;
+
+__global__ void __launch_bounds__(kRingThreads) edge_grads_to_ring_kernel(
+    float4* __restrict__ v_edges, float* __restrict__ v_ring, long long npaths, int G, int E,
+    float half_w, float half_h, int clear) {
+  __shared__ float cub[kRingThreads][9];
+  const int ppb = max(1, kRingThreads / G);
+  const long long p0 = (long long)blockIdx.x * ppb;
+  const int nseg = (int)min((long long)ppb * G, (npaths - p0) * G);
+  const float inv_e = 1.0f / (float)E;
+  for (int t = threadIdx.x; t < nseg; t += kRingThreads) {
+    const long long sid = p0 * G + t;
+    float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int e = 0; e < E; ++e) {
+      float t0 = (float)e * inv_e, t1 = (float)(e + 1) * inv_e;
+      float o0 = 1.0f - t0, o1 = 1.0f - t1;
+      float o0s = o0 * o0, o1s = o1 * o1, t0s = t0 * t0, t1s = t1 * t1;
+      float b0[4] = {o0s * o0, 3.0f * o0s * t0, 3.0f * o0 * t0s, t0s * t0};
+      float b1[4] = {o1s * o1, 3.0f * o1s * t1, 3.0f * o1 * t1s, t1s * t1};
+      float4* gp = v_edges + sid * E + e;
+      const float4 g = *gp;
+      if (clear) *gp = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        a[2 * c] = a[2 * c] + g.x * b0[c] + g.z * b1[c];
+        a[2 * c + 1] = a[2 * c + 1] + g.y * b0[c] + g.w * b1[c];
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      cub[t][2 * c] = (a[2 * c] * half_w) / half_w;
+      cub[t][2 * c + 1] = (a[2 * c + 1] * half_h) / half_h;
+    }
+  }
+  __syncthreads();
+  const int npts = nseg / G * 3 * G;
+  for (int t = threadIdx.x; t < npts; t += kRingThreads) {
+    const int path = t / (3 * G), r = t - path * 3 * G;
+    const int k = r / 3, j = r - 3 * k;
+    const int s = path * G + k;
+    float gx = cub[s][2 * j], gy = cub[s][2 * j + 1];
+    if (j == 0) {  // shared with the end point of the previous segment
+      const int sp = path * G + (k == 0 ? G - 1 : k - 1);
+      gx = gx + cub[sp][6];
+      gy = gy + cub[sp][7];
+    }
+    reinterpret_cast<float2*>(v_ring)[(p0 * 3 * G) + t] = make_float2(gx, gy);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Adam over one flat parameter buffer with two learning rates (elements
+// [0, n_first) use lr0, the rest lr1):  m = b1 m + (1-b1) g,
+// v = b2 v + (1-b2) g^2, p -= lr (m / (1-b1^t)) / (sqrt(v / (1-b2^t)) + eps),
+// t = *step + 1 read on the device; the last CTA to finish stores t.
+// Optionally the gradient is cleared after use.
+__global__ void adam_kernel(float* __restrict__ p, float* __restrict__ g, float* __restrict__ m,
+                            float* __restrict__ v, long long n, long long n_first, float lr0,
+                            float lr1, float b1, float b2, float eps, int* __restrict__ step,
+                            unsigned int* __restrict__ ticket, int clear) {
+  __shared__ bool last;
+  const int t = *step + 1;
+  const float bc1 = 1.0f - powf(b1, (float)t);
+  const float bc2 = 1.0f - powf(b2, (float)t);
+  const float rb2 = 1.0f / sqrtf(bc2);
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    const float gi = g[i];
+    const float mi = b1 * m[i] + (1.0f - b1) * gi;
+    const float vi = b2 * v[i] + (1.0f - b2) * gi * gi;
+    m[i] = mi;
+    v[i] = vi;
+    const float lr = i < n_first ? lr0 : lr1;
+    p[i] = p[i] - (lr / bc1) * mi / (sqrtf(vi) * rb2 + eps);
+    if (clear) g[i] = 0.0f;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    last = atomicAdd(ticket, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (last && threadIdx.x == 0) {
+    *step = t;
+    *ticket = 0u;
+  }
+}
+
 }  // namespace cs
 
 using namespace cs;
@@ -157,6 +270,45 @@ int cs_ring_segments_backward(const float* grad_segments, const float* basis,
   if (n == 0) return CS_OK;
   ring_backward_kernel<<<ceil_div(n, 256), 256, 0, (cudaStream_t)stream>>>(
       grad_segments, basis, deriv_basis, dt, grad_control_points, n, k, subdiv);
+  return launch_status();
+}
+
+int cs_ring_to_cubics(const float* ring, float* cubics_norm, int64_t num_paths,
+                      int32_t segs_per_path, int32_t img_height, int32_t img_width, void* stream) {
+  if (num_paths < 0 || segs_per_path <= 0 || img_height <= 0 || img_width <= 0) return CS_ERR_ARG;
+  const long long n = num_paths * segs_per_path * 4;
+  if (n == 0) return CS_OK;
+  ring_to_cubics_kernel<<<ceil_div(n, 256), 256, 0, (cudaStream_t)stream>>>(
+      ring, cubics_norm, num_paths, segs_per_path, 0.5f * (float)img_width,
+      0.5f * (float)img_height);
+  return launch_status();
+}
+
+int cs_edge_grads_to_ring(float* v_edges, float* v_ring, int64_t num_paths, int32_t segs_per_path,
+                          int32_t edges_per_segment, int32_t img_height, int32_t img_width,
+                          int32_t clear_edges, void* stream) {
+  if (num_paths < 0 || segs_per_path <= 0 || segs_per_path > kRingThreads ||
+      edges_per_segment <= 0)
+    return CS_ERR_ARG;
+  if (num_paths == 0) return CS_OK;
+  const int ppb = max(1, kRingThreads / segs_per_path);
+  edge_grads_to_ring_kernel<<<ceil_div(num_paths, ppb), kRingThreads, 0, (cudaStream_t)stream>>>(
+      reinterpret_cast<float4*>(v_edges), v_ring, num_paths, segs_per_path, edges_per_segment,
+      0.5f * (float)img_width, 0.5f * (float)img_height, clear_edges);
+  return launch_status();
+}
+
+size_t cs_adam_workspace_size(void) { return 256; }
+
+int cs_adam_step(float* params, float* grads, float* exp_avg, float* exp_avg_sq, int64_t n,
+                 int64_t n_first, float lr_first, float lr_rest, float beta1, float beta2,
+                 float eps, int32_t* step, void* workspace, int32_t clear_grads, void* stream) {
+  if (n < 0 || n_first < 0 || !step || !workspace) return CS_ERR_ARG;
+  if (n == 0) return CS_OK;
+  const int blocks = (int)((n + 255) / 256 < 148 * 4 ? (n + 255) / 256 : 148 * 4);
+  adam_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(
+      params, grads, exp_avg, exp_avg_sq, n, n_first, lr_first, lr_rest, beta1, beta2, eps, step,
+      static_cast<unsigned int*>(workspace), clear_grads);
   return launch_status();
 }
 

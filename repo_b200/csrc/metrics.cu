@@ -89,96 +89,133 @@ __global__ void mse_backward_kernel(const float* __restrict__ lhs, const float* 
 }
 
 // --------------------------------------------------------------------------
-// SSIM
+// SSIM: one launch.  Each CTA computes a 32x32 block of the SSIM map of one
+// plane: the (32+R)^2 input window is loaded to shared memory, a horizontal
+// pass writes the five windowed moments (x, y, x^2, y^2, xy) for 32 output
+// columns, each thread producing 8 columns from one register window, then a
+// vertical pass produces 4 output rows per thread the same way.  Per-CTA SSIM
+// sums are reduced per plane by the last CTA to finish.
 
-constexpr int kSsimTx = 32;   // output tile width
-constexpr int kSsimTy = 16;   // output tile height
+constexpr int kSsimT = 32;         // output tile edge
 constexpr int kSsimThreads = 256;
 constexpr int kMaxWin = 15;
+constexpr int kMaxR = kMaxWin - 1;
+constexpr int kSsimIn = kSsimT + kMaxR;
 
-__global__ void __launch_bounds__(kSsimThreads) ssim_tile_kernel(
+__global__ void __launch_bounds__(kSsimThreads) ssim_kernel(
     const float* __restrict__ x, const float* __restrict__ y, const float* __restrict__ gauss,
-    int h, int w, int win, float c1, float c2, float* __restrict__ ssim_map,
-    float* __restrict__ partials) {
-  extern __shared__ float smem[];
-  const int R = win - 1;
-  const int in_w = kSsimTx + R, in_h = kSsimTy + R;
-  float* sx = smem;                          // [in_h][in_w]
-  float* sy = sx + in_h * in_w;
-  float* hs = sy + in_h * in_w;              // 5 x [in_h][kSsimTx]
+    int h, int w, int win, float c1, float c2, float inv_count, float* __restrict__ ssim_map,
+    float* __restrict__ partials, unsigned int* __restrict__ ticket,
+    float* __restrict__ plane_means) {
+  __shared__ float sx[kSsimIn][kSsimIn + 1];
+  __shared__ float sy[kSsimIn][kSsimIn + 1];
+  __shared__ float hs[5][kSsimIn][kSsimT + 1];
   __shared__ float g[kMaxWin];
-  __shared__ float red[32];
+  __shared__ float red[kSsimThreads / 32];
+  __shared__ bool last;
+  const int R = win - 1;
+  const int in_n = kSsimT + R;
   const long long plane = blockIdx.z;
   const int oh = h - R, ow = w - R;
-  const int ox0 = blockIdx.x * kSsimTx, oy0 = blockIdx.y * kSsimTy;
+  const int ox0 = blockIdx.x * kSsimT, oy0 = blockIdx.y * kSsimT;
   const float* xp = x + plane * (long long)h * w;
   const float* yp = y + plane * (long long)h * w;
-  if (threadIdx.x < win) g[threadIdx.x] = gauss[threadIdx.x];
-  for (int idx = threadIdx.x; idx < in_h * in_w; idx += kSsimThreads) {
-    int r = idx / in_w, c = idx - r * in_w;
-    int gy = oy0 + r, gx = ox0 + c;
-    bool ok = gy < h && gx < w;
-    sx[idx] = ok ? xp[(long long)gy * w + gx] : 0.0f;
-    sy[idx] = ok ? yp[(long long)gy * w + gx] : 0.0f;
+  const int tid = threadIdx.x;
+  if (tid < win) g[tid] = gauss[tid];
+  for (int idx = tid; idx < in_n * in_n; idx += kSsimThreads) {
+    const int r = idx / in_n, c = idx - r * in_n;
+    const int gy = oy0 + r, gx = ox0 + c;
+    const bool ok = gy < h && gx < w;
+    sx[r][c] = ok ? __ldg(xp + (long long)gy * w + gx) : 0.0f;
+    sy[r][c] = ok ? __ldg(yp + (long long)gy * w + gx) : 0.0f;
   }
   __syncthreads();
-  const int plane_sz = in_h * kSsimTx;
-  for (int idx = threadIdx.x; idx < plane_sz; idx += kSsimThreads) {
-    int r = idx / kSsimTx, c = idx - r * kSsimTx;
-    float m1 = 0.f, m2 = 0.f, e11 = 0.f, e22 = 0.f, e12 = 0.f;
-    const float* rx = sx + r * in_w + c;
-    const float* ry = sy + r * in_w + c;
-    for (int k = 0; k < win; ++k) {
-      float gk = g[k], a = rx[k], b = ry[k];
-      m1 = __fmaf_rn(gk, a, m1);
-      m2 = __fmaf_rn(gk, b, m2);
-      e11 = __fmaf_rn(gk, a * a, e11);
-      e22 = __fmaf_rn(gk, b * b, e22);
-      e12 = __fmaf_rn(gk, a * b, e12);
+  // horizontal: item = (input row r, 8 output columns)
+  for (int item = tid; item < in_n * (kSsimT / 8); item += kSsimThreads) {
+    const int r = item >> 2, c0 = (item & 3) * 8;
+    float a[8 + kMaxR], b[8 + kMaxR];
+#pragma unroll
+    for (int q = 0; q < 8 + kMaxR; ++q) {
+      a[q] = q < 8 + R ? sx[r][c0 + q] : 0.0f;
+      b[q] = q < 8 + R ? sy[r][c0 + q] : 0.0f;
     }
-    hs[idx] = m1;
-    hs[plane_sz + idx] = m2;
-    hs[2 * plane_sz + idx] = e11;
-    hs[3 * plane_sz + idx] = e22;
-    hs[4 * plane_sz + idx] = e12;
+#pragma unroll
+    for (int o = 0; o < 8; ++o) {
+      float m1 = 0.f, m2 = 0.f, e11 = 0.f, e22 = 0.f, e12 = 0.f;
+#pragma unroll
+      for (int k = 0; k < kMaxWin; ++k) {
+        if (k < win) {
+          const float gk = g[k], u = a[o + k], v = b[o + k];
+          m1 = __fmaf_rn(gk, u, m1);
+          m2 = __fmaf_rn(gk, v, m2);
+          e11 = __fmaf_rn(gk, u * u, e11);
+          e22 = __fmaf_rn(gk, v * v, e22);
+          e12 = __fmaf_rn(gk, u * v, e12);
+        }
+      }
+      hs[0][r][c0 + o] = m1;
+      hs[1][r][c0 + o] = m2;
+      hs[2][r][c0 + o] = e11;
+      hs[3][r][c0 + o] = e22;
+      hs[4][r][c0 + o] = e12;
+    }
   }
   __syncthreads();
+  // vertical: item = (output column c, 4 output rows)
   float local = 0.0f;
-  for (int idx = threadIdx.x; idx < kSsimTx * kSsimTy; idx += kSsimThreads) {
-    int r = idx / kSsimTx, c = idx - r * kSsimTx;
-    int oy = oy0 + r, ox = ox0 + c;
-    if (oy >= oh || ox >= ow) continue;
-    float mu1 = 0.f, mu2 = 0.f, ex2 = 0.f, ey2 = 0.f, exy = 0.f;
-    for (int k = 0; k < win; ++k) {
-      int o = (r + k) * kSsimTx + c;
-      float gk = g[k];
-      mu1 = __fmaf_rn(gk, hs[o], mu1);
-      mu2 = __fmaf_rn(gk, hs[plane_sz + o], mu2);
-      ex2 = __fmaf_rn(gk, hs[2 * plane_sz + o], ex2);
-      ey2 = __fmaf_rn(gk, hs[3 * plane_sz + o], ey2);
-      exy = __fmaf_rn(gk, hs[4 * plane_sz + o], exy);
+  {
+    const int c = tid & 31, r0 = (tid >> 5) * 4;
+    float mom[4][5];
+#pragma unroll
+    for (int o = 0; o < 4; ++o)
+#pragma unroll
+      for (int q = 0; q < 5; ++q) mom[o][q] = 0.0f;
+#pragma unroll
+    for (int q = 0; q < 5; ++q) {
+      float col[4 + kMaxR];
+#pragma unroll
+      for (int t = 0; t < 4 + kMaxR; ++t) col[t] = t < 4 + R ? hs[q][r0 + t][c] : 0.0f;
+#pragma unroll
+      for (int o = 0; o < 4; ++o) {
+        float acc = 0.0f;
+#pragma unroll
+        for (int k = 0; k < kMaxWin; ++k)
+          if (k < win) acc = __fmaf_rn(g[k], col[o + k], acc);
+        mom[o][q] = acc;
+      }
     }
-    float mu1_sq = mu1 * mu1, mu2_sq = mu2 * mu2, mu12 = mu1 * mu2;
-    float s1 = ex2 - mu1_sq, s2 = ey2 - mu2_sq, s12 = exy - mu12;
-    float lum = (2.0f * mu12 + c1) / (mu1_sq + mu2_sq + c1);
-    float cs_ = (2.0f * s12 + c2) / (s1 + s2 + c2);
-    float v = lum * cs_;
-    if (ssim_map) ssim_map[(plane * oh + oy) * (long long)ow + ox] = v;
-    local += v;
+#pragma unroll
+    for (int o = 0; o < 4; ++o) {
+      const int oy = oy0 + r0 + o, ox = ox0 + c;
+      if (oy >= oh || ox >= ow) continue;
+      const float mu1 = mom[o][0], mu2 = mom[o][1];
+      const float mu1_sq = mu1 * mu1, mu2_sq = mu2 * mu2, mu12 = mu1 * mu2;
+      const float s1 = mom[o][2] - mu1_sq, s2 = mom[o][3] - mu2_sq, s12 = mom[o][4] - mu12;
+      const float lum = (2.0f * mu12 + c1) / (mu1_sq + mu2_sq + c1);
+      const float cs_ = (2.0f * s12 + c2) / (s1 + s2 + c2);
+      const float v = lum * cs_;
+      if (ssim_map) ssim_map[(plane * oh + oy) * (long long)ow + ox] = v;
+      local += v;
+    }
   }
-  float bs = block_sum(local, red);
-  if (threadIdx.x == 0)
-    partials[plane * (long long)(gridDim.x * gridDim.y) + blockIdx.y * gridDim.x + blockIdx.x] = bs;
-}
-
-__global__ void ssim_reduce_kernel(const float* __restrict__ partials, int nblk, float inv_count,
-                                   float* __restrict__ plane_means) {
-  __shared__ float red[32];
-  const long long plane = blockIdx.x;
-  float v = 0.0f;
-  for (int i = threadIdx.x; i < nblk; i += blockDim.x) v += partials[plane * nblk + i];
-  float t = block_sum(v, red);
-  if (threadIdx.x == 0) plane_means[plane] = t * inv_count;
+  const float bs = block_sum(local, red);
+  const unsigned tiles = gridDim.x * gridDim.y;
+  const unsigned nblk = tiles * gridDim.z;
+  if (tid == 0) {
+    partials[plane * tiles + blockIdx.y * gridDim.x + blockIdx.x] = bs;
+    __threadfence();
+    last = atomicAdd(ticket, 1u) == nblk - 1;
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  for (unsigned pl = 0; pl < gridDim.z; ++pl) {
+    float v = 0.0f;
+    for (unsigned q = tid; q < tiles; q += kSsimThreads) v += partials[pl * tiles + q];
+    const float t = block_sum(v, red);
+    if (tid == 0) plane_means[pl] = t * inv_count;
+  }
+  if (tid == 0) *ticket = 0u;
 }
 
 inline int mse_blocks(long long n) {
@@ -218,34 +255,32 @@ int cs_mse_backward(const float* lhs, const float* rhs, const float* scale, floa
 }
 
 static inline void ssim_grid(int32_t h, int32_t w, int32_t win, int& gx, int& gy) {
-  gx = (w - win + 1 + kSsimTx - 1) / kSsimTx;
-  gy = (h - win + 1 + kSsimTy - 1) / kSsimTy;
+  gx = (w - win + 1 + kSsimT - 1) / kSsimT;
+  gy = (h - win + 1 + kSsimT - 1) / kSsimT;
 }
 
 size_t cs_ssim_workspace_size(int64_t planes, int32_t h, int32_t w, int32_t win) {
   int gx, gy;
   ssim_grid(h, w, win, gx, gy);
-  return sizeof(float) * (size_t)planes * gx * gy;
+  return 256 + sizeof(float) * (size_t)planes * gx * gy;
 }
 
 int cs_ssim(const float* x, const float* y, const float* gauss, int64_t planes, int32_t h,
             int32_t w, int32_t win, float c1, float c2, float* plane_means, float* ssim_map,
             void* workspace, void* stream) {
-  if (planes <= 0 || win <= 0 || win % 2 == 0 || win > kMaxWin || h < win || w < win ||
-      !workspace || !plane_means)
+  if (planes <= 0 || win <= 0 || win % 2 == 0 || h < win || w < win || !workspace ||
+      !plane_means)
     return CS_ERR_ARG;
-  if (planes > 65535) return CS_ERR_UNSUPPORTED;
+  if (win > kMaxWin || planes > 65535) return CS_ERR_UNSUPPORTED;
   cudaStream_t st = (cudaStream_t)stream;
   int gx, gy;
   ssim_grid(h, w, win, gx, gy);
   const int R = win - 1;
-  size_t smem = sizeof(float) * ((size_t)2 * (kSsimTy + R) * (kSsimTx + R) +
-                                 (size_t)5 * (kSsimTy + R) * kSsimTx);
-  float* partials = static_cast<float*>(workspace);
-  ssim_tile_kernel<<<dim3(gx, gy, (unsigned)planes), kSsimThreads, smem, st>>>(
-      x, y, gauss, h, w, win, c1, c2, ssim_map, partials);
-  float inv_count = 1.0f / ((float)(h - R) * (float)(w - R));
-  ssim_reduce_kernel<<<(unsigned)planes, 256, 0, st>>>(partials, gx * gy, inv_count, plane_means);
+  unsigned int* ticket = static_cast<unsigned int*>(workspace);
+  float* partials = reinterpret_cast<float*>(static_cast<char*>(workspace) + 256);
+  const float inv_count = 1.0f / ((float)(h - R) * (float)(w - R));
+  ssim_kernel<<<dim3(gx, gy, (unsigned)planes), kSsimThreads, 0, st>>>(
+      x, y, gauss, h, w, win, c1, c2, inv_count, ssim_map, partials, ticket, plane_means);
   return launch_status();
 }
 

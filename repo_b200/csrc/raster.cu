@@ -54,6 +54,10 @@ struct RasterArgs {
   float* fts;
   int* fidx;
   float* out_chw;
+  const float* loss_tgt;     // optional [3, H, W] target: fused SSE / MSE
+  float* loss_out;           // [2]: sse of the launched tiles, sse / (3 H W)
+  float* loss_partials;      // [launched CTAs]
+  unsigned int* loss_ticket;
   // backward
   const float* fts_in;
   const int* fidx_in;
@@ -299,13 +303,13 @@ __global__ void __launch_bounds__(kRT) raster_forward_kernel(const RasterArgs A)
     }
     __syncthreads();  // this chunk's buffer may be refilled
   }
-  if (!ok) return;
   const float bg0 = A.bg[0], bg1 = A.bg[1], bg2 = A.bg[2];
   const long long hw = (long long)A.H * A.W;
+  float sse = 0.0f;
 #pragma unroll
   for (int u = 0; u < 2; ++u) {
     const FwdPix& p = u ? p1 : p0;
-    if (!(u ? in1 : in0)) continue;
+    if (!ok || !(u ? in1 : in0)) continue;
     const long long pix = (long long)i * A.W + j0 + u;
     const float o0 = p.a0 + p.T * bg0, o1 = p.a1 + p.T * bg1, o2 = p.a2 + p.T * bg2;
     A.fts[pix] = p.T;
@@ -313,13 +317,55 @@ __global__ void __launch_bounds__(kRT) raster_forward_kernel(const RasterArgs A)
     A.out[pix * 3] = o0;
     A.out[pix * 3 + 1] = o1;
     A.out[pix * 3 + 2] = o2;
+    const float k0 = fminf(fmaxf(o0, 0.0f), 1.0f), k1 = fminf(fmaxf(o1, 0.0f), 1.0f),
+                k2 = fminf(fmaxf(o2, 0.0f), 1.0f);
     if (A.out_chw) {
-      A.out_chw[pix] = fminf(fmaxf(o0, 0.0f), 1.0f);
-      A.out_chw[hw + pix] = fminf(fmaxf(o1, 0.0f), 1.0f);
-      A.out_chw[2 * hw + pix] = fminf(fmaxf(o2, 0.0f), 1.0f);
+      A.out_chw[pix] = k0;
+      A.out_chw[hw + pix] = k1;
+      A.out_chw[2 * hw + pix] = k2;
+    }
+    if (A.loss_tgt) {
+      const float d0 = k0 - A.loss_tgt[pix], d1 = k1 - A.loss_tgt[hw + pix],
+                  d2 = k2 - A.loss_tgt[2 * hw + pix];
+      sse = __fmaf_rn(d0, d0, sse);
+      sse = __fmaf_rn(d1, d1, sse);
+      sse = __fmaf_rn(d2, d2, sse);
     }
   }
-  (void)lane;
+  if (A.loss_tgt) {
+    // per-CTA partial; the last CTA to finish reduces them in a fixed order
+    __shared__ float red[kRT / 32];
+    __shared__ bool last;
+    sse = warp_sum(sse);
+    if (lane == 0) red[tid >> 5] = sse;
+    __syncthreads();
+    const unsigned nblk = gridDim.x * gridDim.y;
+    if (tid == 0) {
+      float bsum = 0.0f;
+#pragma unroll
+      for (int w = 0; w < kRT / 32; ++w) bsum += red[w];
+      A.loss_partials[blockIdx.y * gridDim.x + blockIdx.x] = bsum;
+      __threadfence();
+      last = atomicAdd(A.loss_ticket, 1u) == nblk - 1;
+    }
+    __syncthreads();
+    if (last) {
+      __threadfence();
+      float v = 0.0f;
+      for (unsigned q = tid; q < nblk; q += kRT) v += A.loss_partials[q];
+      v = warp_sum(v);
+      if (lane == 0) red[tid >> 5] = v;
+      __syncthreads();
+      if (tid == 0) {
+        float t = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kRT / 32; ++w) t += red[w];
+        A.loss_out[0] = t;
+        A.loss_out[1] = t / (3.0f * (float)A.H * (float)A.W);
+        *A.loss_ticket = 0u;
+      }
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -440,8 +486,8 @@ __device__ __forceinline__ void bwd_pixel(BwdPix& s, const IMeta& m, float px, f
 __device__ __forceinline__ void flush_acc(const RasterArgs& A, int pid, int k, int c, float v) {
   if (v == 0.0f) return;
   if (c < 3) atomicAdd(A.v_colors + pid * 3 + c, v);
-  else if (c == 3) atomicAdd(A.v_opac + pid, v);
-  else if (c == 4) atomicAdd(A.v_inv + pid, v);
+  else if (c == 3) { if (A.v_opac) atomicAdd(A.v_opac + pid, v); }
+  else if (c == 4) { if (A.v_inv) atomicAdd(A.v_inv + pid, v); }
   else if (c == 5) atomicAdd(A.v_sw + pid, v);
   else if (c < 9) { if (A.contrib) atomicAdd(A.contrib + pid * 3 + (c - 6), v); }
   else if (A.icontrib) atomicAdd(A.icontrib + k, v);
@@ -678,10 +724,12 @@ static int raster_forward(bool stroke, const int32_t* prim_ids_sorted, const int
                           const int32_t* tile_dlist, const void* imeta, const int32_t* rowoff,
                           const void* dlist, const float* background, float* out_img,
                           float* final_Ts, int32_t* final_idx, float* out_chw_clamped,
+                          const float* target_chw, float* loss_out, void* loss_ws,
                           int32_t* status, int32_t img_height, int32_t img_width,
                           int32_t tile_row_begin, int32_t tile_row_end, void* stream) {
   if (img_height <= 0 || img_width <= 0 || !tile_bins || !tile_dlist || !imeta || !dlist ||
-      !background || !out_img || !final_Ts || !final_idx || (!stroke && !rowoff))
+      !background || !out_img || !final_Ts || !final_idx || (!stroke && !rowoff) ||
+      (target_chw && (!loss_out || !loss_ws)))
     return CS_ERR_ARG;
   RasterArgs a{};
   stage_args(a, prim_ids_sorted, tile_bins, tile_dlist, imeta, rowoff, dlist, background, status);
@@ -689,30 +737,42 @@ static int raster_forward(bool stroke, const int32_t* prim_ids_sorted, const int
   a.fts = final_Ts;
   a.fidx = final_idx;
   a.out_chw = out_chw_clamped;
+  a.loss_tgt = target_chw;
+  a.loss_out = loss_out;
+  a.loss_ticket = static_cast<unsigned int*>(loss_ws);
+  a.loss_partials = reinterpret_cast<float*>(static_cast<char*>(loss_ws) + 256);
   return launch_raster(stroke, false, a, img_height, img_width, tile_row_begin, tile_row_end,
                        (cudaStream_t)stream);
+}
+
+size_t cs_loss_workspace_size(int64_t num_tiles) {
+  return 256 + sizeof(float) * (size_t)(num_tiles > 0 ? num_tiles : 1);
 }
 
 int cs_fill_forward(const int32_t* prim_ids_sorted, const int32_t* tile_bins,
                     const int32_t* tile_dlist, const void* imeta, const int32_t* rowoff,
                     const void* dlist, const float* background, float* out_img, float* final_Ts,
-                    int32_t* final_idx, float* out_chw_clamped, int32_t* status,
-                    int32_t img_height, int32_t img_width, int32_t tile_row_begin,
-                    int32_t tile_row_end, void* stream) {
+                    int32_t* final_idx, float* out_chw_clamped, const float* target_chw,
+                    float* loss_out, void* loss_ws, int32_t* status, int32_t img_height,
+                    int32_t img_width, int32_t tile_row_begin, int32_t tile_row_end,
+                    void* stream) {
   return raster_forward(false, prim_ids_sorted, tile_bins, tile_dlist, imeta, rowoff, dlist,
-                        background, out_img, final_Ts, final_idx, out_chw_clamped, status,
-                        img_height, img_width, tile_row_begin, tile_row_end, stream);
+                        background, out_img, final_Ts, final_idx, out_chw_clamped, target_chw,
+                        loss_out, loss_ws, status, img_height, img_width, tile_row_begin,
+                        tile_row_end, stream);
 }
 
 int cs_stroke_forward(const int32_t* prim_ids_sorted, const int32_t* tile_bins,
                       const int32_t* tile_dlist, const void* imeta, const void* dlist,
                       const float* background, float* out_img, float* final_Ts,
-                      int32_t* final_idx, float* out_chw_clamped, int32_t* status,
-                      int32_t img_height, int32_t img_width, int32_t tile_row_begin,
-                      int32_t tile_row_end, void* stream) {
+                      int32_t* final_idx, float* out_chw_clamped, const float* target_chw,
+                      float* loss_out, void* loss_ws, int32_t* status, int32_t img_height,
+                      int32_t img_width, int32_t tile_row_begin, int32_t tile_row_end,
+                      void* stream) {
   return raster_forward(true, prim_ids_sorted, tile_bins, tile_dlist, imeta, nullptr, dlist,
-                        background, out_img, final_Ts, final_idx, out_chw_clamped, status,
-                        img_height, img_width, tile_row_begin, tile_row_end, stream);
+                        background, out_img, final_Ts, final_idx, out_chw_clamped, target_chw,
+                        loss_out, loss_ws, status, img_height, img_width, tile_row_begin,
+                        tile_row_end, stream);
 }
 
 static int raster_backward(bool stroke, const int32_t* prim_ids_sorted, const int32_t* tile_bins,
@@ -727,7 +787,7 @@ static int raster_backward(bool stroke, const int32_t* prim_ids_sorted, const in
                            void* stream) {
   if (img_height <= 0 || img_width <= 0 || !prim_ids_sorted || !tile_bins || !tile_dlist ||
       !imeta || !dlist || !background || !final_Ts || !final_idx || !v_edges || !v_colors ||
-      !v_opacities || !v_inv_sigma2s || (!stroke && !rowoff) || (stroke && !v_stroke_widths))
+      (!stroke && !rowoff) || (stroke && !v_stroke_widths))
     return CS_ERR_ARG;
   if (!v_output && (!out_img || !target_chw || !mse_scale)) return CS_ERR_ARG;
   RasterArgs a{};

@@ -24,11 +24,13 @@ _WS_CACHE: Dict[Tuple[str, str], torch.Tensor] = {}
 
 
 def _workspace(device: torch.device, kind: str, nbytes: int) -> torch.Tensor:
-    """Per-device scratch buffer, grown on demand, used in stream order."""
+    """Per-device scratch buffer, grown on demand, used in stream order.  It is
+    zeroed when allocated: the kernels' completion tickets start at zero and
+    are reset by the kernels themselves."""
     key = (str(device), kind)
     buf = _WS_CACHE.get(key)
     if buf is None or buf.numel() < nbytes:
-        buf = torch.empty((max(nbytes, 256),), dtype=torch.uint8, device=device)
+        buf = torch.zeros((max(nbytes, 256),), dtype=torch.uint8, device=device)
         _WS_CACHE[key] = buf
     return buf
 

@@ -271,14 +271,14 @@ def forward_raster(b: Binning, background, img_h: int, img_w: int, out_chw=None,
         nat.check(nat.call("cs_fill_forward", nat.ptr(b.prim_ids_sorted), nat.ptr(b.tile_bins),
                            nat.ptr(b.tile_dlist), nat.ptr(b.imeta), nat.ptr(b.rowoff),
                            nat.ptr(b.dlist), nat.ptr(background), nat.ptr(out), nat.ptr(fts),
-                           nat.ptr(fidx), nat.ptr(out_chw), nat.ptr(status), img_h, img_w,
-                           b.tile_rows[0], b.tile_rows[1], st), "cs_fill_forward")
+                           nat.ptr(fidx), nat.ptr(out_chw), None, None, None, nat.ptr(status),
+                           img_h, img_w, b.tile_rows[0], b.tile_rows[1], st), "cs_fill_forward")
     else:
         nat.check(nat.call("cs_stroke_forward", nat.ptr(b.prim_ids_sorted), nat.ptr(b.tile_bins),
                            nat.ptr(b.tile_dlist), nat.ptr(b.imeta), nat.ptr(b.dlist),
                            nat.ptr(background), nat.ptr(out), nat.ptr(fts), nat.ptr(fidx),
-                           nat.ptr(out_chw), nat.ptr(status), img_h, img_w, b.tile_rows[0],
-                           b.tile_rows[1], st), "cs_stroke_forward")
+                           nat.ptr(out_chw), None, None, None, nat.ptr(status), img_h, img_w,
+                           b.tile_rows[0], b.tile_rows[1], st), "cs_stroke_forward")
     return out, fts, fidx
 
 

@@ -1,18 +1,27 @@
 """Device-resident training step for closed cubic fills (the B200-native path).
 
-One step = parameters -> normalised cubics -> fused binning -> forward raster
-(which also writes the clamped CHW image) -> MSE and SSIM -> backward raster
-with the MSE gradient computed in the kernel -> cubic / ring gradients ->
-Adam.  Nothing synchronises with the host, so the whole step can be captured
-into one CUDA graph and replayed.  This is the same computation as the
-reference's training step (manbo/gaussian_trace/train_ops.py:36-68 with the
-cubic_fill renderer, an MSE data loss and SSIM as a forward metric), with the
-intersect list sized by a fixed capacity: an overflow is reported through a
-device status word (check_status) and never reads or writes out of bounds.
+One step, all on the device and capturable as one CUDA graph:
+
+  ring params -> normalised cubics               cs_ring_to_cubics
+  projection, AABB, flatten, tile counts, scans  cs_bin_count
+  scatter, per-tile sort, edge staging           cs_bin_sort
+  forward raster + clamped CHW image + MSE loss  cs_fill_forward (target given)
+  SSIM (forward metric)                          cs_ssim
+  backward raster with the MSE gradient inside   cs_fill_backward (v_output NULL)
+  edge -> ring gradients (clears edge grads)     cs_edge_grads_to_ring
+  Adam on [ring | colours] (clears grads)        cs_adam_step
+
+This is the reference's training step (manbo/gaussian_trace/train_ops.py:36-68
+with the cubic_fill renderer, an MSE data loss and SSIM as a forward metric)
+with Adam (lr 0.5 on points, 0.01 on colours).  Gradient buffers are cleared
+by the kernels that consume them, so no memset is needed between steps.  The
+intersect list and staged edge records use fixed capacities: an overflow is
+recorded in a sticky device status word (check_status) and never reads or
+writes out of bounds.
 
 For multi-GPU runs ``tile_rows`` restricts the rank to a band of tile rows and
-``grad_hook`` (e.g. an NCCL all-reduce) is applied to the flat gradient buffer
-before the optimiser step.
+``grad_hook`` (e.g. an NCCL all-reduce) is applied to the flat buffer
+[ring grads | colour grads | sse, mse] before the optimiser step.
 """
 from __future__ import annotations
 
@@ -24,7 +33,7 @@ import torch
 from . import _native as nat
 from . import metric as _metric
 from . import render as _render
-from .scenes import FillScene, ring_gather_index
+from .scenes import FillScene
 
 INT64_MAX = (1 << 63) - 1
 
@@ -33,25 +42,43 @@ class FillTrainer:
     """Adam fitting of closed cubic fill paths to a target image on one GPU."""
 
     def __init__(self, scene: FillScene, device: torch.device, *, lr_points: float = 0.5,
-                 lr_colors: float = 0.01, with_ssim: bool = True, capacity: Optional[int] = None,
+                 lr_colors: float = 0.01, with_ssim: bool = True, capacity=None,
                  tile_rows: Optional[tuple] = None,
-                 grad_hook: Optional[Callable[[torch.Tensor], None]] = None):
+                 grad_hook: Optional[Callable[[torch.Tensor], None]] = None,
+                 betas=(0.9, 0.999), eps: float = 1e-8):
         dev = torch.device(device)
         self.device = dev
         self.h, self.w, self.s = int(scene.height), int(scene.width), int(scene.samples)
-        self.g_per_path = int(scene.segs_per_path)
+        self.g_per_path = G = int(scene.segs_per_path)
         self.num_paths = p = scene.num_paths
-        self.num_segments = g = p * self.g_per_path
+        self.num_segments = g = p * G
         tbx, tby, _ = _render.tile_bounds_for(self.h, self.w)
         self.tbx, self.tby = tbx, tby
-        self.num_tiles = tbx * tby
+        self.num_tiles = nt = tbx * tby
         self.tile_rows = (0, tby) if tile_rows is None else (int(tile_rows[0]), int(tile_rows[1]))
         self.with_ssim = bool(with_ssim)
         self.grad_hook = grad_hook
+        self.lr = (float(lr_points), float(lr_colors))
+        self.betas, self.eps = (float(betas[0]), float(betas[1])), float(eps)
 
         f32, i32 = torch.float32, torch.int32
-        self.ring = scene.ring.to(dev, f32).clone().contiguous()
-        self.colors = scene.colors.to(dev, f32).clone().contiguous()
+        n_ring = p * 3 * G * 2
+        self.n_ring = n_ring
+        self.n_params = n_ring + 3 * p
+        # parameters [ring | colours], Adam moments, gradients [.. | sse, mse]
+        self.params = torch.cat([scene.ring.reshape(-1), scene.colors.reshape(-1)]).to(dev, f32)
+        self.ring = self.params[:n_ring].view(p, 3 * G, 2)
+        self.colors = self.params[n_ring:].view(p, 3)
+        self.exp_avg = torch.zeros_like(self.params)
+        self.exp_avg_sq = torch.zeros_like(self.params)
+        self.flat_grad = torch.zeros((self.n_params + 2,), device=dev, dtype=f32)
+        self.v_ring = self.flat_grad[:n_ring]
+        self.v_colors = self.flat_grad[n_ring:self.n_params]
+        self.loss = self.flat_grad[self.n_params:]      # [sse, mse] of this rank's tiles
+        self.step_count = torch.zeros((1,), device=dev, dtype=i32)
+        self.adam_ws = torch.zeros((int(nat.call("cs_adam_workspace_size")),), device=dev,
+                                   dtype=torch.uint8)
+
         self.opac = scene.opacities.to(dev, f32).contiguous()
         self.depths = scene.depths.to(dev, f32).contiguous()
         self.rules = scene.fill_rules.to(dev, i32).contiguous()
@@ -60,59 +87,36 @@ class FillTrainer:
         self.bg = scene.background.to(dev, f32).contiguous()
         self.offs = scene.seg_offsets().to(dev, i32).contiguous()
         self.edge_offs = (self.offs.to(torch.int64) * (self.s - 1)).to(i32).contiguous()
-        self.gidx = ring_gather_index(self.g_per_path).to(dev)
-        self.half = torch.tensor([0.5 * self.w, 0.5 * self.h], device=dev, dtype=f32)
         self.target = scene.target.to(dev, f32)[0].contiguous()        # [3, H, W]
         self.basis = _render.bernstein_basis(self.s, dev)
 
         e = g * (self.s - 1)
-        self.cub = torch.empty((p, 4 * self.g_per_path, 2), device=dev, dtype=f32)
         self.cn = torch.empty((g, 4, 2), device=dev, dtype=f32)
         self.cubics_px = torch.empty((g, 4, 2), device=dev, dtype=f32)
         self.edges = torch.empty((e, 2, 2), device=dev, dtype=f32)
+        self.v_edges = torch.zeros((e, 2, 2), device=dev, dtype=f32)
         self.prim_ranges = torch.empty((p, 4), device=dev, dtype=i32)
         self.num_hit = torch.empty((p,), device=dev, dtype=i32)
-        self.tile_bins = torch.empty((self.num_tiles, 2), device=dev, dtype=i32)
-        self.tile_dlist = torch.empty((self.num_tiles, 2), device=dev, dtype=i32)
-        # intersects, status, staged-record bound, unused
+        self.tile_bins = torch.empty((nt, 2), device=dev, dtype=i32)
+        self.tile_dlist = torch.empty((nt, 2), device=dev, dtype=i32)
+        # intersects, sticky status, staged-record bound, unused
         self.counters = torch.zeros((4,), device=dev, dtype=i32)
-        self.bin_ws = torch.empty((int(nat.call("cs_bin_workspace_size", self.num_tiles)),),
-                                  device=dev, dtype=torch.uint8)
+        self.bin_ws = torch.empty((int(nat.call("cs_bin_workspace_size", nt)),), device=dev,
+                                  dtype=torch.uint8)
+        self.loss_ws = torch.zeros((int(nat.call("cs_loss_workspace_size", nt)),), device=dev,
+                                   dtype=torch.uint8)
         self.out = torch.empty((self.h, self.w, 3), device=dev, dtype=f32)
         self.img_chw = torch.zeros((3, self.h, self.w), device=dev, dtype=f32)
         self.fts = torch.empty((self.h, self.w), device=dev, dtype=f32)
         self.fidx = torch.empty((self.h, self.w), device=dev, dtype=i32)
-        self.sse = torch.zeros((3,), device=dev, dtype=f32)
-        self.mse = torch.zeros((), device=dev, dtype=f32)
         n_total = 3 * self.h * self.w
         # d loss / d image = 2/N (image - target), in float32 like the reference
-        self.mse_scale = (torch.ones((1,), device=dev, dtype=f32) * (2.0 / float(n_total)))
-        self.mse_ws = torch.empty((int(nat.call("cs_mse_workspace_size", n_total)),), device=dev,
-                                  dtype=torch.uint8)
+        self.mse_scale = torch.ones((1,), device=dev, dtype=f32) * (2.0 / float(n_total))
         self.ssim_planes = torch.zeros((3,), device=dev, dtype=f32)
         self.gauss = _metric.gaussian_1d(11, 1.5, dev)
-        self.ssim_ws = torch.empty(
+        self.ssim_ws = torch.zeros(
             (int(nat.call("cs_ssim_workspace_size", 3, self.h, self.w, 11)),), device=dev,
             dtype=torch.uint8)
-
-        # raster scratch gradients: v_edges | v_opacity | v_inv_sigma2 (zeroed every step)
-        self.scratch = torch.zeros((e * 4 + 2 * p,), device=dev, dtype=f32)
-        self.v_edges = self.scratch[:e * 4].view(e, 2, 2)
-        self.v_opac = self.scratch[e * 4:e * 4 + p]
-        self.v_inv = self.scratch[e * 4 + p:]
-        self.v_cn = torch.empty((g, 4, 2), device=dev, dtype=f32)
-        self.v_cub = torch.empty((p, 4 * self.g_per_path, 2), device=dev, dtype=f32)
-        # parameter gradients live in one flat buffer: ring | colors | band SSE
-        n_ring = self.ring.numel()
-        self.flat_grad = torch.zeros((n_ring + 3 * p + 1,), device=dev, dtype=f32)
-        self.ring.grad = self.flat_grad[:n_ring].view_as(self.ring)
-        self.colors.grad = self.flat_grad[n_ring:n_ring + 3 * p].view(p, 3)
-        self.sse_slot = self.flat_grad[n_ring + 3 * p:]
-        self.ring.requires_grad_(True)
-        self.colors.requires_grad_(True)
-        self.opt = torch.optim.Adam([{"params": [self.ring], "lr": float(lr_points)},
-                                     {"params": [self.colors], "lr": float(lr_colors)}],
-                                    fused=True, capturable=True)
         if capacity is None:
             capacity = self.probe_capacity()
         self.capacity, self.dcapacity = (int(c) for c in capacity)
@@ -122,19 +126,16 @@ class FillTrainer:
         self.rowoff = torch.empty((self.capacity, 16), device=dev, dtype=i32)
         self.dlist = torch.empty((self.dcapacity, 8), device=dev, dtype=f32)
         self.graph: Optional[torch.cuda.CUDAGraph] = None
-        self.launches_per_step = 0
+        self.launches_per_step = 8 + (1 if self.with_ssim else 0)
 
     # ------------------------------------------------------------------
-    def _params_to_cubics(self):
-        with torch.no_grad():
-            torch.index_select(self.ring, 1, self.gidx, out=self.cub)
-            torch.div(self.cub.view(-1, 4, 2), self.half, out=self.cn)
-            self.cn.sub_(1.0)
+    def _params_to_cubics(self, st):
+        nat.check(nat.call("cs_ring_to_cubics", self.ring.data_ptr(), self.cn.data_ptr(),
+                           self.num_paths, self.g_per_path, self.h, self.w, st),
+                  "cs_ring_to_cubics")
 
-    def _bin(self, capacity: int, dcapacity: int):
-        st = nat.stream(self.device)
+    def _bin(self, capacity: int, dcapacity: int, st):
         r0, r1 = self.tile_rows
-        self.counters.zero_()
         nat.check(nat.call("cs_bin_count", self.cn.data_ptr(), self.offs.data_ptr(),
                            self.widths.data_ptr(), None, self.basis.data_ptr(),
                            self.cubics_px.data_ptr(), self.edges.data_ptr(),
@@ -147,8 +148,9 @@ class FillTrainer:
     def probe_capacity(self, slack: float = 1.5, extra: int = 4096) -> tuple[int, int]:
         """Intersect and staged-record capacities from one counting pass (one
         host sync, at set-up), with slack for the parameters to move."""
-        self._params_to_cubics()
-        self._bin(INT64_MAX, INT64_MAX)
+        st = nat.stream(self.device)
+        self._params_to_cubics(st)
+        self._bin(INT64_MAX, INT64_MAX, st)
         n, _, nd, _ = (int(v) for v in self.counters.tolist())
         return int(math.ceil(n * slack)) + extra, int(math.ceil(nd * slack)) + 16 * extra
 
@@ -156,9 +158,9 @@ class FillTrainer:
         """Enqueue one forward + loss + backward; no host synchronisation."""
         st = nat.stream(self.device)
         r0, r1 = self.tile_rows
-        self._params_to_cubics()
-        self._bin(self.capacity, self.dcapacity)
         status = self.counters.data_ptr() + 4
+        self._params_to_cubics(st)
+        self._bin(self.capacity, self.dcapacity, st)
         nat.check(nat.call("cs_bin_sort", self.prim_ranges.data_ptr(), self.depths.data_ptr(),
                            self.tile_bins.data_ptr(), self.prim_sorted.data_ptr(),
                            self.isect_sorted.data_ptr(), self.counters.data_ptr(),
@@ -172,59 +174,34 @@ class FillTrainer:
                            self.tile_bins.data_ptr(), self.tile_dlist.data_ptr(),
                            self.imeta.data_ptr(), self.rowoff.data_ptr(), self.dlist.data_ptr(),
                            self.bg.data_ptr(), self.out.data_ptr(), self.fts.data_ptr(),
-                           self.fidx.data_ptr(), self.img_chw.data_ptr(), status, self.h, self.w,
+                           self.fidx.data_ptr(), self.img_chw.data_ptr(), self.target.data_ptr(),
+                           self.loss.data_ptr(), self.loss_ws.data_ptr(), status, self.h, self.w,
                            r0, r1, st), "cs_fill_forward")
-        self._loss(st)
-        self.scratch.zero_()
-        self.flat_grad.zero_()
+        if self.with_ssim:
+            nat.check(nat.call("cs_ssim", self.img_chw.data_ptr(), self.target.data_ptr(),
+                               self.gauss.data_ptr(), 3, self.h, self.w, 11, 0.01 ** 2, 0.03 ** 2,
+                               self.ssim_planes.data_ptr(), None, self.ssim_ws.data_ptr(), st),
+                      "cs_ssim")
         nat.check(nat.call("cs_fill_backward", self.prim_sorted.data_ptr(),
                            self.tile_bins.data_ptr(), self.tile_dlist.data_ptr(),
                            self.imeta.data_ptr(), self.rowoff.data_ptr(), self.dlist.data_ptr(),
                            self.bg.data_ptr(), self.fts.data_ptr(), self.fidx.data_ptr(), None,
                            self.out.data_ptr(), self.target.data_ptr(),
                            self.mse_scale.data_ptr(), self.v_edges.data_ptr(),
-                           self.colors.grad.data_ptr(), self.v_opac.data_ptr(),
-                           self.v_inv.data_ptr(), None, None, status, self.h, self.w, r0, r1, st),
-                  "cs_fill_backward")
-        nat.check(nat.call("cs_edge_grads_to_cubics", self.v_edges.data_ptr(),
-                           self.v_cn.data_ptr(), self.num_segments, self.s - 1,
-                           0.5 * float(self.w), 0.5 * float(self.h), st),
-                  "cs_edge_grads_to_cubics")
-        with torch.no_grad():
-            # d/d ring of (gather(ring) / half - 1): scatter-add of grad / half
-            torch.div(self.v_cn.view(self.num_paths, -1, 2), self.half, out=self.v_cub)
-            self.ring.grad.index_add_(1, self.gidx, self.v_cub)
-            self.sse_slot.copy_(self.sse.sum().view(1))
-        self.launches_per_step = 9 + (2 if self.with_ssim else 0) + (
-            2 if self.tile_rows != (0, self.tby) else 0)
-
-    def _loss(self, st):
-        r0, r1 = self.tile_rows
-        hw = self.h * self.w
-        if self.tile_rows == (0, self.tby):
-            nat.check(nat.call("cs_mse_forward", self.img_chw.data_ptr(), self.target.data_ptr(),
-                               3 * hw, self.sse.data_ptr(), self.mse.data_ptr(),
-                               self.mse_ws.data_ptr(), st), "cs_mse_forward")
-            if self.with_ssim:
-                nat.check(nat.call("cs_ssim", self.img_chw.data_ptr(), self.target.data_ptr(),
-                                   self.gauss.data_ptr(), 3, self.h, self.w, 11, 0.01 ** 2,
-                                   0.03 ** 2, self.ssim_planes.data_ptr(), None,
-                                   self.ssim_ws.data_ptr(), st), "cs_ssim")
-        else:
-            # band: SSE of this rank's rows, one contiguous span per channel
-            y0, y1 = r0 * 16, min(self.h, r1 * 16)
-            n = (y1 - y0) * self.w
-            self.sse.zero_()
-            for c in range(3):
-                off = 4 * (c * hw + y0 * self.w)
-                nat.check(nat.call("cs_mse_forward", self.img_chw.data_ptr() + off,
-                                   self.target.data_ptr() + off, n, self.sse.data_ptr() + 4 * c,
-                                   None, self.mse_ws.data_ptr(), st), "cs_mse_forward")
+                           self.v_colors.data_ptr(), None, None, None, None, status, self.h,
+                           self.w, r0, r1, st), "cs_fill_backward")
+        nat.check(nat.call("cs_edge_grads_to_ring", self.v_edges.data_ptr(),
+                           self.v_ring.data_ptr(), self.num_paths, self.g_per_path, self.s - 1,
+                           self.h, self.w, 1, st), "cs_edge_grads_to_ring")
 
     def optimizer_step(self):
         if self.grad_hook is not None:
             self.grad_hook(self.flat_grad)
-        self.opt.step()
+        nat.check(nat.call("cs_adam_step", self.params.data_ptr(), self.flat_grad.data_ptr(),
+                           self.exp_avg.data_ptr(), self.exp_avg_sq.data_ptr(), self.n_params,
+                           self.n_ring, self.lr[0], self.lr[1], self.betas[0], self.betas[1],
+                           self.eps, self.step_count.data_ptr(), self.adam_ws.data_ptr(), 1,
+                           nat.stream(self.device)), "cs_adam_step")
 
     def step_eager(self):
         self.forward_backward()
@@ -251,12 +228,12 @@ class FillTrainer:
 
     # ------------------------------------------------------------------
     def check_status(self) -> tuple[int, int]:
-        """(intersect count of the last step, device status); syncs."""
+        """(intersect count of the last step, sticky device status); syncs."""
         n, status, _, _ = (int(v) for v in self.counters.tolist())
         return n, status
 
     def loss_value(self) -> float:
-        return float(self.mse)
+        return float(self.loss[1])
 
     def ssim_value(self) -> float:
         return float(self.ssim_planes.mean())

@@ -312,6 +312,38 @@ CS_API int cs_ssim(const float *x, const float *y, const float *gauss, int64_t p
             int32_t w, int32_t win, float c1, float c2, float *plane_means, float *ssim_map,
             void *workspace, void *stream);
 
+/* Largest planes * ceil((h-win+1)/32) * ceil((w-win+1)/32) that
+ * cs_ssim_noalloc accepts: e.g. 3 planes of up to about 4700 x 4700 pixels. */
+#define CS_SSIM_NOALLOC_MAX_PARTIALS 65536
+
+/* cs_ssim without a workspace argument, for callers that cannot hand the
+ * library device memory: a plain C host with no device allocator or memory
+ * pool of its own, or a host that has reserved its whole memory budget up
+ * front and must not call cudaMalloc/cudaFree (which also synchronise the
+ * device) once its loop runs.  This entry point has no counterpart in the
+ * reference; it computes exactly what cs_ssim computes, with the same
+ * arguments minus the workspace.
+ *
+ * Its scratch (a 256-byte completion ticket and
+ * CS_SSIM_NOALLOC_MAX_PARTIALS per-block partial sums, 256 KB + 256 B) is a
+ * fixed array in the library's device memory, one per GPU.  The first call on
+ * each device looks up that array's address (cudaGetSymbolAddress, with the
+ * calling thread's current device); make that first call on each device
+ * before any stream capture.  Every call clears the ticket with
+ * cudaMemsetAsync on `stream` before its launch, so nothing needs to be
+ * zeroed by the caller.  Nothing is allocated or freed, on the host or the
+ * device.
+ *
+ * Limits: planes * tiles above CS_SSIM_NOALLOC_MAX_PARTIALS returns
+ * CS_ERR_CAPACITY without launching; devices with ordinal >= 64 return
+ * CS_ERR_UNSUPPORTED.  Because the scratch is shared, two calls on the same
+ * device whose executions overlap (different streams with no ordering between
+ * them, or several host threads) race on it and give wrong results; order
+ * them on one stream, or use cs_ssim with a workspace per stream. */
+CS_API int cs_ssim_noalloc(const float *x, const float *y, const float *gauss, int64_t planes,
+            int32_t h, int32_t w, int32_t win, float c1, float c2, float *plane_means,
+            float *ssim_map, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

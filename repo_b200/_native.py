@@ -65,6 +65,8 @@ SIGNATURES = {
     "cs_mse_backward": (ctypes.c_int, [_P, _P, _P, _P, _I64, _P]),
     "cs_ssim_workspace_size": (_SZ, [_I64, _I32, _I32, _I32]),
     "cs_ssim": (ctypes.c_int, [_P, _P, _P, _I64, _I32, _I32, _I32, _F32, _F32, _P, _P, _P, _P]),
+    "cs_ssim_noalloc": (ctypes.c_int, [_P, _P, _P, _I64, _I32, _I32, _I32, _F32, _F32, _P, _P,
+                                       _P]),
 }
 
 _lock = threading.Lock()

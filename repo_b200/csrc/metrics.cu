@@ -10,6 +10,7 @@
 // into shared memory, then a vertical pass, instead of the reference's direct
 // 121-tap window (manbo/ops/metric.py:300-339).
 #include <algorithm>
+#include <atomic>
 
 #include "cs_common.cuh"
 
@@ -218,6 +219,13 @@ __global__ void __launch_bounds__(kSsimThreads) ssim_kernel(
   if (tid == 0) *ticket = 0u;
 }
 
+// Fixed scratch of cs_ssim_noalloc: one copy per device, loaded with the
+// module.  Bytes [0, 256) hold the completion ticket, the partial sums follow.
+constexpr int kNoAllocMaxDevices = 64;
+static __device__ __align__(256) unsigned char
+    g_ssim_noalloc_scratch[256 + sizeof(float) * CS_SSIM_NOALLOC_MAX_PARTIALS];
+static std::atomic<unsigned char*> g_ssim_noalloc_base[kNoAllocMaxDevices];
+
 inline int mse_blocks(long long n) {
   long long b = (n + kMseThreads * 8 - 1) / (kMseThreads * 8);
   return (int)std::max<long long>(1, std::min<long long>(b, kMseMaxBlocks));
@@ -278,6 +286,47 @@ int cs_ssim(const float* x, const float* y, const float* gauss, int64_t planes, 
   const int R = win - 1;
   unsigned int* ticket = static_cast<unsigned int*>(workspace);
   float* partials = reinterpret_cast<float*>(static_cast<char*>(workspace) + 256);
+  const float inv_count = 1.0f / ((float)(h - R) * (float)(w - R));
+  ssim_kernel<<<dim3(gx, gy, (unsigned)planes), kSsimThreads, 0, st>>>(
+      x, y, gauss, h, w, win, c1, c2, inv_count, ssim_map, partials, ticket, plane_means);
+  return launch_status();
+}
+
+int cs_ssim_noalloc(const float* x, const float* y, const float* gauss, int64_t planes,
+                    int32_t h, int32_t w, int32_t win, float c1, float c2, float* plane_means,
+                    float* ssim_map, void* stream) {
+  if (planes <= 0 || win <= 0 || win % 2 == 0 || h < win || w < win || !plane_means)
+    return CS_ERR_ARG;
+  if (win > kMaxWin || planes > 65535) return CS_ERR_UNSUPPORTED;
+  int gx, gy;
+  ssim_grid(h, w, win, gx, gy);
+  if (planes * (int64_t)gx * gy > CS_SSIM_NOALLOC_MAX_PARTIALS) return CS_ERR_CAPACITY;
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return CS_ERR_CUDA;
+  }
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return CS_ERR_UNSUPPORTED;
+  unsigned char* base = g_ssim_noalloc_base[dev].load(std::memory_order_acquire);
+  if (!base) {
+    // The symbol's address differs per device; it is resolved with `dev`
+    // current.  Two threads racing here store the same value.
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_ssim_noalloc_scratch) != cudaSuccess || !p) {
+      cudaGetLastError();
+      return CS_ERR_CUDA;
+    }
+    base = static_cast<unsigned char*>(p);
+    g_ssim_noalloc_base[dev].store(base, std::memory_order_release);
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  unsigned int* ticket = reinterpret_cast<unsigned int*>(base);
+  float* partials = reinterpret_cast<float*>(base + 256);
+  if (cudaMemsetAsync(ticket, 0, sizeof(unsigned int), st) != cudaSuccess) {
+    cudaGetLastError();
+    return CS_ERR_CUDA;
+  }
+  const int R = win - 1;
   const float inv_count = 1.0f / ((float)(h - R) * (float)(w - R));
   ssim_kernel<<<dim3(gx, gy, (unsigned)planes), kSsimThreads, 0, st>>>(
       x, y, gauss, h, w, win, c1, c2, inv_count, ssim_map, partials, ticket, plane_means);

@@ -105,6 +105,10 @@ CS_API int cs_isect_edge_ranges(const int32_t *prim_ids_sorted, const int32_t *p
  * CS_ERR_CAPACITY, so no later kernel reads past the caller's buffers.
  * Offsets that do not start at 0, end at num_segments and increase set
  * counters[1] to CS_ERR_ARG (the primitive is treated as empty).
+ * tile_order (may be NULL) [band tiles] receives the band's tiles, as indices
+ * from the band's first tile, heaviest first by an edge-slot and intersect
+ * count estimate; the raster entry points take it to dispatch long tiles
+ * before short ones.
  * With cs_bin_sort this replaces project (K3) + flatten + K4 + cumsum + K5 +
  * torch.sort + K6 of _CubicFillSplatFunction.forward, cubic_splatting.py:2815-2908.
  * Workspace: cs_bin_workspace_size(num_tiles). */
@@ -113,7 +117,7 @@ CS_API int cs_bin_count(const float *cubics_norm, const int32_t *prim_seg_offset
                  const float *aa_widths, const float *stroke_widths, const float *basis,
                  float *cubics_px, float *edges_px, int32_t *prim_tile_ranges,
                  int32_t *num_tiles_hit, int32_t *tile_bins, int32_t *tile_dlist,
-                 int32_t *counters, void *workspace, int64_t num_primitives,
+                 int32_t *tile_order, int32_t *counters, void *workspace, int64_t num_primitives,
                  int64_t num_segments, int64_t isect_capacity, int64_t dlist_capacity,
                  int32_t samples, int32_t img_height, int32_t img_width, int32_t tile_row_begin,
                  int32_t tile_row_end, float aabb_pad, int32_t aniso, void *stream);
@@ -170,14 +174,16 @@ CS_API int cs_tile_stage(const int32_t *prim_ids_sorted, const int32_t *tile_bin
  * tiles, loss_out[1] = that / (3 H W), reduced in a fixed order by the last
  * CTA (workspace loss_ws: cs_loss_workspace_size(num_tiles) bytes, zeroed
  * once).  Tile rows outside [tile_row_begin, tile_row_end) are not touched.
+ * tile_order (may be NULL): the dispatch order of cs_bin_count for the same
+ * band; it changes only which CTA renders which tile, never a result.
  * Replaces rasterize_cubic_fill_forward_kernel, cubic_splatting.py:918-1194,
  * and (with target_chw) mse_partial_sum_kernel + reduce_sum_partial_kernel,
  * manbo/ops/metric.py:18-163. */
 CS_API size_t cs_loss_workspace_size(int64_t num_tiles);
 CS_API int cs_fill_forward(const int32_t *prim_ids_sorted, const int32_t *tile_bins,
                     const int32_t *tile_dlist, const void *imeta, const int32_t *rowoff,
-                    const void *dlist, const float *background, float *out_img,
-                    float *final_Ts, int32_t *final_idx, float *out_chw_clamped,
+                    const void *dlist, const int32_t *tile_order, const float *background,
+                    float *out_img, float *final_Ts, int32_t *final_idx, float *out_chw_clamped,
                     const float *target_chw, float *loss_out, void *loss_ws, int32_t *status,
                     int32_t img_height, int32_t img_width, int32_t tile_row_begin,
                     int32_t tile_row_end, void *stream);
@@ -194,10 +200,10 @@ CS_API int cs_fill_forward(const int32_t *prim_ids_sorted, const int32_t *tile_b
  * Replaces rasterize_cubic_fill_backward_kernel, cubic_splatting.py:1197-1651. */
 CS_API int cs_fill_backward(const int32_t *prim_ids_sorted, const int32_t *tile_bins,
                      const int32_t *tile_dlist, const void *imeta, const int32_t *rowoff,
-                     const void *dlist, const float *background, const float *final_Ts,
-                     const int32_t *final_idx, const float *v_output, const float *out_img,
-                     const float *target_chw, const float *mse_scale, float *v_edges,
-                     float *v_colors, float *v_opacities, float *v_inv_sigma2s,
+                     const void *dlist, const int32_t *tile_order, const float *background,
+                     const float *final_Ts, const int32_t *final_idx, const float *v_output,
+                     const float *out_img, const float *target_chw, const float *mse_scale,
+                     float *v_edges, float *v_colors, float *v_opacities, float *v_inv_sigma2s,
                      float *curve_contrib_rgb, float *curve_isect_contrib, int32_t *status,
                      int32_t img_height, int32_t img_width, int32_t tile_row_begin,
                      int32_t tile_row_end, void *stream);
@@ -207,7 +213,8 @@ CS_API int cs_fill_backward(const int32_t *prim_ids_sorted, const int32_t *tile_
  * cubic_polyline_splatting.py:33-249. */
 CS_API int cs_stroke_forward(const int32_t *prim_ids_sorted, const int32_t *tile_bins,
                       const int32_t *tile_dlist, const void *imeta, const void *dlist,
-                      const float *background, float *out_img, float *final_Ts,
+                      const int32_t *tile_order, const float *background, float *out_img,
+                      float *final_Ts,
                       int32_t *final_idx, float *out_chw_clamped, const float *target_chw,
                       float *loss_out, void *loss_ws, int32_t *status, int32_t img_height,
                       int32_t img_width, int32_t tile_row_begin, int32_t tile_row_end,
@@ -218,7 +225,7 @@ CS_API int cs_stroke_forward(const int32_t *prim_ids_sorted, const int32_t *tile
  * cubic_polyline_splatting.py:252-660. */
 CS_API int cs_stroke_backward(const int32_t *prim_ids_sorted, const int32_t *tile_bins,
                        const int32_t *tile_dlist, const void *imeta, const void *dlist,
-                       const float *background, const float *final_Ts,
+                       const int32_t *tile_order, const float *background, const float *final_Ts,
                        const int32_t *final_idx, const float *v_output, const float *out_img,
                        const float *target_chw, const float *mse_scale, float *v_edges,
                        float *v_colors, float *v_opacities, float *v_stroke_widths,

@@ -323,18 +323,31 @@ __global__ void __launch_bounds__(256) bin_prep_kernel(
   }
 }
 
+// Work estimate of a tile for dispatch ordering: its edge slots (every edge
+// of every primitive on it) plus 8 per intersect, bucketed by bit length so
+// that bucket 0 holds the heaviest tiles.
+__device__ __forceinline__ int work_bucket(const int* counts, const int* ecounts, long long i) {
+  const unsigned est = (counts ? 8u * (unsigned)counts[i] : 0u) + (ecounts ? (unsigned)ecounts[i] : 0u);
+  return 31 - min(31, 32 - __clz(est));
+}
+
 // Exclusive scan of per-tile intersect counts into tile ranges [start, end)
 // and of per-tile edge-slot counts into staged-record ranges [base, bound);
 // one CTA of 1024.  Either input may be NULL.  If a total exceeds its
-// capacity every range is written empty and the status is set.
+// capacity every range is written empty and the status is set.  When `order`
+// is given it receives the band's tiles (indices relative to the band's first
+// tile) heaviest first, so that the raster kernels start the longest tiles
+// first and the light ones fill the tail.
 __global__ void __launch_bounds__(1024) bin_scan_kernel(const int* __restrict__ counts,
                                                         const int* __restrict__ ecounts,
                                                         int* __restrict__ bins,
                                                         int* __restrict__ dlr,
                                                         int* __restrict__ cursor,
                                                         int* __restrict__ counters, long long nt,
-                                                        long long icap, long long dcap) {
-  __shared__ int wa[32], wb[32];
+                                                        long long icap, long long dcap,
+                                                        int* __restrict__ order,
+                                                        long long band0, long long band_n) {
+  __shared__ int wa[32], wb[32], hist[32];
   __shared__ long long s_ta, s_tb;
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   const long long chunk = (nt + 1023) / 1024;
@@ -381,6 +394,20 @@ __global__ void __launch_bounds__(1024) bin_scan_kernel(const int* __restrict__ 
       rb += c;
     }
   }
+  if (!order) return;
+  // counting sort of the band's tiles by work bucket (order within a bucket
+  // is arbitrary; it affects only scheduling)
+  if (tid < 32) hist[tid] = 0;
+  __syncthreads();
+  for (long long t = tid; t < band_n; t += 1024) atomicAdd(&hist[work_bucket(counts, ecounts, band0 + t)], 1);
+  __syncthreads();
+  if (wid == 0) {
+    const int v = hist[lane];
+    hist[lane] = warp_incl_scan(v, lane) - v;
+  }
+  __syncthreads();
+  for (long long t = tid; t < band_n; t += 1024)
+    order[atomicAdd(&hist[work_bucket(counts, ecounts, band0 + t)], 1)] = (int)t;
 }
 
 // One warp per primitive: scatter (depth key << 32 | primitive id) into the
@@ -405,9 +432,9 @@ __global__ void __launch_bounds__(256) bin_scatter_kernel(
   }
 }
 
-constexpr int kSortThreads = 128;
+constexpr int kSortThreads = 256;   // one CTA per tile for the sort and the staging
 constexpr int kSortSmem = 4096;
-constexpr int kStageChunk = 1024;
+constexpr int kStageU = 2;          // edge slots per thread per staging round
 
 __device__ __forceinline__ void emit_sorted(unsigned long long v, long long tile, long long pos,
                                             int* __restrict__ pids, long long* __restrict__ ids) {
@@ -503,114 +530,158 @@ __device__ __forceinline__ void isect_edges(const StageIO& io, int k, int pid, i
   }
 }
 
+// Shared state of stage_tile for one chunk of up to kSortThreads intersects.
+struct StageShared {
+  int sstart[kSortThreads + 1];  // first edge slot of each intersect; [m] = slot total
+  int eb[kSortThreads];          // first edge of each intersect
+  float dthr[kSortThreads];      // culling distance of each intersect
+  int dstart[kSortThreads + 1];  // first near record of each intersect; [m] = chunk end
+  unsigned bal[kStageU][kSortThreads / 32];  // near ballots of the current round
+  int pre[kStageU][kSortThreads / 32];       // their exclusive prefix counts
+  int wsum[kSortThreads / 32];
+  int total;
+};
+
 // Classify the edges of intersects [rs, re) of one tile and write its staged
-// records (CTA of kSortThreads; see stage.cuh).  Intersects are processed in
-// chunks of kStageChunk: pass 1 counts near edges per intersect (one warp per
-// intersect) and writes the far-edge row offsets; a block scan gives every
-// intersect its record range; pass 2 writes the records in edge order.
+// records (CTA of kSortThreads; see stage.cuh), in one pass.  The intersects
+// are taken in chunks of kSortThreads, one per thread for their attributes;
+// the chunk's edges are laid out as consecutive slots (intersect-major, edge
+// order within), which every thread walks kStageU slots per round.  A near
+// edge's record position is the number of near slots before it (ballots and
+// a prefix over the round's warps), which keeps (intersect, edge) order, and
+// an intersect's first record is that count at its first slot.  Far edges
+// right of the tile add to the intersect's per-row winding accumulators in
+// shared memory (`rows`, kSortThreads x 32 ints: 16 winding sums, 16 counts).
 template <bool STROKE>
 __device__ void stage_tile(const StageIO& io, long long tile, int rs, int re, int dbase,
-                           int* s_cnt, int (*s_row)[32], int* s_wt) {
+                           StageShared& sh, int (*rows)[32]) {
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   constexpr int nw = kSortThreads / 32;
+  constexpr int kRound = kSortThreads * kStageU;
   const float bx0 = (float)((tile % io.tbx) * kTile) + 0.5f;
   const float by0 = (float)((tile / io.tbx) * kTile) + 0.5f;
   const unsigned lt = (1u << lane) - 1u;
-  int base = 0;
-  for (int c0 = rs; c0 < re; c0 += kStageChunk) {
-    const int m = min(kStageChunk, re - c0);
-    for (int i = wid; i < m; i += nw) {
-      const int k = c0 + i;
+  int near_base = 0;
+  for (int c0 = rs; c0 < re; c0 += kSortThreads) {
+    const int m = min(kSortThreads, re - c0);
+    // per intersect: attributes, edge range, slot count
+    IMeta im;
+    int ne = 0;
+    if (tid < m) {
+      const int k = c0 + tid;
       const int pid = io.pids[k];
       int eb, ee;
       isect_edges(io, k, pid, eb, ee);
-      IMeta im;
       intersect_attrs<STROKE>(pid, io.colors, io.opac, io.inv_s2, io.rules, io.sw, im);
-      if (!STROKE) s_row[wid][lane] = 0;
-      __syncwarp();
-      int cnt = 0;
-      for (int e0 = eb; e0 < ee; e0 += 32) {
-        const int e = e0 + lane;
-        bool near = false;
-        unsigned rows = 0u;
-        float4 E = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (e < ee) {
-          E = __ldg(io.edges + e);
-          near = edge_is_near(E, im.dthr, bx0, by0);
-          if (!STROKE && !near) rows = far_right_rows(E, bx0, by0);
+      ne = max(0, ee - eb);
+      sh.eb[tid] = eb;
+      sh.dthr[tid] = im.dthr;
+      if (!STROKE) {
+#pragma unroll
+        for (int r = 0; r < 32; ++r) rows[tid][r] = 0;
+      }
+    }
+    const int incl = warp_incl_scan(ne, lane);
+    if (lane == 31) sh.wsum[wid] = incl;
+    __syncthreads();
+    int wbase = 0, total = 0;
+#pragma unroll
+    for (int w2 = 0; w2 < nw; ++w2) {
+      const int v = sh.wsum[w2];
+      wbase += w2 < wid ? v : 0;
+      total += v;
+    }
+    if (tid < m) sh.sstart[tid] = wbase + incl - ne;
+    if (tid == 0) sh.sstart[m] = total;
+    __syncthreads();
+    for (int rb = 0; rb < total; rb += kRound) {
+      int kk[kStageU], ee_[kStageU];
+      float4 E[kStageU];
+#pragma unroll
+      for (int u = 0; u < kStageU; ++u) {
+        const int j = rb + u * kSortThreads + tid;
+        kk[u] = -1;
+        if (j < total) {
+          int lo = 0, hi = m;  // last intersect whose first slot is <= j
+          while (hi - lo > 1) {
+            const int mid = (lo + hi) >> 1;
+            if (sh.sstart[mid] <= j) lo = mid; else hi = mid;
+          }
+          kk[u] = lo;
+          ee_[u] = sh.eb[lo] + (j - sh.sstart[lo]);
         }
-        cnt += __popc(__ballot_sync(0xffffffffu, near));
-        if (!STROKE && rows) {
-          const int dir = (E.w - E.y) > 0.0f ? 1 : -1;
-          while (rows) {
-            const int r = __ffs(rows) - 1;
-            rows &= rows - 1u;
-            atomicAdd(&s_row[wid][r], dir);
-            atomicAdd(&s_row[wid][16 + r], 1);
+      }
+#pragma unroll
+      for (int u = 0; u < kStageU; ++u)
+        E[u] = kk[u] >= 0 ? __ldg(io.edges + ee_[u]) : make_float4(0.f, 0.f, 0.f, 0.f);
+      bool near[kStageU];
+      unsigned bal[kStageU];
+#pragma unroll
+      for (int u = 0; u < kStageU; ++u) {
+        near[u] = kk[u] >= 0 && edge_is_near(E[u], sh.dthr[kk[u]], bx0, by0);
+        bal[u] = __ballot_sync(0xffffffffu, near[u]);
+        if (lane == 0) sh.bal[u][wid] = bal[u];
+        if (!STROKE && kk[u] >= 0 && !near[u]) {
+          unsigned rr = far_right_rows(E[u], bx0, by0);
+          if (rr) {
+            const int dir = (E[u].w - E[u].y) > 0.0f ? 1 : -1;
+            while (rr) {
+              const int r = __ffs(rr) - 1;
+              rr &= rr - 1u;
+              atomicAdd(&rows[kk[u]][r], dir);
+              atomicAdd(&rows[kk[u]][16 + r], 1);
+            }
           }
         }
       }
-      if (!STROKE) {
-        __syncwarp();
-        if (lane < 16) io.rowoff[(long long)k * 16 + lane] = pack_row(s_row[wid][lane], s_row[wid][16 + lane]);
-        __syncwarp();
+      __syncthreads();
+      if (wid == 0) {  // exclusive prefix of the round's (u, warp) near counts
+        const int v = lane < kStageU * nw ? __popc(sh.bal[lane / nw][lane % nw]) : 0;
+        const int x = warp_incl_scan(v, lane);
+        if (lane < kStageU * nw) sh.pre[lane / nw][lane % nw] = x - v;
+        if (lane == 31) sh.total = x;
       }
-      if (lane == 0) s_cnt[i] = cnt;
-    }
-    __syncthreads();
-    // exclusive scan of s_cnt[0, m) in place
-    const int per = (m + kSortThreads - 1) / kSortThreads;
-    const int b0 = tid * per, b1 = min(m, b0 + per);
-    int local = 0;
-    for (int q = b0; q < b1; ++q) local += s_cnt[q];
-    const int incl = warp_incl_scan(local, lane);
-    if (lane == 31) s_wt[wid] = incl;
-    __syncthreads();
-    int run = incl - local;
-    for (int w2 = 0; w2 < wid; ++w2) run += s_wt[w2];
-    int total = 0;
-    for (int w2 = 0; w2 < nw; ++w2) total += s_wt[w2];
-    for (int q = b0; q < b1; ++q) {
-      const int c = s_cnt[q];
-      s_cnt[q] = run;
-      run += c;
-    }
-    __syncthreads();
-    for (int i = wid; i < m; i += nw) {
-      const int k = c0 + i;
-      const int pid = io.pids[k];
-      int eb, ee;
-      isect_edges(io, k, pid, eb, ee);
-      IMeta im;
-      intersect_attrs<STROKE>(pid, io.colors, io.opac, io.inv_s2, io.rules, io.sw, im);
-      const int dstart = base + s_cnt[i];
-      int pos = dstart;
-      for (int e0 = eb; e0 < ee; e0 += 32) {
-        const int e = e0 + lane;
-        bool near = false;
-        float4 E = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (e < ee) {
-          E = __ldg(io.edges + e);
-          near = edge_is_near(E, im.dthr, bx0, by0);
+      __syncthreads();
+#pragma unroll
+      for (int u = 0; u < kStageU; ++u) {
+        if (near[u]) {
+          const int pos = near_base + sh.pre[u][wid] + __popc(bal[u] & lt);
+          io.dl[dbase + pos] = make_entry(E[u], ee_[u]);
         }
-        const unsigned bal = __ballot_sync(0xffffffffu, near);
-        if (near) io.dl[dbase + pos + __popc(bal & lt)] = make_entry(E, e);
-        pos += __popc(bal);
       }
-      if (lane == 0) {
-        im.dstart = dstart;
-        im.dcount = pos - dstart;
-        int4* dst = reinterpret_cast<int4*>(io.imeta + k);
-        dst[0] = make_int4(im.dstart, im.dcount, im.pid, im.rule);
-        dst[1] = make_int4(__float_as_int(im.c0), __float_as_int(im.c1), __float_as_int(im.c2),
-                           __float_as_int(im.op));
-        dst[2] = make_int4(__float_as_int(im.a), __float_as_int(im.b), __float_as_int(im.dthr), 0);
+      if (tid < m) {
+        const int st = sh.sstart[tid] - rb;
+        if (st >= 0 && st < kRound && sh.sstart[tid] < total) {
+          const int u = st / kSortThreads, w2 = (st % kSortThreads) >> 5, l = st & 31;
+          sh.dstart[tid] = near_base + sh.pre[u][w2] + __popc(sh.bal[u][w2] & ((1u << l) - 1u));
+        }
+      }
+      near_base += sh.total;
+      __syncthreads();
+    }
+    // intersects with no slot left (empty, at the end of the chunk)
+    if (tid < m && sh.sstart[tid] >= total) sh.dstart[tid] = near_base;
+    if (tid == 0) sh.dstart[m] = near_base;
+    __syncthreads();
+    if (tid < m) {
+      const int k = c0 + tid;
+      im.dstart = sh.dstart[tid];
+      im.dcount = sh.dstart[tid + 1] - sh.dstart[tid];
+      int4* dst = reinterpret_cast<int4*>(io.imeta + k);
+      dst[0] = make_int4(im.dstart, im.dcount, im.pid, im.rule);
+      dst[1] = make_int4(__float_as_int(im.c0), __float_as_int(im.c1), __float_as_int(im.c2),
+                         __float_as_int(im.op));
+      dst[2] = make_int4(__float_as_int(im.a), __float_as_int(im.b), __float_as_int(im.dthr), 0);
+    }
+    if (!STROKE) {
+      for (int q = tid; q < m * 16; q += kSortThreads) {
+        const int t = q >> 4, r = q & 15;
+        io.rowoff[(long long)(c0 + t) * 16 + r] = pack_row(rows[t][r], rows[t][16 + r]);
       }
     }
-    base += total;
-    __syncthreads();
+    __syncthreads();  // shared state is reused by the next chunk
   }
-  if (tid == 0) io.dlr[tile].y = base;
+  if (tid == 0) io.dlr[tile].y = near_base;
 }
 
 // One CTA per tile: sort the tile's pairs and emit primitive ids and
@@ -621,10 +692,11 @@ __global__ void __launch_bounds__(kSortThreads) bin_tile_kernel(
     const int* __restrict__ bins, const float* __restrict__ depths,
     unsigned long long* __restrict__ pairs, int* __restrict__ pids, long long* __restrict__ ids,
     const int* __restrict__ counters, long long icap, long long dcap, int r0, StageIO io) {
-  __shared__ unsigned long long s[kSortSmem];
-  __shared__ int s_cnt[kStageChunk];
-  __shared__ int s_row[kSortThreads / 32][32];
-  __shared__ int s_wt[kSortThreads / 32];
+  // the sort buffer is reused for the staging row accumulators
+  static_assert(sizeof(unsigned long long) * kSortSmem >= sizeof(int) * kSortThreads * 32,
+                "row accumulators must fit the sort buffer");
+  __shared__ __align__(16) unsigned long long s[kSortSmem];
+  __shared__ StageShared sh;
   const long long tile = (long long)(r0 + blockIdx.y) * io.tbx + blockIdx.x;
   const int start = bins[2 * tile], end = bins[2 * tile + 1];
   const int n = end - start;
@@ -634,7 +706,8 @@ __global__ void __launch_bounds__(kSortThreads) bin_tile_kernel(
   if (!io.imeta) return;
   if (counters[2] > dcap) return;
   __syncthreads();
-  stage_tile<STROKE>(io, tile, start, end, io.dlr[tile].x, s_cnt, s_row, s_wt);
+  stage_tile<STROKE>(io, tile, start, end, io.dlr[tile].x, sh,
+                     reinterpret_cast<int (*)[32]>(s));
 }
 
 // Standalone staging for a reference-format intersect list: per-tile edge-slot
@@ -666,14 +739,13 @@ template <bool STROKE>
 __global__ void __launch_bounds__(kSortThreads) tile_stage_kernel(const int* __restrict__ bins,
                                                                   const int* __restrict__ counters,
                                                                   long long dcap, StageIO io) {
-  __shared__ int s_cnt[kStageChunk];
-  __shared__ int s_row[kSortThreads / 32][32];
-  __shared__ int s_wt[kSortThreads / 32];
+  __shared__ int s_row[STROKE ? 1 : kSortThreads][32];
+  __shared__ StageShared sh;
   const long long tile = (long long)blockIdx.y * io.tbx + blockIdx.x;
   const int rs = bins[2 * tile], re = bins[2 * tile + 1];
   if (re <= rs) return;
   if (counters[2] > dcap) return;
-  stage_tile<STROKE>(io, tile, rs, re, io.dlr[tile].x, s_cnt, s_row, s_wt);
+  stage_tile<STROKE>(io, tile, rs, re, io.dlr[tile].x, sh, s_row);
 }
 
 }  // namespace cs
@@ -759,7 +831,8 @@ size_t cs_bin_workspace_size(int64_t num_tiles) {
 int cs_bin_count(const float* cubics_norm, const int32_t* prim_seg_offsets, const float* aa_widths,
                  const float* stroke_widths, const float* basis, float* cubics_px,
                  float* edges_px, int32_t* prim_tile_ranges, int32_t* num_tiles_hit,
-                 int32_t* tile_bins, int32_t* tile_dlist, int32_t* counters, void* workspace,
+                 int32_t* tile_bins, int32_t* tile_dlist, int32_t* tile_order, int32_t* counters,
+                 void* workspace,
                  int64_t num_primitives, int64_t num_segments, int64_t isect_capacity,
                  int64_t dlist_capacity, int32_t samples, int32_t img_height, int32_t img_width,
                  int32_t tile_row_begin, int32_t tile_row_end, float aabb_pad, int32_t aniso,
@@ -782,7 +855,8 @@ int cs_bin_count(const float* cubics_norm, const int32_t* prim_seg_offsets, cons
   }
   bin_scan_kernel<<<1, 1024, 0, st>>>(ws.tile_counts, ws.tile_ecounts, tile_bins, tile_dlist,
                                       ws.cursor, counters, nt, (isect_capacity > 0 ? isect_capacity : 0),
-                                      (dlist_capacity > 0 ? dlist_capacity : 0));
+                                      (dlist_capacity > 0 ? dlist_capacity : 0), tile_order,
+                                      (long long)r0 * tbx, (long long)max(0, r1 - r0) * tbx);
   return launch_status();
 }
 
@@ -870,7 +944,8 @@ int cs_tile_stage(const int32_t* prim_ids_sorted, const int32_t* tile_bins, cons
       tile_bins, prim_ids_sorted, reinterpret_cast<const int2*>(isect_edge_ranges),
       prim_edge_offsets, ecounts, nt);
   bin_scan_kernel<<<1, 1024, 0, st>>>(nullptr, ecounts, nullptr, tile_dlist, nullptr, counters,
-                                      nt, 0, (dlist_capacity > 0 ? dlist_capacity : 0));
+                                      nt, 0, (dlist_capacity > 0 ? dlist_capacity : 0), nullptr, 0,
+                                      0);
   StageIO io = stage_io(prim_ids_sorted, edges_px, isect_edge_ranges, prim_edge_offsets, colors,
                         opacities, inv_sigma2s, fill_rules, stroke_widths, tile_dlist, imeta,
                         rowoff, dlist, tbx);

@@ -145,38 +145,52 @@ __global__ void ring_to_cubics_kernel(const float* __restrict__ ring, float* __r
 // (W/2, H/2) (the derivative of the normalisation), summed over the one or
 // two control points that share the ring point.  One CTA handles whole
 // paths; optionally v_edges is cleared after it is read.
-constexpr int kRingThreads = 128;
+constexpr int kRingThreads = 128;                                 // also the max segments per path
+constexpr int kRingEdgeLanes = 16;                                // lanes per segment
+constexpr int kRingSegsPerPass = kRingThreads / kRingEdgeLanes;  // segments per block pass
 
 __global__ void __launch_bounds__(kRingThreads) edge_grads_to_ring_kernel(
     float4* __restrict__ v_edges, float* __restrict__ v_ring, long long npaths, int G, int E,
     float half_w, float half_h, int clear) {
   __shared__ float cub[kRingThreads][9];
-  const int ppb = max(1, kRingThreads / G);
+  const int ppb = max(1, kRingSegsPerPass / G);
   const long long p0 = (long long)blockIdx.x * ppb;
   const int nseg = (int)min((long long)ppb * G, (npaths - p0) * G);
   const float inv_e = 1.0f / (float)E;
-  for (int t = threadIdx.x; t < nseg; t += kRingThreads) {
-    const long long sid = p0 * G + t;
+  // A half-warp per segment: lane `sub` takes edges sub, sub+16, ..., so the
+  // edge-gradient loads of a segment are in flight together; the 8 control
+  // point sums are then reduced across the half-warp.
+  const int sub = threadIdx.x & (kRingEdgeLanes - 1), hw = threadIdx.x / kRingEdgeLanes;
+  for (int s0 = 0; s0 < nseg; s0 += kRingSegsPerPass) {  // uniform trip count
+    const int t = s0 + hw;
     float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int e = 0; e < E; ++e) {
-      float t0 = (float)e * inv_e, t1 = (float)(e + 1) * inv_e;
-      float o0 = 1.0f - t0, o1 = 1.0f - t1;
-      float o0s = o0 * o0, o1s = o1 * o1, t0s = t0 * t0, t1s = t1 * t1;
-      float b0[4] = {o0s * o0, 3.0f * o0s * t0, 3.0f * o0 * t0s, t0s * t0};
-      float b1[4] = {o1s * o1, 3.0f * o1s * t1, 3.0f * o1 * t1s, t1s * t1};
-      float4* gp = v_edges + sid * E + e;
-      const float4 g = *gp;
-      if (clear) *gp = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (t < nseg) {
+      float4* gseg = v_edges + (p0 * G + t) * E;
+      for (int e = sub; e < E; e += kRingEdgeLanes) {
+        const float t0 = (float)e * inv_e, t1 = (float)(e + 1) * inv_e;
+        const float o0 = 1.0f - t0, o1 = 1.0f - t1;
+        const float o0s = o0 * o0, o1s = o1 * o1, t0s = t0 * t0, t1s = t1 * t1;
+        const float b0[4] = {o0s * o0, 3.0f * o0s * t0, 3.0f * o0 * t0s, t0s * t0};
+        const float b1[4] = {o1s * o1, 3.0f * o1s * t1, 3.0f * o1 * t1s, t1s * t1};
+        const float4 g = gseg[e];
+        if (clear) gseg[e] = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        a[2 * c] = a[2 * c] + g.x * b0[c] + g.z * b1[c];
-        a[2 * c + 1] = a[2 * c + 1] + g.y * b0[c] + g.w * b1[c];
+        for (int c = 0; c < 4; ++c) {
+          a[2 * c] = a[2 * c] + g.x * b0[c] + g.z * b1[c];
+          a[2 * c + 1] = a[2 * c + 1] + g.y * b0[c] + g.w * b1[c];
+        }
       }
     }
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      cub[t][2 * c] = (a[2 * c] * half_w) / half_w;
-      cub[t][2 * c + 1] = (a[2 * c + 1] * half_h) / half_h;
+    for (int off = kRingEdgeLanes / 2; off > 0; off >>= 1)
+#pragma unroll
+      for (int c = 0; c < 8; ++c) a[c] += __shfl_xor_sync(0xffffffffu, a[c], off);
+    if (sub == 0 && t < nseg) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        cub[t][2 * c] = (a[2 * c] * half_w) / half_w;
+        cub[t][2 * c + 1] = (a[2 * c + 1] * half_h) / half_h;
+      }
     }
   }
   __syncthreads();
@@ -291,7 +305,7 @@ int cs_edge_grads_to_ring(float* v_edges, float* v_ring, int64_t num_paths, int3
       edges_per_segment <= 0)
     return CS_ERR_ARG;
   if (num_paths == 0) return CS_OK;
-  const int ppb = max(1, kRingThreads / segs_per_path);
+  const int ppb = max(1, kRingSegsPerPass / segs_per_path);
   edge_grads_to_ring_kernel<<<ceil_div(num_paths, ppb), kRingThreads, 0, (cudaStream_t)stream>>>(
       reinterpret_cast<float4*>(v_edges), v_ring, num_paths, segs_per_path, edges_per_segment,
       0.5f * (float)img_width, 0.5f * (float)img_height, clear_edges);

@@ -93,97 +93,130 @@ __global__ void mse_backward_kernel(const float* __restrict__ lhs, const float* 
 // SSIM: one launch.  Each CTA computes a 32x32 block of the SSIM map of one
 // plane: the (32+R)^2 input window is loaded to shared memory, a horizontal
 // pass writes the five windowed moments (x, y, x^2, y^2, xy) for 32 output
-// columns, each thread producing 8 columns from one register window, then a
-// vertical pass produces 4 output rows per thread the same way.  Per-CTA SSIM
-// sums are reduced per plane by the last CTA to finish.
+// columns, each thread producing 8 columns of one input row, then a vertical
+// pass produces 4 output rows of one column per thread.  Both passes walk
+// their inputs once and scatter each into the outputs whose window covers it,
+// so every product is formed once and every sum still adds its taps in
+// window order.  The window size is a template parameter, so no tap is
+// predicated away.  Per-CTA SSIM sums are reduced per plane by the last CTA
+// to finish.
 
 constexpr int kSsimT = 32;         // output tile edge
 constexpr int kSsimThreads = 256;
 constexpr int kMaxWin = 15;
-constexpr int kMaxR = kMaxWin - 1;
-constexpr int kSsimIn = kSsimT + kMaxR;
 
-__global__ void __launch_bounds__(kSsimThreads) ssim_kernel(
+template <int WIN>
+__global__ void __launch_bounds__(kSsimThreads, 4) ssim_kernel(
     const float* __restrict__ x, const float* __restrict__ y, const float* __restrict__ gauss,
-    int h, int w, int win, float c1, float c2, float inv_count, float* __restrict__ ssim_map,
+    int h, int w, float c1, float c2, float inv_count, float* __restrict__ ssim_map,
     float* __restrict__ partials, unsigned int* __restrict__ ticket,
     float* __restrict__ plane_means) {
-  __shared__ float sx[kSsimIn][kSsimIn + 1];
-  __shared__ float sy[kSsimIn][kSsimIn + 1];
-  __shared__ float hs[5][kSsimIn][kSsimT + 1];
-  __shared__ float g[kMaxWin];
+  constexpr int R = WIN - 1;
+  constexpr int IN = kSsimT + R;  // even, so the pitch IN + 1 is odd
+  constexpr int LOADS = (IN * IN + kSsimThreads - 1) / kSsimThreads;
+  __shared__ float sx[IN][IN + 1];
+  __shared__ float sy[IN][IN + 1];
+  __shared__ float hs[5][IN][kSsimT + 1];
+  __shared__ float g[WIN];
   __shared__ float red[kSsimThreads / 32];
   __shared__ bool last;
-  const int R = win - 1;
-  const int in_n = kSsimT + R;
   const long long plane = blockIdx.z;
   const int oh = h - R, ow = w - R;
   const int ox0 = blockIdx.x * kSsimT, oy0 = blockIdx.y * kSsimT;
   const float* xp = x + plane * (long long)h * w;
   const float* yp = y + plane * (long long)h * w;
-  const int tid = threadIdx.x;
-  if (tid < win) g[tid] = gauss[tid];
-  for (int idx = tid; idx < in_n * in_n; idx += kSsimThreads) {
-    const int r = idx / in_n, c = idx - r * in_n;
-    const int gy = oy0 + r, gx = ox0 + c;
-    const bool ok = gy < h && gx < w;
-    sx[r][c] = ok ? __ldg(xp + (long long)gy * w + gx) : 0.0f;
-    sy[r][c] = ok ? __ldg(yp + (long long)gy * w + gx) : 0.0f;
-  }
-  __syncthreads();
-  // horizontal: item = (input row r, 8 output columns)
-  for (int item = tid; item < in_n * (kSsimT / 8); item += kSsimThreads) {
-    const int r = item >> 2, c0 = (item & 3) * 8;
-    float a[8 + kMaxR], b[8 + kMaxR];
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  if (tid < WIN) g[tid] = gauss[tid];
+  {
+    // all of a thread's loads are issued before any is stored, so the tile
+    // costs one memory round trip rather than one per element
+    float xa[LOADS], ya[LOADS];
 #pragma unroll
-    for (int q = 0; q < 8 + kMaxR; ++q) {
-      a[q] = q < 8 + R ? sx[r][c0 + q] : 0.0f;
-      b[q] = q < 8 + R ? sy[r][c0 + q] : 0.0f;
+    for (int i = 0; i < LOADS; ++i) {
+      const int idx = tid + i * kSsimThreads;
+      const int r = idx / IN, c = idx - r * IN;
+      const int gy = oy0 + r, gx = ox0 + c;
+      const bool ok = idx < IN * IN && gy < h && gx < w;
+      xa[i] = ok ? __ldg(xp + (long long)gy * w + gx) : 0.0f;
+      ya[i] = ok ? __ldg(yp + (long long)gy * w + gx) : 0.0f;
     }
 #pragma unroll
-    for (int o = 0; o < 8; ++o) {
-      float m1 = 0.f, m2 = 0.f, e11 = 0.f, e22 = 0.f, e12 = 0.f;
+    for (int i = 0; i < LOADS; ++i) {
+      const int idx = tid + i * kSsimThreads;
+      if (idx < IN * IN) {
+        const int r = idx / IN, c = idx - r * IN;
+        sx[r][c] = xa[i];
+        sy[r][c] = ya[i];
+      }
+    }
+  }
+  __syncthreads();
+  float gk[WIN];
 #pragma unroll
-      for (int k = 0; k < kMaxWin; ++k) {
-        if (k < win) {
-          const float gk = g[k], u = a[o + k], v = b[o + k];
-          m1 = __fmaf_rn(gk, u, m1);
-          m2 = __fmaf_rn(gk, v, m2);
-          e11 = __fmaf_rn(gk, u * u, e11);
-          e22 = __fmaf_rn(gk, v * v, e22);
-          e12 = __fmaf_rn(gk, u * v, e12);
+  for (int k = 0; k < WIN; ++k) gk[k] = g[k];
+  // horizontal: (input row r, output columns c0 .. c0+7).  Warps 0-3 take rows
+  // 0-31 of column group `wid` (lanes = rows: distinct banks); warps 4-5 take
+  // the remaining R rows of all four groups.
+  {
+    int r = lane, grp = wid;
+    bool active = wid < 4;
+    if (R > 0 && wid >= 4) {
+      const int j = tid - 128;
+      grp = j / (R > 0 ? R : 1);
+      r = 32 + (j - grp * (R > 0 ? R : 1));
+      active = j < 4 * R;
+    }
+    if (active) {
+      const int c0 = grp * 8;
+      float m1[8], m2[8], e11[8], e22[8], e12[8];
+#pragma unroll
+      for (int o = 0; o < 8; ++o) m1[o] = m2[o] = e11[o] = e22[o] = e12[o] = 0.0f;
+#pragma unroll
+      for (int q = 0; q < 8 + R; ++q) {
+        const float u = sx[r][c0 + q], v = sy[r][c0 + q];
+        const float uu = u * u, vv = v * v, uv = u * v;
+#pragma unroll
+        for (int o = 0; o < 8; ++o) {
+          const int k = q - o;
+          if (k >= 0 && k < WIN) {
+            m1[o] = __fmaf_rn(gk[k], u, m1[o]);
+            m2[o] = __fmaf_rn(gk[k], v, m2[o]);
+            e11[o] = __fmaf_rn(gk[k], uu, e11[o]);
+            e22[o] = __fmaf_rn(gk[k], vv, e22[o]);
+            e12[o] = __fmaf_rn(gk[k], uv, e12[o]);
+          }
         }
       }
-      hs[0][r][c0 + o] = m1;
-      hs[1][r][c0 + o] = m2;
-      hs[2][r][c0 + o] = e11;
-      hs[3][r][c0 + o] = e22;
-      hs[4][r][c0 + o] = e12;
+#pragma unroll
+      for (int o = 0; o < 8; ++o) {
+        hs[0][r][c0 + o] = m1[o];
+        hs[1][r][c0 + o] = m2[o];
+        hs[2][r][c0 + o] = e11[o];
+        hs[3][r][c0 + o] = e22[o];
+        hs[4][r][c0 + o] = e12[o];
+      }
     }
   }
   __syncthreads();
-  // vertical: item = (output column c, 4 output rows)
+  // vertical: (output column lane, output rows r0 .. r0+3)
   float local = 0.0f;
   {
-    const int c = tid & 31, r0 = (tid >> 5) * 4;
+    const int c = lane, r0 = wid * 4;
     float mom[4][5];
 #pragma unroll
-    for (int o = 0; o < 4; ++o)
-#pragma unroll
-      for (int q = 0; q < 5; ++q) mom[o][q] = 0.0f;
-#pragma unroll
     for (int q = 0; q < 5; ++q) {
-      float col[4 + kMaxR];
+      float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-      for (int t = 0; t < 4 + kMaxR; ++t) col[t] = t < 4 + R ? hs[q][r0 + t][c] : 0.0f;
+      for (int t = 0; t < 4 + R; ++t) {
+        const float val = hs[q][r0 + t][c];
 #pragma unroll
-      for (int o = 0; o < 4; ++o) {
-        float acc = 0.0f;
-#pragma unroll
-        for (int k = 0; k < kMaxWin; ++k)
-          if (k < win) acc = __fmaf_rn(g[k], col[o + k], acc);
-        mom[o][q] = acc;
+        for (int o = 0; o < 4; ++o) {
+          const int k = t - o;
+          if (k >= 0 && k < WIN) acc[o] = __fmaf_rn(gk[k], val, acc[o]);
+        }
       }
+#pragma unroll
+      for (int o = 0; o < 4; ++o) mom[o][q] = acc[o];
     }
 #pragma unroll
     for (int o = 0; o < 4; ++o) {
@@ -217,6 +250,31 @@ __global__ void __launch_bounds__(kSsimThreads) ssim_kernel(
     if (tid == 0) plane_means[pl] = t * inv_count;
   }
   if (tid == 0) *ticket = 0u;
+}
+
+// Launch the instance for an odd window size 1 <= win <= kMaxWin.
+inline void launch_ssim(int win, dim3 grid, cudaStream_t st, const float* x, const float* y,
+                        const float* gauss, int h, int w, float c1, float c2, float inv_count,
+                        float* ssim_map, float* partials, unsigned int* ticket,
+                        float* plane_means) {
+#define CS_SSIM_CASE(WIN)                                                                  \
+  case WIN:                                                                                \
+    ssim_kernel<WIN><<<grid, kSsimThreads, 0, st>>>(x, y, gauss, h, w, c1, c2, inv_count,  \
+                                                    ssim_map, partials, ticket, plane_means); \
+    break;
+  switch (win) {
+    CS_SSIM_CASE(1)
+    CS_SSIM_CASE(3)
+    CS_SSIM_CASE(5)
+    CS_SSIM_CASE(7)
+    CS_SSIM_CASE(9)
+    CS_SSIM_CASE(11)
+    CS_SSIM_CASE(13)
+    CS_SSIM_CASE(15)
+    default:
+      break;
+  }
+#undef CS_SSIM_CASE
 }
 
 // Fixed scratch of cs_ssim_noalloc: one copy per device, loaded with the
@@ -287,8 +345,8 @@ int cs_ssim(const float* x, const float* y, const float* gauss, int64_t planes, 
   unsigned int* ticket = static_cast<unsigned int*>(workspace);
   float* partials = reinterpret_cast<float*>(static_cast<char*>(workspace) + 256);
   const float inv_count = 1.0f / ((float)(h - R) * (float)(w - R));
-  ssim_kernel<<<dim3(gx, gy, (unsigned)planes), kSsimThreads, 0, st>>>(
-      x, y, gauss, h, w, win, c1, c2, inv_count, ssim_map, partials, ticket, plane_means);
+  launch_ssim(win, dim3(gx, gy, (unsigned)planes), st, x, y, gauss, h, w, c1, c2, inv_count,
+              ssim_map, partials, ticket, plane_means);
   return launch_status();
 }
 
@@ -328,8 +386,8 @@ int cs_ssim_noalloc(const float* x, const float* y, const float* gauss, int64_t 
   }
   const int R = win - 1;
   const float inv_count = 1.0f / ((float)(h - R) * (float)(w - R));
-  ssim_kernel<<<dim3(gx, gy, (unsigned)planes), kSsimThreads, 0, st>>>(
-      x, y, gauss, h, w, win, c1, c2, inv_count, ssim_map, partials, ticket, plane_means);
+  launch_ssim(win, dim3(gx, gy, (unsigned)planes), st, x, y, gauss, h, w, c1, c2, inv_count,
+              ssim_map, partials, ticket, plane_means);
   return launch_status();
 }
 

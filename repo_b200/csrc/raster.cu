@@ -47,6 +47,7 @@ struct RasterArgs {
   const int* rowoff;    // [I][16] packed row winding offsets (fill)
   const DEntry* dl;
   const float* bg;
+  const int* order;     // optional dispatch order: CTA b renders band tile order[b]
   int H, W, tbx, r0;
   int* status;
   // forward outputs
@@ -235,12 +236,27 @@ __device__ __forceinline__ void fwd_composite(FwdPix& p, const IMeta& m, int k) 
   if (nT <= kTransStop) p.done = true;
 }
 
+// The tile a CTA renders: band tile order[b] for linear block id b when an
+// order is given (heaviest tiles first), else the tile at the block's position.
+__device__ __forceinline__ void block_tile(const RasterArgs& A, int& tx, int& ty) {
+  if (A.order) {
+    const int t = __ldg(A.order + blockIdx.y * gridDim.x + blockIdx.x);
+    const int ry = t / A.tbx;
+    tx = t - ry * A.tbx;
+    ty = A.r0 + ry;
+  } else {
+    tx = blockIdx.x;
+    ty = A.r0 + blockIdx.y;
+  }
+}
+
 template <bool STROKE>
 __global__ void __launch_bounds__(kRT) raster_forward_kernel(const RasterArgs A) {
   __shared__ __align__(128) DEntry buf[2][kChunk];
   __shared__ __align__(8) uint64_t bars[2];
   const int tid = threadIdx.x, lane = tid & 31;
-  const int tx = blockIdx.x, ty = A.r0 + blockIdx.y;
+  int tx, ty;
+  block_tile(A, tx, ty);
   const long long tile = (long long)ty * A.tbx + tx;
   const int rs = A.bins[2 * tile], re = A.bins[2 * tile + 1];
   const int2 dr = A.dlr[tile];
@@ -344,7 +360,9 @@ __global__ void __launch_bounds__(kRT) raster_forward_kernel(const RasterArgs A)
       float bsum = 0.0f;
 #pragma unroll
       for (int w = 0; w < kRT / 32; ++w) bsum += red[w];
-      A.loss_partials[blockIdx.y * gridDim.x + blockIdx.x] = bsum;
+      // indexed by tile, so the fixed-order reduction does not depend on the
+      // dispatch order
+      A.loss_partials[(ty - A.r0) * A.tbx + tx] = bsum;
       __threadfence();
       last = atomicAdd(A.loss_ticket, 1u) == nblk - 1;
     }
@@ -500,7 +518,8 @@ __global__ void __launch_bounds__(kRT) raster_backward_kernel(const RasterArgs A
   __shared__ float pacc[kPaccCap][kAcc];
   __shared__ __align__(8) uint64_t bars[2];
   const int tid = threadIdx.x, lane = tid & 31;
-  const int tx = blockIdx.x, ty = A.r0 + blockIdx.y;
+  int tx, ty;
+  block_tile(A, tx, ty);
   const long long tile = (long long)ty * A.tbx + tx;
   const int rs = A.bins[2 * tile], re = A.bins[2 * tile + 1];
   if (re <= rs) return;
@@ -703,7 +722,9 @@ inline int launch_raster(bool stroke, bool bwd, const RasterArgs& a, int H, int 
 
 inline void stage_args(RasterArgs& a, const int32_t* prim_ids_sorted, const int32_t* tile_bins,
                        const int32_t* tile_dlist, const void* imeta, const int32_t* rowoff,
-                       const void* dlist, const float* background, int32_t* status) {
+                       const void* dlist, const int32_t* tile_order, const float* background,
+                       int32_t* status) {
+  a.order = tile_order;
   a.pids = prim_ids_sorted;
   a.bins = tile_bins;
   a.dlr = reinterpret_cast<const int2*>(tile_dlist);
@@ -722,7 +743,8 @@ extern "C" {
 
 static int raster_forward(bool stroke, const int32_t* prim_ids_sorted, const int32_t* tile_bins,
                           const int32_t* tile_dlist, const void* imeta, const int32_t* rowoff,
-                          const void* dlist, const float* background, float* out_img,
+                          const void* dlist, const int32_t* tile_order, const float* background,
+                          float* out_img,
                           float* final_Ts, int32_t* final_idx, float* out_chw_clamped,
                           const float* target_chw, float* loss_out, void* loss_ws,
                           int32_t* status, int32_t img_height, int32_t img_width,
@@ -732,7 +754,8 @@ static int raster_forward(bool stroke, const int32_t* prim_ids_sorted, const int
       (target_chw && (!loss_out || !loss_ws)))
     return CS_ERR_ARG;
   RasterArgs a{};
-  stage_args(a, prim_ids_sorted, tile_bins, tile_dlist, imeta, rowoff, dlist, background, status);
+  stage_args(a, prim_ids_sorted, tile_bins, tile_dlist, imeta, rowoff, dlist, tile_order, background,
+             status);
   a.out = out_img;
   a.fts = final_Ts;
   a.fidx = final_idx;
@@ -751,33 +774,36 @@ size_t cs_loss_workspace_size(int64_t num_tiles) {
 
 int cs_fill_forward(const int32_t* prim_ids_sorted, const int32_t* tile_bins,
                     const int32_t* tile_dlist, const void* imeta, const int32_t* rowoff,
-                    const void* dlist, const float* background, float* out_img, float* final_Ts,
+                    const void* dlist, const int32_t* tile_order, const float* background,
+                    float* out_img, float* final_Ts,
                     int32_t* final_idx, float* out_chw_clamped, const float* target_chw,
                     float* loss_out, void* loss_ws, int32_t* status, int32_t img_height,
                     int32_t img_width, int32_t tile_row_begin, int32_t tile_row_end,
                     void* stream) {
   return raster_forward(false, prim_ids_sorted, tile_bins, tile_dlist, imeta, rowoff, dlist,
-                        background, out_img, final_Ts, final_idx, out_chw_clamped, target_chw,
+                        tile_order, background, out_img, final_Ts, final_idx, out_chw_clamped, target_chw,
                         loss_out, loss_ws, status, img_height, img_width, tile_row_begin,
                         tile_row_end, stream);
 }
 
 int cs_stroke_forward(const int32_t* prim_ids_sorted, const int32_t* tile_bins,
                       const int32_t* tile_dlist, const void* imeta, const void* dlist,
-                      const float* background, float* out_img, float* final_Ts,
+                      const int32_t* tile_order, const float* background, float* out_img,
+                      float* final_Ts,
                       int32_t* final_idx, float* out_chw_clamped, const float* target_chw,
                       float* loss_out, void* loss_ws, int32_t* status, int32_t img_height,
                       int32_t img_width, int32_t tile_row_begin, int32_t tile_row_end,
                       void* stream) {
   return raster_forward(true, prim_ids_sorted, tile_bins, tile_dlist, imeta, nullptr, dlist,
-                        background, out_img, final_Ts, final_idx, out_chw_clamped, target_chw,
+                        tile_order, background, out_img, final_Ts, final_idx, out_chw_clamped, target_chw,
                         loss_out, loss_ws, status, img_height, img_width, tile_row_begin,
                         tile_row_end, stream);
 }
 
 static int raster_backward(bool stroke, const int32_t* prim_ids_sorted, const int32_t* tile_bins,
                            const int32_t* tile_dlist, const void* imeta, const int32_t* rowoff,
-                           const void* dlist, const float* background, const float* final_Ts,
+                           const void* dlist, const int32_t* tile_order, const float* background,
+                           const float* final_Ts,
                            const int32_t* final_idx, const float* v_output, const float* out_img,
                            const float* target_chw, const float* mse_scale, float* v_edges,
                            float* v_colors, float* v_opacities, float* v_stroke_widths,
@@ -791,7 +817,8 @@ static int raster_backward(bool stroke, const int32_t* prim_ids_sorted, const in
     return CS_ERR_ARG;
   if (!v_output && (!out_img || !target_chw || !mse_scale)) return CS_ERR_ARG;
   RasterArgs a{};
-  stage_args(a, prim_ids_sorted, tile_bins, tile_dlist, imeta, rowoff, dlist, background, status);
+  stage_args(a, prim_ids_sorted, tile_bins, tile_dlist, imeta, rowoff, dlist, tile_order, background,
+             status);
   a.fts_in = final_Ts;
   a.fidx_in = final_idx;
   a.v_out = v_output;
@@ -811,7 +838,8 @@ static int raster_backward(bool stroke, const int32_t* prim_ids_sorted, const in
 
 int cs_fill_backward(const int32_t* prim_ids_sorted, const int32_t* tile_bins,
                      const int32_t* tile_dlist, const void* imeta, const int32_t* rowoff,
-                     const void* dlist, const float* background, const float* final_Ts,
+                     const void* dlist, const int32_t* tile_order, const float* background,
+                     const float* final_Ts,
                      const int32_t* final_idx, const float* v_output, const float* out_img,
                      const float* target_chw, const float* mse_scale, float* v_edges,
                      float* v_colors, float* v_opacities, float* v_inv_sigma2s,
@@ -819,7 +847,7 @@ int cs_fill_backward(const int32_t* prim_ids_sorted, const int32_t* tile_bins,
                      int32_t img_height, int32_t img_width, int32_t tile_row_begin,
                      int32_t tile_row_end, void* stream) {
   return raster_backward(false, prim_ids_sorted, tile_bins, tile_dlist, imeta, rowoff, dlist,
-                         background, final_Ts, final_idx, v_output, out_img, target_chw,
+                         tile_order, background, final_Ts, final_idx, v_output, out_img, target_chw,
                          mse_scale, v_edges, v_colors, v_opacities, nullptr, v_inv_sigma2s,
                          curve_contrib_rgb, curve_isect_contrib, status, img_height, img_width,
                          tile_row_begin, tile_row_end, stream);
@@ -827,7 +855,8 @@ int cs_fill_backward(const int32_t* prim_ids_sorted, const int32_t* tile_bins,
 
 int cs_stroke_backward(const int32_t* prim_ids_sorted, const int32_t* tile_bins,
                        const int32_t* tile_dlist, const void* imeta, const void* dlist,
-                       const float* background, const float* final_Ts, const int32_t* final_idx,
+                       const int32_t* tile_order, const float* background, const float* final_Ts,
+                       const int32_t* final_idx,
                        const float* v_output, const float* out_img, const float* target_chw,
                        const float* mse_scale, float* v_edges, float* v_colors,
                        float* v_opacities, float* v_stroke_widths, float* v_inv_sigma2s,
@@ -835,7 +864,7 @@ int cs_stroke_backward(const int32_t* prim_ids_sorted, const int32_t* tile_bins,
                        int32_t img_height, int32_t img_width, int32_t tile_row_begin,
                        int32_t tile_row_end, void* stream) {
   return raster_backward(true, prim_ids_sorted, tile_bins, tile_dlist, imeta, nullptr, dlist,
-                         background, final_Ts, final_idx, v_output, out_img, target_chw,
+                         tile_order, background, final_Ts, final_idx, v_output, out_img, target_chw,
                          mse_scale, v_edges, v_colors, v_opacities, v_stroke_widths,
                          v_inv_sigma2s, curve_contrib_rgb, curve_isect_contrib, status,
                          img_height, img_width, tile_row_begin, tile_row_end, stream);

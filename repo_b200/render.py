@@ -125,6 +125,7 @@ class Binning:
     dlist: torch.Tensor
     counters: torch.Tensor
     stroke: bool
+    tile_order: Optional[torch.Tensor] = None  # heaviest-first dispatch order of the band
 
 
 def _offsets_error(offs: torch.Tensor, num_segments: int) -> ValueError:
@@ -164,6 +165,7 @@ def bin_primitives(cubics_norm: torch.Tensor, offs: torch.Tensor, depths: torch.
     tile_bins = torch.empty((nt, 2), dtype=torch.int32, device=dev)
     tile_dlist = torch.empty((nt, 2), dtype=torch.int32, device=dev)
     counters = torch.zeros((4,), dtype=torch.int32, device=dev)
+    tile_order = torch.empty((max(0, r1 - r0) * tbx,), dtype=torch.int32, device=dev)
     ws = torch.empty((int(nat.call("cs_bin_workspace_size", nt)),), dtype=torch.uint8, device=dev)
     st = nat.stream(dev)
     cn = _f32(cubics_norm)
@@ -173,7 +175,8 @@ def bin_primitives(cubics_norm: torch.Tensor, offs: torch.Tensor, depths: torch.
     nat.check(nat.call("cs_bin_count", nat.ptr(cn), nat.ptr(offs), nat.ptr(aw), nat.ptr(sw),
                        nat.ptr(basis), nat.ptr(cubics_px), nat.ptr(edges), nat.ptr(prim_ranges),
                        nat.ptr(num_hit), nat.ptr(tile_bins), nat.ptr(tile_dlist),
-                       nat.ptr(counters), ws.data_ptr(), p, g, INT64_MAX, INT64_MAX, s,
+                       nat.ptr(tile_order), nat.ptr(counters), ws.data_ptr(), p, g, INT64_MAX,
+                       INT64_MAX, s,
                        int(img_h), int(img_w), r0, r1, float(aabb_pad), int(bool(aniso)), st),
               "cs_bin_count")
     # the one host synchronisation of the forward: sizes + status
@@ -197,7 +200,7 @@ def bin_primitives(cubics_norm: torch.Tensor, offs: torch.Tensor, depths: torch.
                            nat.ptr(dlist), max(n_dbound, 1), st), "cs_bin_sort")
     return Binning(cubics_px, edges, edge_offs, prim_ranges, num_hit, tile_bins, prim_sorted,
                    isect_sorted, n_isect, (tbx, tby, 1), s, (r0, r1), tile_dlist, imeta, rowoff,
-                   dlist, counters, stroke)
+                   dlist, counters, stroke, tile_order)
 
 
 def stage_reference_lists(prim_ids_sorted, tile_bins, edges_px, isect_edge_ranges, colors,
@@ -270,13 +273,15 @@ def forward_raster(b: Binning, background, img_h: int, img_w: int, out_chw=None,
     if not b.stroke:
         nat.check(nat.call("cs_fill_forward", nat.ptr(b.prim_ids_sorted), nat.ptr(b.tile_bins),
                            nat.ptr(b.tile_dlist), nat.ptr(b.imeta), nat.ptr(b.rowoff),
-                           nat.ptr(b.dlist), nat.ptr(background), nat.ptr(out), nat.ptr(fts),
+                           nat.ptr(b.dlist), nat.ptr(b.tile_order), nat.ptr(background),
+                           nat.ptr(out), nat.ptr(fts),
                            nat.ptr(fidx), nat.ptr(out_chw), None, None, None, nat.ptr(status),
                            img_h, img_w, b.tile_rows[0], b.tile_rows[1], st), "cs_fill_forward")
     else:
         nat.check(nat.call("cs_stroke_forward", nat.ptr(b.prim_ids_sorted), nat.ptr(b.tile_bins),
                            nat.ptr(b.tile_dlist), nat.ptr(b.imeta), nat.ptr(b.dlist),
-                           nat.ptr(background), nat.ptr(out), nat.ptr(fts), nat.ptr(fidx),
+                           nat.ptr(b.tile_order), nat.ptr(background), nat.ptr(out),
+                           nat.ptr(fts), nat.ptr(fidx),
                            nat.ptr(out_chw), None, None, None, nat.ptr(status), img_h, img_w,
                            b.tile_rows[0], b.tile_rows[1], st), "cs_stroke_forward")
     return out, fts, fidx
@@ -318,7 +323,8 @@ def raster_backward(b: Binning, num_primitives: int, background, final_ts, final
         if not b.stroke:
             nat.check(nat.call("cs_fill_backward", nat.ptr(b.prim_ids_sorted), nat.ptr(b.tile_bins),
                                nat.ptr(b.tile_dlist), nat.ptr(b.imeta), nat.ptr(b.rowoff),
-                               nat.ptr(b.dlist), nat.ptr(background), nat.ptr(final_ts),
+                               nat.ptr(b.dlist), nat.ptr(b.tile_order), nat.ptr(background),
+                               nat.ptr(final_ts),
                                nat.ptr(final_idx), nat.ptr(vo), nat.ptr(out_img),
                                nat.ptr(target_chw), nat.ptr(mse_scale), nat.ptr(v_edges),
                                nat.ptr(v_colors), nat.ptr(v_opac), nat.ptr(v_inv),
@@ -327,7 +333,8 @@ def raster_backward(b: Binning, num_primitives: int, background, final_ts, final
         else:
             nat.check(nat.call("cs_stroke_backward", nat.ptr(b.prim_ids_sorted),
                                nat.ptr(b.tile_bins), nat.ptr(b.tile_dlist), nat.ptr(b.imeta),
-                               nat.ptr(b.dlist), nat.ptr(background), nat.ptr(final_ts),
+                               nat.ptr(b.dlist), nat.ptr(b.tile_order), nat.ptr(background),
+                               nat.ptr(final_ts),
                                nat.ptr(final_idx), nat.ptr(vo), nat.ptr(out_img),
                                nat.ptr(target_chw), nat.ptr(mse_scale), nat.ptr(v_edges),
                                nat.ptr(v_colors), nat.ptr(v_opac), nat.ptr(v_sw), nat.ptr(v_inv),

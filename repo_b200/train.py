@@ -99,6 +99,8 @@ class FillTrainer:
         self.num_hit = torch.empty((p,), device=dev, dtype=i32)
         self.tile_bins = torch.empty((nt, 2), device=dev, dtype=i32)
         self.tile_dlist = torch.empty((nt, 2), device=dev, dtype=i32)
+        self.tile_order = torch.empty((max(1, (self.tile_rows[1] - self.tile_rows[0]) * tbx),),
+                                      device=dev, dtype=i32)
         # intersects, sticky status, staged-record bound, unused
         self.counters = torch.zeros((4,), device=dev, dtype=i32)
         self.bin_ws = torch.empty((int(nat.call("cs_bin_workspace_size", nt)),), device=dev,
@@ -141,7 +143,8 @@ class FillTrainer:
                            self.cubics_px.data_ptr(), self.edges.data_ptr(),
                            self.prim_ranges.data_ptr(), self.num_hit.data_ptr(),
                            self.tile_bins.data_ptr(), self.tile_dlist.data_ptr(),
-                           self.counters.data_ptr(), self.bin_ws.data_ptr(), self.num_paths,
+                           self.tile_order.data_ptr(), self.counters.data_ptr(),
+                           self.bin_ws.data_ptr(), self.num_paths,
                            self.num_segments, capacity, dcapacity, self.s, self.h, self.w, r0, r1,
                            float(_render.DEFAULT_AABB_PAD), 0, st), "cs_bin_count")
 
@@ -173,7 +176,8 @@ class FillTrainer:
         nat.check(nat.call("cs_fill_forward", self.prim_sorted.data_ptr(),
                            self.tile_bins.data_ptr(), self.tile_dlist.data_ptr(),
                            self.imeta.data_ptr(), self.rowoff.data_ptr(), self.dlist.data_ptr(),
-                           self.bg.data_ptr(), self.out.data_ptr(), self.fts.data_ptr(),
+                           self.tile_order.data_ptr(), self.bg.data_ptr(), self.out.data_ptr(),
+                           self.fts.data_ptr(),
                            self.fidx.data_ptr(), self.img_chw.data_ptr(), self.target.data_ptr(),
                            self.loss.data_ptr(), self.loss_ws.data_ptr(), status, self.h, self.w,
                            r0, r1, st), "cs_fill_forward")
@@ -185,7 +189,8 @@ class FillTrainer:
         nat.check(nat.call("cs_fill_backward", self.prim_sorted.data_ptr(),
                            self.tile_bins.data_ptr(), self.tile_dlist.data_ptr(),
                            self.imeta.data_ptr(), self.rowoff.data_ptr(), self.dlist.data_ptr(),
-                           self.bg.data_ptr(), self.fts.data_ptr(), self.fidx.data_ptr(), None,
+                           self.tile_order.data_ptr(), self.bg.data_ptr(), self.fts.data_ptr(),
+                           self.fidx.data_ptr(), None,
                            self.out.data_ptr(), self.target.data_ptr(),
                            self.mse_scale.data_ptr(), self.v_edges.data_ptr(),
                            self.v_colors.data_ptr(), None, None, None, None, status, self.h,

@@ -416,6 +416,37 @@ def test_tile_row_bands_stitch_to_full_image():
     assert torch.equal(stitched, full)
 
 
+@pytest.mark.parametrize("rows", [None, (2, 9)])
+def test_tile_order_is_heaviest_first_permutation_and_changes_no_result(rows):
+    import dataclasses
+    sc = scenes.config1()
+    args = fill_inputs(sc)
+    h, w = args[5], args[6]
+    b, inv, out, fts, fidx = gpu_fill(*args, tile_rows=rows)
+    tbx = (w + 15) // 16
+    r0, r1 = b.tile_rows
+    order = _np(b.tile_order)
+    assert sorted(order.tolist()) == list(range((r1 - r0) * tbx))
+    # work estimate of every band tile: 8 per intersect + its primitives' edges
+    bins = _np(b.tile_bins)[r0 * tbx:r1 * tbx]
+    eoffs = _np(b.prim_edge_offsets).astype(np.int64)
+    ne = (eoffs[1:] - eoffs[:-1])[_np(b.prim_ids_sorted)]
+    cum = np.concatenate([[0], np.cumsum(ne)])
+    est = 8 * (bins[:, 1] - bins[:, 0]) + (cum[bins[:, 1]] - cum[bins[:, 0]])
+    bucket = np.array([int(v).bit_length() for v in est[order]])
+    assert np.all(np.diff(bucket) <= 0), "tiles are dispatched by decreasing work bucket"
+    plain = dataclasses.replace(b, tile_order=None)
+    out2, fts2, fidx2 = render.forward_raster(plain, _t(args[7], torch.float32), h, w)
+    band = slice(r0 * 16, min(h, r1 * 16))  # rows outside the band are not written
+    assert torch.equal(out[band], out2[band]) and torch.equal(fts[band], fts2[band])
+    assert torch.equal(fidx[band], fidx2[band])
+    v_out = np.asarray(scenes.seeded_grad(5, h, w), np.float32)
+    g1 = gpu_fill_backward(b, args[2], args[3], inv, args[8], args[7], fts, fidx, v_out, h, w)
+    g2 = gpu_fill_backward(plain, args[2], args[3], inv, args[8], args[7], fts, fidx, v_out, h, w)
+    for k in g1:
+        assert_grad_close(g1[k], g2[k], k)
+
+
 def test_image_size_not_multiple_of_tile():
     sc = scenes.small_fill_scene(77, h=45, w=61, paths=7)
     args = fill_inputs(sc)

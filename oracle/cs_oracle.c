@@ -300,6 +300,24 @@ void cso_tile_bins(int64_t n, const int64_t *ids_sorted, int num_tiles, int32_t 
 /* ------------------------------------------------------------------------ */
 /* per-pixel geometry shared by the fill forward and backward restatements   */
 
+/* Squared distance from the pixel centre (px, py) to edge (x0, y0) + t (vx, vy),
+   t in [0, 1]: the reference's proj = (w . v) / max(|v|^2, eps) clamped to
+   [0, 1], closest point c = p0 + proj v, d2 = |c - p|^2
+   (cubic_splatting.py:1095-1110, :1451-1470).  The dot product, the closest
+   point and the squared length are each evaluated with one fused
+   multiply-add (fmaf), as the B200 kernels do. */
+static inline float edge_d2(float x0, float y0, float vx, float vy, float inv_vv, float px, float py,
+                            float *proj, float *cx, float *cy) {
+    float wx = px - x0, wy = py - y0;
+    float pr = fmaf(wx, vx, wy * vy) * inv_vv;
+    pr = fmaxf_(0.0f, fminf_(1.0f, pr));
+    *cx = fmaf(pr, vx, x0);
+    *cy = fmaf(pr, vy, y0);
+    float dx = *cx - px, dy = *cy - py;
+    *proj = pr;
+    return fmaf(dx, dx, dy * dy);
+}
+
 typedef struct {
     float min_d2, best_proj, best_cx, best_cy;
     int best_eid, parity, winding;
@@ -319,12 +337,8 @@ static inline void fill_pixel_geom(const float *edges, int e0, int e1, float px,
         float vx = x1 - x0, vy = y1 - y0;
         float vv = vx * vx + vy * vy;
         float inv_vv = 1.0f / fmaxf_(vv, EPS_F);
-        float wx = px - x0, wy = py - y0;
-        float proj = (wx * vx + wy * vy) * inv_vv;
-        proj = fmaxf_(0.0f, fminf_(1.0f, proj));
-        float cx = x0 + proj * vx, cy = y0 + proj * vy;
-        float dx = cx - px, dy = cy - py;
-        float d2 = dx * dx + dy * dy;
+        float proj, cx, cy;
+        float d2 = edge_d2(x0, y0, vx, vy, inv_vv, px, py, &proj, &cx, &cy);
         if (d2 < g->min_d2) {
             g->min_d2 = d2; g->best_eid = e; g->best_proj = proj; g->best_cx = cx; g->best_cy = cy;
         }
@@ -584,12 +598,8 @@ static inline float stroke_min_d2(const float *edges, int e0, int e1, float px, 
         float vx = x1 - x0, vy = y1 - y0;
         float vv = vx * vx + vy * vy;
         float inv_vv = 1.0f / fmaxf_(vv, EPS_F);
-        float wx = px - x0, wy = py - y0;
-        float proj = (wx * vx + wy * vy) * inv_vv;
-        proj = fmaxf_(0.0f, fminf_(1.0f, proj));
-        float cx = x0 + proj * vx, cy = y0 + proj * vy;
-        float dx = cx - px, dy = cy - py;
-        float d2 = dx * dx + dy * dy;
+        float proj, cx, cy;
+        float d2 = edge_d2(x0, y0, vx, vy, inv_vv, px, py, &proj, &cx, &cy);
         if (d2 < min_d2) {
             min_d2 = d2; *best_eid = e; *best_proj = proj; *best_cx = cx; *best_cy = cy;
         }

@@ -136,16 +136,20 @@ __device__ __forceinline__ bool wait_chunk(uint64_t* bar, uint32_t parity, int* 
 // ---------------------------------------------------------------------------
 // per-pixel arithmetic (reference formulas, written order)
 
+// Squared distance to the edge of record (A, B): proj = (w . v) / |v|^2
+// clamped to [0, 1], closest point c = p0 + proj v, d2 = |c - p|^2, with one
+// fused multiply-add each for the dot product, the closest point and the
+// squared length (the CPU oracle evaluates the same expressions).
 __device__ __forceinline__ float seg_d2(float px, float py, float wy, const float4& A,
                                         const float4& B, float& proj, float& cx, float& cy) {
   const float wx = px - A.x;
-  float pr = (wx * A.z + wy * A.w) * B.x;
+  float pr = __fmaf_rn(wx, A.z, wy * A.w) * B.x;
   pr = fmaxf(0.0f, fminf(1.0f, pr));
-  cx = A.x + pr * A.z;
-  cy = A.y + pr * A.w;
+  cx = __fmaf_rn(pr, A.z, A.x);
+  cy = __fmaf_rn(pr, A.w, A.y);
   const float dx = cx - px, dy = cy - py;
   proj = pr;
-  return dx * dx + dy * dy;
+  return __fmaf_rn(dx, dx, dy * dy);
 }
 
 __device__ __forceinline__ float fill_coverage(float md, int w, int n, int rule, float inv_sigma,
@@ -397,25 +401,33 @@ struct BwdPix {
   int be, bl, w, n;  // bl: staged record of the closest edge in the current chunk, or -1
 };
 
-template <bool STROKE>
+// Closest record of the intersect so far and the crossing counts.  Records of
+// an intersect lie in edge order, so while they are visited in order a strict
+// < keeps the reference's first minimum.  An intersect whose records span
+// staging chunks is visited chunk by chunk from the top; in every chunk after
+// the first (TIES) an equal distance goes to the lower edge id explicitly.
+// Only the distance and the record index are tracked here; the closest point
+// of the winner is recomputed once per intersect (best_point).
+template <bool STROKE, bool TIES>
 __device__ __forceinline__ void bwd_entries(const DEntry* __restrict__ buf, int c0, int lo, int hi,
                                             const float px[2], float py, BwdPix s[2]) {
   for (int d = lo; d < hi; ++d) {
     const float4 EA = buf[d - c0].a;
     const float4 EB = buf[d - c0].b;
-    const int eid = __float_as_int(EB.w);
     const float wy = py - EA.y;
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
       float pr, cx, cy;
       const float d2 = seg_d2(px[u], py, wy, EA, EB, pr, cx, cy);
-      if (d2 < s[u].md || (d2 == s[u].md && eid < s[u].be)) {
+      bool take = d2 < s[u].md;
+      if (TIES) {
+        const int eid = __float_as_int(EB.w);
+        take = take || (d2 == s[u].md && eid < s[u].be);
+        if (take) s[u].be = eid;
+      }
+      if (take) {
         s[u].md = d2;
-        s[u].be = eid;
         s[u].bl = d;
-        s[u].bp = pr;
-        s[u].bcx = cx;
-        s[u].bcy = cy;
       }
     }
     if (!STROKE) {
@@ -433,6 +445,16 @@ __device__ __forceinline__ void bwd_entries(const DEntry* __restrict__ buf, int 
       }
     }
   }
+}
+
+// Projection, closest point and edge id of the pixel's closest record, which
+// must be resident in the current chunk (bl >= 0).
+__device__ __forceinline__ void best_point(const DEntry* __restrict__ buf, int c0, float px,
+                                           float py, BwdPix& s) {
+  const float4 EA = buf[s.bl - c0].a;
+  const float4 EB = buf[s.bl - c0].b;
+  s.be = __float_as_int(EB.w);
+  seg_d2(px, py, py - EA.y, EA, EB, s.bp, s.bcx, s.bcy);
 }
 
 template <bool STROKE>
@@ -602,8 +624,6 @@ __global__ void __launch_bounds__(kRT) raster_backward_kernel(const RasterArgs A
       if (!wait_chunk(&bars[c & 1], (uint32_t)(((last - c) >> 1) & 1), A.status)) return;
     }
     const DEntry* cb = buf[c & 1];  // record d of the tile is cb[d - c0]
-    s[0].bl = -1;  // records of other chunks are flushed / not resident
-    s[1].bl = -1;
     while (k >= rs) {
       const bool v0 = s[0].in && k <= s[0].fidx;
       const bool v1 = s[1].in && k <= s[1].fidx;
@@ -626,7 +646,19 @@ __global__ void __launch_bounds__(kRT) raster_backward_kernel(const RasterArgs A
         }
       }
       if (de > ds && de <= c0) break;  // its records lie in a lower chunk
-      bwd_entries<STROKE>(cb, c0, max(ds, c0), min(de, c1), px, py, s);
+      if (mid)
+        bwd_entries<STROKE, true>(cb, c0, max(ds, c0), min(de, c1), px, py, s);
+      else
+        bwd_entries<STROKE, false>(cb, c0, max(ds, c0), min(de, c1), px, py, s);
+      // the winner so far, while its record is resident; bl = -2 marks a
+      // winner from a chunk that is no longer resident (bp, bcx, bcy, be hold it)
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        if (s[u].bl >= 0) {
+          best_point(cb, c0, px[u], py, s[u]);
+          if (ds < c0) s[u].bl = -2;
+        }
+      }
       if (ds < c0) {
         mid = true;
         break;

@@ -96,7 +96,8 @@ CS_API int cs_isect_edge_ranges(const int32_t *prim_ids_sorted, const int32_t *p
  * segment, per-primitive tile rectangles, per-tile intersect and edge-slot
  * counts restricted to tile rows [tile_row_begin, tile_row_end), and their
  * exclusive scans: tile_bins [T, 2] (intersect [start, end)) and tile_dlist
- * [T, 2] (first staged record, record bound).  counters is a device int32[4]:
+ * [T, 2] (first staged record of the tile, per-strip record capacity c: the
+ * tile's 4 strip lists start at first + s c).  counters is a device int32[4]:
  * [0] intersect total, [1] status, [2] staged-record bound, [3] unused.
  * stroke_widths may be NULL (fill mode: zero stroke width); aniso selects the
  * chord-anisotropic padding of the reference's aniso_intersects.  If a total
@@ -105,10 +106,6 @@ CS_API int cs_isect_edge_ranges(const int32_t *prim_ids_sorted, const int32_t *p
  * CS_ERR_CAPACITY, so no later kernel reads past the caller's buffers.
  * Offsets that do not start at 0, end at num_segments and increase set
  * counters[1] to CS_ERR_ARG (the primitive is treated as empty).
- * tile_order (may be NULL) [band tiles] receives the band's tiles, as indices
- * from the band's first tile, heaviest first by an edge-slot and intersect
- * count estimate; the raster entry points take it to dispatch long tiles
- * before short ones.
  * With cs_bin_sort this replaces project (K3) + flatten + K4 + cumsum + K5 +
  * torch.sort + K6 of _CubicFillSplatFunction.forward, cubic_splatting.py:2815-2908.
  * Workspace: cs_bin_workspace_size(num_tiles). */
@@ -117,7 +114,7 @@ CS_API int cs_bin_count(const float *cubics_norm, const int32_t *prim_seg_offset
                  const float *aa_widths, const float *stroke_widths, const float *basis,
                  float *cubics_px, float *edges_px, int32_t *prim_tile_ranges,
                  int32_t *num_tiles_hit, int32_t *tile_bins, int32_t *tile_dlist,
-                 int32_t *tile_order, int32_t *counters, void *workspace, int64_t num_primitives,
+                 int32_t *counters, void *workspace, int64_t num_primitives,
                  int64_t num_segments, int64_t isect_capacity, int64_t dlist_capacity,
                  int32_t samples, int32_t img_height, int32_t img_width, int32_t tile_row_begin,
                  int32_t tile_row_end, float aabb_pad, int32_t aniso, void *stream);
@@ -126,12 +123,19 @@ CS_API int cs_bin_count(const float *cubics_norm, const int32_t *prim_seg_offset
  * its tile's range and sort every tile's pairs by (depth key, primitive id),
  * the order of a stable sort of the reference's keys.  Writes prim_ids_sorted
  * and isect_ids_sorted (reference key format; also used as scratch) [capacity].
- * When imeta is not NULL the same per-tile pass also stages the raster input:
- * per intersect a 48-byte record (imeta [I]) and, in fill mode, packed per-row
- * winding offsets (rowoff [I, 16]); per tile the near-edge records (dlist
- * [dlist_capacity] of 32 bytes; tile_dlist[t].y receives the record count).
- * stroke_widths non-NULL selects stroke mode (fill_rules, rowoff unused).
- * Work stops at the device when counters report an overflow. */
+ * When imeta is not NULL the same per-tile pass also stages the raster input.
+ * A tile is rasterised as 4 strips of 4 pixel rows ("units", unit id =
+ * 4 * (band tile index) + strip).  Per intersect: a 48-byte record (imeta
+ * [I]), per strip its (first record, record count) in that strip's list
+ * (isect_strips [I, 4, 2]) and, in fill mode, packed per-row winding offsets
+ * (rowoff [I, 16]); per strip the near-edge records (dlist [dlist_capacity]
+ * of 32 bytes, at the offsets tile_dlist gives).  unit_order (may be NULL;
+ * cs_unit_lists_size(band tiles) bytes) receives the band's units in 64
+ * buckets of their staged work, heaviest first, which the raster entry
+ * points use as their dispatch order.  stroke_widths non-NULL selects stroke
+ * mode (fill_rules, rowoff unused).  Work stops at the device when counters
+ * report an overflow. */
+CS_API size_t cs_unit_lists_size(int64_t num_tiles);
 CS_API int cs_bin_sort(const int32_t *prim_tile_ranges, const float *depths,
                 const int32_t *tile_bins, int32_t *prim_ids_sorted, int64_t *isect_ids_sorted,
                 int32_t *counters, void *workspace, int64_t num_primitives,
@@ -139,8 +143,8 @@ CS_API int cs_bin_sort(const int32_t *prim_tile_ranges, const float *depths,
                 int32_t tile_row_begin, int32_t tile_row_end, const float *edges_px,
                 const int32_t *prim_edge_offsets, const float *colors, const float *opacities,
                 const float *inv_sigma2s, const int32_t *fill_rules, const float *stroke_widths,
-                int32_t *tile_dlist, void *imeta, int32_t *rowoff, void *dlist,
-                int64_t dlist_capacity, void *stream);
+                int32_t *tile_dlist, void *imeta, int32_t *rowoff, int32_t *isect_strips,
+                void *dlist, int64_t dlist_capacity, int32_t *unit_order, void *stream);
 
 /* Staging of a reference-format sorted intersect list (primitive_ids_sorted,
  * tile_bins and isect_edge_ranges [I, 2] or prim_edge_offsets [P + 1]) into
@@ -153,40 +157,42 @@ CS_API int cs_tile_stage(const int32_t *prim_ids_sorted, const int32_t *tile_bin
                   const float *edges_px, const int32_t *isect_edge_ranges,
                   const int32_t *prim_edge_offsets, const float *colors, const float *opacities,
                   const float *inv_sigma2s, const int32_t *fill_rules, const float *stroke_widths,
-                  int32_t *tile_dlist, void *imeta, int32_t *rowoff, void *dlist,
-                  int32_t *counters, void *workspace, int64_t dlist_capacity, int32_t img_height,
-                  int32_t img_width, void *stream);
+                  int32_t *tile_dlist, void *imeta, int32_t *rowoff, int32_t *isect_strips,
+                  void *dlist, int32_t *unit_order, int32_t *counters, void *workspace,
+                  int64_t dlist_capacity, int32_t img_height, int32_t img_width, void *stream);
 
 /* --------------------------------------------------------------------------
- * Rasterisation (one CTA per 16x16 tile, front-to-back compositing)
+ * Rasterisation (one warp per 4 x 16-pixel strip, front-to-back compositing)
  * ------------------------------------------------------------------------ */
 
 /* Closed-fill forward: per pixel, winding number / crossing parity and the
  * minimum distance to the primitive's polyline, sigmoid soft coverage, then
  * front-to-back alpha compositing with early termination.  Input is the
- * staged tile data of cs_bin_sort / cs_tile_stage.  out_chw_clamped
+ * staged data of cs_bin_sort / cs_tile_stage (tile_dlist, imeta,
+ * isect_strips, rowoff, dlist; unit_order may be NULL).  out_chw_clamped
  * [3, H, W] (may be NULL) also receives clamp(out, 0, 1) channel-major, the
  * image the training loss sees (the reference does torch.clamp + permute,
  * manbo/gaussian_trace/render.py:1309-1310).  status (device int, may be NULL)
  * receives CS_ERR_TIMEOUT if a bounded wait gave up.  When target_chw
  * [3, H, W] is given the same launch also computes the MSE loss of the
- * clamped image: loss_out[0] = sum of squared differences over the launched
- * tiles, loss_out[1] = that / (3 H W), reduced in a fixed order by the last
- * CTA (workspace loss_ws: cs_loss_workspace_size(num_tiles) bytes, zeroed
- * once).  Tile rows outside [tile_row_begin, tile_row_end) are not touched.
- * tile_order (may be NULL): the dispatch order of cs_bin_count for the same
- * band; it changes only which CTA renders which tile, never a result.
+ * clamped image: loss_out[0] = sum of squared differences over the band,
+ * loss_out[1] = that / (3 H W), reduced in a fixed order.  workspace:
+ * cs_raster_workspace_size(num_tiles) bytes, zeroed before its first use; the
+ * launch leaves it ready for the next one (launches sharing a workspace must
+ * be ordered on one stream).  Tile rows outside [tile_row_begin, tile_row_end)
+ * are not touched.
  * Replaces rasterize_cubic_fill_forward_kernel, cubic_splatting.py:918-1194,
  * and (with target_chw) mse_partial_sum_kernel + reduce_sum_partial_kernel,
  * manbo/ops/metric.py:18-163. */
-CS_API size_t cs_loss_workspace_size(int64_t num_tiles);
+CS_API size_t cs_raster_workspace_size(int64_t num_tiles);
 CS_API int cs_fill_forward(const int32_t *prim_ids_sorted, const int32_t *tile_bins,
-                    const int32_t *tile_dlist, const void *imeta, const int32_t *rowoff,
-                    const void *dlist, const int32_t *tile_order, const float *background,
-                    float *out_img, float *final_Ts, int32_t *final_idx, float *out_chw_clamped,
-                    const float *target_chw, float *loss_out, void *loss_ws, int32_t *status,
-                    int32_t img_height, int32_t img_width, int32_t tile_row_begin,
-                    int32_t tile_row_end, void *stream);
+                    const int32_t *tile_dlist, const void *imeta, const int32_t *isect_strips,
+                    const int32_t *rowoff, const void *dlist, const int32_t *unit_order,
+                    const float *background, float *out_img, float *final_Ts,
+                    int32_t *final_idx, float *out_chw_clamped, const float *target_chw,
+                    float *loss_out, int32_t *status, void *workspace, int32_t img_height,
+                    int32_t img_width, int32_t tile_row_begin, int32_t tile_row_end,
+                    void *stream);
 
 /* Closed-fill backward: reverse compositing from final_idx, gradients of the
  * colours, opacities, 1/sigma^2 and edge endpoints (closest edge only).
@@ -196,15 +202,16 @@ CS_API int cs_fill_forward(const int32_t *prim_ids_sorted, const int32_t *tile_b
  * gradient is computed in the kernel instead: v = scale * (clamp(out) - target)
  * masked to 0 <= out <= 1, with out_img [H, W, 3], target_chw [3, H, W] and
  * *mse_scale (device scalar, e.g. 2/N * dLoss).  v_opacities and
- * v_inv_sigma2s may be NULL (not accumulated).
+ * v_inv_sigma2s may be NULL (not accumulated).  workspace as for the forward.
  * Replaces rasterize_cubic_fill_backward_kernel, cubic_splatting.py:1197-1651. */
 CS_API int cs_fill_backward(const int32_t *prim_ids_sorted, const int32_t *tile_bins,
-                     const int32_t *tile_dlist, const void *imeta, const int32_t *rowoff,
-                     const void *dlist, const int32_t *tile_order, const float *background,
-                     const float *final_Ts, const int32_t *final_idx, const float *v_output,
-                     const float *out_img, const float *target_chw, const float *mse_scale,
-                     float *v_edges, float *v_colors, float *v_opacities, float *v_inv_sigma2s,
-                     float *curve_contrib_rgb, float *curve_isect_contrib, int32_t *status,
+                     const int32_t *tile_dlist, const void *imeta, const int32_t *isect_strips,
+                     const int32_t *rowoff, const void *dlist, const int32_t *unit_order,
+                     const float *background, const float *final_Ts, const int32_t *final_idx,
+                     const float *v_output, const float *out_img, const float *target_chw,
+                     const float *mse_scale, float *v_edges, float *v_colors,
+                     float *v_opacities, float *v_inv_sigma2s, float *curve_contrib_rgb,
+                     float *curve_isect_contrib, int32_t *status, void *workspace,
                      int32_t img_height, int32_t img_width, int32_t tile_row_begin,
                      int32_t tile_row_end, void *stream);
 
@@ -212,27 +219,26 @@ CS_API int cs_fill_backward(const int32_t *prim_ids_sorted, const int32_t *tile_
  * Replaces rasterize_cubic_polyline_forward_kernel,
  * cubic_polyline_splatting.py:33-249. */
 CS_API int cs_stroke_forward(const int32_t *prim_ids_sorted, const int32_t *tile_bins,
-                      const int32_t *tile_dlist, const void *imeta, const void *dlist,
-                      const int32_t *tile_order, const float *background, float *out_img,
-                      float *final_Ts,
-                      int32_t *final_idx, float *out_chw_clamped, const float *target_chw,
-                      float *loss_out, void *loss_ws, int32_t *status, int32_t img_height,
-                      int32_t img_width, int32_t tile_row_begin, int32_t tile_row_end,
-                      void *stream);
+                      const int32_t *tile_dlist, const void *imeta, const int32_t *isect_strips,
+                      const void *dlist, const int32_t *unit_order, const float *background,
+                      float *out_img, float *final_Ts, int32_t *final_idx,
+                      float *out_chw_clamped, const float *target_chw, float *loss_out,
+                      int32_t *status, void *workspace, int32_t img_height, int32_t img_width,
+                      int32_t tile_row_begin, int32_t tile_row_end, void *stream);
 
 /* Stroke backward (adds d/d stroke width).
  * Replaces rasterize_cubic_polyline_backward_kernel,
  * cubic_polyline_splatting.py:252-660. */
 CS_API int cs_stroke_backward(const int32_t *prim_ids_sorted, const int32_t *tile_bins,
-                       const int32_t *tile_dlist, const void *imeta, const void *dlist,
-                       const int32_t *tile_order, const float *background, const float *final_Ts,
-                       const int32_t *final_idx, const float *v_output, const float *out_img,
-                       const float *target_chw, const float *mse_scale, float *v_edges,
-                       float *v_colors, float *v_opacities, float *v_stroke_widths,
-                       float *v_inv_sigma2s, float *curve_contrib_rgb,
-                       float *curve_isect_contrib, int32_t *status, int32_t img_height,
-                       int32_t img_width, int32_t tile_row_begin, int32_t tile_row_end,
-                       void *stream);
+                       const int32_t *tile_dlist, const void *imeta, const int32_t *isect_strips,
+                       const void *dlist, const int32_t *unit_order, const float *background,
+                       const float *final_Ts, const int32_t *final_idx, const float *v_output,
+                       const float *out_img, const float *target_chw, const float *mse_scale,
+                       float *v_edges, float *v_colors, float *v_opacities,
+                       float *v_stroke_widths, float *v_inv_sigma2s, float *curve_contrib_rgb,
+                       float *curve_isect_contrib, int32_t *status, void *workspace,
+                       int32_t img_height, int32_t img_width, int32_t tile_row_begin,
+                       int32_t tile_row_end, void *stream);
 
 /* Edge endpoint gradients -> cubic control-point gradients with the Bernstein
  * weights at t = e / (S-1); optional scale (sx, sy) applied to the result

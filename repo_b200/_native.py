@@ -41,17 +41,18 @@ SIGNATURES = {
     "cs_tile_bin_edges": (ctypes.c_int, [_P, _I64, _P, _I64, _P]),
     "cs_isect_edge_ranges": (ctypes.c_int, [_P, _P, _P, _I64, _P]),
     "cs_bin_workspace_size": (_SZ, [_I64]),
-    "cs_bin_count": (ctypes.c_int, [_P] * 14 + [_I64, _I64, _I64, _I64, _I32, _I32, _I32, _I32,
+    "cs_unit_lists_size": (_SZ, [_I64]),
+    "cs_bin_count": (ctypes.c_int, [_P] * 13 + [_I64, _I64, _I64, _I64, _I32, _I32, _I32, _I32,
                                                 _I32, _F32, _I32, _P]),
-    "cs_bin_sort": (ctypes.c_int, [_P] * 7 + [_I64, _I64, _I32, _I32, _I32, _I32] + [_P] * 11
-                    + [_I64, _P]),
+    "cs_bin_sort": (ctypes.c_int, [_P] * 7 + [_I64, _I64, _I32, _I32, _I32, _I32] + [_P] * 12
+                    + [_I64, _P, _P]),
     "cs_stage_workspace_size": (_SZ, [_I64]),
-    "cs_tile_stage": (ctypes.c_int, [_P] * 16 + [_I64, _I32, _I32, _P]),
-    "cs_loss_workspace_size": (_SZ, [_I64]),
-    "cs_fill_forward": (ctypes.c_int, [_P] * 16 + [_I32, _I32, _I32, _I32, _P]),
-    "cs_fill_backward": (ctypes.c_int, [_P] * 21 + [_I32, _I32, _I32, _I32, _P]),
-    "cs_stroke_forward": (ctypes.c_int, [_P] * 15 + [_I32, _I32, _I32, _I32, _P]),
-    "cs_stroke_backward": (ctypes.c_int, [_P] * 21 + [_I32, _I32, _I32, _I32, _P]),
+    "cs_tile_stage": (ctypes.c_int, [_P] * 18 + [_I64, _I32, _I32, _P]),
+    "cs_raster_workspace_size": (_SZ, [_I64]),
+    "cs_fill_forward": (ctypes.c_int, [_P] * 17 + [_I32, _I32, _I32, _I32, _P]),
+    "cs_fill_backward": (ctypes.c_int, [_P] * 23 + [_I32, _I32, _I32, _I32, _P]),
+    "cs_stroke_forward": (ctypes.c_int, [_P] * 16 + [_I32, _I32, _I32, _I32, _P]),
+    "cs_stroke_backward": (ctypes.c_int, [_P] * 23 + [_I32, _I32, _I32, _I32, _P]),
     "cs_edge_grads_to_cubics": (ctypes.c_int, [_P, _P, _I64, _I32, _F32, _F32, _P]),
     "cs_ring_to_cubics": (ctypes.c_int, [_P, _P, _I64, _I32, _I32, _I32, _P]),
     "cs_edge_grads_to_ring": (ctypes.c_int, [_P, _P, _I64, _I32, _I32, _I32, _I32, _I32, _P]),

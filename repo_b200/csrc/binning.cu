@@ -234,9 +234,9 @@ __global__ void edge_ranges_kernel(const int* __restrict__ pids, const int* __re
 // fused pipeline
 
 struct BinWorkspace {
-  int* tile_counts;   // [T] intersects per tile
-  int* tile_ecounts;  // [T] edge slots per tile (upper bound of staged records)
-  int* cursor;        // [T] scatter cursors
+  int* tile_counts;     // [T] intersects per tile
+  int* tile_ecounts;    // [T] edge slots per tile (each strip's record capacity)
+  int* cursor;          // [T] scatter cursors
 };
 
 __host__ __device__ inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
@@ -250,6 +250,8 @@ inline BinWorkspace bin_ws(void* base, long long ntiles) {
   w.cursor = reinterpret_cast<int*>(b + 2 * a);
   return w;
 }
+
+inline size_t bin_ws_size(long long ntiles) { return align256(sizeof(int) * ntiles) * 3; }
 
 // One warp per primitive: project + bound every segment, union the rects,
 // flatten all segments into edges, and add the primitive to the intersect and
@@ -323,31 +325,20 @@ __global__ void __launch_bounds__(256) bin_prep_kernel(
   }
 }
 
-// Work estimate of a tile for dispatch ordering: its edge slots (every edge
-// of every primitive on it) plus 8 per intersect, bucketed by bit length so
-// that bucket 0 holds the heaviest tiles.
-__device__ __forceinline__ int work_bucket(const int* counts, const int* ecounts, long long i) {
-  const unsigned est = (counts ? 8u * (unsigned)counts[i] : 0u) + (ecounts ? (unsigned)ecounts[i] : 0u);
-  return 31 - min(31, 32 - __clz(est));
-}
-
 // Exclusive scan of per-tile intersect counts into tile ranges [start, end)
-// and of per-tile edge-slot counts into staged-record ranges [base, bound);
-// one CTA of 1024.  Either input may be NULL.  If a total exceeds its
-// capacity every range is written empty and the status is set.  When `order`
-// is given it receives the band's tiles (indices relative to the band's first
-// tile) heaviest first, so that the raster kernels start the longest tiles
-// first and the light ones fill the tail.
+// and of per-tile edge-slot counts into staged-record ranges: tile t owns
+// kStrips consecutive lists of capacity ecount[t] each, so tile_dlist[t] =
+// (first record, ecount[t]) and the record bound is kStrips * sum(ecount).
+// One CTA of 1024.  Either input may be NULL.  If a total exceeds its
+// capacity every range is written empty and the status is set.
 __global__ void __launch_bounds__(1024) bin_scan_kernel(const int* __restrict__ counts,
                                                         const int* __restrict__ ecounts,
                                                         int* __restrict__ bins,
                                                         int* __restrict__ dlr,
                                                         int* __restrict__ cursor,
                                                         int* __restrict__ counters, long long nt,
-                                                        long long icap, long long dcap,
-                                                        int* __restrict__ order,
-                                                        long long band0, long long band_n) {
-  __shared__ int wa[32], wb[32], hist[32];
+                                                        long long icap, long long dcap) {
+  __shared__ int wa[32], wb[32];
   __shared__ long long s_ta, s_tb;
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   const long long chunk = (nt + 1023) / 1024;
@@ -370,10 +361,10 @@ __global__ void __launch_bounds__(1024) bin_scan_kernel(const int* __restrict__ 
     wb[lane] = xb - vb;
     if (lane == 31) {
       s_ta = xa;
-      s_tb = xb;
+      s_tb = (long long)kStrips * xb;
       if (counts) counters[0] = xa;
-      if (ecounts) counters[2] = xb;
-      if ((counts && xa > icap) || (ecounts && xb > dcap)) counters[1] = CS_ERR_CAPACITY;
+      if (ecounts) counters[2] = (int)min((long long)kStrips * xb, (long long)INT32_MAX);
+      if ((counts && xa > icap) || (ecounts && s_tb > dcap)) counters[1] = CS_ERR_CAPACITY;
     }
   }
   __syncthreads();
@@ -389,25 +380,11 @@ __global__ void __launch_bounds__(1024) bin_scan_kernel(const int* __restrict__ 
     }
     if (ecounts) {
       const int c = overflow ? 0 : ecounts[i];
-      dlr[2 * i] = c > 0 ? rb : 0;
+      dlr[2 * i] = c > 0 ? kStrips * rb : 0;
       dlr[2 * i + 1] = c > 0 ? c : 0;
       rb += c;
     }
   }
-  if (!order) return;
-  // counting sort of the band's tiles by work bucket (order within a bucket
-  // is arbitrary; it affects only scheduling)
-  if (tid < 32) hist[tid] = 0;
-  __syncthreads();
-  for (long long t = tid; t < band_n; t += 1024) atomicAdd(&hist[work_bucket(counts, ecounts, band0 + t)], 1);
-  __syncthreads();
-  if (wid == 0) {
-    const int v = hist[lane];
-    hist[lane] = warp_incl_scan(v, lane) - v;
-  }
-  __syncthreads();
-  for (long long t = tid; t < band_n; t += 1024)
-    order[atomicAdd(&hist[work_bucket(counts, ecounts, band0 + t)], 1)] = (int)t;
 }
 
 // One warp per primitive: scatter (depth key << 32 | primitive id) into the
@@ -515,6 +492,7 @@ struct StageIO {
   int2* dlr;
   IMeta* imeta;
   int* rowoff;
+  int2* istrip;         // per intersect and strip: (first record, record count)
   DEntry* dl;
   int tbx;
 };
@@ -535,11 +513,11 @@ struct StageShared {
   int sstart[kSortThreads + 1];  // first edge slot of each intersect; [m] = slot total
   int eb[kSortThreads];          // first edge of each intersect
   float dthr[kSortThreads];      // culling distance of each intersect
-  int dstart[kSortThreads + 1];  // first near record of each intersect; [m] = chunk end
-  unsigned bal[kStageU][kSortThreads / 32];  // near ballots of the current round
-  int pre[kStageU][kSortThreads / 32];       // their exclusive prefix counts
+  int dstart[kStrips][kSortThreads + 1];  // first record per strip; [m] = chunk end
+  unsigned bal[kStrips][kStageU][kSortThreads / 32];  // near ballots of the round
+  int pre[kStrips][kStageU][kSortThreads / 32];       // their exclusive prefix counts
   int wsum[kSortThreads / 32];
-  int total;
+  int total[kStrips];
 };
 
 // Classify the edges of intersects [rs, re) of one tile and write its staged
@@ -547,21 +525,25 @@ struct StageShared {
 // are taken in chunks of kSortThreads, one per thread for their attributes;
 // the chunk's edges are laid out as consecutive slots (intersect-major, edge
 // order within), which every thread walks kStageU slots per round.  A near
-// edge's record position is the number of near slots before it (ballots and
-// a prefix over the round's warps), which keeps (intersect, edge) order, and
-// an intersect's first record is that count at its first slot.  Far edges
-// right of the tile add to the intersect's per-row winding accumulators in
-// shared memory (`rows`, kSortThreads x 32 ints: 16 winding sums, 16 counts).
+// edge's position in a strip's list is the number of slots before it that are
+// near that strip (ballots and a prefix over the round's warps), which keeps
+// (intersect, edge) order; an intersect's first record in a strip is that
+// count at its first slot.  Strip st's list starts at dbase + st * stride.
+// Far edges right of the tile add to the intersect's per-row winding
+// accumulators in shared memory (`rows`, kSortThreads x 32 ints: 16 winding
+// sums, 16 counts).  Returns the strips' record totals (in every thread).
 template <bool STROKE>
 __device__ void stage_tile(const StageIO& io, long long tile, int rs, int re, int dbase,
-                           StageShared& sh, int (*rows)[32]) {
+                           int stride, StageShared& sh, int (*rows)[32], int totals[kStrips]) {
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   constexpr int nw = kSortThreads / 32;
   constexpr int kRound = kSortThreads * kStageU;
   const float bx0 = (float)((tile % io.tbx) * kTile) + 0.5f;
   const float by0 = (float)((tile / io.tbx) * kTile) + 0.5f;
   const unsigned lt = (1u << lane) - 1u;
-  int near_base = 0;
+  int near_base[kStrips];
+#pragma unroll
+  for (int st = 0; st < kStrips; ++st) near_base[st] = 0;
   for (int c0 = rs; c0 < re; c0 += kSortThreads) {
     const int m = min(kSortThreads, re - c0);
     // per intersect: attributes, edge range, slot count
@@ -601,6 +583,7 @@ __device__ void stage_tile(const StageIO& io, long long tile, int rs, int re, in
       for (int u = 0; u < kStageU; ++u) {
         const int j = rb + u * kSortThreads + tid;
         kk[u] = -1;
+        ee_[u] = 0;
         if (j < total) {
           int lo = 0, hi = m;  // last intersect whose first slot is <= j
           while (hi - lo > 1) {
@@ -614,15 +597,17 @@ __device__ void stage_tile(const StageIO& io, long long tile, int rs, int re, in
 #pragma unroll
       for (int u = 0; u < kStageU; ++u)
         E[u] = kk[u] >= 0 ? __ldg(io.edges + ee_[u]) : make_float4(0.f, 0.f, 0.f, 0.f);
-      bool near[kStageU];
-      unsigned bal[kStageU];
+      unsigned nm[kStageU], bal[kStrips][kStageU];
 #pragma unroll
       for (int u = 0; u < kStageU; ++u) {
-        near[u] = kk[u] >= 0 && edge_is_near(E[u], sh.dthr[kk[u]], bx0, by0);
-        bal[u] = __ballot_sync(0xffffffffu, near[u]);
-        if (lane == 0) sh.bal[u][wid] = bal[u];
-        if (!STROKE && kk[u] >= 0 && !near[u]) {
-          unsigned rr = far_right_rows(E[u], bx0, by0);
+        nm[u] = kk[u] >= 0 ? edge_near_strips(E[u], sh.dthr[kk[u]], bx0, by0) : 0u;
+#pragma unroll
+        for (int st = 0; st < kStrips; ++st) {
+          bal[st][u] = __ballot_sync(0xffffffffu, (nm[u] >> st) & 1u);
+          if (lane == 0) sh.bal[st][u][wid] = bal[st][u];
+        }
+        if (!STROKE && kk[u] >= 0) {
+          unsigned rr = far_right_rows(E[u], bx0, by0) & ~strip_rows(nm[u]);
           if (rr) {
             const int dir = (E[u].w - E[u].y) > 0.0f ? 1 : -1;
             while (rr) {
@@ -635,43 +620,67 @@ __device__ void stage_tile(const StageIO& io, long long tile, int rs, int re, in
         }
       }
       __syncthreads();
-      if (wid == 0) {  // exclusive prefix of the round's (u, warp) near counts
-        const int v = lane < kStageU * nw ? __popc(sh.bal[lane / nw][lane % nw]) : 0;
+      if (wid < kStrips) {  // warp st: exclusive prefix of strip st's (u, warp) counts
+        const int st = wid;
+        const int v = lane < kStageU * nw ? __popc(sh.bal[st][lane / nw][lane % nw]) : 0;
         const int x = warp_incl_scan(v, lane);
-        if (lane < kStageU * nw) sh.pre[lane / nw][lane % nw] = x - v;
-        if (lane == 31) sh.total = x;
+        if (lane < kStageU * nw) sh.pre[st][lane / nw][lane % nw] = x - v;
+        if (lane == 31) sh.total[st] = x;
       }
       __syncthreads();
 #pragma unroll
       for (int u = 0; u < kStageU; ++u) {
-        if (near[u]) {
-          const int pos = near_base + sh.pre[u][wid] + __popc(bal[u] & lt);
-          io.dl[dbase + pos] = make_entry(E[u], ee_[u]);
+        if (nm[u]) {
+          const DEntry rec = make_entry(E[u], ee_[u]);
+#pragma unroll
+          for (int st = 0; st < kStrips; ++st) {
+            if ((nm[u] >> st) & 1u) {
+              const int pos = near_base[st] + sh.pre[st][u][wid] + __popc(bal[st][u] & lt);
+              io.dl[dbase + st * stride + pos] = rec;
+            }
+          }
         }
       }
       if (tid < m) {
-        const int st = sh.sstart[tid] - rb;
-        if (st >= 0 && st < kRound && sh.sstart[tid] < total) {
-          const int u = st / kSortThreads, w2 = (st % kSortThreads) >> 5, l = st & 31;
-          sh.dstart[tid] = near_base + sh.pre[u][w2] + __popc(sh.bal[u][w2] & ((1u << l) - 1u));
+        const int sl = sh.sstart[tid] - rb;
+        if (sl >= 0 && sl < kRound && sh.sstart[tid] < total) {
+          const int u = sl / kSortThreads, w2 = (sl % kSortThreads) >> 5, l = sl & 31;
+          const unsigned below = (1u << l) - 1u;
+#pragma unroll
+          for (int st = 0; st < kStrips; ++st)
+            sh.dstart[st][tid] = near_base[st] + sh.pre[st][u][w2] + __popc(sh.bal[st][u][w2] & below);
         }
       }
-      near_base += sh.total;
+#pragma unroll
+      for (int st = 0; st < kStrips; ++st) near_base[st] += sh.total[st];
       __syncthreads();
     }
     // intersects with no slot left (empty, at the end of the chunk)
-    if (tid < m && sh.sstart[tid] >= total) sh.dstart[tid] = near_base;
-    if (tid == 0) sh.dstart[m] = near_base;
+    if (tid < m && sh.sstart[tid] >= total) {
+#pragma unroll
+      for (int st = 0; st < kStrips; ++st) sh.dstart[st][tid] = near_base[st];
+    }
+    if (tid == 0) {
+#pragma unroll
+      for (int st = 0; st < kStrips; ++st) sh.dstart[st][m] = near_base[st];
+    }
     __syncthreads();
     if (tid < m) {
       const int k = c0 + tid;
-      im.dstart = sh.dstart[tid];
-      im.dcount = sh.dstart[tid + 1] - sh.dstart[tid];
       int4* dst = reinterpret_cast<int4*>(io.imeta + k);
-      dst[0] = make_int4(im.dstart, im.dcount, im.pid, im.rule);
+      dst[0] = make_int4(0, 0, im.pid, im.rule);
       dst[1] = make_int4(__float_as_int(im.c0), __float_as_int(im.c1), __float_as_int(im.c2),
                          __float_as_int(im.op));
       dst[2] = make_int4(__float_as_int(im.a), __float_as_int(im.b), __float_as_int(im.dthr), 0);
+      int4* sr = reinterpret_cast<int4*>(io.istrip + (long long)k * kStrips);
+      int v[2 * kStrips];
+#pragma unroll
+      for (int st = 0; st < kStrips; ++st) {
+        v[2 * st] = sh.dstart[st][tid];
+        v[2 * st + 1] = sh.dstart[st][tid + 1] - sh.dstart[st][tid];
+      }
+      sr[0] = make_int4(v[0], v[1], v[2], v[3]);
+      sr[1] = make_int4(v[4], v[5], v[6], v[7]);
     }
     if (!STROKE) {
       for (int q = tid; q < m * 16; q += kSortThreads) {
@@ -681,33 +690,52 @@ __device__ void stage_tile(const StageIO& io, long long tile, int rs, int re, in
     }
     __syncthreads();  // shared state is reused by the next chunk
   }
-  if (tid == 0) io.dlr[tile].y = near_base;
+#pragma unroll
+  for (int st = 0; st < kStrips; ++st) totals[st] = near_base[st];
+}
+
+// Work estimate of a strip for dispatch ordering: its staged records plus two
+// per intersect (the per-intersect compositing costs about two records).
+__device__ __forceinline__ int strip_weight(int records, int intersects) {
+  return intersects > 0 ? 2 * records + 5 * intersects : 0;
 }
 
 // One CTA per tile: sort the tile's pairs and emit primitive ids and
 // reference-format intersect ids; then, when staging outputs are given,
-// classify the tile's edges into its staged records.
+// classify the tile's edges into its strips' records, store the strips' work
+// estimates and (last CTA) order the band's strips heaviest first.
 template <bool STROKE>
 __global__ void __launch_bounds__(kSortThreads) bin_tile_kernel(
     const int* __restrict__ bins, const float* __restrict__ depths,
     unsigned long long* __restrict__ pairs, int* __restrict__ pids, long long* __restrict__ ids,
-    const int* __restrict__ counters, long long icap, long long dcap, int r0, StageIO io) {
+    const int* __restrict__ counters, long long icap, long long dcap, int r0, StageIO io,
+    int* __restrict__ lists) {
   // the sort buffer is reused for the staging row accumulators
   static_assert(sizeof(unsigned long long) * kSortSmem >= sizeof(int) * kSortThreads * 32,
                 "row accumulators must fit the sort buffer");
   __shared__ __align__(16) unsigned long long s[kSortSmem];
   __shared__ StageShared sh;
   const long long tile = (long long)(r0 + blockIdx.y) * io.tbx + blockIdx.x;
+  const int unit0 = kStrips * (blockIdx.y * gridDim.x + blockIdx.x);
   const int start = bins[2 * tile], end = bins[2 * tile + 1];
   const int n = end - start;
-  if (n <= 0) return;
-  if (counters[0] > icap) return;  // overflow: the pairs were not all written
-  sort_tile(pairs, start, n, tile, depths, pids, ids, s);
+  const bool sorted = n > 0 && counters[0] <= icap;  // on overflow the pairs were not all written
+  if (sorted) sort_tile(pairs, start, n, tile, depths, pids, ids, s);
   if (!io.imeta) return;
-  if (counters[2] > dcap) return;
-  __syncthreads();
-  stage_tile<STROKE>(io, tile, start, end, io.dlr[tile].x, sh,
-                     reinterpret_cast<int (*)[32]>(s));
+  int totals[kStrips] = {0, 0, 0, 0};
+  if (sorted && counters[2] <= dcap) {
+    __syncthreads();
+    const int2 dl = io.dlr[tile];
+    stage_tile<STROKE>(io, tile, start, end, dl.x, dl.y, sh, reinterpret_cast<int (*)[32]>(s),
+                       totals);
+  }
+  if (lists && threadIdx.x < kStrips) {
+    int t = 0;
+#pragma unroll
+    for (int st = 0; st < kStrips; ++st) t = threadIdx.x == st ? totals[st] : t;
+    append_unit(lists, kStrips * gridDim.x * gridDim.y, unit0 + threadIdx.x,
+                sorted ? strip_weight(t, n) : 0);
+  }
 }
 
 // Standalone staging for a reference-format intersect list: per-tile edge-slot
@@ -738,14 +766,26 @@ __global__ void tile_esum_kernel(const int* __restrict__ bins, const int* __rest
 template <bool STROKE>
 __global__ void __launch_bounds__(kSortThreads) tile_stage_kernel(const int* __restrict__ bins,
                                                                   const int* __restrict__ counters,
-                                                                  long long dcap, StageIO io) {
+                                                                  long long dcap, StageIO io,
+                                                                  int* __restrict__ lists) {
   __shared__ int s_row[STROKE ? 1 : kSortThreads][32];
   __shared__ StageShared sh;
   const long long tile = (long long)blockIdx.y * io.tbx + blockIdx.x;
+  const int unit0 = kStrips * (blockIdx.y * gridDim.x + blockIdx.x);
   const int rs = bins[2 * tile], re = bins[2 * tile + 1];
-  if (re <= rs) return;
-  if (counters[2] > dcap) return;
-  stage_tile<STROKE>(io, tile, rs, re, io.dlr[tile].x, sh, s_row);
+  int totals[kStrips] = {0, 0, 0, 0};
+  const bool staged = re > rs && counters[2] <= dcap;
+  if (staged) {
+    const int2 dl = io.dlr[tile];
+    stage_tile<STROKE>(io, tile, rs, re, dl.x, dl.y, sh, s_row, totals);
+  }
+  if (lists && threadIdx.x < kStrips) {
+    int t = 0;
+#pragma unroll
+    for (int st = 0; st < kStrips; ++st) t = threadIdx.x == st ? totals[st] : t;
+    append_unit(lists, kStrips * gridDim.x * gridDim.y, unit0 + threadIdx.x,
+                staged ? strip_weight(t, re - rs) : 0);
+  }
 }
 
 }  // namespace cs
@@ -824,15 +864,17 @@ int cs_isect_edge_ranges(const int32_t* prim_ids_sorted, const int32_t* prim_edg
   return launch_status();
 }
 
-size_t cs_bin_workspace_size(int64_t num_tiles) {
-  return align256(sizeof(int) * num_tiles) * 3;
+size_t cs_bin_workspace_size(int64_t num_tiles) { return bin_ws_size(num_tiles); }
+
+size_t cs_unit_lists_size(int64_t num_tiles) {
+  const long long units = (long long)kStrips * (num_tiles > 0 ? num_tiles : 1);
+  return sizeof(int32_t) * (size_t)(kUnitBuckets + kUnitBuckets * units);
 }
 
 int cs_bin_count(const float* cubics_norm, const int32_t* prim_seg_offsets, const float* aa_widths,
                  const float* stroke_widths, const float* basis, float* cubics_px,
                  float* edges_px, int32_t* prim_tile_ranges, int32_t* num_tiles_hit,
-                 int32_t* tile_bins, int32_t* tile_dlist, int32_t* tile_order, int32_t* counters,
-                 void* workspace,
+                 int32_t* tile_bins, int32_t* tile_dlist, int32_t* counters, void* workspace,
                  int64_t num_primitives, int64_t num_segments, int64_t isect_capacity,
                  int64_t dlist_capacity, int32_t samples, int32_t img_height, int32_t img_width,
                  int32_t tile_row_begin, int32_t tile_row_end, float aabb_pad, int32_t aniso,
@@ -855,8 +897,7 @@ int cs_bin_count(const float* cubics_norm, const int32_t* prim_seg_offsets, cons
   }
   bin_scan_kernel<<<1, 1024, 0, st>>>(ws.tile_counts, ws.tile_ecounts, tile_bins, tile_dlist,
                                       ws.cursor, counters, nt, (isect_capacity > 0 ? isect_capacity : 0),
-                                      (dlist_capacity > 0 ? dlist_capacity : 0), tile_order,
-                                      (long long)r0 * tbx, (long long)max(0, r1 - r0) * tbx);
+                                      (dlist_capacity > 0 ? dlist_capacity : 0));
   return launch_status();
 }
 
@@ -864,7 +905,7 @@ static StageIO stage_io(const int32_t* pids, const float* edges_px, const int32_
                         const int32_t* eoffs, const float* colors, const float* opacities,
                         const float* inv_sigma2s, const int32_t* fill_rules,
                         const float* stroke_widths, int32_t* tile_dlist, void* imeta,
-                        int32_t* rowoff, void* dlist, int tbx) {
+                        int32_t* rowoff, int32_t* istrip, void* dlist, int tbx) {
   StageIO io;
   io.pids = pids;
   io.edges = reinterpret_cast<const float4*>(edges_px);
@@ -878,6 +919,7 @@ static StageIO stage_io(const int32_t* pids, const float* edges_px, const int32_
   io.dlr = reinterpret_cast<int2*>(tile_dlist);
   io.imeta = reinterpret_cast<IMeta*>(imeta);
   io.rowoff = rowoff;
+  io.istrip = reinterpret_cast<int2*>(istrip);
   io.dl = reinterpret_cast<DEntry*>(dlist);
   io.tbx = tbx;
   return io;
@@ -890,13 +932,14 @@ int cs_bin_sort(const int32_t* prim_tile_ranges, const float* depths, const int3
                 int32_t tile_row_end, const float* edges_px, const int32_t* prim_edge_offsets,
                 const float* colors, const float* opacities, const float* inv_sigma2s,
                 const int32_t* fill_rules, const float* stroke_widths, int32_t* tile_dlist,
-                void* imeta, int32_t* rowoff, void* dlist, int64_t dlist_capacity,
-                void* stream) {
+                void* imeta, int32_t* rowoff, int32_t* isect_strips, void* dlist,
+                int64_t dlist_capacity, int32_t* unit_order, void* stream) {
   if (num_primitives < 0 || isect_capacity < 0 || !workspace || !isect_ids_sorted || !counters)
     return CS_ERR_ARG;
   const bool stage = imeta != nullptr;
   if (stage && (!edges_px || !prim_edge_offsets || !colors || !opacities || !inv_sigma2s ||
-                !tile_dlist || !dlist || (!stroke_widths && (!fill_rules || !rowoff))))
+                !tile_dlist || !dlist || !isect_strips ||
+                (!stroke_widths && (!fill_rules || !rowoff))))
     return CS_ERR_ARG;
   cudaStream_t st = (cudaStream_t)stream;
   const int tbx = (img_width + kTile - 1) / kTile, tby = (img_height + kTile - 1) / kTile;
@@ -909,17 +952,19 @@ int cs_bin_sort(const int32_t* prim_tile_ranges, const float* depths, const int3
       prim_tile_ranges, depths, ws.cursor, pairs, counters, num_primitives, tbx, isect_capacity,
       r0, r1);
   StageIO io = stage_io(prim_ids_sorted, edges_px, nullptr, prim_edge_offsets, colors, opacities,
-                        inv_sigma2s, fill_rules, stroke_widths, tile_dlist, imeta, rowoff, dlist,
-                        tbx);
+                        inv_sigma2s, fill_rules, stroke_widths, tile_dlist, imeta, rowoff,
+                        isect_strips, dlist, tbx);
   dim3 grid(tbx, r1 - r0);
+  int* lists = stage ? unit_order : nullptr;
+  if (lists) cudaMemsetAsync(lists, 0, sizeof(int) * kUnitBuckets, st);
   if (stroke_widths)
     bin_tile_kernel<true><<<grid, kSortThreads, 0, st>>>(
         tile_bins, depths, pairs, prim_ids_sorted, reinterpret_cast<long long*>(isect_ids_sorted),
-        counters, isect_capacity, (dlist_capacity > 0 ? dlist_capacity : 0), r0, io);
+        counters, isect_capacity, (dlist_capacity > 0 ? dlist_capacity : 0), r0, io, lists);
   else
     bin_tile_kernel<false><<<grid, kSortThreads, 0, st>>>(
         tile_bins, depths, pairs, prim_ids_sorted, reinterpret_cast<long long*>(isect_ids_sorted),
-        counters, isect_capacity, (dlist_capacity > 0 ? dlist_capacity : 0), r0, io);
+        counters, isect_capacity, (dlist_capacity > 0 ? dlist_capacity : 0), r0, io, lists);
   return launch_status();
 }
 
@@ -929,10 +974,12 @@ int cs_tile_stage(const int32_t* prim_ids_sorted, const int32_t* tile_bins, cons
                   const int32_t* isect_edge_ranges, const int32_t* prim_edge_offsets,
                   const float* colors, const float* opacities, const float* inv_sigma2s,
                   const int32_t* fill_rules, const float* stroke_widths, int32_t* tile_dlist,
-                  void* imeta, int32_t* rowoff, void* dlist, int32_t* counters, void* workspace,
+                  void* imeta, int32_t* rowoff, int32_t* isect_strips, void* dlist,
+                  int32_t* unit_order, int32_t* counters, void* workspace,
                   int64_t dlist_capacity, int32_t img_height, int32_t img_width, void* stream) {
   if (!prim_ids_sorted || !tile_bins || !edges_px || (!isect_edge_ranges && !prim_edge_offsets) ||
       !colors || !opacities || !inv_sigma2s || !tile_dlist || !imeta || !dlist || !counters ||
+      !isect_strips ||
       !workspace || (!stroke_widths && (!fill_rules || !rowoff)) || img_height <= 0 ||
       img_width <= 0)
     return CS_ERR_ARG;
@@ -940,22 +987,23 @@ int cs_tile_stage(const int32_t* prim_ids_sorted, const int32_t* tile_bins, cons
   const int tbx = (img_width + kTile - 1) / kTile, tby = (img_height + kTile - 1) / kTile;
   const long long nt = (long long)tbx * tby;
   int* ecounts = static_cast<int*>(workspace);
+  if (unit_order) cudaMemsetAsync(unit_order, 0, sizeof(int) * kUnitBuckets, st);
   tile_esum_kernel<<<ceil_div(nt * 32, 256), 256, 0, st>>>(
       tile_bins, prim_ids_sorted, reinterpret_cast<const int2*>(isect_edge_ranges),
       prim_edge_offsets, ecounts, nt);
   bin_scan_kernel<<<1, 1024, 0, st>>>(nullptr, ecounts, nullptr, tile_dlist, nullptr, counters,
-                                      nt, 0, (dlist_capacity > 0 ? dlist_capacity : 0), nullptr, 0,
-                                      0);
+                                      nt, 0, (dlist_capacity > 0 ? dlist_capacity : 0));
   StageIO io = stage_io(prim_ids_sorted, edges_px, isect_edge_ranges, prim_edge_offsets, colors,
                         opacities, inv_sigma2s, fill_rules, stroke_widths, tile_dlist, imeta,
-                        rowoff, dlist, tbx);
+                        rowoff, isect_strips, dlist, tbx);
   dim3 grid(tbx, tby);
+  const long long dcap = dlist_capacity > 0 ? dlist_capacity : 0;
   if (stroke_widths)
-    tile_stage_kernel<true><<<grid, kSortThreads, 0, st>>>(tile_bins, counters,
-                                                           (dlist_capacity > 0 ? dlist_capacity : 0), io);
+    tile_stage_kernel<true><<<grid, kSortThreads, 0, st>>>(tile_bins, counters, dcap, io,
+                                                           unit_order);
   else
-    tile_stage_kernel<false><<<grid, kSortThreads, 0, st>>>(tile_bins, counters,
-                                                            (dlist_capacity > 0 ? dlist_capacity : 0), io);
+    tile_stage_kernel<false><<<grid, kSortThreads, 0, st>>>(tile_bins, counters, dcap, io,
+                                                            unit_order);
   return launch_status();
 }
 

@@ -10,7 +10,7 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 
-#include "../../include/cubicsplat_b200.h"
+#include "cubicsplat_b200.h"
 
 namespace cs {
 

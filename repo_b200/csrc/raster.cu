@@ -1,64 +1,70 @@
-// Per-tile rasterisation of closed fills and open strokes, forward and
-// backward (sm_100a).
+// Rasterisation of closed fills and open strokes, forward and backward
+// (sm_100a).
 //
-// One CTA per 16x16 tile, 128 threads, two horizontally adjacent pixels per
-// thread (a warp owns four pixel rows).  The tile's geometry was staged once
-// per frame by the binning pass (stage.cuh): a compact list of the edges that
-// come within d_thr of the tile, per intersect, plus per-row winding offsets
-// for far edges right of the tile.  The CTA brings that list into shared
-// memory with cp.async.bulk copies of up to kChunk records, double-buffered
-// and completed on an mbarrier; after that every warp walks the intersects on
-// its own, with no CTA barrier until the next chunk.
+// The unit of work is a strip: 4 pixel rows x 16 columns of a 16x16 tile, one
+// warp, two horizontally adjacent pixels per lane.  The kernels are
+// persistent: every warp takes its first strip by its global warp id and the
+// next ones from a device counter, in the heaviest-first order computed by
+// the staging pass, so the SMs stay evenly loaded to the end of the launch.
+// A strip's geometry was staged once per frame (stage.cuh): the compact list
+// of the edges that come within d_thr of the strip, per intersect, plus
+// per-row winding offsets for far edges right of the tile.  Each warp brings
+// its strip's list into its own shared-memory buffers with cp.async.bulk
+// copies of up to kWChunk records, double-buffered and completed on the
+// warp's own mbarriers, and walks the intersects on its own: there is no CTA
+// barrier until the launch ends.
 //
 // Why visiting only near edges is exact: d_thr is the distance beyond which a
 // pixel's coverage is saturated for the primitive (fill: exactly 1.0f inside
 // and below alpha_min outside; stroke: below alpha_min).  A pixel closer than
-// d_thr to the polyline has its closest edge in the near list, so its minimum
-// distance is the exact one; a farther pixel gets a saturated coverage from
-// whatever edges it sees, identical to visiting every edge.  The crossing
-// test needs all edges that span the pixel's row and lie right of it: near
-// ones are tested per pixel, far ones are the per-row offsets.  This is the
-// reference's per-pixel loop over every edge of every intersect
+// d_thr to the polyline has its closest edge in its strip's list, so its
+// minimum distance is the exact one; a farther pixel gets a saturated
+// coverage from whatever edges it sees, identical to visiting every edge.
+// The crossing test needs all edges that span the pixel's row and lie right
+// of it: near ones are tested per pixel, far ones are the per-row offsets.
+// This is the reference's per-pixel loop over every edge of every intersect
 // (manbo/ops/cubic_splatting.py:1070-1136 forward, :1429-1501 backward;
-// cubic_polyline_splatting.py:175-216, :480-529) with the same arithmetic in
-// the same order (-fmad=false) and exp = cs_expf.
+// cubic_polyline_splatting.py:175-216, :480-529) with the same formulas in
+// the same order and exp = cs_expf.
 //
-// The backward walks the intersects in reverse from each warp's largest
+// The backward walks the intersects in reverse from the warp's largest
 // final_idx with T <- T / (1 - alpha), takes the first-minimum closest edge
-// (lexicographic on (d^2, edge id), the reference's strict-< rule), reduces
-// per-primitive gradients over the warp into shared memory, and accumulates
-// edge gradients per staged edge in shared memory before one global atomic
+// (the reference's strict-< rule in edge order), reduces per-primitive
+// gradients over the warp before one atomic per primitive, and accumulates
+// edge gradients per staged record in shared memory before one global atomic
 // per edge and chunk.
 #include "stage.cuh"
 
 namespace cs {
 
-constexpr int kRT = 128;              // threads per CTA: 16 rows x 8 pixel pairs
-constexpr int kChunk = 256;           // staged edge records per shared-memory buffer
-constexpr int kPaccCap = 64;          // intersects per tile with shared accumulators
+constexpr int kRW = 4;                // warps per CTA (independent strip processors)
+constexpr int kRT = 32 * kRW;
+constexpr int kWChunk = 64;           // staged records per warp buffer
 constexpr int kAcc = 10;              // per-intersect gradient accumulators
 constexpr int kSpinLimit = 1 << 22;   // mbarrier polls before reporting a timeout
 
 struct RasterArgs {
   const int* pids;
   const int* bins;
-  const int2* dlr;      // per tile: first staged record, record count
+  const int2* dlr;       // per tile: first staged record, per-strip capacity
   const IMeta* meta;
-  const int* rowoff;    // [I][16] packed row winding offsets (fill)
+  const int2* istrip;    // per intersect and strip: (first record, record count)
+  const int* rowoff;     // [I][16] packed row winding offsets (fill)
   const DEntry* dl;
+  const int* order;      // optional unit lists (stage.cuh), heaviest bucket first
   const float* bg;
-  const int* order;     // optional dispatch order: CTA b renders band tile order[b]
-  int H, W, tbx, r0;
+  int H, W, tbx, r0, nunits;
   int* status;
+  unsigned* queue;       // workspace: next dynamically taken unit
+  unsigned* ticket;      // workspace: CTA completion ticket
+  float* partials;       // workspace: per-unit sums of squared differences
   // forward outputs
   float* out;
   float* fts;
   int* fidx;
   float* out_chw;
   const float* loss_tgt;     // optional [3, H, W] target: fused SSE / MSE
-  float* loss_out;           // [2]: sse of the launched tiles, sse / (3 H W)
-  float* loss_partials;      // [launched CTAs]
-  unsigned int* loss_ticket;
+  float* loss_out;           // [2]: sse of the band, sse / (3 H W)
   // backward
   const float* fts_in;
   const int* fidx_in;
@@ -74,6 +80,122 @@ struct RasterArgs {
   float* contrib;
   float* icontrib;
 };
+
+// Tile, strip and first record of a unit (unit = kStrips * band tile + strip).
+struct UnitGeom {
+  long long tile;
+  int tx, ty, st, rs, re;
+  long long base;  // first record of the strip's list
+};
+
+__device__ __forceinline__ UnitGeom unit_geom(const RasterArgs& A, int unit) {
+  UnitGeom g;
+  const int trel = unit / kStrips;
+  g.st = unit - trel * kStrips;
+  const int ry = trel / A.tbx;
+  g.tx = trel - ry * A.tbx;
+  g.ty = A.r0 + ry;
+  g.tile = (long long)g.ty * A.tbx + g.tx;
+  g.rs = __ldg(A.bins + 2 * g.tile);
+  g.re = __ldg(A.bins + 2 * g.tile + 1);
+  g.base = 0;
+  if (g.re > g.rs) {
+    const int2 dl = A.dlr[g.tile];
+    g.base = (long long)dl.x + (long long)g.st * dl.y;
+  }
+  return g;
+}
+
+// Number of records of intersects [rs, k] in strip st's list.
+__device__ __forceinline__ int strip_records_upto(const RasterArgs& A, int k, int st) {
+  const int2 r = A.istrip[(long long)k * kStrips + st];
+  return r.x + r.y;
+}
+
+// Next unit of this warp: the first by warp id, the rest from the counter.
+__device__ __forceinline__ int next_unit(const RasterArgs& A) {
+  unsigned v = 0u;
+  if ((threadIdx.x & 31) == 0) v = gridDim.x * kRW + atomicAdd(A.queue, 1u);
+  return (int)__shfl_sync(0xffffffffu, v, 0);
+}
+
+// The last CTA to finish resets the counters (and reduces the loss partials
+// in a fixed order when asked), so the workspace is ready for the next launch.
+__device__ __forceinline__ void finish_launch(const RasterArgs& A, bool reduce_loss) {
+  __shared__ bool last;
+  __shared__ float red[kRW];
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    last = atomicAdd(A.ticket, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  if (reduce_loss) {
+    float v = 0.0f;
+    for (int q = threadIdx.x; q < A.nunits; q += kRT) v += A.partials[q];
+    v = warp_sum(v);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float t = 0.0f;
+#pragma unroll
+      for (int w = 0; w < kRW; ++w) t += red[w];
+      A.loss_out[0] = t;
+      A.loss_out[1] = t / (3.0f * (float)A.H * (float)A.W);
+    }
+  }
+  if (threadIdx.x == 0) {
+    *A.queue = 0u;
+    *A.ticket = 0u;
+  }
+}
+
+// Per-warp batch of up to 32 consecutive intersects' records in shared
+// memory: the IMeta record (three 16-byte parts), the strip's record range and
+// the strip's four packed row offsets.  One coalesced load per lane replaces a
+// chain of dependent global loads per intersect.
+struct IBatch {
+  int4 m[3][32];
+  int2 rg[32];
+  int4 ro[32];
+};
+
+template <bool STROKE>
+__device__ __forceinline__ void load_batch(const RasterArgs& A, int k0, int n, int st,
+                                           IBatch& b) {
+  const int lane = threadIdx.x & 31;
+  __syncwarp();  // every lane is done with the previous batch
+  if (lane < n) {
+    const long long k = (long long)k0 + lane;
+    const int4* q = reinterpret_cast<const int4*>(A.meta + k);
+    const int4 m0 = __ldg(q), m1 = __ldg(q + 1), m2 = __ldg(q + 2);
+    const int2 rg = __ldg(A.istrip + k * kStrips + st);
+    int4 ro = make_int4(0, 0, 0, 0);
+    if (!STROKE) ro = __ldg(reinterpret_cast<const int4*>(A.rowoff + k * 16 + st * kStripRows));
+    b.m[0][lane] = m0;
+    b.m[1][lane] = m1;
+    b.m[2][lane] = m2;
+    b.rg[lane] = rg;
+    b.ro[lane] = ro;
+  }
+  __syncwarp();
+}
+
+__device__ __forceinline__ void batch_meta(const IBatch& b, int j, IMeta& m) {
+  const int4 x = b.m[0][j], y = b.m[1][j], z = b.m[2][j];
+  m.dstart = x.x; m.dcount = x.y; m.pid = x.z; m.rule = x.w;
+  m.c0 = __int_as_float(y.x); m.c1 = __int_as_float(y.y);
+  m.c2 = __int_as_float(y.z); m.op = __int_as_float(y.w);
+  m.a = __int_as_float(z.x); m.b = __int_as_float(z.y); m.dthr = __int_as_float(z.z);
+  m.spare = 0.0f;
+}
+
+// Packed row offset of this lane's pixel row (row lane / 8 of the strip).
+__device__ __forceinline__ int batch_rowoff(const IBatch& b, int j) {
+  return reinterpret_cast<const int*>(&b.ro[j])[(threadIdx.x & 31) >> 3];
+}
 
 // ---------------------------------------------------------------------------
 // bulk copies into shared memory (non-multicast cp.async.bulk + mbarrier)
@@ -118,9 +240,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait; the outcome is agreed by the whole CTA so that nobody is left
-// at a later barrier.  On timeout the device status is set and the CTA stops.
-__device__ __forceinline__ bool wait_chunk(uint64_t* bar, uint32_t parity, int* status) {
+// Bounded wait of one warp on its own buffer's mbarrier; the outcome is agreed
+// by the warp.  On timeout the device status is set and the warp stops.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* status) {
   bool ok = false;
   for (int i = 0; i < kSpinLimit; ++i) {
     if (mbar_try_wait(bar, parity)) {
@@ -128,9 +250,17 @@ __device__ __forceinline__ bool wait_chunk(uint64_t* bar, uint32_t parity, int* 
       break;
     }
   }
-  const bool all = __syncthreads_and(ok);
-  if (!all && threadIdx.x == 0 && status) atomicExch(status, CS_ERR_TIMEOUT);
+  const bool all = __all_sync(0xffffffffu, ok);
+  if (!all && (threadIdx.x & 31) == 0 && status) atomicExch(status, CS_ERR_TIMEOUT);
   return all;
+}
+
+// Wait for the next completion of buffer b's barrier (b = 0 or 1; bit b of
+// phase holds its parity and flips with every completion).
+__device__ __forceinline__ bool wait_buffer(uint64_t* bars, int b, uint32_t& phase, int* status) {
+  const bool ok = warp_wait(&bars[b], (phase >> b) & 1u, status);
+  phase ^= 1u << b;
+  return ok;
 }
 
 // ---------------------------------------------------------------------------
@@ -240,68 +370,60 @@ __device__ __forceinline__ void fwd_composite(FwdPix& p, const IMeta& m, int k) 
   if (nT <= kTransStop) p.done = true;
 }
 
-// The tile a CTA renders: band tile order[b] for linear block id b when an
-// order is given (heaviest tiles first), else the tile at the block's position.
-__device__ __forceinline__ void block_tile(const RasterArgs& A, int& tx, int& ty) {
-  if (A.order) {
-    const int t = __ldg(A.order + blockIdx.y * gridDim.x + blockIdx.x);
-    const int ry = t / A.tbx;
-    tx = t - ry * A.tbx;
-    ty = A.r0 + ry;
-  } else {
-    tx = blockIdx.x;
-    ty = A.r0 + blockIdx.y;
-  }
-}
-
+// Forward of one unit by one warp.  Returns false if a bounded wait gave up.
 template <bool STROKE>
-__global__ void __launch_bounds__(kRT) raster_forward_kernel(const RasterArgs A) {
-  __shared__ __align__(128) DEntry buf[2][kChunk];
-  __shared__ __align__(8) uint64_t bars[2];
-  const int tid = threadIdx.x, lane = tid & 31;
-  int tx, ty;
-  block_tile(A, tx, ty);
-  const long long tile = (long long)ty * A.tbx + tx;
-  const int rs = A.bins[2 * tile], re = A.bins[2 * tile + 1];
-  const int2 dr = A.dlr[tile];
-  const int nd = re > rs ? dr.y : 0;
-  const int nchunks = max(1, (nd + kChunk - 1) / kChunk);
-  const int ly = tid >> 3, lx = (tid & 7) * 2;
-  const int i = ty * kTile + ly, j0 = tx * kTile + lx;
+__device__ __forceinline__ bool forward_unit(const RasterArgs& A, int unit,
+                                             DEntry (*buf)[kWChunk], uint64_t* bars,
+                                             uint32_t& phase, IBatch& ib) {
+  const int lane = threadIdx.x & 31;
+  const UnitGeom g = unit_geom(A, unit);
+  const int rs = g.rs, re = g.re, st = g.st;
+  const int nd = re > rs ? strip_records_upto(A, re - 1, st) : 0;
+  const int nchunks = max(1, (nd + kWChunk - 1) / kWChunk);
+  const int ly = st * kStripRows + (lane >> 3), lx = (lane & 7) * 2;
+  const int i = g.ty * kTile + ly, j0 = g.tx * kTile + lx;
   const bool in0 = i < A.H && j0 < A.W, in1 = i < A.H && j0 + 1 < A.W;
   const float py = (float)i + 0.5f;
   const float px0 = (float)j0 + 0.5f, px1 = (float)(j0 + 1) + 0.5f;
   FwdPix p0{1.0f, 0.f, 0.f, 0.f, 1e30f, 0, 0, 0, !in0};
   FwdPix p1{1.0f, 0.f, 0.f, 0.f, 1e30f, 0, 0, 0, !in1};
-  if (tid == 0 && nd > 0) {
-    mbar_init(&bars[0]);
-    mbar_init(&bars[1]);
-    fence_barrier_init();
-    bulk_load(buf[0], A.dl + dr.x, (uint32_t)min(nd, kChunk) * sizeof(DEntry), &bars[0]);
-  }
-  __syncthreads();  // barriers initialised before anyone waits on them
-  int k = rs;          // next intersect of this warp
+  if (nd > 0 && lane == 0)
+    bulk_load(buf[0], A.dl + g.base, (uint32_t)min(nd, kWChunk) * sizeof(DEntry), &bars[0]);
+  int k = rs;          // next intersect
+  int kb = rs - 32;    // first intersect of the batch in shared memory
   bool mid = false;    // k partially visited (split across chunks)
   bool ok = true;
   for (int c = 0; c < nchunks; ++c) {
-    const int c0 = c * kChunk, c1 = min(nd, c0 + kChunk);
+    const int c0 = c * kWChunk, c1 = min(nd, c0 + kWChunk);
+    const bool more = nd > 0 && c + 1 < nchunks;
     if (nd > 0) {
-      if (tid == 0 && c + 1 < nchunks) {
-        fence_proxy_async();
-        const int n1 = min(nd - c1, kChunk);
-        bulk_load(buf[(c + 1) & 1], A.dl + dr.x + c1, (uint32_t)n1 * sizeof(DEntry),
-                  &bars[(c + 1) & 1]);
+      if (more) {
+        __syncwarp();  // every lane is done with the buffer about to be refilled
+        if (lane == 0) {
+          fence_proxy_async();
+          bulk_load(buf[(c + 1) & 1], A.dl + g.base + c1,
+                    (uint32_t)min(nd - c1, kWChunk) * sizeof(DEntry), &bars[(c + 1) & 1]);
+        }
       }
-      if (!wait_chunk(&bars[c & 1], (uint32_t)((c >> 1) & 1), A.status)) {
-        ok = false;
+      ok = wait_buffer(bars, c & 1, phase, A.status);
+      if (!ok) break;
+    }
+    const DEntry* cb = buf[c & 1];  // record d of the strip is cb[d - c0]
+    bool finished = false;
+    while (k < re) {
+      if (!__any_sync(0xffffffffu, !(p0.done && p1.done))) {
+        finished = true;
         break;
       }
-    }
-    const DEntry* cb = buf[c & 1];  // record d of the tile is cb[d - c0]
-    while (k < re && __any_sync(0xffffffffu, !(p0.done && p1.done))) {
+      if (k >= kb + 32) {
+        kb = k;
+        load_batch<STROKE>(A, kb, min(32, re - kb), st, ib);
+      }
+      const int j = k - kb;
       IMeta m;
-      load_meta(A.meta + k, m);
-      const int ds = m.dstart, de = m.dstart + m.dcount;
+      batch_meta(ib, j, m);
+      const int2 rg = ib.rg[j];
+      const int ds = rg.x, de = rg.x + rg.y;
       if (!mid) {
         p0.md = p1.md = 1e30f;
         p0.w = p0.n = p1.w = p1.n = 0;
@@ -312,7 +434,7 @@ __global__ void __launch_bounds__(kRT) raster_forward_kernel(const RasterArgs A)
         break;
       }
       if (!STROKE) {
-        const int ro = __ldg(A.rowoff + (long long)k * 16 + ly);
+        const int ro = batch_rowoff(ib, j);
         const int rw = row_wind(ro), rc = row_cnt(ro);
         p0.w += rw; p1.w += rw; p0.n += rc; p1.n += rc;
       }
@@ -321,8 +443,14 @@ __global__ void __launch_bounds__(kRT) raster_forward_kernel(const RasterArgs A)
       mid = false;
       ++k;
     }
-    __syncthreads();  // this chunk's buffer may be refilled
+    if (finished || k >= re) {
+      if (more) {  // drain the prefetched chunk before the buffer is reused
+        ok = wait_buffer(bars, (c + 1) & 1, phase, A.status);
+      }
+      break;
+    }
   }
+  __syncwarp();  // the buffers are free for the next unit
   const float bg0 = A.bg[0], bg1 = A.bg[1], bg2 = A.bg[2];
   const long long hw = (long long)A.H * A.W;
   float sse = 0.0f;
@@ -353,41 +481,39 @@ __global__ void __launch_bounds__(kRT) raster_forward_kernel(const RasterArgs A)
     }
   }
   if (A.loss_tgt) {
-    // per-CTA partial; the last CTA to finish reduces them in a fixed order
-    __shared__ float red[kRT / 32];
-    __shared__ bool last;
     sse = warp_sum(sse);
-    if (lane == 0) red[tid >> 5] = sse;
-    __syncthreads();
-    const unsigned nblk = gridDim.x * gridDim.y;
-    if (tid == 0) {
-      float bsum = 0.0f;
-#pragma unroll
-      for (int w = 0; w < kRT / 32; ++w) bsum += red[w];
-      // indexed by tile, so the fixed-order reduction does not depend on the
-      // dispatch order
-      A.loss_partials[(ty - A.r0) * A.tbx + tx] = bsum;
-      __threadfence();
-      last = atomicAdd(A.loss_ticket, 1u) == nblk - 1;
-    }
-    __syncthreads();
-    if (last) {
-      __threadfence();
-      float v = 0.0f;
-      for (unsigned q = tid; q < nblk; q += kRT) v += A.loss_partials[q];
-      v = warp_sum(v);
-      if (lane == 0) red[tid >> 5] = v;
-      __syncthreads();
-      if (tid == 0) {
-        float t = 0.0f;
-#pragma unroll
-        for (int w = 0; w < kRT / 32; ++w) t += red[w];
-        A.loss_out[0] = t;
-        A.loss_out[1] = t / (3.0f * (float)A.H * (float)A.W);
-        *A.loss_ticket = 0u;
-      }
-    }
+    if (lane == 0) A.partials[unit] = sse;  // indexed by unit: a fixed reduction order
   }
+  return ok;
+}
+
+template <bool STROKE>
+__global__ void __launch_bounds__(kRT) raster_forward_kernel(const RasterArgs A) {
+  __shared__ __align__(128) DEntry sbuf[kRW][2][kWChunk];
+  __shared__ __align__(16) IBatch sib[kRW];
+  __shared__ __align__(8) uint64_t sbar[kRW][2];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  uint64_t* bars = sbar[wid];
+  if (lane == 0) {
+    mbar_init(&bars[0]);
+    mbar_init(&bars[1]);
+    fence_barrier_init();
+  }
+  __syncwarp();  // the warp's barriers are initialised before anyone waits on them
+  uint32_t phase = 0u;  // bit b: parity of the next completion of buffer b's barrier
+  int pre0 = 0, pre1 = 0;
+  if (A.order) unit_prefix(A.order, pre0, pre1);
+  int u = blockIdx.x * kRW + wid;
+  while (u < A.nunits) {
+    const int unit = A.order ? unit_at(A.order, A.nunits, u, pre0, pre1) : u;
+    if ((unsigned)unit >= (unsigned)A.nunits) {  // malformed dispatch lists
+      if (lane == 0 && A.status) atomicExch(A.status, CS_ERR_ARG);
+      break;
+    }
+    if (!forward_unit<STROKE>(A, unit, sbuf[wid], bars, phase, sib[wid])) break;
+    u = next_unit(A);
+  }
+  finish_launch(A, A.loss_tgt != nullptr);
 }
 
 // ---------------------------------------------------------------------------
@@ -533,23 +659,17 @@ __device__ __forceinline__ void flush_acc(const RasterArgs& A, int pid, int k, i
   else if (A.icontrib) atomicAdd(A.icontrib + k, v);
 }
 
+// Backward of one unit by one warp.  Returns false if a bounded wait gave up.
 template <bool STROKE>
-__global__ void __launch_bounds__(kRT) raster_backward_kernel(const RasterArgs A) {
-  __shared__ __align__(128) DEntry buf[2][kChunk];
-  __shared__ __align__(16) float4 dgrad[kChunk];
-  __shared__ float pacc[kPaccCap][kAcc];
-  __shared__ __align__(8) uint64_t bars[2];
-  const int tid = threadIdx.x, lane = tid & 31;
-  int tx, ty;
-  block_tile(A, tx, ty);
-  const long long tile = (long long)ty * A.tbx + tx;
-  const int rs = A.bins[2 * tile], re = A.bins[2 * tile + 1];
-  if (re <= rs) return;
-  const int2 dr = A.dlr[tile];
-  const int nd = dr.y;
-  const int nchunks = max(1, (nd + kChunk - 1) / kChunk);
-  const int ly = tid >> 3, lx = (tid & 7) * 2;
-  const int i = ty * kTile + ly, j0 = tx * kTile + lx;
+__device__ __forceinline__ bool backward_unit(const RasterArgs& A, int unit,
+                                              DEntry (*buf)[kWChunk], uint64_t* bars,
+                                              uint32_t& phase, float4* dgrad, IBatch& ib) {
+  const int lane = threadIdx.x & 31;
+  const UnitGeom g = unit_geom(A, unit);
+  const int rs = g.rs, re = g.re, st = g.st;
+  if (re <= rs) return true;
+  const int ly = st * kStripRows + (lane >> 3), lx = (lane & 7) * 2;
+  const int i = g.ty * kTile + ly, j0 = g.tx * kTile + lx;
   const float py = (float)i + 0.5f;
   const float px[2] = {(float)j0 + 0.5f, (float)(j0 + 1) + 0.5f};
   const bool collect = (A.contrib != nullptr) | (A.icontrib != nullptr);
@@ -597,33 +717,35 @@ __global__ void __launch_bounds__(kRT) raster_backward_kernel(const RasterArgs A
     s[u].Tf = s[u].T;
   }
   kmax = min(warp_max_i(kmax), re - 1);  // this warp's last needed intersect
-  for (int q = tid; q < kPaccCap * kAcc; q += kRT) (&pacc[0][0])[q] = 0.0f;
-  for (int q = tid; q < kChunk; q += kRT) dgrad[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (kmax < rs) return true;
+  const int nd = strip_records_upto(A, kmax, st);  // records of intersects <= kmax
+  const int nchunks = max(1, (nd + kWChunk - 1) / kWChunk);
   const int last = nchunks - 1;
-  if (tid == 0 && nd > 0) {
-    mbar_init(&bars[0]);
-    mbar_init(&bars[1]);
-    fence_barrier_init();
-    const int c0 = last * kChunk;
-    bulk_load(buf[last & 1], A.dl + dr.x + c0, (uint32_t)(nd - c0) * sizeof(DEntry),
+  if (nd > 0 && lane == 0) {
+    const int c0 = last * kWChunk;
+    bulk_load(buf[last & 1], A.dl + g.base + c0, (uint32_t)(nd - c0) * sizeof(DEntry),
               &bars[last & 1]);
   }
-  __syncthreads();
-  int k = kmax;       // next intersect of this warp (walking down)
+  int k = kmax;       // next intersect (walking down)
+  int kb = kmax + 1;  // first intersect of the batch in shared memory (batch: kb .. kb + 31)
   bool mid = false;   // k partially visited
+  bool ok = true;
   for (int c = last; c >= 0; --c) {
-    const int c0 = c * kChunk, c1 = min(nd, c0 + kChunk);
+    const int c0 = c * kWChunk, c1 = min(nd, c0 + kWChunk);
+    const bool more = nd > 0 && c > 0;
     if (nd > 0) {
-      if (tid == 0 && c > 0) {
-        fence_proxy_async();
-        bulk_load(buf[(c - 1) & 1], A.dl + dr.x + (c - 1) * kChunk,
-                  (uint32_t)kChunk * sizeof(DEntry), &bars[(c - 1) & 1]);
+      if (more) {
+        __syncwarp();  // every lane is done with the buffer about to be refilled
+        if (lane == 0) {
+          fence_proxy_async();
+          bulk_load(buf[(c - 1) & 1], A.dl + g.base + (c - 1) * kWChunk,
+                    (uint32_t)kWChunk * sizeof(DEntry), &bars[(c - 1) & 1]);
+        }
       }
-      // buffer b is used by chunks b, b+2, ...; walking down from `last`, this
-      // is use number (last - c) / 2 of buffer c & 1
-      if (!wait_chunk(&bars[c & 1], (uint32_t)(((last - c) >> 1) & 1), A.status)) return;
+      ok = wait_buffer(bars, c & 1, phase, A.status);
+      if (!ok) break;
     }
-    const DEntry* cb = buf[c & 1];  // record d of the tile is cb[d - c0]
+    const DEntry* cb = buf[c & 1];  // record d of the strip is cb[d - c0]
     while (k >= rs) {
       const bool v0 = s[0].in && k <= s[0].fidx;
       const bool v1 = s[1].in && k <= s[1].fidx;
@@ -632,9 +754,15 @@ __global__ void __launch_bounds__(kRT) raster_backward_kernel(const RasterArgs A
         mid = false;
         continue;
       }
+      if (k < kb) {
+        kb = max(rs, k - 31);
+        load_batch<STROKE>(A, kb, k - kb + 1, st, ib);
+      }
+      const int j = k - kb;
       IMeta m;
-      load_meta(A.meta + k, m);
-      const int ds = m.dstart, de = m.dstart + m.dcount;
+      batch_meta(ib, j, m);
+      const int2 rg = ib.rg[j];
+      const int ds = rg.x, de = rg.x + rg.y;
       if (!mid) {
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
@@ -664,7 +792,7 @@ __global__ void __launch_bounds__(kRT) raster_backward_kernel(const RasterArgs A
         break;
       }
       if (!STROKE) {
-        const int ro = __ldg(A.rowoff + (long long)k * 16 + ly);
+        const int ro = batch_rowoff(ib, j);
         const int rw = row_wind(ro), rc = row_cnt(ro);
         s[0].w += rw; s[1].w += rw; s[0].n += rc; s[1].n += rc;
       }
@@ -679,60 +807,113 @@ __global__ void __launch_bounds__(kRT) raster_backward_kernel(const RasterArgs A
         bwd_pixel<STROKE>(s[u], m, px[u], py, u ? v1 : v0, acc, collect, eg, has_eg, contributed);
         if (has_eg) {
           if (s[u].bl >= 0) {
-            float4* g = &dgrad[s[u].bl - c0];
-            atomicAdd(&g->x, eg.x);
-            atomicAdd(&g->y, eg.y);
-            atomicAdd(&g->z, eg.z);
-            atomicAdd(&g->w, eg.w);
+            float4* gp = &dgrad[s[u].bl - c0];
+            atomicAdd(&gp->x, eg.x);
+            atomicAdd(&gp->y, eg.y);
+            atomicAdd(&gp->z, eg.z);
+            atomicAdd(&gp->w, eg.w);
           } else {
-            float* g = A.v_edges + (long long)s[u].be * 4;
-            atomicAdd(g, eg.x);
-            atomicAdd(g + 1, eg.y);
-            atomicAdd(g + 2, eg.z);
-            atomicAdd(g + 3, eg.w);
+            float* gp = A.v_edges + (long long)s[u].be * 4;
+            atomicAdd(gp, eg.x);
+            atomicAdd(gp + 1, eg.y);
+            atomicAdd(gp + 2, eg.z);
+            atomicAdd(gp + 3, eg.w);
           }
         }
       }
       if (__any_sync(0xffffffffu, contributed)) {
-        const int kl = k - rs;
 #pragma unroll
         for (int q = 0; q < kAcc; ++q) {
+          if (q == 3 && !A.v_opac) continue;
+          if (q == 4 && !A.v_inv) continue;
           if (q == 5 && !STROKE) continue;
           if (q >= 6 && !collect) continue;
           const float v = warp_sum(acc[q]);
-          if (lane == 0 && v != 0.0f) {
-            if (kl < kPaccCap) atomicAdd(&pacc[kl][q], v);
-            else flush_acc(A, m.pid, k, q, v);
-          }
+          if (lane == 0) flush_acc(A, m.pid, k, q, v);
         }
       }
       mid = false;
       --k;
     }
-    __syncthreads();
-    // flush this chunk's edge gradients while its records are still resident
-    for (int d = c0 + tid; d < c1; d += kRT) {
-      const float4 g = dgrad[d - c0];
-      if (g.x == 0.0f && g.y == 0.0f && g.z == 0.0f && g.w == 0.0f) continue;
+    __syncwarp();
+    // flush this chunk's edge gradients while its records are resident
+    for (int d = c0 + lane; d < c1; d += 32) {
+      const float4 gv = dgrad[d - c0];
+      if (gv.x == 0.0f && gv.y == 0.0f && gv.z == 0.0f && gv.w == 0.0f) continue;
       float* dst = A.v_edges + (long long)__float_as_int(cb[d - c0].b.w) * 4;
-      atomicAdd(dst, g.x);
-      atomicAdd(dst + 1, g.y);
-      atomicAdd(dst + 2, g.z);
-      atomicAdd(dst + 3, g.w);
+      atomicAdd(dst, gv.x);
+      atomicAdd(dst + 1, gv.y);
+      atomicAdd(dst + 2, gv.z);
+      atomicAdd(dst + 3, gv.w);
       dgrad[d - c0] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    __syncthreads();
+    __syncwarp();
+    if (k < rs) {
+      if (more) {  // drain the prefetched chunk before the buffer is reused
+        ok = wait_buffer(bars, (c - 1) & 1, phase, A.status);
+      }
+      break;
+    }
   }
-  const int np = min(re - rs, kPaccCap);
-  for (int q = tid; q < np * kAcc; q += kRT) {
-    const int kl = q / kAcc, c = q - kl * kAcc;
-    const float v = pacc[kl][c];
-    if (v != 0.0f) flush_acc(A, A.pids[rs + kl], rs + kl, c, v);
+  __syncwarp();
+  return ok;
+}
+
+template <bool STROKE>
+__global__ void __launch_bounds__(kRT) raster_backward_kernel(const RasterArgs A) {
+  __shared__ __align__(128) DEntry sbuf[kRW][2][kWChunk];
+  __shared__ __align__(16) float4 sgrad[kRW][kWChunk];
+  __shared__ __align__(16) IBatch sib[kRW];
+  __shared__ __align__(8) uint64_t sbar[kRW][2];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  uint64_t* bars = sbar[wid];
+  float4* dgrad = sgrad[wid];
+  for (int q = lane; q < kWChunk; q += 32) dgrad[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (lane == 0) {
+    mbar_init(&bars[0]);
+    mbar_init(&bars[1]);
+    fence_barrier_init();
   }
+  __syncwarp();
+  uint32_t phase = 0u;
+  int pre0 = 0, pre1 = 0;
+  if (A.order) unit_prefix(A.order, pre0, pre1);
+  int u = blockIdx.x * kRW + wid;
+  while (u < A.nunits) {
+    const int unit = A.order ? unit_at(A.order, A.nunits, u, pre0, pre1) : u;
+    if ((unsigned)unit >= (unsigned)A.nunits) {  // malformed dispatch lists
+      if (lane == 0 && A.status) atomicExch(A.status, CS_ERR_ARG);
+      break;
+    }
+    if (!backward_unit<STROKE>(A, unit, sbuf[wid], bars, phase, dgrad, sib[wid])) break;
+    u = next_unit(A);
+  }
+  finish_launch(A, false);
 }
 
 // ---------------------------------------------------------------------------
-// host launch helper
+// host launch
+
+// Persistent grid: as many CTAs as fit on the device at once (cached per
+// kernel and device), no more than the units need.  ID tells the kernels
+// apart (they share one function type).
+template <int ID, typename K>
+inline int persistent_ctas(K kernel, int nunits) {
+  constexpr int kMaxDev = 64;
+  static int sms[kMaxDev] = {0};
+  static int occ[kMaxDev] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) dev = 0;
+  if (sms[dev] == 0) {
+    int n = 0, o = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, kernel, kRT, 0);
+    occ[dev] = max(1, o);
+    sms[dev] = max(1, n);
+  }
+  const int need = (nunits + kRW - 1) / kRW;
+  return max(1, min(need, sms[dev] * occ[dev]));
+}
 
 inline int launch_raster(bool stroke, bool bwd, const RasterArgs& a, int H, int W, int r_begin,
                          int r_end, cudaStream_t st) {
@@ -744,27 +925,41 @@ inline int launch_raster(bool stroke, bool bwd, const RasterArgs& a, int H, int 
   args.r0 = r0;
   args.H = H;
   args.W = W;
-  dim3 grid(tbx, r1 - r0);
-  if (!stroke && !bwd) raster_forward_kernel<false><<<grid, kRT, 0, st>>>(args);
-  if (stroke && !bwd) raster_forward_kernel<true><<<grid, kRT, 0, st>>>(args);
-  if (!stroke && bwd) raster_backward_kernel<false><<<grid, kRT, 0, st>>>(args);
-  if (stroke && bwd) raster_backward_kernel<true><<<grid, kRT, 0, st>>>(args);
+  args.nunits = kStrips * tbx * (r1 - r0);
+  if (!stroke && !bwd) {
+    auto k = raster_forward_kernel<false>;
+    k<<<persistent_ctas<0>(k, args.nunits), kRT, 0, st>>>(args);
+  } else if (stroke && !bwd) {
+    auto k = raster_forward_kernel<true>;
+    k<<<persistent_ctas<1>(k, args.nunits), kRT, 0, st>>>(args);
+  } else if (!stroke && bwd) {
+    auto k = raster_backward_kernel<false>;
+    k<<<persistent_ctas<2>(k, args.nunits), kRT, 0, st>>>(args);
+  } else {
+    auto k = raster_backward_kernel<true>;
+    k<<<persistent_ctas<3>(k, args.nunits), kRT, 0, st>>>(args);
+  }
   return launch_status();
 }
 
 inline void stage_args(RasterArgs& a, const int32_t* prim_ids_sorted, const int32_t* tile_bins,
-                       const int32_t* tile_dlist, const void* imeta, const int32_t* rowoff,
-                       const void* dlist, const int32_t* tile_order, const float* background,
-                       int32_t* status) {
-  a.order = tile_order;
+                       const int32_t* tile_dlist, const void* imeta, const int32_t* isect_strips,
+                       const int32_t* rowoff, const void* dlist, const int32_t* unit_order,
+                       const float* background, int32_t* status, void* workspace) {
   a.pids = prim_ids_sorted;
   a.bins = tile_bins;
   a.dlr = reinterpret_cast<const int2*>(tile_dlist);
   a.meta = reinterpret_cast<const IMeta*>(imeta);
+  a.istrip = reinterpret_cast<const int2*>(isect_strips);
   a.rowoff = rowoff;
   a.dl = reinterpret_cast<const DEntry*>(dlist);
+  a.order = unit_order;
   a.bg = background;
   a.status = status;
+  char* w = static_cast<char*>(workspace);
+  a.queue = reinterpret_cast<unsigned*>(w);
+  a.ticket = reinterpret_cast<unsigned*>(w + 4);
+  a.partials = reinterpret_cast<float*>(w + 256);
 }
 
 }  // namespace cs
@@ -773,84 +968,82 @@ using namespace cs;
 
 extern "C" {
 
+size_t cs_raster_workspace_size(int64_t num_tiles) {
+  return 256 + sizeof(float) * (size_t)kStrips * (size_t)(num_tiles > 0 ? num_tiles : 1);
+}
+
 static int raster_forward(bool stroke, const int32_t* prim_ids_sorted, const int32_t* tile_bins,
-                          const int32_t* tile_dlist, const void* imeta, const int32_t* rowoff,
-                          const void* dlist, const int32_t* tile_order, const float* background,
-                          float* out_img,
+                          const int32_t* tile_dlist, const void* imeta,
+                          const int32_t* isect_strips, const int32_t* rowoff, const void* dlist,
+                          const int32_t* unit_order, const float* background, float* out_img,
                           float* final_Ts, int32_t* final_idx, float* out_chw_clamped,
-                          const float* target_chw, float* loss_out, void* loss_ws,
-                          int32_t* status, int32_t img_height, int32_t img_width,
+                          const float* target_chw, float* loss_out, int32_t* status,
+                          void* workspace, int32_t img_height, int32_t img_width,
                           int32_t tile_row_begin, int32_t tile_row_end, void* stream) {
-  if (img_height <= 0 || img_width <= 0 || !tile_bins || !tile_dlist || !imeta || !dlist ||
-      !background || !out_img || !final_Ts || !final_idx || (!stroke && !rowoff) ||
-      (target_chw && (!loss_out || !loss_ws)))
+  if (img_height <= 0 || img_width <= 0 || !tile_bins || !tile_dlist || !imeta || !isect_strips ||
+      !dlist || !background || !out_img || !final_Ts || !final_idx || !workspace ||
+      (!stroke && !rowoff) || (target_chw && !loss_out))
     return CS_ERR_ARG;
   RasterArgs a{};
-  stage_args(a, prim_ids_sorted, tile_bins, tile_dlist, imeta, rowoff, dlist, tile_order, background,
-             status);
+  stage_args(a, prim_ids_sorted, tile_bins, tile_dlist, imeta, isect_strips, rowoff, dlist,
+             unit_order, background, status, workspace);
   a.out = out_img;
   a.fts = final_Ts;
   a.fidx = final_idx;
   a.out_chw = out_chw_clamped;
   a.loss_tgt = target_chw;
   a.loss_out = loss_out;
-  a.loss_ticket = static_cast<unsigned int*>(loss_ws);
-  a.loss_partials = reinterpret_cast<float*>(static_cast<char*>(loss_ws) + 256);
   return launch_raster(stroke, false, a, img_height, img_width, tile_row_begin, tile_row_end,
                        (cudaStream_t)stream);
 }
 
-size_t cs_loss_workspace_size(int64_t num_tiles) {
-  return 256 + sizeof(float) * (size_t)(num_tiles > 0 ? num_tiles : 1);
-}
-
 int cs_fill_forward(const int32_t* prim_ids_sorted, const int32_t* tile_bins,
-                    const int32_t* tile_dlist, const void* imeta, const int32_t* rowoff,
-                    const void* dlist, const int32_t* tile_order, const float* background,
-                    float* out_img, float* final_Ts,
+                    const int32_t* tile_dlist, const void* imeta, const int32_t* isect_strips,
+                    const int32_t* rowoff, const void* dlist, const int32_t* unit_order,
+                    const float* background, float* out_img, float* final_Ts,
                     int32_t* final_idx, float* out_chw_clamped, const float* target_chw,
-                    float* loss_out, void* loss_ws, int32_t* status, int32_t img_height,
+                    float* loss_out, int32_t* status, void* workspace, int32_t img_height,
                     int32_t img_width, int32_t tile_row_begin, int32_t tile_row_end,
                     void* stream) {
-  return raster_forward(false, prim_ids_sorted, tile_bins, tile_dlist, imeta, rowoff, dlist,
-                        tile_order, background, out_img, final_Ts, final_idx, out_chw_clamped, target_chw,
-                        loss_out, loss_ws, status, img_height, img_width, tile_row_begin,
-                        tile_row_end, stream);
+  return raster_forward(false, prim_ids_sorted, tile_bins, tile_dlist, imeta, isect_strips,
+                        rowoff, dlist, unit_order, background, out_img, final_Ts, final_idx,
+                        out_chw_clamped, target_chw, loss_out, status, workspace, img_height,
+                        img_width, tile_row_begin, tile_row_end, stream);
 }
 
 int cs_stroke_forward(const int32_t* prim_ids_sorted, const int32_t* tile_bins,
-                      const int32_t* tile_dlist, const void* imeta, const void* dlist,
-                      const int32_t* tile_order, const float* background, float* out_img,
-                      float* final_Ts,
-                      int32_t* final_idx, float* out_chw_clamped, const float* target_chw,
-                      float* loss_out, void* loss_ws, int32_t* status, int32_t img_height,
-                      int32_t img_width, int32_t tile_row_begin, int32_t tile_row_end,
-                      void* stream) {
-  return raster_forward(true, prim_ids_sorted, tile_bins, tile_dlist, imeta, nullptr, dlist,
-                        tile_order, background, out_img, final_Ts, final_idx, out_chw_clamped, target_chw,
-                        loss_out, loss_ws, status, img_height, img_width, tile_row_begin,
-                        tile_row_end, stream);
+                      const int32_t* tile_dlist, const void* imeta, const int32_t* isect_strips,
+                      const void* dlist, const int32_t* unit_order, const float* background,
+                      float* out_img, float* final_Ts, int32_t* final_idx,
+                      float* out_chw_clamped, const float* target_chw, float* loss_out,
+                      int32_t* status, void* workspace, int32_t img_height, int32_t img_width,
+                      int32_t tile_row_begin, int32_t tile_row_end, void* stream) {
+  return raster_forward(true, prim_ids_sorted, tile_bins, tile_dlist, imeta, isect_strips,
+                        nullptr, dlist, unit_order, background, out_img, final_Ts, final_idx,
+                        out_chw_clamped, target_chw, loss_out, status, workspace, img_height,
+                        img_width, tile_row_begin, tile_row_end, stream);
 }
 
 static int raster_backward(bool stroke, const int32_t* prim_ids_sorted, const int32_t* tile_bins,
-                           const int32_t* tile_dlist, const void* imeta, const int32_t* rowoff,
-                           const void* dlist, const int32_t* tile_order, const float* background,
-                           const float* final_Ts,
-                           const int32_t* final_idx, const float* v_output, const float* out_img,
-                           const float* target_chw, const float* mse_scale, float* v_edges,
-                           float* v_colors, float* v_opacities, float* v_stroke_widths,
-                           float* v_inv_sigma2s, float* curve_contrib_rgb,
-                           float* curve_isect_contrib, int32_t* status, int32_t img_height,
+                           const int32_t* tile_dlist, const void* imeta,
+                           const int32_t* isect_strips, const int32_t* rowoff, const void* dlist,
+                           const int32_t* unit_order, const float* background,
+                           const float* final_Ts, const int32_t* final_idx,
+                           const float* v_output, const float* out_img, const float* target_chw,
+                           const float* mse_scale, float* v_edges, float* v_colors,
+                           float* v_opacities, float* v_stroke_widths, float* v_inv_sigma2s,
+                           float* curve_contrib_rgb, float* curve_isect_contrib,
+                           int32_t* status, void* workspace, int32_t img_height,
                            int32_t img_width, int32_t tile_row_begin, int32_t tile_row_end,
                            void* stream) {
   if (img_height <= 0 || img_width <= 0 || !prim_ids_sorted || !tile_bins || !tile_dlist ||
-      !imeta || !dlist || !background || !final_Ts || !final_idx || !v_edges || !v_colors ||
-      (!stroke && !rowoff) || (stroke && !v_stroke_widths))
+      !imeta || !isect_strips || !dlist || !background || !final_Ts || !final_idx || !v_edges ||
+      !v_colors || !workspace || (!stroke && !rowoff) || (stroke && !v_stroke_widths))
     return CS_ERR_ARG;
   if (!v_output && (!out_img || !target_chw || !mse_scale)) return CS_ERR_ARG;
   RasterArgs a{};
-  stage_args(a, prim_ids_sorted, tile_bins, tile_dlist, imeta, rowoff, dlist, tile_order, background,
-             status);
+  stage_args(a, prim_ids_sorted, tile_bins, tile_dlist, imeta, isect_strips, rowoff, dlist,
+             unit_order, background, status, workspace);
   a.fts_in = final_Ts;
   a.fidx_in = final_idx;
   a.v_out = v_output;
@@ -869,37 +1062,38 @@ static int raster_backward(bool stroke, const int32_t* prim_ids_sorted, const in
 }
 
 int cs_fill_backward(const int32_t* prim_ids_sorted, const int32_t* tile_bins,
-                     const int32_t* tile_dlist, const void* imeta, const int32_t* rowoff,
-                     const void* dlist, const int32_t* tile_order, const float* background,
-                     const float* final_Ts,
-                     const int32_t* final_idx, const float* v_output, const float* out_img,
-                     const float* target_chw, const float* mse_scale, float* v_edges,
-                     float* v_colors, float* v_opacities, float* v_inv_sigma2s,
-                     float* curve_contrib_rgb, float* curve_isect_contrib, int32_t* status,
+                     const int32_t* tile_dlist, const void* imeta, const int32_t* isect_strips,
+                     const int32_t* rowoff, const void* dlist, const int32_t* unit_order,
+                     const float* background, const float* final_Ts, const int32_t* final_idx,
+                     const float* v_output, const float* out_img, const float* target_chw,
+                     const float* mse_scale, float* v_edges, float* v_colors,
+                     float* v_opacities, float* v_inv_sigma2s, float* curve_contrib_rgb,
+                     float* curve_isect_contrib, int32_t* status, void* workspace,
                      int32_t img_height, int32_t img_width, int32_t tile_row_begin,
                      int32_t tile_row_end, void* stream) {
-  return raster_backward(false, prim_ids_sorted, tile_bins, tile_dlist, imeta, rowoff, dlist,
-                         tile_order, background, final_Ts, final_idx, v_output, out_img, target_chw,
-                         mse_scale, v_edges, v_colors, v_opacities, nullptr, v_inv_sigma2s,
-                         curve_contrib_rgb, curve_isect_contrib, status, img_height, img_width,
-                         tile_row_begin, tile_row_end, stream);
+  return raster_backward(false, prim_ids_sorted, tile_bins, tile_dlist, imeta, isect_strips,
+                         rowoff, dlist, unit_order, background, final_Ts, final_idx, v_output,
+                         out_img, target_chw, mse_scale, v_edges, v_colors, v_opacities, nullptr,
+                         v_inv_sigma2s, curve_contrib_rgb, curve_isect_contrib, status,
+                         workspace, img_height, img_width, tile_row_begin, tile_row_end, stream);
 }
 
 int cs_stroke_backward(const int32_t* prim_ids_sorted, const int32_t* tile_bins,
-                       const int32_t* tile_dlist, const void* imeta, const void* dlist,
-                       const int32_t* tile_order, const float* background, const float* final_Ts,
-                       const int32_t* final_idx,
-                       const float* v_output, const float* out_img, const float* target_chw,
-                       const float* mse_scale, float* v_edges, float* v_colors,
-                       float* v_opacities, float* v_stroke_widths, float* v_inv_sigma2s,
-                       float* curve_contrib_rgb, float* curve_isect_contrib, int32_t* status,
+                       const int32_t* tile_dlist, const void* imeta, const int32_t* isect_strips,
+                       const void* dlist, const int32_t* unit_order, const float* background,
+                       const float* final_Ts, const int32_t* final_idx, const float* v_output,
+                       const float* out_img, const float* target_chw, const float* mse_scale,
+                       float* v_edges, float* v_colors, float* v_opacities,
+                       float* v_stroke_widths, float* v_inv_sigma2s, float* curve_contrib_rgb,
+                       float* curve_isect_contrib, int32_t* status, void* workspace,
                        int32_t img_height, int32_t img_width, int32_t tile_row_begin,
                        int32_t tile_row_end, void* stream) {
-  return raster_backward(true, prim_ids_sorted, tile_bins, tile_dlist, imeta, nullptr, dlist,
-                         tile_order, background, final_Ts, final_idx, v_output, out_img, target_chw,
-                         mse_scale, v_edges, v_colors, v_opacities, v_stroke_widths,
-                         v_inv_sigma2s, curve_contrib_rgb, curve_isect_contrib, status,
-                         img_height, img_width, tile_row_begin, tile_row_end, stream);
+  return raster_backward(true, prim_ids_sorted, tile_bins, tile_dlist, imeta, isect_strips,
+                         nullptr, dlist, unit_order, background, final_Ts, final_idx, v_output,
+                         out_img, target_chw, mse_scale, v_edges, v_colors, v_opacities,
+                         v_stroke_widths, v_inv_sigma2s, curve_contrib_rgb, curve_isect_contrib,
+                         status, workspace, img_height, img_width, tile_row_begin, tile_row_end,
+                         stream);
 }
 
 }  // extern "C"

@@ -1,16 +1,21 @@
 // Per-tile staging records shared by the binning kernels (writers) and the
 // raster kernels (readers).
 //
-// For every tile, the edges of its intersects are classified once per frame
-// against the tile's pixel-centre box (see raster.cu for why this is exact):
-//   * near edges become 32-byte DEntry records, compacted in (intersect, edge)
-//     order into one contiguous per-tile range of the D-list, so a raster CTA
-//     brings a whole tile's geometry into shared memory with one bulk copy;
+// A 16x16 tile is rasterised as kStrips strips of kStripRows pixel rows, one
+// warp per strip.  For every tile, the edges of its intersects are classified
+// once per frame against each strip's pixel-centre box (see raster.cu for why
+// this is exact):
+//   * an edge within the primitive's culling distance of a strip becomes a
+//     32-byte DEntry record in that strip's list; each strip's list is
+//     compacted in (intersect, edge) order into its own contiguous range of
+//     the D-list, so a raster warp brings its strip's geometry into shared
+//     memory with bulk copies;
 //   * far edges that cross tile rows while lying entirely right of the tile
 //     become per-row winding offsets (fill mode);
 //   * all other edges are dropped.
 // Each intersect also gets a 48-byte IMeta record with its primitive's
-// colour, opacity, softness and culling distance.
+// colour, opacity, softness and culling distance, and per strip the range
+// (first record, record count) of its records in the strip's list.
 #pragma once
 
 #include <math_constants.h>
@@ -24,9 +29,12 @@ struct __align__(16) DEntry {
   float4 b;  // 1 / max(vx^2 + vy^2, eps), y1, x0 * vy, edge id (int bits)
 };
 
+constexpr int kStrips = 4;                  // strips per tile
+constexpr int kStripRows = kTile / kStrips;  // pixel rows per strip (one warp: 4 x 16 px)
+
 struct __align__(16) IMeta {
-  int dstart;  // first DEntry of this intersect, relative to the tile's range
-  int dcount;  // number of DEntry records
+  int dstart;  // unused (0): per-strip ranges are kept beside the records
+  int dcount;  // unused (0)
   int pid;     // primitive id
   int rule;    // fill rule (0 even-odd, else nonzero); 1 for strokes
   float c0, c1, c2, op;
@@ -92,6 +100,36 @@ __device__ __forceinline__ bool edge_is_near(const float4& e, float d, float bx0
          (xmax >= bx0 - d && xmin <= bx1 + d && ymax >= by0 - d && ymin <= by1 + d);
 }
 
+// Bit s set when the edge comes within d of strip s's pixel-centre box
+// [bx0, bx0+15] x [by0 + 4s, by0 + 4s + 3]; the union over strips is
+// edge_is_near for the whole tile.
+__device__ __forceinline__ unsigned edge_near_strips(const float4& e, float d, float bx0,
+                                                     float by0) {
+  const float bx1 = bx0 + 15.0f;
+  const bool moderate = fabsf(e.x) < 4.0e6f && fabsf(e.y) < 4.0e6f && fabsf(e.z) < 4.0e6f &&
+                        fabsf(e.w) < 4.0e6f;
+  if (!moderate) return (1u << kStrips) - 1u;
+  const float xmin = fminf(e.x, e.z), xmax = fmaxf(e.x, e.z);
+  if (!(xmax >= bx0 - d && xmin <= bx1 + d)) return 0u;
+  const float ymin = fminf(e.y, e.w), ymax = fmaxf(e.y, e.w);
+  unsigned m = 0u;
+#pragma unroll
+  for (int st = 0; st < kStrips; ++st) {
+    const float sy0 = by0 + (float)(st * kStripRows), sy1 = sy0 + (float)(kStripRows - 1);
+    if (ymax >= sy0 - d && ymin <= sy1 + d) m |= 1u << st;
+  }
+  return m;
+}
+
+// Rows (bits of a 16-bit tile row mask) of the strips in strip mask m.
+__device__ __forceinline__ unsigned strip_rows(unsigned m) {
+  unsigned r = 0u;
+#pragma unroll
+  for (int st = 0; st < kStrips; ++st)
+    if (m & (1u << st)) r |= ((1u << kStripRows) - 1u) << (st * kStripRows);
+  return r;
+}
+
 // Far edge entirely right of the box that spans some of its rows: it crosses
 // every pixel of row r when y0 <= py < y1 or y1 <= py < y0 (py = by0 + r), far
 // beyond rounding error of the reference's crossing test.
@@ -114,6 +152,48 @@ __device__ __forceinline__ DEntry make_entry(const float4& e, int eid) {
   d.a = make_float4(e.x, e.y, vx, vy);
   d.b = make_float4(1.0f / fmaxf(vv, kEps), e.w, e.x * vy, __int_as_float(eid));
   return d;
+}
+
+// Dispatch lists of raster work units ("unit lists"): int32 [kUnitBuckets +
+// kUnitBuckets * nunits]: the count of every work bucket, then one list of
+// capacity nunits per bucket.  The staging pass appends every unit to the
+// bucket of its work estimate (two buckets per octave, heaviest first, no
+// work last); the raster kernels take units bucket by bucket.  The order
+// within a bucket is arbitrary: it affects scheduling only.
+constexpr int kUnitBuckets = 64;
+
+__device__ __forceinline__ int work_bucket(int w) {
+  if (w <= 0) return kUnitBuckets - 1;
+  const int msb = 31 - __clz(w);
+  const int half = msb >= 1 ? (w >> (msb - 1)) & 1 : 0;
+  return (kUnitBuckets - 2) - min(2 * msb + half, kUnitBuckets - 2);
+}
+
+__device__ __forceinline__ void append_unit(int* lists, int nunits, int unit, int weight) {
+  const int b = work_bucket(weight);
+  const int pos = atomicAdd(lists + b, 1);
+  lists[kUnitBuckets + (long long)b * nunits + pos] = unit;
+}
+
+// Unit at dispatch position u (u < nunits), for a warp whose lane l holds the
+// exclusive prefix counts pre0 = start of bucket 2l and pre1 = start of 2l+1.
+__device__ __forceinline__ int unit_at(const int* lists, int nunits, int u, int pre0, int pre1) {
+  const unsigned q = __ballot_sync(0xffffffffu, pre0 <= u);  // bit 0 is always set
+  const int L = 31 - __clz(q);
+  const int p0 = __shfl_sync(0xffffffffu, pre0, L), p1 = __shfl_sync(0xffffffffu, pre1, L);
+  const int b = 2 * L + (p1 <= u ? 1 : 0);
+  const int base = p1 <= u ? p1 : p0;
+  return __ldg(lists + kUnitBuckets + (long long)b * nunits + (u - base));
+}
+
+// Per-lane bucket starts for unit_at (one warp).
+__device__ __forceinline__ void unit_prefix(const int* lists, int& pre0, int& pre1) {
+  const int lane = threadIdx.x & 31;
+  const int c0 = __ldg(lists + 2 * lane), c1 = __ldg(lists + 2 * lane + 1);
+  const int pair = c0 + c1;
+  const int incl = warp_incl_scan(pair, lane);
+  pre0 = incl - pair;
+  pre1 = pre0 + c0;
 }
 
 }  // namespace cs

@@ -125,7 +125,8 @@ class Binning:
     dlist: torch.Tensor
     counters: torch.Tensor
     stroke: bool
-    tile_order: Optional[torch.Tensor] = None  # heaviest-first dispatch order of the band
+    isect_strips: torch.Tensor                  # [I, 4, 2] per-strip record ranges
+    unit_order: Optional[torch.Tensor] = None   # heaviest-first strip order of the band
 
 
 def _offsets_error(offs: torch.Tensor, num_segments: int) -> ValueError:
@@ -165,7 +166,6 @@ def bin_primitives(cubics_norm: torch.Tensor, offs: torch.Tensor, depths: torch.
     tile_bins = torch.empty((nt, 2), dtype=torch.int32, device=dev)
     tile_dlist = torch.empty((nt, 2), dtype=torch.int32, device=dev)
     counters = torch.zeros((4,), dtype=torch.int32, device=dev)
-    tile_order = torch.empty((max(0, r1 - r0) * tbx,), dtype=torch.int32, device=dev)
     ws = torch.empty((int(nat.call("cs_bin_workspace_size", nt)),), dtype=torch.uint8, device=dev)
     st = nat.stream(dev)
     cn = _f32(cubics_norm)
@@ -175,8 +175,7 @@ def bin_primitives(cubics_norm: torch.Tensor, offs: torch.Tensor, depths: torch.
     nat.check(nat.call("cs_bin_count", nat.ptr(cn), nat.ptr(offs), nat.ptr(aw), nat.ptr(sw),
                        nat.ptr(basis), nat.ptr(cubics_px), nat.ptr(edges), nat.ptr(prim_ranges),
                        nat.ptr(num_hit), nat.ptr(tile_bins), nat.ptr(tile_dlist),
-                       nat.ptr(tile_order), nat.ptr(counters), ws.data_ptr(), p, g, INT64_MAX,
-                       INT64_MAX, s,
+                       nat.ptr(counters), ws.data_ptr(), p, g, INT64_MAX, INT64_MAX, s,
                        int(img_h), int(img_w), r0, r1, float(aabb_pad), int(bool(aniso)), st),
               "cs_bin_count")
     # the one host synchronisation of the forward: sizes + status
@@ -190,6 +189,9 @@ def bin_primitives(cubics_norm: torch.Tensor, offs: torch.Tensor, depths: torch.
     imeta = torch.empty((max(n_isect, 1), 12), dtype=torch.int32, device=dev)
     rowoff = None if stroke else torch.empty((max(n_isect, 1), 16), dtype=torch.int32, device=dev)
     dlist = torch.empty((max(n_dbound, 1), 8), dtype=torch.float32, device=dev)
+    istrips = torch.empty((max(n_isect, 1), 4, 2), dtype=torch.int32, device=dev)
+    unit_order = torch.empty((int(nat.call("cs_unit_lists_size", max(1, r1 - r0) * tbx)) // 4,),
+                             dtype=torch.int32, device=dev)
     if n_isect > 0:
         nat.check(nat.call("cs_bin_sort", nat.ptr(prim_ranges), nat.ptr(_f32(depths)),
                            nat.ptr(tile_bins), nat.ptr(prim_sorted), nat.ptr(isect_sorted),
@@ -197,10 +199,11 @@ def bin_primitives(cubics_norm: torch.Tensor, offs: torch.Tensor, depths: torch.
                            r0, r1, nat.ptr(edges), nat.ptr(edge_offs), nat.ptr(colors),
                            nat.ptr(opacities), nat.ptr(inv_sigma2s), nat.ptr(fill_rules),
                            nat.ptr(sw), nat.ptr(tile_dlist), nat.ptr(imeta), nat.ptr(rowoff),
-                           nat.ptr(dlist), max(n_dbound, 1), st), "cs_bin_sort")
+                           nat.ptr(istrips), nat.ptr(dlist), max(n_dbound, 1),
+                           nat.ptr(unit_order), st), "cs_bin_sort")
     return Binning(cubics_px, edges, edge_offs, prim_ranges, num_hit, tile_bins, prim_sorted,
                    isect_sorted, n_isect, (tbx, tby, 1), s, (r0, r1), tile_dlist, imeta, rowoff,
-                   dlist, counters, stroke, tile_order)
+                   dlist, counters, stroke, istrips, unit_order if n_isect > 0 else None)
 
 
 def stage_reference_lists(prim_ids_sorted, tile_bins, edges_px, isect_edge_ranges, colors,
@@ -214,28 +217,49 @@ def stage_reference_lists(prim_ids_sorted, tile_bins, edges_px, isect_edge_range
     n = int(prim_ids_sorted.numel())
     stroke = stroke_widths is not None
     if isect_edge_ranges is not None:
-        bound = int((isect_edge_ranges[:, 1] - isect_edge_ranges[:, 0]).clamp_min(0).sum().item())
+        slots = int((isect_edge_ranges[:, 1] - isect_edge_ranges[:, 0]).clamp_min(0).sum().item())
     else:
         eo = prim_edge_offsets.to(torch.int64)
         pid = prim_ids_sorted.to(torch.int64)
-        bound = int((eo[pid + 1] - eo[pid]).clamp_min(0).sum().item())
+        slots = int((eo[pid + 1] - eo[pid]).clamp_min(0).sum().item())
+    bound = 4 * slots  # every strip of a tile has room for all of the tile's edge slots
     tile_dlist = torch.empty((nt, 2), dtype=torch.int32, device=dev)
     counters = torch.zeros((4,), dtype=torch.int32, device=dev)
     imeta = torch.empty((max(n, 1), 12), dtype=torch.int32, device=dev)
     rowoff = None if stroke else torch.empty((max(n, 1), 16), dtype=torch.int32, device=dev)
     dlist = torch.empty((max(bound, 1), 8), dtype=torch.float32, device=dev)
+    istrips = torch.empty((max(n, 1), 4, 2), dtype=torch.int32, device=dev)
+    unit_order = torch.empty((int(nat.call("cs_unit_lists_size", nt)) // 4,), dtype=torch.int32,
+                             device=dev)
     ws = torch.empty((int(nat.call("cs_stage_workspace_size", nt)),), dtype=torch.uint8,
                      device=dev)
     nat.check(nat.call("cs_tile_stage", nat.ptr(prim_ids_sorted), nat.ptr(tile_bins),
                        nat.ptr(edges_px), nat.ptr(isect_edge_ranges), nat.ptr(prim_edge_offsets),
                        nat.ptr(colors), nat.ptr(opacities), nat.ptr(inv_sigma2s),
                        nat.ptr(fill_rules), nat.ptr(stroke_widths), nat.ptr(tile_dlist),
-                       nat.ptr(imeta), nat.ptr(rowoff), nat.ptr(dlist), nat.ptr(counters),
-                       ws.data_ptr(), max(bound, 1), int(img_h), int(img_w), nat.stream(dev)),
+                       nat.ptr(imeta), nat.ptr(rowoff), nat.ptr(istrips), nat.ptr(dlist),
+                       nat.ptr(unit_order), nat.ptr(counters), ws.data_ptr(), max(bound, 1),
+                       int(img_h), int(img_w), nat.stream(dev)),
               "cs_tile_stage")
     return Binning(None, edges_px, prim_edge_offsets, None, None, tile_bins, prim_ids_sorted,
                    None, n, (tbx, tby, 1), 0, (0, tby), tile_dlist, imeta, rowoff, dlist, counters,
-                   stroke)
+                   stroke, istrips, unit_order)
+
+
+_RASTER_WS: dict = {}
+
+
+def raster_workspace(device: torch.device, num_tiles: int) -> torch.Tensor:
+    """Per-device workspace of the raster kernels (dispatch counter, completion
+    ticket, per-strip loss partials).  It is zeroed when allocated and every
+    launch leaves it zeroed, so launches in stream order share it."""
+    key = str(device)
+    need = int(nat.call("cs_raster_workspace_size", int(num_tiles)))
+    buf = _RASTER_WS.get(key)
+    if buf is None or buf.numel() < need:
+        buf = torch.zeros((need,), dtype=torch.uint8, device=device)
+        _RASTER_WS[key] = buf
+    return buf
 
 
 def _inv_sigma2(widths: torch.Tensor) -> torch.Tensor:
@@ -270,19 +294,20 @@ def forward_raster(b: Binning, background, img_h: int, img_w: int, out_chw=None,
         return out, fts, fidx
     st = nat.stream(dev)
     status = b.counters[1:2]
+    ws = raster_workspace(dev, b.tile_bounds[0] * b.tile_bounds[1])
     if not b.stroke:
         nat.check(nat.call("cs_fill_forward", nat.ptr(b.prim_ids_sorted), nat.ptr(b.tile_bins),
-                           nat.ptr(b.tile_dlist), nat.ptr(b.imeta), nat.ptr(b.rowoff),
-                           nat.ptr(b.dlist), nat.ptr(b.tile_order), nat.ptr(background),
-                           nat.ptr(out), nat.ptr(fts),
-                           nat.ptr(fidx), nat.ptr(out_chw), None, None, None, nat.ptr(status),
+                           nat.ptr(b.tile_dlist), nat.ptr(b.imeta), nat.ptr(b.isect_strips),
+                           nat.ptr(b.rowoff), nat.ptr(b.dlist), nat.ptr(b.unit_order),
+                           nat.ptr(background), nat.ptr(out), nat.ptr(fts), nat.ptr(fidx),
+                           nat.ptr(out_chw), None, None, nat.ptr(status), ws.data_ptr(),
                            img_h, img_w, b.tile_rows[0], b.tile_rows[1], st), "cs_fill_forward")
     else:
         nat.check(nat.call("cs_stroke_forward", nat.ptr(b.prim_ids_sorted), nat.ptr(b.tile_bins),
-                           nat.ptr(b.tile_dlist), nat.ptr(b.imeta), nat.ptr(b.dlist),
-                           nat.ptr(b.tile_order), nat.ptr(background), nat.ptr(out),
-                           nat.ptr(fts), nat.ptr(fidx),
-                           nat.ptr(out_chw), None, None, None, nat.ptr(status), img_h, img_w,
+                           nat.ptr(b.tile_dlist), nat.ptr(b.imeta), nat.ptr(b.isect_strips),
+                           nat.ptr(b.dlist), nat.ptr(b.unit_order), nat.ptr(background),
+                           nat.ptr(out), nat.ptr(fts), nat.ptr(fidx), nat.ptr(out_chw), None,
+                           None, nat.ptr(status), ws.data_ptr(), img_h, img_w,
                            b.tile_rows[0], b.tile_rows[1], st), "cs_stroke_forward")
     return out, fts, fidx
 
@@ -320,26 +345,29 @@ def raster_backward(b: Binning, num_primitives: int, background, final_ts, final
         st = nat.stream(dev)
         vo = None if v_output is None else _f32(v_output)
         status = b.counters[1:2]
+        ws = raster_workspace(dev, b.tile_bounds[0] * b.tile_bounds[1])
         if not b.stroke:
             nat.check(nat.call("cs_fill_backward", nat.ptr(b.prim_ids_sorted), nat.ptr(b.tile_bins),
-                               nat.ptr(b.tile_dlist), nat.ptr(b.imeta), nat.ptr(b.rowoff),
-                               nat.ptr(b.dlist), nat.ptr(b.tile_order), nat.ptr(background),
-                               nat.ptr(final_ts),
+                               nat.ptr(b.tile_dlist), nat.ptr(b.imeta),
+                               nat.ptr(b.isect_strips), nat.ptr(b.rowoff), nat.ptr(b.dlist),
+                               nat.ptr(b.unit_order), nat.ptr(background), nat.ptr(final_ts),
                                nat.ptr(final_idx), nat.ptr(vo), nat.ptr(out_img),
                                nat.ptr(target_chw), nat.ptr(mse_scale), nat.ptr(v_edges),
                                nat.ptr(v_colors), nat.ptr(v_opac), nat.ptr(v_inv),
-                               nat.ptr(contrib), nat.ptr(icontrib), nat.ptr(status), img_h, img_w,
-                               b.tile_rows[0], b.tile_rows[1], st), "cs_fill_backward")
+                               nat.ptr(contrib), nat.ptr(icontrib), nat.ptr(status),
+                               ws.data_ptr(), img_h, img_w, b.tile_rows[0], b.tile_rows[1], st),
+                      "cs_fill_backward")
         else:
             nat.check(nat.call("cs_stroke_backward", nat.ptr(b.prim_ids_sorted),
                                nat.ptr(b.tile_bins), nat.ptr(b.tile_dlist), nat.ptr(b.imeta),
-                               nat.ptr(b.dlist), nat.ptr(b.tile_order), nat.ptr(background),
-                               nat.ptr(final_ts),
+                               nat.ptr(b.isect_strips), nat.ptr(b.dlist), nat.ptr(b.unit_order),
+                               nat.ptr(background), nat.ptr(final_ts),
                                nat.ptr(final_idx), nat.ptr(vo), nat.ptr(out_img),
                                nat.ptr(target_chw), nat.ptr(mse_scale), nat.ptr(v_edges),
                                nat.ptr(v_colors), nat.ptr(v_opac), nat.ptr(v_sw), nat.ptr(v_inv),
-                               nat.ptr(contrib), nat.ptr(icontrib), nat.ptr(status), img_h,
-                               img_w, b.tile_rows[0], b.tile_rows[1], st), "cs_stroke_backward")
+                               nat.ptr(contrib), nat.ptr(icontrib), nat.ptr(status),
+                               ws.data_ptr(), img_h, img_w, b.tile_rows[0], b.tile_rows[1], st),
+                      "cs_stroke_backward")
     return v_edges, v_colors, v_opac, v_inv, v_sw, contrib, icontrib
 
 

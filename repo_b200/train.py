@@ -99,13 +99,15 @@ class FillTrainer:
         self.num_hit = torch.empty((p,), device=dev, dtype=i32)
         self.tile_bins = torch.empty((nt, 2), device=dev, dtype=i32)
         self.tile_dlist = torch.empty((nt, 2), device=dev, dtype=i32)
-        self.tile_order = torch.empty((max(1, (self.tile_rows[1] - self.tile_rows[0]) * tbx),),
+        # dispatch lists of the band's strips (4 per tile), heaviest bucket first
+        band_tiles = max(1, (self.tile_rows[1] - self.tile_rows[0]) * tbx)
+        self.unit_order = torch.empty((int(nat.call("cs_unit_lists_size", band_tiles)) // 4,),
                                       device=dev, dtype=i32)
         # intersects, sticky status, staged-record bound, unused
         self.counters = torch.zeros((4,), device=dev, dtype=i32)
         self.bin_ws = torch.empty((int(nat.call("cs_bin_workspace_size", nt)),), device=dev,
                                   dtype=torch.uint8)
-        self.loss_ws = torch.zeros((int(nat.call("cs_loss_workspace_size", nt)),), device=dev,
+        self.raster_ws = torch.zeros((int(nat.call("cs_raster_workspace_size", nt)),), device=dev,
                                    dtype=torch.uint8)
         self.out = torch.empty((self.h, self.w, 3), device=dev, dtype=f32)
         self.img_chw = torch.zeros((3, self.h, self.w), device=dev, dtype=f32)
@@ -126,6 +128,7 @@ class FillTrainer:
         self.isect_sorted = torch.empty((self.capacity,), device=dev, dtype=torch.int64)
         self.imeta = torch.empty((self.capacity, 12), device=dev, dtype=i32)
         self.rowoff = torch.empty((self.capacity, 16), device=dev, dtype=i32)
+        self.istrips = torch.empty((self.capacity, 4, 2), device=dev, dtype=i32)
         self.dlist = torch.empty((self.dcapacity, 8), device=dev, dtype=f32)
         self.graph: Optional[torch.cuda.CUDAGraph] = None
         self.launches_per_step = 8 + (1 if self.with_ssim else 0)
@@ -143,8 +146,7 @@ class FillTrainer:
                            self.cubics_px.data_ptr(), self.edges.data_ptr(),
                            self.prim_ranges.data_ptr(), self.num_hit.data_ptr(),
                            self.tile_bins.data_ptr(), self.tile_dlist.data_ptr(),
-                           self.tile_order.data_ptr(), self.counters.data_ptr(),
-                           self.bin_ws.data_ptr(), self.num_paths,
+                           self.counters.data_ptr(), self.bin_ws.data_ptr(), self.num_paths,
                            self.num_segments, capacity, dcapacity, self.s, self.h, self.w, r0, r1,
                            float(_render.DEFAULT_AABB_PAD), 0, st), "cs_bin_count")
 
@@ -155,7 +157,7 @@ class FillTrainer:
         self._params_to_cubics(st)
         self._bin(INT64_MAX, INT64_MAX, st)
         n, _, nd, _ = (int(v) for v in self.counters.tolist())
-        return int(math.ceil(n * slack)) + extra, int(math.ceil(nd * slack)) + 16 * extra
+        return int(math.ceil(n * slack)) + extra, int(math.ceil(nd * slack)) + 64 * extra
 
     def forward_backward(self):
         """Enqueue one forward + loss + backward; no host synchronisation."""
@@ -171,16 +173,17 @@ class FillTrainer:
                            r0, r1, self.edges.data_ptr(), self.edge_offs.data_ptr(),
                            self.colors.data_ptr(), self.opac.data_ptr(), self.inv_s2.data_ptr(),
                            self.rules.data_ptr(), None, self.tile_dlist.data_ptr(),
-                           self.imeta.data_ptr(), self.rowoff.data_ptr(), self.dlist.data_ptr(),
-                           self.dcapacity, st), "cs_bin_sort")
+                           self.imeta.data_ptr(), self.rowoff.data_ptr(), self.istrips.data_ptr(),
+                           self.dlist.data_ptr(), self.dcapacity, self.unit_order.data_ptr(), st),
+                  "cs_bin_sort")
         nat.check(nat.call("cs_fill_forward", self.prim_sorted.data_ptr(),
                            self.tile_bins.data_ptr(), self.tile_dlist.data_ptr(),
-                           self.imeta.data_ptr(), self.rowoff.data_ptr(), self.dlist.data_ptr(),
-                           self.tile_order.data_ptr(), self.bg.data_ptr(), self.out.data_ptr(),
-                           self.fts.data_ptr(),
-                           self.fidx.data_ptr(), self.img_chw.data_ptr(), self.target.data_ptr(),
-                           self.loss.data_ptr(), self.loss_ws.data_ptr(), status, self.h, self.w,
-                           r0, r1, st), "cs_fill_forward")
+                           self.imeta.data_ptr(), self.istrips.data_ptr(), self.rowoff.data_ptr(),
+                           self.dlist.data_ptr(), self.unit_order.data_ptr(), self.bg.data_ptr(),
+                           self.out.data_ptr(), self.fts.data_ptr(), self.fidx.data_ptr(),
+                           self.img_chw.data_ptr(), self.target.data_ptr(), self.loss.data_ptr(),
+                           status, self.raster_ws.data_ptr(), self.h, self.w, r0, r1, st),
+                  "cs_fill_forward")
         if self.with_ssim:
             nat.check(nat.call("cs_ssim", self.img_chw.data_ptr(), self.target.data_ptr(),
                                self.gauss.data_ptr(), 3, self.h, self.w, 11, 0.01 ** 2, 0.03 ** 2,
@@ -188,13 +191,13 @@ class FillTrainer:
                       "cs_ssim")
         nat.check(nat.call("cs_fill_backward", self.prim_sorted.data_ptr(),
                            self.tile_bins.data_ptr(), self.tile_dlist.data_ptr(),
-                           self.imeta.data_ptr(), self.rowoff.data_ptr(), self.dlist.data_ptr(),
-                           self.tile_order.data_ptr(), self.bg.data_ptr(), self.fts.data_ptr(),
-                           self.fidx.data_ptr(), None,
-                           self.out.data_ptr(), self.target.data_ptr(),
-                           self.mse_scale.data_ptr(), self.v_edges.data_ptr(),
-                           self.v_colors.data_ptr(), None, None, None, None, status, self.h,
-                           self.w, r0, r1, st), "cs_fill_backward")
+                           self.imeta.data_ptr(), self.istrips.data_ptr(), self.rowoff.data_ptr(),
+                           self.dlist.data_ptr(), self.unit_order.data_ptr(), self.bg.data_ptr(),
+                           self.fts.data_ptr(), self.fidx.data_ptr(), None, self.out.data_ptr(),
+                           self.target.data_ptr(), self.mse_scale.data_ptr(),
+                           self.v_edges.data_ptr(), self.v_colors.data_ptr(), None, None, None,
+                           None, status, self.raster_ws.data_ptr(), self.h, self.w, r0, r1, st),
+                  "cs_fill_backward")
         nat.check(nat.call("cs_edge_grads_to_ring", self.v_edges.data_ptr(),
                            self.v_ring.data_ptr(), self.num_paths, self.g_per_path, self.s - 1,
                            self.h, self.w, 1, st), "cs_edge_grads_to_ring")

@@ -94,3 +94,13 @@ def test_scenes_are_deterministic():
     assert a.num_paths == 512 and a.cubics_norm().shape == (2048, 4, 2)
     assert scenes.config3().cubics_norm().shape == (4096 * 6, 4, 2)
     assert len(set(a.depths.tolist())) == 512
+
+
+def test_workspace_and_list_sizes():
+    """Sizes the host allocates from: raster workspace (dispatch counter,
+    ticket, one loss partial per strip) and unit lists (64 bucket counts, one
+    list of all of the band's strips per bucket)."""
+    from repo_b200 import _native as nat
+    for nt in (1, 7, 1536):
+        assert nat.call("cs_unit_lists_size", nt) == 4 * (64 + 64 * 4 * nt)
+        assert nat.call("cs_raster_workspace_size", nt) == 256 + 4 * 4 * nt

@@ -353,7 +353,8 @@ def test_bad_offsets_raise_value_error():
 
 
 def test_primitive_larger_than_staging_capacity_is_split():
-    # one path of 48 segments x 23 edges = 1104 edges > 512 staged per batch
+    # one path of 48 segments x 23 edges = 1104 edges: a strip sees more of its
+    # records than one warp buffer holds (64), so intersects span buffer chunks
     gen = torch.Generator().manual_seed(9)
     g = 48
     centre = torch.tensor([[40.0, 30.0]])
@@ -417,7 +418,10 @@ def test_tile_row_bands_stitch_to_full_image():
 
 
 @pytest.mark.parametrize("rows", [None, (2, 9)])
-def test_tile_order_is_heaviest_first_permutation_and_changes_no_result(rows):
+def test_unit_lists_bucket_every_strip_by_work_and_change_no_result(rows):
+    """The staging pass files the band's strips (4 per tile) into 64 buckets of
+    staged work, heaviest first; the lists only schedule the raster warps, so
+    results match the launch without them."""
     import dataclasses
     sc = scenes.config1()
     args = fill_inputs(sc)
@@ -425,17 +429,33 @@ def test_tile_order_is_heaviest_first_permutation_and_changes_no_result(rows):
     b, inv, out, fts, fidx = gpu_fill(*args, tile_rows=rows)
     tbx = (w + 15) // 16
     r0, r1 = b.tile_rows
-    order = _np(b.tile_order)
-    assert sorted(order.tolist()) == list(range((r1 - r0) * tbx))
-    # work estimate of every band tile: 8 per intersect + its primitives' edges
+    nunits = 4 * (r1 - r0) * tbx
+    lists = _np(b.unit_order)
+    counts = lists[:64]
+    assert counts.sum() == nunits
+    # work estimate of every strip: 2 per staged record + 5 per intersect of its tile
     bins = _np(b.tile_bins)[r0 * tbx:r1 * tbx]
-    eoffs = _np(b.prim_edge_offsets).astype(np.int64)
-    ne = (eoffs[1:] - eoffs[:-1])[_np(b.prim_ids_sorted)]
-    cum = np.concatenate([[0], np.cumsum(ne)])
-    est = 8 * (bins[:, 1] - bins[:, 0]) + (cum[bins[:, 1]] - cum[bins[:, 0]])
-    bucket = np.array([int(v).bit_length() for v in est[order]])
-    assert np.all(np.diff(bucket) <= 0), "tiles are dispatched by decreasing work bucket"
-    plain = dataclasses.replace(b, tile_order=None)
+    strips = _np(b.isect_strips)
+    est = np.zeros(nunits, np.int64)
+    for t in range(len(bins)):
+        rs, re = bins[t]
+        if re > rs:
+            for st in range(4):
+                est[4 * t + st] = 2 * int(strips[re - 1, st].sum()) + 5 * (re - rs)
+
+    def bucket(v):  # two buckets per octave, heaviest first, no work last
+        if v <= 0:
+            return 63
+        msb = int(v).bit_length() - 1
+        half = (v >> (msb - 1)) & 1 if msb >= 1 else 0
+        return 62 - min(2 * msb + half, 62)
+    seen = []
+    for bk in range(64):
+        members = lists[64 + bk * nunits: 64 + bk * nunits + counts[bk]]
+        assert all(bucket(est[u]) == bk for u in members), bk
+        seen.extend(members.tolist())
+    assert sorted(seen) == list(range(nunits))
+    plain = dataclasses.replace(b, unit_order=None)
     out2, fts2, fidx2 = render.forward_raster(plain, _t(args[7], torch.float32), h, w)
     band = slice(r0 * 16, min(h, r1 * 16))  # rows outside the band are not written
     assert torch.equal(out[band], out2[band]) and torch.equal(fts[band], fts2[band])

@@ -169,7 +169,10 @@ CS_API int cs_tile_stage(const int32_t *prim_ids_sorted, const int32_t *tile_bin
  * minimum distance to the primitive's polyline, sigmoid soft coverage, then
  * front-to-back alpha compositing with early termination.  Input is the
  * staged data of cs_bin_sort / cs_tile_stage (tile_dlist, imeta,
- * isect_strips, rowoff, dlist; unit_order may be NULL).  out_chw_clamped
+ * isect_strips, rowoff, dlist; unit_order may be NULL).  unit_order_bwd (may
+ * be NULL; cs_unit_lists_size bytes) receives the same units bucketed by the
+ * work this launch measured, the better dispatch order for the backward.
+ * out_chw_clamped
  * [3, H, W] (may be NULL) also receives clamp(out, 0, 1) channel-major, the
  * image the training loss sees (the reference does torch.clamp + permute,
  * manbo/gaussian_trace/render.py:1309-1310).  status (device int, may be NULL)
@@ -188,11 +191,11 @@ CS_API size_t cs_raster_workspace_size(int64_t num_tiles);
 CS_API int cs_fill_forward(const int32_t *prim_ids_sorted, const int32_t *tile_bins,
                     const int32_t *tile_dlist, const void *imeta, const int32_t *isect_strips,
                     const int32_t *rowoff, const void *dlist, const int32_t *unit_order,
-                    const float *background, float *out_img, float *final_Ts,
-                    int32_t *final_idx, float *out_chw_clamped, const float *target_chw,
-                    float *loss_out, int32_t *status, void *workspace, int32_t img_height,
-                    int32_t img_width, int32_t tile_row_begin, int32_t tile_row_end,
-                    void *stream);
+                    int32_t *unit_order_bwd, const float *background, float *out_img,
+                    float *final_Ts, int32_t *final_idx, float *out_chw_clamped,
+                    const float *target_chw, float *loss_out, int32_t *status,
+                    void *workspace, int32_t img_height, int32_t img_width,
+                    int32_t tile_row_begin, int32_t tile_row_end, void *stream);
 
 /* Closed-fill backward: reverse compositing from final_idx, gradients of the
  * colours, opacities, 1/sigma^2 and edge endpoints (closest edge only).
@@ -220,9 +223,10 @@ CS_API int cs_fill_backward(const int32_t *prim_ids_sorted, const int32_t *tile_
  * cubic_polyline_splatting.py:33-249. */
 CS_API int cs_stroke_forward(const int32_t *prim_ids_sorted, const int32_t *tile_bins,
                       const int32_t *tile_dlist, const void *imeta, const int32_t *isect_strips,
-                      const void *dlist, const int32_t *unit_order, const float *background,
-                      float *out_img, float *final_Ts, int32_t *final_idx,
-                      float *out_chw_clamped, const float *target_chw, float *loss_out,
+                      const void *dlist, const int32_t *unit_order, int32_t *unit_order_bwd,
+                      const float *background, float *out_img, float *final_Ts,
+                      int32_t *final_idx, float *out_chw_clamped, const float *target_chw,
+                      float *loss_out,
                       int32_t *status, void *workspace, int32_t img_height, int32_t img_width,
                       int32_t tile_row_begin, int32_t tile_row_end, void *stream);
 

@@ -410,7 +410,7 @@ __global__ void __launch_bounds__(256) bin_scatter_kernel(
 }
 
 constexpr int kSortThreads = 256;   // one CTA per tile for the sort and the staging
-constexpr int kSortSmem = 4096;
+constexpr int kSortSmem = 4096;     // pairs sorted in shared memory (more: rank sort)
 constexpr int kStageU = 2;          // edge slots per thread per staging round
 
 __device__ __forceinline__ void emit_sorted(unsigned long long v, long long tile, long long pos,

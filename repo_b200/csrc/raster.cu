@@ -52,6 +52,7 @@ struct RasterArgs {
   const int* rowoff;     // [I][16] packed row winding offsets (fill)
   const DEntry* dl;
   const int* order;      // optional unit lists (stage.cuh), heaviest bucket first
+  int* order_next;       // forward: optional unit lists for the backward, by measured work
   const float* bg;
   int H, W, tbx, r0, nunits;
   int* status;
@@ -374,7 +375,7 @@ __device__ __forceinline__ void fwd_composite(FwdPix& p, const IMeta& m, int k) 
 template <bool STROKE>
 __device__ __forceinline__ bool forward_unit(const RasterArgs& A, int unit,
                                              DEntry (*buf)[kWChunk], uint64_t* bars,
-                                             uint32_t& phase, IBatch& ib) {
+                                             uint32_t& phase, IBatch& ib, int& work) {
   const int lane = threadIdx.x & 31;
   const UnitGeom g = unit_geom(A, unit);
   const int rs = g.rs, re = g.re, st = g.st;
@@ -391,6 +392,7 @@ __device__ __forceinline__ bool forward_unit(const RasterArgs& A, int unit,
     bulk_load(buf[0], A.dl + g.base, (uint32_t)min(nd, kWChunk) * sizeof(DEntry), &bars[0]);
   int k = rs;          // next intersect
   int kb = rs - 32;    // first intersect of the batch in shared memory
+  int recs = 0;        // records visited (a work measure for the backward's dispatch)
   bool mid = false;    // k partially visited (split across chunks)
   bool ok = true;
   for (int c = 0; c < nchunks; ++c) {
@@ -429,6 +431,7 @@ __device__ __forceinline__ bool forward_unit(const RasterArgs& A, int unit,
         p0.w = p0.n = p1.w = p1.n = 0;
       }
       fwd_entries<STROKE>(cb, c0, max(ds, c0), min(de, c1), px0, px1, py, p0, p1);
+      recs += max(0, min(de, c1) - max(ds, c0));
       if (de > c1) {
         mid = true;
         break;
@@ -484,6 +487,8 @@ __device__ __forceinline__ bool forward_unit(const RasterArgs& A, int unit,
     sse = warp_sum(sse);
     if (lane == 0) A.partials[unit] = sse;  // indexed by unit: a fixed reduction order
   }
+  // the backward visits about the same intersects and records
+  work = k > rs ? 2 * recs + 8 * (k - rs + (k < re ? 1 : 0)) : 0;
   return ok;
 }
 
@@ -510,7 +515,10 @@ __global__ void __launch_bounds__(kRT) raster_forward_kernel(const RasterArgs A)
       if (lane == 0 && A.status) atomicExch(A.status, CS_ERR_ARG);
       break;
     }
-    if (!forward_unit<STROKE>(A, unit, sbuf[wid], bars, phase, sib[wid])) break;
+    int work = 0;
+    const bool ok = forward_unit<STROKE>(A, unit, sbuf[wid], bars, phase, sib[wid], work);
+    if (A.order_next && lane == 0) append_unit(A.order_next, A.nunits, unit, work);
+    if (!ok) break;
     u = next_unit(A);
   }
   finish_launch(A, A.loss_tgt != nullptr);
@@ -975,11 +983,12 @@ size_t cs_raster_workspace_size(int64_t num_tiles) {
 static int raster_forward(bool stroke, const int32_t* prim_ids_sorted, const int32_t* tile_bins,
                           const int32_t* tile_dlist, const void* imeta,
                           const int32_t* isect_strips, const int32_t* rowoff, const void* dlist,
-                          const int32_t* unit_order, const float* background, float* out_img,
-                          float* final_Ts, int32_t* final_idx, float* out_chw_clamped,
-                          const float* target_chw, float* loss_out, int32_t* status,
-                          void* workspace, int32_t img_height, int32_t img_width,
-                          int32_t tile_row_begin, int32_t tile_row_end, void* stream) {
+                          const int32_t* unit_order, int32_t* unit_order_bwd,
+                          const float* background, float* out_img, float* final_Ts,
+                          int32_t* final_idx, float* out_chw_clamped, const float* target_chw,
+                          float* loss_out, int32_t* status, void* workspace, int32_t img_height,
+                          int32_t img_width, int32_t tile_row_begin, int32_t tile_row_end,
+                          void* stream) {
   if (img_height <= 0 || img_width <= 0 || !tile_bins || !tile_dlist || !imeta || !isect_strips ||
       !dlist || !background || !out_img || !final_Ts || !final_idx || !workspace ||
       (!stroke && !rowoff) || (target_chw && !loss_out))
@@ -987,6 +996,9 @@ static int raster_forward(bool stroke, const int32_t* prim_ids_sorted, const int
   RasterArgs a{};
   stage_args(a, prim_ids_sorted, tile_bins, tile_dlist, imeta, isect_strips, rowoff, dlist,
              unit_order, background, status, workspace);
+  a.order_next = unit_order_bwd;
+  if (unit_order_bwd)
+    cudaMemsetAsync(unit_order_bwd, 0, sizeof(int32_t) * kUnitBuckets, (cudaStream_t)stream);
   a.out = out_img;
   a.fts = final_Ts;
   a.fidx = final_idx;
@@ -1000,26 +1012,27 @@ static int raster_forward(bool stroke, const int32_t* prim_ids_sorted, const int
 int cs_fill_forward(const int32_t* prim_ids_sorted, const int32_t* tile_bins,
                     const int32_t* tile_dlist, const void* imeta, const int32_t* isect_strips,
                     const int32_t* rowoff, const void* dlist, const int32_t* unit_order,
-                    const float* background, float* out_img, float* final_Ts,
+                    int32_t* unit_order_bwd, const float* background, float* out_img, float* final_Ts,
                     int32_t* final_idx, float* out_chw_clamped, const float* target_chw,
                     float* loss_out, int32_t* status, void* workspace, int32_t img_height,
                     int32_t img_width, int32_t tile_row_begin, int32_t tile_row_end,
                     void* stream) {
   return raster_forward(false, prim_ids_sorted, tile_bins, tile_dlist, imeta, isect_strips,
-                        rowoff, dlist, unit_order, background, out_img, final_Ts, final_idx,
+                        rowoff, dlist, unit_order, unit_order_bwd, background, out_img, final_Ts, final_idx,
                         out_chw_clamped, target_chw, loss_out, status, workspace, img_height,
                         img_width, tile_row_begin, tile_row_end, stream);
 }
 
 int cs_stroke_forward(const int32_t* prim_ids_sorted, const int32_t* tile_bins,
                       const int32_t* tile_dlist, const void* imeta, const int32_t* isect_strips,
-                      const void* dlist, const int32_t* unit_order, const float* background,
-                      float* out_img, float* final_Ts, int32_t* final_idx,
+                      const void* dlist, const int32_t* unit_order, int32_t* unit_order_bwd,
+                      const float* background, float* out_img, float* final_Ts,
+                      int32_t* final_idx,
                       float* out_chw_clamped, const float* target_chw, float* loss_out,
                       int32_t* status, void* workspace, int32_t img_height, int32_t img_width,
                       int32_t tile_row_begin, int32_t tile_row_end, void* stream) {
   return raster_forward(true, prim_ids_sorted, tile_bins, tile_dlist, imeta, isect_strips,
-                        nullptr, dlist, unit_order, background, out_img, final_Ts, final_idx,
+                        nullptr, dlist, unit_order, unit_order_bwd, background, out_img, final_Ts, final_idx,
                         out_chw_clamped, target_chw, loss_out, status, workspace, img_height,
                         img_width, tile_row_begin, tile_row_end, stream);
 }

@@ -126,7 +126,8 @@ class Binning:
     counters: torch.Tensor
     stroke: bool
     isect_strips: torch.Tensor                  # [I, 4, 2] per-strip record ranges
-    unit_order: Optional[torch.Tensor] = None   # heaviest-first strip order of the band
+    unit_order: Optional[torch.Tensor] = None   # strip dispatch lists (staged work)
+    unit_order_bwd: Optional[torch.Tensor] = None  # strip dispatch lists (forward's work)
 
 
 def _offsets_error(offs: torch.Tensor, num_segments: int) -> ValueError:
@@ -249,6 +250,12 @@ def stage_reference_lists(prim_ids_sorted, tile_bins, edges_px, isect_edge_range
 _RASTER_WS: dict = {}
 
 
+def _bwd_lists(b: "Binning"):
+    """Dispatch lists for the backward: the forward's (measured work) when the
+    forward filled them, else the staging pass's."""
+    return b.unit_order_bwd if b.unit_order_bwd is not None else b.unit_order
+
+
 def raster_workspace(device: torch.device, num_tiles: int) -> torch.Tensor:
     """Per-device workspace of the raster kernels (dispatch counter, completion
     ticket, per-strip loss partials).  It is zeroed when allocated and every
@@ -295,18 +302,22 @@ def forward_raster(b: Binning, background, img_h: int, img_w: int, out_chw=None,
     st = nat.stream(dev)
     status = b.counters[1:2]
     ws = raster_workspace(dev, b.tile_bounds[0] * b.tile_bounds[1])
+    if b.unit_order is not None and b.unit_order_bwd is None:
+        b.unit_order_bwd = torch.empty_like(b.unit_order)
     if not b.stroke:
         nat.check(nat.call("cs_fill_forward", nat.ptr(b.prim_ids_sorted), nat.ptr(b.tile_bins),
                            nat.ptr(b.tile_dlist), nat.ptr(b.imeta), nat.ptr(b.isect_strips),
                            nat.ptr(b.rowoff), nat.ptr(b.dlist), nat.ptr(b.unit_order),
-                           nat.ptr(background), nat.ptr(out), nat.ptr(fts), nat.ptr(fidx),
+                           nat.ptr(b.unit_order_bwd), nat.ptr(background), nat.ptr(out),
+                           nat.ptr(fts), nat.ptr(fidx),
                            nat.ptr(out_chw), None, None, nat.ptr(status), ws.data_ptr(),
                            img_h, img_w, b.tile_rows[0], b.tile_rows[1], st), "cs_fill_forward")
     else:
         nat.check(nat.call("cs_stroke_forward", nat.ptr(b.prim_ids_sorted), nat.ptr(b.tile_bins),
                            nat.ptr(b.tile_dlist), nat.ptr(b.imeta), nat.ptr(b.isect_strips),
-                           nat.ptr(b.dlist), nat.ptr(b.unit_order), nat.ptr(background),
-                           nat.ptr(out), nat.ptr(fts), nat.ptr(fidx), nat.ptr(out_chw), None,
+                           nat.ptr(b.dlist), nat.ptr(b.unit_order), nat.ptr(b.unit_order_bwd),
+                           nat.ptr(background), nat.ptr(out), nat.ptr(fts), nat.ptr(fidx),
+                           nat.ptr(out_chw), None,
                            None, nat.ptr(status), ws.data_ptr(), img_h, img_w,
                            b.tile_rows[0], b.tile_rows[1], st), "cs_stroke_forward")
     return out, fts, fidx
@@ -350,7 +361,7 @@ def raster_backward(b: Binning, num_primitives: int, background, final_ts, final
             nat.check(nat.call("cs_fill_backward", nat.ptr(b.prim_ids_sorted), nat.ptr(b.tile_bins),
                                nat.ptr(b.tile_dlist), nat.ptr(b.imeta),
                                nat.ptr(b.isect_strips), nat.ptr(b.rowoff), nat.ptr(b.dlist),
-                               nat.ptr(b.unit_order), nat.ptr(background), nat.ptr(final_ts),
+                               nat.ptr(_bwd_lists(b)), nat.ptr(background), nat.ptr(final_ts),
                                nat.ptr(final_idx), nat.ptr(vo), nat.ptr(out_img),
                                nat.ptr(target_chw), nat.ptr(mse_scale), nat.ptr(v_edges),
                                nat.ptr(v_colors), nat.ptr(v_opac), nat.ptr(v_inv),
@@ -360,8 +371,8 @@ def raster_backward(b: Binning, num_primitives: int, background, final_ts, final
         else:
             nat.check(nat.call("cs_stroke_backward", nat.ptr(b.prim_ids_sorted),
                                nat.ptr(b.tile_bins), nat.ptr(b.tile_dlist), nat.ptr(b.imeta),
-                               nat.ptr(b.isect_strips), nat.ptr(b.dlist), nat.ptr(b.unit_order),
-                               nat.ptr(background), nat.ptr(final_ts),
+                               nat.ptr(b.isect_strips), nat.ptr(b.dlist),
+                               nat.ptr(_bwd_lists(b)), nat.ptr(background), nat.ptr(final_ts),
                                nat.ptr(final_idx), nat.ptr(vo), nat.ptr(out_img),
                                nat.ptr(target_chw), nat.ptr(mse_scale), nat.ptr(v_edges),
                                nat.ptr(v_colors), nat.ptr(v_opac), nat.ptr(v_sw), nat.ptr(v_inv),

@@ -103,6 +103,7 @@ class FillTrainer:
         band_tiles = max(1, (self.tile_rows[1] - self.tile_rows[0]) * tbx)
         self.unit_order = torch.empty((int(nat.call("cs_unit_lists_size", band_tiles)) // 4,),
                                       device=dev, dtype=i32)
+        self.unit_order_bwd = torch.empty_like(self.unit_order)  # filled by the forward
         # intersects, sticky status, staged-record bound, unused
         self.counters = torch.zeros((4,), device=dev, dtype=i32)
         self.bin_ws = torch.empty((int(nat.call("cs_bin_workspace_size", nt)),), device=dev,
@@ -131,6 +132,14 @@ class FillTrainer:
         self.istrips = torch.empty((self.capacity, 4, 2), device=dev, dtype=i32)
         self.dlist = torch.empty((self.dcapacity, 8), device=dev, dtype=f32)
         self.graph: Optional[torch.cuda.CUDAGraph] = None
+        # SSIM runs beside the backward at low priority, so that it takes only
+        # the SMs the backward leaves free; the step itself is captured on a
+        # high-priority stream
+        lo, hi = torch.cuda.Stream.priority_range()
+        self._side = torch.cuda.Stream(dev, priority=lo)
+        self._main = torch.cuda.Stream(dev, priority=hi)
+        self._fork = torch.cuda.Event()
+        self._join = torch.cuda.Event()
         self.launches_per_step = 8 + (1 if self.with_ssim else 0)
 
     # ------------------------------------------------------------------
@@ -179,21 +188,29 @@ class FillTrainer:
         nat.check(nat.call("cs_fill_forward", self.prim_sorted.data_ptr(),
                            self.tile_bins.data_ptr(), self.tile_dlist.data_ptr(),
                            self.imeta.data_ptr(), self.istrips.data_ptr(), self.rowoff.data_ptr(),
-                           self.dlist.data_ptr(), self.unit_order.data_ptr(), self.bg.data_ptr(),
+                           self.dlist.data_ptr(), self.unit_order.data_ptr(),
+                           self.unit_order_bwd.data_ptr(), self.bg.data_ptr(),
                            self.out.data_ptr(), self.fts.data_ptr(), self.fidx.data_ptr(),
                            self.img_chw.data_ptr(), self.target.data_ptr(), self.loss.data_ptr(),
                            status, self.raster_ws.data_ptr(), self.h, self.w, r0, r1, st),
                   "cs_fill_forward")
         if self.with_ssim:
+            # SSIM needs only the forward's image: it runs on a side stream
+            # beside the backward and fills the SMs the backward leaves idle
+            main = torch.cuda.current_stream(self.device)
+            self._fork.record(main)
+            self._side.wait_event(self._fork)
             nat.check(nat.call("cs_ssim", self.img_chw.data_ptr(), self.target.data_ptr(),
                                self.gauss.data_ptr(), 3, self.h, self.w, 11, 0.01 ** 2, 0.03 ** 2,
-                               self.ssim_planes.data_ptr(), None, self.ssim_ws.data_ptr(), st),
-                      "cs_ssim")
+                               self.ssim_planes.data_ptr(), None, self.ssim_ws.data_ptr(),
+                               self._side.cuda_stream), "cs_ssim")
+            self._join.record(self._side)
         nat.check(nat.call("cs_fill_backward", self.prim_sorted.data_ptr(),
                            self.tile_bins.data_ptr(), self.tile_dlist.data_ptr(),
                            self.imeta.data_ptr(), self.istrips.data_ptr(), self.rowoff.data_ptr(),
-                           self.dlist.data_ptr(), self.unit_order.data_ptr(), self.bg.data_ptr(),
-                           self.fts.data_ptr(), self.fidx.data_ptr(), None, self.out.data_ptr(),
+                           self.dlist.data_ptr(), self.unit_order_bwd.data_ptr(),
+                           self.bg.data_ptr(), self.fts.data_ptr(), self.fidx.data_ptr(), None,
+                           self.out.data_ptr(),
                            self.target.data_ptr(), self.mse_scale.data_ptr(),
                            self.v_edges.data_ptr(), self.v_colors.data_ptr(), None, None, None,
                            None, status, self.raster_ws.data_ptr(), self.h, self.w, r0, r1, st),
@@ -201,6 +218,8 @@ class FillTrainer:
         nat.check(nat.call("cs_edge_grads_to_ring", self.v_edges.data_ptr(),
                            self.v_ring.data_ptr(), self.num_paths, self.g_per_path, self.s - 1,
                            self.h, self.w, 1, st), "cs_edge_grads_to_ring")
+        if self.with_ssim:
+            torch.cuda.current_stream(self.device).wait_event(self._join)
 
     def optimizer_step(self):
         if self.grad_hook is not None:
@@ -224,7 +243,7 @@ class FillTrainer:
                 self.step_eager()
         torch.cuda.current_stream(self.device).wait_stream(side)
         self.graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(self.graph):
+        with torch.cuda.graph(self.graph, stream=self._main):
             self.step_eager()
         return self.graph
 

@@ -455,7 +455,12 @@ def test_unit_lists_bucket_every_strip_by_work_and_change_no_result(rows):
         assert all(bucket(est[u]) == bk for u in members), bk
         seen.extend(members.tolist())
     assert sorted(seen) == list(range(nunits))
-    plain = dataclasses.replace(b, unit_order=None)
+    # the forward files every strip once more, by its measured work, for the backward
+    bl = _np(b.unit_order_bwd)
+    assert bl[:64].sum() == nunits
+    seen_b = np.concatenate([bl[64 + bk * nunits: 64 + bk * nunits + bl[bk]] for bk in range(64)])
+    assert sorted(seen_b.tolist()) == list(range(nunits))
+    plain = dataclasses.replace(b, unit_order=None, unit_order_bwd=None)
     out2, fts2, fidx2 = render.forward_raster(plain, _t(args[7], torch.float32), h, w)
     band = slice(r0 * 16, min(h, r1 * 16))  # rows outside the band are not written
     assert torch.equal(out[band], out2[band]) and torch.equal(fts[band], fts2[band])

@@ -190,6 +190,22 @@ def raster_work(tr):
     return int(pe_fwd), int(vis_fwd), int(pe_bwd), int(vis_bwd), n
 
 
+def ncu_traffic(kernel: str):
+    """DRAM bytes (read + write) per launch of `kernel` from the committed ncu
+    summary of the config-2 raster kernels (profiles/raster_fill_config2.md),
+    or None when the summary is absent."""
+    path = os.path.join(ROOT, "profiles", "raster_fill_config2.md")
+    try:
+        with open(path) as f:
+            for line in f:
+                parts = line.split()
+                if len(parts) == 3 and parts[0] == "traffic_bytes" and parts[1] == kernel:
+                    return int(parts[2])
+    except OSError:
+        pass
+    return None
+
+
 def run_b200(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
@@ -280,7 +296,9 @@ def run_b200(args, rank, world, local_rank):
                 "kernel": "raster_backward (fill)", "bound": "fp32",
                 "achieved": round(achieved_bwd, 3), "peak": round(fp32_peak, 2),
                 "unit": "TFLOP/s", "frac": round(achieved_bwd / fp32_peak, 4),
-                "traffic": None,
+                "traffic": ncu_traffic("raster_backward_kernel"),
+                "traffic_note": "dram read+write bytes per launch from one ncu capture of "
+                                "the same workload (profiles/raster_fill_config2.md)",
                 "peak_note": "SIMT FP32 FMA peak 148 SM x 128 lanes x 2 at the sampled median SM "
                              "clock; MEASURED_PEAKS.json holds only HBM and bf16 tensor peaks",
                 "flop_per_launch": flop_bwd,

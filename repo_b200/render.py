@@ -185,12 +185,16 @@ def bin_primitives(cubics_norm: torch.Tensor, offs: torch.Tensor, depths: torch.
         raise _offsets_error(offs, g)
     nat.check(status, "cs_bin_count")
     edge_offs = (offs.to(torch.int64) * (s - 1)).to(torch.int32)
-    prim_sorted = torch.empty((n_isect,), dtype=torch.int32, device=dev)
-    isect_sorted = torch.empty((n_isect,), dtype=torch.int64, device=dev)
-    imeta = torch.empty((max(n_isect, 1), 12), dtype=torch.int32, device=dev)
-    rowoff = None if stroke else torch.empty((max(n_isect, 1), 16), dtype=torch.int32, device=dev)
-    dlist = torch.empty((max(n_dbound, 1), 8), dtype=torch.float32, device=dev)
-    istrips = torch.empty((max(n_isect, 1), 4, 2), dtype=torch.int32, device=dev)
+    # per-frame buffers are sized in a few classes (_size_class), so that the
+    # caching allocator reuses blocks from frame to frame; the sorted lists
+    # are exact-length views
+    ci, cd = _size_class(n_isect), _size_class(n_dbound)
+    prim_sorted = torch.empty((ci,), dtype=torch.int32, device=dev)[:n_isect]
+    isect_sorted = torch.empty((ci,), dtype=torch.int64, device=dev)[:n_isect]
+    imeta = torch.empty((ci, 12), dtype=torch.int32, device=dev)
+    rowoff = None if stroke else torch.empty((ci, 16), dtype=torch.int32, device=dev)
+    dlist = torch.empty((cd, 8), dtype=torch.float32, device=dev)
+    istrips = torch.empty((ci, 4, 2), dtype=torch.int32, device=dev)
     unit_order = torch.empty((int(nat.call("cs_unit_lists_size", max(1, r1 - r0) * tbx)) // 4,),
                              dtype=torch.int32, device=dev)
     if n_isect > 0:
@@ -245,6 +249,16 @@ def stage_reference_lists(prim_ids_sorted, tile_bins, edges_px, isect_edge_range
     return Binning(None, edges_px, prim_edge_offsets, None, None, tile_bins, prim_ids_sorted,
                    None, n, (tbx, tby, 1), 0, (0, tby), tile_dlist, imeta, rowoff, dlist, counters,
                    stroke, istrips, unit_order)
+
+
+def _size_class(n: int) -> int:
+    """Smallest allocation size class >= max(n, 1): multiples of 1/16 of the
+    power of two below n (at most 6.25% over), and at least 4096."""
+    n = max(int(n), 1)
+    if n <= 4096:
+        return 4096
+    step = 1 << (n.bit_length() - 5)
+    return (n + step - 1) // step * step
 
 
 _RASTER_WS: dict = {}

@@ -16,6 +16,13 @@ Multi-GPU (torchrun, N>1): every rank optimises its own config-2 scene
 (different seed), no collective on the data path; value = all ranks'
 iterations / max over ranks of the device time ("scaling": "weak").
 
+--workload config3: one 2040x1356 image with 4096 closed paths x 6 segments
+split across the ranks in tile-row bands balanced by per-row work; every step
+all-reduces the gradient buffer over NCCL inside the step's CUDA graph
+(repo_b200/bands.py); value = iterations of the one image / max device time
+("scaling": "strong").  SSIM is not part of this step (a band lacks the rows
+the SSIM window needs).
+
 --impl reference times the reference algorithm's CPU implementation (the C
 oracle restating manbo/ops/cubic_splatting.py, all host threads) on the same
 workload; the reference has no CPU renderer of its own.
@@ -48,6 +55,7 @@ def parse_args(argv=None):
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
+    ap.add_argument("--workload", default="config2", choices=["config2", "config3"])
     return ap.parse_args(argv)
 
 
@@ -314,6 +322,68 @@ def run_b200(args, rank, world, local_rank):
     return result, tr
 
 
+def run_bands(args, rank, world, local_rank):
+    """Config 3: one large image across the ranks in tile-row bands."""
+    import torch
+    import torch.distributed as dist
+
+    from repo_b200 import bands, scenes
+    from repo_b200.train import FillTrainer
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream(dev)
+    scene = scenes.config3()
+    split = bands.balanced_bands(bands.tile_row_work(scene, dev), world)
+    band = split[rank]
+    hook = bands.allreduce_hook() if world > 1 else None
+    tr = FillTrainer(scene, dev, lr_points=0.5, lr_colors=0.01, with_ssim=False,
+                     tile_rows=band if world > 1 else None, grad_hook=hook)
+    flush_buf = torch.empty((L2_FLUSH_BYTES // 4,), dtype=torch.float32, device=dev)
+
+    def flush():
+        flush_buf.zero_()
+
+    tr.capture(warmup=max(3, args.warmup))
+    for _ in range(args.warmup):
+        tr.step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    gpu_index = local_rank
+    with ClockSampler(gpu_index) as clk:
+        durs = time_steps(tr.step, args.steps, flush, stream)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    _, status = tr.check_status()
+    if status != 0:
+        raise RuntimeError(f"device status {status}")
+    t_max = torch.tensor([sum(durs)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
+    total_ms = float(t_max.item())
+    result = None
+    if rank == 0:
+        result = {
+            "metric": "fwd+bwd iters/s at 2040x1356, 4096 paths (tile-row bands)",
+            "value": round(args.steps / (total_ms / 1e3), 3), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "config3: 2040x1356 RGB, 4096 closed cubic paths x 6 segs, "
+                                   "S=16, fwd+MSE+bwd+Adam, gradient all-reduce per step",
+                       "bands": split, "parallelism": f"tile-row bands x{world}"
+                       + (" + NCCL all-reduce" if world > 1 else ""),
+                       "l2": "flushed before every step (256 MiB write), outside the step events"},
+            "final_loss": tr.loss_value(),
+            "gpu_launches": args.steps * tr.launches_per_step,
+            "clocks": clk.summary(),
+        }
+    return result, tr
+
+
 def run_e2e(scene, dev, args, flush, stream, world):
     """Training steps through the manbo API: target H2D from pinned memory and
     loss D2H every step, timed with CUDA events."""
@@ -475,6 +545,13 @@ def main(argv=None):
         dist.init_process_group("nccl", timeout=timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
     try:
+        if args.workload == "config3":
+            res, tr = run_bands(args, rank, world, local_rank)
+            if rank == 0:
+                print(json.dumps(res), flush=True)
+            tr.graph = None  # graphs holding NCCL work go before the process group
+            del tr
+            return 0
         res, tr = run_b200(args, rank, world, local_rank)
         if rank == 0 and not args.no_cpu_baseline:
             value, iters, dt, cores = run_cpu(args.cpu_seconds, 1000)

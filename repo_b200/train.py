@@ -57,6 +57,10 @@ class FillTrainer:
         self.num_tiles = nt = tbx * tby
         self.tile_rows = (0, tby) if tile_rows is None else (int(tile_rows[0]), int(tile_rows[1]))
         self.with_ssim = bool(with_ssim)
+        if self.with_ssim and self.tile_rows != (0, tby):
+            # a band renders only its own rows; SSIM's window needs the whole image
+            raise ValueError("with_ssim=True needs the whole image: pass with_ssim=False "
+                             "with tile_rows (bands)")
         self.grad_hook = grad_hook
         self.lr = (float(lr_points), float(lr_colors))
         self.betas, self.eps = (float(betas[0]), float(betas[1])), float(eps)

@@ -1,0 +1,76 @@
+"""Host logic of the multi-GPU band layout: the band split and the gradient
+all-reduce hook, the latter between two gloo ranks on the CPU."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from repo_b200.bands import allreduce_hook, balanced_bands
+
+
+def test_bands_cover_rows_once_and_in_order():
+    work = [5, 1, 1, 9, 2, 2, 2, 7, 0, 3, 4]
+    for parts in (1, 2, 3, 4, 8, 11):
+        bands = balanced_bands(work, parts)
+        assert len(bands) == parts
+        assert bands[0][0] == 0 and bands[-1][1] == len(work)
+        for (a0, a1), (b0, b1) in zip(bands, bands[1:]):
+            assert a1 == b0
+        assert all(r1 > r0 for r0, r1 in bands), "every band non-empty when rows >= parts"
+
+
+def test_bands_minimise_the_largest_band():
+    work = [1, 1, 1, 1, 10, 1, 1, 1]
+    bands = balanced_bands(work, 3)
+    loads = [sum(work[a:b]) for a, b in bands]
+    assert max(loads) == 10  # the heavy row alone; no split can do better
+    brute = min(max(sum(work[:i]), sum(work[i:j]), sum(work[j:]))
+                for i in range(1, 7) for j in range(i + 1, 8))
+    assert max(loads) == brute
+
+
+def test_more_parts_than_rows_gives_trailing_empty_bands():
+    bands = balanced_bands([3, 4], 4)
+    assert bands == [(0, 1), (1, 2), (2, 2), (2, 2)]
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port, out):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=__import__("datetime").timedelta(seconds=60))
+    try:
+        # partial gradients of all primitives + [band sse, band mse]
+        flat = torch.arange(10, dtype=torch.float32) * (rank + 1)
+        allreduce_hook()(flat)
+        out[rank] = flat.tolist()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_allreduce_hook_sums_band_gradients_across_gloo_ranks():
+    world = 2
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as mgr:
+        out = mgr.dict()
+        mp.start_processes(_rank_main, args=(world, _free_port(), out), nprocs=world,
+                           join=True, start_method="spawn")
+        want = (torch.arange(10, dtype=torch.float32) * 3).tolist()
+        assert out[0] == want and out[1] == want
+
+
+def test_trainer_refuses_ssim_on_a_band():
+    from repo_b200 import scenes
+    from repo_b200.train import FillTrainer
+    sc = scenes.small_fill_scene(1, h=64, w=64, paths=3)
+    with pytest.raises(ValueError, match="whole image"):
+        FillTrainer(sc, torch.device("cpu"), tile_rows=(0, 2))

@@ -111,3 +111,28 @@ def test_config2_training_reduces_loss():
     _, status = tr.check_status()
     assert status == 0
     assert tr.loss_value() < 0.8 * first
+
+
+def test_band_gradients_sum_to_the_full_image_gradient():
+    """The multi-GPU band layout, emulated on one GPU: each band renders its own
+    rows bit-exactly and the sum of the bands' gradient buffers (what the
+    all-reduce forms) is the full-image gradient."""
+    from repo_b200.bands import balanced_bands, tile_row_work
+    dev = torch.device("cuda")
+    sc = scenes.small_fill_scene(70, h=96, w=80, paths=14)
+    full = FillTrainer(sc, dev, with_ssim=False)
+    full.forward_backward()
+    bands = balanced_bands(tile_row_work(sc, dev), 3)
+    assert len({b for b in bands}) == 3
+    parts = [FillTrainer(sc, dev, with_ssim=False, tile_rows=b) for b in bands]
+    for t in parts:
+        t.forward_backward()
+    torch.cuda.synchronize()
+    n = full.n_params
+    total = sum(t.flat_grad for t in parts)
+    assert rel_l2(total[:n].cpu().numpy(), full.flat_grad[:n].cpu().numpy()) <= 1e-5
+    assert abs(float(total[n]) - float(full.flat_grad[n])) <= 1e-5 * float(full.flat_grad[n])
+    assert abs(float(total[n + 1]) - float(full.flat_grad[n + 1])) <= 1e-5 * float(full.flat_grad[n + 1])
+    for t, (r0, r1) in zip(parts, bands):
+        rows = slice(r0 * 16, min(sc.height, r1 * 16))
+        assert torch.equal(t.out[rows], full.out[rows])

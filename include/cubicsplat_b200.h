@@ -10,7 +10,8 @@
  *
  * Reference interfaces are cited by file:line inside the reference project
  * (manbo/ops/cubic_splatting.py, manbo/ops/cubic_polyline_splatting.py,
- * manbo/ops/tile_bins.py, manbo/ops/metric.py, manbo/metric.py).  Tiles are
+ * manbo/ops/tile_bins.py, manbo/ops/metric.py, manbo/metric.py,
+ * manbo/ops/optim.py).  Tiles are
  * 16x16 pixels as in the reference default (BLOCK_X = BLOCK_Y = 16); other
  * block sizes return CS_ERR_UNSUPPORTED.  Images are [H, W, 3] float32
  * (HWC) as the reference renderer returns them; metric inputs are [N, C, H, W].
@@ -360,6 +361,24 @@ CS_API int cs_ssim(const float *x, const float *y, const float *gauss, int64_t p
 CS_API int cs_ssim_noalloc(const float *x, const float *y, const float *gauss, int64_t planes,
             int32_t h, int32_t w, int32_t win, float c1, float c2, float *plane_means,
             float *ssim_map, void *stream);
+
+/* --------------------------------------------------------------------------
+ * Optimiser
+ * ------------------------------------------------------------------------ */
+
+/* One Adan step in place from a gradient, element by element over numel
+ * float32 values: m (exp_avg), n (exp_avg_sq), d (exp_avg_diff) and the
+ * negated previous gradient are updated, then the parameter, with decoupled
+ * (no_prox != 0) or proximal weight decay; the gradient is scaled by
+ * clip_global_grad_norm first and step == 1 starts the gradient difference at
+ * zero.  Arguments as the reference kernel's, in its order.
+ * Replaces adan_step_from_grad_kernel, manbo/ops/optim.py:8-106. */
+CS_API int cs_adan_step(float *param, const float *grad, float *exp_avg, float *exp_avg_sq,
+                 float *exp_avg_diff, float *neg_pre_grad, int64_t numel, int32_t step,
+                 float beta1, float beta2, float beta3, float bias_correction1,
+                 float bias_correction2, float bias_correction3_sqrt, float lr,
+                 float weight_decay, float eps, float clip_global_grad_norm, int32_t no_prox,
+                 void *stream);
 
 #ifdef __cplusplus
 }

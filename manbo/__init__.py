@@ -2,10 +2,11 @@
 
 Same module paths and names as the reference's ``manbo`` (manbo/__init__.py:1-29)
 for the render/optimise hot path: the cubic fill and stroke renderers, their
-per-stage operators, the ring-segment conversion and the MSE / PSNR / SSIM
-metrics.  Subsystems outside that path (Gaussian renderer, regularisation,
-connected components, Adan) keep their names so that imports succeed, and
-raise NotImplementedError when called.
+per-stage operators, the ring-segment conversion, the MSE / PSNR / SSIM
+metrics and the Adan optimiser that train.py uses by default.  Subsystems
+outside that path (Gaussian renderer, regularisation, connected components)
+keep their names so that imports succeed, and raise NotImplementedError when
+called.
 """
 from . import ops
 from .metric import mse_loss_tilelang, psnr, ssim

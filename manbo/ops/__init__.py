@@ -2,9 +2,10 @@
 
 Hot-path operators (cubic fill / stroke renderer stages, tile bins, ring
 segments, metric kernels) run on the B200 sm_100a kernels.  The Gaussian
-renderer, regularisation, connected-components and Adan operators are outside
-the B200 hot path: their names exist so imports succeed, and calling them
-raises NotImplementedError.
+renderer, regularisation and connected-components operators are outside the
+B200 hot path: their names exist so imports succeed, and calling them raises
+NotImplementedError.  The Adan step (train.py's default optimiser) runs on
+its own B200 kernel.
 """
 from .._unavailable import unavailable
 from .cubic_polyline_splatting import render_cubic_polyline_splat_tilelang
@@ -30,6 +31,7 @@ from .metric import (
     reduce_sum_partial_kernel,
     ssim_map_kernel,
 )
+from .optim import adan_step_from_grad_tilelang
 from .tile_bins import get_tile_bin_edges_tilelang
 
 _OUT_OF_SCOPE = [
@@ -42,7 +44,6 @@ _OUT_OF_SCOPE = [
     "connected_components_labels_4_tilelang",
     "connected_components_with_stats_4_tilelang",
     "select_largest_component_center",
-    "adan_step_from_grad_tilelang",
     "bezier_shape_backward_kernel",
     "bezier_open_backward_kernel",
     "opacity_backward_kernel",
@@ -90,6 +91,7 @@ __all__ = [
     "reduce_sum_partial_kernel",
     "ssim_map_kernel",
     "reduce_sum_1d_tilelang",
+    "adan_step_from_grad_tilelang",
     "DEFAULT_REG_THREADS",
     "DEFAULT_REG_ITEMS_PER_THREAD",
 ] + _OUT_OF_SCOPE

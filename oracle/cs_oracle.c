@@ -872,3 +872,38 @@ void cso_ring_segments_backward(int64_t num_curves, int k, int subdiv, const flo
 }
 
 int cso_num_threads(void) { return oracle_threads(); }
+
+/* ------------------------------------------------------------------------ */
+/* Adan step (manbo/ops/optim.py:60-104), element by element in float32.     */
+
+void cso_adan_step(float *param, const float *grad, float *exp_avg, float *exp_avg_sq,
+                   float *exp_avg_diff, float *neg_pre_grad, int64_t numel, int step,
+                   float beta1, float beta2, float beta3, float bc1, float bc2, float bc3_sqrt,
+                   float lr, float weight_decay, float eps, float clip, int no_prox) {
+    for (int64_t i = 0; i < numel; ++i) {
+        float g = grad[i] * clip;
+        float ngod = (step == 1) ? 0.0f : neg_pre_grad[i] + g;
+        float m_t = exp_avg[i] * beta1 + g * (1.0f - beta1);
+        float d_t = exp_avg_diff[i] * beta2 + ngod * (1.0f - beta2);
+        float ngod2 = ngod * beta2 + g;
+        float n_t = exp_avg_sq[i] * beta3 + ngod2 * ngod2 * (1.0f - beta3);
+        float denom = sqrtf(n_t) / bc3_sqrt + eps;
+        float step_size = lr / bc1;
+        float step_size_diff = lr * beta2 / bc2;
+        float p = param[i];
+        if (no_prox) {
+            p = p * (1.0f - lr * weight_decay);
+            p = p - step_size * m_t / denom;
+            p = p - step_size_diff * d_t / denom;
+        } else {
+            p = p - step_size * m_t / denom;
+            p = p - step_size_diff * d_t / denom;
+            p = p / (1.0f + lr * weight_decay);
+        }
+        param[i] = p;
+        exp_avg[i] = m_t;
+        exp_avg_diff[i] = d_t;
+        exp_avg_sq[i] = n_t;
+        neg_pre_grad[i] = -g;
+    }
+}

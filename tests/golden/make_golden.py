@@ -223,6 +223,38 @@ def metric_case(metric, dev):
     }
 
 
+ADAN_VARIANTS = {
+    "prox": dict(lr=0.05, weight_decay=0.02),
+    "noprox": dict(lr=0.05, weight_decay=0.02, no_prox=True),
+    "clip": dict(lr=0.05, max_grad_norm=0.5),
+}
+
+
+def adan_case(manbo, dev):
+    """Three steps of the reference Adan optimiser in three variants, on one
+    odd-length and one 4-aligned parameter with seeded gradients."""
+    gen = torch.Generator().manual_seed(13)
+    shapes = [(37, 2), (64,)]
+    params0 = [torch.randn(s, generator=gen) for s in shapes]
+    grads = [[torch.randn(s, generator=gen) * 0.1 for s in shapes] for _ in range(3)]
+    out = {f"param0_{i}": _np(p) for i, p in enumerate(params0)}
+    for t in range(3):
+        for i, g in enumerate(grads[t]):
+            out[f"grad{t}_{i}"] = _np(g)
+    for name, kw in ADAN_VARIANTS.items():
+        ps = [p.clone().to(dev).requires_grad_(True) for p in params0]
+        opt = manbo.Adan(ps, **kw)
+        for t in range(3):
+            for p, g in zip(ps, grads[t]):
+                p.grad = g.to(dev).clone()
+            opt.step()
+        for i, p in enumerate(ps):
+            out[f"{name}_param_{i}"] = _np(p)
+            for k in ("exp_avg", "exp_avg_sq", "exp_avg_diff", "neg_pre_grad"):
+                out[f"{name}_{k}_{i}"] = _np(opt.state[p][k])
+    return out
+
+
 def time_config2(manbo, cs, dev, iters: int, warmup: int):
     """Reference training step at config 2: render + MSE + SSIM + backward + Adam."""
     sc = scenes.config2()
@@ -272,6 +304,8 @@ def main(argv=None):
     ap.add_argument("--no-golden", action="store_true")
     ap.add_argument("--iters", type=int, default=100)
     ap.add_argument("--json", default=None)
+    ap.add_argument("--cases", default="all",
+                    help="comma-separated fixtures to (re)generate, e.g. adan; default all")
     args = ap.parse_args(argv)
 
     sys.path.insert(0, os.path.abspath(args.ref))
@@ -286,7 +320,12 @@ def main(argv=None):
     info = {"torch": torch.__version__, "tilelang": getattr(tilelang, "__version__", "?"),
             "gpu": torch.cuda.get_device_name(0)}
     print(info, flush=True)
-    if not args.no_golden:
+    cases = None if args.cases == "all" else set(args.cases.split(","))
+    if not args.no_golden and cases is not None:
+        if "adan" in cases:
+            _save(args.out, "adan", adan_case(manbo, dev))
+    elif not args.no_golden:
+        _save(args.out, "adan", adan_case(manbo, dev))
         _save(args.out, "fill_small_a", fill_case(cs, tb, scenes.small_fill_scene(21), 31, dev))
         _save(args.out, "fill_small_b", fill_case(cs, tb, scenes.small_fill_scene(22, h=40, w=72, paths=9, samples=5), 32, dev))
         ties = scenes.small_fill_scene(23, paths=7, mixed=False)

@@ -64,8 +64,19 @@ def test_out_of_scope_names_raise():
         ops.rasterize_forward_tilelang()
     with pytest.raises(NotImplementedError):
         manbo.gs_render()
-    with pytest.raises(NotImplementedError):
-        manbo.Adan([])
+
+
+def test_adan_is_a_real_optimizer_with_reference_validation():
+    import torch
+    import manbo
+    p = torch.zeros(3, requires_grad=True)
+    with pytest.raises(ValueError, match="Invalid epsilon value"):
+        manbo.Adan([p], eps=-1.0)
+    opt = manbo.Adan([p], lr=0.1)
+    assert opt.defaults["betas"] == (0.98, 0.92, 0.99)
+    p.grad = torch.ones(3)
+    with pytest.raises(ValueError):  # CPU tensors: no host fallback
+        opt.step()
 
 
 def test_cpu_tensors_are_rejected_without_fallback():

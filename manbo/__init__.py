@@ -8,6 +8,29 @@ outside that path (Gaussian renderer, regularisation, connected components)
 keep their names so that imports succeed, and raise NotImplementedError when
 called.
 """
+import importlib.util as _ilu
+import pkgutil as _pkgutil
+import sys as _sys
+
+# Subpackages this package does not provide (the reference's model glue
+# `gaussian_trace`, its `profile` tooling, `sparse_init`) are found in any
+# other `manbo` directory on sys.path, such as an installed copy of the
+# reference: its Python glue then runs on these kernels, because it imports
+# the renderer, metrics and optimiser from `manbo`, which is this package.
+__path__ = _pkgutil.extend_path(__path__, __name__)
+def _importable(name: str) -> bool:
+    if name in _sys.modules:
+        return True
+    try:
+        return _ilu.find_spec(name) is not None
+    except (ImportError, ValueError):
+        return False
+
+
+if not _importable("visual_debug"):
+    from . import _visual_debug
+    _sys.modules["visual_debug"] = _visual_debug
+
 from . import ops
 from .metric import mse_loss_tilelang, psnr, ssim
 from .optim import Adan

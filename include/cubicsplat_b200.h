@@ -106,7 +106,9 @@ CS_API int cs_isect_edge_ranges(const int32_t *prim_ids_sorted, const int32_t *p
  * afterwards) every tile range is written empty and counters[1] is set to
  * CS_ERR_CAPACITY, so no later kernel reads past the caller's buffers.
  * Offsets that do not start at 0, end at num_segments and increase set
- * counters[1] to CS_ERR_ARG (the primitive is treated as empty).
+ * counters[1] to CS_ERR_ARG (the primitive is treated as empty).  For a band
+ * (rows other than the whole grid), tiles outside it read as empty and the
+ * edges of primitives whose tile rows miss the band are not written.
  * With cs_bin_sort this replaces project (K3) + flatten + K4 + cumsum + K5 +
  * torch.sort + K6 of _CubicFillSplatFunction.forward, cubic_splatting.py:2815-2908.
  * Workspace: cs_bin_workspace_size(num_tiles). */
@@ -266,10 +268,15 @@ CS_API int cs_ring_to_cubics(const float *ring, float *cubics_norm, int64_t num_
  * (written, not accumulated): the per-segment Bernstein accumulation of
  * cs_edge_grads_to_cubics in normalised space, then the derivative of the
  * normalisation, summed over the control points that share a ring point.
- * clear_edges != 0 zeroes v_edges after reading it.  G <= 128. */
+ * clear_edges != 0 zeroes v_edges after reading it.  G <= 128.  With
+ * prim_tile_ranges [P, 4] (may be NULL) a path whose tile rectangle misses the
+ * tile rows [tile_row_begin, tile_row_end) gets zero gradients without its
+ * edges being read (a band renders only its rows). */
 CS_API int cs_edge_grads_to_ring(float *v_edges, float *v_ring, int64_t num_paths,
                           int32_t segs_per_path, int32_t edges_per_segment, int32_t img_height,
-                          int32_t img_width, int32_t clear_edges, void *stream);
+                          int32_t img_width, int32_t clear_edges,
+                          const int32_t *prim_tile_ranges, int32_t tile_row_begin,
+                          int32_t tile_row_end, void *stream);
 
 /* Adam step over one flat fp32 parameter buffer, elements [0, n_first) with
  * lr_first and the rest with lr_rest; step (device int32) holds the number of

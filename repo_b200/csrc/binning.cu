@@ -299,7 +299,10 @@ __global__ void __launch_bounds__(256) bin_prep_kernel(
     *reinterpret_cast<int4*>(pr + p * 4) = make_int4(mnx, mny, mxx, mxy);
     hits[p] = count;
   }
-  const int npts = nseg * S;
+  // edges are needed only by the band's tiles: a primitive whose tile rows
+  // miss the band is not flattened
+  const bool in_band = max(mny, r0) < min(mxy, r1) && mnx < mxx;
+  const int npts = in_band ? nseg * S : 0;
   for (int q = lane; q < npts; q += 32) {
     int si = q / S;
     int s = q - si * S;
@@ -325,7 +328,7 @@ __global__ void __launch_bounds__(256) bin_prep_kernel(
   }
 }
 
-// Exclusive scan of per-tile intersect counts into tile ranges [start, end)
+// Exclusive scan over the tiles [t0, t1) of per-tile intersect counts into tile ranges [start, end)
 // and of per-tile edge-slot counts into staged-record ranges: tile t owns
 // kStrips consecutive lists of capacity ecount[t] each, so tile_dlist[t] =
 // (first record, ecount[t]) and the record bound is kStrips * sum(ecount).
@@ -336,13 +339,15 @@ __global__ void __launch_bounds__(1024) bin_scan_kernel(const int* __restrict__ 
                                                         int* __restrict__ bins,
                                                         int* __restrict__ dlr,
                                                         int* __restrict__ cursor,
-                                                        int* __restrict__ counters, long long nt,
-                                                        long long icap, long long dcap) {
+                                                        int* __restrict__ counters, long long t0,
+                                                        long long t1, long long icap,
+                                                        long long dcap) {
   __shared__ int wa[32], wb[32];
   __shared__ long long s_ta, s_tb;
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const long long nt = t1 - t0;  // tiles [t0, t1): the band
   const long long chunk = (nt + 1023) / 1024;
-  const long long b = tid * chunk, e = min(nt, b + chunk);
+  const long long b = t0 + tid * chunk, e = min(t1, b + chunk);
   int la = 0, lb = 0;
   for (long long i = b; i < e; ++i) {
     if (counts) la += counts[i];
@@ -895,8 +900,14 @@ int cs_bin_count(const float* cubics_norm, const int32_t* prim_seg_offsets, cons
         num_primitives, num_segments, samples, 0.5f * (float)img_width,
         0.5f * (float)img_height, tbx, tby, r0, r1, aabb_pad, aniso);
   }
+  const long long t0 = (long long)r0 * tbx, t1 = (long long)max(r0, r1) * tbx;
+  if (t0 > 0 || t1 < nt) {  // a band: tiles outside it read as empty
+    cudaMemsetAsync(tile_bins, 0, sizeof(int32_t) * 2 * nt, st);
+    cudaMemsetAsync(tile_dlist, 0, sizeof(int32_t) * 2 * nt, st);
+  }
   bin_scan_kernel<<<1, 1024, 0, st>>>(ws.tile_counts, ws.tile_ecounts, tile_bins, tile_dlist,
-                                      ws.cursor, counters, nt, (isect_capacity > 0 ? isect_capacity : 0),
+                                      ws.cursor, counters, t0, t1,
+                                      (isect_capacity > 0 ? isect_capacity : 0),
                                       (dlist_capacity > 0 ? dlist_capacity : 0));
   return launch_status();
 }
@@ -992,7 +1003,7 @@ int cs_tile_stage(const int32_t* prim_ids_sorted, const int32_t* tile_bins, cons
       tile_bins, prim_ids_sorted, reinterpret_cast<const int2*>(isect_edge_ranges),
       prim_edge_offsets, ecounts, nt);
   bin_scan_kernel<<<1, 1024, 0, st>>>(nullptr, ecounts, nullptr, tile_dlist, nullptr, counters,
-                                      nt, 0, (dlist_capacity > 0 ? dlist_capacity : 0));
+                                      0, nt, 0, (dlist_capacity > 0 ? dlist_capacity : 0));
   StageIO io = stage_io(prim_ids_sorted, edges_px, isect_edge_ranges, prim_edge_offsets, colors,
                         opacities, inv_sigma2s, fill_rules, stroke_widths, tile_dlist, imeta,
                         rowoff, isect_strips, dlist, tbx);

@@ -151,7 +151,7 @@ constexpr int kRingSegsPerPass = kRingThreads / kRingEdgeLanes;  // segments per
 
 __global__ void __launch_bounds__(kRingThreads) edge_grads_to_ring_kernel(
     float4* __restrict__ v_edges, float* __restrict__ v_ring, long long npaths, int G, int E,
-    float half_w, float half_h, int clear) {
+    float half_w, float half_h, int clear, const int4* __restrict__ prim_ranges, int r0, int r1) {
   __shared__ float cub[kRingThreads][9];
   const int ppb = max(1, kRingSegsPerPass / G);
   const long long p0 = (long long)blockIdx.x * ppb;
@@ -164,7 +164,13 @@ __global__ void __launch_bounds__(kRingThreads) edge_grads_to_ring_kernel(
   for (int s0 = 0; s0 < nseg; s0 += kRingSegsPerPass) {  // uniform trip count
     const int t = s0 + hw;
     float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    if (t < nseg) {
+    // a path whose tile rows miss the band [r0, r1) has no edge gradient here
+    bool live = t < nseg;
+    if (live && prim_ranges) {
+      const int4 rr = __ldg(prim_ranges + p0 + t / G);
+      live = max(rr.y, r0) < min(rr.w, r1) && rr.x < rr.z;
+    }
+    if (live) {
       float4* gseg = v_edges + (p0 * G + t) * E;
       for (int e = sub; e < E; e += kRingEdgeLanes) {
         const float t0 = (float)e * inv_e, t1 = (float)(e + 1) * inv_e;
@@ -300,7 +306,8 @@ int cs_ring_to_cubics(const float* ring, float* cubics_norm, int64_t num_paths,
 
 int cs_edge_grads_to_ring(float* v_edges, float* v_ring, int64_t num_paths, int32_t segs_per_path,
                           int32_t edges_per_segment, int32_t img_height, int32_t img_width,
-                          int32_t clear_edges, void* stream) {
+                          int32_t clear_edges, const int32_t* prim_tile_ranges,
+                          int32_t tile_row_begin, int32_t tile_row_end, void* stream) {
   if (num_paths < 0 || segs_per_path <= 0 || segs_per_path > kRingThreads ||
       edges_per_segment <= 0)
     return CS_ERR_ARG;
@@ -308,7 +315,8 @@ int cs_edge_grads_to_ring(float* v_edges, float* v_ring, int64_t num_paths, int3
   const int ppb = max(1, kRingSegsPerPass / segs_per_path);
   edge_grads_to_ring_kernel<<<ceil_div(num_paths, ppb), kRingThreads, 0, (cudaStream_t)stream>>>(
       reinterpret_cast<float4*>(v_edges), v_ring, num_paths, segs_per_path, edges_per_segment,
-      0.5f * (float)img_width, 0.5f * (float)img_height, clear_edges);
+      0.5f * (float)img_width, 0.5f * (float)img_height, clear_edges,
+      reinterpret_cast<const int4*>(prim_tile_ranges), tile_row_begin, tile_row_end);
   return launch_status();
 }
 

@@ -30,9 +30,12 @@
 // The backward walks the intersects in reverse from the warp's largest
 // final_idx with T <- T / (1 - alpha), takes the first-minimum closest edge
 // (the reference's strict-< rule in edge order), reduces per-primitive
-// gradients over the warp before one atomic per primitive, and accumulates
-// edge gradients per staged record in shared memory before one global atomic
-// per edge and chunk.
+// gradients over the warp (four values per shuffle butterfly) before one
+// atomic per primitive value, and accumulates edge gradients per staged record
+// in shared memory before one global atomic per edge and chunk.  Its per-pixel
+// coverage, reciprocals and square root use the fast hardware forms: the
+// forward image must match the oracle bit for bit, the gradients only within
+// the reference's tolerance.
 #include "stage.cuh"
 
 namespace cs {
@@ -299,6 +302,31 @@ __device__ __forceinline__ float stroke_coverage(float md, float half_sw, float 
   edge_d = fmaxf(0.0f, dist - half_sw);
   const float sigma = 0.5f * edge_d * edge_d * inv_s2;
   return cs_expf(-sigma);
+}
+
+// The backward's coverage: the same formulas with the hardware's fast square
+// root, exponential and division (a few ulp; the forward, whose image must
+// match the oracle bit for bit, keeps the correctly rounded forms above).
+__device__ __forceinline__ float fast_sqrt(float x) {
+  return x > 0.0f ? x * rsqrtf(x) : 0.0f;
+}
+
+__device__ __forceinline__ float fill_coverage_fast(float md, int w, int n, int rule,
+                                                    float inv_sigma, float& sign, float& dist) {
+  const int inside = (rule == 0) ? (n & 1) : (w != 0);
+  dist = fast_sqrt(md);
+  sign = inside ? -1.0f : 1.0f;
+  float logit = sign * dist * inv_sigma * 2.0f;
+  logit = fmaxf(-60.0f, fminf(60.0f, logit));
+  return __fdividef(1.0f, 1.0f + __expf(logit));
+}
+
+__device__ __forceinline__ float stroke_coverage_fast(float md, float half_sw, float inv_s2,
+                                                      float& dist, float& edge_d) {
+  dist = fast_sqrt(md);
+  edge_d = fmaxf(0.0f, dist - half_sw);
+  const float sigma = 0.5f * edge_d * edge_d * inv_s2;
+  return __expf(-sigma);
 }
 
 __device__ __forceinline__ void load_meta(const IMeta* __restrict__ p, IMeta& m) {
@@ -591,23 +619,28 @@ __device__ __forceinline__ void best_point(const DEntry* __restrict__ buf, int c
   seg_d2(px, py, py - EA.y, EA, EB, s.bp, s.bcx, s.bcy);
 }
 
+// One pixel's backward step at one intersect.  need_op / need_inv say whether
+// the opacity and softness gradients are wanted at all (NULL outputs skip
+// their arithmetic).  Uses the fast coverage and reciprocal forms: the
+// gradients only need to match the reference within its tolerance.
 template <bool STROKE>
 __device__ __forceinline__ void bwd_pixel(BwdPix& s, const IMeta& m, float px, float py, bool valid,
-                                          float acc[kAcc], bool collect, float4& eg,
-                                          bool& has_eg, bool& contributed) {
+                                          float acc[kAcc], bool collect, bool need_op,
+                                          bool need_inv, float4& eg, bool& has_eg,
+                                          bool& contributed) {
   has_eg = false;
   if (!valid) return;
   float cov, sign = 1.0f, dist, edge_d = 0.0f;
   if (!STROKE) {
-    cov = fill_coverage(s.md, s.w, s.n, m.rule, m.a, sign, dist);
+    cov = fill_coverage_fast(s.md, s.w, s.n, m.rule, m.a, sign, dist);
   } else {
-    cov = stroke_coverage(s.md, m.b, m.a, dist, edge_d);
+    cov = stroke_coverage_fast(s.md, m.b, m.a, dist, edge_d);
   }
   const float op = m.op;
   const float alpha = fminf(kAlphaCap, op * cov);
   if (!(alpha >= kAlphaMin)) return;
   contributed = true;
-  const float ra = 1.0f / (1.0f - alpha);
+  const float ra = __fdividef(1.0f, 1.0f - alpha);
   s.T = s.T * ra;
   const float fac = alpha * s.T;
   acc[0] += fac * s.v0;
@@ -629,19 +662,21 @@ __device__ __forceinline__ void bwd_pixel(BwdPix& s, const IMeta& m, float px, f
   s.b1 = s.b1 + m.c1 * fac;
   s.b2 = s.b2 + m.c2 * fac;
   if (!(alpha < kAlphaCap)) return;
-  acc[3] += cov * v_alpha;
+  if (need_op) acc[3] += cov * v_alpha;
   float gscale = 0.0f;
   bool geom = false;
   if (!STROKE) {
     const float v_cov = op * v_alpha;
     const float v_logit = -v_cov * cov * (1.0f - cov);
-    const float v_inv_sigma = v_logit * sign * dist * 2.0f;
-    acc[4] += v_inv_sigma * 0.5f / fmaxf(m.a, kEps);
+    if (need_inv) {
+      const float v_inv_sigma = v_logit * sign * dist * 2.0f;
+      acc[4] += __fdividef(v_inv_sigma * 0.5f, fmaxf(m.a, kEps));
+    }
     gscale = v_logit * sign * m.a * 2.0f;
     geom = (dist > kEps) & (s.be >= 0);
   } else {
     const float v_sigma = -op * cov * v_alpha;
-    acc[4] += 0.5f * edge_d * edge_d * v_sigma;
+    if (need_inv) acc[4] += 0.5f * edge_d * edge_d * v_sigma;
     if (edge_d > 0.0f) {
       const float v_edge = v_sigma * edge_d * m.a;
       acc[5] += -0.5f * v_edge;
@@ -650,11 +685,29 @@ __device__ __forceinline__ void bwd_pixel(BwdPix& s, const IMeta& m, float px, f
     }
   }
   if (geom) {
-    const float gx = gscale * (s.bcx - px) / dist;
-    const float gy = gscale * (s.bcy - py) / dist;
+    const float g = __fdividef(gscale, dist);  // gscale / dist, once for both axes
+    const float gx = g * (s.bcx - px);
+    const float gy = g * (s.bcy - py);
     eg = make_float4((1.0f - s.bp) * gx, (1.0f - s.bp) * gy, s.bp * gx, s.bp * gy);
     has_eg = true;
   }
+}
+
+// Warp totals of four values at once (two exchange rounds that halve the
+// values each lane carries, then three plain rounds): returns, in every lane,
+// the total of value ((lane >> 3) & 3).  Six shuffles instead of twenty.
+__device__ __forceinline__ float warp_reduce4(float v0, float v1, float v2, float v3) {
+  const int lane = threadIdx.x & 31;
+  const bool h16 = (lane & 16) != 0, h8 = (lane & 8) != 0;
+  float a = h16 ? v2 : v0, b = h16 ? v3 : v1;
+  a += __shfl_xor_sync(0xffffffffu, h16 ? v0 : v2, 16);
+  b += __shfl_xor_sync(0xffffffffu, h16 ? v1 : v3, 16);
+  float c = h8 ? b : a;
+  c += __shfl_xor_sync(0xffffffffu, h8 ? a : b, 8);
+  c += __shfl_xor_sync(0xffffffffu, c, 4);
+  c += __shfl_xor_sync(0xffffffffu, c, 2);
+  c += __shfl_xor_sync(0xffffffffu, c, 1);
+  return c;
 }
 
 __device__ __forceinline__ void flush_acc(const RasterArgs& A, int pid, int k, int c, float v) {
@@ -812,7 +865,8 @@ __device__ __forceinline__ bool backward_unit(const RasterArgs& A, int unit,
       for (int u = 0; u < 2; ++u) {
         float4 eg;
         bool has_eg;
-        bwd_pixel<STROKE>(s[u], m, px[u], py, u ? v1 : v0, acc, collect, eg, has_eg, contributed);
+        bwd_pixel<STROKE>(s[u], m, px[u], py, u ? v1 : v0, acc, collect, A.v_opac != nullptr,
+                          A.v_inv != nullptr, eg, has_eg, contributed);
         if (has_eg) {
           if (s[u].bl >= 0) {
             float4* gp = &dgrad[s[u].bl - c0];
@@ -830,14 +884,18 @@ __device__ __forceinline__ bool backward_unit(const RasterArgs& A, int unit,
         }
       }
       if (__any_sync(0xffffffffu, contributed)) {
-#pragma unroll
-        for (int q = 0; q < kAcc; ++q) {
-          if (q == 3 && !A.v_opac) continue;
-          if (q == 4 && !A.v_inv) continue;
-          if (q == 5 && !STROKE) continue;
-          if (q >= 6 && !collect) continue;
-          const float v = warp_sum(acc[q]);
-          if (lane == 0) flush_acc(A, m.pid, k, q, v);
+        // four sums per butterfly: lane 8 i holds value i's warp total
+        const int vi = (lane >> 3) & 3;
+        const bool leader = (lane & 7) == 0;
+        float r = warp_reduce4(acc[0], acc[1], acc[2], A.v_opac ? acc[3] : 0.0f);
+        if (leader) flush_acc(A, m.pid, k, vi, r);
+        if (STROKE || A.v_inv) {
+          r = warp_reduce4(acc[4], STROKE ? acc[5] : 0.0f, 0.0f, 0.0f);
+          if (leader && vi < 2) flush_acc(A, m.pid, k, 4 + vi, r);
+        }
+        if (collect) {
+          r = warp_reduce4(acc[6], acc[7], acc[8], acc[9]);
+          if (leader) flush_acc(A, m.pid, k, 6 + vi, r);
         }
       }
       mid = false;

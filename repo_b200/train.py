@@ -221,7 +221,8 @@ class FillTrainer:
                   "cs_fill_backward")
         nat.check(nat.call("cs_edge_grads_to_ring", self.v_edges.data_ptr(),
                            self.v_ring.data_ptr(), self.num_paths, self.g_per_path, self.s - 1,
-                           self.h, self.w, 1, st), "cs_edge_grads_to_ring")
+                           self.h, self.w, 1, self.prim_ranges.data_ptr(), r0, r1, st),
+                  "cs_edge_grads_to_ring")
         if self.with_ssim:
             torch.cuda.current_stream(self.device).wait_event(self._join)
 

@@ -23,6 +23,14 @@ all-reduces the gradient buffer over NCCL inside the step's CUDA graph
 ("scaling": "strong").  SSIM is not part of this step (a band lacks the rows
 the SSIM window needs).
 
+--workload config4: stroke mode, 1024x1024, 2048 open one-segment cubics
+(width U[1,4] px, S=16) through the drop-in manbo API: forward + MSE + backward
++ Adam per step (the API binds each frame with one host synchronisation).
+--workload config5: the batched sweep, one 768x512 scene per rank, paths in
+{256, 1024, 4096, 16384} x S in {4, 8, 16, 32}, the fused step (with SSIM)
+at every point, plus standalone MSE and SSIM kernel bandwidth; one JSON line
+per point.
+
 --impl reference times the reference algorithm's CPU implementation (the C
 oracle restating manbo/ops/cubic_splatting.py, all host threads) on the same
 workload; the reference has no CPU renderer of its own.
@@ -55,7 +63,8 @@ def parse_args(argv=None):
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
-    ap.add_argument("--workload", default="config2", choices=["config2", "config3"])
+    ap.add_argument("--workload", default="config2",
+                    choices=["config2", "config3", "config4", "config5"])
     return ap.parse_args(argv)
 
 
@@ -132,6 +141,26 @@ def time_steps(step_fn, steps, flush, stream):
         durs.append((s, e))
     torch.cuda.synchronize()
     return [s.elapsed_time(e) for s, e in durs]
+
+
+def time_device_calls(fn, reps, flush, stream):
+    """Device time of `fn`'s launches alone: all reps (L2 flush, event, fn,
+    event) are queued behind a sleep kernel, so host launch overhead does not
+    show up between the events."""
+    import torch
+    torch.cuda.synchronize()
+    torch.cuda._sleep(int(4e6))  # a few ms of queue lead for the host
+    evs = []
+    for _ in range(reps):
+        flush()
+        s = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        fn()
+        e.record(stream)
+        evs.append((s, e))
+    torch.cuda.synchronize()
+    return [s.elapsed_time(e) for s, e in evs]
 
 
 def kernel_times(tr, reps, flush, stream):
@@ -384,6 +413,216 @@ def run_bands(args, rank, world, local_rank):
     return result, tr
 
 
+def binning_work(b, fts, fidx, h, w):
+    """Reference-algorithm pixel-edge pairs and pixel-intersect visits of a
+    rendered frame (as raster_work), from a Binning and the forward outputs."""
+    import numpy as np
+    n = int(b.num_intersects)
+    bins = b.tile_bins.cpu().numpy()
+    pids = b.prim_ids_sorted[:n].cpu().numpy()
+    eoffs = b.prim_edge_offsets.cpu().numpy()
+    ne = (eoffs[pids + 1] - eoffs[pids]).astype(np.int64)
+    cum = np.concatenate([[0], np.cumsum(ne)])
+    fidx = fidx.cpu().numpy().astype(np.int64)
+    fts = fts.cpu().numpy()
+    tbx = b.tile_bounds[0]
+    tile = (np.arange(h)[:, None] // 16) * tbx + np.arange(w)[None, :] // 16
+    start = bins[tile, 0].astype(np.int64)
+    end = bins[tile, 1].astype(np.int64)
+    has = end > start
+    stop = np.where(fts <= 1e-4, fidx, end - 1)
+    pe_fwd = np.where(has, cum[np.clip(stop + 1, 0, n)] - cum[start], 0).sum()
+    vis_fwd = np.where(has, stop + 1 - start, 0).sum()
+    valid_b = has & (fidx >= start)
+    pe_bwd = np.where(valid_b, cum[np.clip(fidx + 1, 0, n)] - cum[start], 0).sum()
+    vis_bwd = np.where(valid_b, fidx + 1 - start, 0).sum()
+    return int(pe_fwd), int(vis_fwd), int(pe_bwd), int(vis_bwd)
+
+
+def run_stroke(args, rank, world, local_rank):
+    """Config 4: stroke mode through the manbo API (forward, MSE, backward, Adam)."""
+    import torch
+
+    import manbo
+    from repo_b200 import _native as nat
+    from repo_b200 import render, scenes
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream(dev)
+    sc = scenes.config4(seed=3 + rank)
+    h, w, p = sc.height, sc.width, int(sc.cubics_px.shape[0])
+    cn = scenes.px_to_norm(sc.cubics_px, w, h).to(dev).requires_grad_(True)
+    colors = sc.colors.to(dev).clone().requires_grad_(True)
+    widths = sc.stroke_widths.to(dev).clone().requires_grad_(True)
+    opac, depths = sc.opacities.to(dev), sc.depths.to(dev)
+    aa, bg = sc.aa_widths.to(dev), sc.background.to(dev)
+    offs = torch.arange(p + 1, dtype=torch.int32, device=dev)
+    target = sc.target.to(dev)
+    opt = torch.optim.Adam([{"params": [cn], "lr": 1e-3},
+                            {"params": [colors, widths], "lr": 0.01}], fused=True)
+    flush_buf = torch.empty((L2_FLUSH_BYTES // 4,), dtype=torch.float32, device=dev)
+
+    def flush():
+        flush_buf.zero_()
+
+    def step():
+        opt.zero_grad(set_to_none=True)
+        out = manbo.ops.render_cubic_polyline_splat_tilelang(
+            cn, offs, colors, opac, widths, depths, h, w, 16, 16, bg, aa_widths=aa,
+            distance_samples=sc.samples)
+        img = torch.clamp(out, 0, 1).permute(2, 0, 1).unsqueeze(0).contiguous()
+        loss = manbo.mse_loss_tilelang(img, target)
+        loss.backward()
+        opt.step()
+        return loss
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    with ClockSampler(local_rank) as clk:
+        durs = time_steps(step, args.steps, flush, stream)
+    total_ms = sum(durs)
+    # the two stroke raster kernels, timed live with CUDA events on their stream
+    fwd, bwd = [], []
+    orig = nat.call
+
+    def timed(name, *a):
+        if name in ("cs_stroke_forward", "cs_stroke_backward"):
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            r = orig(name, *a)
+            e1.record(stream)
+            (fwd if name == "cs_stroke_forward" else bwd).append((e0, e1))
+            return r
+        return orig(name, *a)
+
+    nat.call = timed
+    try:
+        for _ in range(5):
+            flush()
+            step()
+        torch.cuda.synchronize()
+    finally:
+        nat.call = orig
+    t_fwd = statistics.mean(a.elapsed_time(b) for a, b in fwd)
+    t_bwd = statistics.mean(a.elapsed_time(b) for a, b in bwd)
+    with torch.no_grad():  # reference-algorithm work of the current state
+        wd = torch.clamp(aa, min=1e-4)
+        b = render.bin_primitives(cn.detach(), offs, depths, wd, h, w, sc.samples,
+                                  colors=colors.detach(), opacities=opac,
+                                  inv_sigma2s=render._inv_sigma2(wd), stroke_widths=widths.detach())
+        _, fts, fidx = render.forward_raster(b, bg, h, w)
+        pe_f, vis_f, pe_b, vis_b = binning_work(b, fts, fidx, h, w)
+    t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms = float(t.item())
+    if rank != 0:
+        return None
+    clocks = clk.summary()
+    peak = 148 * 128 * 2 * (clocks.get("sm_mhz") or 1965.0) * 1e6 / 1e12
+    flop_b = 18 * pe_b + 30 * vis_b
+    flop_f = 14 * pe_f + 12 * vis_f
+    return {
+        "metric": "stroke fwd+bwd iters/s at 1024x1024, 2048 strokes (manbo API)",
+        "value": round(world * args.steps / (total_ms / 1e3), 3), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": "config4: 1024x1024 RGB target of 256 lines, 2048 open cubic "
+                               "strokes (1 segment), width U[1,4], S=16, fwd+MSE+bwd+Adam "
+                               "through manbo.ops.render_cubic_polyline_splat_tilelang",
+                   "l2": "flushed before every step (256 MiB write), outside the step events"},
+        "clocks": clocks,
+        "roofline": {"kernel": "raster_backward (stroke)", "bound": "fp32",
+                     "achieved": round(flop_b / (t_bwd * 1e-3) / 1e12, 3),
+                     "peak": round(peak, 2), "unit": "TFLOP/s",
+                     "frac": round(flop_b / (t_bwd * 1e-3) / 1e12 / peak, 4),
+                     "flop_model": "reference-algorithm work: 18 FLOP per pixel-edge pair up to "
+                                   "final_idx + 30 per pixel-intersect visit",
+                     "launch_ms": round(t_bwd, 4),
+                     "forward": {"launch_ms": round(t_fwd, 4),
+                                 "achieved": round(flop_f / (t_fwd * 1e-3) / 1e12, 3)}},
+    }
+
+
+def run_sweep(args, rank, world, local_rank):
+    """Config 5: path-count x samples sweep of the fused step, one scene per
+    rank, and standalone MSE / SSIM kernel bandwidth.  Yields JSON lines."""
+    import json as _json
+
+    import torch
+    import torch.distributed as dist
+
+    from repo_b200 import metric as mt
+    from repo_b200 import scenes
+    from repo_b200.train import FillTrainer
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream(dev)
+    flush_buf = torch.empty((L2_FLUSH_BYTES // 4,), dtype=torch.float32, device=dev)
+
+    def flush():
+        flush_buf.zero_()
+
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except OSError:
+        pass
+    hbm = float(peaks.get("hbm_gbs", 6650.0))
+    lines = []
+    steps = max(10, args.steps // 4)
+    for paths in (256, 1024, 4096, 16384):
+        for samples in (4, 8, 16, 32):
+            tr = FillTrainer(scenes.config5(rank, paths, samples), dev)
+            tr.capture(warmup=3)
+            for _ in range(max(3, args.warmup)):
+                tr.step()
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+            durs = time_steps(tr.step, steps, flush, stream)
+            t = torch.tensor([sum(durs)], dtype=torch.float64, device=dev)
+            if world > 1:
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            n_isect, status = tr.check_status()
+            lines.append({"metric": "fwd+bwd iters/s at 768x512 (config 5 sweep)",
+                          "value": round(world * steps / (float(t.item()) / 1e3), 3),
+                          "unit": UNIT, "n_gpus": world, "steps": steps,
+                          "ms_per_step": round(float(t.item()) / steps, 4),
+                          "higher_is_better": True, "scaling": "weak", "dtype": "f32",
+                          "data": "synthetic",
+                          "config": {"workload": "config5", "paths": paths, "samples": samples,
+                                     "intersects": n_isect, "status": status}})
+            del tr
+    # standalone metric kernels on one 768x512 RGB pair (inputs > L2 after the flush)
+    x = torch.rand(1, 3, 512, 768, device=dev)
+    y = torch.rand(1, 3, 512, 768, device=dev)
+    n = x.numel()
+    for name, fn, nbytes in (("mse", lambda: mt.sse_mse(x.view(-1), y.view(-1)), 8 * n),
+                             ("ssim", lambda: mt.ssim_per_plane(x, y, 11, 1.5, 1e-4, 9e-4),
+                              8 * n)):
+        for _ in range(5):
+            fn()
+        ms = statistics.median(time_device_calls(fn, 30, flush, stream))
+        lines.append({"metric": f"standalone {name} kernel bandwidth, 768x512x3 fp32 pair",
+                      "value": round(nbytes / (ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                      "ms": round(ms, 5), "bytes": nbytes, "peak_hbm_gbs": hbm,
+                      "frac": round(nbytes / (ms * 1e-3) / 1e9 / hbm, 4),
+                      "l2": "flushed before every call"})
+    if rank != 0:
+        return None
+    return [_json.dumps(line) for line in lines]
+
+
 def run_e2e(scene, dev, args, flush, stream, world):
     """Training steps through the manbo API: target H2D from pinned memory and
     loss D2H every step, timed with CUDA events."""
@@ -551,6 +790,17 @@ def main(argv=None):
                 print(json.dumps(res), flush=True)
             tr.graph = None  # graphs holding NCCL work go before the process group
             del tr
+            return 0
+        if args.workload == "config4":
+            res = run_stroke(args, rank, world, local_rank)
+            if rank == 0:
+                print(json.dumps(res), flush=True)
+            return 0
+        if args.workload == "config5":
+            out = run_sweep(args, rank, world, local_rank)
+            if rank == 0:
+                for line in out:
+                    print(line, flush=True)
             return 0
         res, tr = run_b200(args, rank, world, local_rank)
         if rank == 0 and not args.no_cpu_baseline:

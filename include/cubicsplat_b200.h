@@ -106,7 +106,10 @@ CS_API int cs_isect_edge_ranges(const int32_t *prim_ids_sorted, const int32_t *p
  * afterwards) every tile range is written empty and counters[1] is set to
  * CS_ERR_CAPACITY, so no later kernel reads past the caller's buffers.
  * Offsets that do not start at 0, end at num_segments and increase set
- * counters[1] to CS_ERR_ARG (the primitive is treated as empty).  For a band
+ * counters[1] to CS_ERR_ARG (the primitive is treated as empty).  With ring
+ * (closed paths as ring points [P, 3G, 2] in pixels, G = ring_segs_per_path)
+ * the control points are read from the ring, normalised exactly as
+ * cs_ring_to_cubics does, and cubics_norm may be NULL.  For a band
  * (rows other than the whole grid), tiles outside it read as empty and the
  * edges of primitives whose tile rows miss the band are not written.
  * With cs_bin_sort this replaces project (K3) + flatten + K4 + cumsum + K5 +
@@ -120,7 +123,8 @@ CS_API int cs_bin_count(const float *cubics_norm, const int32_t *prim_seg_offset
                  int32_t *counters, void *workspace, int64_t num_primitives,
                  int64_t num_segments, int64_t isect_capacity, int64_t dlist_capacity,
                  int32_t samples, int32_t img_height, int32_t img_width, int32_t tile_row_begin,
-                 int32_t tile_row_end, float aabb_pad, int32_t aniso, void *stream);
+                 int32_t tile_row_end, float aabb_pad, int32_t aniso, const float *ring,
+                 int32_t ring_segs_per_path, void *stream);
 
 /* Fused B200 binning, stage 2 of 2: scatter each (primitive, tile) pair into
  * its tile's range and sort every tile's pairs by (depth key, primitive id),

@@ -43,7 +43,7 @@ SIGNATURES = {
     "cs_bin_workspace_size": (_SZ, [_I64]),
     "cs_unit_lists_size": (_SZ, [_I64]),
     "cs_bin_count": (ctypes.c_int, [_P] * 13 + [_I64, _I64, _I64, _I64, _I32, _I32, _I32, _I32,
-                                                _I32, _F32, _I32, _P]),
+                                                _I32, _F32, _I32, _P, _I32, _P]),
     "cs_bin_sort": (ctypes.c_int, [_P] * 7 + [_I64, _I64, _I32, _I32, _I32, _I32] + [_P] * 12
                     + [_I64, _P, _P]),
     "cs_stage_workspace_size": (_SZ, [_I64]),

@@ -253,11 +253,37 @@ inline BinWorkspace bin_ws(void* base, long long ntiles) {
 
 inline size_t bin_ws_size(long long ntiles) { return align256(sizeof(int) * ntiles) * 3; }
 
+// Normalised control points of segment `seg`: from cubics_norm [n, 4, 2], or,
+// when ring != NULL, from the ring parameterisation of closed paths (segment k
+// of a path = ring points 3k .. 3k+3 mod 3G, normalised as ring / (W/2, H/2) - 1,
+// the same arithmetic as cs_ring_to_cubics).
+__device__ __forceinline__ void load_segment(const float* __restrict__ cn,
+                                             const float* __restrict__ ring, int G, float half_w,
+                                             float half_h, long long seg, float c[8]) {
+  if (!ring) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) c[k] = cn[seg * 8 + k];
+    return;
+  }
+  const long long path = seg / G;
+  const int k = (int)(seg - path * G);
+  const float2* rp = reinterpret_cast<const float2*>(ring) + path * 3 * G;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    int r = 3 * k + j;
+    if (r >= 3 * G) r -= 3 * G;
+    const float2 v = rp[r];
+    c[2 * j] = v.x / half_w - 1.0f;
+    c[2 * j + 1] = v.y / half_h - 1.0f;
+  }
+}
+
 // One warp per primitive: project + bound every segment, union the rects,
 // flatten all segments into edges, and add the primitive to the intersect and
 // edge-slot counts of its tiles within the band of tile rows [r0, r1).
 __global__ void __launch_bounds__(256) bin_prep_kernel(
-    const float* __restrict__ cn, const int* __restrict__ offs, const float* __restrict__ aa,
+    const float* __restrict__ cn, const float* __restrict__ ring, int ring_g,
+    const int* __restrict__ offs, const float* __restrict__ aa,
     const float* __restrict__ sw, const float* __restrict__ basis, float* __restrict__ cpx,
     float* __restrict__ edges, int* __restrict__ pr, int* __restrict__ hits,
     int* __restrict__ tile_counts, int* __restrict__ tile_ecounts, int* __restrict__ status,
@@ -281,8 +307,7 @@ __global__ void __launch_bounds__(256) bin_prep_kernel(
   int mnx = tbx, mny = tby, mxx = 0, mxy = 0;
   for (int i = s0 + lane; i < s1; i += 32) {
     float c[8], q[8];
-#pragma unroll
-    for (int k = 0; k < 8; ++k) c[k] = cn[(long long)i * 8 + k];
+    load_segment(cn, ring, ring_g, half_w, half_h, i, c);
     project_points(c, half_w, half_h, q);
     float4* dst = reinterpret_cast<float4*>(cpx + (long long)i * 8);
     dst[0] = make_float4(q[0], q[1], q[2], q[3]);
@@ -308,8 +333,7 @@ __global__ void __launch_bounds__(256) bin_prep_kernel(
     int s = q - si * S;
     long long seg = s0 + si;
     float c[8], pp[8];
-#pragma unroll
-    for (int k = 0; k < 8; ++k) c[k] = cn[seg * 8 + k];
+    load_segment(cn, ring, ring_g, half_w, half_h, seg, c);
     project_points(c, half_w, half_h, pp);
     float x, y;
     bernstein_point(pp, basis, S, s, x, y);
@@ -883,9 +907,10 @@ int cs_bin_count(const float* cubics_norm, const int32_t* prim_seg_offsets, cons
                  int64_t num_primitives, int64_t num_segments, int64_t isect_capacity,
                  int64_t dlist_capacity, int32_t samples, int32_t img_height, int32_t img_width,
                  int32_t tile_row_begin, int32_t tile_row_end, float aabb_pad, int32_t aniso,
-                 void* stream) {
+                 const float* ring, int32_t ring_segs_per_path, void* stream) {
   if (num_primitives < 0 || samples < 2 || img_height <= 0 || img_width <= 0 || !workspace ||
-      !counters || !tile_bins || !tile_dlist)
+      !counters || !tile_bins || !tile_dlist || (!ring && !cubics_norm) ||
+      (ring && (ring_segs_per_path <= 0 || num_segments != num_primitives * ring_segs_per_path)))
     return CS_ERR_ARG;
   cudaStream_t st = (cudaStream_t)stream;
   const int tbx = (img_width + kTile - 1) / kTile, tby = (img_height + kTile - 1) / kTile;
@@ -895,7 +920,7 @@ int cs_bin_count(const float* cubics_norm, const int32_t* prim_seg_offsets, cons
   cudaMemsetAsync(ws.tile_counts, 0, align256(sizeof(int) * nt) * 2, st);
   if (num_primitives > 0) {
     bin_prep_kernel<<<ceil_div(num_primitives * 32, 256), 256, 0, st>>>(
-        cubics_norm, prim_seg_offsets, aa_widths, stroke_widths, basis, cubics_px, edges_px,
+        cubics_norm, ring, ring_segs_per_path, prim_seg_offsets, aa_widths, stroke_widths, basis, cubics_px, edges_px,
         prim_tile_ranges, num_tiles_hit, ws.tile_counts, ws.tile_ecounts, counters + 1,
         num_primitives, num_segments, samples, 0.5f * (float)img_width,
         0.5f * (float)img_height, tbx, tby, r0, r1, aabb_pad, aniso);

@@ -376,9 +376,10 @@ __device__ __forceinline__ void fwd_entries(const DEntry* __restrict__ buf, int 
   }
 }
 
+// Returns whether the pixel composited this intersect (alpha >= alpha_min).
 template <bool STROKE>
-__device__ __forceinline__ void fwd_composite(FwdPix& p, const IMeta& m, int k) {
-  if (p.done) return;
+__device__ __forceinline__ bool fwd_composite(FwdPix& p, const IMeta& m, int k) {
+  if (p.done) return false;
   float cov;
   if (!STROKE) {
     float sign, dist;
@@ -388,7 +389,7 @@ __device__ __forceinline__ void fwd_composite(FwdPix& p, const IMeta& m, int k) 
     cov = stroke_coverage(p.md, m.b, m.a, dist, edge_d);
   }
   const float alpha = fminf(kAlphaCap, m.op * cov);
-  if (alpha < kAlphaMin) return;
+  if (alpha < kAlphaMin) return false;
   const float nT = p.T * (1.0f - alpha);
   const float vis = alpha * p.T;
   p.a0 += m.c0 * vis;
@@ -397,6 +398,7 @@ __device__ __forceinline__ void fwd_composite(FwdPix& p, const IMeta& m, int k) 
   p.T = nT;
   p.cur = k;
   if (nT <= kTransStop) p.done = true;
+  return true;
 }
 
 // Forward of one unit by one warp.  Returns false if a bounded wait gave up.
@@ -421,6 +423,7 @@ __device__ __forceinline__ bool forward_unit(const RasterArgs& A, int unit,
   int k = rs;          // next intersect
   int kb = rs - 32;    // first intersect of the batch in shared memory
   int recs = 0;        // records visited (a work measure for the backward's dispatch)
+  int contrib = 0;     // intersects some pixel of the strip composited
   bool mid = false;    // k partially visited (split across chunks)
   bool ok = true;
   for (int c = 0; c < nchunks; ++c) {
@@ -469,8 +472,9 @@ __device__ __forceinline__ bool forward_unit(const RasterArgs& A, int unit,
         const int rw = row_wind(ro), rc = row_cnt(ro);
         p0.w += rw; p1.w += rw; p0.n += rc; p1.n += rc;
       }
-      fwd_composite<STROKE>(p0, m, k);
-      fwd_composite<STROKE>(p1, m, k);
+      const bool c0 = fwd_composite<STROKE>(p0, m, k);
+      const bool c1 = fwd_composite<STROKE>(p1, m, k);
+      contrib += __any_sync(0xffffffffu, c0 || c1) ? 1 : 0;
       mid = false;
       ++k;
     }
@@ -515,8 +519,9 @@ __device__ __forceinline__ bool forward_unit(const RasterArgs& A, int unit,
     sse = warp_sum(sse);
     if (lane == 0) A.partials[unit] = sse;  // indexed by unit: a fixed reduction order
   }
-  // the backward visits about the same intersects and records
-  work = k > rs ? 2 * recs + 8 * (k - rs + (k < re ? 1 : 0)) : 0;
+  // the backward visits about the same intersects and records, and runs the
+  // gradient arithmetic for the whole warp where any pixel composited
+  work = k > rs ? 2 * recs + 4 * (k - rs + (k < re ? 1 : 0)) + 10 * contrib : 0;
   return ok;
 }
 

@@ -177,7 +177,8 @@ def bin_primitives(cubics_norm: torch.Tensor, offs: torch.Tensor, depths: torch.
                        nat.ptr(basis), nat.ptr(cubics_px), nat.ptr(edges), nat.ptr(prim_ranges),
                        nat.ptr(num_hit), nat.ptr(tile_bins), nat.ptr(tile_dlist),
                        nat.ptr(counters), ws.data_ptr(), p, g, INT64_MAX, INT64_MAX, s,
-                       int(img_h), int(img_w), r0, r1, float(aabb_pad), int(bool(aniso)), st),
+                       int(img_h), int(img_w), r0, r1, float(aabb_pad), int(bool(aniso)), None,
+                       0, st),
               "cs_bin_count")
     # the one host synchronisation of the forward: sizes + status
     n_isect, status, n_dbound, _ = (int(v) for v in counters.tolist())

@@ -2,8 +2,8 @@
 
 One step, all on the device and capturable as one CUDA graph:
 
-  ring params -> normalised cubics               cs_ring_to_cubics
-  projection, AABB, flatten, tile counts, scans  cs_bin_count
+  ring params -> projection, AABB, flatten,
+  tile counts, scans                             cs_bin_count (reads the ring)
   scatter, per-tile sort, edge staging           cs_bin_sort
   forward raster + clamped CHW image + MSE loss  cs_fill_forward (target given)
   SSIM (forward metric)                          cs_ssim
@@ -95,7 +95,6 @@ class FillTrainer:
         self.basis = _render.bernstein_basis(self.s, dev)
 
         e = g * (self.s - 1)
-        self.cn = torch.empty((g, 4, 2), device=dev, dtype=f32)
         self.cubics_px = torch.empty((g, 4, 2), device=dev, dtype=f32)
         self.edges = torch.empty((e, 2, 2), device=dev, dtype=f32)
         self.v_edges = torch.zeros((e, 2, 2), device=dev, dtype=f32)
@@ -144,30 +143,27 @@ class FillTrainer:
         self._main = torch.cuda.Stream(dev, priority=hi)
         self._fork = torch.cuda.Event()
         self._join = torch.cuda.Event()
-        self.launches_per_step = 8 + (1 if self.with_ssim else 0)
+        self.launches_per_step = 7 + (1 if self.with_ssim else 0)
 
     # ------------------------------------------------------------------
-    def _params_to_cubics(self, st):
-        nat.check(nat.call("cs_ring_to_cubics", self.ring.data_ptr(), self.cn.data_ptr(),
-                           self.num_paths, self.g_per_path, self.h, self.w, st),
-                  "cs_ring_to_cubics")
-
     def _bin(self, capacity: int, dcapacity: int, st):
+        """Projection, flattening, tile counts and scans, reading the control
+        points straight from the ring parameters."""
         r0, r1 = self.tile_rows
-        nat.check(nat.call("cs_bin_count", self.cn.data_ptr(), self.offs.data_ptr(),
+        nat.check(nat.call("cs_bin_count", None, self.offs.data_ptr(),
                            self.widths.data_ptr(), None, self.basis.data_ptr(),
                            self.cubics_px.data_ptr(), self.edges.data_ptr(),
                            self.prim_ranges.data_ptr(), self.num_hit.data_ptr(),
                            self.tile_bins.data_ptr(), self.tile_dlist.data_ptr(),
                            self.counters.data_ptr(), self.bin_ws.data_ptr(), self.num_paths,
                            self.num_segments, capacity, dcapacity, self.s, self.h, self.w, r0, r1,
-                           float(_render.DEFAULT_AABB_PAD), 0, st), "cs_bin_count")
+                           float(_render.DEFAULT_AABB_PAD), 0, self.ring.data_ptr(),
+                           self.g_per_path, st), "cs_bin_count")
 
     def probe_capacity(self, slack: float = 1.5, extra: int = 4096) -> tuple[int, int]:
         """Intersect and staged-record capacities from one counting pass (one
         host sync, at set-up), with slack for the parameters to move."""
         st = nat.stream(self.device)
-        self._params_to_cubics(st)
         self._bin(INT64_MAX, INT64_MAX, st)
         n, _, nd, _ = (int(v) for v in self.counters.tolist())
         return int(math.ceil(n * slack)) + extra, int(math.ceil(nd * slack)) + 64 * extra
@@ -177,7 +173,6 @@ class FillTrainer:
         st = nat.stream(self.device)
         r0, r1 = self.tile_rows
         status = self.counters.data_ptr() + 4
-        self._params_to_cubics(st)
         self._bin(self.capacity, self.dcapacity, st)
         nat.check(nat.call("cs_bin_sort", self.prim_ranges.data_ptr(), self.depths.data_ptr(),
                            self.tile_bins.data_ptr(), self.prim_sorted.data_ptr(),

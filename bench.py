@@ -227,6 +227,85 @@ def raster_work(tr):
     return int(pe_fwd), int(vis_fwd), int(pe_bwd), int(vis_bwd), n
 
 
+def executed_work(bins, istrips, rowoff, imeta, fidx, fts, h, w, tbx, n, visits=None):
+    """Pixel-edge pairs and pixel-intersect visits the B200 raster kernels
+    evaluate, as opposed to the reference algorithm's (raster_work): a warp
+    runs a 4x16-pixel strip, so every staged near-edge record of a walked
+    intersect costs 64 pixel-edge pairs and every intersect that can change
+    the strip (near records, or a fill row the far-edge offsets put inside)
+    costs 64 pixel visits.  The forward walks a strip's intersects until all
+    of its pixels have T <= 1e-4 (else to the tile's end), the backward from
+    the strip's largest final_idx down -- or, given the forward's visit lists,
+    only the listed intersects.  Intersects that cannot change the strip are
+    skipped in batches and counted as free."""
+    import numpy as np
+    if n == 0:
+        return 0, 0, 0, 0
+    rec = istrips[:n, :, 1].astype(np.int64)                      # [n, 4]
+    act = rec > 0
+    if rowoff is not None:
+        ro = rowoff[:n].reshape(n, 4, 4)
+        wind = (ro & 0xFFFF).astype(np.int16).astype(np.int32)
+        cnt = (ro.view(np.uint32) >> 16).astype(np.int32)
+        rule = imeta[:n, 3][:, None, None]
+        inside = np.where(rule == 0, (cnt & 1) != 0, wind != 0)
+        act |= inside.any(axis=2)
+    crec = np.vstack([np.zeros((1, 4), np.int64), np.cumsum(rec, axis=0)])
+    cact = np.vstack([np.zeros((1, 4), np.int64), np.cumsum(act, axis=0)])
+    tby = (h + 15) // 16
+    hp, wp = tby * 16, tbx * 16
+    fi = np.full((hp, wp), -1, np.int64)
+    fi[:h, :w] = fidx.reshape(h, w)
+    done = np.ones((hp, wp), bool)
+    done[:h, :w] = fts.reshape(h, w) <= 1e-4
+    # [tby, 4 strips, 4 rows, tbx, 16 cols] -> per strip
+    fmax = fi.reshape(tby, 4, 4, tbx, 16).max(axis=(2, 4))        # [tby, 4, tbx]
+    alld = done.reshape(tby, 4, 4, tbx, 16).all(axis=(2, 4))
+    rs = bins[:, 0].astype(np.int64).reshape(tby, 1, tbx)
+    re = bins[:, 1].astype(np.int64).reshape(tby, 1, tbx)
+    st = np.arange(4).reshape(1, 4, 1)
+    has = re > rs
+    kf = np.where(alld, np.minimum(fmax, re - 1), re - 1)
+    kb = np.minimum(fmax, re - 1)
+    okf = has & (kf >= rs)
+    okb = has & (kb >= rs)
+
+    def span(c, k, ok):
+        hi = np.clip(k + 1, 0, n)
+        lo = np.clip(rs, 0, n)
+        return np.where(ok, c[hi, st] - c[lo, st], 0).sum()
+
+    pe_f, vis_f = 64 * int(span(crec, kf, okf)), 64 * int(span(cact, kf, okf))
+    if visits is None:
+        return pe_f, vis_f, 64 * int(span(crec, kb, okb)), 64 * int(span(cact, kb, okb))
+    pe_b = vis_b = 0
+    for t in np.nonzero(bins[:, 1] > bins[:, 0])[0]:
+        t_rs, t_re = int(bins[t, 0]), int(bins[t, 1])
+        for s_ in range(4):
+            base = 4 * (t_rs + int(t)) + s_ * (t_re - t_rs + 1)
+            cnt = int(visits[base])
+            ids = visits[base + 1: base + 1 + cnt]
+            pe_b += int(rec[ids, s_].sum())
+            vis_b += cnt
+    return pe_f, vis_f, 64 * pe_b, 64 * vis_b
+
+
+def executed_roofline(flop_b, t_b, flop_f, t_f, peak):
+    """The raster kernels against the FP32 peak on the work they evaluate
+    (executed_work), beside the reference-algorithm figures: above 1.0 on the
+    reference work means the culled pairs were never computed, this one
+    measures how well the evaluated pairs use the SIMT pipes."""
+    a_b = flop_b / (t_b * 1e-3) / 1e12
+    a_f = flop_f / (t_f * 1e-3) / 1e12
+    return {"flop_per_launch": int(flop_b), "achieved": round(a_b, 3), "frac": round(a_b / peak, 4),
+            "forward": {"flop_per_launch": int(flop_f), "achieved": round(a_f, 3),
+                        "frac": round(a_f / peak, 4)},
+            "model": "same FLOP per pair and per visit, counted over what the kernels evaluate: "
+                     "64 pixels x staged near-edge records of walked intersects, 64 pixels x "
+                     "intersects that can change the strip (backward: the forward's visit "
+                     "lists)"}
+
+
 def ncu_traffic(kernel: str):
     """DRAM bytes (read + write) per launch of `kernel` from the committed ncu
     summary of the config-2 raster kernels (profiles/raster_fill_config2.md),
@@ -298,6 +377,10 @@ def run_b200(args, rank, world, local_rank):
     # dominant kernels, timed live with CUDA events on the launching stream
     t_fwd, t_bwd = kernel_times(tr, 10, flush, stream)
     pe_fwd, vis_fwd, pe_bwd, vis_bwd, n_now = raster_work(tr)
+    xe_fwd, xv_fwd, xe_bwd, xv_bwd = executed_work(
+        tr.tile_bins.cpu().numpy(), tr.istrips.cpu().numpy(), tr.rowoff.cpu().numpy(),
+        tr.imeta.cpu().numpy(), tr.fidx.cpu().numpy(), tr.fts.cpu().numpy(), tr.h, tr.w, tr.tbx,
+        n_now, tr.visits.cpu().numpy())
 
     # e2e through the drop-in API with host buffers
     e2e = None
@@ -344,6 +427,8 @@ def run_b200(args, rank, world, local_rank):
                 "launch_ms": round(t_bwd, 4),
                 "forward": {"launch_ms": round(t_fwd, 4), "flop_per_launch": flop_fwd,
                             "achieved": round(flop_fwd / (t_fwd * 1e-3) / 1e12, 3)},
+                "executed": executed_roofline(24 * xe_bwd + 30 * xv_bwd, t_bwd,
+                                              20 * xe_fwd + 12 * xv_fwd, t_fwd, fp32_peak),
             },
         }
         if e2e is not None:
@@ -518,6 +603,10 @@ def run_stroke(args, rank, world, local_rank):
                                   inv_sigma2s=render._inv_sigma2(wd), stroke_widths=widths.detach())
         _, fts, fidx = render.forward_raster(b, bg, h, w)
         pe_f, vis_f, pe_b, vis_b = binning_work(b, fts, fidx, h, w)
+        xe_f, xv_f, xe_b, xv_b = executed_work(
+            b.tile_bins.cpu().numpy(), b.isect_strips.cpu().numpy(), None, b.imeta.cpu().numpy(),
+            fidx.cpu().numpy(), fts.cpu().numpy(), h, w, b.tile_bounds[0], int(b.num_intersects),
+            b.visit_lists.cpu().numpy())
     t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -547,7 +636,9 @@ def run_stroke(args, rank, world, local_rank):
                                    "final_idx + 30 per pixel-intersect visit",
                      "launch_ms": round(t_bwd, 4),
                      "forward": {"launch_ms": round(t_fwd, 4),
-                                 "achieved": round(flop_f / (t_fwd * 1e-3) / 1e12, 3)}},
+                                 "achieved": round(flop_f / (t_fwd * 1e-3) / 1e12, 3)},
+                     "executed": executed_roofline(18 * xe_b + 30 * xv_b, t_bwd,
+                                                   14 * xe_f + 12 * xv_f, t_fwd, peak)},
     }
 
 

@@ -179,6 +179,10 @@ CS_API int cs_tile_stage(const int32_t *prim_ids_sorted, const int32_t *tile_bin
  * isect_strips, rowoff, dlist; unit_order may be NULL).  unit_order_bwd (may
  * be NULL; cs_unit_lists_size bytes) receives the same units bucketed by the
  * work this launch measured, the better dispatch order for the backward.
+ * visit_lists (may be NULL; cs_visit_lists_size bytes) receives, per 4-row
+ * strip, the ids of the intersects that composited at least one of its
+ * pixels; given to the backward, it walks only those (exactly the ones that
+ * can carry a gradient) instead of every intersect of the tile.
  * out_chw_clamped
  * [3, H, W] (may be NULL) also receives clamp(out, 0, 1) channel-major, the
  * image the training loss sees (the reference does torch.clamp + permute,
@@ -195,10 +199,12 @@ CS_API int cs_tile_stage(const int32_t *prim_ids_sorted, const int32_t *tile_bin
  * and (with target_chw) mse_partial_sum_kernel + reduce_sum_partial_kernel,
  * manbo/ops/metric.py:18-163. */
 CS_API size_t cs_raster_workspace_size(int64_t num_tiles);
+CS_API size_t cs_visit_lists_size(int64_t isect_capacity, int64_t num_tiles);
 CS_API int cs_fill_forward(const int32_t *prim_ids_sorted, const int32_t *tile_bins,
                     const int32_t *tile_dlist, const void *imeta, const int32_t *isect_strips,
                     const int32_t *rowoff, const void *dlist, const int32_t *unit_order,
-                    int32_t *unit_order_bwd, const float *background, float *out_img,
+                    int32_t *unit_order_bwd, int32_t *visit_lists, const float *background,
+                    float *out_img,
                     float *final_Ts, int32_t *final_idx, float *out_chw_clamped,
                     const float *target_chw, float *loss_out, int32_t *status,
                     void *workspace, int32_t img_height, int32_t img_width,
@@ -213,11 +219,15 @@ CS_API int cs_fill_forward(const int32_t *prim_ids_sorted, const int32_t *tile_b
  * masked to 0 <= out <= 1, with out_img [H, W, 3], target_chw [3, H, W] and
  * *mse_scale (device scalar, e.g. 2/N * dLoss).  v_opacities and
  * v_inv_sigma2s may be NULL (not accumulated).  workspace as for the forward.
+ * visit_lists (may be NULL: every intersect up to final_idx is walked) is the
+ * forward's output of the same frame; a list that does not fit the tile bins
+ * sets CS_ERR_ARG in status and its strip is skipped.
  * Replaces rasterize_cubic_fill_backward_kernel, cubic_splatting.py:1197-1651. */
 CS_API int cs_fill_backward(const int32_t *prim_ids_sorted, const int32_t *tile_bins,
                      const int32_t *tile_dlist, const void *imeta, const int32_t *isect_strips,
                      const int32_t *rowoff, const void *dlist, const int32_t *unit_order,
-                     const float *background, const float *final_Ts, const int32_t *final_idx,
+                     const int32_t *visit_lists, const float *background,
+                     const float *final_Ts, const int32_t *final_idx,
                      const float *v_output, const float *out_img, const float *target_chw,
                      const float *mse_scale, float *v_edges, float *v_colors,
                      float *v_opacities, float *v_inv_sigma2s, float *curve_contrib_rgb,
@@ -231,7 +241,8 @@ CS_API int cs_fill_backward(const int32_t *prim_ids_sorted, const int32_t *tile_
 CS_API int cs_stroke_forward(const int32_t *prim_ids_sorted, const int32_t *tile_bins,
                       const int32_t *tile_dlist, const void *imeta, const int32_t *isect_strips,
                       const void *dlist, const int32_t *unit_order, int32_t *unit_order_bwd,
-                      const float *background, float *out_img, float *final_Ts,
+                      int32_t *visit_lists, const float *background, float *out_img,
+                      float *final_Ts,
                       int32_t *final_idx, float *out_chw_clamped, const float *target_chw,
                       float *loss_out,
                       int32_t *status, void *workspace, int32_t img_height, int32_t img_width,
@@ -242,7 +253,8 @@ CS_API int cs_stroke_forward(const int32_t *prim_ids_sorted, const int32_t *tile
  * cubic_polyline_splatting.py:252-660. */
 CS_API int cs_stroke_backward(const int32_t *prim_ids_sorted, const int32_t *tile_bins,
                        const int32_t *tile_dlist, const void *imeta, const int32_t *isect_strips,
-                       const void *dlist, const int32_t *unit_order, const float *background,
+                       const void *dlist, const int32_t *unit_order,
+                       const int32_t *visit_lists, const float *background,
                        const float *final_Ts, const int32_t *final_idx, const float *v_output,
                        const float *out_img, const float *target_chw, const float *mse_scale,
                        float *v_edges, float *v_colors, float *v_opacities,

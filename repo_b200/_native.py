@@ -49,10 +49,11 @@ SIGNATURES = {
     "cs_stage_workspace_size": (_SZ, [_I64]),
     "cs_tile_stage": (ctypes.c_int, [_P] * 18 + [_I64, _I32, _I32, _P]),
     "cs_raster_workspace_size": (_SZ, [_I64]),
-    "cs_fill_forward": (ctypes.c_int, [_P] * 18 + [_I32, _I32, _I32, _I32, _P]),
-    "cs_fill_backward": (ctypes.c_int, [_P] * 23 + [_I32, _I32, _I32, _I32, _P]),
-    "cs_stroke_forward": (ctypes.c_int, [_P] * 17 + [_I32, _I32, _I32, _I32, _P]),
-    "cs_stroke_backward": (ctypes.c_int, [_P] * 23 + [_I32, _I32, _I32, _I32, _P]),
+    "cs_visit_lists_size": (_SZ, [_I64, _I64]),
+    "cs_fill_forward": (ctypes.c_int, [_P] * 19 + [_I32, _I32, _I32, _I32, _P]),
+    "cs_fill_backward": (ctypes.c_int, [_P] * 24 + [_I32, _I32, _I32, _I32, _P]),
+    "cs_stroke_forward": (ctypes.c_int, [_P] * 18 + [_I32, _I32, _I32, _I32, _P]),
+    "cs_stroke_backward": (ctypes.c_int, [_P] * 24 + [_I32, _I32, _I32, _I32, _P]),
     "cs_edge_grads_to_cubics": (ctypes.c_int, [_P, _P, _I64, _I32, _F32, _F32, _P]),
     "cs_ring_to_cubics": (ctypes.c_int, [_P, _P, _I64, _I32, _I32, _I32, _P]),
     "cs_edge_grads_to_ring": (ctypes.c_int, [_P, _P, _I64, _I32, _I32, _I32, _I32, _I32, _P,

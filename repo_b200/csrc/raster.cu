@@ -56,6 +56,8 @@ struct RasterArgs {
   const DEntry* dl;
   const int* order;      // optional unit lists (stage.cuh), heaviest bucket first
   int* order_next;       // forward: optional unit lists for the backward, by measured work
+  int* visits;           // optional per-strip lists of the intersects that composited a pixel
+                         // of the strip: the forward writes them, the backward walks them
   const float* bg;
   int H, W, tbx, r0, nunits;
   int* status;
@@ -91,6 +93,14 @@ struct UnitGeom {
   int tx, ty, st, rs, re;
   long long base;  // first record of the strip's list
 };
+
+// A strip's visit list: count, then up to re - rs intersect ids in ascending
+// order.  Tile t's four lists start at 4 (rs + t), so the lists of all tiles
+// with intersects fit 4 (I + num_tiles) ints without overlap (tiles without
+// intersects have no list).
+__device__ __forceinline__ long long visit_base(const UnitGeom& g) {
+  return 4LL * ((long long)g.rs + g.tile) + (long long)g.st * (g.re - g.rs + 1);
+}
 
 __device__ __forceinline__ UnitGeom unit_geom(const RasterArgs& A, int unit) {
   UnitGeom g;
@@ -164,15 +174,55 @@ struct IBatch {
   int4 m[3][32];
   int2 rg[32];
   int4 ro[32];
+  int kk[32];  // the intersect ids (-1: a listed id outside the tile, skipped)
 };
 
+// Whether intersect (meta m0..m2, strip range rg, row offsets ro) can change
+// any pixel of the strip.  With no near edge every pixel is farther than d_thr
+// from the polyline, so its coverage is saturated: a stroke's op * cov is below
+// alpha_min, and so is a fill's in every row the far-edge offsets put outside.
+// Such an intersect composites nothing in the forward and gets no gradient in
+// the backward, exactly as in the per-pixel loop.  The guard keeps the
+// pathological primitives (no edges, infinite or huge width, opacity or
+// d_thr) on the full path, where op * cov need not stay below alpha_min.
 template <bool STROKE>
-__device__ __forceinline__ void load_batch(const RasterArgs& A, int k0, int n, int st,
-                                           IBatch& b) {
+__device__ __forceinline__ bool intersect_active(const int4& m0, const int4& m1, const int4& m2,
+                                                 const int2& rg, const int4& ro) {
+  if (rg.y > 0) return true;
+  const float op = __int_as_float(m1.w), dthr = __int_as_float(m2.z);
+  if (!(op <= 1e20f && dthr <= 1e6f)) return true;
+  if (STROKE) return false;
+  const int r[4] = {ro.x, ro.y, ro.z, ro.w};
+  bool inside = false;
+#pragma unroll
+  for (int q = 0; q < kStripRows; ++q)
+    inside |= (m0.w == 0) ? (row_cnt(r[q]) & 1) != 0 : row_wind(r[q]) != 0;
+  return inside;
+}
+
+// Loads n intersects into the warp's batch -- k0 .. k0 + n - 1, or the ids
+// lst[0 .. n) of a visit list, each checked against the tile's [rs, re) -- and
+// returns the mask of those that can change a pixel of the strip (bit j:
+// batch entry j).
+template <bool STROKE>
+__device__ __forceinline__ unsigned load_batch(const RasterArgs& A, const int* lst, int k0, int n,
+                                               int st, int rs, int re, IBatch& b) {
   const int lane = threadIdx.x & 31;
+  bool act = false;
   __syncwarp();  // every lane is done with the previous batch
   if (lane < n) {
-    const long long k = (long long)k0 + lane;
+    int kid = k0 + lane;
+    if (lst) {
+      kid = __ldg(lst + lane);
+      if (kid < rs || kid >= re) {  // not a list the forward wrote for this strip
+        if (A.status) atomicExch(A.status, CS_ERR_ARG);
+        kid = -1;
+      }
+    }
+    b.kk[lane] = kid;
+  }
+  if (lane < n && b.kk[lane] >= 0) {
+    const long long k = b.kk[lane];
     const int4* q = reinterpret_cast<const int4*>(A.meta + k);
     const int4 m0 = __ldg(q), m1 = __ldg(q + 1), m2 = __ldg(q + 2);
     const int2 rg = __ldg(A.istrip + k * kStrips + st);
@@ -183,8 +233,10 @@ __device__ __forceinline__ void load_batch(const RasterArgs& A, int k0, int n, i
     b.m[2][lane] = m2;
     b.rg[lane] = rg;
     b.ro[lane] = ro;
+    act = intersect_active<STROKE>(m0, m1, m2, rg, ro);
   }
   __syncwarp();
+  return __ballot_sync(0xffffffffu, act);
 }
 
 __device__ __forceinline__ void batch_meta(const IBatch& b, int j, IMeta& m) {
@@ -411,6 +463,8 @@ __device__ __forceinline__ bool forward_unit(const RasterArgs& A, int unit,
   const int rs = g.rs, re = g.re, st = g.st;
   const int nd = re > rs ? strip_records_upto(A, re - 1, st) : 0;
   const int nchunks = max(1, (nd + kWChunk - 1) / kWChunk);
+  // an empty tile has no list (its bins need not lie between its neighbours')
+  int* vl = (A.visits && re > rs) ? A.visits + visit_base(g) : nullptr;
   const int ly = st * kStripRows + (lane >> 3), lx = (lane & 7) * 2;
   const int i = g.ty * kTile + ly, j0 = g.tx * kTile + lx;
   const bool in0 = i < A.H && j0 < A.W, in1 = i < A.H && j0 + 1 < A.W;
@@ -423,7 +477,9 @@ __device__ __forceinline__ bool forward_unit(const RasterArgs& A, int unit,
   int k = rs;          // next intersect
   int kb = rs - 32;    // first intersect of the batch in shared memory
   int recs = 0;        // records visited (a work measure for the backward's dispatch)
+  int visits = 0;      // intersects that could change a pixel of the strip
   int contrib = 0;     // intersects some pixel of the strip composited
+  unsigned amask = 0u; // active intersects of the batch
   bool mid = false;    // k partially visited (split across chunks)
   bool ok = true;
   for (int c = 0; c < nchunks; ++c) {
@@ -450,9 +506,14 @@ __device__ __forceinline__ bool forward_unit(const RasterArgs& A, int unit,
       }
       if (k >= kb + 32) {
         kb = k;
-        load_batch<STROKE>(A, kb, min(32, re - kb), st, ib);
+        amask = load_batch<STROKE>(A, nullptr, kb, min(32, re - kb), st, rs, re, ib);
       }
       const int j = k - kb;
+      if (!mid && !((amask >> j) & 1u)) {  // skip to the batch's next active intersect
+        const unsigned rest = amask & (0xfffffffeu << j);
+        k = rest ? kb + __ffs(rest) - 1 : min(kb + 32, re);
+        continue;
+      }
       IMeta m;
       batch_meta(ib, j, m);
       const int2 rg = ib.rg[j];
@@ -474,7 +535,11 @@ __device__ __forceinline__ bool forward_unit(const RasterArgs& A, int unit,
       }
       const bool c0 = fwd_composite<STROKE>(p0, m, k);
       const bool c1 = fwd_composite<STROKE>(p1, m, k);
-      contrib += __any_sync(0xffffffffu, c0 || c1) ? 1 : 0;
+      if (__any_sync(0xffffffffu, c0 || c1)) {
+        if (vl && lane == 0) vl[1 + contrib] = k;
+        ++contrib;
+      }
+      ++visits;
       mid = false;
       ++k;
     }
@@ -519,9 +584,10 @@ __device__ __forceinline__ bool forward_unit(const RasterArgs& A, int unit,
     sse = warp_sum(sse);
     if (lane == 0) A.partials[unit] = sse;  // indexed by unit: a fixed reduction order
   }
+  if (vl && lane == 0) vl[0] = contrib;
   // the backward visits about the same intersects and records, and runs the
   // gradient arithmetic for the whole warp where any pixel composited
-  work = k > rs ? 2 * recs + 4 * (k - rs + (k < re ? 1 : 0)) + 10 * contrib : 0;
+  work = k > rs ? 2 * recs + 4 * (visits + (k < re ? 1 : 0)) + 10 * contrib + (k - rs) / 4 : 0;
   return ok;
 }
 
@@ -784,6 +850,26 @@ __device__ __forceinline__ bool backward_unit(const RasterArgs& A, int unit,
   }
   kmax = min(warp_max_i(kmax), re - 1);  // this warp's last needed intersect
   if (kmax < rs) return true;
+  // The walk runs over positions q = nq - 1 .. 0: every intersect rs .. kmax
+  // (position q is intersect rs + q), or the forward's list of the strip's
+  // intersects that composited a pixel (no other intersect changes a pixel's
+  // T or gets a gradient: a pixel composites k exactly when alpha_k >=
+  // alpha_min and k <= final_idx).
+  const int* vl = nullptr;
+  int nq = kmax - rs + 1;
+  if (A.visits) {
+    vl = A.visits + visit_base(g);
+    const int cnt = vl[0];
+    if (cnt < 0 || cnt > re - rs) {  // not a list the forward wrote for this strip
+      if (lane == 0 && A.status) atomicExch(A.status, CS_ERR_ARG);
+      return true;
+    }
+    ++vl;
+    nq = cnt;
+    if (nq == 0) return true;
+    const int klast = vl[nq - 1];
+    if (klast >= rs && klast < kmax) kmax = klast;  // fewer record chunks to bring in
+  }
   const int nd = strip_records_upto(A, kmax, st);  // records of intersects <= kmax
   const int nchunks = max(1, (nd + kWChunk - 1) / kWChunk);
   const int last = nchunks - 1;
@@ -792,9 +878,10 @@ __device__ __forceinline__ bool backward_unit(const RasterArgs& A, int unit,
     bulk_load(buf[last & 1], A.dl + g.base + c0, (uint32_t)(nd - c0) * sizeof(DEntry),
               &bars[last & 1]);
   }
-  int k = kmax;       // next intersect (walking down)
-  int kb = kmax + 1;  // first intersect of the batch in shared memory (batch: kb .. kb + 31)
-  bool mid = false;   // k partially visited
+  int q = nq - 1;     // next position (walking down)
+  int qb = nq;        // first position of the batch in shared memory (batch: qb .. qb + 31)
+  unsigned amask = 0u;  // active intersects of the batch
+  bool mid = false;   // the intersect at q partially visited
   bool ok = true;
   for (int c = last; c >= 0; --c) {
     const int c0 = c * kWChunk, c1 = min(nd, c0 + kWChunk);
@@ -812,19 +899,20 @@ __device__ __forceinline__ bool backward_unit(const RasterArgs& A, int unit,
       if (!ok) break;
     }
     const DEntry* cb = buf[c & 1];  // record d of the strip is cb[d - c0]
-    while (k >= rs) {
-      const bool v0 = s[0].in && k <= s[0].fidx;
-      const bool v1 = s[1].in && k <= s[1].fidx;
-      if (!__any_sync(0xffffffffu, v0 || v1)) {
-        --k;
-        mid = false;
+    while (q >= 0) {
+      if (q < qb) {
+        qb = max(0, q - 31);
+        amask = load_batch<STROKE>(A, vl ? vl + qb : nullptr, rs + qb, q - qb + 1, st, rs, re, ib);
+      }
+      const int j = q - qb;
+      if (!mid && !((amask >> j) & 1u)) {  // skip to the batch's next lower active intersect
+        const unsigned below = amask & ((1u << j) - 1u);
+        q = below ? qb + 31 - __clz(below) : qb - 1;
         continue;
       }
-      if (k < kb) {
-        kb = max(rs, k - 31);
-        load_batch<STROKE>(A, kb, k - kb + 1, st, ib);
-      }
-      const int j = k - kb;
+      const int k = ib.kk[j];
+      const bool v0 = s[0].in && k <= s[0].fidx;
+      const bool v1 = s[1].in && k <= s[1].fidx;
       IMeta m;
       batch_meta(ib, j, m);
       const int2 rg = ib.rg[j];
@@ -904,7 +992,7 @@ __device__ __forceinline__ bool backward_unit(const RasterArgs& A, int unit,
         }
       }
       mid = false;
-      --k;
+      --q;
     }
     __syncwarp();
     // flush this chunk's edge gradients while its records are resident
@@ -919,7 +1007,7 @@ __device__ __forceinline__ bool backward_unit(const RasterArgs& A, int unit,
       dgrad[d - c0] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
     __syncwarp();
-    if (k < rs) {
+    if (q < 0) {
       if (more) {  // drain the prefetched chunk before the buffer is reused
         ok = wait_buffer(bars, (c - 1) & 1, phase, A.status);
       }
@@ -1039,6 +1127,11 @@ using namespace cs;
 
 extern "C" {
 
+size_t cs_visit_lists_size(int64_t isect_capacity, int64_t num_tiles) {
+  const int64_t n = (isect_capacity > 0 ? isect_capacity : 0) + (num_tiles > 0 ? num_tiles : 1);
+  return sizeof(int32_t) * (size_t)kStrips * (size_t)n;
+}
+
 size_t cs_raster_workspace_size(int64_t num_tiles) {
   return 256 + sizeof(float) * (size_t)kStrips * (size_t)(num_tiles > 0 ? num_tiles : 1);
 }
@@ -1047,7 +1140,8 @@ static int raster_forward(bool stroke, const int32_t* prim_ids_sorted, const int
                           const int32_t* tile_dlist, const void* imeta,
                           const int32_t* isect_strips, const int32_t* rowoff, const void* dlist,
                           const int32_t* unit_order, int32_t* unit_order_bwd,
-                          const float* background, float* out_img, float* final_Ts,
+                          int32_t* visit_lists, const float* background, float* out_img,
+                          float* final_Ts,
                           int32_t* final_idx, float* out_chw_clamped, const float* target_chw,
                           float* loss_out, int32_t* status, void* workspace, int32_t img_height,
                           int32_t img_width, int32_t tile_row_begin, int32_t tile_row_end,
@@ -1060,6 +1154,7 @@ static int raster_forward(bool stroke, const int32_t* prim_ids_sorted, const int
   stage_args(a, prim_ids_sorted, tile_bins, tile_dlist, imeta, isect_strips, rowoff, dlist,
              unit_order, background, status, workspace);
   a.order_next = unit_order_bwd;
+  a.visits = visit_lists;
   if (unit_order_bwd)
     cudaMemsetAsync(unit_order_bwd, 0, sizeof(int32_t) * kUnitBuckets, (cudaStream_t)stream);
   a.out = out_img;
@@ -1075,13 +1170,15 @@ static int raster_forward(bool stroke, const int32_t* prim_ids_sorted, const int
 int cs_fill_forward(const int32_t* prim_ids_sorted, const int32_t* tile_bins,
                     const int32_t* tile_dlist, const void* imeta, const int32_t* isect_strips,
                     const int32_t* rowoff, const void* dlist, const int32_t* unit_order,
-                    int32_t* unit_order_bwd, const float* background, float* out_img, float* final_Ts,
+                    int32_t* unit_order_bwd, int32_t* visit_lists, const float* background,
+                    float* out_img, float* final_Ts,
                     int32_t* final_idx, float* out_chw_clamped, const float* target_chw,
                     float* loss_out, int32_t* status, void* workspace, int32_t img_height,
                     int32_t img_width, int32_t tile_row_begin, int32_t tile_row_end,
                     void* stream) {
   return raster_forward(false, prim_ids_sorted, tile_bins, tile_dlist, imeta, isect_strips,
-                        rowoff, dlist, unit_order, unit_order_bwd, background, out_img, final_Ts, final_idx,
+                        rowoff, dlist, unit_order, unit_order_bwd, visit_lists, background, out_img,
+                        final_Ts, final_idx,
                         out_chw_clamped, target_chw, loss_out, status, workspace, img_height,
                         img_width, tile_row_begin, tile_row_end, stream);
 }
@@ -1089,13 +1186,14 @@ int cs_fill_forward(const int32_t* prim_ids_sorted, const int32_t* tile_bins,
 int cs_stroke_forward(const int32_t* prim_ids_sorted, const int32_t* tile_bins,
                       const int32_t* tile_dlist, const void* imeta, const int32_t* isect_strips,
                       const void* dlist, const int32_t* unit_order, int32_t* unit_order_bwd,
-                      const float* background, float* out_img, float* final_Ts,
-                      int32_t* final_idx,
+                      int32_t* visit_lists, const float* background, float* out_img,
+                      float* final_Ts, int32_t* final_idx,
                       float* out_chw_clamped, const float* target_chw, float* loss_out,
                       int32_t* status, void* workspace, int32_t img_height, int32_t img_width,
                       int32_t tile_row_begin, int32_t tile_row_end, void* stream) {
   return raster_forward(true, prim_ids_sorted, tile_bins, tile_dlist, imeta, isect_strips,
-                        nullptr, dlist, unit_order, unit_order_bwd, background, out_img, final_Ts, final_idx,
+                        nullptr, dlist, unit_order, unit_order_bwd, visit_lists, background, out_img,
+                        final_Ts, final_idx,
                         out_chw_clamped, target_chw, loss_out, status, workspace, img_height,
                         img_width, tile_row_begin, tile_row_end, stream);
 }
@@ -1103,8 +1201,9 @@ int cs_stroke_forward(const int32_t* prim_ids_sorted, const int32_t* tile_bins,
 static int raster_backward(bool stroke, const int32_t* prim_ids_sorted, const int32_t* tile_bins,
                            const int32_t* tile_dlist, const void* imeta,
                            const int32_t* isect_strips, const int32_t* rowoff, const void* dlist,
-                           const int32_t* unit_order, const float* background,
-                           const float* final_Ts, const int32_t* final_idx,
+                           const int32_t* unit_order, const int32_t* visit_lists,
+                           const float* background, const float* final_Ts,
+                           const int32_t* final_idx,
                            const float* v_output, const float* out_img, const float* target_chw,
                            const float* mse_scale, float* v_edges, float* v_colors,
                            float* v_opacities, float* v_stroke_widths, float* v_inv_sigma2s,
@@ -1120,6 +1219,7 @@ static int raster_backward(bool stroke, const int32_t* prim_ids_sorted, const in
   RasterArgs a{};
   stage_args(a, prim_ids_sorted, tile_bins, tile_dlist, imeta, isect_strips, rowoff, dlist,
              unit_order, background, status, workspace);
+  a.visits = const_cast<int32_t*>(visit_lists);  // read only by the backward
   a.fts_in = final_Ts;
   a.fidx_in = final_idx;
   a.v_out = v_output;
@@ -1140,7 +1240,7 @@ static int raster_backward(bool stroke, const int32_t* prim_ids_sorted, const in
 int cs_fill_backward(const int32_t* prim_ids_sorted, const int32_t* tile_bins,
                      const int32_t* tile_dlist, const void* imeta, const int32_t* isect_strips,
                      const int32_t* rowoff, const void* dlist, const int32_t* unit_order,
-                     const float* background, const float* final_Ts, const int32_t* final_idx,
+                     const int32_t* visit_lists, const float* background, const float* final_Ts, const int32_t* final_idx,
                      const float* v_output, const float* out_img, const float* target_chw,
                      const float* mse_scale, float* v_edges, float* v_colors,
                      float* v_opacities, float* v_inv_sigma2s, float* curve_contrib_rgb,
@@ -1148,7 +1248,8 @@ int cs_fill_backward(const int32_t* prim_ids_sorted, const int32_t* tile_bins,
                      int32_t img_height, int32_t img_width, int32_t tile_row_begin,
                      int32_t tile_row_end, void* stream) {
   return raster_backward(false, prim_ids_sorted, tile_bins, tile_dlist, imeta, isect_strips,
-                         rowoff, dlist, unit_order, background, final_Ts, final_idx, v_output,
+                         rowoff, dlist, unit_order, visit_lists, background, final_Ts, final_idx,
+                         v_output,
                          out_img, target_chw, mse_scale, v_edges, v_colors, v_opacities, nullptr,
                          v_inv_sigma2s, curve_contrib_rgb, curve_isect_contrib, status,
                          workspace, img_height, img_width, tile_row_begin, tile_row_end, stream);
@@ -1156,8 +1257,8 @@ int cs_fill_backward(const int32_t* prim_ids_sorted, const int32_t* tile_bins,
 
 int cs_stroke_backward(const int32_t* prim_ids_sorted, const int32_t* tile_bins,
                        const int32_t* tile_dlist, const void* imeta, const int32_t* isect_strips,
-                       const void* dlist, const int32_t* unit_order, const float* background,
-                       const float* final_Ts, const int32_t* final_idx, const float* v_output,
+                       const void* dlist, const int32_t* unit_order,
+                       const int32_t* visit_lists, const float* background, const float* final_Ts, const int32_t* final_idx, const float* v_output,
                        const float* out_img, const float* target_chw, const float* mse_scale,
                        float* v_edges, float* v_colors, float* v_opacities,
                        float* v_stroke_widths, float* v_inv_sigma2s, float* curve_contrib_rgb,
@@ -1165,7 +1266,8 @@ int cs_stroke_backward(const int32_t* prim_ids_sorted, const int32_t* tile_bins,
                        int32_t img_height, int32_t img_width, int32_t tile_row_begin,
                        int32_t tile_row_end, void* stream) {
   return raster_backward(true, prim_ids_sorted, tile_bins, tile_dlist, imeta, isect_strips,
-                         nullptr, dlist, unit_order, background, final_Ts, final_idx, v_output,
+                         nullptr, dlist, unit_order, visit_lists, background, final_Ts, final_idx,
+                         v_output,
                          out_img, target_chw, mse_scale, v_edges, v_colors, v_opacities,
                          v_stroke_widths, v_inv_sigma2s, curve_contrib_rgb, curve_isect_contrib,
                          status, workspace, img_height, img_width, tile_row_begin, tile_row_end,

@@ -128,6 +128,7 @@ class Binning:
     isect_strips: torch.Tensor                  # [I, 4, 2] per-strip record ranges
     unit_order: Optional[torch.Tensor] = None   # strip dispatch lists (staged work)
     unit_order_bwd: Optional[torch.Tensor] = None  # strip dispatch lists (forward's work)
+    visit_lists: Optional[torch.Tensor] = None  # per strip: intersects that composited a pixel
 
 
 def _offsets_error(offs: torch.Tensor, num_segments: int) -> ValueError:
@@ -319,19 +320,24 @@ def forward_raster(b: Binning, background, img_h: int, img_w: int, out_chw=None,
     ws = raster_workspace(dev, b.tile_bounds[0] * b.tile_bounds[1])
     if b.unit_order is not None and b.unit_order_bwd is None:
         b.unit_order_bwd = torch.empty_like(b.unit_order)
+    if b.visit_lists is None:
+        nbytes = int(nat.call("cs_visit_lists_size", int(b.num_intersects),
+                              b.tile_bounds[0] * b.tile_bounds[1]))
+        b.visit_lists = torch.empty((nbytes // 4,), dtype=torch.int32, device=dev)
     if not b.stroke:
         nat.check(nat.call("cs_fill_forward", nat.ptr(b.prim_ids_sorted), nat.ptr(b.tile_bins),
                            nat.ptr(b.tile_dlist), nat.ptr(b.imeta), nat.ptr(b.isect_strips),
                            nat.ptr(b.rowoff), nat.ptr(b.dlist), nat.ptr(b.unit_order),
-                           nat.ptr(b.unit_order_bwd), nat.ptr(background), nat.ptr(out),
-                           nat.ptr(fts), nat.ptr(fidx),
+                           nat.ptr(b.unit_order_bwd), nat.ptr(b.visit_lists), nat.ptr(background),
+                           nat.ptr(out), nat.ptr(fts), nat.ptr(fidx),
                            nat.ptr(out_chw), None, None, nat.ptr(status), ws.data_ptr(),
                            img_h, img_w, b.tile_rows[0], b.tile_rows[1], st), "cs_fill_forward")
     else:
         nat.check(nat.call("cs_stroke_forward", nat.ptr(b.prim_ids_sorted), nat.ptr(b.tile_bins),
                            nat.ptr(b.tile_dlist), nat.ptr(b.imeta), nat.ptr(b.isect_strips),
                            nat.ptr(b.dlist), nat.ptr(b.unit_order), nat.ptr(b.unit_order_bwd),
-                           nat.ptr(background), nat.ptr(out), nat.ptr(fts), nat.ptr(fidx),
+                           nat.ptr(b.visit_lists), nat.ptr(background), nat.ptr(out),
+                           nat.ptr(fts), nat.ptr(fidx),
                            nat.ptr(out_chw), None,
                            None, nat.ptr(status), ws.data_ptr(), img_h, img_w,
                            b.tile_rows[0], b.tile_rows[1], st), "cs_stroke_forward")
@@ -376,7 +382,8 @@ def raster_backward(b: Binning, num_primitives: int, background, final_ts, final
             nat.check(nat.call("cs_fill_backward", nat.ptr(b.prim_ids_sorted), nat.ptr(b.tile_bins),
                                nat.ptr(b.tile_dlist), nat.ptr(b.imeta),
                                nat.ptr(b.isect_strips), nat.ptr(b.rowoff), nat.ptr(b.dlist),
-                               nat.ptr(_bwd_lists(b)), nat.ptr(background), nat.ptr(final_ts),
+                               nat.ptr(_bwd_lists(b)), nat.ptr(b.visit_lists),
+                               nat.ptr(background), nat.ptr(final_ts),
                                nat.ptr(final_idx), nat.ptr(vo), nat.ptr(out_img),
                                nat.ptr(target_chw), nat.ptr(mse_scale), nat.ptr(v_edges),
                                nat.ptr(v_colors), nat.ptr(v_opac), nat.ptr(v_inv),
@@ -387,7 +394,8 @@ def raster_backward(b: Binning, num_primitives: int, background, final_ts, final
             nat.check(nat.call("cs_stroke_backward", nat.ptr(b.prim_ids_sorted),
                                nat.ptr(b.tile_bins), nat.ptr(b.tile_dlist), nat.ptr(b.imeta),
                                nat.ptr(b.isect_strips), nat.ptr(b.dlist),
-                               nat.ptr(_bwd_lists(b)), nat.ptr(background), nat.ptr(final_ts),
+                               nat.ptr(_bwd_lists(b)), nat.ptr(b.visit_lists),
+                               nat.ptr(background), nat.ptr(final_ts),
                                nat.ptr(final_idx), nat.ptr(vo), nat.ptr(out_img),
                                nat.ptr(target_chw), nat.ptr(mse_scale), nat.ptr(v_edges),
                                nat.ptr(v_colors), nat.ptr(v_opac), nat.ptr(v_sw), nat.ptr(v_inv),

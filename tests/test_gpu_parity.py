@@ -472,6 +472,111 @@ def test_unit_lists_bucket_every_strip_by_work_and_change_no_result(rows):
         assert_grad_close(g1[k], g2[k], k)
 
 
+def _stroke_binning(keep=300, h=256, w=256):
+    """Config-4 strokes over a 256x256 corner, binned and rendered forward."""
+    sc = scenes.config4()
+    cn = _t(sc.cubics_norm()[:keep])
+    offs = _t(np.arange(keep + 1, dtype=np.int32))
+    aa = torch.clamp(_t(sc.aa_widths[:keep]), min=1e-4)
+    col, op = _t(sc.colors[:keep]), _t(sc.opacities[:keep])
+    b = render.bin_primitives(cn, offs, _t(sc.depths[:keep]), aa, h, w, sc.samples, colors=col,
+                              opacities=op, inv_sigma2s=render._inv_sigma2(aa),
+                              stroke_widths=_t(sc.stroke_widths[:keep]))
+    bg = _t(sc.background)
+    out, fts, fidx = render.forward_raster(b, bg, h, w)
+    return b, bg, keep, out, fts, fidx
+
+
+def _check_visit_lists(b, fidx, h, w):
+    """Each strip's list: ascending ids inside its tile's [rs, re), ending at
+    the strip's largest final_idx (the last intersect any of its pixels
+    composited)."""
+    tbx = (w + 15) // 16
+    r0, r1 = b.tile_rows
+    bins = _np(b.tile_bins)
+    vl = _np(b.visit_lists)
+    fi = _np(fidx)
+    listed = 0
+    for ty in range(r0, r1):
+        for tx in range(tbx):
+            t = ty * tbx + tx
+            rs, re = (int(v) for v in bins[t])
+            if re <= rs:  # no intersects, no list
+                continue
+            for st in range(4):
+                base = 4 * (rs + t) + st * (re - rs + 1)
+                n = int(vl[base])
+                assert 0 <= n <= re - rs
+                ids = vl[base + 1: base + 1 + n]
+                assert np.all(np.diff(ids) > 0) and np.all((ids >= rs) & (ids < re))
+                rows = slice(ty * 16 + 4 * st, min(h, ty * 16 + 4 * st + 4))
+                cols = slice(tx * 16, min(w, tx * 16 + 16))
+                if n:
+                    assert ids[-1] == fi[rows, cols].max()
+                listed += n
+    return listed
+
+
+@pytest.mark.parametrize("stroke", [False, True])
+def test_visit_lists_walk_only_composited_intersects(stroke):
+    """The forward lists, per strip, the intersects that composited a pixel of
+    it; the backward walks only those and its gradients match the walk over
+    every intersect up to final_idx."""
+    import dataclasses
+    if stroke:
+        b, bg, p, out, fts, fidx = _stroke_binning()
+        h = w = 256
+    else:
+        args = fill_inputs(scenes.config1())
+        h, w = args[5], args[6]
+        b, inv, out, fts, fidx = gpu_fill(*args)
+        bg, p = _t(args[7], torch.float32), int(np.asarray(args[2]).shape[0])
+    assert _check_visit_lists(b, fidx, h, w) > 0
+    v_out = _t(np.asarray(scenes.seeded_grad(9, h, w), np.float32))
+    plain = dataclasses.replace(b, visit_lists=None)
+    g1 = render.raster_backward(b, p, bg, fts, fidx, v_out, h, w, collect_contrib=True,
+                                collect_isect_contrib=True)
+    g2 = render.raster_backward(plain, p, bg, fts, fidx, v_out, h, w, collect_contrib=True,
+                                collect_isect_contrib=True)
+    assert int(b.counters[1]) == 0
+    for name, a, c in zip(["v_edges", "v_colors", "v_opac", "v_inv", "v_sw", "contrib",
+                           "icontrib"], g1, g2):
+        if a is not None:
+            assert_grad_close(_np(a), _np(c), name)
+
+
+def test_visit_lists_that_do_not_fit_the_bins_set_an_error():
+    """A visit list not written by this frame's forward (counts past the
+    tile's intersects, ids outside it) is rejected strip by strip with
+    CS_ERR_ARG in the status word; every read stays inside the list buffer."""
+    from repo_b200 import _native as nat
+    b, bg, p, out, fts, fidx = _stroke_binning()
+    v_out = _t(np.asarray(scenes.seeded_grad(9, 256, 256), np.float32))
+    good = b.visit_lists.clone()
+    for fill in (1 << 30, -7):
+        b.visit_lists.fill_(fill)
+        b.counters[1] = 0
+        render.raster_backward(b, p, bg, fts, fidx, v_out, 256, 256)
+        assert int(b.counters[1]) == nat.CS_ERR_ARG
+    # counts that fit, ids that do not
+    bins = _np(b.tile_bins)
+    bases = [4 * (int(rs) + t) + st * (int(re) - int(rs) + 1)
+             for t, (rs, re) in enumerate(bins) if re > rs for st in range(4)]
+    host = _np(good).copy()
+    keep = np.zeros(host.shape, bool)
+    keep[bases] = True
+    assert (host[bases] > 0).any()
+    host[~keep] = -1
+    b.visit_lists.copy_(torch.from_numpy(host))
+    b.counters[1] = 0
+    render.raster_backward(b, p, bg, fts, fidx, v_out, 256, 256)
+    assert int(b.counters[1]) == nat.CS_ERR_ARG
+    b.visit_lists.copy_(good)
+    b.counters[1] = 0
+    g = render.raster_backward(b, p, bg, fts, fidx, v_out, 256, 256)
+    assert int(b.counters[1]) == 0 and torch.isfinite(g[0]).all()
+
+
 def test_image_size_not_multiple_of_tile():
     sc = scenes.small_fill_scene(77, h=45, w=61, paths=7)
     args = fill_inputs(sc)

@@ -50,8 +50,9 @@ CS_API const char *cs_version(void);
  * the roots of B'(t), padded by max(aabb_pad, support) + half stroke width (or
  * the chord-anisotropic pad), tile rectangle [min, max) clamped to the grid.
  * Replaces project_cubics_2d_forward_kernel, cubic_splatting.py:546-747.
- * cubics_norm/cubics_px: [n, 4, 2]; stroke_widths, support_radii: [n];
- * tile_ranges: [n, 4]; num_tiles_hit: [n]. */
+ * cubics_norm/cubics_px: [n, 4, 2]; stroke_widths, support_radii: [n] (NULL
+ * reads as 0); tile_ranges: [n, 4]; num_tiles_hit: [n] (may be NULL).  With
+ * tile_ranges NULL only cubics_px is written (projection only). */
 CS_API int cs_project_cubics(const float *cubics_norm, const float *stroke_widths,
                       const float *support_radii, float *cubics_px, int32_t *tile_ranges,
                       int32_t *num_tiles_hit, int64_t num_curves, int32_t img_height,
@@ -64,6 +65,40 @@ CS_API int cs_project_cubics(const float *cubics_norm, const float *stroke_width
  * cubics_px: [n, 4, 2] -> edges_px: [n*(S-1), 2, 2]. */
 CS_API int cs_flatten_bernstein(const float *cubics_px, const float *basis, float *edges_px,
                          int64_t num_segments, int32_t samples, void *stream);
+
+/* Adaptive de Casteljau flattening (flatten_method "de_casteljau"): each
+ * cubic is split at t = 1/2 until its inner control points lie within tol_px
+ * (floored at 1e-4) of its chord, at most max_depth = ceil(log2(S - 1)) times;
+ * each leaf becomes one edge (its first and last control points), ordered by
+ * segment then t.  Outputs: edges_px [E, 2, 2], segment_edge_offsets [n + 1]
+ * and (optional, from prim_seg_offsets [P + 1]) prim_edge_offsets [P + 1] CSR
+ * offsets, edge_t_starts / edge_t_ends [E] leaf parameter intervals.  E is at
+ * most n << max_depth (cs_de_casteljau_edge_capacity); the buffers hold that
+ * many edges and E = segment_edge_offsets[n].  Works on the device without a
+ * host synchronisation; status (device int, may be NULL) receives
+ * CS_ERR_CAPACITY if edge_capacity is too small for the leaves written, and
+ * CS_ERR_ARG for segment offsets out of range.
+ * Replaces the de_casteljau branch of _flatten_cubics_to_edges,
+ * cubic_splatting.py:1729-1832, with cubic_adaptive_flatness_flags_kernel
+ * (:1863-1957) and cubic_split_half_kernel (:1960-2068). */
+CS_API int32_t cs_de_casteljau_max_depth(int32_t samples);
+CS_API int64_t cs_de_casteljau_edge_capacity(int64_t num_segments, int32_t samples);
+CS_API int cs_flatten_de_casteljau(const float *cubics_px, const int32_t *prim_seg_offsets,
+                                   int64_t num_segments, int64_t num_primitives,
+                                   int32_t samples, float tol_px, float *edges_px,
+                                   int32_t *prim_edge_offsets, int32_t *segment_edge_offsets,
+                                   float *edge_t_starts, float *edge_t_ends,
+                                   int64_t edge_capacity, int32_t *status, void *stream);
+
+/* The two steps of the adaptive flatten on their own: per-cubic flatness flag
+ * (1 = inner control points within tol_px, floored at 1e-4, of the chord; all
+ * 1 with force_flat) and the midpoint split into left / right halves, each
+ * [n, 4, 2].  Replace cubic_adaptive_flatness_flags_kernel and
+ * cubic_split_half_kernel, cubic_splatting.py:1863-2068. */
+CS_API int cs_cubic_flatness_flags(const float *cubics, uint8_t *out_flat, int64_t num_cubics,
+                                   float tol_px, int32_t force_flat, void *stream);
+CS_API int cs_cubic_split_half(const float *cubics, float *left, float *right,
+                               int64_t num_cubics, void *stream);
 
 /* Union of segment tile rectangles per primitive (CSR offsets over segments).
  * Replaces primitive_tile_ranges_from_segment_ranges_kernel,
@@ -112,15 +147,19 @@ CS_API int cs_isect_edge_ranges(const int32_t *prim_ids_sorted, const int32_t *p
  * cs_ring_to_cubics does, and cubics_norm may be NULL.  For a band
  * (rows other than the whole grid), tiles outside it read as empty and the
  * edges of primitives whose tile rows miss the band are not written.
+ * prim_edge_offsets [P + 1] (may be NULL) selects pre-flattened edges: edges_px
+ * then holds edges already written (e.g. by cs_flatten_de_casteljau) with
+ * these CSR offsets, is only read by later stages, and the edge-slot counts
+ * use each primitive's own edge count.
  * With cs_bin_sort this replaces project (K3) + flatten + K4 + cumsum + K5 +
  * torch.sort + K6 of _CubicFillSplatFunction.forward, cubic_splatting.py:2815-2908.
  * Workspace: cs_bin_workspace_size(num_tiles). */
 CS_API size_t cs_bin_workspace_size(int64_t num_tiles);
 CS_API int cs_bin_count(const float *cubics_norm, const int32_t *prim_seg_offsets,
                  const float *aa_widths, const float *stroke_widths, const float *basis,
-                 float *cubics_px, float *edges_px, int32_t *prim_tile_ranges,
-                 int32_t *num_tiles_hit, int32_t *tile_bins, int32_t *tile_dlist,
-                 int32_t *counters, void *workspace, int64_t num_primitives,
+                 float *cubics_px, float *edges_px, const int32_t *prim_edge_offsets,
+                 int32_t *prim_tile_ranges, int32_t *num_tiles_hit, int32_t *tile_bins,
+                 int32_t *tile_dlist, int32_t *counters, void *workspace, int64_t num_primitives,
                  int64_t num_segments, int64_t isect_capacity, int64_t dlist_capacity,
                  int32_t samples, int32_t img_height, int32_t img_width, int32_t tile_row_begin,
                  int32_t tile_row_end, float aabb_pad, int32_t aniso, const float *ring,
@@ -271,6 +310,18 @@ CS_API int cs_stroke_backward(const int32_t *prim_ids_sorted, const int32_t *til
 CS_API int cs_edge_grads_to_cubics(const float *v_edges, float *v_cubics, int64_t num_segments,
                             int32_t edges_per_segment, float scale_x, float scale_y,
                             void *stream);
+
+/* Edge gradients of a de Casteljau flattening -> cubic control-point
+ * gradients: v_P_k = sum over the segment's edges of gs B_k(t0) + ge B_k(t1),
+ * then the optional per-axis scale.  segment_edge_offsets [n + 1] and
+ * edge_t_starts / edge_t_ends as written by cs_flatten_de_casteljau.
+ * Replaces _accumulate_edge_grads_to_cubics_csr_kernel,
+ * cubic_splatting.py:2399-2487. */
+CS_API int cs_edge_grads_to_cubics_csr(const float *v_edges, const float *edge_t_starts,
+                                       const float *edge_t_ends,
+                                       const int32_t *segment_edge_offsets, float *v_cubics,
+                                       int64_t num_segments, float scale_x, float scale_y,
+                                       void *stream);
 
 /* Ring parameterisation of closed paths (the B200 training step's
  * parameters): ring [P, 3G, 2] pixel-space points; segment k of a path is

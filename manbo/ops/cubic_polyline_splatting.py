@@ -133,8 +133,10 @@ def rasterize_cubic_polyline_backward_tilelang(tile_bounds, block, img_size, pri
         _as_f32_contig(final_Ts), _as_i32_contig(final_idx), _as_f32_contig(v_output), v_edges,
         v_colors, v_opac, v_sw, v_inv, int(curve_contrib_rgb is not None), curve_contrib_rgb,
         int(curve_isect_contrib is not None), curve_isect_contrib)
-    v_cubics_px = _accumulate_edge_grads_to_cubics(v_edges, g, distance_samples=distance_samples,
-                                                   flatten_method=flatten_method)
+    v_cubics_px = _accumulate_edge_grads_to_cubics(
+        v_edges, g, distance_samples=distance_samples, flatten_method=flatten_method,
+        segment_edge_offsets=segment_edge_offsets, edge_t_starts=edge_t_starts,
+        edge_t_ends=edge_t_ends)
     return v_cubics_px, v_colors, v_opac, v_sw, v_inv
 
 

@@ -129,13 +129,14 @@ def project_cubics_2d_forward_tilelang(cubics_norm, stroke_widths, support_radii
 
 def _flatten_cubics_to_edges(cubics_px, primitive_seg_offsets, *, distance_samples,
                              flatten_method=DEFAULT_CUBIC_FLATTEN_METHOD):
-    """Uniform Bernstein flatten (cubic_splatting.py:1654-1846, bernstein branch)."""
+    """Flatten cubics into edges once per frame (cubic_splatting.py:1654-1846):
+    uniform Bernstein samples, or the adaptive de Casteljau split with CSR
+    segment offsets and leaf parameter intervals."""
     cubics = _as_f32_contig(cubics_px)
     offs = _as_i32_contig(primitive_seg_offsets).view(-1)
     s = max(2, int(distance_samples))
     e = s - 1
-    if normalize_cubic_flatten_method(flatten_method) != CUBIC_FLATTEN_METHOD_BERNSTEIN:
-        raise NotImplementedError("de_casteljau flattening is not implemented in the B200 path")
+    method = normalize_cubic_flatten_method(flatten_method)
     if cubics.ndim != 3 or tuple(cubics.shape[1:]) != (4, 2):
         raise ValueError(f"cubics_px must be [N,4,2], got {tuple(cubics.shape)}")
     if offs.ndim != 1 or int(offs.numel()) <= 0:
@@ -146,6 +147,16 @@ def _flatten_cubics_to_edges(cubics_px, primitive_seg_offsets, *, distance_sampl
     if g <= 0:
         return (torch.empty((0, 2, 2), dtype=torch.float32, device=cubics.device), edge_offsets,
                 torch.zeros((1,), dtype=torch.int32, device=cubics.device), None, None)
+    if method == CUBIC_FLATTEN_METHOD_DE_CASTELJAU:
+        status = torch.zeros((1,), dtype=torch.int32, device=cubics.device)
+        edges, peo, seg, t0, t1 = _r.flatten_de_casteljau(cubics, offs, s, status)
+        n_edges, st = (int(v) for v in torch.stack([seg[-1], status[0]]).tolist())
+        nat.check(st, "cs_flatten_de_casteljau")
+        if int(offs[-1].item()) != g:
+            raise ValueError(
+                "primitive_seg_offsets end does not match segment count during flatten: "
+                f"edge_offsets[-1]={int(peo[-1].item())}, expected={n_edges}")
+        return edges[:n_edges], peo, seg, t0[:n_edges], t1[:n_edges]
     edges = torch.empty((g * e, 2, 2), dtype=torch.float32, device=cubics.device)
     nat.check(nat.call("cs_flatten_bernstein", nat.ptr(cubics),
                        nat.ptr(_r.bernstein_basis(s, cubics.device)), nat.ptr(edges), g, s,
@@ -333,10 +344,28 @@ def _accumulate_edge_grads_to_cubics(v_edges, num_segments, *, distance_samples,
                                      segment_edge_offsets=None, edge_t_starts=None,
                                      edge_t_ends=None, threads=DEFAULT_THREADS):
     s = max(2, int(distance_samples))
-    if normalize_cubic_flatten_method(flatten_method) != CUBIC_FLATTEN_METHOD_BERNSTEIN:
-        raise NotImplementedError("de_casteljau flattening is not implemented in the B200 path")
     if int(num_segments) <= 0:
         return torch.empty((0, 4, 2), dtype=torch.float32, device=v_edges.device)
+    if normalize_cubic_flatten_method(flatten_method) == CUBIC_FLATTEN_METHOD_DE_CASTELJAU:
+        if segment_edge_offsets is None or edge_t_starts is None or edge_t_ends is None:
+            raise ValueError("de_casteljau flatten backward requires CSR metadata "
+                             "(segment_edge_offsets, edge_t_starts, edge_t_ends)")
+        seg = _as_i32_contig(segment_edge_offsets).view(-1)
+        if int(seg.numel()) != int(num_segments) + 1:
+            raise ValueError("segment_edge_offsets size mismatch: "
+                             f"got {int(seg.numel())}, expected {int(num_segments) + 1}")
+        first, last = (int(v) for v in seg[[0, -1]].tolist())
+        if first != 0:
+            raise ValueError(f"segment_edge_offsets must start at 0, got {first}")
+        if last != int(v_edges.shape[0]) or last != int(edge_t_starts.numel()) or \
+                last != int(edge_t_ends.numel()):
+            raise ValueError("de_casteljau edge metadata size mismatch: "
+                             f"offsets end at {last}, v_edges {int(v_edges.shape[0])}, "
+                             f"t starts {int(edge_t_starts.numel())}, "
+                             f"t ends {int(edge_t_ends.numel())}")
+        return _r.edge_grads_to_cubics_csr(_as_f32_contig(v_edges), seg,
+                                           _as_f32_contig(edge_t_starts).view(-1),
+                                           _as_f32_contig(edge_t_ends).view(-1), int(num_segments))
     expected = int(num_segments) * (s - 1)
     if int(v_edges.shape[0]) != expected:
         raise ValueError(f"v_edges size mismatch: got {int(v_edges.shape[0])}, expected {expected}")
@@ -383,8 +412,10 @@ def rasterize_cubic_fill_backward_tilelang(tile_bounds, block, img_size, primiti
         _as_f32_contig(final_Ts), _as_i32_contig(final_idx), _as_f32_contig(v_output), v_edges,
         v_colors, v_opac, v_inv, int(curve_contrib_rgb is not None), curve_contrib_rgb,
         int(curve_isect_contrib is not None), curve_isect_contrib)
-    v_cubics_px = _accumulate_edge_grads_to_cubics(v_edges, g, distance_samples=distance_samples,
-                                                   flatten_method=flatten_method)
+    v_cubics_px = _accumulate_edge_grads_to_cubics(
+        v_edges, g, distance_samples=distance_samples, flatten_method=flatten_method,
+        segment_edge_offsets=segment_edge_offsets, edge_t_starts=edge_t_starts,
+        edge_t_ends=edge_t_ends)
     return v_cubics_px, v_colors, v_opac, v_inv
 
 
@@ -407,12 +438,32 @@ def render_cubic_fill_splat_tilelang(cubics_norm, primitive_seg_offsets, colors,
         flatten_method=flatten_method, process_fn=process_fn)
 
 
-def cubic_adaptive_flatness_flags_tilelang(*args, **kwargs):
-    raise NotImplementedError("de_casteljau adaptive flattening is not implemented in the B200 path")
+def cubic_adaptive_flatness_flags_tilelang(cubics, *, tol_px, force_flat=False,
+                                           threads=DEFAULT_THREADS):
+    """Per-cubic flatness flags [N] uint8 of the adaptive flatten
+    (cubic_splatting.py:1915-1957)."""
+    c = _as_f32_contig(cubics)
+    nat.require_cuda(c, "cubics")
+    n = int(c.shape[0])
+    out = torch.empty((n,), dtype=torch.uint8, device=c.device)
+    if n > 0:
+        nat.check(nat.call("cs_cubic_flatness_flags", nat.ptr(c), nat.ptr(out), n,
+                           float(tol_px), int(bool(force_flat)), _stream(c)),
+                  "cs_cubic_flatness_flags")
+    return out
 
 
-def cubic_split_half_tilelang(*args, **kwargs):
-    raise NotImplementedError("de_casteljau adaptive flattening is not implemented in the B200 path")
+def cubic_split_half_tilelang(cubics, *, threads=DEFAULT_THREADS):
+    """Split cubics at t = 1/2 into left / right halves (cubic_splatting.py:2031-2068)."""
+    c = _as_f32_contig(cubics)
+    nat.require_cuda(c, "cubics")
+    n = int(c.shape[0])
+    left = torch.empty((n, 4, 2), dtype=torch.float32, device=c.device)
+    right = torch.empty((n, 4, 2), dtype=torch.float32, device=c.device)
+    if n > 0:
+        nat.check(nat.call("cs_cubic_split_half", nat.ptr(c), nat.ptr(left), nat.ptr(right), n,
+                           _stream(c)), "cs_cubic_split_half")
+    return left, right
 
 
 __all__ = [

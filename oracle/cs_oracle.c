@@ -586,6 +586,136 @@ void cso_edge_grads_to_cubics(int64_t num_segments, int edges_per_segment, const
 }
 
 /* ------------------------------------------------------------------------ */
+/* adaptive de Casteljau flattening, restated breadth-first as the reference  */
+/* runs it (manbo/ops/cubic_splatting.py:1729-1832): per depth, flatness      */
+/* flags (:1925-1953, its host branch :1924-1946), split of the non-flat      */
+/* cubics at t = 1/2 (:2000-2028), leaves sorted by (segment, t0).            */
+
+static inline float dc_max(float a, float b) { /* torch.maximum: NaN wins */
+    if (a != a) return a;
+    if (b != b) return b;
+    return a > b ? a : b;
+}
+
+static inline float dc_clamp_min(float a, float lo) { return a != a ? a : (a < lo ? lo : a); }
+
+static int dc_is_flat(const float *c, float tol) {
+    const float lx = c[6] - c[0], ly = c[7] - c[1];
+    const float chord2 = lx * lx + ly * ly;
+    const float chord = sqrtf(dc_clamp_min(chord2, 1e-6f));
+    const float v1x = c[2] - c[0], v1y = c[3] - c[1], v2x = c[4] - c[0], v2y = c[5] - c[1];
+    const float cross1 = fabsf(lx * v1y - ly * v1x);
+    const float cross2 = fabsf(lx * v2y - ly * v2x);
+    float dmax = dc_max(cross1 / chord, cross2 / chord);
+    if (chord2 <= 1e-6f) {
+        const float n1 = sqrtf(dc_clamp_min(v1x * v1x + v1y * v1y, 0.0f));
+        const float n2 = sqrtf(dc_clamp_min(v2x * v2x + v2y * v2y, 0.0f));
+        dmax = dc_max(n1, dc_max(n2, sqrtf(dc_clamp_min(chord2, 0.0f))));
+    }
+    return dmax <= tol;
+}
+
+typedef struct { float c[8]; int64_t sid; float t0, t1; } dc_node;
+
+static int64_t dc_key_base;
+static int dc_cmp(const void *a, const void *b) {
+    const dc_node *x = (const dc_node *)a, *y = (const dc_node *)b;
+    const int64_t kx = x->sid * (dc_key_base + 1) + (int64_t)rintf(x->t0 * (float)dc_key_base);
+    const int64_t ky = y->sid * (dc_key_base + 1) + (int64_t)rintf(y->t0 * (float)dc_key_base);
+    return kx < ky ? -1 : (kx > ky ? 1 : 0);
+}
+
+/* Returns the number of edges E; edges [E, 2, 2], t0/t1 [E], seg_offs
+   [nseg + 1].  The output buffers hold nseg << max_depth edges. */
+int64_t cso_flatten_de_casteljau(int64_t nseg, int samples, float tol, const float *cubics,
+                                 float *edges, float *t0o, float *t1o, int32_t *seg_offs) {
+    const int e_per = (samples < 2 ? 2 : samples) - 1;
+    const int max_depth = (int)ceil(log2((double)(e_per > 1 ? e_per : 1)));
+    if (tol < 1e-4f) tol = 1e-4f;
+    const int64_t cap = nseg << max_depth;
+    dc_node *active = (dc_node *)malloc(sizeof(dc_node) * (size_t)(cap > 0 ? cap : 1));
+    dc_node *next = (dc_node *)malloc(sizeof(dc_node) * (size_t)(cap > 0 ? cap : 1));
+    dc_node *leaves = (dc_node *)malloc(sizeof(dc_node) * (size_t)(cap > 0 ? cap : 1));
+    int64_t na = nseg, nl = 0;
+    for (int64_t g = 0; g < nseg; ++g) {
+        memcpy(active[g].c, cubics + g * 8, sizeof(float) * 8);
+        active[g].sid = g;
+        active[g].t0 = 0.0f;
+        active[g].t1 = 1.0f;
+    }
+    for (int depth = 0; depth <= max_depth && na > 0; ++depth) {
+        int64_t nsplit = 0;
+        for (int64_t i = 0; i < na; ++i) {
+            if (depth >= max_depth || dc_is_flat(active[i].c, tol)) leaves[nl++] = active[i];
+            else active[nsplit++] = active[i];
+        }
+        /* children: all left halves, then all right halves */
+        for (int64_t i = 0; i < nsplit; ++i) {
+            const dc_node *p = &active[i];
+            dc_node *l = &next[i], *r = &next[nsplit + i];
+            for (int a = 0; a < 2; ++a) {
+                const float p0 = p->c[a], p1 = p->c[2 + a], p2 = p->c[4 + a], p3 = p->c[6 + a];
+                const float p01 = 0.5f * (p0 + p1), p12 = 0.5f * (p1 + p2), p23 = 0.5f * (p2 + p3);
+                const float p012 = 0.5f * (p01 + p12), p123 = 0.5f * (p12 + p23);
+                const float p0123 = 0.5f * (p012 + p123);
+                l->c[a] = p0; l->c[2 + a] = p01; l->c[4 + a] = p012; l->c[6 + a] = p0123;
+                r->c[a] = p0123; r->c[2 + a] = p123; r->c[4 + a] = p23; r->c[6 + a] = p3;
+            }
+            const float tm = 0.5f * (p->t0 + p->t1);
+            l->sid = r->sid = p->sid;
+            l->t0 = p->t0; l->t1 = tm;
+            r->t0 = tm; r->t1 = p->t1;
+        }
+        dc_node *tmp = active; active = next; next = tmp;
+        na = 2 * nsplit;
+    }
+    dc_key_base = (int64_t)1 << max_depth;
+    qsort(leaves, (size_t)nl, sizeof(dc_node), dc_cmp);
+    for (int64_t g = 0; g <= nseg; ++g) seg_offs[g] = 0;
+    for (int64_t i = 0; i < nl; ++i) {
+        const dc_node *q = &leaves[i];
+        edges[i * 4 + 0] = q->c[0]; edges[i * 4 + 1] = q->c[1];
+        edges[i * 4 + 2] = q->c[6]; edges[i * 4 + 3] = q->c[7];
+        t0o[i] = q->t0;
+        t1o[i] = q->t1;
+        seg_offs[q->sid + 1] += 1;
+    }
+    for (int64_t g = 0; g < nseg; ++g) seg_offs[g + 1] += seg_offs[g];
+    free(active); free(next); free(leaves);
+    return nl;
+}
+
+/* de Casteljau edge grads -> cubic grads over CSR edge ranges with the
+   leaves' parameter intervals (cubic_splatting.py:2420-2487) */
+void cso_edge_grads_csr(int64_t num_segments, const int32_t *seg_offs, const float *t_start,
+                        const float *t_end, const float *v_edges, float *v_cubics) {
+    for (int64_t g = 0; g < num_segments; ++g) {
+        float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        for (int64_t e = seg_offs[g]; e < seg_offs[g + 1]; ++e) {
+            const float t0 = t_start[e], t1 = t_end[e];
+            const float omt0 = 1.0f - t0, omt1 = 1.0f - t1;
+            const float omt0_2 = omt0 * omt0, omt1_2 = omt1 * omt1;
+            const float t0_2 = t0 * t0, t1_2 = t1 * t1;
+            const float b00 = omt0_2 * omt0, b01 = 3.0f * omt0_2 * t0, b02 = 3.0f * omt0 * t0_2,
+                        b03 = t0_2 * t0;
+            const float b10 = omt1_2 * omt1, b11 = 3.0f * omt1_2 * t1, b12 = 3.0f * omt1 * t1_2,
+                        b13 = t1_2 * t1;
+            const float *v = v_edges + e * 4;
+            const float gsx = v[0], gsy = v[1], gex = v[2], gey = v[3];
+            acc[0] = acc[0] + gsx * b00 + gex * b10;
+            acc[1] = acc[1] + gsy * b00 + gey * b10;
+            acc[2] = acc[2] + gsx * b01 + gex * b11;
+            acc[3] = acc[3] + gsy * b01 + gey * b11;
+            acc[4] = acc[4] + gsx * b02 + gex * b12;
+            acc[5] = acc[5] + gsy * b02 + gey * b12;
+            acc[6] = acc[6] + gsx * b03 + gex * b13;
+            acc[7] = acc[7] + gsy * b03 + gey * b13;
+        }
+        memcpy(v_cubics + g * 8, acc, sizeof(acc));
+    }
+}
+
+/* ------------------------------------------------------------------------ */
 /* stroke mode (manbo/ops/cubic_polyline_splatting.py:145-247, 393-658)      */
 
 static inline float stroke_min_d2(const float *edges, int e0, int e1, float px, float py, int *best_eid,

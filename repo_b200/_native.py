@@ -42,13 +42,20 @@ SIGNATURES = {
     "cs_isect_edge_ranges": (ctypes.c_int, [_P, _P, _P, _I64, _P]),
     "cs_bin_workspace_size": (_SZ, [_I64]),
     "cs_unit_lists_size": (_SZ, [_I64]),
-    "cs_bin_count": (ctypes.c_int, [_P] * 13 + [_I64, _I64, _I64, _I64, _I32, _I32, _I32, _I32,
+    "cs_bin_count": (ctypes.c_int, [_P] * 14 + [_I64, _I64, _I64, _I64, _I32, _I32, _I32, _I32,
                                                 _I32, _F32, _I32, _P, _I32, _P]),
     "cs_bin_sort": (ctypes.c_int, [_P] * 7 + [_I64, _I64, _I32, _I32, _I32, _I32] + [_P] * 12
                     + [_I64, _P, _P]),
     "cs_stage_workspace_size": (_SZ, [_I64]),
     "cs_tile_stage": (ctypes.c_int, [_P] * 18 + [_I64, _I32, _I32, _P]),
     "cs_raster_workspace_size": (_SZ, [_I64]),
+    "cs_de_casteljau_max_depth": (_I32, [_I32]),
+    "cs_de_casteljau_edge_capacity": (_I64, [_I64, _I32]),
+    "cs_flatten_de_casteljau": (ctypes.c_int, [_P, _P, _I64, _I64, _I32, _F32, _P, _P, _P, _P,
+                                               _P, _I64, _P, _P]),
+    "cs_edge_grads_to_cubics_csr": (ctypes.c_int, [_P] * 5 + [_I64, _F32, _F32, _P]),
+    "cs_cubic_flatness_flags": (ctypes.c_int, [_P, _P, _I64, _F32, _I32, _P]),
+    "cs_cubic_split_half": (ctypes.c_int, [_P, _P, _P, _I64, _P]),
     "cs_visit_lists_size": (_SZ, [_I64, _I64]),
     "cs_fill_forward": (ctypes.c_int, [_P] * 19 + [_I32, _I32, _I32, _I32, _P]),
     "cs_fill_backward": (ctypes.c_int, [_P] * 24 + [_I32, _I32, _I32, _I32, _P]),

@@ -144,11 +144,12 @@ __global__ void project_kernel(const float* __restrict__ cn, const float* __rest
   project_points(c, half_w, half_h, p);
 #pragma unroll
   for (int i = 0; i < 8; ++i) cpx[g * 8 + i] = p[i];
+  if (!ranges) return;  // projection only
   int r[4];
-  segment_rect(p, sw[g], sr[g], pad, aniso, tbx, tby, r);
+  segment_rect(p, sw ? sw[g] : 0.0f, sr ? sr[g] : 0.0f, pad, aniso, tbx, tby, r);
 #pragma unroll
   for (int i = 0; i < 4; ++i) ranges[g * 4 + i] = r[i];
-  hits[g] = max(0, (r[2] - r[0]) * (r[3] - r[1]));
+  if (hits) hits[g] = max(0, (r[2] - r[0]) * (r[3] - r[1]));
 }
 
 __global__ void flatten_kernel(const float* __restrict__ cpx, const float* __restrict__ basis,
@@ -279,11 +280,12 @@ __device__ __forceinline__ void load_segment(const float* __restrict__ cn,
 }
 
 // One warp per primitive: project + bound every segment, union the rects,
-// flatten all segments into edges, and add the primitive to the intersect and
-// edge-slot counts of its tiles within the band of tile rows [r0, r1).
+// flatten all segments into edges (unless peo gives pre-flattened edges with
+// their CSR offsets), and add the primitive to the intersect and edge-slot
+// counts of its tiles within the band of tile rows [r0, r1).
 __global__ void __launch_bounds__(256) bin_prep_kernel(
     const float* __restrict__ cn, const float* __restrict__ ring, int ring_g,
-    const int* __restrict__ offs, const float* __restrict__ aa,
+    const int* __restrict__ offs, const int* __restrict__ peo, const float* __restrict__ aa,
     const float* __restrict__ sw, const float* __restrict__ basis, float* __restrict__ cpx,
     float* __restrict__ edges, int* __restrict__ pr, int* __restrict__ hits,
     int* __restrict__ tile_counts, int* __restrict__ tile_ecounts, int* __restrict__ status,
@@ -327,7 +329,7 @@ __global__ void __launch_bounds__(256) bin_prep_kernel(
   // edges are needed only by the band's tiles: a primitive whose tile rows
   // miss the band is not flattened
   const bool in_band = max(mny, r0) < min(mxy, r1) && mnx < mxx;
-  const int npts = in_band ? nseg * S : 0;
+  const int npts = (in_band && !peo) ? nseg * S : 0;
   for (int q = lane; q < npts; q += 32) {
     int si = q / S;
     int s = q - si * S;
@@ -339,7 +341,14 @@ __global__ void __launch_bounds__(256) bin_prep_kernel(
     bernstein_point(pp, basis, S, s, x, y);
     store_point(edges, seg, S, s, x, y);
   }
-  const int nedge = nseg * (S - 1);
+  int nedge = nseg * (S - 1);
+  if (peo) {  // pre-flattened: the primitive's edges are peo[p] .. peo[p + 1]
+    nedge = peo[p + 1] - peo[p];
+    if (nedge < 0 || peo[p] < 0) {
+      if (lane == 0 && status) atomicExch(status, CS_ERR_ARG);
+      nedge = 0;
+    }
+  }
   int y0 = max(mny, r0), y1 = min(mxy, r1);
   int wdt = mxx - mnx, hgt = y1 - y0;
   if (wdt > 0 && hgt > 0) {
@@ -833,6 +842,7 @@ int cs_project_cubics(const float* cubics_norm, const float* stroke_widths,
   if (block_x != kTile || block_y != kTile) return CS_ERR_UNSUPPORTED;
   if (num_curves < 0 || img_height <= 0 || img_width <= 0) return CS_ERR_ARG;
   if (num_curves == 0) return CS_OK;
+  if (!cubics_norm || !cubics_px) return CS_ERR_ARG;
   int tbx = (img_width + kTile - 1) / kTile, tby = (img_height + kTile - 1) / kTile;
   project_kernel<<<ceil_div(num_curves, 256), 256, 0, (cudaStream_t)stream>>>(
       cubics_norm, stroke_widths, support_radii, cubics_px, tile_ranges, num_tiles_hit,
@@ -902,8 +912,9 @@ size_t cs_unit_lists_size(int64_t num_tiles) {
 
 int cs_bin_count(const float* cubics_norm, const int32_t* prim_seg_offsets, const float* aa_widths,
                  const float* stroke_widths, const float* basis, float* cubics_px,
-                 float* edges_px, int32_t* prim_tile_ranges, int32_t* num_tiles_hit,
-                 int32_t* tile_bins, int32_t* tile_dlist, int32_t* counters, void* workspace,
+                 float* edges_px, const int32_t* prim_edge_offsets, int32_t* prim_tile_ranges,
+                 int32_t* num_tiles_hit, int32_t* tile_bins, int32_t* tile_dlist,
+                 int32_t* counters, void* workspace,
                  int64_t num_primitives, int64_t num_segments, int64_t isect_capacity,
                  int64_t dlist_capacity, int32_t samples, int32_t img_height, int32_t img_width,
                  int32_t tile_row_begin, int32_t tile_row_end, float aabb_pad, int32_t aniso,
@@ -920,7 +931,8 @@ int cs_bin_count(const float* cubics_norm, const int32_t* prim_seg_offsets, cons
   cudaMemsetAsync(ws.tile_counts, 0, align256(sizeof(int) * nt) * 2, st);
   if (num_primitives > 0) {
     bin_prep_kernel<<<ceil_div(num_primitives * 32, 256), 256, 0, st>>>(
-        cubics_norm, ring, ring_segs_per_path, prim_seg_offsets, aa_widths, stroke_widths, basis, cubics_px, edges_px,
+        cubics_norm, ring, ring_segs_per_path, prim_seg_offsets, prim_edge_offsets, aa_widths,
+        stroke_widths, basis, cubics_px, edges_px,
         prim_tile_ranges, num_tiles_hit, ws.tile_counts, ws.tile_ecounts, counters + 1,
         num_primitives, num_segments, samples, 0.5f * (float)img_width,
         0.5f * (float)img_height, tbx, tby, r0, r1, aabb_pad, aniso);

@@ -40,6 +40,7 @@ _FLATTEN_ALIASES = {
     "de-casteljau": CUBIC_FLATTEN_METHOD_DE_CASTELJAU,
 }
 INT64_MAX = (1 << 63) - 1
+DE_CASTELJAU_TOL_PX = 0.5  # DEFAULT_DE_CASTELJAU_FLATNESS_TOL_PX (cubic_splatting.py:18)
 
 CubicProcessPayload = MutableMapping[str, Any]
 CubicProcessFn = Callable[[str, CubicProcessPayload], Optional[Mapping[str, Any]]]
@@ -129,6 +130,10 @@ class Binning:
     unit_order: Optional[torch.Tensor] = None   # strip dispatch lists (staged work)
     unit_order_bwd: Optional[torch.Tensor] = None  # strip dispatch lists (forward's work)
     visit_lists: Optional[torch.Tensor] = None  # per strip: intersects that composited a pixel
+    flatten_method: str = CUBIC_FLATTEN_METHOD_BERNSTEIN
+    segment_edge_offsets: Optional[torch.Tensor] = None  # de Casteljau CSR [G + 1]
+    edge_t_starts: Optional[torch.Tensor] = None         # de Casteljau leaf intervals [E]
+    edge_t_ends: Optional[torch.Tensor] = None
 
 
 def _offsets_error(offs: torch.Tensor, num_segments: int) -> ValueError:
@@ -138,20 +143,46 @@ def _offsets_error(offs: torch.Tensor, num_segments: int) -> ValueError:
         f"(got start={int(o[0])}, end={int(o[-1])}, num_segments={num_segments})")
 
 
+def flatten_de_casteljau(cubics_px: torch.Tensor, offs: torch.Tensor, samples: int,
+                         status: Optional[torch.Tensor] = None, tol_px: float = DE_CASTELJAU_TOL_PX):
+    """Adaptive de Casteljau flatten on the device, without a host
+    synchronisation: edges [cap, 2, 2], prim_edge_offsets [P + 1],
+    segment_edge_offsets [G + 1], edge t starts / ends [cap], where cap bounds
+    the edge count E = segment_edge_offsets[-1]."""
+    dev = cubics_px.device
+    g = int(cubics_px.shape[0])
+    p = max(0, int(offs.numel()) - 1)
+    s = max(2, int(samples))
+    cap = int(nat.call("cs_de_casteljau_edge_capacity", g, s))
+    edges = torch.empty((max(cap, 1), 2, 2), dtype=torch.float32, device=dev)
+    t0 = torch.empty((max(cap, 1),), dtype=torch.float32, device=dev)
+    t1 = torch.empty((max(cap, 1),), dtype=torch.float32, device=dev)
+    seg = torch.empty((g + 1,), dtype=torch.int32, device=dev)
+    prim = torch.empty((p + 1,), dtype=torch.int32, device=dev)
+    nat.check(nat.call("cs_flatten_de_casteljau", nat.ptr(cubics_px), nat.ptr(offs), g, p, s,
+                       float(tol_px), nat.ptr(edges), nat.ptr(prim), nat.ptr(seg), nat.ptr(t0),
+                       nat.ptr(t1), cap, nat.ptr(status), nat.stream(dev)),
+              "cs_flatten_de_casteljau")
+    return edges, prim, seg, t0, t1
+
+
 def bin_primitives(cubics_norm: torch.Tensor, offs: torch.Tensor, depths: torch.Tensor,
                    aa_widths: torch.Tensor, img_h: int, img_w: int, samples: int, *,
                    colors: torch.Tensor, opacities: torch.Tensor, inv_sigma2s: torch.Tensor,
                    fill_rules: Optional[torch.Tensor] = None,
                    stroke_widths: Optional[torch.Tensor] = None,
                    aabb_pad: float = DEFAULT_AABB_PAD, aniso: bool = False,
-                   tile_rows: Optional[tuple] = None) -> Binning:
+                   tile_rows: Optional[tuple] = None,
+                   flatten_method: str = CUBIC_FLATTEN_METHOD_BERNSTEIN) -> Binning:
     """Project, bound, flatten, bin, sort and stage all primitives (fused B200
     pipeline, one host synchronisation to size the intersect list).
 
     The intersect list equals the reference's K3 + flatten + K4 + cumsum + K5 +
     sort + K6 (cubic_splatting.py:2815-2908): tile_bins [T, 2] of [start, end)
     into prim_ids_sorted / isect_ids_sorted, front (small depth) first.
-    stroke_widths selects stroke mode.
+    stroke_widths selects stroke mode.  flatten_method "de_casteljau" flattens
+    adaptively (cs_flatten_de_casteljau) before the counts instead of the
+    uniform Bernstein flatten inside cs_bin_count.
     """
     dev = cubics_norm.device
     s = max(2, int(samples))
@@ -162,7 +193,7 @@ def bin_primitives(cubics_norm: torch.Tensor, offs: torch.Tensor, depths: torch.
     r0, r1 = (0, tby) if tile_rows is None else (int(tile_rows[0]), int(tile_rows[1]))
     stroke = stroke_widths is not None
     cubics_px = torch.empty((g, 4, 2), dtype=torch.float32, device=dev)
-    edges = torch.empty((g * (s - 1), 2, 2), dtype=torch.float32, device=dev)
+    dc = flatten_method == CUBIC_FLATTEN_METHOD_DE_CASTELJAU
     prim_ranges = torch.empty((p, 4), dtype=torch.int32, device=dev)
     num_hit = torch.empty((p,), dtype=torch.int32, device=dev)
     tile_bins = torch.empty((nt, 2), dtype=torch.int32, device=dev)
@@ -174,8 +205,17 @@ def bin_primitives(cubics_norm: torch.Tensor, offs: torch.Tensor, depths: torch.
     aw = _f32(aa_widths)
     sw = None if stroke_widths is None else _f32(stroke_widths)
     basis = bernstein_basis(s, dev)
+    peo = seg_eo = t0 = t1 = None
+    if dc:
+        nat.check(nat.call("cs_project_cubics", nat.ptr(cn), None, None, nat.ptr(cubics_px), None,
+                           None, g, int(img_h), int(img_w), 16, 16, 0.0, 0, st),
+                  "cs_project_cubics")
+        edges, peo, seg_eo, t0, t1 = flatten_de_casteljau(cubics_px, offs, s, counters[1:2])
+    else:
+        edges = torch.empty((g * (s - 1), 2, 2), dtype=torch.float32, device=dev)
     nat.check(nat.call("cs_bin_count", nat.ptr(cn), nat.ptr(offs), nat.ptr(aw), nat.ptr(sw),
-                       nat.ptr(basis), nat.ptr(cubics_px), nat.ptr(edges), nat.ptr(prim_ranges),
+                       nat.ptr(basis), nat.ptr(cubics_px), nat.ptr(edges), nat.ptr(peo),
+                       nat.ptr(prim_ranges),
                        nat.ptr(num_hit), nat.ptr(tile_bins), nat.ptr(tile_dlist),
                        nat.ptr(counters), ws.data_ptr(), p, g, INT64_MAX, INT64_MAX, s,
                        int(img_h), int(img_w), r0, r1, float(aabb_pad), int(bool(aniso)), None,
@@ -186,7 +226,7 @@ def bin_primitives(cubics_norm: torch.Tensor, offs: torch.Tensor, depths: torch.
     if status == nat.CS_ERR_ARG:
         raise _offsets_error(offs, g)
     nat.check(status, "cs_bin_count")
-    edge_offs = (offs.to(torch.int64) * (s - 1)).to(torch.int32)
+    edge_offs = peo if dc else (offs.to(torch.int64) * (s - 1)).to(torch.int32)
     # per-frame buffers are sized in a few classes (_size_class), so that the
     # caching allocator reuses blocks from frame to frame; the sorted lists
     # are exact-length views
@@ -210,7 +250,9 @@ def bin_primitives(cubics_norm: torch.Tensor, offs: torch.Tensor, depths: torch.
                            nat.ptr(unit_order), st), "cs_bin_sort")
     return Binning(cubics_px, edges, edge_offs, prim_ranges, num_hit, tile_bins, prim_sorted,
                    isect_sorted, n_isect, (tbx, tby, 1), s, (r0, r1), tile_dlist, imeta, rowoff,
-                   dlist, counters, stroke, istrips, unit_order if n_isect > 0 else None)
+                   dlist, counters, stroke, istrips, unit_order if n_isect > 0 else None,
+                   flatten_method=flatten_method, segment_edge_offsets=seg_eo,
+                   edge_t_starts=t0, edge_t_ends=t1)
 
 
 def stage_reference_lists(prim_ids_sorted, tile_bins, edges_px, isect_edge_ranges, colors,
@@ -405,6 +447,30 @@ def raster_backward(b: Binning, num_primitives: int, background, final_ts, final
     return v_edges, v_colors, v_opac, v_inv, v_sw, contrib, icontrib
 
 
+def edge_grads_to_cubics_csr(v_edges: torch.Tensor, segment_edge_offsets: torch.Tensor,
+                             edge_t_starts: torch.Tensor, edge_t_ends: torch.Tensor,
+                             num_segments: int, scale=(1.0, 1.0)) -> torch.Tensor:
+    """Edge gradients of a de Casteljau flattening -> cubic gradients."""
+    dev = v_edges.device
+    out = torch.empty((num_segments, 4, 2), dtype=torch.float32, device=dev)
+    if num_segments > 0:
+        nat.check(nat.call("cs_edge_grads_to_cubics_csr", nat.ptr(v_edges),
+                           nat.ptr(edge_t_starts), nat.ptr(edge_t_ends),
+                           nat.ptr(segment_edge_offsets), nat.ptr(out), int(num_segments),
+                           float(scale[0]), float(scale[1]), nat.stream(dev)),
+                  "cs_edge_grads_to_cubics_csr")
+    return out
+
+
+def binning_edge_grads(b: Binning, v_edges: torch.Tensor, num_segments: int,
+                       scale=(1.0, 1.0)) -> torch.Tensor:
+    """Cubic gradients from edge gradients with the binning's flatten method."""
+    if b.flatten_method == CUBIC_FLATTEN_METHOD_DE_CASTELJAU:
+        return edge_grads_to_cubics_csr(v_edges, b.segment_edge_offsets, b.edge_t_starts,
+                                        b.edge_t_ends, num_segments, scale)
+    return edge_grads_to_cubics(v_edges, num_segments, b.samples, scale)
+
+
 def edge_grads_to_cubics(v_edges: torch.Tensor, num_segments: int, samples: int,
                          scale=(1.0, 1.0)) -> torch.Tensor:
     dev = v_edges.device
@@ -446,8 +512,6 @@ class CubicFillSplatFunction(torch.autograd.Function):
                 flatten_method=DEFAULT_CUBIC_FLATTEN_METHOD, process_fn=None, tile_rows=None):
         nat.require_cuda(cubics_norm, "cubics_norm")
         method = normalize_cubic_flatten_method(flatten_method)
-        if method != CUBIC_FLATTEN_METHOD_BERNSTEIN:
-            raise NotImplementedError("de_casteljau flattening is not implemented in the B200 path")
         _check_block(block_x, block_y)
         num_segments = int(cubics_norm.shape[0])
         offs = _i32(primitive_seg_offsets).view(-1)
@@ -473,7 +537,8 @@ class CubicFillSplatFunction(torch.autograd.Function):
         b = bin_primitives(cubics_norm, offs, depths.reshape(-1), widths, int(img_h), int(img_w),
                            int(distance_samples), colors=col, opacities=op, inv_sigma2s=inv_s2,
                            fill_rules=rules, aabb_pad=float(aabb_pad),
-                           aniso=bool(aniso_intersects), tile_rows=tile_rows)
+                           aniso=bool(aniso_intersects), tile_rows=tile_rows,
+                           flatten_method=method)
         if b.num_intersects <= 0:
             ctx.empty = True
             return _empty_image(bg, img_h, img_w)
@@ -506,10 +571,10 @@ class CubicFillSplatFunction(torch.autograd.Function):
             collect_contrib=cc, collect_isect_contrib=ci)
         half_w, half_h = 0.5 * float(ctx.img_w), 0.5 * float(ctx.img_h)
         if process_fn is None:
-            v_cubics_norm = edge_grads_to_cubics(v_edges, ctx.num_segments, b.samples,
-                                                 (half_w, half_h))
+            v_cubics_norm = binning_edge_grads(b, v_edges, ctx.num_segments,
+                                               (half_w, half_h))
         else:
-            v_cubics_px = edge_grads_to_cubics(v_edges, ctx.num_segments, b.samples)
+            v_cubics_px = binning_edge_grads(b, v_edges, ctx.num_segments)
             post = _run_process_fn(process_fn, "post_backward_rasterize", {
                 "v_cubics_px": v_cubics_px, "v_colors": v_colors, "v_opacity": v_opac,
                 "curve_contrib_rgb": contrib, "curve_isect_contrib": icontrib,
@@ -544,8 +609,6 @@ class CubicPolylineSplatFunction(torch.autograd.Function):
                 flatten_method=DEFAULT_CUBIC_FLATTEN_METHOD, process_fn=None, tile_rows=None):
         nat.require_cuda(cubics_norm, "cubics_norm")
         method = normalize_cubic_flatten_method(flatten_method)
-        if method != CUBIC_FLATTEN_METHOD_BERNSTEIN:
-            raise NotImplementedError("de_casteljau flattening is not implemented in the B200 path")
         _check_block(block_x, block_y)
         num_segments = int(cubics_norm.shape[0])
         offs = _i32(primitive_seg_offsets).view(-1)
@@ -571,7 +634,8 @@ class CubicPolylineSplatFunction(torch.autograd.Function):
         b = bin_primitives(cubics_norm, offs, depths.reshape(-1), widths, int(img_h), int(img_w),
                            int(distance_samples), colors=col, opacities=op, inv_sigma2s=inv_s2,
                            stroke_widths=sw, aabb_pad=float(aabb_pad),
-                           aniso=bool(aniso_intersects), tile_rows=tile_rows)
+                           aniso=bool(aniso_intersects), tile_rows=tile_rows,
+                           flatten_method=method)
         if b.num_intersects <= 0:
             ctx.empty = True
             return _empty_image(bg, img_h, img_w)
@@ -604,10 +668,10 @@ class CubicPolylineSplatFunction(torch.autograd.Function):
             collect_contrib=cc, collect_isect_contrib=ci)
         half_w, half_h = 0.5 * float(ctx.img_w), 0.5 * float(ctx.img_h)
         if process_fn is None:
-            v_cubics_norm = edge_grads_to_cubics(v_edges, ctx.num_segments, b.samples,
-                                                 (half_w, half_h))
+            v_cubics_norm = binning_edge_grads(b, v_edges, ctx.num_segments,
+                                               (half_w, half_h))
         else:
-            v_cubics_px = edge_grads_to_cubics(v_edges, ctx.num_segments, b.samples)
+            v_cubics_px = binning_edge_grads(b, v_edges, ctx.num_segments)
             post = _run_process_fn(process_fn, "post_backward_rasterize", {
                 "v_cubics_px": v_cubics_px, "v_colors": v_colors, "v_opacity": v_opac,
                 "v_stroke": v_sw, "curve_contrib_rgb": contrib, "curve_isect_contrib": icontrib,

@@ -255,6 +255,81 @@ def adan_case(manbo, dev):
     return out
 
 
+def dc_cubics(seed: int, n: int) -> torch.Tensor:
+    """Pixel-space cubics for the adaptive flatten: random ones plus straight,
+    fully degenerate, closed-loop (zero chord), tiny and very large ones."""
+    g = torch.Generator().manual_seed(seed)
+    rnd = torch.rand(n, 4, 2, generator=g) * 200.0
+    t = torch.linspace(0.0, 1.0, 4).view(4, 1)
+    line = torch.tensor([[3.0, 5.0]]) + t * torch.tensor([[90.0, 40.0]])
+    point = torch.full((4, 2), 17.25)
+    loop = torch.tensor([[50.0, 50.0], [120.0, 10.0], [-20.0, 10.0], [50.0, 50.0]])
+    tiny = torch.tensor([[10.0, 10.0], [10.1, 10.3], [10.2, 9.9], [10.4, 10.1]])
+    huge = torch.tensor([[0.0, 0.0], [5000.0, 9000.0], [-4000.0, 7000.0], [3000.0, -100.0]])
+    near = torch.tensor([[0.0, 0.0], [30.0, 0.49], [60.0, -0.5], [90.0, 0.0]])
+    return torch.cat([rnd, torch.stack([line, point, loop, tiny, huge, near])], 0).contiguous()
+
+
+def dc_flatten_case(cs):
+    """The reference's adaptive de Casteljau flatten on its host branch
+    (cubic_splatting.py:1729-1832, CPU tensors) for several sample counts."""
+    out = {}
+    cub = dc_cubics(51, 58)
+    g = int(cub.shape[0])
+    offs = torch.tensor([0, 5, 5, 17, 40, g], dtype=torch.int32)  # an empty primitive
+    out["cubics_px"] = _np(cub)
+    out["offs"] = _np(offs)
+    out["flat_tol0.5"] = _np(cs.cubic_adaptive_flatness_flags_tilelang(cub, tol_px=0.5))
+    out["flat_tol3"] = _np(cs.cubic_adaptive_flatness_flags_tilelang(cub, tol_px=3.0))
+    left, right = cs.cubic_split_half_tilelang(cub)
+    out["split_left"] = _np(left)
+    out["split_right"] = _np(right)
+    for s in (5, 16, 24, 33):
+        edges, peo, seo, t0, t1 = cs._flatten_cubics_to_edges(
+            cub, offs, distance_samples=s, flatten_method="de_casteljau")
+        out[f"s{s}_edges_px"] = _np(edges)
+        out[f"s{s}_prim_edge_offsets"] = _np(peo)
+        out[f"s{s}_segment_edge_offsets"] = _np(seo)
+        out[f"s{s}_edge_t_starts"] = _np(t0)
+        out[f"s{s}_edge_t_ends"] = _np(t1)
+    return out
+
+
+def dc_api_case(cs, ps, scene, grad_seed, dev, stroke=False):
+    """Image and gradients of the public entry point with
+    flatten_method="de_casteljau" (fill or stroke)."""
+    h, w, s = scene.height, scene.width, scene.samples
+    cn = scene.cubics_norm().to(dev).clone().requires_grad_(True)
+    offs = scene.seg_offsets().to(dev)
+    col = scene.colors.to(dev).clone().requires_grad_(True)
+    op = scene.opacities.to(dev).clone().requires_grad_(True)
+    depths = scene.depths.to(dev)
+    aw = scene.aa_widths.to(dev).clone().requires_grad_(True)
+    bg = scene.background.to(dev)
+    v_out = scenes.seeded_grad(grad_seed, h, w).to(dev)
+    res = {"cubics_norm": _np(cn), "offs": _np(offs), "colors": _np(col), "opacities": _np(op),
+           "depths": _np(depths), "aa_widths": _np(aw), "background": _np(bg),
+           "hw_s": np.array([h, w, s], np.int32), "v_output": _np(v_out)}
+    if stroke:
+        sw = scene.stroke_widths.to(dev).clone().requires_grad_(True)
+        out = ps.render_cubic_polyline_splat_tilelang(
+            cn, offs, col, op, sw, depths, h, w, 16, 16, bg, aa_widths=aw, distance_samples=s,
+            flatten_method="de_casteljau")
+        res["stroke_widths"] = _np(sw)
+    else:
+        rules = scene.fill_rules.to(dev)
+        out = cs.render_cubic_fill_splat_tilelang(
+            cn, offs, col, op, depths, h, w, 16, 16, bg, fill_rules=rules, aa_widths=aw,
+            distance_samples=s, flatten_method="de_casteljau")
+        res["fill_rules"] = _np(rules)
+    (out * v_out).sum().backward()
+    res.update(api_image=_np(out), api_v_cubics_norm=_np(cn.grad), api_v_colors=_np(col.grad),
+               api_v_opacities=_np(op.grad), api_v_aa_widths=_np(aw.grad))
+    if stroke:
+        res["api_v_stroke_widths"] = _np(sw.grad)
+    return res
+
+
 def time_config2(manbo, cs, dev, iters: int, warmup: int):
     """Reference training step at config 2: render + MSE + SSIM + backward + Adam."""
     sc = scenes.config2()
@@ -316,15 +391,30 @@ def main(argv=None):
     from manbo.ops import cubic_splatting as cs
     from manbo.ops import tile_bins as tb
 
+    cases = None if args.cases == "all" else set(args.cases.split(","))
+    if cases == {"dc_flatten"}:  # the host branch needs no GPU
+        _save(args.out, "dc_flatten", dc_flatten_case(cs))
+        return
     dev = torch.device("cuda")
     info = {"torch": torch.__version__, "tilelang": getattr(tilelang, "__version__", "?"),
             "gpu": torch.cuda.get_device_name(0)}
     print(info, flush=True)
-    cases = None if args.cases == "all" else set(args.cases.split(","))
+    dc_fill = lambda: dc_api_case(cs, ps, scenes.small_fill_scene(61, paths=8), 62, dev)  # noqa
+    dc_stroke = lambda: dc_api_case(cs, ps, scenes.small_stroke_scene(63), 64, dev,  # noqa
+                                    stroke=True)
     if not args.no_golden and cases is not None:
         if "adan" in cases:
             _save(args.out, "adan", adan_case(manbo, dev))
+        if "dc_flatten" in cases:
+            _save(args.out, "dc_flatten", dc_flatten_case(cs))
+        if "dc_fill" in cases:
+            _save(args.out, "dc_fill", dc_fill())
+        if "dc_stroke" in cases:
+            _save(args.out, "dc_stroke", dc_stroke())
     elif not args.no_golden:
+        _save(args.out, "dc_flatten", dc_flatten_case(cs))
+        _save(args.out, "dc_fill", dc_fill())
+        _save(args.out, "dc_stroke", dc_stroke())
         _save(args.out, "adan", adan_case(manbo, dev))
         _save(args.out, "fill_small_a", fill_case(cs, tb, scenes.small_fill_scene(21), 31, dev))
         _save(args.out, "fill_small_b", fill_case(cs, tb, scenes.small_fill_scene(22, h=40, w=72, paths=9, samples=5), 32, dev))

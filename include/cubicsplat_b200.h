@@ -150,7 +150,8 @@ CS_API int cs_isect_edge_ranges(const int32_t *prim_ids_sorted, const int32_t *p
  * prim_edge_offsets [P + 1] (may be NULL) selects pre-flattened edges: edges_px
  * then holds edges already written (e.g. by cs_flatten_de_casteljau) with
  * these CSR offsets, is only read by later stages, and the edge-slot counts
- * use each primitive's own edge count.
+ * use each primitive's own edge count.  Otherwise prim_edge_offsets_out [P + 1]
+ * (may be NULL) receives the uniform flatten's offsets offs * (S - 1).
  * With cs_bin_sort this replaces project (K3) + flatten + K4 + cumsum + K5 +
  * torch.sort + K6 of _CubicFillSplatFunction.forward, cubic_splatting.py:2815-2908.
  * Workspace: cs_bin_workspace_size(num_tiles). */
@@ -158,7 +159,7 @@ CS_API size_t cs_bin_workspace_size(int64_t num_tiles);
 CS_API int cs_bin_count(const float *cubics_norm, const int32_t *prim_seg_offsets,
                  const float *aa_widths, const float *stroke_widths, const float *basis,
                  float *cubics_px, float *edges_px, const int32_t *prim_edge_offsets,
-                 int32_t *prim_tile_ranges, int32_t *num_tiles_hit, int32_t *tile_bins,
+                 int32_t *prim_edge_offsets_out, int32_t *prim_tile_ranges, int32_t *num_tiles_hit, int32_t *tile_bins,
                  int32_t *tile_dlist, int32_t *counters, void *workspace, int64_t num_primitives,
                  int64_t num_segments, int64_t isect_capacity, int64_t dlist_capacity,
                  int32_t samples, int32_t img_height, int32_t img_width, int32_t tile_row_begin,
@@ -323,6 +324,17 @@ CS_API int cs_edge_grads_to_cubics_csr(const float *v_edges, const float *edge_t
                                        int64_t num_segments, float scale_x, float scale_y,
                                        void *stream);
 
+/* Anti-aliasing widths of the renderer: widths_clamped = clamp(aa, min=1e-4)
+ * and inv_sigma2s = 1 / clamp(w^2, min=1e-6) (cubic_splatting.py:2820-2821);
+ * backward v_aa = -2 v_inv / clamp(w^3, min=1e-12) (:3101-3104), and with
+ * aa_widths (may be NULL) also the entry clamp's backward: 0 where
+ * !(aa >= 1e-4).  [n] each; NaN propagates as through torch.clamp. */
+CS_API int cs_aa_widths_forward(const float *aa_widths, float *widths_clamped,
+                                float *inv_sigma2s, int64_t n, void *stream);
+CS_API int cs_aa_widths_backward(const float *aa_widths, const float *widths_clamped,
+                                 const float *v_inv_sigma2s, float *v_aa_widths, int64_t n,
+                                 void *stream);
+
 /* Ring parameterisation of closed paths (the B200 training step's
  * parameters): ring [P, 3G, 2] pixel-space points; segment k of a path is
  * (r[3k], r[3k+1], r[3k+2], r[3k+3 mod 3G]).  cubics_norm [P*G, 4, 2] =
@@ -386,10 +398,11 @@ CS_API size_t cs_mse_workspace_size(int64_t n);
 CS_API int cs_mse_forward(const float *x, const float *y, int64_t n, float *out_sse, float *out_mse,
                    void *workspace, void *stream);
 
-/* grad = (*scale) * (lhs - rhs), scale read on the device (no host sync).
+/* grad = s * (lhs - rhs) with s = (*scale) * factor, scale read on the
+ * device (no host sync), or s = factor when scale is NULL.
  * Replaces mse_backward_diff_kernel, manbo/ops/metric.py:166-202. */
-CS_API int cs_mse_backward(const float *lhs, const float *rhs, const float *scale, float *grad,
-                    int64_t n, void *stream);
+CS_API int cs_mse_backward(const float *lhs, const float *rhs, const float *scale, float factor,
+                           float *grad, int64_t n, void *stream);
 
 /* SSIM with a separable Gaussian window g [win] (win odd, win2d = outer(g, g)),
  * valid-window semantics, per plane (N*C planes of H x W).  Writes the mean

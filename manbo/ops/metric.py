@@ -61,8 +61,7 @@ def reduce_sum_partial_kernel(threads: int = DEFAULT_THREADS,
 
 def mse_backward_diff_kernel(threads: int = DEFAULT_THREADS, dtype="float32"):
     def kernel(lhs, rhs, scale, grad):
-        s = torch.full((1,), float(scale), dtype=torch.float32, device=grad.device)
-        nat.check(nat.call("cs_mse_backward", nat.ptr(lhs), nat.ptr(rhs), nat.ptr(s),
+        nat.check(nat.call("cs_mse_backward", nat.ptr(lhs), nat.ptr(rhs), None, float(scale),
                            nat.ptr(grad), int(grad.numel()), nat.stream(grad.device)),
                   "cs_mse_backward")
     return kernel

@@ -42,7 +42,7 @@ SIGNATURES = {
     "cs_isect_edge_ranges": (ctypes.c_int, [_P, _P, _P, _I64, _P]),
     "cs_bin_workspace_size": (_SZ, [_I64]),
     "cs_unit_lists_size": (_SZ, [_I64]),
-    "cs_bin_count": (ctypes.c_int, [_P] * 14 + [_I64, _I64, _I64, _I64, _I32, _I32, _I32, _I32,
+    "cs_bin_count": (ctypes.c_int, [_P] * 15 + [_I64, _I64, _I64, _I64, _I32, _I32, _I32, _I32,
                                                 _I32, _F32, _I32, _P, _I32, _P]),
     "cs_bin_sort": (ctypes.c_int, [_P] * 7 + [_I64, _I64, _I32, _I32, _I32, _I32] + [_P] * 12
                     + [_I64, _P, _P]),
@@ -56,6 +56,8 @@ SIGNATURES = {
     "cs_edge_grads_to_cubics_csr": (ctypes.c_int, [_P] * 5 + [_I64, _F32, _F32, _P]),
     "cs_cubic_flatness_flags": (ctypes.c_int, [_P, _P, _I64, _F32, _I32, _P]),
     "cs_cubic_split_half": (ctypes.c_int, [_P, _P, _P, _I64, _P]),
+    "cs_aa_widths_forward": (ctypes.c_int, [_P, _P, _P, _I64, _P]),
+    "cs_aa_widths_backward": (ctypes.c_int, [_P, _P, _P, _P, _I64, _P]),
     "cs_visit_lists_size": (_SZ, [_I64, _I64]),
     "cs_fill_forward": (ctypes.c_int, [_P] * 19 + [_I32, _I32, _I32, _I32, _P]),
     "cs_fill_backward": (ctypes.c_int, [_P] * 24 + [_I32, _I32, _I32, _I32, _P]),
@@ -73,7 +75,7 @@ SIGNATURES = {
     "cs_ring_segments_backward": (ctypes.c_int, [_P, _P, _P, _P, _P, _I64, _I32, _I32, _P]),
     "cs_mse_workspace_size": (_SZ, [_I64]),
     "cs_mse_forward": (ctypes.c_int, [_P, _P, _I64, _P, _P, _P, _P]),
-    "cs_mse_backward": (ctypes.c_int, [_P, _P, _P, _P, _I64, _P]),
+    "cs_mse_backward": (ctypes.c_int, [_P, _P, _P, _F32, _P, _I64, _P]),
     "cs_ssim_workspace_size": (_SZ, [_I64, _I32, _I32, _I32]),
     "cs_ssim": (ctypes.c_int, [_P, _P, _P, _I64, _I32, _I32, _I32, _F32, _F32, _P, _P, _P, _P]),
     "cs_ssim_noalloc": (ctypes.c_int, [_P, _P, _P, _I64, _I32, _I32, _I32, _F32, _F32, _P, _P,
@@ -127,7 +129,17 @@ def ptr(t) -> int | None:
 
 
 def stream(device=None) -> int:
-    return torch.cuda.current_stream(device).cuda_stream
+    """The current torch CUDA stream of `device` (default: the current
+    device) as a raw cudaStream_t, without building a torch Stream object."""
+    if device is None:
+        idx = torch.cuda.current_device()
+    elif isinstance(device, int):
+        idx = device
+    else:
+        idx = torch.device(device).index
+        if idx is None:
+            idx = torch.cuda.current_device()
+    return torch._C._cuda_getCurrentRawStream(idx)
 
 
 def call(name: str, *args) -> int:

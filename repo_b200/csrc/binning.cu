@@ -285,7 +285,8 @@ __device__ __forceinline__ void load_segment(const float* __restrict__ cn,
 // counts of its tiles within the band of tile rows [r0, r1).
 __global__ void __launch_bounds__(256) bin_prep_kernel(
     const float* __restrict__ cn, const float* __restrict__ ring, int ring_g,
-    const int* __restrict__ offs, const int* __restrict__ peo, const float* __restrict__ aa,
+    const int* __restrict__ offs, const int* __restrict__ peo, int* __restrict__ peo_out,
+    const float* __restrict__ aa,
     const float* __restrict__ sw, const float* __restrict__ basis, float* __restrict__ cpx,
     float* __restrict__ edges, int* __restrict__ pr, int* __restrict__ hits,
     int* __restrict__ tile_counts, int* __restrict__ tile_ecounts, int* __restrict__ status,
@@ -295,6 +296,10 @@ __global__ void __launch_bounds__(256) bin_prep_kernel(
   int lane = threadIdx.x & 31;
   if (p >= np) return;
   int s0 = offs[p], s1 = offs[p + 1];
+  if (peo_out && lane == 0) {  // primitive edge offsets of the uniform flatten: offs * (S - 1)
+    peo_out[p] = (int)((long long)s0 * (S - 1));
+    if (p == np - 1) peo_out[np] = (int)((long long)s1 * (S - 1));
+  }
   // CSR offsets must start at 0, end at the segment count and not decrease;
   // a bad primitive is reported and treated as empty (no out-of-bounds reads).
   const bool bad = s0 < 0 || s1 < s0 || s1 > nseg_total || (p == 0 && s0 != 0) ||
@@ -912,7 +917,8 @@ size_t cs_unit_lists_size(int64_t num_tiles) {
 
 int cs_bin_count(const float* cubics_norm, const int32_t* prim_seg_offsets, const float* aa_widths,
                  const float* stroke_widths, const float* basis, float* cubics_px,
-                 float* edges_px, const int32_t* prim_edge_offsets, int32_t* prim_tile_ranges,
+                 float* edges_px, const int32_t* prim_edge_offsets,
+                 int32_t* prim_edge_offsets_out, int32_t* prim_tile_ranges,
                  int32_t* num_tiles_hit, int32_t* tile_bins, int32_t* tile_dlist,
                  int32_t* counters, void* workspace,
                  int64_t num_primitives, int64_t num_segments, int64_t isect_capacity,
@@ -931,7 +937,8 @@ int cs_bin_count(const float* cubics_norm, const int32_t* prim_seg_offsets, cons
   cudaMemsetAsync(ws.tile_counts, 0, align256(sizeof(int) * nt) * 2, st);
   if (num_primitives > 0) {
     bin_prep_kernel<<<ceil_div(num_primitives * 32, 256), 256, 0, st>>>(
-        cubics_norm, ring, ring_segs_per_path, prim_seg_offsets, prim_edge_offsets, aa_widths,
+        cubics_norm, ring, ring_segs_per_path, prim_seg_offsets, prim_edge_offsets,
+        prim_edge_offsets ? nullptr : prim_edge_offsets_out, aa_widths,
         stroke_widths, basis, cubics_px, edges_px,
         prim_tile_ranges, num_tiles_hit, ws.tile_counts, ws.tile_ecounts, counters + 1,
         num_primitives, num_segments, samples, 0.5f * (float)img_width,

@@ -39,6 +39,38 @@ __global__ void edge_grads_kernel(const float4* __restrict__ v_edges, float* __r
   }
 }
 
+// Anti-aliasing widths -> clamped widths and 1/sigma^2 (the renderer's
+// prologue, cubic_splatting.py:2820-2821): w = clamp(aa, min=1e-4),
+// inv = 1 / clamp(w * w, min=1e-6), NaN propagating like torch.clamp.
+__global__ void aa_widths_forward_kernel(const float* __restrict__ aa, float* __restrict__ w_out,
+                                         float* __restrict__ inv_out, long long n) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float a = aa[i];
+  const float w = a != a ? a : fmaxf(a, 1e-4f);
+  const float w2 = w * w;
+  const float d = w2 != w2 ? w2 : fmaxf(w2, 1e-6f);
+  w_out[i] = w;
+  inv_out[i] = 1.0f / d;
+}
+
+// v_aa = -2 v_inv / clamp(w^3, min=1e-12) with the clamped widths (the
+// backward epilogue, cubic_splatting.py:3101-3104), then, given the raw
+// widths, the backward of the entry's clamp(aa, min=1e-4): zero where
+// !(aa >= 1e-4), as torch's clamp backward.
+__global__ void aa_widths_backward_kernel(const float* __restrict__ aa,
+                                          const float* __restrict__ w,
+                                          const float* __restrict__ v_inv,
+                                          float* __restrict__ v_aa, long long n) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float wi = w[i];
+  const float w3 = wi * wi * wi;
+  const float d = w3 != w3 ? w3 : fmaxf(w3, 1e-12f);
+  const float g = (-2.0f * v_inv[i]) / d;
+  v_aa[i] = (aa && !(aa[i] >= 1e-4f)) ? 0.0f : g;
+}
+
 // Closed K-point control polygon -> two degree-(K/2) Bernstein branches ->
 // `subdiv` Hermite cubics per branch (manbo/ops/cubic_splatting.py:190-266).
 __global__ void ring_forward_kernel(const float* __restrict__ cp, const float* __restrict__ basis,
@@ -267,6 +299,25 @@ int cs_edge_grads_to_cubics(const float* v_edges, float* v_cubics, int64_t num_s
   edge_grads_kernel<<<ceil_div(num_segments, 128), 128, 0, (cudaStream_t)stream>>>(
       reinterpret_cast<const float4*>(v_edges), v_cubics, num_segments, edges_per_segment,
       scale_x, scale_y);
+  return launch_status();
+}
+
+int cs_aa_widths_forward(const float* aa_widths, float* widths_clamped, float* inv_sigma2s,
+                         int64_t n, void* stream) {
+  if (n < 0 || (n > 0 && (!aa_widths || !widths_clamped || !inv_sigma2s))) return CS_ERR_ARG;
+  if (n == 0) return CS_OK;
+  aa_widths_forward_kernel<<<ceil_div(n, 256), 256, 0, (cudaStream_t)stream>>>(
+      aa_widths, widths_clamped, inv_sigma2s, n);
+  return launch_status();
+}
+
+int cs_aa_widths_backward(const float* aa_widths, const float* widths_clamped,
+                          const float* v_inv_sigma2s, float* v_aa_widths, int64_t n,
+                          void* stream) {
+  if (n < 0 || (n > 0 && (!widths_clamped || !v_inv_sigma2s || !v_aa_widths))) return CS_ERR_ARG;
+  if (n == 0) return CS_OK;
+  aa_widths_backward_kernel<<<ceil_div(n, 256), 256, 0, (cudaStream_t)stream>>>(
+      aa_widths, widths_clamped, v_inv_sigma2s, v_aa_widths, n);
   return launch_status();
 }
 

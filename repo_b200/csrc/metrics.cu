@@ -101,9 +101,9 @@ __global__ void __launch_bounds__(kMseThreads) mse_kernel(const float* __restric
 }
 
 __global__ void mse_backward_kernel(const float* __restrict__ lhs, const float* __restrict__ rhs,
-                                    const float* __restrict__ scale, float* __restrict__ grad,
-                                    long long n) {
-  const float s = *scale;
+                                    const float* __restrict__ scale, float factor,
+                                    float* __restrict__ grad, long long n) {
+  const float s = scale ? *scale * factor : factor;
   const long long stride = (long long)gridDim.x * blockDim.x;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
     grad[i] = s * (lhs[i] - rhs[i]);
@@ -331,12 +331,12 @@ int cs_mse_forward(const float* x, const float* y, int64_t n, float* out_sse, fl
   return launch_status();
 }
 
-int cs_mse_backward(const float* lhs, const float* rhs, const float* scale, float* grad, int64_t n,
-                    void* stream) {
-  if (n < 0 || !scale) return CS_ERR_ARG;
+int cs_mse_backward(const float* lhs, const float* rhs, const float* scale, float factor,
+                    float* grad, int64_t n, void* stream) {
+  if (n < 0) return CS_ERR_ARG;
   if (n == 0) return CS_OK;
   int blocks = (int)std::min<long long>((n + 255) / 256, 148LL * 16);
-  mse_backward_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(lhs, rhs, scale, grad, n);
+  mse_backward_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(lhs, rhs, scale, factor, grad, n);
   return launch_status();
 }
 

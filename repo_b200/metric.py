@@ -81,10 +81,13 @@ def sse_mse(x: torch.Tensor, y: torch.Tensor, out_sse=None, out_mse=None):
     return out_sse, out_mse
 
 
-def mse_backward(lhs: torch.Tensor, rhs: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
+def mse_backward(lhs: torch.Tensor, rhs: torch.Tensor, scale: torch.Tensor,
+                 factor: float = 1.0) -> torch.Tensor:
+    """grad = scale * factor * (lhs - rhs), scale a device scalar."""
     grad = torch.empty_like(lhs, dtype=torch.float32)
     nat.check(nat.call("cs_mse_backward", nat.ptr(lhs), nat.ptr(rhs), nat.ptr(scale),
-                       nat.ptr(grad), int(lhs.numel()), nat.stream(lhs.device)), "cs_mse_backward")
+                       float(factor), nat.ptr(grad), int(lhs.numel()), nat.stream(lhs.device)),
+              "cs_mse_backward")
     return grad
 
 
@@ -106,11 +109,14 @@ class MSELossFunction(torch.autograd.Function):
         x, y = ctx.saved_tensors
         grad_x = grad_y = None
         if ctx.needs_input_grad[0] or ctx.needs_input_grad[1]:
-            scale = (grad_output.to(torch.float32) * (2.0 / float(ctx.numel))).reshape(1).contiguous()
+            # d loss / dx = grad_output * (2 / N) * (x - y); the product with
+            # the device scalar grad_output is formed in the kernel
+            g = _as_cuda_f32(grad_output.reshape(1), "grad_output")
+            factor = 2.0 / float(ctx.numel)
             if ctx.needs_input_grad[0]:
-                grad_x = mse_backward(x, y, scale).to(ctx.x_dtype)
+                grad_x = mse_backward(x, y, g, factor).to(ctx.x_dtype)
             if ctx.needs_input_grad[1]:
-                grad_y = mse_backward(y, x, scale).to(ctx.y_dtype)
+                grad_y = mse_backward(y, x, g, factor).to(ctx.y_dtype)
         return grad_x, grad_y, None, None, None
 
 

@@ -206,6 +206,7 @@ def bin_primitives(cubics_norm: torch.Tensor, offs: torch.Tensor, depths: torch.
     sw = None if stroke_widths is None else _f32(stroke_widths)
     basis = bernstein_basis(s, dev)
     peo = seg_eo = t0 = t1 = None
+    edge_offs = None
     if dc:
         nat.check(nat.call("cs_project_cubics", nat.ptr(cn), None, None, nat.ptr(cubics_px), None,
                            None, g, int(img_h), int(img_w), 16, 16, 0.0, 0, st),
@@ -213,9 +214,10 @@ def bin_primitives(cubics_norm: torch.Tensor, offs: torch.Tensor, depths: torch.
         edges, peo, seg_eo, t0, t1 = flatten_de_casteljau(cubics_px, offs, s, counters[1:2])
     else:
         edges = torch.empty((g * (s - 1), 2, 2), dtype=torch.float32, device=dev)
+        edge_offs = torch.empty((p + 1,), dtype=torch.int32, device=dev)
     nat.check(nat.call("cs_bin_count", nat.ptr(cn), nat.ptr(offs), nat.ptr(aw), nat.ptr(sw),
                        nat.ptr(basis), nat.ptr(cubics_px), nat.ptr(edges), nat.ptr(peo),
-                       nat.ptr(prim_ranges),
+                       nat.ptr(edge_offs), nat.ptr(prim_ranges),
                        nat.ptr(num_hit), nat.ptr(tile_bins), nat.ptr(tile_dlist),
                        nat.ptr(counters), ws.data_ptr(), p, g, INT64_MAX, INT64_MAX, s,
                        int(img_h), int(img_w), r0, r1, float(aabb_pad), int(bool(aniso)), None,
@@ -226,7 +228,8 @@ def bin_primitives(cubics_norm: torch.Tensor, offs: torch.Tensor, depths: torch.
     if status == nat.CS_ERR_ARG:
         raise _offsets_error(offs, g)
     nat.check(status, "cs_bin_count")
-    edge_offs = peo if dc else (offs.to(torch.int64) * (s - 1)).to(torch.int32)
+    if dc:
+        edge_offs = peo
     # per-frame buffers are sized in a few classes (_size_class), so that the
     # caching allocator reuses blocks from frame to frame; the sorted lists
     # are exact-length views
@@ -325,6 +328,26 @@ def raster_workspace(device: torch.device, num_tiles: int) -> torch.Tensor:
         buf = torch.zeros((need,), dtype=torch.uint8, device=device)
         _RASTER_WS[key] = buf
     return buf
+
+
+def _aa_widths(raw: torch.Tensor):
+    """Clamped anti-aliasing widths and 1/sigma^2 in one launch
+    (cs_aa_widths_forward): clamp(aa, min=1e-4), 1 / clamp(w^2, min=1e-6)."""
+    n = int(raw.numel())
+    buf = torch.empty((2, n), dtype=torch.float32, device=raw.device)
+    nat.check(nat.call("cs_aa_widths_forward", nat.ptr(raw), nat.ptr(buf[0]), nat.ptr(buf[1]), n,
+                       nat.stream(raw.device)), "cs_aa_widths_forward")
+    return buf[0], buf[1]
+
+
+def _aa_widths_grad(raw: torch.Tensor, widths: torch.Tensor, v_inv: torch.Tensor):
+    """Gradient of the raw anti-aliasing widths: -2 v_inv / clamp(w^3, 1e-12)
+    through the clamp(aa, min=1e-4) of the entry (cs_aa_widths_backward)."""
+    n = int(widths.numel())
+    out = torch.empty((n,), dtype=torch.float32, device=widths.device)
+    nat.check(nat.call("cs_aa_widths_backward", nat.ptr(raw), nat.ptr(widths), nat.ptr(v_inv),
+                       nat.ptr(out), n, nat.stream(widths.device)), "cs_aa_widths_backward")
+    return out
 
 
 def _inv_sigma2(widths: torch.Tensor) -> torch.Tensor:
@@ -525,12 +548,11 @@ class CubicFillSplatFunction(torch.autograd.Function):
         if int(fill_rules.reshape(-1).shape[0]) != num_primitives:
             raise ValueError(
                 f"fill_rules size must match primitive count ({num_primitives}), got {int(fill_rules.reshape(-1).shape[0])}")
-        widths = aa_widths.to(device=cubics_norm.device, dtype=torch.float32).reshape(-1)
-        if int(widths.numel()) != num_primitives:
+        raw = _f32(aa_widths.to(device=cubics_norm.device, dtype=torch.float32).reshape(-1))
+        if int(raw.numel()) != num_primitives:
             raise ValueError(
-                f"aa_widths size must match primitive count ({num_primitives}), got {int(widths.numel())}")
-        widths = torch.clamp(_f32(widths), min=1e-4)
-        inv_s2 = _inv_sigma2(widths)
+                f"aa_widths size must match primitive count ({num_primitives}), got {int(raw.numel())}")
+        widths, inv_s2 = _aa_widths(raw)
         col = _f32(colors)
         op = _f32(opacities).view(-1)
         rules = _i32(fill_rules).view(-1)
@@ -547,7 +569,7 @@ class CubicFillSplatFunction(torch.autograd.Function):
         ctx.binning = b
         ctx.process_fn = process_fn
         ctx.num_segments = num_segments
-        ctx.save_for_backward(cubics_norm, offs, col, op, rules, widths, inv_s2, bg, fts, fidx)
+        ctx.save_for_backward(cubics_norm, offs, col, op, rules, raw, widths, inv_s2, bg, fts, fidx)
         return out
 
     @staticmethod
@@ -555,7 +577,8 @@ class CubicFillSplatFunction(torch.autograd.Function):
         nones = (None,) * 20
         if getattr(ctx, "empty", False):
             return nones
-        cubics_norm, offs, colors, opac, rules, widths, inv_s2, bg, fts, fidx = ctx.saved_tensors
+        cubics_norm, offs, colors, opac, rules, raw, widths, inv_s2, bg, fts, fidx = \
+            ctx.saved_tensors
         b: Binning = ctx.binning
         process_fn = ctx.process_fn
         pre = _run_process_fn(process_fn, "pre_backward_rasterize", {
@@ -587,8 +610,7 @@ class CubicFillSplatFunction(torch.autograd.Function):
             v_cubics_norm = torch.empty_like(cubics_norm, dtype=torch.float32)
             v_cubics_norm[..., 0] = v_cubics_px[..., 0] * half_w
             v_cubics_norm[..., 1] = v_cubics_px[..., 1] * half_h
-        denom = torch.clamp(widths * widths * widths, min=1e-12)
-        v_aa = (-2.0 * v_inv / denom).contiguous()
+        v_aa = _aa_widths_grad(raw, widths, v_inv)
         out = [None] * 20
         out[0] = v_cubics_norm
         out[2] = v_colors
@@ -622,12 +644,11 @@ class CubicPolylineSplatFunction(torch.autograd.Function):
         if int(stroke_widths.reshape(-1).shape[0]) != num_primitives:
             raise ValueError(
                 f"stroke_widths size must match primitive count ({num_primitives}), got {int(stroke_widths.reshape(-1).shape[0])}")
-        widths = aa_widths.to(device=cubics_norm.device, dtype=torch.float32).reshape(-1)
-        if int(widths.numel()) != num_primitives:
+        raw = _f32(aa_widths.to(device=cubics_norm.device, dtype=torch.float32).reshape(-1))
+        if int(raw.numel()) != num_primitives:
             raise ValueError(
-                f"aa_widths size must match primitive count ({num_primitives}), got {int(widths.numel())}")
-        widths = torch.clamp(_f32(widths), min=1e-4)
-        inv_s2 = _inv_sigma2(widths)
+                f"aa_widths size must match primitive count ({num_primitives}), got {int(raw.numel())}")
+        widths, inv_s2 = _aa_widths(raw)
         sw = _f32(stroke_widths).view(-1)
         col = _f32(colors)
         op = _f32(opacities).view(-1)
@@ -644,7 +665,7 @@ class CubicPolylineSplatFunction(torch.autograd.Function):
         ctx.binning = b
         ctx.process_fn = process_fn
         ctx.num_segments = num_segments
-        ctx.save_for_backward(cubics_norm, offs, col, op, sw, widths, inv_s2, bg, fts, fidx)
+        ctx.save_for_backward(cubics_norm, offs, col, op, sw, raw, widths, inv_s2, bg, fts, fidx)
         return out
 
     @staticmethod
@@ -652,7 +673,8 @@ class CubicPolylineSplatFunction(torch.autograd.Function):
         nones = (None,) * 20
         if getattr(ctx, "empty", False):
             return nones
-        cubics_norm, offs, colors, opac, sw, widths, inv_s2, bg, fts, fidx = ctx.saved_tensors
+        cubics_norm, offs, colors, opac, sw, raw, widths, inv_s2, bg, fts, fidx = \
+            ctx.saved_tensors
         b: Binning = ctx.binning
         process_fn = ctx.process_fn
         pre = _run_process_fn(process_fn, "pre_backward_rasterize", {
@@ -686,8 +708,7 @@ class CubicPolylineSplatFunction(torch.autograd.Function):
             v_cubics_norm = torch.empty_like(cubics_norm, dtype=torch.float32)
             v_cubics_norm[..., 0] = v_cubics_px[..., 0] * half_w
             v_cubics_norm[..., 1] = v_cubics_px[..., 1] * half_h
-        denom = torch.clamp(widths * widths * widths, min=1e-12)
-        v_aa = (-2.0 * v_inv / denom).contiguous()
+        v_aa = _aa_widths_grad(raw, widths, v_inv)
         out = [None] * 20
         out[0] = v_cubics_norm
         out[2] = v_colors
@@ -732,8 +753,9 @@ def render_cubic_fill_splat(cubics_norm, primitive_seg_offsets, colors, opacitie
     _validate_common(num_primitives, num_segments, offs, colors, opacities, depths)
     dev = cubics_norm.device
     rules = _prim_param(fill_rules, 1, num_primitives, dev, torch.int32, "fill_rules")
-    widths = _prim_param(aa_widths, aa_width, num_primitives, dev, torch.float32, "aa_widths")
-    widths = torch.clamp(_f32(widths), min=1e-4)
+    # raw widths: the Function clamps them (min 1e-4) and masks their gradient
+    widths = _f32(_prim_param(aa_widths, aa_width, num_primitives, dev, torch.float32,
+                              "aa_widths"))
     method = normalize_cubic_flatten_method(flatten_method)
     return CubicFillSplatFunction.apply(
         cubics_norm, offs.contiguous(), colors.contiguous(), opacities.reshape(-1).contiguous(),
@@ -763,8 +785,9 @@ def render_cubic_polyline_splat(cubics_norm, primitive_seg_offsets, colors, opac
         raise ValueError(
             f"stroke_widths size must match primitive count ({num_primitives}), got {int(stroke_widths.reshape(-1).shape[0])}")
     dev = cubics_norm.device
-    widths = _prim_param(aa_widths, aa_width, num_primitives, dev, torch.float32, "aa_widths")
-    widths = torch.clamp(_f32(widths), min=1e-4)
+    # raw widths: the Function clamps them (min 1e-4) and masks their gradient
+    widths = _f32(_prim_param(aa_widths, aa_width, num_primitives, dev, torch.float32,
+                              "aa_widths"))
     method = normalize_cubic_flatten_method(flatten_method)
     return CubicPolylineSplatFunction.apply(
         cubics_norm, offs.contiguous(), colors.contiguous(), opacities.reshape(-1).contiguous(),

@@ -155,7 +155,7 @@ class FillTrainer:
         r0, r1 = self.tile_rows
         nat.check(nat.call("cs_bin_count", None, self.offs.data_ptr(),
                            self.widths.data_ptr(), None, self.basis.data_ptr(),
-                           self.cubics_px.data_ptr(), self.edges.data_ptr(), None,
+                           self.cubics_px.data_ptr(), self.edges.data_ptr(), None, None,
                            self.prim_ranges.data_ptr(), self.num_hit.data_ptr(),
                            self.tile_bins.data_ptr(), self.tile_dlist.data_ptr(),
                            self.counters.data_ptr(), self.bin_ws.data_ptr(), self.num_paths,

@@ -781,6 +781,38 @@ __device__ __forceinline__ float warp_reduce4(float v0, float v1, float v2, floa
   return c;
 }
 
+// Edge-endpoint gradients of one visit.  Many pixels of a strip share a
+// winner edge, and per-pixel atomics on one address serialise, so the warp
+// first sums its contributions per distinct winner -- one ballot round and one
+// four-value butterfly per winner -- and then four lanes add the four
+// components.  key >= 0: the winner's record is resident, the sum goes to the
+// chunk's shared accumulator dgrad[key - c0]; key = -(edge + 2): its record
+// is no longer resident, the sum goes to v_edges directly.
+__device__ __forceinline__ void add_edge_grads(const RasterArgs& A, float4* dgrad, int c0,
+                                               int key0, bool has0, const float4& g0, int key1,
+                                               bool has1, const float4& g1) {
+  const int lane = threadIdx.x & 31;
+  unsigned p0 = __ballot_sync(0xffffffffu, has0), p1 = __ballot_sync(0xffffffffu, has1);
+  while (p0 | p1) {  // every round clears at least the source lane's bit
+    const int src = p0 ? __ffs(p0) - 1 : __ffs(p1) - 1;
+    const int k = __shfl_sync(0xffffffffu, p0 ? key0 : key1, src);
+    const bool m0 = has0 && key0 == k, m1 = has1 && key1 == k;
+    p0 &= ~__ballot_sync(0xffffffffu, m0);
+    p1 &= ~__ballot_sync(0xffffffffu, m1);
+    float x = 0.0f, y = 0.0f, z = 0.0f, w = 0.0f;
+    if (m0) { x = g0.x; y = g0.y; z = g0.z; w = g0.w; }
+    if (m1) { x += g1.x; y += g1.y; z += g1.z; w += g1.w; }
+    const float r = warp_reduce4(x, y, z, w);
+    if ((lane & 7) == 0 && r != 0.0f) {
+      const int vi = lane >> 3;
+      if (k >= 0)
+        atomicAdd(reinterpret_cast<float*>(dgrad + (k - c0)) + vi, r);
+      else
+        atomicAdd(A.v_edges + (long long)(-(k + 2)) * 4 + vi, r);
+    }
+  }
+}
+
 __device__ __forceinline__ void flush_acc(const RasterArgs& A, int pid, int k, int c, float v) {
   if (v == 0.0f) return;
   if (c < 3) atomicAdd(A.v_colors + pid * 3 + c, v);
@@ -952,30 +984,16 @@ __device__ __forceinline__ bool backward_unit(const RasterArgs& A, int unit,
       }
       float acc[kAcc];
 #pragma unroll
-      for (int q = 0; q < kAcc; ++q) acc[q] = 0.0f;
+      for (int a = 0; a < kAcc; ++a) acc[a] = 0.0f;
       bool contributed = false;
+      float4 eg[2];
+      bool has_eg[2];
 #pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        float4 eg;
-        bool has_eg;
+      for (int u = 0; u < 2; ++u)
         bwd_pixel<STROKE>(s[u], m, px[u], py, u ? v1 : v0, acc, collect, A.v_opac != nullptr,
-                          A.v_inv != nullptr, eg, has_eg, contributed);
-        if (has_eg) {
-          if (s[u].bl >= 0) {
-            float4* gp = &dgrad[s[u].bl - c0];
-            atomicAdd(&gp->x, eg.x);
-            atomicAdd(&gp->y, eg.y);
-            atomicAdd(&gp->z, eg.z);
-            atomicAdd(&gp->w, eg.w);
-          } else {
-            float* gp = A.v_edges + (long long)s[u].be * 4;
-            atomicAdd(gp, eg.x);
-            atomicAdd(gp + 1, eg.y);
-            atomicAdd(gp + 2, eg.z);
-            atomicAdd(gp + 3, eg.w);
-          }
-        }
-      }
+                          A.v_inv != nullptr, eg[u], has_eg[u], contributed);
+      add_edge_grads(A, dgrad, c0, s[0].bl >= 0 ? s[0].bl : -(s[0].be + 2), has_eg[0], eg[0],
+                     s[1].bl >= 0 ? s[1].bl : -(s[1].be + 2), has_eg[1], eg[1]);
       if (__any_sync(0xffffffffu, contributed)) {
         // four sums per butterfly: lane 8 i holds value i's warp total
         const int vi = (lane >> 3) & 3;

@@ -171,8 +171,10 @@ class FillTrainer:
         n, _, nd, _ = (int(v) for v in self.counters.tolist())
         return int(math.ceil(n * slack)) + extra, int(math.ceil(nd * slack)) + 64 * extra
 
-    def forward_backward(self):
-        """Enqueue one forward + loss + backward; no host synchronisation."""
+    def forward_backward(self, join: bool = True):
+        """Enqueue one forward + loss + backward; no host synchronisation.  The
+        SSIM side stream is joined back unless join is False (the caller then
+        calls _join_side once the rest of its step is enqueued)."""
         st = nat.stream(self.device)
         r0, r1 = self.tile_rows
         status = self.counters.data_ptr() + 4
@@ -223,6 +225,10 @@ class FillTrainer:
                            self.v_ring.data_ptr(), self.num_paths, self.g_per_path, self.s - 1,
                            self.h, self.w, 1, self.prim_ranges.data_ptr(), r0, r1, st),
                   "cs_edge_grads_to_ring")
+        if join:
+            self._join_side()
+
+    def _join_side(self):
         if self.with_ssim:
             torch.cuda.current_stream(self.device).wait_event(self._join)
 
@@ -236,8 +242,11 @@ class FillTrainer:
                            nat.stream(self.device)), "cs_adam_step")
 
     def step_eager(self):
-        self.forward_backward()
+        # SSIM overlaps the backward, the edge-to-ring pass and the optimiser
+        # step; the step ends when it is done
+        self.forward_backward(join=False)
         self.optimizer_step()
+        self._join_side()
 
     def capture(self, warmup: int = 3):
         """Capture one full training step into a CUDA graph."""

@@ -306,11 +306,11 @@ def executed_roofline(flop_b, t_b, flop_f, t_f, peak):
                      "lists)"}
 
 
-def ncu_traffic(kernel: str):
-    """DRAM bytes (read + write) per launch of `kernel` from the committed ncu
-    summary of the config-2 raster kernels (profiles/raster_fill_config2.md),
-    or None when the summary is absent."""
-    path = os.path.join(ROOT, "profiles", "raster_fill_config2.md")
+def ncu_traffic(kernel: str, summary: str = "raster_fill_config2.md"):
+    """DRAM bytes (read + write) per launch of `kernel` from a committed ncu
+    summary under profiles/ (default: the config-2 raster kernels), or None
+    when the summary is absent."""
+    path = os.path.join(ROOT, "profiles", summary)
     try:
         with open(path) as f:
             for line in f:
@@ -629,6 +629,9 @@ def run_stroke(args, rank, world, local_rank):
                    "l2": "flushed before every step (256 MiB write), outside the step events"},
         "clocks": clocks,
         "roofline": {"kernel": "raster_backward (stroke)", "bound": "fp32",
+                     "traffic": ncu_traffic("raster_backward_kernel", "raster_stroke_config4.md"),
+                     "traffic_note": "dram read+write bytes per launch from one ncu capture "
+                                     "(profiles/raster_stroke_config4.md)",
                      "achieved": round(flop_b / (t_bwd * 1e-3) / 1e12, 3),
                      "peak": round(peak, 2), "unit": "TFLOP/s",
                      "frac": round(flop_b / (t_bwd * 1e-3) / 1e12 / peak, 4),

@@ -60,6 +60,8 @@ struct RasterArgs {
                          // of the strip: the forward writes them, the backward walks them
   const float* bg;
   int H, W, tbx, r0, nunits;
+  int vec2;              // W even and per-pixel buffers 8-byte aligned: a lane's two
+                         // pixels move as one 8-byte access per plane
   int* status;
   unsigned* queue;       // workspace: next dynamically taken unit
   unsigned* ticket;      // workspace: CTA completion ticket
@@ -554,6 +556,42 @@ __device__ __forceinline__ bool forward_unit(const RasterArgs& A, int unit,
   const float bg0 = A.bg[0], bg1 = A.bg[1], bg2 = A.bg[2];
   const long long hw = (long long)A.H * A.W;
   float sse = 0.0f;
+  if (ok && A.vec2 && in0 && in1) {  // both pixels: paired 8-byte stores and loads
+    const long long pix = (long long)i * A.W + j0;
+    const float o[2][3] = {{p0.a0 + p0.T * bg0, p0.a1 + p0.T * bg1, p0.a2 + p0.T * bg2},
+                           {p1.a0 + p1.T * bg0, p1.a1 + p1.T * bg1, p1.a2 + p1.T * bg2}};
+    *reinterpret_cast<float2*>(A.fts + pix) = make_float2(p0.T, p1.T);
+    *reinterpret_cast<int2*>(A.fidx + pix) = make_int2(p0.cur, p1.cur);
+    float2* oh = reinterpret_cast<float2*>(A.out + pix * 3);
+    oh[0] = make_float2(o[0][0], o[0][1]);
+    oh[1] = make_float2(o[0][2], o[1][0]);
+    oh[2] = make_float2(o[1][1], o[1][2]);
+    float kc[2][3];
+#pragma unroll
+    for (int u = 0; u < 2; ++u)
+#pragma unroll
+      for (int c = 0; c < 3; ++c) kc[u][c] = fminf(fmaxf(o[u][c], 0.0f), 1.0f);
+    if (A.out_chw) {
+#pragma unroll
+      for (int c = 0; c < 3; ++c)
+        *reinterpret_cast<float2*>(A.out_chw + c * hw + pix) = make_float2(kc[0][c], kc[1][c]);
+    }
+    if (A.loss_tgt) {
+      float2 t[3];
+#pragma unroll
+      for (int c = 0; c < 3; ++c) t[c] = *reinterpret_cast<const float2*>(A.loss_tgt + c * hw + pix);
+#pragma unroll
+      for (int c = 0; c < 3; ++c) {
+        const float d = kc[0][c] - t[c].x;
+        sse = __fmaf_rn(d, d, sse);
+      }
+#pragma unroll
+      for (int c = 0; c < 3; ++c) {
+        const float d = kc[1][c] - t[c].y;
+        sse = __fmaf_rn(d, d, sse);
+      }
+    }
+  } else {
 #pragma unroll
   for (int u = 0; u < 2; ++u) {
     const FwdPix& p = u ? p1 : p0;
@@ -579,6 +617,7 @@ __device__ __forceinline__ bool forward_unit(const RasterArgs& A, int unit,
       sse = __fmaf_rn(d1, d1, sse);
       sse = __fmaf_rn(d2, d2, sse);
     }
+  }
   }
   if (A.loss_tgt) {
     sse = warp_sum(sse);
@@ -840,44 +879,69 @@ __device__ __forceinline__ bool backward_unit(const RasterArgs& A, int unit,
   const float scale = A.v_out ? 0.0f : *A.mse_scale;
   BwdPix s[2];
   int kmax = -1;
+  // per-pixel inputs: T, final_idx and the image gradient (given, or the MSE
+  // gradient from the image and the target), paired 8-byte loads when both
+  // pixels are in the image
+  const bool in2[2] = {i < A.H && j0 < A.W, i < A.H && j0 + 1 < A.W};
+  float T2[2] = {1.0f, 1.0f}, vv[2][3] = {{0.f, 0.f, 0.f}, {0.f, 0.f, 0.f}};
+  int F2[2] = {-1, -1};
+  const long long hw = (long long)A.H * A.W;
+  const long long pix0 = (long long)i * A.W + j0;
+  if (A.vec2 && in2[0] && in2[1]) {
+    const float2 t2 = *reinterpret_cast<const float2*>(A.fts_in + pix0);
+    const int2 f2 = *reinterpret_cast<const int2*>(A.fidx_in + pix0);
+    T2[0] = t2.x; T2[1] = t2.y; F2[0] = f2.x; F2[1] = f2.y;
+    const float2* src = reinterpret_cast<const float2*>((A.v_out ? A.v_out : A.out_img) + pix0 * 3);
+    const float2 a = src[0], b = src[1], c = src[2];
+    const float o[2][3] = {{a.x, a.y, b.x}, {b.y, c.x, c.y}};
+    if (A.v_out) {
+#pragma unroll
+      for (int u = 0; u < 2; ++u)
+#pragma unroll
+        for (int ch = 0; ch < 3; ++ch) vv[u][ch] = o[u][ch];
+    } else {
+#pragma unroll
+      for (int ch = 0; ch < 3; ++ch) {
+        const float2 t = *reinterpret_cast<const float2*>(A.tgt + ch * hw + pix0);
+        vv[0][ch] = (o[0][ch] >= 0.0f && o[0][ch] <= 1.0f) ? scale * (o[0][ch] - t.x) : 0.0f;
+        vv[1][ch] = (o[1][ch] >= 0.0f && o[1][ch] <= 1.0f) ? scale * (o[1][ch] - t.y) : 0.0f;
+      }
+    }
+  } else {
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      if (!in2[u]) continue;
+      const long long pix = pix0 + u;
+      T2[u] = A.fts_in[pix];
+      F2[u] = A.fidx_in[pix];
+#pragma unroll
+      for (int ch = 0; ch < 3; ++ch) {
+        if (A.v_out) {
+          vv[u][ch] = A.v_out[pix * 3 + ch];
+        } else {
+          const float o = A.out_img[pix * 3 + ch];
+          const float t = A.tgt[ch * hw + pix];
+          vv[u][ch] = (o >= 0.0f && o <= 1.0f) ? scale * (o - t) : 0.0f;
+        }
+      }
+    }
+  }
 #pragma unroll
   for (int u = 0; u < 2; ++u) {
-    const int j = j0 + u;
-    s[u].in = i < A.H && j < A.W;
+    s[u].in = in2[u];
     s[u].b0 = s[u].b1 = s[u].b2 = 0.0f;
     s[u].md = 1e30f;
     s[u].be = -1;
     s[u].bl = -1;
     s[u].bp = s[u].bcx = s[u].bcy = 0.0f;
     s[u].w = s[u].n = 0;
-    if (s[u].in) {
-      const long long pix = (long long)i * A.W + j;
-      s[u].T = A.fts_in[pix];
-      s[u].fidx = A.fidx_in[pix];
-      float v[3];
-      if (A.v_out) {
-        v[0] = A.v_out[pix * 3];
-        v[1] = A.v_out[pix * 3 + 1];
-        v[2] = A.v_out[pix * 3 + 2];
-      } else {
-        const long long hw = (long long)A.H * A.W;
-#pragma unroll
-        for (int c = 0; c < 3; ++c) {
-          const float o = A.out_img[pix * 3 + c];
-          const float t = A.tgt[c * hw + pix];
-          v[c] = (o >= 0.0f && o <= 1.0f) ? scale * (o - t) : 0.0f;
-        }
-      }
-      s[u].v0 = v[0];
-      s[u].v1 = v[1];
-      s[u].v2 = v[2];
-      s[u].bgd = A.bg[0] * v[0] + A.bg[1] * v[1] + A.bg[2] * v[2];
-      kmax = max(kmax, s[u].fidx);
-    } else {
-      s[u].T = 1.0f;
-      s[u].fidx = -1;
-      s[u].v0 = s[u].v1 = s[u].v2 = s[u].bgd = 0.0f;
-    }
+    s[u].T = T2[u];
+    s[u].fidx = F2[u];
+    s[u].v0 = vv[u][0];
+    s[u].v1 = vv[u][1];
+    s[u].v2 = vv[u][2];
+    s[u].bgd = in2[u] ? A.bg[0] * vv[u][0] + A.bg[1] * vv[u][1] + A.bg[2] * vv[u][2] : 0.0f;
+    if (in2[u]) kmax = max(kmax, s[u].fidx);
     s[u].Tf = s[u].T;
   }
   kmax = min(warp_max_i(kmax), re - 1);  // this warp's last needed intersect
@@ -1103,6 +1167,12 @@ inline int launch_raster(bool stroke, bool bwd, const RasterArgs& a, int H, int 
   args.H = H;
   args.W = W;
   args.nunits = kStrips * tbx * (r1 - r0);
+  {
+    auto al8 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 7u) == 0; };
+    args.vec2 = (W % 2 == 0) && al8(args.fts) && al8(args.fidx) && al8(args.out) &&
+                al8(args.out_chw) && al8(args.loss_tgt) && al8(args.fts_in) &&
+                al8(args.fidx_in) && al8(args.v_out) && al8(args.out_img) && al8(args.tgt);
+  }
   if (!stroke && !bwd) {
     auto k = raster_forward_kernel<false>;
     k<<<persistent_ctas<0>(k, args.nunits), kRT, 0, st>>>(args);

@@ -697,21 +697,25 @@ def run_sweep(args, rank, world, local_rank):
                           "config": {"workload": "config5", "paths": paths, "samples": samples,
                                      "intersects": n_isect, "status": status}})
             del tr
-    # standalone metric kernels on one 768x512 RGB pair (inputs > L2 after the flush)
-    x = torch.rand(1, 3, 512, 768, device=dev)
-    y = torch.rand(1, 3, 512, 768, device=dev)
-    n = x.numel()
-    for name, fn, nbytes in (("mse", lambda: mt.sse_mse(x.view(-1), y.view(-1)), 8 * n),
-                             ("ssim", lambda: mt.ssim_per_plane(x, y, 11, 1.5, 1e-4, 9e-4),
-                              8 * n)):
-        for _ in range(5):
-            fn()
-        ms = statistics.median(time_device_calls(fn, 30, flush, stream))
-        lines.append({"metric": f"standalone {name} kernel bandwidth, 768x512x3 fp32 pair",
-                      "value": round(nbytes / (ms * 1e-3) / 1e9, 1), "unit": "GB/s",
-                      "ms": round(ms, 5), "bytes": nbytes, "peak_hbm_gbs": hbm,
-                      "frac": round(nbytes / (ms * 1e-3) / 1e9 / hbm, 4),
-                      "l2": "flushed before every call"})
+    # standalone metric kernels: one 768x512 RGB pair (9.4 MB, launch-latency
+    # bound) and the sweep's 64 scenes as one [64, 3, 512, 768] batch (604 MB,
+    # HBM bound); L2 flushed before every call
+    for batch in (1, 64):
+        x = torch.rand(batch, 3, 512, 768, device=dev)
+        y = torch.rand(batch, 3, 512, 768, device=dev)
+        n = x.numel()
+        for name, fn, nbytes in (("mse", lambda: mt.sse_mse(x.view(-1), y.view(-1)), 8 * n),
+                                 ("ssim", lambda: mt.ssim_per_plane(x, y, 11, 1.5, 1e-4, 9e-4),
+                                  8 * n)):
+            for _ in range(5):
+                fn()
+            ms = statistics.median(time_device_calls(fn, 30 if batch == 1 else 10, flush, stream))
+            lines.append({"metric": f"standalone {name} kernel bandwidth, {batch}x3x512x768 fp32 pair",
+                          "value": round(nbytes / (ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                          "ms": round(ms, 5), "bytes": nbytes, "peak_hbm_gbs": hbm,
+                          "frac": round(nbytes / (ms * 1e-3) / 1e9 / hbm, 4),
+                          "l2": "flushed before every call"})
+        del x, y
     if rank != 0:
         return None
     return [_json.dumps(line) for line in lines]

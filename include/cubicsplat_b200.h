@@ -154,7 +154,10 @@ CS_API int cs_isect_edge_ranges(const int32_t *prim_ids_sorted, const int32_t *p
  * (may be NULL) receives the uniform flatten's offsets offs * (S - 1).
  * With cs_bin_sort this replaces project (K3) + flatten + K4 + cumsum + K5 +
  * torch.sort + K6 of _CubicFillSplatFunction.forward, cubic_splatting.py:2815-2908.
- * Workspace: cs_bin_workspace_size(num_tiles). */
+ * Workspace: cs_bin_workspace_size(num_tiles) bytes, zeroed before its first
+ * use; every call leaves it zeroed again (cs_bin_sort reads the cursors it
+ * holds, so a call's cs_bin_sort must follow it before the next cs_bin_count
+ * on the same workspace). */
 CS_API size_t cs_bin_workspace_size(int64_t num_tiles);
 CS_API int cs_bin_count(const float *cubics_norm, const int32_t *prim_seg_offsets,
                  const float *aa_widths, const float *stroke_widths, const float *basis,

@@ -234,10 +234,13 @@ __global__ void edge_ranges_kernel(const int* __restrict__ pids, const int* __re
 // ---------------------------------------------------------------------------
 // fused pipeline
 
+// Zeroed before its first use; every cs_bin_count leaves the counts and the
+// ticket zeroed again (the scan clears what it read).
 struct BinWorkspace {
   int* tile_counts;     // [T] intersects per tile
   int* tile_ecounts;    // [T] edge slots per tile (each strip's record capacity)
   int* cursor;          // [T] scatter cursors
+  unsigned* ticket;     // bin_prep CTAs done (the last one runs the scan)
 };
 
 __host__ __device__ inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
@@ -249,10 +252,94 @@ inline BinWorkspace bin_ws(void* base, long long ntiles) {
   w.tile_counts = reinterpret_cast<int*>(b);
   w.tile_ecounts = reinterpret_cast<int*>(b + a);
   w.cursor = reinterpret_cast<int*>(b + 2 * a);
+  w.ticket = reinterpret_cast<unsigned*>(b + 3 * a);
   return w;
 }
 
-inline size_t bin_ws_size(long long ntiles) { return align256(sizeof(int) * ntiles) * 3; }
+inline size_t bin_ws_size(long long ntiles) { return align256(sizeof(int) * ntiles) * 3 + 256; }
+
+// Exclusive scans over the tiles [t0, t1) (the band) of the per-tile
+// intersect counts into tile ranges [start, end) and of the per-tile edge-slot
+// counts into staged-record ranges -- tile t owns kStrips consecutive lists of
+// capacity ecount[t] each, so tile_dlist[t] = (first record, ecount[t]) and
+// the record bound is kStrips * sum(ecount) -- by one CTA of any multiple of
+// 32 threads.  Tiles outside the band read as empty.  If a total exceeds its
+// capacity every range is written empty and the status is set.  The counts
+// are zeroed as they are consumed.  counts (with bins, cursor) or ecounts
+// (with dlr) may be NULL.
+__device__ void scan_tiles(int* __restrict__ counts, int* __restrict__ ecounts,
+                           int* __restrict__ bins, int* __restrict__ dlr,
+                           int* __restrict__ cursor, int* __restrict__ counters, long long t0,
+                           long long t1, long long nt, long long icap, long long dcap) {
+  __shared__ int wa[32], wb[32];
+  __shared__ long long s_ta, s_tb;
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const int nthr = blockDim.x, nw = nthr >> 5;
+  const long long n = t1 - t0;
+  const long long chunk = (n + nthr - 1) / nthr;
+  const long long b = t0 + tid * chunk, e = min(t1, b + chunk);
+  int la = 0, lb = 0;
+  for (long long i = b; i < e; ++i) {
+    if (counts) la += __ldcg(counts + i);
+    if (ecounts) lb += __ldcg(ecounts + i);
+  }
+  int ia = warp_incl_scan(la, lane), ib = warp_incl_scan(lb, lane);
+  if (lane == 31) {
+    wa[wid] = ia;
+    wb[wid] = ib;
+  }
+  __syncthreads();
+  if (wid == 0) {
+    const int va = lane < nw ? wa[lane] : 0, vb = lane < nw ? wb[lane] : 0;
+    const int xa = warp_incl_scan(va, lane), xb = warp_incl_scan(vb, lane);
+    wa[lane] = xa - va;
+    wb[lane] = xb - vb;
+    if (lane == 31) {
+      s_ta = xa;
+      s_tb = (long long)kStrips * xb;
+      if (counts) counters[0] = xa;
+      if (ecounts) counters[2] = (int)min((long long)kStrips * xb, (long long)INT32_MAX);
+      if ((counts && xa > icap) || (ecounts && s_tb > dcap)) counters[1] = CS_ERR_CAPACITY;
+    }
+  }
+  __syncthreads();
+  const bool overflow = (counts && s_ta > icap) || (ecounts && s_tb > dcap);
+  int ra = wa[wid] + ia - la, rb = wb[wid] + ib - lb;
+  for (long long i = b; i < e; ++i) {
+    if (counts) {
+      const int c = overflow ? 0 : __ldcg(counts + i);
+      counts[i] = 0;
+      cursor[i] = ra;
+      bins[2 * i] = c > 0 ? ra : 0;
+      bins[2 * i + 1] = c > 0 ? ra + c : 0;
+      ra += c;
+    }
+    if (ecounts) {
+      const int c = overflow ? 0 : __ldcg(ecounts + i);
+      ecounts[i] = 0;
+      dlr[2 * i] = c > 0 ? kStrips * rb : 0;
+      dlr[2 * i + 1] = c > 0 ? c : 0;
+      rb += c;
+    }
+  }
+  for (long long i = tid; i < nt; i += nthr) {  // a band: the other tiles are empty
+    if (i >= t0 && i < t1) continue;
+    if (counts) bins[2 * i] = bins[2 * i + 1] = 0;
+    if (ecounts) dlr[2 * i] = dlr[2 * i + 1] = 0;
+  }
+}
+
+// The scan on its own (the per-stage staging path): one CTA of 1024.
+__global__ void __launch_bounds__(1024) bin_scan_kernel(int* __restrict__ counts,
+                                                        int* __restrict__ ecounts,
+                                                        int* __restrict__ bins,
+                                                        int* __restrict__ dlr,
+                                                        int* __restrict__ cursor,
+                                                        int* __restrict__ counters, long long t0,
+                                                        long long t1, long long icap,
+                                                        long long dcap) {
+  scan_tiles(counts, ecounts, bins, dlr, cursor, counters, t0, t1, t1, icap, dcap);
+}
 
 // Normalised control points of segment `seg`: from cubics_norm [n, 4, 2], or,
 // when ring != NULL, from the ring parameterisation of closed paths (segment k
@@ -279,22 +366,18 @@ __device__ __forceinline__ void load_segment(const float* __restrict__ cn,
   }
 }
 
-// One warp per primitive: project + bound every segment, union the rects,
-// flatten all segments into edges (unless peo gives pre-flattened edges with
-// their CSR offsets), and add the primitive to the intersect and edge-slot
-// counts of its tiles within the band of tile rows [r0, r1).
-__global__ void __launch_bounds__(256) bin_prep_kernel(
+// One warp: project + bound every segment of primitive p, union the rects,
+// flatten the segments (unless pre-flattened), and count the primitive in
+// its tiles within the band.
+__device__ __forceinline__ void prep_primitive(
     const float* __restrict__ cn, const float* __restrict__ ring, int ring_g,
     const int* __restrict__ offs, const int* __restrict__ peo, int* __restrict__ peo_out,
-    const float* __restrict__ aa,
-    const float* __restrict__ sw, const float* __restrict__ basis, float* __restrict__ cpx,
-    float* __restrict__ edges, int* __restrict__ pr, int* __restrict__ hits,
-    int* __restrict__ tile_counts, int* __restrict__ tile_ecounts, int* __restrict__ status,
-    long long np, long long nseg_total, int S, float half_w, float half_h, int tbx, int tby,
-    int r0, int r1, float pad, int aniso) {
-  long long p = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const float* __restrict__ aa, const float* __restrict__ sw, const float* __restrict__ basis,
+    float* __restrict__ cpx, float* __restrict__ edges, int* __restrict__ pr,
+    int* __restrict__ hits, int* __restrict__ tile_counts, int* __restrict__ tile_ecounts,
+    int* __restrict__ status, long long p, long long np, long long nseg_total, int S,
+    float half_w, float half_h, int tbx, int tby, int r0, int r1, float pad, int aniso) {
   int lane = threadIdx.x & 31;
-  if (p >= np) return;
   int s0 = offs[p], s1 = offs[p + 1];
   if (peo_out && lane == 0) {  // primitive edge offsets of the uniform flatten: offs * (S - 1)
     peo_out[p] = (int)((long long)s0 * (S - 1));
@@ -366,68 +449,38 @@ __global__ void __launch_bounds__(256) bin_prep_kernel(
   }
 }
 
-// Exclusive scan over the tiles [t0, t1) of per-tile intersect counts into tile ranges [start, end)
-// and of per-tile edge-slot counts into staged-record ranges: tile t owns
-// kStrips consecutive lists of capacity ecount[t] each, so tile_dlist[t] =
-// (first record, ecount[t]) and the record bound is kStrips * sum(ecount).
-// One CTA of 1024.  Either input may be NULL.  If a total exceeds its
-// capacity every range is written empty and the status is set.
-__global__ void __launch_bounds__(1024) bin_scan_kernel(const int* __restrict__ counts,
-                                                        const int* __restrict__ ecounts,
-                                                        int* __restrict__ bins,
-                                                        int* __restrict__ dlr,
-                                                        int* __restrict__ cursor,
-                                                        int* __restrict__ counters, long long t0,
-                                                        long long t1, long long icap,
-                                                        long long dcap) {
-  __shared__ int wa[32], wb[32];
-  __shared__ long long s_ta, s_tb;
-  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-  const long long nt = t1 - t0;  // tiles [t0, t1): the band
-  const long long chunk = (nt + 1023) / 1024;
-  const long long b = t0 + tid * chunk, e = min(t1, b + chunk);
-  int la = 0, lb = 0;
-  for (long long i = b; i < e; ++i) {
-    if (counts) la += counts[i];
-    if (ecounts) lb += ecounts[i];
-  }
-  int ia = warp_incl_scan(la, lane), ib = warp_incl_scan(lb, lane);
-  if (lane == 31) {
-    wa[wid] = ia;
-    wb[wid] = ib;
+// One warp per primitive: project + bound every segment, union the rects,
+// flatten all segments into edges (unless peo gives pre-flattened edges with
+// their CSR offsets), and add the primitive to the intersect and edge-slot
+// counts of its tiles within the band of tile rows [r0, r1).
+__global__ void __launch_bounds__(256) bin_prep_kernel(
+    const float* __restrict__ cn, const float* __restrict__ ring, int ring_g,
+    const int* __restrict__ offs, const int* __restrict__ peo, int* __restrict__ peo_out,
+    const float* __restrict__ aa,
+    const float* __restrict__ sw, const float* __restrict__ basis, float* __restrict__ cpx,
+    float* __restrict__ edges, int* __restrict__ pr, int* __restrict__ hits,
+    BinWorkspace ws, int* __restrict__ bins, int* __restrict__ dlr, int* __restrict__ counters,
+    long long np, long long nseg_total, int S, float half_w, float half_h, int tbx, int tby,
+    int r0, int r1, float pad, int aniso, long long icap, long long dcap) {
+  const long long p = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (p < np) prep_primitive(cn, ring, ring_g, offs, peo, peo_out, aa, sw, basis, cpx, edges, pr,
+                             hits, ws.tile_counts, ws.tile_ecounts, counters + 1, p, np,
+                             nseg_total, S, half_w, half_h, tbx, tby, r0, r1, pad, aniso);
+  // the last CTA to finish scans the counts
+  __shared__ bool last;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    last = atomicAdd(ws.ticket, 1u) == gridDim.x - 1;
   }
   __syncthreads();
-  if (wid == 0) {
-    int va = wa[lane], vb = wb[lane];
-    int xa = warp_incl_scan(va, lane), xb = warp_incl_scan(vb, lane);
-    wa[lane] = xa - va;
-    wb[lane] = xb - vb;
-    if (lane == 31) {
-      s_ta = xa;
-      s_tb = (long long)kStrips * xb;
-      if (counts) counters[0] = xa;
-      if (ecounts) counters[2] = (int)min((long long)kStrips * xb, (long long)INT32_MAX);
-      if ((counts && xa > icap) || (ecounts && s_tb > dcap)) counters[1] = CS_ERR_CAPACITY;
-    }
-  }
-  __syncthreads();
-  const bool overflow = (counts && s_ta > icap) || (ecounts && s_tb > dcap);
-  int ra = wa[wid] + ia - la, rb = wb[wid] + ib - lb;
-  for (long long i = b; i < e; ++i) {
-    if (counts) {
-      const int c = overflow ? 0 : counts[i];
-      cursor[i] = ra;
-      bins[2 * i] = c > 0 ? ra : 0;
-      bins[2 * i + 1] = c > 0 ? ra + c : 0;
-      ra += c;
-    }
-    if (ecounts) {
-      const int c = overflow ? 0 : ecounts[i];
-      dlr[2 * i] = c > 0 ? kStrips * rb : 0;
-      dlr[2 * i + 1] = c > 0 ? c : 0;
-      rb += c;
-    }
-  }
+  if (!last) return;
+  __threadfence();
+  const long long nt = (long long)tbx * tby;
+  const long long t0 = (long long)r0 * tbx, t1 = (long long)max(r0, r1) * tbx;
+  scan_tiles(ws.tile_counts, ws.tile_ecounts, bins, dlr, ws.cursor, counters, t0, t1, nt, icap,
+             dcap);
+  if (threadIdx.x == 0) *ws.ticket = 0u;
 }
 
 // One warp per primitive: scatter (depth key << 32 | primitive id) into the
@@ -435,9 +488,11 @@ __global__ void __launch_bounds__(1024) bin_scan_kernel(const int* __restrict__ 
 __global__ void __launch_bounds__(256) bin_scatter_kernel(
     const int* __restrict__ pr, const float* __restrict__ depths, int* __restrict__ cursor,
     unsigned long long* __restrict__ pairs, const int* __restrict__ counters, long long np,
-    int tbx, long long capacity, int r0, int r1) {
+    int tbx, long long capacity, int r0, int r1, int* __restrict__ lists) {
   long long p = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   int lane = threadIdx.x & 31;
+  // the staging pass appends to the dispatch lists: start them empty
+  if (lists && blockIdx.x == 0 && threadIdx.x < kUnitBuckets) lists[threadIdx.x] = 0;
   if (p >= np) return;
   if (counters[0] > capacity) return;  // overflow reported by the scan
   int4 r = *reinterpret_cast<const int4*>(pr + p * 4);
@@ -934,25 +989,15 @@ int cs_bin_count(const float* cubics_norm, const int32_t* prim_seg_offsets, cons
   const long long nt = (long long)tbx * tby;
   const int r0 = max(0, tile_row_begin), r1 = min(tby, tile_row_end);
   BinWorkspace ws = bin_ws(workspace, nt);
-  cudaMemsetAsync(ws.tile_counts, 0, align256(sizeof(int) * nt) * 2, st);
-  if (num_primitives > 0) {
-    bin_prep_kernel<<<ceil_div(num_primitives * 32, 256), 256, 0, st>>>(
-        cubics_norm, ring, ring_segs_per_path, prim_seg_offsets, prim_edge_offsets,
-        prim_edge_offsets ? nullptr : prim_edge_offsets_out, aa_widths,
-        stroke_widths, basis, cubics_px, edges_px,
-        prim_tile_ranges, num_tiles_hit, ws.tile_counts, ws.tile_ecounts, counters + 1,
-        num_primitives, num_segments, samples, 0.5f * (float)img_width,
-        0.5f * (float)img_height, tbx, tby, r0, r1, aabb_pad, aniso);
-  }
-  const long long t0 = (long long)r0 * tbx, t1 = (long long)max(r0, r1) * tbx;
-  if (t0 > 0 || t1 < nt) {  // a band: tiles outside it read as empty
-    cudaMemsetAsync(tile_bins, 0, sizeof(int32_t) * 2 * nt, st);
-    cudaMemsetAsync(tile_dlist, 0, sizeof(int32_t) * 2 * nt, st);
-  }
-  bin_scan_kernel<<<1, 1024, 0, st>>>(ws.tile_counts, ws.tile_ecounts, tile_bins, tile_dlist,
-                                      ws.cursor, counters, t0, t1,
-                                      (isect_capacity > 0 ? isect_capacity : 0),
-                                      (dlist_capacity > 0 ? dlist_capacity : 0));
+  // one launch: a warp per primitive, then the last CTA scans the tile counts
+  // (at least one CTA, so that an empty scene still gets empty tile ranges)
+  bin_prep_kernel<<<max(1, ceil_div(num_primitives * 32, 256)), 256, 0, st>>>(
+      cubics_norm, ring, ring_segs_per_path, prim_seg_offsets, prim_edge_offsets,
+      prim_edge_offsets ? nullptr : prim_edge_offsets_out, aa_widths, stroke_widths, basis,
+      cubics_px, edges_px, prim_tile_ranges, num_tiles_hit, ws, tile_bins, tile_dlist, counters,
+      num_primitives, num_segments, samples, 0.5f * (float)img_width, 0.5f * (float)img_height,
+      tbx, tby, r0, r1, aabb_pad, aniso, (isect_capacity > 0 ? isect_capacity : 0),
+      (dlist_capacity > 0 ? dlist_capacity : 0));
   return launch_status();
 }
 
@@ -1005,13 +1050,12 @@ int cs_bin_sort(const int32_t* prim_tile_ranges, const float* depths, const int3
   unsigned long long* pairs = reinterpret_cast<unsigned long long*>(isect_ids_sorted);
   bin_scatter_kernel<<<ceil_div(num_primitives * 32, 256), 256, 0, st>>>(
       prim_tile_ranges, depths, ws.cursor, pairs, counters, num_primitives, tbx, isect_capacity,
-      r0, r1);
+      r0, r1, stage ? unit_order : nullptr);
   StageIO io = stage_io(prim_ids_sorted, edges_px, nullptr, prim_edge_offsets, colors, opacities,
                         inv_sigma2s, fill_rules, stroke_widths, tile_dlist, imeta, rowoff,
                         isect_strips, dlist, tbx);
   dim3 grid(tbx, r1 - r0);
-  int* lists = stage ? unit_order : nullptr;
-  if (lists) cudaMemsetAsync(lists, 0, sizeof(int) * kUnitBuckets, st);
+  int* lists = stage ? unit_order : nullptr;  // counts cleared by bin_scatter_kernel
   if (stroke_widths)
     bin_tile_kernel<true><<<grid, kSortThreads, 0, st>>>(
         tile_bins, depths, pairs, prim_ids_sorted, reinterpret_cast<long long*>(isect_ids_sorted),

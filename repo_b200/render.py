@@ -199,7 +199,7 @@ def bin_primitives(cubics_norm: torch.Tensor, offs: torch.Tensor, depths: torch.
     tile_bins = torch.empty((nt, 2), dtype=torch.int32, device=dev)
     tile_dlist = torch.empty((nt, 2), dtype=torch.int32, device=dev)
     counters = torch.zeros((4,), dtype=torch.int32, device=dev)
-    ws = torch.empty((int(nat.call("cs_bin_workspace_size", nt)),), dtype=torch.uint8, device=dev)
+    ws = _cached_workspace(_BIN_WS, dev, int(nat.call("cs_bin_workspace_size", nt)))
     st = nat.stream(dev)
     cn = _f32(cubics_norm)
     aw = _f32(aa_widths)
@@ -309,6 +309,20 @@ def _size_class(n: int) -> int:
 
 
 _RASTER_WS: dict = {}
+_BIN_WS: dict = {}
+
+
+def _cached_workspace(cache: dict, device: torch.device, nbytes: int) -> torch.Tensor:
+    """Workspace per device and exact size, zeroed when allocated and left
+    zeroed by every launch that uses it, so launches in stream order share it.
+    Keyed by size because its layout depends on the tile count: a buffer laid
+    out for another grid would put the counters where that grid left data."""
+    key = (str(device), int(nbytes))
+    buf = cache.get(key)
+    if buf is None:
+        buf = torch.zeros((max(nbytes, 256),), dtype=torch.uint8, device=device)
+        cache[key] = buf
+    return buf
 
 
 def _bwd_lists(b: "Binning"):

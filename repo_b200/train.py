@@ -109,7 +109,8 @@ class FillTrainer:
         self.unit_order_bwd = torch.empty_like(self.unit_order)  # filled by the forward
         # intersects, sticky status, staged-record bound, unused
         self.counters = torch.zeros((4,), device=dev, dtype=i32)
-        self.bin_ws = torch.empty((int(nat.call("cs_bin_workspace_size", nt)),), device=dev,
+        # zeroed once: every cs_bin_count leaves its counters zeroed again
+        self.bin_ws = torch.zeros((int(nat.call("cs_bin_workspace_size", nt)),), device=dev,
                                   dtype=torch.uint8)
         self.raster_ws = torch.zeros((int(nat.call("cs_raster_workspace_size", nt)),), device=dev,
                                    dtype=torch.uint8)

@@ -226,6 +226,11 @@ CS_API int cs_tile_stage(const int32_t *prim_ids_sorted, const int32_t *tile_bin
  * strip, the ids of the intersects that composited at least one of its
  * pixels; given to the backward, it walks only those (exactly the ones that
  * can carry a gradient) instead of every intersect of the tile.
+ * visit_winners (may be NULL; cs_visit_winners_size bytes; used only with
+ * visit_lists) receives, per listed visit and lane, each of the lane's two
+ * pixels' closest record (relative to the intersect's first, 7 bits) and
+ * inside state (1 bit); given to the backward, it evaluates only that record
+ * per pixel instead of walking all of the intersect's records.
  * out_chw_clamped
  * [3, H, W] (may be NULL) also receives clamp(out, 0, 1) channel-major, the
  * image the training loss sees (the reference does torch.clamp + permute,
@@ -243,11 +248,12 @@ CS_API int cs_tile_stage(const int32_t *prim_ids_sorted, const int32_t *tile_bin
  * manbo/ops/metric.py:18-163. */
 CS_API size_t cs_raster_workspace_size(int64_t num_tiles);
 CS_API size_t cs_visit_lists_size(int64_t isect_capacity, int64_t num_tiles);
+CS_API size_t cs_visit_winners_size(int64_t isect_capacity, int64_t num_tiles);
 CS_API int cs_fill_forward(const int32_t *prim_ids_sorted, const int32_t *tile_bins,
                     const int32_t *tile_dlist, const void *imeta, const int32_t *isect_strips,
                     const int32_t *rowoff, const void *dlist, const int32_t *unit_order,
-                    int32_t *unit_order_bwd, int32_t *visit_lists, const float *background,
-                    float *out_img,
+                    int32_t *unit_order_bwd, int32_t *visit_lists, uint16_t *visit_winners,
+                    const float *background, float *out_img,
                     float *final_Ts, int32_t *final_idx, float *out_chw_clamped,
                     const float *target_chw, float *loss_out, int32_t *status,
                     void *workspace, int32_t img_height, int32_t img_width,
@@ -264,13 +270,14 @@ CS_API int cs_fill_forward(const int32_t *prim_ids_sorted, const int32_t *tile_b
  * v_inv_sigma2s may be NULL (not accumulated).  workspace as for the forward.
  * visit_lists (may be NULL: every intersect up to final_idx is walked) is the
  * forward's output of the same frame; a list that does not fit the tile bins
- * sets CS_ERR_ARG in status and its strip is skipped.
+ * sets CS_ERR_ARG in status and its strip is skipped.  visit_winners (may be
+ * NULL) likewise; a code past its intersect's records sets CS_ERR_ARG.
  * Replaces rasterize_cubic_fill_backward_kernel, cubic_splatting.py:1197-1651. */
 CS_API int cs_fill_backward(const int32_t *prim_ids_sorted, const int32_t *tile_bins,
                      const int32_t *tile_dlist, const void *imeta, const int32_t *isect_strips,
                      const int32_t *rowoff, const void *dlist, const int32_t *unit_order,
-                     const int32_t *visit_lists, const float *background,
-                     const float *final_Ts, const int32_t *final_idx,
+                     const int32_t *visit_lists, const uint16_t *visit_winners,
+                     const float *background, const float *final_Ts, const int32_t *final_idx,
                      const float *v_output, const float *out_img, const float *target_chw,
                      const float *mse_scale, float *v_edges, float *v_colors,
                      float *v_opacities, float *v_inv_sigma2s, float *curve_contrib_rgb,
@@ -284,8 +291,8 @@ CS_API int cs_fill_backward(const int32_t *prim_ids_sorted, const int32_t *tile_
 CS_API int cs_stroke_forward(const int32_t *prim_ids_sorted, const int32_t *tile_bins,
                       const int32_t *tile_dlist, const void *imeta, const int32_t *isect_strips,
                       const void *dlist, const int32_t *unit_order, int32_t *unit_order_bwd,
-                      int32_t *visit_lists, const float *background, float *out_img,
-                      float *final_Ts,
+                      int32_t *visit_lists, uint16_t *visit_winners, const float *background,
+                      float *out_img, float *final_Ts,
                       int32_t *final_idx, float *out_chw_clamped, const float *target_chw,
                       float *loss_out,
                       int32_t *status, void *workspace, int32_t img_height, int32_t img_width,
@@ -297,8 +304,9 @@ CS_API int cs_stroke_forward(const int32_t *prim_ids_sorted, const int32_t *tile
 CS_API int cs_stroke_backward(const int32_t *prim_ids_sorted, const int32_t *tile_bins,
                        const int32_t *tile_dlist, const void *imeta, const int32_t *isect_strips,
                        const void *dlist, const int32_t *unit_order,
-                       const int32_t *visit_lists, const float *background,
-                       const float *final_Ts, const int32_t *final_idx, const float *v_output,
+                       const int32_t *visit_lists, const uint16_t *visit_winners,
+                       const float *background, const float *final_Ts, const int32_t *final_idx,
+                       const float *v_output,
                        const float *out_img, const float *target_chw, const float *mse_scale,
                        float *v_edges, float *v_colors, float *v_opacities,
                        float *v_stroke_widths, float *v_inv_sigma2s, float *curve_contrib_rgb,

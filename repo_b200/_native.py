@@ -59,10 +59,11 @@ SIGNATURES = {
     "cs_aa_widths_forward": (ctypes.c_int, [_P, _P, _P, _I64, _P]),
     "cs_aa_widths_backward": (ctypes.c_int, [_P, _P, _P, _P, _I64, _P]),
     "cs_visit_lists_size": (_SZ, [_I64, _I64]),
-    "cs_fill_forward": (ctypes.c_int, [_P] * 19 + [_I32, _I32, _I32, _I32, _P]),
-    "cs_fill_backward": (ctypes.c_int, [_P] * 24 + [_I32, _I32, _I32, _I32, _P]),
-    "cs_stroke_forward": (ctypes.c_int, [_P] * 18 + [_I32, _I32, _I32, _I32, _P]),
-    "cs_stroke_backward": (ctypes.c_int, [_P] * 24 + [_I32, _I32, _I32, _I32, _P]),
+    "cs_visit_winners_size": (_SZ, [_I64, _I64]),
+    "cs_fill_forward": (ctypes.c_int, [_P] * 20 + [_I32, _I32, _I32, _I32, _P]),
+    "cs_fill_backward": (ctypes.c_int, [_P] * 25 + [_I32, _I32, _I32, _I32, _P]),
+    "cs_stroke_forward": (ctypes.c_int, [_P] * 19 + [_I32, _I32, _I32, _I32, _P]),
+    "cs_stroke_backward": (ctypes.c_int, [_P] * 25 + [_I32, _I32, _I32, _I32, _P]),
     "cs_edge_grads_to_cubics": (ctypes.c_int, [_P, _P, _I64, _I32, _F32, _F32, _P]),
     "cs_ring_to_cubics": (ctypes.c_int, [_P, _P, _I64, _I32, _I32, _I32, _P]),
     "cs_edge_grads_to_ring": (ctypes.c_int, [_P, _P, _I64, _I32, _I32, _I32, _I32, _I32, _P,

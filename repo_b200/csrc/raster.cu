@@ -58,6 +58,8 @@ struct RasterArgs {
   int* order_next;       // forward: optional unit lists for the backward, by measured work
   int* visits;           // optional per-strip lists of the intersects that composited a pixel
                          // of the strip: the forward writes them, the backward walks them
+  unsigned short* winners;  // optional, beside the visit lists: per listed visit and lane, the
+                            // two pixels' closest-record codes (see winner_code)
   const float* bg;
   int H, W, tbx, r0, nunits;
   int vec2;              // W even and per-pixel buffers 8-byte aligned: a lane's two
@@ -400,19 +402,41 @@ struct FwdPix {
   float T, a0, a1, a2, md;
   int cur, w, n;
   bool done;
+  int win;  // closest record of the current intersect, relative to its first
 };
 
+// A pixel's code for the backward: bits 0-6 the closest record of the
+// intersect relative to its first (127: none or not representable), bit 7
+// the pixel's inside/outside state (fills).
+constexpr int kNoWinner = 127;
+__device__ __forceinline__ unsigned winner_code(int win, bool inside) {
+  return (unsigned)(win < kNoWinner ? win : kNoWinner) | (inside ? 128u : 0u);
+}
+
 template <bool STROKE>
-__device__ __forceinline__ void fwd_entries(const DEntry* __restrict__ buf, int c0, int lo, int hi,
-                                            float px0, float px1, float py, FwdPix& p0,
+__device__ __forceinline__ void fwd_entries(const DEntry* __restrict__ buf, int c0, int ds, int lo,
+                                            int hi, float px0, float px1, float py, FwdPix& p0,
                                             FwdPix& p1) {
   for (int d = lo; d < hi; ++d) {
     const float4 EA = buf[d - c0].a;
     const float4 EB = buf[d - c0].b;
     const float wy = py - EA.y;
     float pr, cx, cy;
-    p0.md = fminf(p0.md, seg_d2(px0, py, wy, EA, EB, pr, cx, cy));
-    p1.md = fminf(p1.md, seg_d2(px1, py, wy, EA, EB, pr, cx, cy));
+    if (!STROKE) {  // the running minimum and its first record (strict <: the first minimum)
+      const float d20 = seg_d2(px0, py, wy, EA, EB, pr, cx, cy);
+      const float d21 = seg_d2(px1, py, wy, EA, EB, pr, cx, cy);
+      if (d20 < p0.md) {
+        p0.md = d20;
+        p0.win = d - ds;
+      }
+      if (d21 < p1.md) {
+        p1.md = d21;
+        p1.win = d - ds;
+      }
+    } else {
+      p0.md = fminf(p0.md, seg_d2(px0, py, wy, EA, EB, pr, cx, cy));
+      p1.md = fminf(p1.md, seg_d2(px1, py, wy, EA, EB, pr, cx, cy));
+    }
     if (!STROKE) {
       if (((EA.y <= py) & (EB.y > py)) | ((EA.y > py) & (EB.y <= py))) {
         const float lhs = EB.z + wy * EA.z;
@@ -472,8 +496,8 @@ __device__ __forceinline__ bool forward_unit(const RasterArgs& A, int unit,
   const bool in0 = i < A.H && j0 < A.W, in1 = i < A.H && j0 + 1 < A.W;
   const float py = (float)i + 0.5f;
   const float px0 = (float)j0 + 0.5f, px1 = (float)(j0 + 1) + 0.5f;
-  FwdPix p0{1.0f, 0.f, 0.f, 0.f, 1e30f, 0, 0, 0, !in0};
-  FwdPix p1{1.0f, 0.f, 0.f, 0.f, 1e30f, 0, 0, 0, !in1};
+  FwdPix p0{1.0f, 0.f, 0.f, 0.f, 1e30f, 0, 0, 0, !in0, kNoWinner};
+  FwdPix p1{1.0f, 0.f, 0.f, 0.f, 1e30f, 0, 0, 0, !in1, kNoWinner};
   if (nd > 0 && lane == 0)
     bulk_load(buf[0], A.dl + g.base, (uint32_t)min(nd, kWChunk) * sizeof(DEntry), &bars[0]);
   int k = rs;          // next intersect
@@ -522,9 +546,10 @@ __device__ __forceinline__ bool forward_unit(const RasterArgs& A, int unit,
       const int ds = rg.x, de = rg.x + rg.y;
       if (!mid) {
         p0.md = p1.md = 1e30f;
+        p0.win = p1.win = kNoWinner;
         p0.w = p0.n = p1.w = p1.n = 0;
       }
-      fwd_entries<STROKE>(cb, c0, max(ds, c0), min(de, c1), px0, px1, py, p0, p1);
+      fwd_entries<STROKE>(cb, c0, ds, max(ds, c0), min(de, c1), px0, px1, py, p0, p1);
       recs += max(0, min(de, c1) - max(ds, c0));
       if (de > c1) {
         mid = true;
@@ -539,6 +564,12 @@ __device__ __forceinline__ bool forward_unit(const RasterArgs& A, int unit,
       const bool c1 = fwd_composite<STROKE>(p1, m, k);
       if (__any_sync(0xffffffffu, c0 || c1)) {
         if (vl && lane == 0) vl[1 + contrib] = k;
+        if (!STROKE && vl && A.winners) {  // this visit's closest records, for the backward
+          const bool i0 = m.rule == 0 ? (p0.n & 1) != 0 : p0.w != 0;
+          const bool i1 = m.rule == 0 ? (p1.n & 1) != 0 : p1.w != 0;
+          A.winners[(visit_base(g) + 1 + contrib) * 32 + lane] =
+              (unsigned short)(winner_code(p0.win, i0) | (winner_code(p1.win, i1) << 8));
+        }
         ++contrib;
       }
       ++visits;
@@ -952,6 +983,7 @@ __device__ __forceinline__ bool backward_unit(const RasterArgs& A, int unit,
   // T or gets a gradient: a pixel composites k exactly when alpha_k >=
   // alpha_min and k <= final_idx).
   const int* vl = nullptr;
+  long long wslot = 0;  // visit-list slot of position 0 (for the winner codes)
   int nq = kmax - rs + 1;
   if (A.visits) {
     vl = A.visits + visit_base(g);
@@ -962,6 +994,7 @@ __device__ __forceinline__ bool backward_unit(const RasterArgs& A, int unit,
     }
     ++vl;
     nq = cnt;
+    wslot = visit_base(g) + 1;
     if (nq == 0) return true;
     const int klast = vl[nq - 1];
     if (klast >= rs && klast < kmax) kmax = klast;  // fewer record chunks to bring in
@@ -1024,27 +1057,66 @@ __device__ __forceinline__ bool backward_unit(const RasterArgs& A, int unit,
         }
       }
       if (de > ds && de <= c0) break;  // its records lie in a lower chunk
-      if (mid)
-        bwd_entries<STROKE, true>(cb, c0, max(ds, c0), min(de, c1), px, py, s);
-      else
-        bwd_entries<STROKE, false>(cb, c0, max(ds, c0), min(de, c1), px, py, s);
-      // the winner so far, while its record is resident; bl = -2 marks a
-      // winner from a chunk that is no longer resident (bp, bcx, bcy, be hold it)
+      // The forward's closest record and inside state of each pixel of this
+      // visit (winner codes): only the winner record is evaluated.  Any
+      // pixel that needs the walk (no representable code) sends the warp down
+      // the record walk below.
+      bool fast = false;
+      unsigned wc = 0u;
+      if (!STROKE && A.winners && vl && !mid) {
+        wc = __ldg(A.winners + (wslot + q) * 32 + lane);
+        const bool need0 = v0 && de > ds && (wc & 127u) == kNoWinner;
+        const bool need1 = v1 && de > ds && ((wc >> 8) & 127u) == kNoWinner;
+        fast = !__any_sync(0xffffffffu, need0 || need1);
+      }
+      if (fast) {
 #pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        if (s[u].bl >= 0) {
-          best_point(cb, c0, px[u], py, s[u]);
-          if (ds < c0) s[u].bl = -2;
+        for (int u = 0; u < 2; ++u) {
+          const unsigned c = (wc >> (8 * u)) & 255u;
+          const int win = (int)(c & 127u);
+          s[u].w = s[u].n = (int)(c >> 7);
+          if (win == kNoWinner || de <= ds) continue;
+          if (win >= de - ds) {  // not a code the forward wrote for this intersect
+            if (A.status) atomicExch(A.status, CS_ERR_ARG);
+            continue;
+          }
+          const int d = ds + win;
+          const bool res = d >= c0 && d < c1;  // record in the resident chunk
+          float4 EA, EB;
+          if (res) {
+            EA = cb[d - c0].a;
+            EB = cb[d - c0].b;
+          } else {
+            EA = __ldg(&A.dl[g.base + d].a);
+            EB = __ldg(&A.dl[g.base + d].b);
+          }
+          s[u].md = seg_d2(px[u], py, py - EA.y, EA, EB, s[u].bp, s[u].bcx, s[u].bcy);
+          s[u].be = __float_as_int(EB.w);
+          s[u].bl = res ? d : -2;
         }
-      }
-      if (ds < c0) {
-        mid = true;
-        break;
-      }
-      if (!STROKE) {
-        const int ro = batch_rowoff(ib, j);
-        const int rw = row_wind(ro), rc = row_cnt(ro);
-        s[0].w += rw; s[1].w += rw; s[0].n += rc; s[1].n += rc;
+      } else {
+        if (mid)
+          bwd_entries<STROKE, true>(cb, c0, max(ds, c0), min(de, c1), px, py, s);
+        else
+          bwd_entries<STROKE, false>(cb, c0, max(ds, c0), min(de, c1), px, py, s);
+        // the winner so far, while its record is resident; bl = -2 marks a
+        // winner from a chunk that is no longer resident (bp, bcx, bcy, be hold it)
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          if (s[u].bl >= 0) {
+            best_point(cb, c0, px[u], py, s[u]);
+            if (ds < c0) s[u].bl = -2;
+          }
+        }
+        if (ds < c0) {
+          mid = true;
+          break;
+        }
+        if (!STROKE) {
+          const int ro = batch_rowoff(ib, j);
+          const int rw = row_wind(ro), rc = row_cnt(ro);
+          s[0].w += rw; s[1].w += rw; s[0].n += rc; s[1].n += rc;
+        }
       }
       float acc[kAcc];
 #pragma unroll
@@ -1215,6 +1287,10 @@ using namespace cs;
 
 extern "C" {
 
+size_t cs_visit_winners_size(int64_t isect_capacity, int64_t num_tiles) {
+  return 16 * cs_visit_lists_size(isect_capacity, num_tiles);  // 32 x 2 bytes per list slot
+}
+
 size_t cs_visit_lists_size(int64_t isect_capacity, int64_t num_tiles) {
   const int64_t n = (isect_capacity > 0 ? isect_capacity : 0) + (num_tiles > 0 ? num_tiles : 1);
   return sizeof(int32_t) * (size_t)kStrips * (size_t)n;
@@ -1228,8 +1304,8 @@ static int raster_forward(bool stroke, const int32_t* prim_ids_sorted, const int
                           const int32_t* tile_dlist, const void* imeta,
                           const int32_t* isect_strips, const int32_t* rowoff, const void* dlist,
                           const int32_t* unit_order, int32_t* unit_order_bwd,
-                          int32_t* visit_lists, const float* background, float* out_img,
-                          float* final_Ts,
+                          int32_t* visit_lists, uint16_t* visit_winners,
+                          const float* background, float* out_img, float* final_Ts,
                           int32_t* final_idx, float* out_chw_clamped, const float* target_chw,
                           float* loss_out, int32_t* status, void* workspace, int32_t img_height,
                           int32_t img_width, int32_t tile_row_begin, int32_t tile_row_end,
@@ -1243,6 +1319,7 @@ static int raster_forward(bool stroke, const int32_t* prim_ids_sorted, const int
              unit_order, background, status, workspace);
   a.order_next = unit_order_bwd;
   a.visits = visit_lists;
+  a.winners = visit_lists ? visit_winners : nullptr;
   if (unit_order_bwd)
     cudaMemsetAsync(unit_order_bwd, 0, sizeof(int32_t) * kUnitBuckets, (cudaStream_t)stream);
   a.out = out_img;
@@ -1258,15 +1335,15 @@ static int raster_forward(bool stroke, const int32_t* prim_ids_sorted, const int
 int cs_fill_forward(const int32_t* prim_ids_sorted, const int32_t* tile_bins,
                     const int32_t* tile_dlist, const void* imeta, const int32_t* isect_strips,
                     const int32_t* rowoff, const void* dlist, const int32_t* unit_order,
-                    int32_t* unit_order_bwd, int32_t* visit_lists, const float* background,
-                    float* out_img, float* final_Ts,
+                    int32_t* unit_order_bwd, int32_t* visit_lists, uint16_t* visit_winners,
+                    const float* background, float* out_img, float* final_Ts,
                     int32_t* final_idx, float* out_chw_clamped, const float* target_chw,
                     float* loss_out, int32_t* status, void* workspace, int32_t img_height,
                     int32_t img_width, int32_t tile_row_begin, int32_t tile_row_end,
                     void* stream) {
   return raster_forward(false, prim_ids_sorted, tile_bins, tile_dlist, imeta, isect_strips,
-                        rowoff, dlist, unit_order, unit_order_bwd, visit_lists, background, out_img,
-                        final_Ts, final_idx,
+                        rowoff, dlist, unit_order, unit_order_bwd, visit_lists, visit_winners,
+                        background, out_img, final_Ts, final_idx,
                         out_chw_clamped, target_chw, loss_out, status, workspace, img_height,
                         img_width, tile_row_begin, tile_row_end, stream);
 }
@@ -1274,14 +1351,14 @@ int cs_fill_forward(const int32_t* prim_ids_sorted, const int32_t* tile_bins,
 int cs_stroke_forward(const int32_t* prim_ids_sorted, const int32_t* tile_bins,
                       const int32_t* tile_dlist, const void* imeta, const int32_t* isect_strips,
                       const void* dlist, const int32_t* unit_order, int32_t* unit_order_bwd,
-                      int32_t* visit_lists, const float* background, float* out_img,
-                      float* final_Ts, int32_t* final_idx,
+                      int32_t* visit_lists, uint16_t* visit_winners, const float* background,
+                      float* out_img, float* final_Ts, int32_t* final_idx,
                       float* out_chw_clamped, const float* target_chw, float* loss_out,
                       int32_t* status, void* workspace, int32_t img_height, int32_t img_width,
                       int32_t tile_row_begin, int32_t tile_row_end, void* stream) {
   return raster_forward(true, prim_ids_sorted, tile_bins, tile_dlist, imeta, isect_strips,
-                        nullptr, dlist, unit_order, unit_order_bwd, visit_lists, background, out_img,
-                        final_Ts, final_idx,
+                        nullptr, dlist, unit_order, unit_order_bwd, visit_lists, visit_winners,
+                        background, out_img, final_Ts, final_idx,
                         out_chw_clamped, target_chw, loss_out, status, workspace, img_height,
                         img_width, tile_row_begin, tile_row_end, stream);
 }
@@ -1290,7 +1367,8 @@ static int raster_backward(bool stroke, const int32_t* prim_ids_sorted, const in
                            const int32_t* tile_dlist, const void* imeta,
                            const int32_t* isect_strips, const int32_t* rowoff, const void* dlist,
                            const int32_t* unit_order, const int32_t* visit_lists,
-                           const float* background, const float* final_Ts,
+                           const uint16_t* visit_winners, const float* background,
+                           const float* final_Ts,
                            const int32_t* final_idx,
                            const float* v_output, const float* out_img, const float* target_chw,
                            const float* mse_scale, float* v_edges, float* v_colors,
@@ -1308,6 +1386,7 @@ static int raster_backward(bool stroke, const int32_t* prim_ids_sorted, const in
   stage_args(a, prim_ids_sorted, tile_bins, tile_dlist, imeta, isect_strips, rowoff, dlist,
              unit_order, background, status, workspace);
   a.visits = const_cast<int32_t*>(visit_lists);  // read only by the backward
+  a.winners = visit_lists ? const_cast<uint16_t*>(visit_winners) : nullptr;
   a.fts_in = final_Ts;
   a.fidx_in = final_idx;
   a.v_out = v_output;
@@ -1328,7 +1407,8 @@ static int raster_backward(bool stroke, const int32_t* prim_ids_sorted, const in
 int cs_fill_backward(const int32_t* prim_ids_sorted, const int32_t* tile_bins,
                      const int32_t* tile_dlist, const void* imeta, const int32_t* isect_strips,
                      const int32_t* rowoff, const void* dlist, const int32_t* unit_order,
-                     const int32_t* visit_lists, const float* background, const float* final_Ts, const int32_t* final_idx,
+                     const int32_t* visit_lists, const uint16_t* visit_winners,
+                     const float* background, const float* final_Ts, const int32_t* final_idx,
                      const float* v_output, const float* out_img, const float* target_chw,
                      const float* mse_scale, float* v_edges, float* v_colors,
                      float* v_opacities, float* v_inv_sigma2s, float* curve_contrib_rgb,
@@ -1336,7 +1416,8 @@ int cs_fill_backward(const int32_t* prim_ids_sorted, const int32_t* tile_bins,
                      int32_t img_height, int32_t img_width, int32_t tile_row_begin,
                      int32_t tile_row_end, void* stream) {
   return raster_backward(false, prim_ids_sorted, tile_bins, tile_dlist, imeta, isect_strips,
-                         rowoff, dlist, unit_order, visit_lists, background, final_Ts, final_idx,
+                         rowoff, dlist, unit_order, visit_lists, visit_winners, background, final_Ts,
+                         final_idx,
                          v_output,
                          out_img, target_chw, mse_scale, v_edges, v_colors, v_opacities, nullptr,
                          v_inv_sigma2s, curve_contrib_rgb, curve_isect_contrib, status,
@@ -1346,7 +1427,9 @@ int cs_fill_backward(const int32_t* prim_ids_sorted, const int32_t* tile_bins,
 int cs_stroke_backward(const int32_t* prim_ids_sorted, const int32_t* tile_bins,
                        const int32_t* tile_dlist, const void* imeta, const int32_t* isect_strips,
                        const void* dlist, const int32_t* unit_order,
-                       const int32_t* visit_lists, const float* background, const float* final_Ts, const int32_t* final_idx, const float* v_output,
+                       const int32_t* visit_lists, const uint16_t* visit_winners,
+                       const float* background, const float* final_Ts, const int32_t* final_idx,
+                       const float* v_output,
                        const float* out_img, const float* target_chw, const float* mse_scale,
                        float* v_edges, float* v_colors, float* v_opacities,
                        float* v_stroke_widths, float* v_inv_sigma2s, float* curve_contrib_rgb,
@@ -1354,7 +1437,8 @@ int cs_stroke_backward(const int32_t* prim_ids_sorted, const int32_t* tile_bins,
                        int32_t img_height, int32_t img_width, int32_t tile_row_begin,
                        int32_t tile_row_end, void* stream) {
   return raster_backward(true, prim_ids_sorted, tile_bins, tile_dlist, imeta, isect_strips,
-                         nullptr, dlist, unit_order, visit_lists, background, final_Ts, final_idx,
+                         nullptr, dlist, unit_order, visit_lists, visit_winners, background, final_Ts,
+                         final_idx,
                          v_output,
                          out_img, target_chw, mse_scale, v_edges, v_colors, v_opacities,
                          v_stroke_widths, v_inv_sigma2s, curve_contrib_rgb, curve_isect_contrib,

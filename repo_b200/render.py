@@ -130,6 +130,7 @@ class Binning:
     unit_order: Optional[torch.Tensor] = None   # strip dispatch lists (staged work)
     unit_order_bwd: Optional[torch.Tensor] = None  # strip dispatch lists (forward's work)
     visit_lists: Optional[torch.Tensor] = None  # per strip: intersects that composited a pixel
+    visit_winners: Optional[torch.Tensor] = None  # per listed visit and lane: closest-record codes
     flatten_method: str = CUBIC_FLATTEN_METHOD_BERNSTEIN
     segment_edge_offsets: Optional[torch.Tensor] = None  # de Casteljau CSR [G + 1]
     edge_t_starts: Optional[torch.Tensor] = None         # de Casteljau leaf intervals [E]
@@ -400,14 +401,18 @@ def forward_raster(b: Binning, background, img_h: int, img_w: int, out_chw=None,
     if b.unit_order is not None and b.unit_order_bwd is None:
         b.unit_order_bwd = torch.empty_like(b.unit_order)
     if b.visit_lists is None:
-        nbytes = int(nat.call("cs_visit_lists_size", int(b.num_intersects),
-                              b.tile_bounds[0] * b.tile_bounds[1]))
+        nt = b.tile_bounds[0] * b.tile_bounds[1]
+        nbytes = int(nat.call("cs_visit_lists_size", int(b.num_intersects), nt))
         b.visit_lists = torch.empty((nbytes // 4,), dtype=torch.int32, device=dev)
+        if not b.stroke:  # closest-record codes: fills only
+            wbytes = int(nat.call("cs_visit_winners_size", int(b.num_intersects), nt))
+            b.visit_winners = torch.empty((wbytes // 2,), dtype=torch.int16, device=dev)
     if not b.stroke:
         nat.check(nat.call("cs_fill_forward", nat.ptr(b.prim_ids_sorted), nat.ptr(b.tile_bins),
                            nat.ptr(b.tile_dlist), nat.ptr(b.imeta), nat.ptr(b.isect_strips),
                            nat.ptr(b.rowoff), nat.ptr(b.dlist), nat.ptr(b.unit_order),
-                           nat.ptr(b.unit_order_bwd), nat.ptr(b.visit_lists), nat.ptr(background),
+                           nat.ptr(b.unit_order_bwd), nat.ptr(b.visit_lists),
+                           nat.ptr(b.visit_winners), nat.ptr(background),
                            nat.ptr(out), nat.ptr(fts), nat.ptr(fidx),
                            nat.ptr(out_chw), None, None, nat.ptr(status), ws.data_ptr(),
                            img_h, img_w, b.tile_rows[0], b.tile_rows[1], st), "cs_fill_forward")
@@ -415,8 +420,8 @@ def forward_raster(b: Binning, background, img_h: int, img_w: int, out_chw=None,
         nat.check(nat.call("cs_stroke_forward", nat.ptr(b.prim_ids_sorted), nat.ptr(b.tile_bins),
                            nat.ptr(b.tile_dlist), nat.ptr(b.imeta), nat.ptr(b.isect_strips),
                            nat.ptr(b.dlist), nat.ptr(b.unit_order), nat.ptr(b.unit_order_bwd),
-                           nat.ptr(b.visit_lists), nat.ptr(background), nat.ptr(out),
-                           nat.ptr(fts), nat.ptr(fidx),
+                           nat.ptr(b.visit_lists), nat.ptr(b.visit_winners),
+                           nat.ptr(background), nat.ptr(out), nat.ptr(fts), nat.ptr(fidx),
                            nat.ptr(out_chw), None,
                            None, nat.ptr(status), ws.data_ptr(), img_h, img_w,
                            b.tile_rows[0], b.tile_rows[1], st), "cs_stroke_forward")
@@ -462,7 +467,7 @@ def raster_backward(b: Binning, num_primitives: int, background, final_ts, final
                                nat.ptr(b.tile_dlist), nat.ptr(b.imeta),
                                nat.ptr(b.isect_strips), nat.ptr(b.rowoff), nat.ptr(b.dlist),
                                nat.ptr(_bwd_lists(b)), nat.ptr(b.visit_lists),
-                               nat.ptr(background), nat.ptr(final_ts),
+                               nat.ptr(b.visit_winners), nat.ptr(background), nat.ptr(final_ts),
                                nat.ptr(final_idx), nat.ptr(vo), nat.ptr(out_img),
                                nat.ptr(target_chw), nat.ptr(mse_scale), nat.ptr(v_edges),
                                nat.ptr(v_colors), nat.ptr(v_opac), nat.ptr(v_inv),
@@ -474,7 +479,7 @@ def raster_backward(b: Binning, num_primitives: int, background, final_ts, final
                                nat.ptr(b.tile_bins), nat.ptr(b.tile_dlist), nat.ptr(b.imeta),
                                nat.ptr(b.isect_strips), nat.ptr(b.dlist),
                                nat.ptr(_bwd_lists(b)), nat.ptr(b.visit_lists),
-                               nat.ptr(background), nat.ptr(final_ts),
+                               nat.ptr(b.visit_winners), nat.ptr(background), nat.ptr(final_ts),
                                nat.ptr(final_idx), nat.ptr(vo), nat.ptr(out_img),
                                nat.ptr(target_chw), nat.ptr(mse_scale), nat.ptr(v_edges),
                                nat.ptr(v_colors), nat.ptr(v_opac), nat.ptr(v_sw), nat.ptr(v_inv),

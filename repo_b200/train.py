@@ -138,6 +138,9 @@ class FillTrainer:
         self.visits = torch.empty(
             (int(nat.call("cs_visit_lists_size", self.capacity, self.tile_bins.shape[0])) // 4,),
             device=dev, dtype=i32)
+        self.winners = torch.empty(
+            (int(nat.call("cs_visit_winners_size", self.capacity, self.tile_bins.shape[0])) // 2,),
+            device=dev, dtype=torch.int16)
         self.graph: Optional[torch.cuda.CUDAGraph] = None
         # SSIM runs beside the backward at low priority, so that it takes only
         # the SMs the backward leaves free; the step itself is captured on a
@@ -195,7 +198,8 @@ class FillTrainer:
                            self.imeta.data_ptr(), self.istrips.data_ptr(), self.rowoff.data_ptr(),
                            self.dlist.data_ptr(), self.unit_order.data_ptr(),
                            self.unit_order_bwd.data_ptr(), self.visits.data_ptr(),
-                           self.bg.data_ptr(), self.out.data_ptr(), self.fts.data_ptr(),
+                           self.winners.data_ptr(), self.bg.data_ptr(), self.out.data_ptr(),
+                           self.fts.data_ptr(),
                            self.fidx.data_ptr(),
                            self.img_chw.data_ptr(), self.target.data_ptr(), self.loss.data_ptr(),
                            status, self.raster_ws.data_ptr(), self.h, self.w, r0, r1, st),
@@ -215,7 +219,8 @@ class FillTrainer:
                            self.tile_bins.data_ptr(), self.tile_dlist.data_ptr(),
                            self.imeta.data_ptr(), self.istrips.data_ptr(), self.rowoff.data_ptr(),
                            self.dlist.data_ptr(), self.unit_order_bwd.data_ptr(),
-                           self.visits.data_ptr(), self.bg.data_ptr(), self.fts.data_ptr(),
+                           self.visits.data_ptr(), self.winners.data_ptr(), self.bg.data_ptr(),
+                           self.fts.data_ptr(),
                            self.fidx.data_ptr(), None,
                            self.out.data_ptr(),
                            self.target.data_ptr(), self.mse_scale.data_ptr(),

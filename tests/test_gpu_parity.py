@@ -545,6 +545,33 @@ def test_visit_lists_walk_only_composited_intersects(stroke):
             assert_grad_close(_np(a), _np(c), name)
 
 
+def test_fill_winner_codes_fall_back_and_reject_bad_codes():
+    """The forward's closest-record codes (fills): the backward that
+    evaluates only each pixel's stored winner gives the gradients of the one
+    that walks every record; a code past its intersect's records sets
+    CS_ERR_ARG and is ignored (every read stays inside the strip's records)."""
+    import dataclasses
+    from repo_b200 import _native as nat
+    args = fill_inputs(scenes.config1())
+    h, w = args[5], args[6]
+    b, inv, out, fts, fidx = gpu_fill(*args)
+    assert b.visit_winners is not None
+    bg, p = _t(args[7], torch.float32), int(np.asarray(args[2]).shape[0])
+    v_out = _t(np.asarray(scenes.seeded_grad(11, h, w), np.float32))
+    g1 = render.raster_backward(b, p, bg, fts, fidx, v_out, h, w)
+    good = b.visit_winners.clone()
+    g2 = render.raster_backward(dataclasses.replace(b, visit_winners=None), p, bg, fts, fidx,
+                                v_out, h, w)
+    assert int(b.counters[1]) == 0
+    for name, a, c in zip(["v_edges", "v_colors", "v_opac", "v_inv"], g1, g2):
+        assert_grad_close(_np(a), _np(c), name)
+    b.visit_winners.fill_(0x7E7E)  # record 126 of intersects with fewer records
+    render.raster_backward(b, p, bg, fts, fidx, v_out, h, w)
+    assert int(b.counters[1]) == nat.CS_ERR_ARG
+    b.counters[1] = 0
+    b.visit_winners.copy_(good)
+
+
 def test_visit_lists_that_do_not_fit_the_bins_set_an_error():
     """A visit list not written by this frame's forward (counts past the
     tile's intersects, ids outside it) is rejected strip by strip with

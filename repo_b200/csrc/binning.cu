@@ -453,7 +453,9 @@ __device__ __forceinline__ void prep_primitive(
 // flatten all segments into edges (unless peo gives pre-flattened edges with
 // their CSR offsets), and add the primitive to the intersect and edge-slot
 // counts of its tiles within the band of tile rows [r0, r1).
-__global__ void __launch_bounds__(256) bin_prep_kernel(
+constexpr int kPrepThreads = 512;  // one warp per primitive; the last CTA to finish scans the tiles
+
+__global__ void __launch_bounds__(kPrepThreads) bin_prep_kernel(
     const float* __restrict__ cn, const float* __restrict__ ring, int ring_g,
     const int* __restrict__ offs, const int* __restrict__ peo, int* __restrict__ peo_out,
     const float* __restrict__ aa,
@@ -991,7 +993,7 @@ int cs_bin_count(const float* cubics_norm, const int32_t* prim_seg_offsets, cons
   BinWorkspace ws = bin_ws(workspace, nt);
   // one launch: a warp per primitive, then the last CTA scans the tile counts
   // (at least one CTA, so that an empty scene still gets empty tile ranges)
-  bin_prep_kernel<<<max(1, ceil_div(num_primitives * 32, 256)), 256, 0, st>>>(
+  bin_prep_kernel<<<max(1, ceil_div(num_primitives * 32, kPrepThreads)), kPrepThreads, 0, st>>>(
       cubics_norm, ring, ring_segs_per_path, prim_seg_offsets, prim_edge_offsets,
       prim_edge_offsets ? nullptr : prim_edge_offsets_out, aa_widths, stroke_widths, basis,
       cubics_px, edges_px, prim_tile_ranges, num_tiles_hit, ws, tile_bins, tile_dlist, counters,

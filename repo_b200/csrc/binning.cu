@@ -520,9 +520,7 @@ __device__ __forceinline__ void emit_sorted(unsigned long long v, long long tile
 }
 
 // Sort one tile's pairs ascending (CTA of kSortThreads); pairs are unique.
-// A tile of at most 32 pairs is sorted in warp 0's registers, and thread
-// t < n gets back pair t (everything else gets ~0).
-__device__ unsigned long long sort_tile(unsigned long long* __restrict__ pairs, int start, int n, long long tile,
+__device__ void sort_tile(unsigned long long* __restrict__ pairs, int start, int n, long long tile,
                           const float* __restrict__ depths, int* __restrict__ pids,
                           long long* __restrict__ ids, unsigned long long* s) {
   const int tid = threadIdx.x, lane = tid & 31;
@@ -540,9 +538,8 @@ __device__ unsigned long long sort_tile(unsigned long long* __restrict__ pairs, 
         }
       }
       if (lane < n) emit_sorted(v, tile, start + lane, pids, ids);
-      return v;
     }
-    return ~0ull;
+    return;
   }
   if (n <= kSortSmem) {
     int m = 64;
@@ -563,7 +560,7 @@ __device__ unsigned long long sort_tile(unsigned long long* __restrict__ pairs, 
       }
     }
     for (int i = tid; i < n; i += kSortThreads) emit_sorted(s[i], tile, start + i, pids, ids);
-    return ~0ull;
+    return;
   }
   // Large tile: rank each pair by counting smaller pairs, then rebuild keys.
   for (int i = tid; i < n; i += kSortThreads) {
@@ -580,7 +577,6 @@ __device__ unsigned long long sort_tile(unsigned long long* __restrict__ pairs, 
                                    (unsigned long long)depth_sort_key(depths[p]));
     }
   }
-  return ~0ull;
 }
 
 struct StageIO {
@@ -619,13 +615,9 @@ struct StageShared {
   float dthr[kSortThreads];      // culling distance of each intersect
   int dstart[kStrips][kSortThreads + 1];  // first record per strip; [m] = chunk end
   unsigned bal[kStrips][kStageU][kSortThreads / 32];  // near ballots of the round
+  int pre[kStrips][kStageU][kSortThreads / 32];       // their exclusive prefix counts
   int wsum[kSortThreads / 32];
-  // chunks of at most 32 intersects: the intersects that own slots, in order
-  int nel[32];    // chunk index
-  int nes[32];    // first slot
-  int neb[32];    // first edge
-  float ndthr[32];
-  int nnz;
+  int total[kStrips];
 };
 
 // Classify the edges of intersects [rs, re) of one tile and write its staged
@@ -639,21 +631,13 @@ struct StageShared {
 // count at its first slot.  Strip st's list starts at dbase + st * stride.
 // Far edges right of the tile add to the intersect's per-row winding
 // accumulators in shared memory (`rows`, kSortThreads x 32 ints: 16 winding
-// and 16 count differences between consecutive rows, summed when written).
-// A chunk of at most 32 intersects (nearly every fill tile) is set up by warp
-// 0 alone, and a slot finds its intersect from the slot starts of the
-// intersects that own slots (a ballot and a bit mask) instead of a search.
-// With `hint`, the tile has at most 32 intersects and thread t < re - rs holds
-// the primitive id of intersect rs + t in pid_hint.  Returns the strips'
-// record totals (in every thread).
+// sums, 16 counts).  Returns the strips' record totals (in every thread).
 template <bool STROKE>
 __device__ void stage_tile(const StageIO& io, long long tile, int rs, int re, int dbase,
-                           int stride, StageShared& sh, int (*rows)[32], int totals[kStrips],
-                           bool hint, int pid_hint) {
+                           int stride, StageShared& sh, int (*rows)[32], int totals[kStrips]) {
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   constexpr int nw = kSortThreads / 32;
   constexpr int kRound = kSortThreads * kStageU;
-  static_assert(kStageU * nw <= 32, "a round's (u, warp) counts are scanned by one warp");
   const float bx0 = (float)((tile % io.tbx) * kTile) + 0.5f;
   const float by0 = (float)((tile / io.tbx) * kTile) + 0.5f;
   const unsigned lt = (1u << lane) - 1u;
@@ -662,87 +646,45 @@ __device__ void stage_tile(const StageIO& io, long long tile, int rs, int re, in
   for (int st = 0; st < kStrips; ++st) near_base[st] = 0;
   for (int c0 = rs; c0 < re; c0 += kSortThreads) {
     const int m = min(kSortThreads, re - c0);
-    const bool small = m <= 32;
     // per intersect: attributes, edge range, slot count
     IMeta im;
-    int ne = 0, eb = 0;
+    int ne = 0;
     if (tid < m) {
       const int k = c0 + tid;
-      const int pid = hint ? pid_hint : io.pids[k];
-      int ee;
+      const int pid = io.pids[k];
+      int eb, ee;
       isect_edges(io, k, pid, eb, ee);
       intersect_attrs<STROKE>(pid, io.colors, io.opac, io.inv_s2, io.rules, io.sw, im);
       ne = max(0, ee - eb);
-      if (!small) {
-        sh.eb[tid] = eb;
-        sh.dthr[tid] = im.dthr;
-      }
-    }
-    if (!STROKE)
-      for (int q = tid; q < m * 32; q += kSortThreads) (&rows[0][0])[q] = 0;
-    int total;
-    if (small) {
-      if (wid == 0) {
-        const int incl = warp_incl_scan(ne, lane);
-        const unsigned owners = __ballot_sync(0xffffffffu, ne > 0);
-        if (ne > 0) {
-          const int q = __popc(owners & lt);
-          sh.nel[q] = lane;
-          sh.nes[q] = incl - ne;
-          sh.neb[q] = eb;
-          sh.ndthr[q] = im.dthr;
-        }
-        if (lane < m) sh.sstart[lane] = incl - ne;
-        if (lane == 31) {
-          sh.sstart[m] = incl;
-          sh.nnz = __popc(owners);
-        }
-      }
-      __syncthreads();
-      total = sh.sstart[m];
-    } else {
-      const int incl = warp_incl_scan(ne, lane);
-      if (lane == 31) sh.wsum[wid] = incl;
-      __syncthreads();
-      int wbase = 0;
-      total = 0;
+      sh.eb[tid] = eb;
+      sh.dthr[tid] = im.dthr;
+      if (!STROKE) {
 #pragma unroll
-      for (int w2 = 0; w2 < nw; ++w2) {
-        const int v = sh.wsum[w2];
-        wbase += w2 < wid ? v : 0;
-        total += v;
+        for (int r = 0; r < 32; ++r) rows[tid][r] = 0;
       }
-      if (tid < m) sh.sstart[tid] = wbase + incl - ne;
-      if (tid == 0) sh.sstart[m] = total;
-      __syncthreads();
     }
-    // slot starts of the owning intersects, one per lane (small chunks)
-    const int own_start = small && lane < sh.nnz ? sh.nes[lane] : INT_MAX;
+    const int incl = warp_incl_scan(ne, lane);
+    if (lane == 31) sh.wsum[wid] = incl;
+    __syncthreads();
+    int wbase = 0, total = 0;
+#pragma unroll
+    for (int w2 = 0; w2 < nw; ++w2) {
+      const int v = sh.wsum[w2];
+      wbase += w2 < wid ? v : 0;
+      total += v;
+    }
+    if (tid < m) sh.sstart[tid] = wbase + incl - ne;
+    if (tid == 0) sh.sstart[m] = total;
+    __syncthreads();
     for (int rb = 0; rb < total; rb += kRound) {
       int kk[kStageU], ee_[kStageU];
-      float dd[kStageU];
       float4 E[kStageU];
 #pragma unroll
       for (int u = 0; u < kStageU; ++u) {
-        const int j0 = rb + u * kSortThreads + wid * 32, j = j0 + lane;
+        const int j = rb + u * kSortThreads + tid;
         kk[u] = -1;
         ee_[u] = 0;
-        dd[u] = 0.0f;
-        if (small) {
-          if (j0 < total) {
-            // owner of slot j0, then one more for each owner starting in (j0, j]
-            const int base = __popc(__ballot_sync(0xffffffffu, own_start <= j0)) - 1;
-            const unsigned bit =
-                own_start > j0 && own_start <= j0 + 31 ? 1u << (own_start - j0) : 0u;
-            const unsigned starts = __reduce_or_sync(0xffffffffu, bit);
-            const int q = base + __popc(starts & ((2u << lane) - 1u));
-            if (j < total) {
-              kk[u] = sh.nel[q];
-              ee_[u] = sh.neb[q] + (j - sh.nes[q]);
-              dd[u] = sh.ndthr[q];
-            }
-          }
-        } else if (j < total) {
+        if (j < total) {
           int lo = 0, hi = m;  // last intersect whose first slot is <= j
           while (hi - lo > 1) {
             const int mid = (lo + hi) >> 1;
@@ -750,7 +692,6 @@ __device__ void stage_tile(const StageIO& io, long long tile, int rs, int re, in
           }
           kk[u] = lo;
           ee_[u] = sh.eb[lo] + (j - sh.sstart[lo]);
-          dd[u] = sh.dthr[lo];
         }
       }
 #pragma unroll
@@ -759,77 +700,59 @@ __device__ void stage_tile(const StageIO& io, long long tile, int rs, int re, in
       unsigned nm[kStageU], bal[kStrips][kStageU];
 #pragma unroll
       for (int u = 0; u < kStageU; ++u) {
-        nm[u] = kk[u] >= 0 ? edge_near_strips(E[u], dd[u], bx0, by0) : 0u;
+        nm[u] = kk[u] >= 0 ? edge_near_strips(E[u], sh.dthr[kk[u]], bx0, by0) : 0u;
 #pragma unroll
         for (int st = 0; st < kStrips; ++st) {
           bal[st][u] = __ballot_sync(0xffffffffu, (nm[u] >> st) & 1u);
           if (lane == 0) sh.bal[st][u][wid] = bal[st][u];
         }
         if (!STROKE && kk[u] >= 0) {
-          // the crossed rows form at most two runs (a range of rows less the
-          // near strips); each run [a, b) adds to the row differences
           unsigned rr = far_right_rows(E[u], bx0, by0) & ~strip_rows(nm[u]);
           if (rr) {
             const int dir = (E[u].w - E[u].y) > 0.0f ? 1 : -1;
-            int* rw = rows[kk[u]];
             while (rr) {
-              const int a = __ffs(rr) - 1;
-              const int len = __ffs(~(rr >> a)) - 1;
-              rr &= ~(((1u << len) - 1u) << a);
-              atomicAdd(rw + a, dir);
-              atomicAdd(rw + 16 + a, 1);
-              if (a + len < 16) {
-                atomicAdd(rw + a + len, -dir);
-                atomicAdd(rw + 16 + a + len, -1);
-              }
+              const int r = __ffs(rr) - 1;
+              rr &= rr - 1u;
+              atomicAdd(&rows[kk[u]][r], dir);
+              atomicAdd(&rows[kk[u]][16 + r], 1);
             }
           }
         }
       }
       __syncthreads();
-      // every warp scans the round's (u, warp) near counts of each strip
-      int excl[kStrips], tot[kStrips];
-#pragma unroll
-      for (int st = 0; st < kStrips; ++st) {
+      if (wid < kStrips) {  // warp st: exclusive prefix of strip st's (u, warp) counts
+        const int st = wid;
         const int v = lane < kStageU * nw ? __popc(sh.bal[st][lane / nw][lane % nw]) : 0;
         const int x = warp_incl_scan(v, lane);
-        excl[st] = x - v;
-        tot[st] = __shfl_sync(0xffffffffu, x, 31);
+        if (lane < kStageU * nw) sh.pre[st][lane / nw][lane % nw] = x - v;
+        if (lane == 31) sh.total[st] = x;
       }
+      __syncthreads();
 #pragma unroll
       for (int u = 0; u < kStageU; ++u) {
-        int pre[kStrips];
-#pragma unroll
-        for (int st = 0; st < kStrips; ++st)
-          pre[st] = __shfl_sync(0xffffffffu, excl[st], u * nw + wid);
         if (nm[u]) {
           const DEntry rec = make_entry(E[u], ee_[u]);
 #pragma unroll
           for (int st = 0; st < kStrips; ++st) {
             if ((nm[u] >> st) & 1u) {
-              const int pos = near_base[st] + pre[st] + __popc(bal[st][u] & lt);
+              const int pos = near_base[st] + sh.pre[st][u][wid] + __popc(bal[st][u] & lt);
               io.dl[dbase + st * stride + pos] = rec;
             }
           }
         }
       }
-      if (wid * 32 < m) {  // first record per strip of the intersects whose first slot is here
-        int sl = -1;
-        if (tid < m) {
-          const int s0 = sh.sstart[tid];
-          sl = s0 < total ? s0 - rb : -1;
-        }
-        const bool here = sl >= 0 && sl < kRound;
-        const int u = here ? sl / kSortThreads : 0, w2 = here ? (sl % kSortThreads) >> 5 : 0;
-        const unsigned below = (1u << (sl & 31)) - 1u;
+      if (tid < m) {
+        const int sl = sh.sstart[tid] - rb;
+        if (sl >= 0 && sl < kRound && sh.sstart[tid] < total) {
+          const int u = sl / kSortThreads, w2 = (sl % kSortThreads) >> 5, l = sl & 31;
+          const unsigned below = (1u << l) - 1u;
 #pragma unroll
-        for (int st = 0; st < kStrips; ++st) {
-          const int p = __shfl_sync(0xffffffffu, excl[st], u * nw + w2);
-          if (here) sh.dstart[st][tid] = near_base[st] + p + __popc(sh.bal[st][u][w2] & below);
+          for (int st = 0; st < kStrips; ++st)
+            sh.dstart[st][tid] = near_base[st] + sh.pre[st][u][w2] + __popc(sh.bal[st][u][w2] & below);
         }
       }
 #pragma unroll
-      for (int st = 0; st < kStrips; ++st) near_base[st] += tot[st];
+      for (int st = 0; st < kStrips; ++st) near_base[st] += sh.total[st];
       __syncthreads();
     }
     // intersects with no slot left (empty, at the end of the chunk)
@@ -859,21 +782,10 @@ __device__ void stage_tile(const StageIO& io, long long tile, int rs, int re, in
       sr[0] = make_int4(v[0], v[1], v[2], v[3]);
       sr[1] = make_int4(v[4], v[5], v[6], v[7]);
     }
-    if (!STROKE) {  // row offsets: prefix sums of the differences, 16 lanes per intersect
-      for (int q0 = wid * 32; q0 < m * 16; q0 += kSortThreads) {
-        const int q = q0 + lane, t = q >> 4, r = lane & 15;
-        const bool ok = q < m * 16;
-        int w = ok ? rows[t][r] : 0, c = ok ? rows[t][16 + r] : 0;
-#pragma unroll
-        for (int o = 1; o < 16; o <<= 1) {
-          const int w2 = __shfl_up_sync(0xffffffffu, w, o, 16);
-          const int c2 = __shfl_up_sync(0xffffffffu, c, o, 16);
-          if (r >= o) {
-            w += w2;
-            c += c2;
-          }
-        }
-        if (ok) io.rowoff[(long long)(c0 + t) * 16 + r] = pack_row(w, c);
+    if (!STROKE) {
+      for (int q = tid; q < m * 16; q += kSortThreads) {
+        const int t = q >> 4, r = q & 15;
+        io.rowoff[(long long)(c0 + t) * 16 + r] = pack_row(rows[t][r], rows[t][16 + r]);
       }
     }
     __syncthreads();  // shared state is reused by the next chunk
@@ -893,7 +805,7 @@ __device__ __forceinline__ int strip_weight(int records, int intersects) {
 // classify the tile's edges into its strips' records, store the strips' work
 // estimates and (last CTA) order the band's strips heaviest first.
 template <bool STROKE>
-__global__ void __launch_bounds__(kSortThreads, 4) bin_tile_kernel(
+__global__ void __launch_bounds__(kSortThreads) bin_tile_kernel(
     const int* __restrict__ bins, const float* __restrict__ depths,
     unsigned long long* __restrict__ pairs, int* __restrict__ pids, long long* __restrict__ ids,
     const int* __restrict__ counters, long long icap, long long dcap, int r0, StageIO io,
@@ -908,14 +820,14 @@ __global__ void __launch_bounds__(kSortThreads, 4) bin_tile_kernel(
   const int start = bins[2 * tile], end = bins[2 * tile + 1];
   const int n = end - start;
   const bool sorted = n > 0 && counters[0] <= icap;  // on overflow the pairs were not all written
-  const unsigned long long v0 = sorted ? sort_tile(pairs, start, n, tile, depths, pids, ids, s) : ~0ull;
+  if (sorted) sort_tile(pairs, start, n, tile, depths, pids, ids, s);
   if (!io.imeta) return;
   int totals[kStrips] = {0, 0, 0, 0};
   if (sorted && counters[2] <= dcap) {
     __syncthreads();
     const int2 dl = io.dlr[tile];
     stage_tile<STROKE>(io, tile, start, end, dl.x, dl.y, sh, reinterpret_cast<int (*)[32]>(s),
-                       totals, n <= 32, (int)(v0 & 0xffffffffull));
+                       totals);
   }
   if (lists && threadIdx.x < kStrips) {
     int t = 0;
@@ -965,7 +877,7 @@ __global__ void __launch_bounds__(kSortThreads) tile_stage_kernel(const int* __r
   const bool staged = re > rs && counters[2] <= dcap;
   if (staged) {
     const int2 dl = io.dlr[tile];
-    stage_tile<STROKE>(io, tile, rs, re, dl.x, dl.y, sh, s_row, totals, false, 0);
+    stage_tile<STROKE>(io, tile, rs, re, dl.x, dl.y, sh, s_row, totals);
   }
   if (lists && threadIdx.x < kStrips) {
     int t = 0;

@@ -130,25 +130,19 @@ __device__ __forceinline__ unsigned strip_rows(unsigned m) {
   return r;
 }
 
-// Rows r in [0, 16) with by0 + r < v (by0 + r is exact, so the rounded
-// estimate is corrected against the exact comparisons).
-__device__ __forceinline__ int rows_below(float v, float by0) {
-  int r = (int)fminf(fmaxf(ceilf(v - by0), 0.0f), 16.0f);
-  if (r > 0 && by0 + (float)(r - 1) >= v) --r;
-  if (r < 16 && by0 + (float)r < v) ++r;
-  return r;
-}
-
 // Far edge entirely right of the box that spans some of its rows: it crosses
 // every pixel of row r when y0 <= py < y1 or y1 <= py < y0 (py = by0 + r), far
-// beyond rounding error of the reference's crossing test.  Those rows are
-// min(y0, y1) <= py < max(y0, y1): one run of the 16-bit row mask.
+// beyond rounding error of the reference's crossing test.
 __device__ __forceinline__ unsigned far_right_rows(const float4& e, float bx0, float by0) {
   const float bx1 = bx0 + 15.0f, by1 = by0 + 15.0f;
   if (!(fminf(e.x, e.z) > bx1) || fmaxf(e.y, e.w) < by0 || fminf(e.y, e.w) > by1) return 0u;
-  if (!(e.y == e.y) || !(e.w == e.w)) return 0u;
-  const int a = rows_below(fminf(e.y, e.w), by0), b = rows_below(fmaxf(e.y, e.w), by0);
-  return ((1u << b) - 1u) & ~((1u << a) - 1u);
+  unsigned rows = 0u;
+#pragma unroll
+  for (int r = 0; r < 16; ++r) {
+    const float py = by0 + (float)r;
+    if (((e.y <= py) & (e.w > py)) | ((e.y > py) & (e.w <= py))) rows |= 1u << r;
+  }
+  return rows;
 }
 
 __device__ __forceinline__ DEntry make_entry(const float4& e, int eid) {

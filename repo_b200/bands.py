@@ -11,6 +11,14 @@ the band gradients is exactly the full-image gradient up to summation order.
 
 Bands are balanced by a per-tile-row work estimate (edge slots + 8 per
 intersect, from one binning pass of the starting scene).
+
+SSIM over bands (band_ssim_sums): the valid-window SSIM output of row y reads
+input rows [y, y + win - 1], so a band owning pixel rows [y0, y1) produces the
+outputs of rows [y0, min(y1, H - win + 1)) from its own rows plus the first
+win - 1 rows of the next band (the halo, one point-to-point transfer per
+band boundary); the per-plane sums of the bands' outputs then add up
+(all-reduce) to the whole image's (manbo/metric.py:215-273 takes the mean of
+each plane's map, then over planes).
 """
 from __future__ import annotations
 
@@ -95,4 +103,93 @@ def allreduce_hook(group=None) -> Callable[[torch.Tensor], None]:
     return hook
 
 
-__all__ = ["balanced_bands", "tile_row_work", "band_for_rank", "allreduce_hook"]
+def ssim_halo_rows(bands_px: Sequence[Tuple[int, int]], index: int, height: int,
+                   win_size: int) -> int:
+    """Rows the band `index` of pixel-row bands `bands_px` (contiguous,
+    covering [0, height) in order) needs from the next band: win_size - 1,
+    fewer at the bottom of the image, none for an empty band."""
+    y0, y1 = bands_px[index]
+    if y1 <= y0:
+        return 0
+    need = min(win_size - 1, height - y1)
+    if need > 0:
+        nxt = bands_px[index + 1] if index + 1 < len(bands_px) else (y1, y1)
+        if nxt[0] != y1 or nxt[1] - nxt[0] < need:
+            raise ValueError(f"band {index} needs {need} halo rows from the next band, "
+                             f"which has {max(0, nxt[1] - nxt[0])}")
+    return max(0, need)
+
+
+def exchange_ssim_halo(img_chw: torch.Tensor, bands_px: Sequence[Tuple[int, int]], rank: int,
+                       win_size: int, group=None) -> torch.Tensor:
+    """This rank's rows of img_chw [C, H, W] (full-size buffer; only the band's
+    rows are read) extended by the next band's first rows: [C, rows + halo, W].
+    Every rank sends its first rows to the previous rank and receives the
+    next rank's (torch.distributed point-to-point; rank i owns band i)."""
+    import torch.distributed as dist
+
+    c, h, w = img_chw.shape
+    y0, y1 = bands_px[rank]
+    ops = []
+    recv = None
+    halo = ssim_halo_rows(bands_px, rank, h, win_size)
+    if halo > 0:
+        recv = torch.empty((c, halo, w), dtype=img_chw.dtype, device=img_chw.device)
+        ops.append(dist.P2POp(dist.irecv, recv, rank + 1, group))
+    send = None
+    if rank > 0:
+        prev_halo = ssim_halo_rows(bands_px, rank - 1, h, win_size)
+        if prev_halo > 0:
+            send = img_chw[:, y0:y0 + prev_halo, :].contiguous()
+            ops.append(dist.P2POp(dist.isend, send, rank - 1, group))
+    if ops:
+        for work in dist.batch_isend_irecv(ops):
+            work.wait()
+    own = img_chw[:, y0:y1, :]
+    return torch.cat([own, recv], dim=1) if recv is not None else own.contiguous()
+
+
+def band_ssim_sums(img_ext: torch.Tensor, target_chw: torch.Tensor, y0: int, win_size: int,
+                   plane_means: Callable[[torch.Tensor, torch.Tensor], torch.Tensor]
+                   ) -> torch.Tensor:
+    """Per-plane sums of the SSIM outputs a band owns, from its rows extended
+    by the halo (exchange_ssim_halo) and the matching target rows.
+    plane_means(x, y) returns the mean of each plane's valid SSIM map of
+    [C, rows, W] inputs (metric.ssim_per_plane on the GPU)."""
+    c, rows, w = img_ext.shape
+    out_rows, out_cols = rows - win_size + 1, w - win_size + 1
+    if out_rows <= 0 or out_cols <= 0:
+        return torch.zeros((c,), dtype=torch.float64, device=img_ext.device)
+    tgt = target_chw[:, y0:y0 + rows, :].contiguous()
+    means = plane_means(img_ext.contiguous(), tgt).to(torch.float64)
+    return means * float(out_rows * out_cols)
+
+
+def band_ssim(img_chw: torch.Tensor, target_chw: torch.Tensor,
+              bands_px: Sequence[Tuple[int, int]], rank: int, *, win_size: int = 11,
+              win_sigma: float = 1.5, k1: float = 0.01, k2: float = 0.03,
+              data_range: float = 1.0, plane_means=None, group=None) -> torch.Tensor:
+    """Whole-image SSIM (mean over planes of each plane's mean) of an image
+    rendered in bands, each rank holding its own rows of img_chw [C, H, W]:
+    one halo exchange, the band's per-plane sums, one all-reduce (SUM) of C
+    values.  Returns the same scalar on every rank."""
+    import torch.distributed as dist
+
+    from . import metric as _metric
+
+    c, h, w = img_chw.shape
+    if plane_means is None:
+        c1, c2 = (k1 * data_range) ** 2, (k2 * data_range) ** 2
+
+        def plane_means(x, y):
+            return _metric.ssim_per_plane(x.unsqueeze(0), y.unsqueeze(0), win_size, win_sigma,
+                                          c1, c2)
+    ext = exchange_ssim_halo(img_chw, bands_px, rank, win_size, group)
+    sums = band_ssim_sums(ext, target_chw, bands_px[rank][0], win_size, plane_means)
+    dist.all_reduce(sums, op=dist.ReduceOp.SUM, group=group)
+    count = float((h - win_size + 1) * (w - win_size + 1))
+    return (sums / count).mean()
+
+
+__all__ = ["balanced_bands", "tile_row_work", "band_for_rank", "allreduce_hook",
+           "ssim_halo_rows", "exchange_ssim_halo", "band_ssim_sums", "band_ssim"]

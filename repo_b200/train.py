@@ -60,7 +60,8 @@ class FillTrainer:
         if self.with_ssim and self.tile_rows != (0, tby):
             # a band renders only its own rows; SSIM's window needs the whole image
             raise ValueError("with_ssim=True needs the whole image: pass with_ssim=False "
-                             "with tile_rows (bands)")
+                             "with tile_rows (bands) and take SSIM across the bands with "
+                             "repo_b200.bands.band_ssim")
         self.grad_hook = grad_hook
         self.lr = (float(lr_points), float(lr_colors))
         self.betas, self.eps = (float(betas[0]), float(betas[1])), float(eps)

@@ -68,6 +68,62 @@ def test_allreduce_hook_sums_band_gradients_across_gloo_ranks():
         assert out[0] == want and out[1] == want
 
 
+def _ssim_rank_main(rank, world, port, bands_px, seed, out):
+    import numpy as np
+
+    import oracle
+    from repo_b200.bands import band_ssim
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=__import__("datetime").timedelta(seconds=60))
+    try:
+        g = torch.Generator().manual_seed(seed)
+        h = bands_px[-1][1]
+        img = torch.rand(3, h, 37, generator=g)
+        tgt = torch.rand(3, h, 37, generator=g)
+        # only this rank's rows are valid: the others are overwritten
+        mine = img.clone()
+        y0, y1 = bands_px[rank]
+        mine[:, :y0] = float("nan")
+        mine[:, y1:] = float("nan")
+
+        def plane_means(x, y):
+            m = oracle.ssim_map(x.unsqueeze(0).numpy(), y.unsqueeze(0).numpy())
+            return torch.from_numpy(m.reshape(3, -1).astype(np.float64).mean(axis=1))
+        out[rank] = float(band_ssim(mine, tgt, bands_px, rank, plane_means=plane_means))
+        if rank == 0:
+            out["full"] = oracle.ssim(img.unsqueeze(0).numpy(), tgt.unsqueeze(0).numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("bands_px", [[(0, 16), (16, 45)], [(0, 16), (16, 32), (32, 45)],
+                                      [(0, 16), (16, 32), (32, 36)]])
+def test_band_ssim_matches_whole_image_ssim_across_gloo_ranks(bands_px):
+    """Each rank holds only its band's rows; one halo exchange and one
+    all-reduce give the whole image's SSIM on every rank (the last case's
+    bottom band is shorter than the window and owns no output row)."""
+    world = len(bands_px)
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as mgr:
+        out = mgr.dict()
+        mp.start_processes(_ssim_rank_main, args=(world, _free_port(), bands_px, 5, out),
+                           nprocs=world, join=True, start_method="spawn")
+        for r in range(world):
+            assert abs(out[r] - out["full"]) <= 1e-6, (r, out[r], out["full"])
+
+
+def test_band_ssim_halo_rows():
+    from repo_b200.bands import ssim_halo_rows
+    bands = [(0, 16), (16, 32), (32, 36)]
+    assert [ssim_halo_rows(bands, i, 36, 11) for i in range(3)] == [10, 4, 0]
+    assert ssim_halo_rows([(0, 16), (16, 16)], 1, 16, 11) == 0
+    with pytest.raises(ValueError, match="halo"):
+        ssim_halo_rows([(0, 16), (16, 20), (20, 48)], 0, 48, 11)
+
+
 def test_trainer_refuses_ssim_on_a_band():
     from repo_b200 import scenes
     from repo_b200.train import FillTrainer

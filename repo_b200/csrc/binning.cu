@@ -794,16 +794,17 @@ __device__ void stage_tile(const StageIO& io, long long tile, int rs, int re, in
   for (int st = 0; st < kStrips; ++st) totals[st] = near_base[st];
 }
 
-// Work estimate of a strip for dispatch ordering: its staged records plus two
-// per intersect (the per-intersect compositing costs about two records).
+// Work estimate of a strip for dispatch ordering, in half-records: its staged
+// records plus two and a half per intersect (an intersect's compositing costs
+// about as much as two and a half records).
 __device__ __forceinline__ int strip_weight(int records, int intersects) {
   return intersects > 0 ? 2 * records + 5 * intersects : 0;
 }
 
 // One CTA per tile: sort the tile's pairs and emit primitive ids and
 // reference-format intersect ids; then, when staging outputs are given,
-// classify the tile's edges into its strips' records, store the strips' work
-// estimates and (last CTA) order the band's strips heaviest first.
+// classify the tile's edges into its strips' records and file each strip into
+// the dispatch lists by its work estimate (one atomic per strip).
 template <bool STROKE>
 __global__ void __launch_bounds__(kSortThreads) bin_tile_kernel(
     const int* __restrict__ bins, const float* __restrict__ depths,

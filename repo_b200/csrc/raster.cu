@@ -32,10 +32,14 @@
 // (the reference's strict-< rule in edge order), reduces per-primitive
 // gradients over the warp (four values per shuffle butterfly) before one
 // atomic per primitive value, and accumulates edge gradients per staged record
-// in shared memory before one global atomic per edge and chunk.  Its per-pixel
-// coverage, reciprocals and square root use the fast hardware forms: the
-// forward image must match the oracle bit for bit, the gradients only within
-// the reference's tolerance.
+// in shared memory before one global atomic per edge and chunk (each warp
+// first sums its lanes' contributions per distinct closest edge).  With visit
+// lists it walks only the intersects that composited a pixel of the strip;
+// with a fill forward's winner codes it evaluates only each pixel's closest
+// record of such an intersect (and whether the pixel is inside) instead of
+// every record.  Its per-pixel coverage, reciprocals and square root use the
+// fast hardware forms: the forward image must match the oracle bit for bit,
+// the gradients only within the reference's tolerance.
 #include "stage.cuh"
 
 namespace cs {

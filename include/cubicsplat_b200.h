@@ -478,6 +478,42 @@ CS_API int cs_adan_step(float *param, const float *grad, float *exp_avg, float *
                  float weight_decay, float eps, float clip_global_grad_norm, int32_t no_prox,
                  void *stream);
 
+/* --------------------------------------------------------------------------
+ * Regularisation loss of the curve model
+ * (manbo/regularization.py:65-250, manbo/ops/regularization.py)
+ *
+ * L = lambda_proj / N * sum phi(alpha)  +  opacity_weight * mean |sigmoid(op) - 1|
+ *   + [closed] masked second-difference energy / (N * ceil(2M / stride))
+ *   + [closed] joint hinge sum / (N * ceil(K / boundary_degree) * 2)
+ *
+ * control_points [N, K, 2]; opacity [num_opacity]; xyz [N, 2, M, 2] sampled
+ * paths (closed only, M = points_per_side).  Open mode projects the middle
+ * points onto p[0] -> p[K-1]; closed mode onto p[0] -> p[split_idx] (the
+ * shape degree + 1) and skips p[split_idx].  curvature_cos_thresh is
+ * cos(angle threshold).  N >= 1.
+ * ------------------------------------------------------------------------ */
+/* Workspace: cs_regularization_workspace_size() bytes, zeroed once. */
+CS_API size_t cs_regularization_workspace_size(void);
+/* The scalar loss into *loss (device). */
+CS_API int cs_regularization_forward(const float *control_points, const float *opacity,
+                              const float *xyz, int64_t num_curves, int64_t num_ctrl,
+                              int64_t num_opacity, int64_t points_per_side, int32_t closed,
+                              int32_t split_idx, int32_t boundary_degree, float boundary_bound,
+                              int32_t curvature_stride, float curvature_cos_thresh,
+                              float lambda_proj, float opacity_weight, float *loss,
+                              void *workspace, void *stream);
+/* Gradients times *grad_output (device scalar; NULL = 1): grad_control_points
+ * [N, K, 2] and grad_xyz [N, 2, M, 2] are overwritten (zeroed, then the terms'
+ * atomics), grad_opacity [num_opacity] written; any output may be NULL. */
+CS_API int cs_regularization_backward(const float *control_points, const float *opacity,
+                               const float *xyz, int64_t num_curves, int64_t num_ctrl,
+                               int64_t num_opacity, int64_t points_per_side, int32_t closed,
+                               int32_t split_idx, int32_t boundary_degree, float boundary_bound,
+                               int32_t curvature_stride, float curvature_cos_thresh,
+                               float lambda_proj, float opacity_weight, const float *grad_output,
+                               float *grad_control_points, float *grad_opacity, float *grad_xyz,
+                               void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -69,6 +69,13 @@ SIGNATURES = {
     "cs_edge_grads_to_ring": (ctypes.c_int, [_P, _P, _I64, _I32, _I32, _I32, _I32, _I32, _P,
                                              _I32, _I32, _P]),
     "cs_adan_step": (ctypes.c_int, [_P] * 6 + [_I64, _I32] + [_F32] * 10 + [_I32, _P]),
+    "cs_regularization_workspace_size": (_SZ, []),
+    "cs_regularization_forward": (ctypes.c_int, [_P, _P, _P, _I64, _I64, _I64, _I64, _I32, _I32,
+                                                 _I32, _F32, _I32, _F32, _F32, _F32, _P, _P,
+                                                 _P]),
+    "cs_regularization_backward": (ctypes.c_int, [_P, _P, _P, _I64, _I64, _I64, _I64, _I32,
+                                                  _I32, _I32, _F32, _I32, _F32, _F32, _F32, _P,
+                                                  _P, _P, _P, _P]),
     "cs_adam_workspace_size": (_SZ, []),
     "cs_adam_step": (ctypes.c_int, [_P, _P, _P, _P, _I64, _I64, _F32, _F32, _F32, _F32, _F32, _P,
                                     _P, _I32, _P]),

@@ -255,6 +255,34 @@ def adan_case(manbo, dev):
     return out
 
 
+REG_KW = dict(num_beziers=2, bezier_degree=4, num_samples=3, lambda_proj=0.7,
+              opacity_weight=0.3, boundary_bound=1.0, curvature_angle_thresh_deg=60.0)
+
+
+def reg_case(manbo, dev):
+    """The reference's regularisation loss and its gradients (autograd through
+    its backward kernels) on seeded closed (K = 10, sampled paths) and open
+    (K = 4) curves."""
+    gen = torch.Generator().manual_seed(17)
+    out = {}
+    for mode, k in (("closed", 10), ("unclosed", 4)):
+        n = 7
+        cp = (torch.rand(n, k, 2, generator=gen) * 2.6 - 1.3)
+        op = torch.randn(n, 1, generator=gen) * 2.0
+        xyz = torch.rand(n, 2, 24, 2, generator=gen) * 2.0 - 1.0
+        out[f"{mode}_cp"], out[f"{mode}_op"], out[f"{mode}_xyz"] = _np(cp), _np(op), _np(xyz)
+        tcp = cp.to(dev).requires_grad_(True)
+        top = op.to(dev).requires_grad_(True)
+        txyz = xyz.to(dev).requires_grad_(True) if mode == "closed" else None
+        loss = manbo.regularization_loss_tilelang(tcp, top, txyz, mode=mode, **REG_KW)
+        loss.backward()
+        out[f"{mode}_loss"] = _np(loss.detach().reshape(1))
+        out[f"{mode}_g_cp"], out[f"{mode}_g_op"] = _np(tcp.grad), _np(top.grad)
+        if txyz is not None:
+            out[f"{mode}_g_xyz"] = _np(txyz.grad)
+    return out
+
+
 def dc_cubics(seed: int, n: int) -> torch.Tensor:
     """Pixel-space cubics for the adaptive flatten: random ones plus straight,
     fully degenerate, closed-loop (zero chord), tiny and very large ones."""
@@ -411,11 +439,14 @@ def main(argv=None):
             _save(args.out, "dc_fill", dc_fill())
         if "dc_stroke" in cases:
             _save(args.out, "dc_stroke", dc_stroke())
+        if "regularization" in cases:
+            _save(args.out, "regularization", reg_case(manbo, dev))
     elif not args.no_golden:
         _save(args.out, "dc_flatten", dc_flatten_case(cs))
         _save(args.out, "dc_fill", dc_fill())
         _save(args.out, "dc_stroke", dc_stroke())
         _save(args.out, "adan", adan_case(manbo, dev))
+        _save(args.out, "regularization", reg_case(manbo, dev))
         _save(args.out, "fill_small_a", fill_case(cs, tb, scenes.small_fill_scene(21), 31, dev))
         _save(args.out, "fill_small_b", fill_case(cs, tb, scenes.small_fill_scene(22, h=40, w=72, paths=9, samples=5), 32, dev))
         ties = scenes.small_fill_scene(23, paths=7, mixed=False)

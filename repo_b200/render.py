@@ -532,13 +532,19 @@ def _empty_image(bg: torch.Tensor, img_h: int, img_w: int) -> torch.Tensor:
     return bg.view(1, 1, 3).expand(int(img_h), int(img_w), 3).clone()
 
 
-def _validate_common(num_primitives, num_segments, offs, colors, opacities, depths):
+def _validate_common(num_primitives, num_segments, offs, colors, opacities, depths,
+                     stroke_widths=None):
+    """The entries' size checks in the reference's order (the stroke entry
+    checks stroke widths before depths, cubic_polyline_splatting.py:1371-1387)."""
     if int(colors.shape[0]) != num_primitives:
         raise ValueError(
             f"colors first dim must match primitive count ({num_primitives}), got {int(colors.shape[0])}")
     if int(opacities.reshape(-1).shape[0]) != num_primitives:
         raise ValueError(
             f"opacities size must match primitive count ({num_primitives}), got {int(opacities.reshape(-1).shape[0])}")
+    if stroke_widths is not None and int(stroke_widths.reshape(-1).shape[0]) != num_primitives:
+        raise ValueError(
+            f"stroke_widths size must match primitive count ({num_primitives}), got {int(stroke_widths.reshape(-1).shape[0])}")
     if int(depths.reshape(-1).shape[0]) != num_primitives:
         raise ValueError(
             f"depths size must match primitive count ({num_primitives}), got {int(depths.reshape(-1).shape[0])}")
@@ -659,10 +665,8 @@ class CubicPolylineSplatFunction(torch.autograd.Function):
         if num_primitives <= 0:
             ctx.empty = True
             return _empty_image(bg, img_h, img_w)
-        _validate_common(num_primitives, num_segments, offs, colors, opacities, depths)
-        if int(stroke_widths.reshape(-1).shape[0]) != num_primitives:
-            raise ValueError(
-                f"stroke_widths size must match primitive count ({num_primitives}), got {int(stroke_widths.reshape(-1).shape[0])}")
+        _validate_common(num_primitives, num_segments, offs, colors, opacities, depths,
+                         stroke_widths=stroke_widths)
         raw = _f32(aa_widths.to(device=cubics_norm.device, dtype=torch.float32).reshape(-1))
         if int(raw.numel()) != num_primitives:
             raise ValueError(
@@ -799,10 +803,8 @@ def render_cubic_polyline_splat(cubics_norm, primitive_seg_offsets, colors, opac
     if num_primitives <= 0:
         bg = background.to(device=cubics_norm.device, dtype=torch.float32).view(1, 1, 3)
         return bg.expand(int(img_h), int(img_w), 3).clone()
-    _validate_common(num_primitives, num_segments, offs, colors, opacities, depths)
-    if int(stroke_widths.reshape(-1).shape[0]) != num_primitives:
-        raise ValueError(
-            f"stroke_widths size must match primitive count ({num_primitives}), got {int(stroke_widths.reshape(-1).shape[0])}")
+    _validate_common(num_primitives, num_segments, offs, colors, opacities, depths,
+                     stroke_widths=stroke_widths)
     dev = cubics_norm.device
     # raw widths: the Function clamps them (min 1e-4) and masks their gradient
     widths = _f32(_prim_param(aa_widths, aa_width, num_primitives, dev, torch.float32,

@@ -115,3 +115,49 @@ def test_workspace_and_list_sizes():
     for nt in (1, 7, 1536):
         assert nat.call("cs_unit_lists_size", nt) == 4 * (64 + 64 * 4 * nt)
         assert nat.call("cs_raster_workspace_size", nt) == 256 + 4 * 4 * nt
+
+
+def test_entry_validation_messages_match_the_reference():
+    """Size checks run before any device work, with the reference's messages
+    (cubic_splatting.py:3158-3205, cubic_polyline_splatting.py:1365-1400), and
+    a scene without primitives is the background (no device needed)."""
+    import torch
+
+    import manbo
+    fill = manbo.ops.render_cubic_fill_splat_tilelang
+    stroke = manbo.ops.render_cubic_polyline_splat_tilelang
+    g, p = 6, 3
+    cn = torch.zeros(g, 4, 2)
+    offs = torch.tensor([0, 2, 4, 6], dtype=torch.int32)
+    col, op, dep, bg = torch.zeros(p, 3), torch.ones(p), torch.arange(p).float(), torch.ones(3)
+    base = (cn, offs, col, op, dep, 32, 48, 16, 16, bg)
+    cases = [
+        (dict(colors=torch.zeros(2, 3)), "colors first dim must match primitive count \\(3\\), got 2"),
+        (dict(opacities=torch.ones(4)), "opacities size must match primitive count \\(3\\), got 4"),
+        (dict(depths=torch.ones(1)), "depths size must match primitive count \\(3\\), got 1"),
+    ]
+    for repl, msg in cases:
+        args = list(base)
+        for k, v in repl.items():
+            args[{"colors": 2, "opacities": 3, "depths": 4}[k]] = v
+        with pytest.raises(ValueError, match=msg):
+            fill(*args)
+    with pytest.raises(ValueError, match="fill_rules size must match primitive count \\(3\\), got 2"):
+        fill(*base, fill_rules=torch.ones(2, dtype=torch.int32))
+    with pytest.raises(ValueError, match="aa_widths size must match primitive count \\(3\\), got 2"):
+        fill(*base, aa_widths=torch.ones(2))
+    sw = torch.ones(p)
+    with pytest.raises(ValueError, match="stroke_widths size must match primitive count \\(3\\), got 5"):
+        stroke(cn, offs, col, op, torch.ones(5), dep, 32, 48, 16, 16, bg)
+    # the stroke entry checks stroke widths before depths, as the reference does
+    with pytest.raises(ValueError, match="stroke_widths size"):
+        stroke(cn, offs, col, op, torch.ones(5), dep[:1], 32, 48, 16, 16, bg)
+    with pytest.raises(ValueError, match="flatten_method"):
+        fill(*base, flatten_method="bezier-magic")
+    # no primitives: the background, [H, W, 3]
+    empty = fill(cn[:0], torch.zeros(1, dtype=torch.int32), col[:0], op[:0], dep[:0], 5, 7, 16,
+                 16, torch.tensor([0.1, 0.2, 0.3]))
+    assert empty.shape == (5, 7, 3) and torch.equal(empty[2, 3], torch.tensor([0.1, 0.2, 0.3]))
+    empty = stroke(cn[:0], torch.zeros(1, dtype=torch.int32), col[:0], op[:0], sw[:0], dep[:0],
+                   5, 7, 16, 16, torch.tensor([0.1, 0.2, 0.3]))
+    assert empty.shape == (5, 7, 3)

@@ -125,7 +125,10 @@ def exchange_ssim_halo(img_chw: torch.Tensor, bands_px: Sequence[Tuple[int, int]
     """This rank's rows of img_chw [C, H, W] (full-size buffer; only the band's
     rows are read) extended by the next band's first rows: [C, rows + halo, W].
     Every rank sends its first rows to the previous rank and receives the
-    next rank's (torch.distributed point-to-point; rank i owns band i)."""
+    next rank's (torch.distributed point-to-point; rank i owns band i).  A
+    rank with neither (an empty band) makes no call, so with NCCL some
+    collective must have run on the group before (NCCL's batched
+    point-to-point needs every rank in its first call)."""
     import torch.distributed as dist
 
     c, h, w = img_chw.shape

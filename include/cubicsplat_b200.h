@@ -514,6 +514,29 @@ CS_API int cs_regularization_backward(const float *control_points, const float *
                                float *grad_control_points, float *grad_opacity, float *grad_xyz,
                                void *stream);
 
+/* --------------------------------------------------------------------------
+ * 4-connected component labelling of a uint8 mask [H, W]
+ * (manbo/ops/connected_components.py:98-236)
+ *
+ * cs_ccl_labels_4: raw labels [H, W] int32, each component labelled with its
+ * smallest linear index + 1, background 0 (the reference's relaxation result).
+ * cs_ccl_compact_4 (after it, on its labels, same workspace): components
+ * renumbered 1.. in raster order of their first pixel, their count into
+ * *num_components (device).  cs_ccl_stats_4 (after that, same workspace):
+ * stats [n, 5] int32 (x, y, width, height, area) and centers [n, 2] float32
+ * (mean x, mean y) of the n = num_components components.  status (device
+ * int32) records a union that exceeded its retry bound or a label outside
+ * [0, H*W].  H * W < 2^31 - 1.
+ * ------------------------------------------------------------------------ */
+CS_API size_t cs_ccl_workspace_size(int64_t num_pixels);
+CS_API int cs_ccl_labels_4(const uint8_t *mask, int32_t height, int32_t width, int32_t *labels,
+                    int32_t *status, void *workspace, void *stream);
+CS_API int cs_ccl_compact_4(const int32_t *labels, int32_t height, int32_t width,
+                     int32_t *labels_compact, int32_t *num_components, int32_t *status,
+                     void *workspace, void *stream);
+CS_API int cs_ccl_stats_4(int32_t height, int32_t width, int32_t num_components, int32_t *stats,
+                   float *centers, void *workspace, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

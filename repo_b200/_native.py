@@ -70,6 +70,10 @@ SIGNATURES = {
                                              _I32, _I32, _P]),
     "cs_adan_step": (ctypes.c_int, [_P] * 6 + [_I64, _I32] + [_F32] * 10 + [_I32, _P]),
     "cs_regularization_workspace_size": (_SZ, []),
+    "cs_ccl_workspace_size": (_SZ, [_I64]),
+    "cs_ccl_labels_4": (ctypes.c_int, [_P, _I32, _I32, _P, _P, _P, _P]),
+    "cs_ccl_compact_4": (ctypes.c_int, [_P, _I32, _I32, _P, _P, _P, _P, _P]),
+    "cs_ccl_stats_4": (ctypes.c_int, [_I32, _I32, _I32, _P, _P, _P, _P]),
     "cs_regularization_forward": (ctypes.c_int, [_P, _P, _P, _I64, _I64, _I64, _I64, _I32, _I32,
                                                  _I32, _F32, _I32, _F32, _F32, _F32, _P, _P,
                                                  _P]),

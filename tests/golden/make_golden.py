@@ -283,6 +283,23 @@ def reg_case(manbo, dev):
     return out
 
 
+def ccl_case(dev):
+    """The reference's 4-connected labelling (raw labels and the stats
+    variant) on seeded masks."""
+    from manbo.ops import connected_components as ccm
+    out = {}
+    for i, (shape, density) in enumerate((((13, 19), 0.5), ((64, 97), 0.6), ((40, 40), 0.0))):
+        gen = torch.Generator().manual_seed(70 + i)
+        mask = torch.rand(shape, generator=gen) < density
+        out[f"m{i}_mask"] = _np(mask.to(torch.uint8))
+        out[f"m{i}_raw"] = _np(ccm.connected_components_labels_4_tilelang(mask.to(dev)))
+        n, lab, stats, cent = ccm.connected_components_with_stats_4_tilelang(mask.to(dev))
+        out[f"m{i}_n"] = np.array([n], np.int32)
+        out[f"m{i}_labels"], out[f"m{i}_stats"], out[f"m{i}_centers"] = \
+            _np(lab), _np(stats), _np(cent)
+    return out
+
+
 def dc_cubics(seed: int, n: int) -> torch.Tensor:
     """Pixel-space cubics for the adaptive flatten: random ones plus straight,
     fully degenerate, closed-loop (zero chord), tiny and very large ones."""
@@ -441,12 +458,15 @@ def main(argv=None):
             _save(args.out, "dc_stroke", dc_stroke())
         if "regularization" in cases:
             _save(args.out, "regularization", reg_case(manbo, dev))
+        if "components" in cases:
+            _save(args.out, "components", ccl_case(dev))
     elif not args.no_golden:
         _save(args.out, "dc_flatten", dc_flatten_case(cs))
         _save(args.out, "dc_fill", dc_fill())
         _save(args.out, "dc_stroke", dc_stroke())
         _save(args.out, "adan", adan_case(manbo, dev))
         _save(args.out, "regularization", reg_case(manbo, dev))
+        _save(args.out, "components", ccl_case(dev))
         _save(args.out, "fill_small_a", fill_case(cs, tb, scenes.small_fill_scene(21), 31, dev))
         _save(args.out, "fill_small_b", fill_case(cs, tb, scenes.small_fill_scene(22, h=40, w=72, paths=9, samples=5), 32, dev))
         ties = scenes.small_fill_scene(23, paths=7, mixed=False)

@@ -40,3 +40,32 @@ def test_executed_work_with_visit_lists():
     _, _, pe_b, vis_b = bench.executed_work(bins, istrips, None, None, fidx, fts, h, w, 1, 2,
                                             visits=visits)
     assert pe_b == 64 * (2 + 3 + 0 + 1) and vis_b == 64 * (1 + 1 + 0 + 2)
+
+
+def test_reference_work_count_follows_the_per_pixel_stop():
+    """raster_work: every pixel visits its tile's intersects up to its stop
+    and every edge of each (forward: final_idx where T fell below 1e-4, else
+    the tile's end; backward: final_idx)."""
+    import torch
+
+    class Trainer:
+        h = w = 16
+        tbx = 1
+        counters = torch.tensor([2, 0, 0, 0], dtype=torch.int32)
+        tile_bins = torch.tensor([[0, 2]], dtype=torch.int32)
+        prim_sorted = torch.tensor([0, 1], dtype=torch.int32)
+        edge_offs = torch.tensor([0, 60, 90], dtype=torch.int32)    # 60 and 30 edges
+        fidx = torch.zeros(16, 16, dtype=torch.int32)
+        fts = torch.zeros(16, 16)
+
+    tr = Trainer()
+    tr.fidx[8:] = 1
+    tr.fts[8:] = 0.5          # rows 8-15 never saturate: the forward walks to the end
+    pe_f, vis_f, pe_b, vis_b, n = bench.raster_work(tr)
+    assert n == 2
+    assert (pe_f, vis_f) == (128 * 60 + 128 * 90, 128 * 1 + 128 * 2)
+    assert (pe_b, vis_b) == (128 * 60 + 128 * 90, 128 * 1 + 128 * 2)
+    tr.fts[8:] = 0.0          # now saturated at final_idx 1: the same stops
+    assert bench.raster_work(tr)[:2] == (pe_f, vis_f)
+    tr.fidx[8:] = 0           # saturated after intersect 0 everywhere
+    assert bench.raster_work(tr)[:4] == (256 * 60, 256, 256 * 60, 256)

@@ -69,3 +69,14 @@ def test_reference_work_count_follows_the_per_pixel_stop():
     assert bench.raster_work(tr)[:2] == (pe_f, vis_f)
     tr.fidx[8:] = 0           # saturated after intersect 0 everywhere
     assert bench.raster_work(tr)[:4] == (256 * 60, 256, 256 * 60, 256)
+
+
+def test_profile_summaries_hold_the_traffic_bench_reports():
+    """roofline.traffic comes from the committed ncu summaries: each kernel the
+    bench reports has its per-launch DRAM bytes there."""
+    for kernel, summary in (("raster_backward_kernel", "raster_fill_config2.md"),
+                            ("raster_forward_kernel", "raster_fill_config2.md"),
+                            ("raster_backward_kernel", "raster_stroke_config4.md")):
+        t = bench.ncu_traffic(kernel, summary)
+        assert isinstance(t, int) and t > 0, (kernel, summary)
+    assert bench.ncu_traffic("raster_backward_kernel", "no_such_summary.md") is None

@@ -58,3 +58,20 @@ def test_host_wrapper_checks_and_largest_component_centre():
     with pytest.raises(ValueError, match="at least one foreground"):
         comp.select_largest_component_center(torch.from_numpy(lab), torch.zeros(0, 5),
                                              torch.zeros(0, 2))
+
+
+@pytest.mark.parametrize("i", [0, 1, 2])
+def test_oracle_matches_reference_golden(i):
+    """Raw labels, count, compact labels and stats bit for bit, centres to
+    float32 rounding, against the reference's own outputs
+    (tests/golden/components.npz, from manbo/ops/connected_components.py run
+    by tests/golden/make_golden.py on a GPU)."""
+    from conftest import load_golden
+    g = load_golden("components")
+    mask = g[f"m{i}_mask"].astype(bool)
+    np.testing.assert_array_equal(cc.labels_4(mask), g[f"m{i}_raw"])
+    n, lab, stats, centres = cc.with_stats_4(mask)
+    assert n == int(g[f"m{i}_n"][0])
+    np.testing.assert_array_equal(lab, g[f"m{i}_labels"])
+    np.testing.assert_array_equal(stats, g[f"m{i}_stats"])
+    np.testing.assert_allclose(centres, g[f"m{i}_centers"], rtol=1e-6, atol=0)

@@ -118,3 +118,24 @@ def test_host_wrapper_checks_arguments_like_the_reference():
         regularization_loss(cp[:0], op, xyz, mode="unclosed", **kw)
     with pytest.raises(ValueError, match="CUDA"):
         regularization_loss(cp, op, xyz, mode="closed", **kw)
+
+
+@pytest.mark.parametrize("mode", ["closed", "unclosed"])
+def test_oracle_matches_reference_golden(mode):
+    """The restatement against the reference's own loss and gradients
+    (tests/golden/regularization.npz, from manbo/regularization.py:359 run by
+    tests/golden/make_golden.py on a GPU; the reference runs in float32 with
+    fast math)."""
+    from conftest import load_golden
+    g = load_golden("regularization")
+    cp = g[f"{mode}_cp"].astype(np.float64)
+    op = g[f"{mode}_op"].astype(np.float64)
+    xyz = g[f"{mode}_xyz"].astype(np.float64) if mode == "closed" else None
+    loss = reg.regularization_loss(cp, op, xyz, mode=mode, **KW)
+    want = float(g[f"{mode}_loss"][0])
+    assert abs(loss - want) <= 1e-5 * abs(want)
+    g_cp, g_op, g_xyz = reg.regularization_grads(cp, op, xyz, mode=mode, **KW)
+    assert rel_l2(g_cp, g[f"{mode}_g_cp"]) <= 1e-4
+    assert rel_l2(g_op, g[f"{mode}_g_op"]) <= 1e-4
+    if mode == "closed":
+        assert rel_l2(g_xyz, g[f"{mode}_g_xyz"]) <= 1e-4

@@ -51,6 +51,9 @@ sys.path.insert(0, ROOT)
 METRIC = "fwd+bwd iters/s at 768x512, 512 paths"
 UNIT = "iters/s"
 E2E_MIN_WARMUP = 25
+KERNEL_TIMING_REPS = 200
+WORKLOAD_CONFIG2 = ("config2: 768x512 RGB, 512 closed cubic paths x 4 segs, S=16, "
+                    "fwd+MSE+SSIM+bwd+Adam (lr 0.5 pts / 0.01 colours)")
 L2_FLUSH_BYTES = 256 << 20
 
 
@@ -65,6 +68,8 @@ def parse_args(argv=None):
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
     ap.add_argument("--workload", default="config2",
                     choices=["config2", "config3", "config4", "config5"])
+    ap.add_argument("--no-gpu-reference", action="store_true")
+    ap.add_argument("--gpu-reference-child", action="store_true", help=argparse.SUPPRESS)
     return ap.parse_args(argv)
 
 
@@ -163,36 +168,20 @@ def time_device_calls(fn, reps, flush, stream):
     return [s.elapsed_time(e) for s, e in evs]
 
 
-def kernel_times(tr, reps, flush, stream):
-    """CUDA-event durations of the forward and backward raster launches, taken
-    inside eager training steps on the launching stream."""
+def graph_kernel_times(tr, reps, flush):
+    """Mean CUDA-event durations of the forward and backward raster launches
+    over `reps` replays of the captured step (events recorded inside the
+    graph around the two launches, read after each replay)."""
     import torch
-    from repo_b200 import _native as nat
     fwd, bwd = [], []
-    orig = nat.call
-
-    def timed_call(name, *args):
-        if name in ("cs_fill_forward", "cs_fill_backward"):  # the two raster kernels
-            s = torch.cuda.Event(enable_timing=True)
-            e = torch.cuda.Event(enable_timing=True)
-            s.record(stream)
-            r = orig(name, *args)
-            e.record(stream)
-            (fwd if name == "cs_fill_forward" else bwd).append((s, e))
-            return r
-        return orig(name, *args)
-
-    nat.call = timed_call
-    try:
-        for _ in range(reps):
-            flush()
-            tr.step_eager()
-        torch.cuda.synchronize()
-    finally:
-        nat.call = orig
-    f = [s.elapsed_time(e) for s, e in fwd]
-    b = [s.elapsed_time(e) for s, e in bwd]
-    return statistics.mean(f), statistics.mean(b)
+    for _ in range(reps):
+        flush()
+        tr.step()
+        f, b = tr.kernel_times()
+        fwd.append(f)
+        bwd.append(b)
+    torch.cuda.synchronize()
+    return statistics.mean(fwd), statistics.mean(bwd)
 
 
 def raster_work(tr):
@@ -345,6 +334,12 @@ def run_b200(args, rank, world, local_rank):
 
     tr = FillTrainer(scene, dev, lr_points=0.5, lr_colors=0.01, with_ssim=True)
     tr.capture(warmup=max(3, args.warmup))
+    # a second capture of the same step with timing events around the two
+    # raster launches, for the kernel times (the timed graph has none)
+    timed = FillTrainer(scene, dev, lr_points=0.5, lr_colors=0.01, with_ssim=True,
+                        capacity=(tr.capacity, tr.dcapacity))
+    timed.enable_kernel_timing()
+    timed.capture(warmup=3)
     for _ in range(args.warmup):
         tr.step()
     torch.cuda.synchronize()
@@ -361,6 +356,9 @@ def run_b200(args, rank, world, local_rank):
         t0 = time.perf_counter()
         durs = time_steps(tr.step, args.steps, flush, stream)
         wall = time.perf_counter() - t0
+        # the dominant kernels, timed live with CUDA events on their stream
+        # inside graph-replayed steps (one synchronisation per replay)
+        t_fwd, t_bwd = graph_kernel_times(timed, KERNEL_TIMING_REPS, flush)
     barrier()
     torch.cuda.synchronize()
     n_isect, status = tr.check_status()
@@ -374,13 +372,14 @@ def run_b200(args, rank, world, local_rank):
     value = world * args.steps / (total_ms / 1e3)
     loss_final, ssim_final = tr.loss_value(), tr.ssim_value()
 
-    # dominant kernels, timed live with CUDA events on the launching stream
-    t_fwd, t_bwd = kernel_times(tr, 10, flush, stream)
-    pe_fwd, vis_fwd, pe_bwd, vis_bwd, n_now = raster_work(tr)
+    # work of the kernel-timing trainer's last step (its state tracks the timed one's)
+    tk = timed
+    pe_fwd, vis_fwd, pe_bwd, vis_bwd, n_now = raster_work(tk)
     xe_fwd, xv_fwd, xe_bwd, xv_bwd = executed_work(
-        tr.tile_bins.cpu().numpy(), tr.istrips.cpu().numpy(), tr.rowoff.cpu().numpy(),
-        tr.imeta.cpu().numpy(), tr.fidx.cpu().numpy(), tr.fts.cpu().numpy(), tr.h, tr.w, tr.tbx,
-        n_now, tr.visits.cpu().numpy())
+        tk.tile_bins.cpu().numpy(), tk.istrips.cpu().numpy(), tk.rowoff.cpu().numpy(),
+        tk.imeta.cpu().numpy(), tk.fidx.cpu().numpy(), tk.fts.cpu().numpy(), tk.h, tk.w, tk.tbx,
+        n_now, tk.visits.cpu().numpy())
+    timed.graph = None
 
     # e2e through the drop-in API with host buffers
     e2e = None
@@ -400,8 +399,7 @@ def run_b200(args, rank, world, local_rank):
             "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "config2: 768x512 RGB, 512 closed cubic paths x 4 segs, S=16, "
-                                   "fwd+MSE+SSIM+bwd+Adam (lr 0.5 pts / 0.01 colours)",
+            "config": {"workload": WORKLOAD_CONFIG2,
                        "scene": "seed-1 value noise + 32 ellipses target, circles r 5-40 px",
                        "parallelism": f"one scene per rank x{world}" if world > 1 else "single GPU",
                        "l2": "flushed before every step (256 MiB write), outside the step events",
@@ -529,7 +527,6 @@ def run_stroke(args, rank, world, local_rank):
     import torch
 
     import manbo
-    from repo_b200 import _native as nat
     from repo_b200 import render, scenes
 
     dev = torch.device("cuda", local_rank)
@@ -571,31 +568,6 @@ def run_stroke(args, rank, world, local_rank):
     with ClockSampler(local_rank) as clk:
         durs = time_steps(step, args.steps, flush, stream)
     total_ms = sum(durs)
-    # the two stroke raster kernels, timed live with CUDA events on their stream
-    fwd, bwd = [], []
-    orig = nat.call
-
-    def timed(name, *a):
-        if name in ("cs_stroke_forward", "cs_stroke_backward"):
-            e0 = torch.cuda.Event(enable_timing=True)
-            e1 = torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-            r = orig(name, *a)
-            e1.record(stream)
-            (fwd if name == "cs_stroke_forward" else bwd).append((e0, e1))
-            return r
-        return orig(name, *a)
-
-    nat.call = timed
-    try:
-        for _ in range(5):
-            flush()
-            step()
-        torch.cuda.synchronize()
-    finally:
-        nat.call = orig
-    t_fwd = statistics.mean(a.elapsed_time(b) for a, b in fwd)
-    t_bwd = statistics.mean(a.elapsed_time(b) for a, b in bwd)
     with torch.no_grad():  # reference-algorithm work of the current state
         wd = torch.clamp(aa, min=1e-4)
         b = render.bin_primitives(cn.detach(), offs, depths, wd, h, w, sc.samples,
@@ -607,6 +579,14 @@ def run_stroke(args, rank, world, local_rank):
             b.tile_bins.cpu().numpy(), b.isect_strips.cpu().numpy(), None, b.imeta.cpu().numpy(),
             fidx.cpu().numpy(), fts.cpu().numpy(), h, w, b.tile_bounds[0], int(b.num_intersects),
             b.visit_lists.cpu().numpy())
+        # the two stroke raster kernels on this frame, timed with CUDA events on
+        # their stream (launches queued behind a sleep, so host work is hidden;
+        # the backward's time includes zeroing its gradient buffers)
+        v_out = scenes.seeded_grad(7, h, w).to(dev)
+        t_fwd = statistics.median(time_device_calls(
+            lambda: render.forward_raster(b, bg, h, w), 20, flush, stream))
+        t_bwd = statistics.median(time_device_calls(
+            lambda: render.raster_backward(b, p, bg, fts, fidx, v_out, h, w), 20, flush, stream))
     t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -721,62 +701,173 @@ def run_sweep(args, rank, world, local_rank):
     return [_json.dumps(line) for line in lines]
 
 
-def run_e2e(scene, dev, args, flush, stream, world):
-    """Training steps through the manbo API: target H2D from pinned memory and
-    loss D2H every step, timed with CUDA events."""
-    import torch
+class E2EStep:
+    """The config-2 training step as a user writes it against the drop-in API:
+    ring points gathered into cubics, manbo.ops.render_cubic_fill_splat_tilelang,
+    clamp + CHW, manbo.mse_loss_tilelang, manbo.ssim (forward metric),
+    backward, torch Adam (lr 0.5 points / 0.01 colours).  Every step copies
+    its target image from pinned host memory (on a copy stream, overlapping
+    the render; the loss waits for it) and reads the loss and SSIM back into
+    pinned host memory."""
 
-    import manbo
-    from repo_b200 import scenes as sc_mod
+    def __init__(self, scene, dev, capturable=False):
+        import torch
 
-    h, w, s = scene.height, scene.width, scene.samples
-    ring = scene.ring.to(dev).clone().requires_grad_(True)
-    colors = scene.colors.to(dev).clone().requires_grad_(True)
-    opac, depths = scene.opacities.to(dev), scene.depths.to(dev)
-    rules, aa, bg = scene.fill_rules.to(dev), scene.aa_widths.to(dev), scene.background.to(dev)
-    offs = scene.seg_offsets().to(dev)
-    gidx = sc_mod.ring_gather_index(scene.segs_per_path).to(dev)
-    half = torch.tensor([0.5 * w, 0.5 * h], device=dev)
-    target_host = scene.target.clone().pin_memory()
-    target_dev = torch.empty_like(target_host, device=dev)
-    loss_host = torch.empty((2,), dtype=torch.float32).pin_memory()
-    opt = torch.optim.Adam([{"params": [ring], "lr": 0.5}, {"params": [colors], "lr": 0.01}],
-                           fused=True)
+        from repo_b200 import scenes as sc_mod
+        self.h, self.w, self.s = scene.height, scene.width, scene.samples
+        self.ring = scene.ring.to(dev).clone().requires_grad_(True)
+        self.colors = scene.colors.to(dev).clone().requires_grad_(True)
+        self.opac, self.depths = scene.opacities.to(dev), scene.depths.to(dev)
+        self.rules = scene.fill_rules.to(dev)
+        self.aa, self.bg = scene.aa_widths.to(dev), scene.background.to(dev)
+        self.offs = scene.seg_offsets().to(dev)
+        self.gidx = sc_mod.ring_gather_index(scene.segs_per_path).to(dev)
+        self.half = torch.tensor([0.5 * self.w, 0.5 * self.h], device=dev)
+        self.target_host = scene.target.clone().pin_memory()
+        self.target_dev = torch.empty_like(self.target_host, device=dev)
+        self.loss_host = torch.empty((2,), dtype=torch.float32).pin_memory()
+        self.capturable = capturable
+        self.opt = torch.optim.Adam([{"params": [self.ring], "lr": 0.5},
+                                     {"params": [self.colors], "lr": 0.01}], fused=True,
+                                    capturable=capturable)
+        self.copy_stream = torch.cuda.Stream(dev)
+        self.h2d_bytes = int(self.target_host.numel() * 4)
+        self.d2h_bytes = 8
 
-    def step():
-        target_dev.copy_(target_host, non_blocking=True)
-        opt.zero_grad(set_to_none=True)
-        cn = ring[:, gidx, :].reshape(-1, 4, 2) / half - 1.0
+    def __call__(self):
+        import torch
+
+        import manbo
+        main = torch.cuda.current_stream()
+        self.copy_stream.wait_stream(main)  # last step's readers of the target are done
+        with torch.cuda.stream(self.copy_stream):
+            self.target_dev.copy_(self.target_host, non_blocking=True)
+        self.opt.zero_grad(set_to_none=not self.capturable)
+        cn = self.ring[:, self.gidx, :].reshape(-1, 4, 2) / self.half - 1.0
         out = manbo.ops.render_cubic_fill_splat_tilelang(
-            cn, offs, colors, opac, depths, h, w, 16, 16, bg, fill_rules=rules, aa_widths=aa,
-            distance_samples=s)
+            cn, self.offs, self.colors, self.opac, self.depths, self.h, self.w, 16, 16, self.bg,
+            fill_rules=self.rules, aa_widths=self.aa, distance_samples=self.s)
         img = torch.clamp(out, 0, 1).permute(2, 0, 1).unsqueeze(0).contiguous()
-        loss = manbo.mse_loss_tilelang(img, target_dev)
+        main.wait_stream(self.copy_stream)
+        loss = manbo.mse_loss_tilelang(img, self.target_dev)
         with torch.no_grad():
-            sv = manbo.ssim(img.detach(), target_dev)
+            sv = manbo.ssim(img.detach(), self.target_dev)
         loss.backward()
-        opt.step()
-        loss_host[0:1].copy_(loss.detach().view(1), non_blocking=True)
-        loss_host[1:2].copy_(sv.view(1), non_blocking=True)
+        self.opt.step()
+        self.loss_host[0:1].copy_(loss.detach().view(1), non_blocking=True)
+        self.loss_host[1:2].copy_(sv.view(1), non_blocking=True)
 
+
+def run_e2e(scene, dev, args, flush, stream, world):
+    """Training steps through the manbo API, timed with CUDA events: eagerly
+    (as train.py runs), and the same calls captured once into a CUDA graph by
+    the caller and replayed (the API is capture-safe: under capture it reads
+    nothing back)."""
+    import torch
+    step = E2EStep(scene, dev)
     # the caching allocator and the host-side caches of the API path take a
     # few dozen steps to settle; time the steady state
     warm = max(E2E_MIN_WARMUP, args.warmup)
     for _ in range(warm):
         step()
     torch.cuda.synchronize()
-    durs = time_steps(step, args.steps, flush, stream)
-    total_ms = sum(durs)
+    total_ms = sum(time_steps(step, args.steps, flush, stream))
+
+    gstep = E2EStep(scene, dev, capturable=True)
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        for _ in range(5):
+            gstep()
+    torch.cuda.current_stream(dev).wait_stream(side)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        gstep()
+    for _ in range(max(3, args.warmup)):
+        graph.replay()
+    torch.cuda.synchronize()
+    g_ms = sum(time_steps(graph.replay, args.steps, flush, stream))
     if world > 1:
         import torch.distributed as dist
-        t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
+        t = torch.tensor([total_ms, g_ms], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        total_ms = float(t.item())
+        total_ms, g_ms = (float(v) for v in t.tolist())
+    del graph
     return {"value": round(world * args.steps / (total_ms / 1e3), 3), "unit": UNIT,
-            "h2d_bytes_per_step": int(target_host.numel() * 4),
-            "d2h_bytes_per_step": 8, "warmup": warm, "path": "manbo.ops.render_cubic_fill_splat_tilelang + "
-            "manbo.mse_loss_tilelang + manbo.ssim + autograd + torch Adam",
-            "ms_per_step": round(total_ms / args.steps, 4)}
+            "h2d_bytes_per_step": step.h2d_bytes, "d2h_bytes_per_step": step.d2h_bytes,
+            "warmup": warm, "path": "manbo.ops.render_cubic_fill_splat_tilelang + "
+            "manbo.mse_loss_tilelang + manbo.ssim + autograd + torch Adam, eager (train.py)",
+            "ms_per_step": round(total_ms / args.steps, 4),
+            "graph": {"value": round(world * args.steps / (g_ms / 1e3), 3), "unit": UNIT,
+                      "ms_per_step": round(g_ms / args.steps, 4),
+                      "h2d_bytes_per_step": gstep.h2d_bytes,
+                      "d2h_bytes_per_step": gstep.d2h_bytes,
+                      "path": "the same API calls captured once into a CUDA graph by the "
+                              "caller (torch Adam capturable), replayed every step"}}
+
+
+# --------------------------------------------------------------------------
+# GPU reference: the reference's own TileLang renderer, same loop, same box
+
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
+
+
+def gpu_reference_child(args):
+    """Runs in a child process: the E2EStep loop on the unmodified reference
+    package installed in baseline/_ref (its TileLang kernels), eager, timed
+    like the B200 arm.  Prints one JSON object."""
+    sys.path.insert(0, REF_DIR)
+    import torch
+
+    import manbo
+    import tilelang
+    from repo_b200 import scenes
+    mpath = os.path.abspath(manbo.__file__)
+    if not mpath.startswith(os.path.abspath(REF_DIR)):
+        raise RuntimeError(f"manbo resolved to {mpath}, not the reference install")
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream(dev)
+    flush_buf = torch.empty((L2_FLUSH_BYTES // 4,), dtype=torch.float32, device=dev)
+    step = E2EStep(scenes.config2(), dev)
+    t0 = time.perf_counter()
+    step()  # TileLang compiles its kernels here
+    torch.cuda.synchronize()
+    compile_s = time.perf_counter() - t0
+    for _ in range(max(E2E_MIN_WARMUP, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    steps = max(20, min(args.steps, 200))
+    total_ms = sum(time_steps(step, steps, flush_buf.zero_, stream))
+    print(json.dumps({"value": round(steps / (total_ms / 1e3), 3), "unit": UNIT,
+                      "ms_per_step": round(total_ms / steps, 4), "steps": steps,
+                      "first_step_s": round(compile_s, 1),
+                      "tilelang": getattr(tilelang, "__version__", "?"),
+                      "manbo": os.path.relpath(mpath, ROOT),
+                      "final_loss": float(step.loss_host[0])}), flush=True)
+
+
+def run_gpu_reference(args):
+    """The reference renderer's training step on this GPU (child process),
+    or why it could not run."""
+    if not os.path.isdir(os.path.join(REF_DIR, "manbo")):
+        return {"unavailable": "the reference is not installed in baseline/_ref"}
+    cmd = [sys.executable, os.path.abspath(__file__), "--gpu-reference-child",
+           "--steps", str(args.steps), "--warmup", str(args.warmup)]
+    try:
+        r = subprocess.run(cmd, capture_output=True, text=True, timeout=900)
+    except subprocess.TimeoutExpired:
+        return {"unavailable": "the reference step did not finish within 900 s"}
+    for line in reversed(r.stdout.strip().splitlines()):
+        if line.startswith("{"):
+            out = json.loads(line)
+            out["path"] = ("reference manbo.ops.render_cubic_fill_splat_tilelang (TileLang) + "
+                           "manbo.mse_loss_tilelang + manbo.ssim + autograd + torch Adam, eager, "
+                           "the same loop as e2e")
+            return out
+    tail = (r.stderr or r.stdout).strip().splitlines()[-1:] or ["no output"]
+    return {"unavailable": f"reference step failed (rc {r.returncode}): {tail[0][:200]}"}
 
 
 # --------------------------------------------------------------------------
@@ -854,8 +945,7 @@ def run_reference(args, rank, world):
             "steps": iters, "warmup": 1, "ms_per_step": round(1e3 * dt / iters, 2),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic", "impl": "reference",
-            "config": {"workload": "config2: 768x512 RGB, 512 closed cubic paths x 4 segs, S=16, "
-                                   "fwd+MSE+SSIM+bwd+Adam", "device": "host CPU"},
+            "config": {"workload": WORKLOAD_CONFIG2, "device": "host CPU"},
             "cpu_baseline": {"value": round(value, 5), "unit": UNIT, "cores": cores,
                              "kind": "port", "sample": sample},
             "e2e": {"value": round(value, 5), "unit": UNIT, "h2d_bytes_per_step": 0,
@@ -869,6 +959,9 @@ def main(argv=None):
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.gpu_reference_child:
+        gpu_reference_child(args)
+        return 0
     if args.impl == "reference":
         res = run_reference(args, rank, world)
         if res is not None:
@@ -901,6 +994,16 @@ def main(argv=None):
                     print(line, flush=True)
             return 0
         res, tr = run_b200(args, rank, world, local_rank)
+        if rank == 0 and world == 1 and not args.no_gpu_reference:
+            ref = run_gpu_reference(args)
+            res["gpu_reference"] = ref
+            if "value" in ref:
+                rv = ref["value"]
+                res["vs_gpu_reference"] = {
+                    "value": round(res["value"] / rv, 2),
+                    "e2e": round(res["e2e"]["value"] / rv, 2) if "e2e" in res else None,
+                    "e2e_graph": round(res["e2e"]["graph"]["value"] / rv, 2)
+                    if "e2e" in res else None}
         if rank == 0 and not args.no_cpu_baseline:
             value, iters, dt, cores = run_cpu(args.cpu_seconds, 1000)
             res["cpu_baseline"] = {

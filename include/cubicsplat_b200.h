@@ -537,6 +537,18 @@ CS_API int cs_ccl_compact_4(const int32_t *labels, int32_t height, int32_t width
 CS_API int cs_ccl_stats_4(int32_t height, int32_t width, int32_t num_components, int32_t *stats,
                    float *centers, void *workspace, void *stream);
 
+/* --------------------------------------------------------------------------
+ * Graph-capture helpers (no counterpart in the reference, whose renderer reads
+ * intersect counts back to the host every frame and cannot be captured)
+ *
+ * cs_stream_is_capturing: 1 if the stream is capturing a CUDA graph, 0 if not,
+ * -1 if the query failed.  cs_poison_on_status: when *status (device int32) is
+ * not CS_OK, every element of data [n] becomes NaN; a frame captured with a
+ * fixed intersect capacity uses it so that an overflow cannot pass unnoticed.
+ * ------------------------------------------------------------------------ */
+CS_API int cs_stream_is_capturing(void *stream);
+CS_API int cs_poison_on_status(const int32_t *status, float *data, int64_t n, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

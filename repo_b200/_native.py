@@ -92,6 +92,8 @@ SIGNATURES = {
     "cs_ssim": (ctypes.c_int, [_P, _P, _P, _I64, _I32, _I32, _I32, _F32, _F32, _P, _P, _P, _P]),
     "cs_ssim_noalloc": (ctypes.c_int, [_P, _P, _P, _I64, _I32, _I32, _I32, _F32, _F32, _P, _P,
                                        _P]),
+    "cs_stream_is_capturing": (ctypes.c_int, [_P]),
+    "cs_poison_on_status": (ctypes.c_int, [_P, _P, _I64, _P]),
 }
 
 _lock = threading.Lock()

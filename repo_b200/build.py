@@ -86,5 +86,46 @@ def build(force: bool = False, verbose_ptxas: bool = False) -> str:
     return LIB_PATH
 
 
+EXT_SRC = os.path.join(CSRC, "torch_api.cpp")
+EXT_PATH = os.path.join(LIB_DIR, "_cs_torch.so")
+
+
+def cuda_include() -> str:
+    return os.path.join(os.path.dirname(os.path.dirname(nvcc_path())), "include")
+
+
+def build_torch_ext(force: bool = False) -> str:
+    """Compile the torch binding (``csrc/torch_api.cpp``, host C++ only) into
+    ``lib/_cs_torch.so``, linked against the C-ABI library beside it."""
+    import sysconfig
+
+    import torch
+    import torch.utils.cpp_extension as ce
+    deps = [EXT_SRC, HEADERS[0], LIB_PATH]
+    if not force and not _stale(EXT_PATH, deps):
+        return EXT_PATH
+    torch_lib = ce.library_paths()[0]
+    cmd = [os.environ.get("CXX", "g++"), "-O2", "-std=c++17", "-shared", "-fPIC",
+           "-fvisibility=hidden",
+           f"-D_GLIBCXX_USE_CXX11_ABI={int(torch.compiled_with_cxx11_abi())}",
+           "-DTORCH_EXTENSION_NAME=_cs_torch", "-DTORCH_API_INCLUDE_EXTENSION_H"]
+    for inc in ce.include_paths() + [sysconfig.get_paths()["include"],
+                                     os.path.join(ROOT, "include"), cuda_include()]:
+        cmd += ["-isystem" if inc != os.path.join(ROOT, "include") else "-I", inc]
+    cmd += [EXT_SRC, "-o", EXT_PATH, "-L", torch_lib, "-lc10", "-lc10_cuda", "-ltorch",
+            "-ltorch_cpu", "-ltorch_python", "-L", LIB_DIR, "-l:libcubicsplat_b200.so",
+            "-Wl,-rpath,$ORIGIN", f"-Wl,-rpath,{torch_lib}"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"torch binding build failed:\n{r.stderr}")
+    return EXT_PATH
+
+
+def build_all(force: bool = False, verbose_ptxas: bool = False) -> str:
+    path = build(force=force, verbose_ptxas=verbose_ptxas)
+    build_torch_ext(force=force)
+    return path
+
+
 if __name__ == "__main__":
-    print(build(force="--force" in sys.argv, verbose_ptxas="-v" in sys.argv))
+    print(build_all(force="--force" in sys.argv, verbose_ptxas="-v" in sys.argv))

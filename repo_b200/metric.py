@@ -11,6 +11,7 @@ from typing import Dict, Tuple
 
 import torch
 
+from . import _ext
 from . import _native as nat
 
 DEFAULT_THREADS = 256
@@ -57,7 +58,7 @@ def _validate_pair_4d(x: torch.Tensor, y: torch.Tensor) -> None:
 def gaussian_1d(win_size: int, win_sigma: float, device: torch.device) -> torch.Tensor:
     """Normalised 1-D Gaussian g; the reference's window is outer(g, g)
     (manbo/metric.py:47-61)."""
-    key = (str(device), int(win_size), float(win_sigma))
+    key = (device.type, device.index, int(win_size), float(win_sigma))
     g = _GAUSS_CACHE.get(key)
     if g is None:
         coords = torch.arange(win_size, dtype=torch.float32, device=device)
@@ -71,10 +72,10 @@ def gaussian_1d(win_size: int, win_sigma: float, device: torch.device) -> torch.
 
 def sse_mse(x: torch.Tensor, y: torch.Tensor, out_sse=None, out_mse=None):
     """Device-resident SSE and MSE of two flattened float32 CUDA tensors."""
+    if out_mse is None:
+        return out_sse, _ext.load().mse_forward(x, y, out_sse)
     n = int(x.numel())
     dev = x.device
-    if out_mse is None:
-        out_mse = torch.empty((), dtype=torch.float32, device=dev)
     ws = _workspace(dev, "mse", int(nat.call("cs_mse_workspace_size", n)))
     nat.check(nat.call("cs_mse_forward", nat.ptr(x), nat.ptr(y), n, nat.ptr(out_sse),
                        nat.ptr(out_mse), ws.data_ptr(), nat.stream(dev)), "cs_mse_forward")
@@ -84,11 +85,7 @@ def sse_mse(x: torch.Tensor, y: torch.Tensor, out_sse=None, out_mse=None):
 def mse_backward(lhs: torch.Tensor, rhs: torch.Tensor, scale: torch.Tensor,
                  factor: float = 1.0) -> torch.Tensor:
     """grad = scale * factor * (lhs - rhs), scale a device scalar."""
-    grad = torch.empty_like(lhs, dtype=torch.float32)
-    nat.check(nat.call("cs_mse_backward", nat.ptr(lhs), nat.ptr(rhs), nat.ptr(scale),
-                       float(factor), nat.ptr(grad), int(lhs.numel()), nat.stream(lhs.device)),
-              "cs_mse_backward")
-    return grad
+    return _ext.load().mse_backward(lhs, rhs, scale, float(factor))
 
 
 class MSELossFunction(torch.autograd.Function):
@@ -147,15 +144,9 @@ def ssim_per_plane(x32: torch.Tensor, y32: torch.Tensor, win_size: int, win_sigm
                    c1: float, c2: float, ssim_map=None) -> torch.Tensor:
     """Mean SSIM of each of the N*C planes of [N, C, H, W] float32 CUDA inputs."""
     n, c, h, w = x32.shape
-    dev = x32.device
-    planes = n * c
-    g = gaussian_1d(win_size, win_sigma, dev)
-    out = torch.empty((planes,), dtype=torch.float32, device=dev)
-    ws = _workspace(dev, "ssim", int(nat.call("cs_ssim_workspace_size", planes, h, w, win_size)))
-    nat.check(nat.call("cs_ssim", nat.ptr(x32), nat.ptr(y32), nat.ptr(g), planes, h, w, win_size,
-                       float(c1), float(c2), nat.ptr(out), nat.ptr(ssim_map), ws.data_ptr(),
-                       nat.stream(dev)), "cs_ssim")
-    return out
+    g = gaussian_1d(win_size, win_sigma, x32.device)
+    return _ext.load().ssim_planes(x32, y32, g, n * c, h, w, int(win_size), float(c1), float(c2),
+                                   ssim_map)
 
 
 def ssim(x: torch.Tensor, y: torch.Tensor, *, data_range: float = 1.0, size_average: bool = True,

@@ -7,21 +7,26 @@ with the same argument meaning, validation messages, empty-scene behaviour and
 ``process_fn`` hook stages.  All device work runs in the sm_100a kernels behind
 the C ABI (``repo_b200._native``); there is no CPU path.
 
+Each autograd stage is one call into the torch binding (``repo_b200._ext``,
+csrc/torch_api.cpp), which launches the stage's kernels on the current stream.
+
 Differences from the reference, by design:
-  * binning is the fused count -> scan -> scatter -> per-tile sort pipeline,
-    which costs one host synchronisation per forward (to size the intersect
-    list) instead of the reference's three or more;
+  * binning is the fused count -> scan -> scatter -> per-tile sort pipeline
+    with intersect buffers sized from the previous frame of the same shape:
+    a forward enqueues all of its launches and then reads the counts back
+    once (the reference synchronises three or more times); a frame that
+    outgrew the cached size is binned again, and under CUDA graph capture
+    nothing is read back (an overflow then leaves the image NaN);
   * ties in depth are ordered by primitive id (the order of a stable sort of
     the reference's keys).
 """
 from __future__ import annotations
 
-import math
-from dataclasses import dataclass
 from typing import Any, Callable, Mapping, MutableMapping, Optional
 
 import torch
 
+from . import _ext
 from . import _native as nat
 
 BLOCK_X = 16
@@ -39,7 +44,6 @@ _FLATTEN_ALIASES = {
     "decasteljau": CUBIC_FLATTEN_METHOD_DE_CASTELJAU,
     "de-casteljau": CUBIC_FLATTEN_METHOD_DE_CASTELJAU,
 }
-INT64_MAX = (1 << 63) - 1
 DE_CASTELJAU_TOL_PX = 0.5  # DEFAULT_DE_CASTELJAU_FLATNESS_TOL_PX (cubic_splatting.py:18)
 
 CubicProcessPayload = MutableMapping[str, Any]
@@ -84,7 +88,7 @@ def bernstein_basis(samples: int, device: torch.device) -> torch.Tensor:
     """[4, S] cubic Bernstein weights at linspace(0, 1, S), computed with torch on
     the host exactly as the reference writes them (cubic_splatting.py:1710-1716)."""
     s = max(2, int(samples))
-    key = (s, str(device))
+    key = (s, device.type, device.index)
     b = _BASIS_CACHE.get(key)
     if b is None:
         t = torch.linspace(0.0, 1.0, s, dtype=torch.float32)
@@ -104,44 +108,32 @@ def _check_block(block_x: int, block_y: int) -> None:
         raise ValueError(f"the B200 renderer uses 16x16 tiles, got block {block_x}x{block_y}")
 
 
-@dataclass
-class Binning:
-    """Binned and staged frame: reference-format intersect list plus the per-tile
-    raster input (near-edge records, per-intersect records, row offsets)."""
-    cubics_px: torch.Tensor
-    edges_px: torch.Tensor
-    prim_edge_offsets: torch.Tensor
-    prim_tile_ranges: torch.Tensor
-    num_tiles_hit: torch.Tensor
-    tile_bins: torch.Tensor
-    prim_ids_sorted: torch.Tensor
-    isect_ids_sorted: torch.Tensor
-    num_intersects: int
-    tile_bounds: tuple
-    samples: int
-    tile_rows: tuple
-    tile_dlist: torch.Tensor
-    imeta: torch.Tensor
-    rowoff: Optional[torch.Tensor]
-    dlist: torch.Tensor
-    counters: torch.Tensor
-    stroke: bool
-    isect_strips: torch.Tensor                  # [I, 4, 2] per-strip record ranges
-    unit_order: Optional[torch.Tensor] = None   # strip dispatch lists (staged work)
-    unit_order_bwd: Optional[torch.Tensor] = None  # strip dispatch lists (forward's work)
-    visit_lists: Optional[torch.Tensor] = None  # per strip: intersects that composited a pixel
-    visit_winners: Optional[torch.Tensor] = None  # per listed visit and lane: closest-record codes
-    flatten_method: str = CUBIC_FLATTEN_METHOD_BERNSTEIN
-    segment_edge_offsets: Optional[torch.Tensor] = None  # de Casteljau CSR [G + 1]
-    edge_t_starts: Optional[torch.Tensor] = None         # de Casteljau leaf intervals [E]
-    edge_t_ends: Optional[torch.Tensor] = None
+class _LazyFrame:
+    """``Binning`` is the binding's Frame type (loaded on first use)."""
+
+    def __call__(self, **fields):
+        f = _ext.load().Frame()
+        for k, v in fields.items():
+            setattr(f, k, v)
+        return f
+
+    def __instancecheck__(self, obj):
+        return isinstance(obj, _ext.load().Frame)
 
 
-def _offsets_error(offs: torch.Tensor, num_segments: int) -> ValueError:
-    o = offs.detach().to("cpu")
-    return ValueError(
-        "primitive_seg_offsets must start at 0 and end at num_segments "
-        f"(got start={int(o[0])}, end={int(o[-1])}, num_segments={num_segments})")
+# A binned and staged frame: reference-format intersect list (tile_bins,
+# prim_ids_sorted, isect_ids_sorted) plus the per-tile raster input (near-edge
+# records, per-intersect records, row offsets, dispatch and visit lists).
+Binning = _LazyFrame()
+
+
+def replace_binning(b, **changes):
+    """A shallow copy of a frame with some fields replaced (the tensors are
+    shared, as dataclasses.replace shares them)."""
+    c = b.copy()
+    for k, v in changes.items():
+        setattr(c, k, v)
+    return c
 
 
 def flatten_de_casteljau(cubics_px: torch.Tensor, offs: torch.Tensor, samples: int,
@@ -174,9 +166,9 @@ def bin_primitives(cubics_norm: torch.Tensor, offs: torch.Tensor, depths: torch.
                    stroke_widths: Optional[torch.Tensor] = None,
                    aabb_pad: float = DEFAULT_AABB_PAD, aniso: bool = False,
                    tile_rows: Optional[tuple] = None,
-                   flatten_method: str = CUBIC_FLATTEN_METHOD_BERNSTEIN) -> Binning:
+                   flatten_method: str = CUBIC_FLATTEN_METHOD_BERNSTEIN):
     """Project, bound, flatten, bin, sort and stage all primitives (fused B200
-    pipeline, one host synchronisation to size the intersect list).
+    pipeline, one read-back of the counts).
 
     The intersect list equals the reference's K3 + flatten + K4 + cumsum + K5 +
     sort + K6 (cubic_splatting.py:2815-2908): tile_bins [T, 2] of [start, end)
@@ -185,78 +177,14 @@ def bin_primitives(cubics_norm: torch.Tensor, offs: torch.Tensor, depths: torch.
     adaptively (cs_flatten_de_casteljau) before the counts instead of the
     uniform Bernstein flatten inside cs_bin_count.
     """
-    dev = cubics_norm.device
     s = max(2, int(samples))
-    g = int(cubics_norm.shape[0])
-    p = int(offs.numel()) - 1
-    tbx, tby, _ = tile_bounds_for(img_h, img_w)
-    nt = tbx * tby
-    r0, r1 = (0, tby) if tile_rows is None else (int(tile_rows[0]), int(tile_rows[1]))
-    stroke = stroke_widths is not None
-    cubics_px = torch.empty((g, 4, 2), dtype=torch.float32, device=dev)
-    dc = flatten_method == CUBIC_FLATTEN_METHOD_DE_CASTELJAU
-    prim_ranges = torch.empty((p, 4), dtype=torch.int32, device=dev)
-    num_hit = torch.empty((p,), dtype=torch.int32, device=dev)
-    tile_bins = torch.empty((nt, 2), dtype=torch.int32, device=dev)
-    tile_dlist = torch.empty((nt, 2), dtype=torch.int32, device=dev)
-    counters = torch.zeros((4,), dtype=torch.int32, device=dev)
-    ws = _cached_workspace(_BIN_WS, dev, int(nat.call("cs_bin_workspace_size", nt)))
-    st = nat.stream(dev)
-    cn = _f32(cubics_norm)
-    aw = _f32(aa_widths)
-    sw = None if stroke_widths is None else _f32(stroke_widths)
-    basis = bernstein_basis(s, dev)
-    peo = seg_eo = t0 = t1 = None
-    edge_offs = None
-    if dc:
-        nat.check(nat.call("cs_project_cubics", nat.ptr(cn), None, None, nat.ptr(cubics_px), None,
-                           None, g, int(img_h), int(img_w), 16, 16, 0.0, 0, st),
-                  "cs_project_cubics")
-        edges, peo, seg_eo, t0, t1 = flatten_de_casteljau(cubics_px, offs, s, counters[1:2])
-    else:
-        edges = torch.empty((g * (s - 1), 2, 2), dtype=torch.float32, device=dev)
-        edge_offs = torch.empty((p + 1,), dtype=torch.int32, device=dev)
-    nat.check(nat.call("cs_bin_count", nat.ptr(cn), nat.ptr(offs), nat.ptr(aw), nat.ptr(sw),
-                       nat.ptr(basis), nat.ptr(cubics_px), nat.ptr(edges), nat.ptr(peo),
-                       nat.ptr(edge_offs), nat.ptr(prim_ranges),
-                       nat.ptr(num_hit), nat.ptr(tile_bins), nat.ptr(tile_dlist),
-                       nat.ptr(counters), ws.data_ptr(), p, g, INT64_MAX, INT64_MAX, s,
-                       int(img_h), int(img_w), r0, r1, float(aabb_pad), int(bool(aniso)), None,
-                       0, st),
-              "cs_bin_count")
-    # the one host synchronisation of the forward: sizes + status
-    n_isect, status, n_dbound, _ = (int(v) for v in counters.tolist())
-    if status == nat.CS_ERR_ARG:
-        raise _offsets_error(offs, g)
-    nat.check(status, "cs_bin_count")
-    if dc:
-        edge_offs = peo
-    # per-frame buffers are sized in a few classes (_size_class), so that the
-    # caching allocator reuses blocks from frame to frame; the sorted lists
-    # are exact-length views
-    ci, cd = _size_class(n_isect), _size_class(n_dbound)
-    prim_sorted = torch.empty((ci,), dtype=torch.int32, device=dev)[:n_isect]
-    isect_sorted = torch.empty((ci,), dtype=torch.int64, device=dev)[:n_isect]
-    imeta = torch.empty((ci, 12), dtype=torch.int32, device=dev)
-    rowoff = None if stroke else torch.empty((ci, 16), dtype=torch.int32, device=dev)
-    dlist = torch.empty((cd, 8), dtype=torch.float32, device=dev)
-    istrips = torch.empty((ci, 4, 2), dtype=torch.int32, device=dev)
-    unit_order = torch.empty((int(nat.call("cs_unit_lists_size", max(1, r1 - r0) * tbx)) // 4,),
-                             dtype=torch.int32, device=dev)
-    if n_isect > 0:
-        nat.check(nat.call("cs_bin_sort", nat.ptr(prim_ranges), nat.ptr(_f32(depths)),
-                           nat.ptr(tile_bins), nat.ptr(prim_sorted), nat.ptr(isect_sorted),
-                           nat.ptr(counters), ws.data_ptr(), p, n_isect, int(img_h), int(img_w),
-                           r0, r1, nat.ptr(edges), nat.ptr(edge_offs), nat.ptr(colors),
-                           nat.ptr(opacities), nat.ptr(inv_sigma2s), nat.ptr(fill_rules),
-                           nat.ptr(sw), nat.ptr(tile_dlist), nat.ptr(imeta), nat.ptr(rowoff),
-                           nat.ptr(istrips), nat.ptr(dlist), max(n_dbound, 1),
-                           nat.ptr(unit_order), st), "cs_bin_sort")
-    return Binning(cubics_px, edges, edge_offs, prim_ranges, num_hit, tile_bins, prim_sorted,
-                   isect_sorted, n_isect, (tbx, tby, 1), s, (r0, r1), tile_dlist, imeta, rowoff,
-                   dlist, counters, stroke, istrips, unit_order if n_isect > 0 else None,
-                   flatten_method=flatten_method, segment_edge_offsets=seg_eo,
-                   edge_t_starts=t0, edge_t_ends=t1)
+    r0, r1 = (0, -1) if tile_rows is None else (int(tile_rows[0]), int(tile_rows[1]))
+    return _ext.load().bin_frame(
+        cubics_norm, _i32(offs), _f32(depths), _f32(aa_widths), _f32(inv_sigma2s), _f32(colors),
+        _f32(opacities), None if fill_rules is None else _i32(fill_rules),
+        None if stroke_widths is None else _f32(stroke_widths),
+        bernstein_basis(s, cubics_norm.device), int(img_h), int(img_w), s, float(aabb_pad),
+        bool(aniso), r0, r1, flatten_method == CUBIC_FLATTEN_METHOD_DE_CASTELJAU)
 
 
 def stage_reference_lists(prim_ids_sorted, tile_bins, edges_px, isect_edge_ranges, colors,
@@ -294,199 +222,46 @@ def stage_reference_lists(prim_ids_sorted, tile_bins, edges_px, isect_edge_range
                        nat.ptr(unit_order), nat.ptr(counters), ws.data_ptr(), max(bound, 1),
                        int(img_h), int(img_w), nat.stream(dev)),
               "cs_tile_stage")
-    return Binning(None, edges_px, prim_edge_offsets, None, None, tile_bins, prim_ids_sorted,
-                   None, n, (tbx, tby, 1), 0, (0, tby), tile_dlist, imeta, rowoff, dlist, counters,
-                   stroke, istrips, unit_order)
-
-
-def _size_class(n: int) -> int:
-    """Smallest allocation size class >= max(n, 1): multiples of 1/16 of the
-    power of two below n (at most 6.25% over), and at least 4096."""
-    n = max(int(n), 1)
-    if n <= 4096:
-        return 4096
-    step = 1 << (n.bit_length() - 5)
-    return (n + step - 1) // step * step
-
-
-_RASTER_WS: dict = {}
-_BIN_WS: dict = {}
-
-
-def _cached_workspace(cache: dict, device: torch.device, nbytes: int) -> torch.Tensor:
-    """Workspace per device and exact size, zeroed when allocated and left
-    zeroed by every launch that uses it, so launches in stream order share it.
-    Keyed by size because its layout depends on the tile count: a buffer laid
-    out for another grid would put the counters where that grid left data."""
-    key = (str(device), int(nbytes))
-    buf = cache.get(key)
-    if buf is None:
-        buf = torch.zeros((max(nbytes, 256),), dtype=torch.uint8, device=device)
-        cache[key] = buf
-    return buf
-
-
-def _bwd_lists(b: "Binning"):
-    """Dispatch lists for the backward: the forward's (measured work) when the
-    forward filled them, else the staging pass's."""
-    return b.unit_order_bwd if b.unit_order_bwd is not None else b.unit_order
-
-
-def raster_workspace(device: torch.device, num_tiles: int) -> torch.Tensor:
-    """Per-device workspace of the raster kernels (dispatch counter, completion
-    ticket, per-strip loss partials).  It is zeroed when allocated and every
-    launch leaves it zeroed, so launches in stream order share it."""
-    key = str(device)
-    need = int(nat.call("cs_raster_workspace_size", int(num_tiles)))
-    buf = _RASTER_WS.get(key)
-    if buf is None or buf.numel() < need:
-        buf = torch.zeros((need,), dtype=torch.uint8, device=device)
-        _RASTER_WS[key] = buf
-    return buf
+    return Binning(edges_px=edges_px, prim_edge_offsets=prim_edge_offsets, tile_bins=tile_bins,
+                   prim_ids_sorted=prim_ids_sorted, num_intersects=n, isect_capacity=max(n, 1),
+                   tile_bounds=(tbx, tby, 1), samples=0, tile_rows=(0, tby),
+                   tile_dlist=tile_dlist, imeta=imeta, rowoff=rowoff, dlist=dlist,
+                   counters=counters, stroke=stroke, isect_strips=istrips, unit_order=unit_order)
 
 
 def _aa_widths(raw: torch.Tensor):
     """Clamped anti-aliasing widths and 1/sigma^2 in one launch
     (cs_aa_widths_forward): clamp(aa, min=1e-4), 1 / clamp(w^2, min=1e-6)."""
-    n = int(raw.numel())
-    buf = torch.empty((2, n), dtype=torch.float32, device=raw.device)
-    nat.check(nat.call("cs_aa_widths_forward", nat.ptr(raw), nat.ptr(buf[0]), nat.ptr(buf[1]), n,
-                       nat.stream(raw.device)), "cs_aa_widths_forward")
-    return buf[0], buf[1]
+    return _ext.load().aa_widths_forward(raw)
 
 
 def _aa_widths_grad(raw: torch.Tensor, widths: torch.Tensor, v_inv: torch.Tensor):
     """Gradient of the raw anti-aliasing widths: -2 v_inv / clamp(w^3, 1e-12)
     through the clamp(aa, min=1e-4) of the entry (cs_aa_widths_backward)."""
-    n = int(widths.numel())
-    out = torch.empty((n,), dtype=torch.float32, device=widths.device)
-    nat.check(nat.call("cs_aa_widths_backward", nat.ptr(raw), nat.ptr(widths), nat.ptr(v_inv),
-                       nat.ptr(out), n, nat.stream(widths.device)), "cs_aa_widths_backward")
-    return out
+    return _ext.load().aa_widths_backward(raw, widths, v_inv)
 
 
 def _inv_sigma2(widths: torch.Tensor) -> torch.Tensor:
     return (1.0 / torch.clamp(widths * widths, min=1e-6)).contiguous()
 
 
-def _zeros_views(dev, *shapes):
-    total = sum(math.prod(sh) for sh in shapes)
-    buf = torch.zeros((max(total, 1),), dtype=torch.float32, device=dev)
-    out, o = [], 0
-    for sh in shapes:
-        n = math.prod(sh)
-        out.append(buf[o:o + n].view(sh))
-        o += n
-    return out
-
-
-def forward_raster(b: Binning, background, img_h: int, img_w: int, out_chw=None, outputs=None):
+def forward_raster(b, background, img_h: int, img_w: int, out_chw=None, outputs=None):
     """Forward rasteriser over staged tiles: image [H, W, 3], final_Ts, final_idx
     (written into ``outputs`` when given)."""
-    dev = b.tile_bins.device
-    if outputs is None:
-        out = torch.empty((img_h, img_w, 3), dtype=torch.float32, device=dev)
-        fts = torch.empty((img_h, img_w), dtype=torch.float32, device=dev)
-        fidx = torch.empty((img_h, img_w), dtype=torch.int32, device=dev)
-    else:
-        out, fts, fidx = outputs
-    if b.num_intersects <= 0:
-        out.copy_(background.view(1, 1, 3).expand(img_h, img_w, 3))
-        fts.fill_(1.0)
-        fidx.fill_(0)
-        return out, fts, fidx
-    st = nat.stream(dev)
-    status = b.counters[1:2]
-    ws = raster_workspace(dev, b.tile_bounds[0] * b.tile_bounds[1])
-    if b.unit_order is not None and b.unit_order_bwd is None:
-        b.unit_order_bwd = torch.empty_like(b.unit_order)
-    if b.visit_lists is None:
-        nt = b.tile_bounds[0] * b.tile_bounds[1]
-        nbytes = int(nat.call("cs_visit_lists_size", int(b.num_intersects), nt))
-        b.visit_lists = torch.empty((nbytes // 4,), dtype=torch.int32, device=dev)
-        if not b.stroke:  # closest-record codes: fills only
-            wbytes = int(nat.call("cs_visit_winners_size", int(b.num_intersects), nt))
-            b.visit_winners = torch.empty((wbytes // 2,), dtype=torch.int16, device=dev)
-    if not b.stroke:
-        nat.check(nat.call("cs_fill_forward", nat.ptr(b.prim_ids_sorted), nat.ptr(b.tile_bins),
-                           nat.ptr(b.tile_dlist), nat.ptr(b.imeta), nat.ptr(b.isect_strips),
-                           nat.ptr(b.rowoff), nat.ptr(b.dlist), nat.ptr(b.unit_order),
-                           nat.ptr(b.unit_order_bwd), nat.ptr(b.visit_lists),
-                           nat.ptr(b.visit_winners), nat.ptr(background),
-                           nat.ptr(out), nat.ptr(fts), nat.ptr(fidx),
-                           nat.ptr(out_chw), None, None, nat.ptr(status), ws.data_ptr(),
-                           img_h, img_w, b.tile_rows[0], b.tile_rows[1], st), "cs_fill_forward")
-    else:
-        nat.check(nat.call("cs_stroke_forward", nat.ptr(b.prim_ids_sorted), nat.ptr(b.tile_bins),
-                           nat.ptr(b.tile_dlist), nat.ptr(b.imeta), nat.ptr(b.isect_strips),
-                           nat.ptr(b.dlist), nat.ptr(b.unit_order), nat.ptr(b.unit_order_bwd),
-                           nat.ptr(b.visit_lists), nat.ptr(b.visit_winners),
-                           nat.ptr(background), nat.ptr(out), nat.ptr(fts), nat.ptr(fidx),
-                           nat.ptr(out_chw), None,
-                           None, nat.ptr(status), ws.data_ptr(), img_h, img_w,
-                           b.tile_rows[0], b.tile_rows[1], st), "cs_stroke_forward")
-    return out, fts, fidx
+    o = (None, None, None) if outputs is None else tuple(outputs)
+    return _ext.load().raster_forward(b, background, int(img_h), int(img_w), out_chw, *o)
 
 
-def raster_backward(b: Binning, num_primitives: int, background, final_ts, final_idx, v_output,
+def raster_backward(b, num_primitives: int, background, final_ts, final_idx, v_output,
                     img_h, img_w, *, collect_contrib: bool = False,
                     collect_isect_contrib: bool = False, out_img=None, target_chw=None,
                     mse_scale=None):
     """Backward rasteriser.  Returns v_edges, v_colors, v_opacities, v_inv_sigma2s,
     v_stroke_widths (stroke only), curve_contrib_rgb, curve_isect_contrib."""
-    dev = b.tile_bins.device
-    p = int(num_primitives)
-    ne = int(b.edges_px.shape[0])
-    ni = int(b.num_intersects)
-    shapes = [(ne, 2, 2), (p, 3), (p,), (p,)]
-    if b.stroke:
-        shapes.append((p,))
-    if collect_contrib:
-        shapes.append((p, 3))
-    if collect_isect_contrib:
-        shapes.append((ni,))
-    views = _zeros_views(dev, *shapes)
-    v_edges, v_colors, v_opac, v_inv = views[:4]
-    i = 4
-    v_sw = None
-    if b.stroke:
-        v_sw = views[i]
-        i += 1
-    contrib = None
-    if collect_contrib:
-        contrib = views[i]
-        i += 1
-    icontrib = views[i] if collect_isect_contrib else None
-    if ni > 0 and ne > 0:
-        st = nat.stream(dev)
-        vo = None if v_output is None else _f32(v_output)
-        status = b.counters[1:2]
-        ws = raster_workspace(dev, b.tile_bounds[0] * b.tile_bounds[1])
-        if not b.stroke:
-            nat.check(nat.call("cs_fill_backward", nat.ptr(b.prim_ids_sorted), nat.ptr(b.tile_bins),
-                               nat.ptr(b.tile_dlist), nat.ptr(b.imeta),
-                               nat.ptr(b.isect_strips), nat.ptr(b.rowoff), nat.ptr(b.dlist),
-                               nat.ptr(_bwd_lists(b)), nat.ptr(b.visit_lists),
-                               nat.ptr(b.visit_winners), nat.ptr(background), nat.ptr(final_ts),
-                               nat.ptr(final_idx), nat.ptr(vo), nat.ptr(out_img),
-                               nat.ptr(target_chw), nat.ptr(mse_scale), nat.ptr(v_edges),
-                               nat.ptr(v_colors), nat.ptr(v_opac), nat.ptr(v_inv),
-                               nat.ptr(contrib), nat.ptr(icontrib), nat.ptr(status),
-                               ws.data_ptr(), img_h, img_w, b.tile_rows[0], b.tile_rows[1], st),
-                      "cs_fill_backward")
-        else:
-            nat.check(nat.call("cs_stroke_backward", nat.ptr(b.prim_ids_sorted),
-                               nat.ptr(b.tile_bins), nat.ptr(b.tile_dlist), nat.ptr(b.imeta),
-                               nat.ptr(b.isect_strips), nat.ptr(b.dlist),
-                               nat.ptr(_bwd_lists(b)), nat.ptr(b.visit_lists),
-                               nat.ptr(b.visit_winners), nat.ptr(background), nat.ptr(final_ts),
-                               nat.ptr(final_idx), nat.ptr(vo), nat.ptr(out_img),
-                               nat.ptr(target_chw), nat.ptr(mse_scale), nat.ptr(v_edges),
-                               nat.ptr(v_colors), nat.ptr(v_opac), nat.ptr(v_sw), nat.ptr(v_inv),
-                               nat.ptr(contrib), nat.ptr(icontrib), nat.ptr(status),
-                               ws.data_ptr(), img_h, img_w, b.tile_rows[0], b.tile_rows[1], st),
-                      "cs_stroke_backward")
-    return v_edges, v_colors, v_opac, v_inv, v_sw, contrib, icontrib
+    return tuple(_ext.load().raster_backward(
+        b, int(num_primitives), background, final_ts, final_idx, v_output, int(img_h),
+        int(img_w), bool(collect_contrib), bool(collect_isect_contrib), out_img, target_chw,
+        mse_scale))
 
 
 def edge_grads_to_cubics_csr(v_edges: torch.Tensor, segment_edge_offsets: torch.Tensor,
@@ -504,13 +279,11 @@ def edge_grads_to_cubics_csr(v_edges: torch.Tensor, segment_edge_offsets: torch.
     return out
 
 
-def binning_edge_grads(b: Binning, v_edges: torch.Tensor, num_segments: int,
+def binning_edge_grads(b, v_edges: torch.Tensor, num_segments: int,
                        scale=(1.0, 1.0)) -> torch.Tensor:
     """Cubic gradients from edge gradients with the binning's flatten method."""
-    if b.flatten_method == CUBIC_FLATTEN_METHOD_DE_CASTELJAU:
-        return edge_grads_to_cubics_csr(v_edges, b.segment_edge_offsets, b.edge_t_starts,
-                                        b.edge_t_ends, num_segments, scale)
-    return edge_grads_to_cubics(v_edges, num_segments, b.samples, scale)
+    return _ext.load().edge_grads(b, v_edges, int(num_segments), float(scale[0]),
+                                  float(scale[1]))
 
 
 def edge_grads_to_cubics(v_edges: torch.Tensor, num_segments: int, samples: int,
@@ -550,93 +323,134 @@ def _validate_common(num_primitives, num_segments, offs, colors, opacities, dept
             f"depths size must match primitive count ({num_primitives}), got {int(depths.reshape(-1).shape[0])}")
 
 
+def _background(background, device) -> torch.Tensor:
+    bg = background
+    if bg.device != device or bg.dtype != torch.float32:
+        bg = bg.to(device=device, dtype=torch.float32)
+    return bg.reshape(3) if bg.is_contiguous() else bg.contiguous().reshape(3)
+
+
+def _backward_common(ctx, grad_out, colors, opac, raw, widths, bg, fts, fidx, extra_post=None):
+    """Backward of both renderers: one binding call without a process_fn;
+    with one, the reference's pre/post hook stages around the raster
+    backward (cubic_splatting.py:3014-3091)."""
+    b = ctx.binning
+    p = int(colors.shape[0])
+    half_w, half_h = 0.5 * float(ctx.img_w), 0.5 * float(ctx.img_h)
+    process_fn = ctx.process_fn
+    if process_fn is None:
+        v_cubics_norm, v_colors, v_opac, v_aa, v_sw = _ext.load().render_backward(
+            b, p, ctx.num_segments, bg, fts, fidx, grad_out, raw, widths, ctx.img_h, ctx.img_w,
+            half_w, half_h)
+        return v_cubics_norm, v_colors, v_opac, v_aa, v_sw
+    pre = _run_process_fn(process_fn, "pre_backward_rasterize", {
+        "collect_curve_contrib_rgb": False,
+        "collect_curve_isect_contrib": False,
+        "num_primitives": p,
+        "colors": colors,
+    })
+    cc = bool(pre.get("collect_curve_contrib_rgb", False))
+    ci = bool(pre.get("collect_curve_isect_contrib", False))
+    v_edges, v_colors, v_opac, v_inv, v_sw, contrib, icontrib = raster_backward(
+        b, p, bg, fts, fidx, grad_out, ctx.img_h, ctx.img_w, collect_contrib=cc,
+        collect_isect_contrib=ci)
+    v_cubics_px = binning_edge_grads(b, v_edges, ctx.num_segments)
+    payload = {
+        "v_cubics_px": v_cubics_px, "v_colors": v_colors, "v_opacity": v_opac,
+        "curve_contrib_rgb": contrib, "curve_isect_contrib": icontrib,
+        "primitive_ids_sorted": b.prim_ids_sorted, "tile_bins": b.tile_bins,
+        "colors": colors, "opacities": opac, "primitive_seg_offsets": ctx.offs,
+    }
+    if extra_post:
+        payload.update(extra_post(v_sw))
+    post = _run_process_fn(process_fn, "post_backward_rasterize", payload)
+    v_cubics_px = post["v_cubics_px"]
+    v_colors = post["v_colors"]
+    v_opac = post["v_opacity"]
+    if b.stroke:
+        v_sw = post["v_stroke"]
+    v_cubics_norm = torch.empty(v_cubics_px.shape, dtype=torch.float32, device=v_cubics_px.device)
+    v_cubics_norm[..., 0] = v_cubics_px[..., 0] * half_w
+    v_cubics_norm[..., 1] = v_cubics_px[..., 1] * half_h
+    v_aa = _aa_widths_grad(raw, widths, v_inv)
+    return v_cubics_norm, v_colors, v_opac, v_aa, v_sw
+
+
+def _forward_common(ctx, cubics_norm, offs, col, op, depths, rules, sw, raw, background, img_h,
+                    img_w, aabb_pad, aniso, distance_samples, method, process_fn, tile_rows):
+    dev = cubics_norm.device
+    bg = _background(background, dev)
+    h, w = int(img_h), int(img_w)
+    ctx.img_h, ctx.img_w = h, w
+    s = max(2, int(distance_samples))
+    r0, r1 = (0, -1) if tile_rows is None else (int(tile_rows[0]), int(tile_rows[1]))
+    out, fts, fidx, b, widths, _ = _ext.load().render_forward(
+        cubics_norm, offs, col, op, depths, rules, sw, raw, bg, bernstein_basis(s, dev), h, w, s,
+        float(aabb_pad), bool(aniso), r0, r1, method == CUBIC_FLATTEN_METHOD_DE_CASTELJAU)
+    if b.num_intersects == 0:
+        ctx.empty = True
+        return out, None
+    ctx.empty = False
+    ctx.binning = b
+    ctx.process_fn = process_fn
+    ctx.num_segments = int(cubics_norm.shape[0])
+    ctx.offs = offs
+    return out, (widths, bg, fts, fidx)
+
+
 class CubicFillSplatFunction(torch.autograd.Function):
-    """Closed-fill renderer (mirrors _CubicFillSplatFunction, cubic_splatting.py:2750-3125)."""
+    """Closed-fill renderer (mirrors _CubicFillSplatFunction, cubic_splatting.py:2750-3125).
+    ``_checked`` (internal) marks arguments already validated and coerced by
+    ``render_cubic_fill_splat``."""
 
     @staticmethod
     def forward(ctx, cubics_norm, primitive_seg_offsets, colors, opacities, depths, fill_rules,
                 img_h, img_w, block_x, block_y, background, project_threads, map_threads,
                 aabb_pad, aniso_intersects, aa_widths, distance_samples,
-                flatten_method=DEFAULT_CUBIC_FLATTEN_METHOD, process_fn=None, tile_rows=None):
-        nat.require_cuda(cubics_norm, "cubics_norm")
-        method = normalize_cubic_flatten_method(flatten_method)
-        _check_block(block_x, block_y)
-        num_segments = int(cubics_norm.shape[0])
-        offs = _i32(primitive_seg_offsets).view(-1)
-        num_primitives = max(0, int(offs.numel()) - 1)
-        bg = background.to(device=cubics_norm.device, dtype=torch.float32).view(3).contiguous()
-        ctx.img_h, ctx.img_w = int(img_h), int(img_w)
-        if num_primitives <= 0:
-            ctx.empty = True
-            return _empty_image(bg, img_h, img_w)
-        _validate_common(num_primitives, num_segments, offs, colors, opacities, depths)
-        if int(fill_rules.reshape(-1).shape[0]) != num_primitives:
-            raise ValueError(
-                f"fill_rules size must match primitive count ({num_primitives}), got {int(fill_rules.reshape(-1).shape[0])}")
-        raw = _f32(aa_widths.to(device=cubics_norm.device, dtype=torch.float32).reshape(-1))
-        if int(raw.numel()) != num_primitives:
-            raise ValueError(
-                f"aa_widths size must match primitive count ({num_primitives}), got {int(raw.numel())}")
-        widths, inv_s2 = _aa_widths(raw)
-        col = _f32(colors)
-        op = _f32(opacities).view(-1)
-        rules = _i32(fill_rules).view(-1)
-        b = bin_primitives(cubics_norm, offs, depths.reshape(-1), widths, int(img_h), int(img_w),
-                           int(distance_samples), colors=col, opacities=op, inv_sigma2s=inv_s2,
-                           fill_rules=rules, aabb_pad=float(aabb_pad),
-                           aniso=bool(aniso_intersects), tile_rows=tile_rows,
-                           flatten_method=method)
-        if b.num_intersects <= 0:
-            ctx.empty = True
-            return _empty_image(bg, img_h, img_w)
-        out, fts, fidx = forward_raster(b, bg, int(img_h), int(img_w))
-        ctx.empty = False
-        ctx.binning = b
-        ctx.process_fn = process_fn
-        ctx.num_segments = num_segments
-        ctx.save_for_backward(cubics_norm, offs, col, op, rules, raw, widths, inv_s2, bg, fts, fidx)
+                flatten_method=DEFAULT_CUBIC_FLATTEN_METHOD, process_fn=None, tile_rows=None,
+                _checked=False):
+        if _checked:
+            method, offs, col, op, rules, raw = (flatten_method, primitive_seg_offsets, colors,
+                                                 opacities, fill_rules, aa_widths)
+            dep = depths
+        else:
+            nat.require_cuda(cubics_norm, "cubics_norm")
+            method = normalize_cubic_flatten_method(flatten_method)
+            _check_block(block_x, block_y)
+            num_segments = int(cubics_norm.shape[0])
+            offs = _i32(primitive_seg_offsets).view(-1)
+            num_primitives = max(0, int(offs.numel()) - 1)
+            if num_primitives <= 0:
+                ctx.empty = True
+                return _empty_image(_background(background, cubics_norm.device), img_h, img_w)
+            _validate_common(num_primitives, num_segments, offs, colors, opacities, depths)
+            if int(fill_rules.reshape(-1).shape[0]) != num_primitives:
+                raise ValueError(
+                    f"fill_rules size must match primitive count ({num_primitives}), got {int(fill_rules.reshape(-1).shape[0])}")
+            raw = _f32(aa_widths.to(device=cubics_norm.device, dtype=torch.float32).reshape(-1))
+            if int(raw.numel()) != num_primitives:
+                raise ValueError(
+                    f"aa_widths size must match primitive count ({num_primitives}), got {int(raw.numel())}")
+            col = _f32(colors)
+            op = _f32(opacities).view(-1)
+            rules = _i32(fill_rules).view(-1)
+            dep = _f32(depths.reshape(-1))
+        out, keep = _forward_common(ctx, cubics_norm, offs, col, op, dep, rules, None, raw,
+                                    background, img_h, img_w, aabb_pad, aniso_intersects,
+                                    distance_samples, method, process_fn, tile_rows)
+        if keep is not None:
+            widths, bg, fts, fidx = keep
+            ctx.save_for_backward(col, op, raw, widths, bg, fts, fidx)
         return out
 
     @staticmethod
     def backward(ctx, grad_out):
-        nones = (None,) * 20
         if getattr(ctx, "empty", False):
-            return nones
-        cubics_norm, offs, colors, opac, rules, raw, widths, inv_s2, bg, fts, fidx = \
-            ctx.saved_tensors
-        b: Binning = ctx.binning
-        process_fn = ctx.process_fn
-        pre = _run_process_fn(process_fn, "pre_backward_rasterize", {
-            "collect_curve_contrib_rgb": False,
-            "collect_curve_isect_contrib": False,
-            "num_primitives": int(colors.shape[0]),
-            "colors": colors,
-        })
-        cc = bool(pre.get("collect_curve_contrib_rgb", False))
-        ci = bool(pre.get("collect_curve_isect_contrib", False))
-        v_edges, v_colors, v_opac, v_inv, _, contrib, icontrib = raster_backward(
-            b, int(colors.shape[0]), bg, fts, fidx, grad_out, ctx.img_h, ctx.img_w,
-            collect_contrib=cc, collect_isect_contrib=ci)
-        half_w, half_h = 0.5 * float(ctx.img_w), 0.5 * float(ctx.img_h)
-        if process_fn is None:
-            v_cubics_norm = binning_edge_grads(b, v_edges, ctx.num_segments,
-                                               (half_w, half_h))
-        else:
-            v_cubics_px = binning_edge_grads(b, v_edges, ctx.num_segments)
-            post = _run_process_fn(process_fn, "post_backward_rasterize", {
-                "v_cubics_px": v_cubics_px, "v_colors": v_colors, "v_opacity": v_opac,
-                "curve_contrib_rgb": contrib, "curve_isect_contrib": icontrib,
-                "primitive_ids_sorted": b.prim_ids_sorted, "tile_bins": b.tile_bins,
-                "colors": colors, "opacities": opac, "primitive_seg_offsets": offs,
-            })
-            v_cubics_px = post["v_cubics_px"]
-            v_colors = post["v_colors"]
-            v_opac = post["v_opacity"]
-            v_cubics_norm = torch.empty_like(cubics_norm, dtype=torch.float32)
-            v_cubics_norm[..., 0] = v_cubics_px[..., 0] * half_w
-            v_cubics_norm[..., 1] = v_cubics_px[..., 1] * half_h
-        v_aa = _aa_widths_grad(raw, widths, v_inv)
-        out = [None] * 20
+            return (None,) * 21
+        colors, opac, raw, widths, bg, fts, fidx = ctx.saved_tensors
+        v_cubics_norm, v_colors, v_opac, v_aa, _ = _backward_common(
+            ctx, grad_out, colors, opac, raw, widths, bg, fts, fidx)
+        out = [None] * 21
         out[0] = v_cubics_norm
         out[2] = v_colors
         out[3] = v_opac.view_as(opac)
@@ -653,86 +467,49 @@ class CubicPolylineSplatFunction(torch.autograd.Function):
     def forward(ctx, cubics_norm, primitive_seg_offsets, colors, opacities, stroke_widths, depths,
                 img_h, img_w, block_x, block_y, background, project_threads, map_threads,
                 aabb_pad, aniso_intersects, aa_widths, distance_samples,
-                flatten_method=DEFAULT_CUBIC_FLATTEN_METHOD, process_fn=None, tile_rows=None):
-        nat.require_cuda(cubics_norm, "cubics_norm")
-        method = normalize_cubic_flatten_method(flatten_method)
-        _check_block(block_x, block_y)
-        num_segments = int(cubics_norm.shape[0])
-        offs = _i32(primitive_seg_offsets).view(-1)
-        num_primitives = max(0, int(offs.numel()) - 1)
-        bg = background.to(device=cubics_norm.device, dtype=torch.float32).view(3).contiguous()
-        ctx.img_h, ctx.img_w = int(img_h), int(img_w)
-        if num_primitives <= 0:
-            ctx.empty = True
-            return _empty_image(bg, img_h, img_w)
-        _validate_common(num_primitives, num_segments, offs, colors, opacities, depths,
-                         stroke_widths=stroke_widths)
-        raw = _f32(aa_widths.to(device=cubics_norm.device, dtype=torch.float32).reshape(-1))
-        if int(raw.numel()) != num_primitives:
-            raise ValueError(
-                f"aa_widths size must match primitive count ({num_primitives}), got {int(raw.numel())}")
-        widths, inv_s2 = _aa_widths(raw)
-        sw = _f32(stroke_widths).view(-1)
-        col = _f32(colors)
-        op = _f32(opacities).view(-1)
-        b = bin_primitives(cubics_norm, offs, depths.reshape(-1), widths, int(img_h), int(img_w),
-                           int(distance_samples), colors=col, opacities=op, inv_sigma2s=inv_s2,
-                           stroke_widths=sw, aabb_pad=float(aabb_pad),
-                           aniso=bool(aniso_intersects), tile_rows=tile_rows,
-                           flatten_method=method)
-        if b.num_intersects <= 0:
-            ctx.empty = True
-            return _empty_image(bg, img_h, img_w)
-        out, fts, fidx = forward_raster(b, bg, int(img_h), int(img_w))
-        ctx.empty = False
-        ctx.binning = b
-        ctx.process_fn = process_fn
-        ctx.num_segments = num_segments
-        ctx.save_for_backward(cubics_norm, offs, col, op, sw, raw, widths, inv_s2, bg, fts, fidx)
+                flatten_method=DEFAULT_CUBIC_FLATTEN_METHOD, process_fn=None, tile_rows=None,
+                _checked=False):
+        if _checked:
+            method, offs, col, op, sw, raw = (flatten_method, primitive_seg_offsets, colors,
+                                              opacities, stroke_widths, aa_widths)
+            dep = depths
+        else:
+            nat.require_cuda(cubics_norm, "cubics_norm")
+            method = normalize_cubic_flatten_method(flatten_method)
+            _check_block(block_x, block_y)
+            num_segments = int(cubics_norm.shape[0])
+            offs = _i32(primitive_seg_offsets).view(-1)
+            num_primitives = max(0, int(offs.numel()) - 1)
+            if num_primitives <= 0:
+                ctx.empty = True
+                return _empty_image(_background(background, cubics_norm.device), img_h, img_w)
+            _validate_common(num_primitives, num_segments, offs, colors, opacities, depths,
+                             stroke_widths=stroke_widths)
+            raw = _f32(aa_widths.to(device=cubics_norm.device, dtype=torch.float32).reshape(-1))
+            if int(raw.numel()) != num_primitives:
+                raise ValueError(
+                    f"aa_widths size must match primitive count ({num_primitives}), got {int(raw.numel())}")
+            sw = _f32(stroke_widths).view(-1)
+            col = _f32(colors)
+            op = _f32(opacities).view(-1)
+            dep = _f32(depths.reshape(-1))
+        out, keep = _forward_common(ctx, cubics_norm, offs, col, op, dep, None, sw, raw,
+                                    background, img_h, img_w, aabb_pad, aniso_intersects,
+                                    distance_samples, method, process_fn, tile_rows)
+        if keep is not None:
+            widths, bg, fts, fidx = keep
+            ctx.save_for_backward(col, op, sw, raw, widths, bg, fts, fidx)
         return out
 
     @staticmethod
     def backward(ctx, grad_out):
-        nones = (None,) * 20
         if getattr(ctx, "empty", False):
-            return nones
-        cubics_norm, offs, colors, opac, sw, raw, widths, inv_s2, bg, fts, fidx = \
-            ctx.saved_tensors
-        b: Binning = ctx.binning
-        process_fn = ctx.process_fn
-        pre = _run_process_fn(process_fn, "pre_backward_rasterize", {
-            "collect_curve_contrib_rgb": False,
-            "collect_curve_isect_contrib": False,
-            "num_primitives": int(colors.shape[0]),
-            "colors": colors,
-        })
-        cc = bool(pre.get("collect_curve_contrib_rgb", False))
-        ci = bool(pre.get("collect_curve_isect_contrib", False))
-        v_edges, v_colors, v_opac, v_inv, v_sw, contrib, icontrib = raster_backward(
-            b, int(colors.shape[0]), bg, fts, fidx, grad_out, ctx.img_h, ctx.img_w,
-            collect_contrib=cc, collect_isect_contrib=ci)
-        half_w, half_h = 0.5 * float(ctx.img_w), 0.5 * float(ctx.img_h)
-        if process_fn is None:
-            v_cubics_norm = binning_edge_grads(b, v_edges, ctx.num_segments,
-                                               (half_w, half_h))
-        else:
-            v_cubics_px = binning_edge_grads(b, v_edges, ctx.num_segments)
-            post = _run_process_fn(process_fn, "post_backward_rasterize", {
-                "v_cubics_px": v_cubics_px, "v_colors": v_colors, "v_opacity": v_opac,
-                "v_stroke": v_sw, "curve_contrib_rgb": contrib, "curve_isect_contrib": icontrib,
-                "primitive_ids_sorted": b.prim_ids_sorted, "tile_bins": b.tile_bins,
-                "colors": colors, "opacities": opac, "stroke_widths": sw,
-                "primitive_seg_offsets": offs,
-            })
-            v_cubics_px = post["v_cubics_px"]
-            v_colors = post["v_colors"]
-            v_opac = post["v_opacity"]
-            v_sw = post["v_stroke"]
-            v_cubics_norm = torch.empty_like(cubics_norm, dtype=torch.float32)
-            v_cubics_norm[..., 0] = v_cubics_px[..., 0] * half_w
-            v_cubics_norm[..., 1] = v_cubics_px[..., 1] * half_h
-        v_aa = _aa_widths_grad(raw, widths, v_inv)
-        out = [None] * 20
+            return (None,) * 21
+        colors, opac, sw, raw, widths, bg, fts, fidx = ctx.saved_tensors
+        v_cubics_norm, v_colors, v_opac, v_aa, v_sw = _backward_common(
+            ctx, grad_out, colors, opac, raw, widths, bg, fts, fidx,
+            extra_post=lambda v: {"v_stroke": v, "stroke_widths": sw})
+        out = [None] * 21
         out[0] = v_cubics_norm
         out[2] = v_colors
         out[3] = v_opac.view_as(opac)
@@ -780,11 +557,13 @@ def render_cubic_fill_splat(cubics_norm, primitive_seg_offsets, colors, opacitie
     widths = _f32(_prim_param(aa_widths, aa_width, num_primitives, dev, torch.float32,
                               "aa_widths"))
     method = normalize_cubic_flatten_method(flatten_method)
+    nat.require_cuda(cubics_norm, "cubics_norm")
+    _check_block(block_x, block_y)
     return CubicFillSplatFunction.apply(
-        cubics_norm, offs.contiguous(), colors.contiguous(), opacities.reshape(-1).contiguous(),
-        depths.reshape(-1).contiguous(), rules.contiguous(), int(img_h), int(img_w), int(block_x),
-        int(block_y), background, int(project_threads), int(map_threads), float(aabb_pad),
-        bool(aniso_intersects), widths, int(distance_samples), method, process_fn, tile_rows)
+        cubics_norm, offs, _f32(colors), _f32(opacities.reshape(-1)), _f32(depths.reshape(-1)),
+        _i32(rules), int(img_h), int(img_w), int(block_x), int(block_y), background,
+        int(project_threads), int(map_threads), float(aabb_pad), bool(aniso_intersects), widths,
+        int(distance_samples), method, process_fn, tile_rows, True)
 
 
 def render_cubic_polyline_splat(cubics_norm, primitive_seg_offsets, colors, opacities,
@@ -810,9 +589,11 @@ def render_cubic_polyline_splat(cubics_norm, primitive_seg_offsets, colors, opac
     widths = _f32(_prim_param(aa_widths, aa_width, num_primitives, dev, torch.float32,
                               "aa_widths"))
     method = normalize_cubic_flatten_method(flatten_method)
+    nat.require_cuda(cubics_norm, "cubics_norm")
+    _check_block(block_x, block_y)
     return CubicPolylineSplatFunction.apply(
-        cubics_norm, offs.contiguous(), colors.contiguous(), opacities.reshape(-1).contiguous(),
-        stroke_widths.reshape(-1).contiguous(), depths.reshape(-1).contiguous(), int(img_h),
-        int(img_w), int(block_x), int(block_y), background, int(project_threads),
-        int(map_threads), float(aabb_pad), bool(aniso_intersects), widths,
-        int(distance_samples), method, process_fn, tile_rows)
+        cubics_norm, offs, _f32(colors), _f32(opacities.reshape(-1)),
+        _f32(stroke_widths.reshape(-1)), _f32(depths.reshape(-1)), int(img_h), int(img_w),
+        int(block_x), int(block_y), background, int(project_threads), int(map_threads),
+        float(aabb_pad), bool(aniso_intersects), widths, int(distance_samples), method,
+        process_fn, tile_rows, True)

@@ -152,6 +152,21 @@ class FillTrainer:
         self._fork = torch.cuda.Event()
         self._join = torch.cuda.Event()
         self.launches_per_step = 7 + (1 if self.with_ssim else 0)
+        self._timing = None  # CUDA events around the raster launches (enable_kernel_timing)
+
+    def enable_kernel_timing(self):
+        """Record timing events around the forward and backward raster
+        launches, also inside a captured graph (external events, so that each
+        replay re-records them): kernel_times() reads the last step's."""
+        self._timing = tuple(torch.cuda.Event(enable_timing=True, external=True)
+                             for _ in range(4))
+
+    def kernel_times(self) -> tuple[float, float]:
+        """(forward, backward) raster launch times of the last step in ms
+        (after enable_kernel_timing; synchronises)."""
+        ev = self._timing
+        ev[3].synchronize()
+        return ev[0].elapsed_time(ev[1]), ev[2].elapsed_time(ev[3])
 
     # ------------------------------------------------------------------
     def _bin(self, capacity: int, dcapacity: int, st):
@@ -194,6 +209,9 @@ class FillTrainer:
                            self.imeta.data_ptr(), self.rowoff.data_ptr(), self.istrips.data_ptr(),
                            self.dlist.data_ptr(), self.dcapacity, self.unit_order.data_ptr(), st),
                   "cs_bin_sort")
+        ev = self._timing
+        if ev is not None:
+            ev[0].record()
         nat.check(nat.call("cs_fill_forward", self.prim_sorted.data_ptr(),
                            self.tile_bins.data_ptr(), self.tile_dlist.data_ptr(),
                            self.imeta.data_ptr(), self.istrips.data_ptr(), self.rowoff.data_ptr(),
@@ -205,6 +223,8 @@ class FillTrainer:
                            self.img_chw.data_ptr(), self.target.data_ptr(), self.loss.data_ptr(),
                            status, self.raster_ws.data_ptr(), self.h, self.w, r0, r1, st),
                   "cs_fill_forward")
+        if ev is not None:
+            ev[1].record()
         if self.with_ssim:
             # SSIM needs only the forward's image: it runs on a side stream
             # beside the backward and fills the SMs the backward leaves idle
@@ -216,6 +236,8 @@ class FillTrainer:
                                self.ssim_planes.data_ptr(), None, self.ssim_ws.data_ptr(),
                                self._side.cuda_stream), "cs_ssim")
             self._join.record(self._side)
+        if ev is not None:
+            ev[2].record()
         nat.check(nat.call("cs_fill_backward", self.prim_sorted.data_ptr(),
                            self.tile_bins.data_ptr(), self.tile_dlist.data_ptr(),
                            self.imeta.data_ptr(), self.istrips.data_ptr(), self.rowoff.data_ptr(),
@@ -228,6 +250,8 @@ class FillTrainer:
                            self.v_edges.data_ptr(), self.v_colors.data_ptr(), None, None, None,
                            None, status, self.raster_ws.data_ptr(), self.h, self.w, r0, r1, st),
                   "cs_fill_backward")
+        if ev is not None:
+            ev[3].record()
         nat.check(nat.call("cs_edge_grads_to_ring", self.v_edges.data_ptr(),
                            self.v_ring.data_ptr(), self.num_paths, self.g_per_path, self.s - 1,
                            self.h, self.w, 1, self.prim_ranges.data_ptr(), r0, r1, st),

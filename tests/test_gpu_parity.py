@@ -422,7 +422,6 @@ def test_unit_lists_bucket_every_strip_by_work_and_change_no_result(rows):
     """The staging pass files the band's strips (4 per tile) into 64 buckets of
     staged work, heaviest first; the lists only schedule the raster warps, so
     results match the launch without them."""
-    import dataclasses
     sc = scenes.config1()
     args = fill_inputs(sc)
     h, w = args[5], args[6]
@@ -460,7 +459,7 @@ def test_unit_lists_bucket_every_strip_by_work_and_change_no_result(rows):
     assert bl[:64].sum() == nunits
     seen_b = np.concatenate([bl[64 + bk * nunits: 64 + bk * nunits + bl[bk]] for bk in range(64)])
     assert sorted(seen_b.tolist()) == list(range(nunits))
-    plain = dataclasses.replace(b, unit_order=None, unit_order_bwd=None)
+    plain = render.replace_binning(b, unit_order=None, unit_order_bwd=None)
     out2, fts2, fidx2 = render.forward_raster(plain, _t(args[7], torch.float32), h, w)
     band = slice(r0 * 16, min(h, r1 * 16))  # rows outside the band are not written
     assert torch.equal(out[band], out2[band]) and torch.equal(fts[band], fts2[band])
@@ -522,7 +521,6 @@ def test_visit_lists_walk_only_composited_intersects(stroke):
     """The forward lists, per strip, the intersects that composited a pixel of
     it; the backward walks only those and its gradients match the walk over
     every intersect up to final_idx."""
-    import dataclasses
     if stroke:
         b, bg, p, out, fts, fidx = _stroke_binning()
         h = w = 256
@@ -533,7 +531,7 @@ def test_visit_lists_walk_only_composited_intersects(stroke):
         bg, p = _t(args[7], torch.float32), int(np.asarray(args[2]).shape[0])
     assert _check_visit_lists(b, fidx, h, w) > 0
     v_out = _t(np.asarray(scenes.seeded_grad(9, h, w), np.float32))
-    plain = dataclasses.replace(b, visit_lists=None)
+    plain = render.replace_binning(b, visit_lists=None)
     g1 = render.raster_backward(b, p, bg, fts, fidx, v_out, h, w, collect_contrib=True,
                                 collect_isect_contrib=True)
     g2 = render.raster_backward(plain, p, bg, fts, fidx, v_out, h, w, collect_contrib=True,
@@ -550,7 +548,6 @@ def test_fill_winner_codes_fall_back_and_reject_bad_codes():
     evaluates only each pixel's stored winner gives the gradients of the one
     that walks every record; a code past its intersect's records sets
     CS_ERR_ARG and is ignored (every read stays inside the strip's records)."""
-    import dataclasses
     from repo_b200 import _native as nat
     args = fill_inputs(scenes.config1())
     h, w = args[5], args[6]
@@ -560,7 +557,7 @@ def test_fill_winner_codes_fall_back_and_reject_bad_codes():
     v_out = _t(np.asarray(scenes.seeded_grad(11, h, w), np.float32))
     g1 = render.raster_backward(b, p, bg, fts, fidx, v_out, h, w)
     good = b.visit_winners.clone()
-    g2 = render.raster_backward(dataclasses.replace(b, visit_winners=None), p, bg, fts, fidx,
+    g2 = render.raster_backward(render.replace_binning(b, visit_winners=None), p, bg, fts, fidx,
                                 v_out, h, w)
     assert int(b.counters[1]) == 0
     for name, a, c in zip(["v_edges", "v_colors", "v_opac", "v_inv"], g1, g2):

@@ -14,7 +14,9 @@ L2 is flushed (256 MiB write) before every timed step, outside its events.
 
 Multi-GPU (torchrun, N>1): every rank optimises its own config-2 scene
 (different seed), no collective on the data path; value = all ranks'
-iterations / max over ranks of the device time ("scaling": "weak").
+iterations / max over ranks of the device time ("scaling": "weak").  At every
+N the line also carries ``strong_config3``: the config-3 image split across
+the N ranks in tile-row bands (below), the strong-scaling curve.
 
 --workload config3: one 2040x1356 image with 4096 closed paths x 6 segments
 split across the ranks in tile-row bands balanced by per-row work; every step
@@ -69,6 +71,8 @@ def parse_args(argv=None):
     ap.add_argument("--workload", default="config2",
                     choices=["config2", "config3", "config4", "config5"])
     ap.add_argument("--no-gpu-reference", action="store_true")
+    ap.add_argument("--no-strong", action="store_true",
+                    help="skip the config-3 strong-scaling step of the default workload")
     ap.add_argument("--gpu-reference-child", action="store_true", help=argparse.SUPPRESS)
     return ap.parse_args(argv)
 
@@ -994,6 +998,19 @@ def main(argv=None):
                     print(line, flush=True)
             return 0
         res, tr = run_b200(args, rank, world, local_rank)
+        del tr
+        if not args.no_strong:
+            # config 3 at the same N: one 2040x1356 image in tile-row bands
+            # with a gradient all-reduce per step (strong scaling)
+            sres, btr = run_bands(args, rank, world, local_rank)
+            btr.graph = None  # graphs holding NCCL work go before the process group
+            del btr
+            if rank == 0:
+                res["strong_config3"] = {
+                    k: sres[k] for k in ("metric", "value", "unit", "ms_per_step", "n_gpus",
+                                         "scaling", "final_loss")}
+                res["strong_config3"]["bands"] = sres["config"]["bands"]
+                res["strong_config3"]["clocks"] = sres["clocks"]
         if rank == 0 and world == 1 and not args.no_gpu_reference:
             ref = run_gpu_reference(args)
             res["gpu_reference"] = ref
@@ -1012,7 +1029,6 @@ def main(argv=None):
                           f"(C oracle, {cores} threads)"}
         if rank == 0:
             print(json.dumps(res), flush=True)
-        del tr
     finally:
         if world > 1:
             dist.barrier()

@@ -3,10 +3,10 @@
 Same module paths and names as the reference's ``manbo`` (manbo/__init__.py:1-29)
 for the render/optimise hot path: the cubic fill and stroke renderers, their
 per-stage operators, the ring-segment conversion, the MSE / PSNR / SSIM
-metrics and the Adan optimiser that train.py uses by default.  Subsystems
-outside that path (Gaussian renderer, regularisation, connected components)
-keep their names so that imports succeed, and raise NotImplementedError when
-called.
+metrics, the Adan optimiser that train.py uses by default, the regularisation
+loss and the connected-component labelling.  The Gaussian renderer, outside
+that path, keeps its names so that imports succeed, and raises
+NotImplementedError when called.
 """
 import importlib.util as _ilu
 import pkgutil as _pkgutil

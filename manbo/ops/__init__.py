@@ -1,13 +1,19 @@
 """``manbo.ops`` with the reference's exported names (manbo/ops/__init__.py:45-176).
 
 Hot-path operators (cubic fill / stroke renderer stages, tile bins, ring
-segments, metric kernels) run on the B200 sm_100a kernels.  The Gaussian
-renderer, regularisation and connected-components operators are outside the
-B200 hot path: their names exist so imports succeed, and calling them raises
-NotImplementedError.  The Adan step (train.py's default optimiser) runs on
-its own B200 kernel.
+segments, metric kernels) run on the B200 sm_100a kernels, and so do the Adan
+step (train.py's default optimiser) and the 4-connected component labelling.
+The Gaussian renderer's operators are outside the B200 hot path, and the
+reference's per-term regularisation kernels have no counterpart (one launch
+computes every term of ``manbo.regularization_loss_tilelang``): their names
+exist so imports succeed, and calling them raises NotImplementedError.
 """
 from .._unavailable import unavailable
+from .connected_components import (
+    connected_components_labels_4_tilelang,
+    connected_components_with_stats_4_tilelang,
+    select_largest_component_center,
+)
 from .cubic_polyline_splatting import render_cubic_polyline_splat_tilelang
 from .cubic_splatting import (
     closed_cubic_fill_segments_backward_kernel,
@@ -41,9 +47,6 @@ _OUT_OF_SCOPE = [
     "map_gaussian_meta_to_intersects",
     "rasterize_forward_tilelang",
     "rasterize_backward_tilelang",
-    "connected_components_labels_4_tilelang",
-    "connected_components_with_stats_4_tilelang",
-    "select_largest_component_center",
     "bezier_shape_backward_kernel",
     "bezier_open_backward_kernel",
     "opacity_backward_kernel",
@@ -92,6 +95,9 @@ __all__ = [
     "ssim_map_kernel",
     "reduce_sum_1d_tilelang",
     "adan_step_from_grad_tilelang",
+    "connected_components_labels_4_tilelang",
+    "connected_components_with_stats_4_tilelang",
+    "select_largest_component_center",
     "DEFAULT_REG_THREADS",
     "DEFAULT_REG_ITEMS_PER_THREAD",
 ] + _OUT_OF_SCOPE

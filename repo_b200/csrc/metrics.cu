@@ -136,7 +136,8 @@ __global__ void __launch_bounds__(kSsimThreads, 4) ssim_kernel(
   constexpr int LOADS = (IN * IN + kSsimThreads - 1) / kSsimThreads;
   __shared__ float sx[IN][IN + 1];
   __shared__ float sy[IN][IN + 1];
-  __shared__ float hs[5][IN][kSsimT + 1];
+  __shared__ float2 hp[2][IN][kSsimT + 1];  // (mu_x, mu_y), (E[x^2], E[y^2]) per row
+  __shared__ float h4[IN][kSsimT + 1];       // E[xy]
   __shared__ float g[WIN];
   __shared__ float red[kSsimThreads / 32];
   __shared__ bool last;
@@ -187,33 +188,37 @@ __global__ void __launch_bounds__(kSsimThreads, 4) ssim_kernel(
       active = j < 4 * R;
     }
     if (active) {
+      // (mu_x, mu_y) and (E[x^2], E[y^2]) share their weights: packed FP32x2
+      // multiply-adds, each component rounded as the scalar one
       const int c0 = grp * 8;
-      float m1[8], m2[8], e11[8], e22[8], e12[8];
+      float2 m12[8], e1122[8];
+      float e12[8];
 #pragma unroll
-      for (int o = 0; o < 8; ++o) m1[o] = m2[o] = e11[o] = e22[o] = e12[o] = 0.0f;
+      for (int o = 0; o < 8; ++o) {
+        m12[o] = e1122[o] = make_float2(0.0f, 0.0f);
+        e12[o] = 0.0f;
+      }
 #pragma unroll
       for (int q = 0; q < 8 + R; ++q) {
-        const float u = sx[r][c0 + q], v = sy[r][c0 + q];
-        const float uu = u * u, vv = v * v, uv = u * v;
+        const float2 uv2 = make_float2(sx[r][c0 + q], sy[r][c0 + q]);
+        const float2 sq = __fmul2_rn(uv2, uv2);
+        const float uv = uv2.x * uv2.y;
 #pragma unroll
         for (int o = 0; o < 8; ++o) {
           const int k = q - o;
           if (k >= 0 && k < WIN) {
-            m1[o] = __fmaf_rn(gk[k], u, m1[o]);
-            m2[o] = __fmaf_rn(gk[k], v, m2[o]);
-            e11[o] = __fmaf_rn(gk[k], uu, e11[o]);
-            e22[o] = __fmaf_rn(gk[k], vv, e22[o]);
+            const float2 gg = make_float2(gk[k], gk[k]);
+            m12[o] = __ffma2_rn(gg, uv2, m12[o]);
+            e1122[o] = __ffma2_rn(gg, sq, e1122[o]);
             e12[o] = __fmaf_rn(gk[k], uv, e12[o]);
           }
         }
       }
 #pragma unroll
       for (int o = 0; o < 8; ++o) {
-        hs[0][r][c0 + o] = m1[o];
-        hs[1][r][c0 + o] = m2[o];
-        hs[2][r][c0 + o] = e11[o];
-        hs[3][r][c0 + o] = e22[o];
-        hs[4][r][c0 + o] = e12[o];
+        hp[0][r][c0 + o] = m12[o];
+        hp[1][r][c0 + o] = e1122[o];
+        h4[r][c0 + o] = e12[o];
       }
     }
   }
@@ -224,11 +229,30 @@ __global__ void __launch_bounds__(kSsimThreads, 4) ssim_kernel(
     const int c = lane, r0 = wid * 4;
     float mom[4][5];
 #pragma unroll
-    for (int q = 0; q < 5; ++q) {
+    for (int q = 0; q < 2; ++q) {  // the moment pairs, packed
+      float2 acc[4];
+#pragma unroll
+      for (int o = 0; o < 4; ++o) acc[o] = make_float2(0.0f, 0.0f);
+#pragma unroll
+      for (int t = 0; t < 4 + R; ++t) {
+        const float2 val = hp[q][r0 + t][c];
+#pragma unroll
+        for (int o = 0; o < 4; ++o) {
+          const int k = t - o;
+          if (k >= 0 && k < WIN) acc[o] = __ffma2_rn(make_float2(gk[k], gk[k]), val, acc[o]);
+        }
+      }
+#pragma unroll
+      for (int o = 0; o < 4; ++o) {
+        mom[o][2 * q] = acc[o].x;
+        mom[o][2 * q + 1] = acc[o].y;
+      }
+    }
+    {
       float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
       for (int t = 0; t < 4 + R; ++t) {
-        const float val = hs[q][r0 + t][c];
+        const float val = h4[r0 + t][c];
 #pragma unroll
         for (int o = 0; o < 4; ++o) {
           const int k = t - o;
@@ -236,7 +260,7 @@ __global__ void __launch_bounds__(kSsimThreads, 4) ssim_kernel(
         }
       }
 #pragma unroll
-      for (int o = 0; o < 4; ++o) mom[o][q] = acc[o];
+      for (int o = 0; o < 4; ++o) mom[o][4] = acc[o];
     }
 #pragma unroll
     for (int o = 0; o < 4; ++o) {

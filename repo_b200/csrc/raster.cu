@@ -417,37 +417,56 @@ __device__ __forceinline__ unsigned winner_code(int win, bool inside) {
   return (unsigned)(win < kNoWinner ? win : kNoWinner) | (inside ? 128u : 0u);
 }
 
+// Squared distances of a lane's two pixels (P = (px0, px1), same row py) to
+// the edge of record (A, B): seg_d2's arithmetic on both pixels at once with
+// the packed FP32x2 operations of sm_100 (each component rounded exactly as
+// the scalar operation: px - x0 is px + (-x0), cx - px is cx + (-px)).
+// NP = -P and npy = (-py, -py) are the caller's loop invariants.
+__device__ __forceinline__ float2 seg_d2_pair(float2 P, float2 NP, float2 npy, float wy,
+                                              const float4& A, const float4& B) {
+  const float2 wx = __fadd2_rn(P, make_float2(-A.x, -A.x));
+  const float t = wy * A.w;
+  float2 pr = __ffma2_rn(wx, make_float2(A.z, A.z), make_float2(t, t));
+  pr = __fmul2_rn(pr, make_float2(B.x, B.x));
+  pr.x = fmaxf(0.0f, fminf(1.0f, pr.x));
+  pr.y = fmaxf(0.0f, fminf(1.0f, pr.y));
+  const float2 cx = __ffma2_rn(pr, make_float2(A.z, A.z), make_float2(A.x, A.x));
+  const float2 cy = __ffma2_rn(pr, make_float2(A.w, A.w), make_float2(A.y, A.y));
+  const float2 dx = __fadd2_rn(cx, NP), dy = __fadd2_rn(cy, npy);
+  return __ffma2_rn(dx, dx, __fmul2_rn(dy, dy));
+}
+
 template <bool STROKE>
 __device__ __forceinline__ void fwd_entries(const DEntry* __restrict__ buf, int c0, int ds, int lo,
                                             int hi, float px0, float px1, float py, FwdPix& p0,
                                             FwdPix& p1) {
+  const float2 P = make_float2(px0, px1), NP = make_float2(-px0, -px1);
+  const float2 npy = make_float2(-py, -py);
   for (int d = lo; d < hi; ++d) {
     const float4 EA = buf[d - c0].a;
     const float4 EB = buf[d - c0].b;
     const float wy = py - EA.y;
-    float pr, cx, cy;
+    const float2 d2 = seg_d2_pair(P, NP, npy, wy, EA, EB);
     if (!STROKE) {  // the running minimum and its first record (strict <: the first minimum)
-      const float d20 = seg_d2(px0, py, wy, EA, EB, pr, cx, cy);
-      const float d21 = seg_d2(px1, py, wy, EA, EB, pr, cx, cy);
-      if (d20 < p0.md) {
-        p0.md = d20;
+      if (d2.x < p0.md) {
+        p0.md = d2.x;
         p0.win = d - ds;
       }
-      if (d21 < p1.md) {
-        p1.md = d21;
+      if (d2.y < p1.md) {
+        p1.md = d2.y;
         p1.win = d - ds;
       }
     } else {
-      p0.md = fminf(p0.md, seg_d2(px0, py, wy, EA, EB, pr, cx, cy));
-      p1.md = fminf(p1.md, seg_d2(px1, py, wy, EA, EB, pr, cx, cy));
+      p0.md = fminf(p0.md, d2.x);
+      p1.md = fminf(p1.md, d2.y);
     }
     if (!STROKE) {
       if (((EA.y <= py) & (EB.y > py)) | ((EA.y > py) & (EB.y <= py))) {
         const float lhs = EB.z + wy * EA.z;
-        const float rhs0 = px0 * EA.w, rhs1 = px1 * EA.w;
+        const float2 rhs = __fmul2_rn(P, make_float2(EA.w, EA.w));
         const bool pos = EA.w > 0.0f;
-        const int h0 = pos ? (lhs > rhs0) : (lhs < rhs0);
-        const int h1 = pos ? (lhs > rhs1) : (lhs < rhs1);
+        const int h0 = pos ? (lhs > rhs.x) : (lhs < rhs.x);
+        const int h1 = pos ? (lhs > rhs.y) : (lhs < rhs.y);
         const int sg = pos ? 1 : -1;
         p0.n += h0;
         p1.n += h1;
@@ -718,14 +737,16 @@ struct BwdPix {
 template <bool STROKE, bool TIES>
 __device__ __forceinline__ void bwd_entries(const DEntry* __restrict__ buf, int c0, int lo, int hi,
                                             const float px[2], float py, BwdPix s[2]) {
+  const float2 P = make_float2(px[0], px[1]), NP = make_float2(-px[0], -px[1]);
+  const float2 npy = make_float2(-py, -py);
   for (int d = lo; d < hi; ++d) {
     const float4 EA = buf[d - c0].a;
     const float4 EB = buf[d - c0].b;
     const float wy = py - EA.y;
+    const float2 dd = seg_d2_pair(P, NP, npy, wy, EA, EB);
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
-      float pr, cx, cy;
-      const float d2 = seg_d2(px[u], py, wy, EA, EB, pr, cx, cy);
+      const float d2 = u ? dd.y : dd.x;
       bool take = d2 < s[u].md;
       if (TIES) {
         const int eid = __float_as_int(EB.w);
@@ -742,9 +763,10 @@ __device__ __forceinline__ void bwd_entries(const DEntry* __restrict__ buf, int 
         const float lhs = EB.z + wy * EA.z;
         const bool pos = EA.w > 0.0f;
         const int sg = pos ? 1 : -1;
+        const float2 rr = __fmul2_rn(P, make_float2(EA.w, EA.w));
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
-          const float rhs = px[u] * EA.w;
+          const float rhs = u ? rr.y : rr.x;
           const int h = pos ? (lhs > rhs) : (lhs < rhs);
           s[u].n += h;
           s[u].w += h * sg;
@@ -897,26 +919,14 @@ __device__ __forceinline__ void flush_acc(const RasterArgs& A, int pid, int k, i
   else if (A.icontrib) atomicAdd(A.icontrib + k, v);
 }
 
-// Backward of one unit by one warp.  Returns false if a bounded wait gave up.
-template <bool STROKE>
-__device__ __forceinline__ bool backward_unit(const RasterArgs& A, int unit,
-                                              DEntry (*buf)[kWChunk], uint64_t* bars,
-                                              uint32_t& phase, float4* dgrad, IBatch& ib) {
-  const int lane = threadIdx.x & 31;
-  const UnitGeom g = unit_geom(A, unit);
-  const int rs = g.rs, re = g.re, st = g.st;
-  if (re <= rs) return true;
-  const int ly = st * kStripRows + (lane >> 3), lx = (lane & 7) * 2;
-  const int i = g.ty * kTile + ly, j0 = g.tx * kTile + lx;
-  const float py = (float)i + 0.5f;
-  const float px[2] = {(float)j0 + 0.5f, (float)(j0 + 1) + 0.5f};
-  const bool collect = (A.contrib != nullptr) | (A.icontrib != nullptr);
+// Per-pixel state of a backward strip: T, final_idx and the image gradient
+// (given, or the MSE gradient from the image and the target), with paired
+// 8-byte loads when both pixels are in the image.  Returns the warp's last
+// needed intersect (the largest final_idx, at most re - 1).
+__device__ __forceinline__ int bwd_setup(const RasterArgs& A, int i, int j0, int re,
+                                         BwdPix s[2]) {
   const float scale = A.v_out ? 0.0f : *A.mse_scale;
-  BwdPix s[2];
   int kmax = -1;
-  // per-pixel inputs: T, final_idx and the image gradient (given, or the MSE
-  // gradient from the image and the target), paired 8-byte loads when both
-  // pixels are in the image
   const bool in2[2] = {i < A.H && j0 < A.W, i < A.H && j0 + 1 < A.W};
   float T2[2] = {1.0f, 1.0f}, vv[2][3] = {{0.f, 0.f, 0.f}, {0.f, 0.f, 0.f}};
   int F2[2] = {-1, -1};
@@ -979,7 +989,25 @@ __device__ __forceinline__ bool backward_unit(const RasterArgs& A, int unit,
     if (in2[u]) kmax = max(kmax, s[u].fidx);
     s[u].Tf = s[u].T;
   }
-  kmax = min(warp_max_i(kmax), re - 1);  // this warp's last needed intersect
+  return min(warp_max_i(kmax), re - 1);  // this warp's last needed intersect
+}
+
+// Backward of one unit by one warp.  Returns false if a bounded wait gave up.
+template <bool STROKE>
+__device__ __forceinline__ bool backward_unit(const RasterArgs& A, int unit,
+                                              DEntry (*buf)[kWChunk], uint64_t* bars,
+                                              uint32_t& phase, float4* dgrad, IBatch& ib) {
+  const int lane = threadIdx.x & 31;
+  const UnitGeom g = unit_geom(A, unit);
+  const int rs = g.rs, re = g.re, st = g.st;
+  if (re <= rs) return true;
+  const int ly = st * kStripRows + (lane >> 3), lx = (lane & 7) * 2;
+  const int i = g.ty * kTile + ly, j0 = g.tx * kTile + lx;
+  const float py = (float)i + 0.5f;
+  const float px[2] = {(float)j0 + 0.5f, (float)(j0 + 1) + 0.5f};
+  const bool collect = (A.contrib != nullptr) | (A.icontrib != nullptr);
+  BwdPix s[2];
+  int kmax = bwd_setup(A, i, j0, re, s);
   if (kmax < rs) return true;
   // The walk runs over positions q = nq - 1 .. 0: every intersect rs .. kmax
   // (position q is intersect rs + q), or the forward's list of the strip's
@@ -1176,6 +1204,142 @@ __device__ __forceinline__ bool backward_unit(const RasterArgs& A, int unit,
   return ok;
 }
 
+// Fill backward of one unit from the forward's visit list and winner codes,
+// with nothing staged: every listed visit evaluates, per pixel, only the
+// closest record the forward found (read from global memory; the records of
+// one intersect sit together), and the warp's edge-gradient sums per distinct
+// winner go straight to v_edges.  An edge record belongs to one intersect, so
+// a strip visits it at most once and a shared accumulator would save no
+// atomics.  A pixel without a representable code (an intersect with more
+// than 127 records in the strip) walks that intersect's records in order
+// (strict <: the reference's first minimum); the code's inside bit holds the
+// pixel's crossing state either way.
+__device__ __forceinline__ bool backward_unit_direct(const RasterArgs& A, int unit, IBatch& ib) {
+  const int lane = threadIdx.x & 31;
+  const UnitGeom g = unit_geom(A, unit);
+  const int rs = g.rs, re = g.re, st = g.st;
+  if (re <= rs) return true;
+  const int ly = st * kStripRows + (lane >> 3), lx = (lane & 7) * 2;
+  const int i = g.ty * kTile + ly, j0 = g.tx * kTile + lx;
+  const float py = (float)i + 0.5f;
+  const float px[2] = {(float)j0 + 0.5f, (float)(j0 + 1) + 0.5f};
+  const bool collect = (A.contrib != nullptr) | (A.icontrib != nullptr);
+  BwdPix s[2];
+  const int kmax = bwd_setup(A, i, j0, re, s);
+  if (kmax < rs) return true;
+  const int* vl = A.visits + visit_base(g);
+  const int cnt = vl[0];
+  if (cnt < 0 || cnt > re - rs) {  // not a list the forward wrote for this strip
+    if (lane == 0 && A.status) atomicExch(A.status, CS_ERR_ARG);
+    return true;
+  }
+  ++vl;
+  const long long wslot = visit_base(g) + 1;  // visit-list slot of position 0
+  const DEntry* dl = A.dl + g.base;
+  int q = cnt - 1;      // next position (walking down)
+  int qb = cnt;         // first position of the batch in shared memory
+  unsigned amask = 0u;  // active intersects of the batch
+  while (q >= 0) {
+    if (q < qb) {
+      qb = max(0, q - 31);
+      amask = load_batch<false>(A, vl + qb, rs + qb, q - qb + 1, st, rs, re, ib);
+    }
+    const int j = q - qb;
+    if (!((amask >> j) & 1u)) {  // skip to the batch's next lower active intersect
+      const unsigned below = amask & ((1u << j) - 1u);
+      q = below ? qb + 31 - __clz(below) : qb - 1;
+      continue;
+    }
+    const int k = ib.kk[j];
+    const bool v0 = s[0].in && k <= s[0].fidx;
+    const bool v1 = s[1].in && k <= s[1].fidx;
+    IMeta m;
+    batch_meta(ib, j, m);
+    const int2 rg = ib.rg[j];
+    const int ds = rg.x, nrec = rg.y;
+    const unsigned wc = __ldg(A.winners + (wslot + q) * 32 + lane);
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const unsigned c = (wc >> (8 * u)) & 255u;
+      const int win = (int)(c & 127u);
+      s[u].w = s[u].n = (int)(c >> 7);
+      s[u].md = 1e30f;
+      s[u].be = -1;
+      s[u].bl = -1;
+      s[u].bp = s[u].bcx = s[u].bcy = 0.0f;
+      if (nrec <= 0 || !(u ? v1 : v0)) continue;
+      int d = ds + win;
+      if (win == kNoWinner) {  // walk the intersect's records (strict <: first minimum)
+        d = -1;
+        for (int e = ds; e < ds + nrec; ++e) {
+          const float4 EA = __ldg(&dl[e].a), EB = __ldg(&dl[e].b);
+          float pr, cx, cy;
+          const float d2 = seg_d2(px[u], py, py - EA.y, EA, EB, pr, cx, cy);
+          if (d2 < s[u].md) {
+            s[u].md = d2;
+            d = e;
+          }
+        }
+        if (d < 0) continue;
+      } else if (win >= nrec) {  // not a code the forward wrote for this intersect
+        if (A.status) atomicExch(A.status, CS_ERR_ARG);
+        continue;
+      }
+      const float4 EA = __ldg(&dl[d].a), EB = __ldg(&dl[d].b);
+      s[u].md = seg_d2(px[u], py, py - EA.y, EA, EB, s[u].bp, s[u].bcx, s[u].bcy);
+      s[u].be = __float_as_int(EB.w);
+    }
+    float acc[kAcc];
+#pragma unroll
+    for (int a = 0; a < kAcc; ++a) acc[a] = 0.0f;
+    bool contributed = false;
+    float4 eg[2];
+    bool has_eg[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u)
+      bwd_pixel<false>(s[u], m, px[u], py, u ? v1 : v0, acc, collect, A.v_opac != nullptr,
+                       A.v_inv != nullptr, eg[u], has_eg[u], contributed);
+    add_edge_grads(A, nullptr, 0, -(s[0].be + 2), has_eg[0], eg[0], -(s[1].be + 2), has_eg[1],
+                   eg[1]);
+    if (__any_sync(0xffffffffu, contributed)) {
+      const int vi = (lane >> 3) & 3;
+      const bool leader = (lane & 7) == 0;
+      float r = warp_reduce4(acc[0], acc[1], acc[2], A.v_opac ? acc[3] : 0.0f);
+      if (leader) flush_acc(A, m.pid, k, vi, r);
+      if (A.v_inv) {
+        r = warp_reduce4(acc[4], 0.0f, 0.0f, 0.0f);
+        if (leader && vi == 0) flush_acc(A, m.pid, k, 4, r);
+      }
+      if (collect) {
+        r = warp_reduce4(acc[6], acc[7], acc[8], acc[9]);
+        if (leader) flush_acc(A, m.pid, k, 6 + vi, r);
+      }
+    }
+    --q;
+  }
+  return true;
+}
+
+// The fill backward over visit lists and winner codes (backward_unit_direct):
+// no record staging, so no record buffers or mbarriers.
+__global__ void __launch_bounds__(kRT) raster_backward_direct_kernel(const RasterArgs A) {
+  __shared__ __align__(16) IBatch sib[kRW];
+  const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int pre0 = 0, pre1 = 0;
+  if (A.order) unit_prefix(A.order, pre0, pre1);
+  int u = blockIdx.x * kRW + wid;
+  while (u < A.nunits) {
+    const int unit = A.order ? unit_at(A.order, A.nunits, u, pre0, pre1) : u;
+    if ((unsigned)unit >= (unsigned)A.nunits) {  // malformed dispatch lists
+      if (lane == 0 && A.status) atomicExch(A.status, CS_ERR_ARG);
+      break;
+    }
+    backward_unit_direct(A, unit, sib[wid]);
+    u = next_unit(A);
+  }
+  finish_launch(A, false);
+}
+
 template <bool STROKE>
 __global__ void __launch_bounds__(kRT) raster_backward_kernel(const RasterArgs A) {
   __shared__ __align__(128) DEntry sbuf[kRW][2][kWChunk];
@@ -1255,6 +1419,9 @@ inline int launch_raster(bool stroke, bool bwd, const RasterArgs& a, int H, int 
   } else if (stroke && !bwd) {
     auto k = raster_forward_kernel<true>;
     k<<<persistent_ctas<1>(k, args.nunits), kRT, 0, st>>>(args);
+  } else if (!stroke && bwd && args.visits && args.winners) {
+    auto k = raster_backward_direct_kernel;
+    k<<<persistent_ctas<4>(k, args.nunits), kRT, 0, st>>>(args);
   } else if (!stroke && bwd) {
     auto k = raster_backward_kernel<false>;
     k<<<persistent_ctas<2>(k, args.nunits), kRT, 0, st>>>(args);

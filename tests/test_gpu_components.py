@@ -97,3 +97,13 @@ def test_largest_component_centre_on_the_gpu_labels():
         torch.from_numpy(mask).to(DEV))
     row, col, label, area, m = comp.select_largest_component_center(lab, stats, centres)
     assert (row, col, label, area) == (3, 4, 2, 25) and int(m.sum()) == 25
+
+
+def test_manbo_names_run_the_kernels():
+    import manbo
+    mask = MASKS["random_64x97_0.55"]
+    t = torch.from_numpy(mask).to(DEV)
+    raw = manbo.ops.connected_components_labels_4_tilelang(t, max_iters=4096, threads=256)
+    np.testing.assert_array_equal(raw.cpu().numpy(), cc.labels_4(mask))
+    n, lab, stats, centres = manbo.ops.connected_components_with_stats_4_tilelang(t)
+    assert n == cc.with_stats_4(mask)[0]

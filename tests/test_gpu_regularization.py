@@ -80,3 +80,17 @@ def test_regularisation_gradient_scales_with_grad_output():
     tcp.grad = None
     regularization_loss(tcp, top, txyz, mode="closed", **KW).backward()
     torch.testing.assert_close(g3, 3.0 * tcp.grad, rtol=1e-6, atol=0)
+
+
+def test_manbo_name_runs_the_kernels():
+    import manbo
+    cp, op, xyz = _scene("closed", 8, 11)
+    tcp = torch.from_numpy(cp).to(DEV).requires_grad_(True)
+    loss = manbo.regularization_loss_tilelang(tcp, torch.from_numpy(op).to(DEV),
+                                              torch.from_numpy(xyz).to(DEV), mode="closed",
+                                              threads=128, items_per_thread=4, **KW)
+    want = reg.regularization_loss(cp.astype(np.float64), op.astype(np.float64),
+                                   xyz.astype(np.float64), mode="closed", **KW)
+    assert abs(float(loss.detach()) - want) <= 1e-5 * abs(want)
+    loss.backward()
+    assert tcp.grad is not None and torch.isfinite(tcp.grad).all()

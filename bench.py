@@ -20,10 +20,10 @@ the N ranks in tile-row bands (below), the strong-scaling curve.
 
 --workload config3: one 2040x1356 image with 4096 closed paths x 6 segments
 split across the ranks in tile-row bands balanced by per-row work; every step
-all-reduces the gradient buffer over NCCL inside the step's CUDA graph
-(repo_b200/bands.py); value = iterations of the one image / max device time
-("scaling": "strong").  SSIM is not part of this step (a band lacks the rows
-the SSIM window needs).
+all-reduces the gradient buffer (with the bands' SSIM sums) over NCCL inside
+the step's CUDA graph, after an all-gather of each band's first 10 rows for
+the SSIM window (repo_b200/bands.py); value = iterations of the one image /
+max device time ("scaling": "strong").
 
 --workload config4: stroke mode, 1024x1024, 2048 open one-segment cubics
 (width U[1,4] px, S=16) through the drop-in manbo API: forward + MSE + backward
@@ -453,8 +453,9 @@ def run_bands(args, rank, world, local_rank):
     split = bands.balanced_bands(bands.tile_row_work(scene, dev), world)
     band = split[rank]
     hook = bands.allreduce_hook() if world > 1 else None
-    tr = FillTrainer(scene, dev, lr_points=0.5, lr_colors=0.01, with_ssim=False,
-                     tile_rows=band if world > 1 else None, grad_hook=hook)
+    halo = bands.allgather_halo(rank, world) if world > 1 else None
+    tr = FillTrainer(scene, dev, lr_points=0.5, lr_colors=0.01, with_ssim=True,
+                     tile_rows=band if world > 1 else None, grad_hook=hook, halo_gather=halo)
     flush_buf = torch.empty((L2_FLUSH_BYTES // 4,), dtype=torch.float32, device=dev)
 
     def flush():
@@ -489,11 +490,12 @@ def run_bands(args, rank, world, local_rank):
             "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": "config3: 2040x1356 RGB, 4096 closed cubic paths x 6 segs, "
-                                   "S=16, fwd+MSE+bwd+Adam, gradient all-reduce per step",
+                                   "S=16, fwd+MSE+SSIM+bwd+Adam, one all-reduce of gradients "
+                                   "and SSIM sums per step (SSIM halo rows by all-gather)",
                        "bands": split, "parallelism": f"tile-row bands x{world}"
                        + (" + NCCL all-reduce" if world > 1 else ""),
                        "l2": "flushed before every step (256 MiB write), outside the step events"},
-            "final_loss": tr.loss_value(),
+            "final_loss": tr.loss_value(), "final_ssim": tr.ssim_value(),
             "gpu_launches": args.steps * tr.launches_per_step,
             "clocks": clk.summary(),
         }
@@ -1008,7 +1010,7 @@ def main(argv=None):
             if rank == 0:
                 res["strong_config3"] = {
                     k: sres[k] for k in ("metric", "value", "unit", "ms_per_step", "n_gpus",
-                                         "scaling", "final_loss")}
+                                         "scaling", "final_loss", "final_ssim")}
                 res["strong_config3"]["bands"] = sres["config"]["bands"]
                 res["strong_config3"]["clocks"] = sres["clocks"]
         if rank == 0 and world == 1 and not args.no_gpu_reference:

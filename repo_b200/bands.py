@@ -12,6 +12,10 @@ the band gradients is exactly the full-image gradient up to summation order.
 Bands are balanced by a per-tile-row work estimate (edge slots + 8 per
 intersect, from one binning pass of the starting scene).
 
+In the fused training step (repo_b200.train.FillTrainer) the band's first
+win - 1 rows reach the previous band by one all-gather (allgather_halo) and
+the band's per-plane SSIM sums ride in the gradient all-reduce.
+
 SSIM over bands (band_ssim_sums): the valid-window SSIM output of row y reads
 input rows [y, y + win - 1], so a band owning pixel rows [y0, y1) produces the
 outputs of rows [y0, min(y1, H - win + 1)) from its own rows plus the first
@@ -101,6 +105,30 @@ def allreduce_hook(group=None) -> Callable[[torch.Tensor], None]:
         dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=group)
 
     return hook
+
+
+def allgather_halo(rank: int, world: int, group=None
+                   ) -> Callable[[torch.Tensor], Optional[torch.Tensor]]:
+    """halo_gather for FillTrainer's band SSIM: every rank contributes the
+    first rows of its band ([C, win - 1, W], one all-gather over the process
+    group, capturable in a CUDA graph) and gets back the next rank's, or None
+    on the last rank.  Rank i owns band i."""
+    import torch.distributed as dist
+    bufs = {}
+
+    def gather(send: torch.Tensor) -> Optional[torch.Tensor]:
+        key = (send.device, tuple(send.shape))
+        out = bufs.get(key)
+        if out is None:  # allocated on the first (eager) call, reused afterwards
+            # the ranks' tensors concatenated along dim 0 (both NCCL and gloo)
+            shape = (world * send.shape[0],) + tuple(send.shape[1:])
+            out = torch.empty(shape, dtype=send.dtype, device=send.device)
+            bufs[key] = out
+        dist.all_gather_into_tensor(out, send, group=group)
+        c = send.shape[0]
+        return out[(rank + 1) * c:(rank + 2) * c] if rank + 1 < world else None
+
+    return gather
 
 
 def ssim_halo_rows(bands_px: Sequence[Tuple[int, int]], index: int, height: int,
@@ -194,5 +222,5 @@ def band_ssim(img_chw: torch.Tensor, target_chw: torch.Tensor,
     return (sums / count).mean()
 
 
-__all__ = ["balanced_bands", "tile_row_work", "band_for_rank", "allreduce_hook",
+__all__ = ["balanced_bands", "tile_row_work", "band_for_rank", "allreduce_hook", "allgather_halo",
            "ssim_halo_rows", "exchange_ssim_halo", "band_ssim_sums", "band_ssim"]

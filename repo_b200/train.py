@@ -21,7 +21,11 @@ writes out of bounds.
 
 For multi-GPU runs ``tile_rows`` restricts the rank to a band of tile rows and
 ``grad_hook`` (e.g. an NCCL all-reduce) is applied to the flat buffer
-[ring grads | colour grads | sse, mse] before the optimiser step.
+[ring grads | colour grads | sse, mse | SSIM sums of the three planes] before
+the optimiser step.  SSIM on a band needs the next band's first win - 1 rows
+(``halo_gather``, e.g. repo_b200.bands.allgather_halo): the band's SSIM runs on
+its own rows plus that halo on the side stream, and its per-plane sums join
+the gradients in the same all-reduce.
 """
 from __future__ import annotations
 
@@ -45,6 +49,7 @@ class FillTrainer:
                  lr_colors: float = 0.01, with_ssim: bool = True, capacity=None,
                  tile_rows: Optional[tuple] = None,
                  grad_hook: Optional[Callable[[torch.Tensor], None]] = None,
+                 halo_gather: Optional[Callable[[torch.Tensor], Optional[torch.Tensor]]] = None,
                  betas=(0.9, 0.999), eps: float = 1e-8):
         dev = torch.device(device)
         self.device = dev
@@ -57,11 +62,14 @@ class FillTrainer:
         self.num_tiles = nt = tbx * tby
         self.tile_rows = (0, tby) if tile_rows is None else (int(tile_rows[0]), int(tile_rows[1]))
         self.with_ssim = bool(with_ssim)
-        if self.with_ssim and self.tile_rows != (0, tby):
-            # a band renders only its own rows; SSIM's window needs the whole image
-            raise ValueError("with_ssim=True needs the whole image: pass with_ssim=False "
-                             "with tile_rows (bands) and take SSIM across the bands with "
-                             "repo_b200.bands.band_ssim")
+        self.band_ssim = self.with_ssim and self.tile_rows != (0, tby)
+        if self.band_ssim and halo_gather is None:
+            # a band renders only its own rows; the SSIM window also reads the
+            # next band's first rows
+            raise ValueError("with_ssim=True on a band of tile rows needs halo_gather (the next "
+                             "band's first rows, e.g. repo_b200.bands.allgather_halo); or pass "
+                             "with_ssim=False")
+        self.halo_gather = halo_gather
         self.grad_hook = grad_hook
         self.lr = (float(lr_points), float(lr_colors))
         self.betas, self.eps = (float(betas[0]), float(betas[1])), float(eps)
@@ -76,10 +84,11 @@ class FillTrainer:
         self.colors = self.params[n_ring:].view(p, 3)
         self.exp_avg = torch.zeros_like(self.params)
         self.exp_avg_sq = torch.zeros_like(self.params)
-        self.flat_grad = torch.zeros((self.n_params + 2,), device=dev, dtype=f32)
+        self.flat_grad = torch.zeros((self.n_params + 5,), device=dev, dtype=f32)
         self.v_ring = self.flat_grad[:n_ring]
         self.v_colors = self.flat_grad[n_ring:self.n_params]
-        self.loss = self.flat_grad[self.n_params:]      # [sse, mse] of this rank's tiles
+        self.loss = self.flat_grad[self.n_params:self.n_params + 2]  # [sse, mse] of this rank's tiles
+        self.ssim_sums = self.flat_grad[self.n_params + 2:]  # band mode: per-plane SSIM sums
         self.step_count = torch.zeros((1,), device=dev, dtype=i32)
         self.adam_ws = torch.zeros((int(nat.call("cs_adam_workspace_size")),), device=dev,
                                    dtype=torch.uint8)
@@ -124,8 +133,23 @@ class FillTrainer:
         self.mse_scale = torch.ones((1,), device=dev, dtype=f32) * (2.0 / float(n_total))
         self.ssim_planes = torch.zeros((3,), device=dev, dtype=f32)
         self.gauss = _metric.gaussian_1d(11, 1.5, dev)
+        win = 11
+        self.ssim_total = float((self.h - win + 1) * (self.w - win + 1))
+        ssim_h = self.h
+        if self.band_ssim:
+            # the band's pixel rows [y0, y1), plus the next band's first rows
+            y0 = self.tile_rows[0] * _render.BLOCK_Y
+            y1 = min(self.tile_rows[1] * _render.BLOCK_Y, self.h)
+            self.band_px = (y0, y1)
+            self.halo = max(0, min(win - 1, self.h - y1))
+            ssim_h = (y1 - y0) + self.halo
+            self.ssim_count = float(max(0, ssim_h - win + 1) * (self.w - win + 1))
+            self.ssim_in = torch.zeros((3, ssim_h, self.w), device=dev, dtype=f32)
+            self.ssim_tgt = self.target[:, y0:y0 + ssim_h, :].contiguous()
+            self.halo_send = torch.zeros((3, win - 1, self.w), device=dev, dtype=f32)
+        self.ssim_h = ssim_h
         self.ssim_ws = torch.zeros(
-            (int(nat.call("cs_ssim_workspace_size", 3, self.h, self.w, 11)),), device=dev,
+            (int(nat.call("cs_ssim_workspace_size", 3, ssim_h, self.w, win)),), device=dev,
             dtype=torch.uint8)
         if capacity is None:
             capacity = self.probe_capacity()
@@ -231,10 +255,14 @@ class FillTrainer:
             main = torch.cuda.current_stream(self.device)
             self._fork.record(main)
             self._side.wait_event(self._fork)
-            nat.check(nat.call("cs_ssim", self.img_chw.data_ptr(), self.target.data_ptr(),
-                               self.gauss.data_ptr(), 3, self.h, self.w, 11, 0.01 ** 2, 0.03 ** 2,
-                               self.ssim_planes.data_ptr(), None, self.ssim_ws.data_ptr(),
-                               self._side.cuda_stream), "cs_ssim")
+            if self.band_ssim:
+                with torch.cuda.stream(self._side):
+                    self._band_ssim()
+            else:
+                nat.check(nat.call("cs_ssim", self.img_chw.data_ptr(), self.target.data_ptr(),
+                                   self.gauss.data_ptr(), 3, self.h, self.w, 11, 0.01 ** 2,
+                                   0.03 ** 2, self.ssim_planes.data_ptr(), None,
+                                   self.ssim_ws.data_ptr(), self._side.cuda_stream), "cs_ssim")
             self._join.record(self._side)
         if ev is not None:
             ev[2].record()
@@ -259,11 +287,34 @@ class FillTrainer:
         if join:
             self._join_side()
 
+    def _band_ssim(self):
+        """SSIM of this band (on the current stream): its first rows go to
+        the other bands, the next band's first rows extend its own, and the
+        SSIM of the extended rows gives the band's per-plane output sums."""
+        y0, y1 = self.band_px
+        rows = y1 - y0
+        send = min(rows, self.halo_send.shape[1])
+        self.halo_send[:, :send].copy_(self.img_chw[:, y0:y0 + send])
+        recv = self.halo_gather(self.halo_send)  # every band takes part
+        self.ssim_in[:, :rows].copy_(self.img_chw[:, y0:y1])
+        if self.halo > 0:
+            self.ssim_in[:, rows:].copy_(recv[:, :self.halo])
+        if self.ssim_count > 0:
+            nat.check(nat.call("cs_ssim", self.ssim_in.data_ptr(), self.ssim_tgt.data_ptr(),
+                               self.gauss.data_ptr(), 3, self.ssim_h, self.w, 11, 0.01 ** 2,
+                               0.03 ** 2, self.ssim_planes.data_ptr(), None,
+                               self.ssim_ws.data_ptr(), nat.stream(self.device)), "cs_ssim")
+            torch.mul(self.ssim_planes, self.ssim_count, out=self.ssim_sums)
+        else:
+            self.ssim_sums.zero_()
+
     def _join_side(self):
         if self.with_ssim:
             torch.cuda.current_stream(self.device).wait_event(self._join)
 
     def optimizer_step(self):
+        if self.band_ssim:
+            self._join_side()  # the band's SSIM sums travel with the gradients
         if self.grad_hook is not None:
             self.grad_hook(self.flat_grad)
         nat.check(nat.call("cs_adam_step", self.params.data_ptr(), self.flat_grad.data_ptr(),
@@ -308,4 +359,8 @@ class FillTrainer:
         return float(self.loss[1])
 
     def ssim_value(self) -> float:
+        """SSIM of the last step: the mean over planes of each plane's mean
+        (in band mode, of the all-reduced per-plane sums)."""
+        if self.band_ssim:
+            return float((self.ssim_sums / self.ssim_total).mean())
         return float(self.ssim_planes.mean())

@@ -3,6 +3,7 @@ all-reduce hook, the latter between two gloo ranks on the CPU."""
 import os
 import socket
 
+import numpy as np
 import pytest
 import torch
 import torch.distributed as dist
@@ -124,9 +125,45 @@ def test_band_ssim_halo_rows():
         ssim_halo_rows([(0, 16), (16, 20), (20, 48)], 0, 48, 11)
 
 
-def test_trainer_refuses_ssim_on_a_band():
+def test_trainer_needs_a_halo_for_ssim_on_a_band():
     from repo_b200 import scenes
     from repo_b200.train import FillTrainer
     sc = scenes.small_fill_scene(1, h=64, w=64, paths=3)
-    with pytest.raises(ValueError, match="whole image"):
+    with pytest.raises(ValueError, match="halo_gather"):
         FillTrainer(sc, torch.device("cpu"), tile_rows=(0, 2))
+
+
+def _halo_worker(rank, world, port, q):
+    import torch.distributed as dist
+
+    from repo_b200.bands import allgather_halo
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world)
+    try:
+        gather = allgather_halo(rank, world)
+        send = torch.full((3, 10, 7), float(rank)) + torch.arange(7.0)
+        got = gather(send)
+        q.put((rank, None if got is None else got.clone().numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_allgather_halo_returns_the_next_ranks_rows():
+    import multiprocessing as mp
+    import socket
+    ctx = mp.get_context("spawn")
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        port = sk.getsockname()[1]
+    world = 3
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_halo_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for r in range(world - 1):
+        np.testing.assert_array_equal(got[r], np.full((3, 10, 7), float(r + 1)) + np.arange(7.0))
+    assert got[world - 1] is None

@@ -136,3 +136,36 @@ def test_band_gradients_sum_to_the_full_image_gradient():
     for t, (r0, r1) in zip(parts, bands):
         rows = slice(r0 * 16, min(sc.height, r1 * 16))
         assert torch.equal(t.out[rows], full.out[rows])
+
+
+def test_band_ssim_sums_add_up_to_the_whole_image_ssim():
+    """Band SSIM of the fused step (FillTrainer with tile_rows and a halo):
+    each band's per-plane SSIM output sums, from its own rows plus the next
+    band's first rows, add up to the whole image's."""
+    from repo_b200.train import FillTrainer
+    dev = torch.device("cuda")
+    sc = scenes.config1()
+    full = FillTrainer(sc, dev, with_ssim=True)
+    full.forward_backward()
+    torch.cuda.synchronize()
+    img = full.img_chw.clone()
+    h, w = sc.height, sc.width
+    want = full.ssim_planes.double() * float((h - 10) * (w - 10))
+    tby = (h + 15) // 16
+    total = torch.zeros(3, dtype=torch.float64, device=dev)
+    for r0, r1 in ((0, 5), (5, 9), (9, tby)):
+        y1 = min(r1 * 16, h)
+
+        def gather(send, y1=y1):
+            n = min(send.shape[1], h - y1)
+            if n <= 0:
+                return None
+            out = torch.zeros_like(send)
+            out[:, :n] = img[:, y1:y1 + n]
+            return out
+
+        tr = FillTrainer(sc, dev, with_ssim=True, tile_rows=(r0, r1), halo_gather=gather)
+        tr.forward_backward()
+        torch.cuda.synchronize()
+        total += tr.ssim_sums.double()
+    torch.testing.assert_close(total, want, rtol=1e-5, atol=0)

@@ -455,7 +455,11 @@ CS_API int cs_ssim(const float *x, const float *y, const float *gauss, int64_t p
  * CS_ERR_UNSUPPORTED.  Because the scratch is shared, two calls on the same
  * device whose executions overlap (different streams with no ordering between
  * them, or several host threads) race on it and give wrong results; order
- * them on one stream, or use cs_ssim with a workspace per stream. */
+ * them on one stream, or use cs_ssim with a workspace per stream.  The
+ * looked-up address is kept for the life of the process: cudaDeviceReset (or
+ * anything else that destroys the device's primary context) reloads the
+ * library's device memory, possibly elsewhere, so a process that resets a
+ * device must not call cs_ssim_noalloc on that device afterwards. */
 CS_API int cs_ssim_noalloc(const float *x, const float *y, const float *gauss, int64_t planes,
             int32_t h, int32_t w, int32_t win, float c1, float c2, float *plane_means,
             float *ssim_map, void *stream);

@@ -20,10 +20,12 @@ the N ranks in tile-row bands (below), the strong-scaling curve.
 
 --workload config3: one 2040x1356 image with 4096 closed paths x 6 segments
 split across the ranks in tile-row bands balanced by per-row work; every step
-all-reduces the gradient buffer (with the bands' SSIM sums) over NCCL inside
-the step's CUDA graph, after an all-gather of each band's first 10 rows for
-the SSIM window (repo_b200/bands.py); value = iterations of the one image /
-max device time ("scaling": "strong").
+sums the ranks' gradients (with the bands' SSIM sums) and takes the Adam step
+in one kernel that reads every rank's gradient buffer through NVLink peer
+memory, and each band reads the next band's first 10 rows for the SSIM window
+the same way (repo_b200/peer.py; --collective nccl uses an NCCL all-reduce and
+all-gather instead); value = iterations of the one image / max device time
+("scaling": "strong").
 
 --workload config4: stroke mode, 1024x1024, 2048 open one-segment cubics
 (width U[1,4] px, S=16) through the drop-in manbo API: forward + MSE + backward
@@ -71,6 +73,8 @@ def parse_args(argv=None):
     ap.add_argument("--workload", default="config2",
                     choices=["config2", "config3", "config4", "config5"])
     ap.add_argument("--no-gpu-reference", action="store_true")
+    ap.add_argument("--collective", default="peer", choices=["peer", "nccl"],
+                    help="band exchange of the config-3 step: peer-memory kernels or NCCL")
     ap.add_argument("--no-strong", action="store_true",
                     help="skip the config-3 strong-scaling step of the default workload")
     ap.add_argument("--gpu-reference-child", action="store_true", help=argparse.SUPPRESS)
@@ -383,7 +387,7 @@ def run_b200(args, rank, world, local_rank):
         tk.tile_bins.cpu().numpy(), tk.istrips.cpu().numpy(), tk.rowoff.cpu().numpy(),
         tk.imeta.cpu().numpy(), tk.fidx.cpu().numpy(), tk.fts.cpu().numpy(), tk.h, tk.w, tk.tbx,
         n_now, tk.visits.cpu().numpy())
-    timed.graph = None
+    timed.release_graphs()
 
     # e2e through the drop-in API with host buffers
     e2e = None
@@ -452,10 +456,18 @@ def run_bands(args, rank, world, local_rank):
     scene = scenes.config3()
     split = bands.balanced_bands(bands.tile_row_work(scene, dev), world)
     band = split[rank]
-    hook = bands.allreduce_hook() if world > 1 else None
-    halo = bands.allgather_halo(rank, world) if world > 1 else None
+    collective = "none"
+    kw = {}
+    if world > 1 and args.collective == "peer":
+        # gradient exchange + Adam in one kernel and the SSIM halo read over
+        # NVLink peer memory (repo_b200/peer.py)
+        kw = dict(peer_group=dist.group.WORLD)
+        collective = "peer memory: fused all-reduce + Adam, halo by peer read"
+    elif world > 1:
+        kw = dict(grad_hook=bands.allreduce_hook(), halo_gather=bands.allgather_halo(rank, world))
+        collective = "NCCL all-reduce + all-gather"
     tr = FillTrainer(scene, dev, lr_points=0.5, lr_colors=0.01, with_ssim=True,
-                     tile_rows=band if world > 1 else None, grad_hook=hook, halo_gather=halo)
+                     tile_rows=band if world > 1 else None, **kw)
     flush_buf = torch.empty((L2_FLUSH_BYTES // 4,), dtype=torch.float32, device=dev)
 
     def flush():
@@ -492,8 +504,8 @@ def run_bands(args, rank, world, local_rank):
             "config": {"workload": "config3: 2040x1356 RGB, 4096 closed cubic paths x 6 segs, "
                                    "S=16, fwd+MSE+SSIM+bwd+Adam, one all-reduce of gradients "
                                    "and SSIM sums per step (SSIM halo rows by all-gather)",
-                       "bands": split, "parallelism": f"tile-row bands x{world}"
-                       + (" + NCCL all-reduce" if world > 1 else ""),
+                       "bands": split, "parallelism": f"tile-row bands x{world}",
+                       "collective": collective,
                        "l2": "flushed before every step (256 MiB write), outside the step events"},
             "final_loss": tr.loss_value(), "final_ssim": tr.ssim_value(),
             "gpu_launches": args.steps * tr.launches_per_step,
@@ -985,7 +997,7 @@ def main(argv=None):
             res, tr = run_bands(args, rank, world, local_rank)
             if rank == 0:
                 print(json.dumps(res), flush=True)
-            tr.graph = None  # graphs holding NCCL work go before the process group
+            tr.release_graphs()  # graphs holding collectives go before the process group
             del tr
             return 0
         if args.workload == "config4":
@@ -1005,13 +1017,14 @@ def main(argv=None):
             # config 3 at the same N: one 2040x1356 image in tile-row bands
             # with a gradient all-reduce per step (strong scaling)
             sres, btr = run_bands(args, rank, world, local_rank)
-            btr.graph = None  # graphs holding NCCL work go before the process group
+            btr.release_graphs()  # graphs holding collectives go before the process group
             del btr
             if rank == 0:
                 res["strong_config3"] = {
                     k: sres[k] for k in ("metric", "value", "unit", "ms_per_step", "n_gpus",
                                          "scaling", "final_loss", "final_ssim")}
                 res["strong_config3"]["bands"] = sres["config"]["bands"]
+                res["strong_config3"]["collective"] = sres["config"]["collective"]
                 res["strong_config3"]["clocks"] = sres["clocks"]
         if rank == 0 and world == 1 and not args.no_gpu_reference:
             ref = run_gpu_reference(args)

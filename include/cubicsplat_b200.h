@@ -542,6 +542,51 @@ CS_API int cs_ccl_stats_4(int32_t height, int32_t width, int32_t num_components,
                    float *centers, void *workspace, void *stream);
 
 /* --------------------------------------------------------------------------
+ * Peer-memory exchange for one image split across GPUs in tile-row bands
+ * (no counterpart in the reference, which renders an image on one GPU; these
+ * replace a library all-reduce and all-gather in the band-parallel step)
+ *
+ * Pointer arrays (flag_ptrs, grad_ptrs) are device arrays of `world` device
+ * addresses, entry q pointing into rank q's buffer as mapped in the calling
+ * process (e.g. symmetric memory).  Flag words are uint32 step numbers, laid
+ * out [slot][world]: word slot * world + q of a rank's array is written by
+ * rank q.  `epoch` is a device int32 (the optimiser's completed-step count);
+ * a signal stores *epoch + epoch_add, a wait waits for at least that value.
+ * Waits poll at most spin_limit times and then record CS_ERR_TIMEOUT in
+ * *status and skip their work; they never hang.  Kernels that wait on another
+ * rank must run on different GPUs at the same time (one process per GPU).
+ *
+ * cs_peer_signal: after the stream's earlier work, store the step into word
+ * slot * world + rank of every rank's flags (or only of rank only_peer >= 0),
+ * with release semantics at system scope.
+ * cs_peer_wait_copy: wait for rank from_rank's word in this rank's flags, then
+ * (src != NULL) copy `planes` blocks of plane_elems floats from src (plane
+ * stride src_plane_stride, e.g. a peer's buffer) to dst (dst_plane_stride).
+ * cs_allreduce_adam: wait for every rank's word in slot flag_slot, then
+ * params[0:n) take one Adam step (two learning rates: lr_first below n_first)
+ * with the gradient sum over ranks of grad_ptrs[q][0:n) (summed in rank order,
+ * so every rank computes identical parameters); the n_tail values after the
+ * gradients are summed into tail_out; clear_buf[0:n + n_tail) is zeroed (this
+ * rank's gradient buffer of the next step); *step is incremented.  With n a
+ * multiple of 4 every buffer must be 16-byte aligned to take the vector path.
+ * ------------------------------------------------------------------------ */
+CS_API size_t cs_allreduce_adam_workspace_size(void);
+CS_API int cs_peer_signal(const uint64_t *flag_ptrs, int32_t rank, int32_t world, int32_t slot,
+                          const int32_t *epoch, int32_t epoch_add, int32_t only_peer,
+                          void *stream);
+CS_API int cs_peer_wait_copy(const uint32_t *flags, int32_t slot, int32_t world,
+                             int32_t from_rank, const int32_t *epoch, int32_t epoch_add,
+                             int64_t spin_limit, int32_t *status, const float *src,
+                             int64_t src_plane_stride, float *dst, int64_t dst_plane_stride,
+                             int64_t plane_elems, int32_t planes, void *stream);
+CS_API int cs_allreduce_adam(const uint64_t *grad_ptrs, int32_t world, float *params,
+                             float *exp_avg, float *exp_avg_sq, int64_t n, int64_t n_first,
+                             int32_t n_tail, float *tail_out, float *clear_buf, float lr_first,
+                             float lr_rest, float beta1, float beta2, float eps, int32_t *step,
+                             const uint32_t *flags, int32_t flag_slot, int64_t spin_limit,
+                             int32_t *status, void *workspace, void *stream);
+
+/* --------------------------------------------------------------------------
  * Graph-capture helpers (no counterpart in the reference, whose renderer reads
  * intersect counts back to the host every frame and cannot be captured)
  *

@@ -92,6 +92,13 @@ SIGNATURES = {
     "cs_ssim": (ctypes.c_int, [_P, _P, _P, _I64, _I32, _I32, _I32, _F32, _F32, _P, _P, _P, _P]),
     "cs_ssim_noalloc": (ctypes.c_int, [_P, _P, _P, _I64, _I32, _I32, _I32, _F32, _F32, _P, _P,
                                        _P]),
+    "cs_allreduce_adam_workspace_size": (_SZ, []),
+    "cs_peer_signal": (ctypes.c_int, [_P, _I32, _I32, _I32, _P, _I32, _I32, _P]),
+    "cs_peer_wait_copy": (ctypes.c_int, [_P, _I32, _I32, _I32, _P, _I32, _I64, _P, _P, _I64, _P,
+                                         _I64, _I64, _I32, _P]),
+    "cs_allreduce_adam": (ctypes.c_int, [_P, _I32, _P, _P, _P, _I64, _I64, _I32, _P, _P, _F32,
+                                         _F32, _F32, _F32, _F32, _P, _P, _I32, _I64, _P, _P,
+                                         _P]),
     "cs_stream_is_capturing": (ctypes.c_int, [_P]),
     "cs_poison_on_status": (ctypes.c_int, [_P, _P, _I64, _P]),
 }

@@ -51,6 +51,18 @@ __device__ __forceinline__ float cs_expf(float x) {
 // (cvt.rzi.s32.f32), the semantics of the reference's T.Cast(int32, float).
 __device__ __forceinline__ int f2i_trunc_sat(float v) { return __float2int_rz(v); }
 
+// One Adam element (torch.optim.Adam's update with bias corrections bc1 =
+// 1 - b1^t and rb2 = 1 / sqrt(1 - b2^t)), in place on p, m, v.
+__device__ __forceinline__ void adam_element(float& p, float& m, float& v, float g, float lr,
+                                             float b1, float b2, float eps, float bc1,
+                                             float rb2) {
+  const float mi = b1 * m + (1.0f - b1) * g;
+  const float vi = b2 * v + (1.0f - b2) * g * g;
+  m = mi;
+  v = vi;
+  p = p - (lr / bc1) * mi / (sqrtf(vi) * rb2 + eps);
+}
+
 __device__ __forceinline__ uint32_t depth_sort_key(float depth) {
   // Integer order of the key equals float order of the depth, for both signs
   // (manbo/ops/cubic_splatting.py:799-805).

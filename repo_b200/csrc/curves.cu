@@ -264,13 +264,11 @@ __global__ void adam_kernel(float* __restrict__ p, float* __restrict__ g, float*
   const float rb2 = 1.0f / sqrtf(bc2);
   const long long stride = (long long)gridDim.x * blockDim.x;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
-    const float gi = g[i];
-    const float mi = b1 * m[i] + (1.0f - b1) * gi;
-    const float vi = b2 * v[i] + (1.0f - b2) * gi * gi;
+    float pi = p[i], mi = m[i], vi = v[i];
+    adam_element(pi, mi, vi, g[i], i < n_first ? lr0 : lr1, b1, b2, eps, bc1, rb2);
+    p[i] = pi;
     m[i] = mi;
     v[i] = vi;
-    const float lr = i < n_first ? lr0 : lr1;
-    p[i] = p[i] - (lr / bc1) * mi / (sqrtf(vi) * rb2 + eps);
     if (clear) g[i] = 0.0f;
   }
   __syncthreads();

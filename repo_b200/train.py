@@ -50,7 +50,7 @@ class FillTrainer:
                  tile_rows: Optional[tuple] = None,
                  grad_hook: Optional[Callable[[torch.Tensor], None]] = None,
                  halo_gather: Optional[Callable[[torch.Tensor], Optional[torch.Tensor]]] = None,
-                 betas=(0.9, 0.999), eps: float = 1e-8):
+                 peer_group=None, betas=(0.9, 0.999), eps: float = 1e-8):
         dev = torch.device(device)
         self.device = dev
         self.h, self.w, self.s = int(scene.height), int(scene.width), int(scene.samples)
@@ -63,7 +63,9 @@ class FillTrainer:
         self.tile_rows = (0, tby) if tile_rows is None else (int(tile_rows[0]), int(tile_rows[1]))
         self.with_ssim = bool(with_ssim)
         self.band_ssim = self.with_ssim and self.tile_rows != (0, tby)
-        if self.band_ssim and halo_gather is None:
+        if peer_group is not None and (grad_hook is not None or halo_gather is not None):
+            raise ValueError("peer_group replaces grad_hook and halo_gather: pass one or the other")
+        if self.band_ssim and halo_gather is None and peer_group is None:
             # a band renders only its own rows; the SSIM window also reads the
             # next band's first rows
             raise ValueError("with_ssim=True on a band of tile rows needs halo_gather (the next "
@@ -84,11 +86,19 @@ class FillTrainer:
         self.colors = self.params[n_ring:].view(p, 3)
         self.exp_avg = torch.zeros_like(self.params)
         self.exp_avg_sq = torch.zeros_like(self.params)
-        self.flat_grad = torch.zeros((self.n_params + 5,), device=dev, dtype=f32)
-        self.v_ring = self.flat_grad[:n_ring]
-        self.v_colors = self.flat_grad[n_ring:self.n_params]
-        self.loss = self.flat_grad[self.n_params:self.n_params + 2]  # [sse, mse] of this rank's tiles
-        self.ssim_sums = self.flat_grad[self.n_params + 2:]  # band mode: per-plane SSIM sums
+        # [primitive gradients | sse, mse of this rank's tiles | per-plane SSIM
+        # sums of its band]; with a peer group, two buffers in its symmetric
+        # memory (step t writes buffer t % 2) and the reduced tail in self.tail
+        self.peer = None
+        if peer_group is not None:
+            from .peer import PeerGroup
+            self.peer = PeerGroup(peer_group, dev, self.n_params + 5, (3, 10, self.w))
+            self._grad_bufs = self.peer.grads
+        else:
+            self._grad_bufs = [torch.zeros((self.n_params + 5,), device=dev, dtype=f32)]
+        self.tail = torch.zeros((5,), device=dev, dtype=f32)
+        self._t = 0  # steps enqueued (host count; selects the gradient buffer)
+        self._set_parity(0)
         self.step_count = torch.zeros((1,), device=dev, dtype=i32)
         self.adam_ws = torch.zeros((int(nat.call("cs_adam_workspace_size")),), device=dev,
                                    dtype=torch.uint8)
@@ -176,6 +186,12 @@ class FillTrainer:
         self._fork = torch.cuda.Event()
         self._join = torch.cuda.Event()
         self.launches_per_step = 7 + (1 if self.with_ssim else 0)
+        if self.peer is not None:  # grads signal; halo signal and wait-copy of band SSIM
+            rank, world = self.peer.rank, self.peer.world
+            self.launches_per_step += 1
+            if self.band_ssim:
+                self.launches_per_step += (1 if rank > 0 else 0) + (1 if self.halo > 0 else 0)
+        self.graphs = None
         self._timing = None  # CUDA events around the raster launches (enable_kernel_timing)
 
     def enable_kernel_timing(self):
@@ -287,6 +303,18 @@ class FillTrainer:
         if join:
             self._join_side()
 
+    def _set_parity(self, parity: int):
+        """Point the gradient views at buffer `parity` (one buffer without a
+        peer group)."""
+        self._parity = parity if len(self._grad_bufs) > 1 else 0
+        fg = self._grad_bufs[self._parity]
+        n_ring, n = self.n_ring, self.n_params
+        self.flat_grad = fg
+        self.v_ring = fg[:n_ring]
+        self.v_colors = fg[n_ring:n]
+        self.loss = fg[n:n + 2]
+        self.ssim_sums = fg[n + 2:]
+
     def _band_ssim(self):
         """SSIM of this band (on the current stream): its first rows go to
         the other bands, the next band's first rows extend its own, and the
@@ -294,11 +322,24 @@ class FillTrainer:
         y0, y1 = self.band_px
         rows = y1 - y0
         send = min(rows, self.halo_send.shape[1])
-        self.halo_send[:, :send].copy_(self.img_chw[:, y0:y0 + send])
-        recv = self.halo_gather(self.halo_send)  # every band takes part
-        self.ssim_in[:, :rows].copy_(self.img_chw[:, y0:y1])
-        if self.halo > 0:
-            self.ssim_in[:, rows:].copy_(recv[:, :self.halo])
+        if self.peer is not None:
+            # my first rows into my halo region, a flag to the previous band,
+            # then the next band's rows read through its peer pointer
+            pg = self.peer
+            pg.halo[:, :send].copy_(self.img_chw[:, y0:y0 + send])
+            if pg.rank > 0:
+                pg.signal(1, self.step_count, only_peer=pg.rank - 1)
+            self.ssim_in[:, :rows].copy_(self.img_chw[:, y0:y1])
+            if self.halo > 0:
+                pg.wait_copy(1, pg.rank + 1, self.step_count, self.counters[1:2],
+                             pg.halo_ptrs[pg.rank + 1], pg.halo_shape[1] * self.w, self.ssim_in,
+                             rows * self.w, self.ssim_h * self.w, self.halo * self.w, 3)
+        else:
+            self.halo_send[:, :send].copy_(self.img_chw[:, y0:y0 + send])
+            recv = self.halo_gather(self.halo_send)  # every band takes part
+            self.ssim_in[:, :rows].copy_(self.img_chw[:, y0:y1])
+            if self.halo > 0:
+                self.ssim_in[:, rows:].copy_(recv[:, :self.halo])
         if self.ssim_count > 0:
             nat.check(nat.call("cs_ssim", self.ssim_in.data_ptr(), self.ssim_tgt.data_ptr(),
                                self.gauss.data_ptr(), 3, self.ssim_h, self.w, 11, 0.01 ** 2,
@@ -317,37 +358,68 @@ class FillTrainer:
             self._join_side()  # the band's SSIM sums travel with the gradients
         if self.grad_hook is not None:
             self.grad_hook(self.flat_grad)
+        if self.peer is not None:
+            # every rank's gradients (and loss / SSIM sums) through peer
+            # memory, summed in rank order, then Adam: one kernel
+            self.peer.signal(0, self.step_count)
+            self.peer.allreduce_adam(self._parity, self.params, self.exp_avg, self.exp_avg_sq,
+                                     self.n_params, self.n_ring, 5, self.tail, self.lr, self.betas,
+                                     self.eps, self.step_count, self.counters[1:2])
+            return
         nat.check(nat.call("cs_adam_step", self.params.data_ptr(), self.flat_grad.data_ptr(),
                            self.exp_avg.data_ptr(), self.exp_avg_sq.data_ptr(), self.n_params,
                            self.n_ring, self.lr[0], self.lr[1], self.betas[0], self.betas[1],
                            self.eps, self.step_count.data_ptr(), self.adam_ws.data_ptr(), 1,
                            nat.stream(self.device)), "cs_adam_step")
 
-    def step_eager(self):
+    def _enqueue(self, parity: int):
         # SSIM overlaps the backward, the edge-to-ring pass and the optimiser
-        # step; the step ends when it is done
+        # step (with a peer group it joins before the gradient exchange,
+        # which carries its sums); the step ends when it is done
+        self._set_parity(parity)
         self.forward_backward(join=False)
         self.optimizer_step()
         self._join_side()
 
+    def _next_parity(self) -> int:
+        return (self._t + 1) % 2
+
+    def step_eager(self):
+        self._enqueue(self._next_parity())
+        self._t += 1
+
     def capture(self, warmup: int = 3):
-        """Capture one full training step into a CUDA graph."""
+        """Capture one full training step into a CUDA graph (with a peer
+        group, one graph per gradient buffer, replayed alternately)."""
         side = torch.cuda.Stream(self.device)
         side.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(side):
             for _ in range(warmup):
                 self.step_eager()
         torch.cuda.current_stream(self.device).wait_stream(side)
-        self.graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(self.graph, stream=self._main):
-            self.step_eager()
+        parities = (0, 1) if self.peer is not None else (0,)
+        graphs = []
+        for parity in parities:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=self._main):
+                self._enqueue(parity)
+            graphs.append(g)
+        self.graphs = graphs
+        self.graph = graphs[0]
         return self.graph
 
     def step(self):
-        if self.graph is not None:
-            self.graph.replay()
+        if self.graphs is not None:
+            self.graphs[self._next_parity() if len(self.graphs) > 1 else 0].replay()
+            self._t += 1
         else:
             self.step_eager()
+
+    def release_graphs(self):
+        """Drop the captured graphs (before the process group they may hold
+        collectives of goes away)."""
+        self.graphs = None
+        self.graph = None
 
     # ------------------------------------------------------------------
     def check_status(self) -> tuple[int, int]:
@@ -356,11 +428,15 @@ class FillTrainer:
         return n, status
 
     def loss_value(self) -> float:
+        """MSE of the last step (with a peer group, summed over the bands)."""
+        if self.peer is not None:
+            return float(self.tail[1])
         return float(self.loss[1])
 
     def ssim_value(self) -> float:
         """SSIM of the last step: the mean over planes of each plane's mean
         (in band mode, of the all-reduced per-plane sums)."""
         if self.band_ssim:
-            return float((self.ssim_sums / self.ssim_total).mean())
+            sums = self.tail[2:5] if self.peer is not None else self.ssim_sums
+            return float((sums / self.ssim_total).mean())
         return float(self.ssim_planes.mean())

@@ -1,0 +1,93 @@
+"""The band-parallel training step across two GPUs (one process per GPU):
+the peer-memory exchange (fused all-reduce + Adam, halo rows read from the
+next band) against the NCCL all-reduce / all-gather of the same step and
+against the whole image on one GPU.  Needs two GPUs; skipped otherwise."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+STEPS = 6
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port, out):
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    from repo_b200 import bands, scenes
+    from repo_b200.train import FillTrainer
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=60), device_id=dev)
+    try:
+        sc = scenes.config1()
+        split = bands.balanced_bands(bands.tile_row_work(sc, dev), world)
+        res = {}
+        for mode in ("peer", "nccl"):
+            kw = (dict(peer_group=dist.group.WORLD) if mode == "peer" else
+                  dict(grad_hook=bands.allreduce_hook(),
+                       halo_gather=bands.allgather_halo(rank, world)))
+            tr = FillTrainer(sc, dev, with_ssim=True, tile_rows=split[rank], **kw)
+            losses, ssims = [], []
+            for _ in range(STEPS // 2):  # eager steps, then graph replays
+                tr.step_eager()
+                losses.append(tr.loss_value())
+                ssims.append(tr.ssim_value())
+            tr.capture(warmup=0)
+            for _ in range(STEPS - STEPS // 2):
+                tr.step()
+                losses.append(tr.loss_value())
+                ssims.append(tr.ssim_value())
+            _, status = tr.check_status()
+            res[mode] = (losses, ssims, tr.params.cpu().numpy(), status)
+            tr.release_graphs()
+            del tr
+            torch.cuda.synchronize()
+            dist.barrier()
+        out[rank] = res
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_gpu_band_step_matches_nccl_and_the_whole_image():
+    from repo_b200 import scenes
+    from repo_b200.train import FillTrainer
+    world = 2
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as mgr:
+        out = mgr.dict()
+        mp.start_processes(_rank_main, args=(world, _free_port(), out), nprocs=world, join=True,
+                           start_method="spawn")
+        res = dict(out)
+    # the whole image on one GPU, the same steps
+    tr = FillTrainer(scenes.config1(), torch.device("cuda", 0), with_ssim=True)
+    losses, ssims = [], []
+    for _ in range(STEPS):
+        tr.step_eager()
+        losses.append(tr.loss_value())
+        ssims.append(tr.ssim_value())
+    for rank in range(world):
+        for mode in ("peer", "nccl"):
+            l, s, params, status = res[rank][mode]
+            assert status == 0, (rank, mode, status)
+            np.testing.assert_allclose(l, losses, rtol=1e-4)
+            np.testing.assert_allclose(s, ssims, rtol=1e-5)
+    # identical parameters on both ranks (every rank sums in rank order)
+    assert np.array_equal(res[0]["peer"][2], res[1]["peer"][2])
+    np.testing.assert_allclose(res[0]["peer"][2], res[0]["nccl"][2], rtol=0, atol=1e-3)

@@ -88,6 +88,9 @@ def test_two_gpu_band_step_matches_nccl_and_the_whole_image():
             assert status == 0, (rank, mode, status)
             np.testing.assert_allclose(l, losses, rtol=1e-4)
             np.testing.assert_allclose(s, ssims, rtol=1e-5)
-    # identical parameters on both ranks (every rank sums in rank order)
+    # identical parameters on both ranks (every rank sums in rank order); the
+    # two exchanges sum in different orders, and Adam's normalised step turns
+    # that rounding into visible moves only on near-zero gradients
     assert np.array_equal(res[0]["peer"][2], res[1]["peer"][2])
-    np.testing.assert_allclose(res[0]["peer"][2], res[0]["nccl"][2], rtol=0, atol=1e-3)
+    a, b = res[0]["peer"][2].astype(np.float64), res[0]["nccl"][2].astype(np.float64)
+    assert np.linalg.norm(a - b) <= 1e-5 * np.linalg.norm(b)

@@ -1,5 +1,7 @@
 // Cubic-domain kernels: edge-gradient accumulation onto cubic control points
 // and the closed control-polygon -> ring-of-cubics conversion (sm_100a).
+#include <algorithm>
+
 #include "cs_common.cuh"
 
 namespace cs {
@@ -177,73 +179,83 @@ __global__ void ring_to_cubics_kernel(const float* __restrict__ ring, float* __r
 // (W/2, H/2) (the derivative of the normalisation), summed over the one or
 // two control points that share the ring point.  One CTA handles whole
 // paths; optionally v_edges is cleared after it is read.
-constexpr int kRingThreads = 128;                                 // also the max segments per path
-constexpr int kRingEdgeLanes = 16;                                // lanes per segment
-constexpr int kRingSegsPerPass = kRingThreads / kRingEdgeLanes;  // segments per block pass
+//
+// One warp per path (a grid-stride loop over paths): a path whose tile rows
+// miss the band [r0, r1) has no edge gradient here and only writes zeros, so
+// a band's launch costs little beyond its own paths.  A live path's segments
+// go two at a time to the warp's half-warps: lane `sub` of a half takes edges
+// sub, sub + 16, ... of its segment, so the edge-gradient loads of a segment
+// are in flight together, and the 8 control-point sums are reduced across the
+// half-warp; the segments' sums wait in shared memory for the ring points.
+constexpr int kRingThreads = 128;   // 4 warps per CTA
+constexpr int kRingMaxSegs = 128;   // segments per path
+constexpr int kRingEdgeLanes = 16;  // lanes per segment
 
 __global__ void __launch_bounds__(kRingThreads) edge_grads_to_ring_kernel(
     float4* __restrict__ v_edges, float* __restrict__ v_ring, long long npaths, int G, int E,
     float half_w, float half_h, int clear, const int4* __restrict__ prim_ranges, int r0, int r1) {
-  __shared__ float cub[kRingThreads][9];
-  const int ppb = max(1, kRingSegsPerPass / G);
-  const long long p0 = (long long)blockIdx.x * ppb;
-  const int nseg = (int)min((long long)ppb * G, (npaths - p0) * G);
+  __shared__ float cub[kRingThreads / 32][kRingMaxSegs][8];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int sub = lane & (kRingEdgeLanes - 1), half = lane >> 4;
   const float inv_e = 1.0f / (float)E;
-  // A half-warp per segment: lane `sub` takes edges sub, sub+16, ..., so the
-  // edge-gradient loads of a segment are in flight together; the 8 control
-  // point sums are then reduced across the half-warp.
-  const int sub = threadIdx.x & (kRingEdgeLanes - 1), hw = threadIdx.x / kRingEdgeLanes;
-  for (int s0 = 0; s0 < nseg; s0 += kRingSegsPerPass) {  // uniform trip count
-    const int t = s0 + hw;
-    float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    // a path whose tile rows miss the band [r0, r1) has no edge gradient here
-    bool live = t < nseg;
-    if (live && prim_ranges) {
-      const int4 rr = __ldg(prim_ranges + p0 + t / G);
+  float(*sc)[8] = cub[wid];
+  const long long nwarps = (long long)gridDim.x * (kRingThreads / 32);
+  for (long long p = (long long)blockIdx.x * (kRingThreads / 32) + wid; p < npaths;
+       p += nwarps) {
+    bool live = true;
+    if (prim_ranges) {
+      const int4 rr = __ldg(prim_ranges + p);
       live = max(rr.y, r0) < min(rr.w, r1) && rr.x < rr.z;
     }
-    if (live) {
-      float4* gseg = v_edges + (p0 * G + t) * E;
-      for (int e = sub; e < E; e += kRingEdgeLanes) {
-        const float t0 = (float)e * inv_e, t1 = (float)(e + 1) * inv_e;
-        const float o0 = 1.0f - t0, o1 = 1.0f - t1;
-        const float o0s = o0 * o0, o1s = o1 * o1, t0s = t0 * t0, t1s = t1 * t1;
-        const float b0[4] = {o0s * o0, 3.0f * o0s * t0, 3.0f * o0 * t0s, t0s * t0};
-        const float b1[4] = {o1s * o1, 3.0f * o1s * t1, 3.0f * o1 * t1s, t1s * t1};
-        const float4 g = gseg[e];
-        if (clear) gseg[e] = make_float4(0.f, 0.f, 0.f, 0.f);
+    float2* out = reinterpret_cast<float2*>(v_ring) + p * 3 * G;
+    if (!live) {
+      for (int t = lane; t < 3 * G; t += 32) out[t] = make_float2(0.0f, 0.0f);
+      continue;
+    }
+    for (int s0 = 0; s0 < G; s0 += 2) {  // uniform trip count over the warp
+      const int seg = s0 + half;
+      float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      if (seg < G) {
+        float4* gseg = v_edges + (p * G + seg) * E;
+        for (int e = sub; e < E; e += kRingEdgeLanes) {
+          const float t0 = (float)e * inv_e, t1 = (float)(e + 1) * inv_e;
+          const float o0 = 1.0f - t0, o1 = 1.0f - t1;
+          const float o0s = o0 * o0, o1s = o1 * o1, t0s = t0 * t0, t1s = t1 * t1;
+          const float b0[4] = {o0s * o0, 3.0f * o0s * t0, 3.0f * o0 * t0s, t0s * t0};
+          const float b1[4] = {o1s * o1, 3.0f * o1s * t1, 3.0f * o1 * t1s, t1s * t1};
+          const float4 g = gseg[e];
+          if (clear) gseg[e] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            a[2 * c] = a[2 * c] + g.x * b0[c] + g.z * b1[c];
+            a[2 * c + 1] = a[2 * c + 1] + g.y * b0[c] + g.w * b1[c];
+          }
+        }
+      }
+#pragma unroll
+      for (int off = kRingEdgeLanes / 2; off > 0; off >>= 1)
+#pragma unroll
+        for (int c = 0; c < 8; ++c) a[c] += __shfl_xor_sync(0xffffffffu, a[c], off);
+      if (sub == 0 && seg < G) {
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-          a[2 * c] = a[2 * c] + g.x * b0[c] + g.z * b1[c];
-          a[2 * c + 1] = a[2 * c + 1] + g.y * b0[c] + g.w * b1[c];
+          sc[seg][2 * c] = (a[2 * c] * half_w) / half_w;
+          sc[seg][2 * c + 1] = (a[2 * c + 1] * half_h) / half_h;
         }
       }
     }
-#pragma unroll
-    for (int off = kRingEdgeLanes / 2; off > 0; off >>= 1)
-#pragma unroll
-      for (int c = 0; c < 8; ++c) a[c] += __shfl_xor_sync(0xffffffffu, a[c], off);
-    if (sub == 0 && t < nseg) {
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        cub[t][2 * c] = (a[2 * c] * half_w) / half_w;
-        cub[t][2 * c + 1] = (a[2 * c + 1] * half_h) / half_h;
+    __syncwarp();
+    for (int t = lane; t < 3 * G; t += 32) {
+      const int k = t / 3, j = t - 3 * k;
+      float gx = sc[k][2 * j], gy = sc[k][2 * j + 1];
+      if (j == 0) {  // shared with the end point of the previous segment
+        const int sp = k == 0 ? G - 1 : k - 1;
+        gx = gx + sc[sp][6];
+        gy = gy + sc[sp][7];
       }
+      out[t] = make_float2(gx, gy);
     }
-  }
-  __syncthreads();
-  const int npts = nseg / G * 3 * G;
-  for (int t = threadIdx.x; t < npts; t += kRingThreads) {
-    const int path = t / (3 * G), r = t - path * 3 * G;
-    const int k = r / 3, j = r - 3 * k;
-    const int s = path * G + k;
-    float gx = cub[s][2 * j], gy = cub[s][2 * j + 1];
-    if (j == 0) {  // shared with the end point of the previous segment
-      const int sp = path * G + (k == 0 ? G - 1 : k - 1);
-      gx = gx + cub[sp][6];
-      gy = gy + cub[sp][7];
-    }
-    reinterpret_cast<float2*>(v_ring)[(p0 * 3 * G) + t] = make_float2(gx, gy);
+    __syncwarp();  // the sums are read before the next path overwrites them
   }
 }
 
@@ -357,12 +369,13 @@ int cs_edge_grads_to_ring(float* v_edges, float* v_ring, int64_t num_paths, int3
                           int32_t edges_per_segment, int32_t img_height, int32_t img_width,
                           int32_t clear_edges, const int32_t* prim_tile_ranges,
                           int32_t tile_row_begin, int32_t tile_row_end, void* stream) {
-  if (num_paths < 0 || segs_per_path <= 0 || segs_per_path > kRingThreads ||
+  if (num_paths < 0 || segs_per_path <= 0 || segs_per_path > kRingMaxSegs ||
       edges_per_segment <= 0)
     return CS_ERR_ARG;
   if (num_paths == 0) return CS_OK;
-  const int ppb = max(1, kRingSegsPerPass / segs_per_path);
-  edge_grads_to_ring_kernel<<<ceil_div(num_paths, ppb), kRingThreads, 0, (cudaStream_t)stream>>>(
+  const long long warps = std::min<long long>(num_paths, 148LL * 64);
+  edge_grads_to_ring_kernel<<<(int)ceil_div(warps, kRingThreads / 32), kRingThreads, 0,
+                              (cudaStream_t)stream>>>(
       reinterpret_cast<float4*>(v_edges), v_ring, num_paths, segs_per_path, edges_per_segment,
       0.5f * (float)img_width, 0.5f * (float)img_height, clear_edges,
       reinterpret_cast<const int4*>(prim_tile_ranges), tile_row_begin, tile_row_end);

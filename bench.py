@@ -224,7 +224,8 @@ def raster_work(tr):
     return int(pe_fwd), int(vis_fwd), int(pe_bwd), int(vis_bwd), n
 
 
-def executed_work(bins, istrips, rowoff, imeta, fidx, fts, h, w, tbx, n, visits=None):
+def executed_work(bins, istrips, rowoff, imeta, fidx, fts, h, w, tbx, n, visits=None,
+                  winner_codes=False):
     """Pixel-edge pairs and pixel-intersect visits the B200 raster kernels
     evaluate, as opposed to the reference algorithm's (raster_work): a warp
     runs a 4x16-pixel strip, so every staged near-edge record of a walked
@@ -233,8 +234,10 @@ def executed_work(bins, istrips, rowoff, imeta, fidx, fts, h, w, tbx, n, visits=
     costs 64 pixel visits.  The forward walks a strip's intersects until all
     of its pixels have T <= 1e-4 (else to the tile's end), the backward from
     the strip's largest final_idx down -- or, given the forward's visit lists,
-    only the listed intersects.  Intersects that cannot change the strip are
-    skipped in batches and counted as free."""
+    only the listed intersects, and with the fill forward's winner codes only
+    each pixel's closest record of a listed intersect (one pair per pixel and
+    visit).  Intersects that cannot change the strip are skipped in batches
+    and counted as free."""
     import numpy as np
     if n == 0:
         return 0, 0, 0, 0
@@ -282,7 +285,7 @@ def executed_work(bins, istrips, rowoff, imeta, fidx, fts, h, w, tbx, n, visits=
             base = 4 * (t_rs + int(t)) + s_ * (t_re - t_rs + 1)
             cnt = int(visits[base])
             ids = visits[base + 1: base + 1 + cnt]
-            pe_b += int(rec[ids, s_].sum())
+            pe_b += cnt if winner_codes else int(rec[ids, s_].sum())
             vis_b += cnt
     return pe_f, vis_f, 64 * pe_b, 64 * vis_b
 
@@ -300,7 +303,8 @@ def executed_roofline(flop_b, t_b, flop_f, t_f, peak):
             "model": "same FLOP per pair and per visit, counted over what the kernels evaluate: "
                      "64 pixels x staged near-edge records of walked intersects, 64 pixels x "
                      "intersects that can change the strip (backward: the forward's visit "
-                     "lists)"}
+                     "lists; for fills one record per pixel and listed visit, the winner "
+                     "code's)"}
 
 
 def ncu_traffic(kernel: str, summary: str = "raster_fill_config2.md"):
@@ -386,7 +390,7 @@ def run_b200(args, rank, world, local_rank):
     xe_fwd, xv_fwd, xe_bwd, xv_bwd = executed_work(
         tk.tile_bins.cpu().numpy(), tk.istrips.cpu().numpy(), tk.rowoff.cpu().numpy(),
         tk.imeta.cpu().numpy(), tk.fidx.cpu().numpy(), tk.fts.cpu().numpy(), tk.h, tk.w, tk.tbx,
-        n_now, tk.visits.cpu().numpy())
+        n_now, tk.visits.cpu().numpy(), winner_codes=True)
     timed.release_graphs()
 
     # e2e through the drop-in API with host buffers

@@ -327,6 +327,28 @@ __device__ __forceinline__ bool wait_buffer(uint64_t* bars, int b, uint32_t& pha
   return ok;
 }
 
+// 16-byte copies global -> shared that complete asynchronously (cp.async,
+// non-bulk): each thread's copies are grouped by cp_async_commit and waited
+// for by that thread with cp_async_wait_all.  The .ca form keeps the line in
+// L1 (lanes of a strip often share a winning record), .cg reads through L2.
+__device__ __forceinline__ void cp_async16_ca(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src)
+               : "memory");
+}
+
+__device__ __forceinline__ void cp_async16_cg(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src)
+               : "memory");
+}
+
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+}
+
 // ---------------------------------------------------------------------------
 // per-pixel arithmetic (reference formulas, written order)
 
@@ -1204,17 +1226,63 @@ __device__ __forceinline__ bool backward_unit(const RasterArgs& A, int unit,
   return ok;
 }
 
+// Per-warp shared state of the direct fill backward beside its intersect
+// batch: the batch's winner codes (32 positions x 32 lanes, two 8-bit codes
+// per lane) and, in two alternating slots, each lane's two pixels' winning
+// records of the current and the next visit.
+struct DirectBuf {
+  unsigned short codes[32 * 32];
+  DEntry rec[2][32][2];
+};
+
+// Starts the copies of the winner codes of batch positions 0 .. n - 1 (64
+// bytes each, contiguous from src) into the warp's shared codes.
+__device__ __forceinline__ void stage_codes(const unsigned short* src, int n, DirectBuf& db) {
+  const int lane = threadIdx.x & 31;
+  for (int c = lane; c < n * 4; c += 32) cp_async16_cg(db.codes + c * 8, src + c * 8);
+  cp_async_commit();
+}
+
+// Starts the copies of this lane's two pixels' winning records of batch entry
+// j into db.rec[slot][lane]: pixels that the visit skips, codes that call for the
+// record walk and codes out of the intersect's range copy nothing (they are
+// handled, or reported, when the visit is evaluated).
+__device__ __forceinline__ void prefetch_winners(const DEntry* dl, const IBatch& ib, int j,
+                                                 const BwdPix s[2], DirectBuf& db, int slot) {
+  const int lane = threadIdx.x & 31;
+  const int k = ib.kk[j];
+  const int2 rg = ib.rg[j];
+  const unsigned wc = db.codes[j * 32 + lane];
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int win = (int)((wc >> (8 * u)) & 127u);
+    if (rg.y > 0 && s[u].in && k <= s[u].fidx && win != kNoWinner && win < rg.y) {
+      const DEntry* e = dl + rg.x + win;
+      cp_async16_ca(&db.rec[slot][lane][u].a, &e->a);
+      cp_async16_ca(&db.rec[slot][lane][u].b, &e->b);
+    }
+  }
+  cp_async_commit();
+}
+
 // Fill backward of one unit from the forward's visit list and winner codes,
 // with nothing staged: every listed visit evaluates, per pixel, only the
-// closest record the forward found (read from global memory; the records of
-// one intersect sit together), and the warp's edge-gradient sums per distinct
-// winner go straight to v_edges.  An edge record belongs to one intersect, so
-// a strip visits it at most once and a shared accumulator would save no
-// atomics.  A pixel without a representable code (an intersect with more
-// than 127 records in the strip) walks that intersect's records in order
-// (strict <: the reference's first minimum); the code's inside bit holds the
-// pixel's crossing state either way.
-__device__ __forceinline__ bool backward_unit_direct(const RasterArgs& A, int unit, IBatch& ib) {
+// closest record the forward found (the records of one intersect sit
+// together), and the warp's edge-gradient sums per distinct winner go straight
+// to v_edges.  An edge record belongs to one intersect, so a strip visits it
+// at most once and a shared accumulator would save no atomics.  A pixel
+// without a representable code (an intersect with more than 127 records in
+// the strip) walks that intersect's records in order (strict <: the
+// reference's first minimum); the code's inside bit holds the pixel's
+// crossing state either way.
+//
+// Memory latency is taken off the per-visit chain: a batch's winner codes are
+// copied into shared memory while its intersect records load, and the
+// winning records of the next visit of the batch are copied (cp.async) while
+// the current visit computes, so a visit waits on memory only when it is the
+// first of its batch.
+__device__ __forceinline__ bool backward_unit_direct(const RasterArgs& A, int unit, IBatch& ib,
+                                                     DirectBuf& db) {
   const int lane = threadIdx.x & 31;
   const UnitGeom g = unit_geom(A, unit);
   const int rs = g.rs, re = g.re, st = g.st;
@@ -1239,16 +1307,26 @@ __device__ __forceinline__ bool backward_unit_direct(const RasterArgs& A, int un
   int q = cnt - 1;      // next position (walking down)
   int qb = cnt;         // first position of the batch in shared memory
   unsigned amask = 0u;  // active intersects of the batch
+  int pf = -1;          // position whose winning records are in db.rec[slot]
+  int slot = 0;
   while (q >= 0) {
     if (q < qb) {
       qb = max(0, q - 31);
+      __syncwarp();  // every lane is done with the previous batch's codes
+      stage_codes(A.winners + (wslot + qb) * 32, q - qb + 1, db);
       amask = load_batch<false>(A, vl + qb, rs + qb, q - qb + 1, st, rs, re, ib);
+      cp_async_wait_all();
+      __syncwarp();  // the codes are visible to every lane
     }
     const int j = q - qb;
     if (!((amask >> j) & 1u)) {  // skip to the batch's next lower active intersect
       const unsigned below = amask & ((1u << j) - 1u);
       q = below ? qb + 31 - __clz(below) : qb - 1;
       continue;
+    }
+    if (pf != q) {  // the first visit of a batch
+      slot ^= 1;
+      prefetch_winners(dl, ib, j, s, db, slot);
     }
     const int k = ib.kk[j];
     const bool v0 = s[0].in && k <= s[0].fidx;
@@ -1257,7 +1335,8 @@ __device__ __forceinline__ bool backward_unit_direct(const RasterArgs& A, int un
     batch_meta(ib, j, m);
     const int2 rg = ib.rg[j];
     const int ds = rg.x, nrec = rg.y;
-    const unsigned wc = __ldg(A.winners + (wslot + q) * 32 + lane);
+    const unsigned wc = db.codes[j * 32 + lane];
+    cp_async_wait_all();  // this visit's winning records
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
       const unsigned c = (wc >> (8 * u)) & 255u;
@@ -1268,26 +1347,41 @@ __device__ __forceinline__ bool backward_unit_direct(const RasterArgs& A, int un
       s[u].bl = -1;
       s[u].bp = s[u].bcx = s[u].bcy = 0.0f;
       if (nrec <= 0 || !(u ? v1 : v0)) continue;
-      int d = ds + win;
+      float4 EA, EB;
       if (win == kNoWinner) {  // walk the intersect's records (strict <: first minimum)
-        d = -1;
+        int d = -1;
         for (int e = ds; e < ds + nrec; ++e) {
-          const float4 EA = __ldg(&dl[e].a), EB = __ldg(&dl[e].b);
+          const float4 WA = __ldg(&dl[e].a), WB = __ldg(&dl[e].b);
           float pr, cx, cy;
-          const float d2 = seg_d2(px[u], py, py - EA.y, EA, EB, pr, cx, cy);
+          const float d2 = seg_d2(px[u], py, py - WA.y, WA, WB, pr, cx, cy);
           if (d2 < s[u].md) {
             s[u].md = d2;
             d = e;
           }
         }
         if (d < 0) continue;
+        EA = __ldg(&dl[d].a);
+        EB = __ldg(&dl[d].b);
       } else if (win >= nrec) {  // not a code the forward wrote for this intersect
         if (A.status) atomicExch(A.status, CS_ERR_ARG);
         continue;
+      } else {
+        EA = db.rec[slot][lane][u].a;
+        EB = db.rec[slot][lane][u].b;
       }
-      const float4 EA = __ldg(&dl[d].a), EB = __ldg(&dl[d].b);
       s[u].md = seg_d2(px[u], py, py - EA.y, EA, EB, s[u].bp, s[u].bcx, s[u].bcy);
       s[u].be = __float_as_int(EB.w);
+    }
+    // the next active visit of the batch: its records load while this one computes
+    {
+      const unsigned below = amask & ((1u << j) - 1u);
+      pf = -1;
+      if (below) {
+        const int jn = 31 - __clz(below);
+        slot ^= 1;  // the other slot: this visit's records stay untouched
+        prefetch_winners(dl, ib, jn, s, db, slot);
+        pf = qb + jn;
+      }
     }
     float acc[kAcc];
 #pragma unroll
@@ -1317,6 +1411,7 @@ __device__ __forceinline__ bool backward_unit_direct(const RasterArgs& A, int un
     }
     --q;
   }
+  cp_async_wait_all();  // nothing in flight into the buffers of the next unit
   return true;
 }
 
@@ -1324,6 +1419,7 @@ __device__ __forceinline__ bool backward_unit_direct(const RasterArgs& A, int un
 // no record staging, so no record buffers or mbarriers.
 __global__ void __launch_bounds__(kRT) raster_backward_direct_kernel(const RasterArgs A) {
   __shared__ __align__(16) IBatch sib[kRW];
+  __shared__ __align__(16) DirectBuf sdb[kRW];
   const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int pre0 = 0, pre1 = 0;
   if (A.order) unit_prefix(A.order, pre0, pre1);
@@ -1334,7 +1430,7 @@ __global__ void __launch_bounds__(kRT) raster_backward_direct_kernel(const Raste
       if (lane == 0 && A.status) atomicExch(A.status, CS_ERR_ARG);
       break;
     }
-    backward_unit_direct(A, unit, sib[wid]);
+    backward_unit_direct(A, unit, sib[wid], sdb[wid]);
     u = next_unit(A);
   }
   finish_launch(A, false);
@@ -1419,7 +1515,10 @@ inline int launch_raster(bool stroke, bool bwd, const RasterArgs& a, int H, int 
   } else if (stroke && !bwd) {
     auto k = raster_forward_kernel<true>;
     k<<<persistent_ctas<1>(k, args.nunits), kRT, 0, st>>>(args);
-  } else if (!stroke && bwd && args.visits && args.winners) {
+  } else if (!stroke && bwd && args.visits && args.winners &&
+             ((reinterpret_cast<uintptr_t>(args.winners) |
+               reinterpret_cast<uintptr_t>(args.dl)) & 15u) == 0) {
+    // (the direct kernel copies codes and records 16 bytes at a time)
     auto k = raster_backward_direct_kernel;
     k<<<persistent_ctas<4>(k, args.nunits), kRT, 0, st>>>(args);
   } else if (!stroke && bwd) {

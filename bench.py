@@ -59,6 +59,7 @@ KERNEL_TIMING_REPS = 200
 WORKLOAD_CONFIG2 = ("config2: 768x512 RGB, 512 closed cubic paths x 4 segs, S=16, "
                     "fwd+MSE+SSIM+bwd+Adam (lr 0.5 pts / 0.01 colours)")
 L2_FLUSH_BYTES = 256 << 20
+FP32_PEAK_TFLOPS = round(148 * 128 * 2 * 1965e6 / 1e12, 2)  # SIMT FMA peak at the max SM clock
 
 
 def parse_args(argv=None):
@@ -712,11 +713,20 @@ def run_sweep(args, rank, world, local_rank):
             for _ in range(5):
                 fn()
             ms = statistics.median(time_device_calls(fn, 30 if batch == 1 else 10, flush, stream))
-            lines.append({"metric": f"standalone {name} kernel bandwidth, {batch}x3x512x768 fp32 pair",
-                          "value": round(nbytes / (ms * 1e-3) / 1e9, 1), "unit": "GB/s",
-                          "ms": round(ms, 5), "bytes": nbytes, "peak_hbm_gbs": hbm,
-                          "frac": round(nbytes / (ms * 1e-3) / 1e9 / hbm, 4),
-                          "l2": "flushed before every call"})
+            line = {"metric": f"standalone {name} kernel bandwidth, {batch}x3x512x768 fp32 pair",
+                    "value": round(nbytes / (ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                    "ms": round(ms, 5), "bytes": nbytes, "peak_hbm_gbs": hbm,
+                    "frac": round(nbytes / (ms * 1e-3) / 1e9 / hbm, 4),
+                    "l2": "flushed before every call"}
+            if name == "ssim":
+                # SSIM is bound by the FP32 pipe: 5 moments x 11 taps x 2 passes
+                # = 110 FMAs (220 FLOP) per valid output
+                flop = 220.0 * batch * 3 * (512 - 10) * (768 - 10)
+                tf = flop / (ms * 1e-3) / 1e12
+                line["fp32"] = {"tflops": round(tf, 3), "peak_tflops": FP32_PEAK_TFLOPS,
+                                "frac": round(tf / FP32_PEAK_TFLOPS, 4),
+                                "flop": flop, "model": "220 FLOP per valid output"}
+            lines.append(line)
         del x, y
     if rank != 0:
         return None

@@ -278,10 +278,30 @@ __device__ void scan_tiles(int* __restrict__ counts, int* __restrict__ ecounts,
   const long long n = t1 - t0;
   const long long chunk = (n + nthr - 1) / nthr;
   const long long b = t0 + tid * chunk, e = min(t1, b + chunk);
+  // up to kScanCache counts per thread are loaded at once and kept in
+  // registers for the second walk (one memory round trip instead of two
+  // per count)
+  constexpr int kScanCache = 8;
+  const bool cached = chunk <= kScanCache;
+  int ca[kScanCache], cb[kScanCache];
   int la = 0, lb = 0;
-  for (long long i = b; i < e; ++i) {
-    if (counts) la += __ldcg(counts + i);
-    if (ecounts) lb += __ldcg(ecounts + i);
+  if (cached) {
+#pragma unroll
+    for (int j = 0; j < kScanCache; ++j) {
+      const long long i = b + j;
+      ca[j] = (counts && i < e) ? __ldcg(counts + i) : 0;
+      cb[j] = (ecounts && i < e) ? __ldcg(ecounts + i) : 0;
+    }
+#pragma unroll
+    for (int j = 0; j < kScanCache; ++j) {
+      la += ca[j];
+      lb += cb[j];
+    }
+  } else {
+    for (long long i = b; i < e; ++i) {
+      if (counts) la += __ldcg(counts + i);
+      if (ecounts) lb += __ldcg(ecounts + i);
+    }
   }
   int ia = warp_incl_scan(la, lane), ib = warp_incl_scan(lb, lane);
   if (lane == 31) {
@@ -305,7 +325,29 @@ __device__ void scan_tiles(int* __restrict__ counts, int* __restrict__ ecounts,
   __syncthreads();
   const bool overflow = (counts && s_ta > icap) || (ecounts && s_tb > dcap);
   int ra = wa[wid] + ia - la, rb = wb[wid] + ib - lb;
-  for (long long i = b; i < e; ++i) {
+  if (cached) {
+#pragma unroll
+    for (int j = 0; j < kScanCache; ++j) {
+      const long long i = b + j;
+      if (i >= e) break;
+      if (counts) {
+        const int c = overflow ? 0 : ca[j];
+        counts[i] = 0;
+        cursor[i] = ra;
+        bins[2 * i] = c > 0 ? ra : 0;
+        bins[2 * i + 1] = c > 0 ? ra + c : 0;
+        ra += c;
+      }
+      if (ecounts) {
+        const int c = overflow ? 0 : cb[j];
+        ecounts[i] = 0;
+        dlr[2 * i] = c > 0 ? kStrips * rb : 0;
+        dlr[2 * i + 1] = c > 0 ? c : 0;
+        rb += c;
+      }
+    }
+  }
+  for (long long i = cached ? e : b; i < e; ++i) {
     if (counts) {
       const int c = overflow ? 0 : __ldcg(counts + i);
       counts[i] = 0;

@@ -78,6 +78,9 @@ def parse_args(argv=None):
                     help="band exchange of the config-3 step: peer-memory kernels or NCCL")
     ap.add_argument("--no-strong", action="store_true",
                     help="skip the config-3 strong-scaling step of the default workload")
+    ap.add_argument("--band", default=None, metavar="K/N",
+                    help="config3 on one GPU: only band K of the N-way tile-row split, no "
+                         "exchange and no SSIM (the per-band compute of an N-GPU step)")
     ap.add_argument("--gpu-reference-child", action="store_true", help=argparse.SUPPRESS)
     return ap.parse_args(argv)
 
@@ -459,8 +462,13 @@ def run_bands(args, rank, world, local_rank):
     torch.cuda.set_device(dev)
     stream = torch.cuda.current_stream(dev)
     scene = scenes.config3()
-    split = bands.balanced_bands(bands.tile_row_work(scene, dev), world)
-    band = split[rank]
+    nb, bi = world, rank
+    if args.band and world == 1 and args.workload == "config3":
+        bi, nb = (int(v) for v in args.band.split("/"))
+        if not 0 <= bi < nb:
+            raise ValueError(f"--band {args.band}: K must be in [0, N)")
+    split = bands.balanced_bands(bands.tile_row_work(scene, dev), nb)
+    band = split[bi]
     collective = "none"
     kw = {}
     if world > 1 and args.collective == "peer":
@@ -471,8 +479,9 @@ def run_bands(args, rank, world, local_rank):
     elif world > 1:
         kw = dict(grad_hook=bands.allreduce_hook(), halo_gather=bands.allgather_halo(rank, world))
         collective = "NCCL all-reduce + all-gather"
-    tr = FillTrainer(scene, dev, lr_points=0.5, lr_colors=0.01, with_ssim=True,
-                     tile_rows=band if world > 1 else None, **kw)
+    one_band = nb > 1 and world == 1
+    tr = FillTrainer(scene, dev, lr_points=0.5, lr_colors=0.01, with_ssim=not one_band,
+                     tile_rows=band if nb > 1 else None, **kw)
     flush_buf = torch.empty((L2_FLUSH_BYTES // 4,), dtype=torch.float32, device=dev)
 
     def flush():
@@ -500,6 +509,8 @@ def run_bands(args, rank, world, local_rank):
     total_ms = float(t_max.item())
     result = None
     if rank == 0:
+        if one_band:
+            collective = f"none: band {bi} of {nb} alone (rows {band}), no SSIM"
         result = {
             "metric": "fwd+bwd iters/s at 2040x1356, 4096 paths (tile-row bands)",
             "value": round(args.steps / (total_ms / 1e3), 3), "unit": UNIT, "n_gpus": world,
@@ -516,6 +527,10 @@ def run_bands(args, rank, world, local_rank):
             "gpu_launches": args.steps * tr.launches_per_step,
             "clocks": clk.summary(),
         }
+        if one_band:
+            result["metric"] = ("config-3 band step on one GPU: band K of an N-way tile-row split "
+                                "alone, no exchange, no SSIM (diagnostic)")
+            result["band"] = {"index": bi, "of": nb, "tile_rows": list(band)}
     return result, tr
 
 

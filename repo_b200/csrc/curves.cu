@@ -183,20 +183,22 @@ __global__ void ring_to_cubics_kernel(const float* __restrict__ ring, float* __r
 // One warp per path (a grid-stride loop over paths): a path whose tile rows
 // miss the band [r0, r1) has no edge gradient here and only writes zeros, so
 // a band's launch costs little beyond its own paths.  A live path's segments
-// go two at a time to the warp's half-warps: lane `sub` of a half takes edges
-// sub, sub + 16, ... of its segment, so the edge-gradient loads of a segment
-// are in flight together, and the 8 control-point sums are reduced across the
-// half-warp; the segments' sums wait in shared memory for the ring points.
-constexpr int kRingThreads = 128;   // 4 warps per CTA
-constexpr int kRingMaxSegs = 128;   // segments per path
-constexpr int kRingEdgeLanes = 16;  // lanes per segment
+// go eight at a time to groups of four lanes: lane `sub` of a group takes
+// edges sub, sub + 4, ... of its segment (loaded four at a time),
+// and the group reduce-scatters its 8 control-point sums in two shuffle
+// rounds, after which lane `sub` holds control point sub; the segments' sums
+// wait in shared memory for the ring points.
+constexpr int kRingThreads = 128;  // 4 warps per CTA
+constexpr int kRingMaxSegs = 128;  // segments per path
+constexpr int kRingEdgeLanes = 4;  // lanes per segment (one per control point)
+constexpr int kRingSegsPerRound = 32 / kRingEdgeLanes;
 
 __global__ void __launch_bounds__(kRingThreads) edge_grads_to_ring_kernel(
     float4* __restrict__ v_edges, float* __restrict__ v_ring, long long npaths, int G, int E,
     float half_w, float half_h, int clear, const int4* __restrict__ prim_ranges, int r0, int r1) {
   __shared__ float cub[kRingThreads / 32][kRingMaxSegs][8];
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  const int sub = lane & (kRingEdgeLanes - 1), half = lane >> 4;
+  const int sub = lane & (kRingEdgeLanes - 1), sl = lane / kRingEdgeLanes;
   const float inv_e = 1.0f / (float)E;
   float(*sc)[8] = cub[wid];
   const long long nwarps = (long long)gridDim.x * (kRingThreads / 32);
@@ -212,36 +214,56 @@ __global__ void __launch_bounds__(kRingThreads) edge_grads_to_ring_kernel(
       for (int t = lane; t < 3 * G; t += 32) out[t] = make_float2(0.0f, 0.0f);
       continue;
     }
-    for (int s0 = 0; s0 < G; s0 += 2) {  // uniform trip count over the warp
-      const int seg = s0 + half;
+    for (int s0 = 0; s0 < G; s0 += kRingSegsPerRound) {  // uniform trip count over the warp
+      const int seg = s0 + sl;
       float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
       if (seg < G) {
         float4* gseg = v_edges + (p * G + seg) * E;
-        for (int e = sub; e < E; e += kRingEdgeLanes) {
-          const float t0 = (float)e * inv_e, t1 = (float)(e + 1) * inv_e;
-          const float o0 = 1.0f - t0, o1 = 1.0f - t1;
-          const float o0s = o0 * o0, o1s = o1 * o1, t0s = t0 * t0, t1s = t1 * t1;
-          const float b0[4] = {o0s * o0, 3.0f * o0s * t0, 3.0f * o0 * t0s, t0s * t0};
-          const float b1[4] = {o1s * o1, 3.0f * o1s * t1, 3.0f * o1 * t1s, t1s * t1};
-          const float4 g = gseg[e];
-          if (clear) gseg[e] = make_float4(0.f, 0.f, 0.f, 0.f);
+        // four of the lane's edges per pass, their loads issued together
+        for (int e0 = sub; e0 < E; e0 += 4 * kRingEdgeLanes) {
+          float4 gv[4];
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            a[2 * c] = a[2 * c] + g.x * b0[c] + g.z * b1[c];
-            a[2 * c + 1] = a[2 * c + 1] + g.y * b0[c] + g.w * b1[c];
+          for (int i = 0; i < 4; ++i) {
+            const int e = e0 + i * kRingEdgeLanes;
+            gv[i] = e < E ? gseg[e] : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int e = e0 + i * kRingEdgeLanes;
+            if (e >= E) continue;
+            if (clear) gseg[e] = make_float4(0.f, 0.f, 0.f, 0.f);
+            const float t0 = (float)e * inv_e, t1 = (float)(e + 1) * inv_e;
+            const float o0 = 1.0f - t0, o1 = 1.0f - t1;
+            const float o0s = o0 * o0, o1s = o1 * o1, t0s = t0 * t0, t1s = t1 * t1;
+            const float b0[4] = {o0s * o0, 3.0f * o0s * t0, 3.0f * o0 * t0s, t0s * t0};
+            const float b1[4] = {o1s * o1, 3.0f * o1s * t1, 3.0f * o1 * t1s, t1s * t1};
+            const float4 g = gv[i];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              a[2 * c] = a[2 * c] + g.x * b0[c] + g.z * b1[c];
+              a[2 * c + 1] = a[2 * c + 1] + g.y * b0[c] + g.w * b1[c];
+            }
           }
         }
       }
+      // reduce-scatter over the group: values 4-7 to lanes with bit 1 set,
+      // 0-3 to the others, then one pair per lane: lane sub keeps values
+      // 2 sub, 2 sub + 1 (control point sub's x, y)
+      const bool hi2 = (sub & 2) != 0, hi1 = (sub & 1) != 0;
+      float k4[4], f[2];
 #pragma unroll
-      for (int off = kRingEdgeLanes / 2; off > 0; off >>= 1)
+      for (int i = 0; i < 4; ++i) {
+        const float send = hi2 ? a[i] : a[4 + i], keep = hi2 ? a[4 + i] : a[i];
+        k4[i] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+      }
 #pragma unroll
-        for (int c = 0; c < 8; ++c) a[c] += __shfl_xor_sync(0xffffffffu, a[c], off);
-      if (sub == 0 && seg < G) {
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          sc[seg][2 * c] = (a[2 * c] * half_w) / half_w;
-          sc[seg][2 * c + 1] = (a[2 * c + 1] * half_h) / half_h;
-        }
+      for (int i = 0; i < 2; ++i) {
+        const float send = hi1 ? k4[i] : k4[2 + i], keep = hi1 ? k4[2 + i] : k4[i];
+        f[i] = keep + __shfl_xor_sync(0xffffffffu, send, 1);
+      }
+      if (seg < G) {
+        sc[seg][2 * sub] = (f[0] * half_w) / half_w;
+        sc[seg][2 * sub + 1] = (f[1] * half_h) / half_h;
       }
     }
     __syncwarp();

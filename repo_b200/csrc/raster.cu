@@ -931,6 +931,65 @@ __device__ __forceinline__ void add_edge_grads(const RasterArgs& A, float4* dgra
   }
 }
 
+// Sums over the warp of eight values at once: on return lane l holds the
+// total of value l / 4 (a reduce-scatter: four, two and one exchanged values,
+// then two butterfly steps).
+__device__ __forceinline__ float warp_reduce8(const float v[8]) {
+  const int lane = threadIdx.x & 31;
+  const bool h16 = (lane & 16) != 0, h8 = (lane & 8) != 0, h4 = (lane & 4) != 0;
+  float a[4], b[2];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    a[i] = (h16 ? v[4 + i] : v[i]) + __shfl_xor_sync(0xffffffffu, h16 ? v[i] : v[4 + i], 16);
+#pragma unroll
+  for (int i = 0; i < 2; ++i)
+    b[i] = (h8 ? a[2 + i] : a[i]) + __shfl_xor_sync(0xffffffffu, h8 ? a[i] : a[2 + i], 8);
+  float c = (h4 ? b[1] : b[0]) + __shfl_xor_sync(0xffffffffu, h4 ? b[0] : b[1], 4);
+  c += __shfl_xor_sync(0xffffffffu, c, 2);
+  c += __shfl_xor_sync(0xffffffffu, c, 1);
+  return c;
+}
+
+// add_edge_grads for the direct backward (every sum goes to v_edges; key =
+// -(edge + 2)), two distinct winners per round when there are two: their
+// eight components share one reduce-scatter, so a visit with several winner
+// edges needs half the dependent shuffle rounds.
+__device__ __forceinline__ void add_edge_grads_direct(const RasterArgs& A, int key0, bool has0,
+                                                      const float4& g0, int key1, bool has1,
+                                                      const float4& g1) {
+  const int lane = threadIdx.x & 31;
+  unsigned p0 = __ballot_sync(0xffffffffu, has0), p1 = __ballot_sync(0xffffffffu, has1);
+  while (p0 | p1) {  // every round clears at least the source lane's bit
+    const int sa = p0 ? __ffs(p0) - 1 : __ffs(p1) - 1;
+    const int ka = __shfl_sync(0xffffffffu, p0 ? key0 : key1, sa);
+    const bool a0 = has0 && key0 == ka, a1 = has1 && key1 == ka;
+    p0 &= ~__ballot_sync(0xffffffffu, a0);
+    p1 &= ~__ballot_sync(0xffffffffu, a1);
+    float v[8];
+    v[0] = v[1] = v[2] = v[3] = 0.0f;
+    if (a0) { v[0] = g0.x; v[1] = g0.y; v[2] = g0.z; v[3] = g0.w; }
+    if (a1) { v[0] += g1.x; v[1] += g1.y; v[2] += g1.z; v[3] += g1.w; }
+    if (!(p0 | p1)) {  // one winner left: the four-value butterfly
+      const float r = warp_reduce4(v[0], v[1], v[2], v[3]);
+      if ((lane & 7) == 0 && r != 0.0f)
+        atomicAdd(A.v_edges + (long long)(-(ka + 2)) * 4 + (lane >> 3), r);
+      break;
+    }
+    const int sb = p0 ? __ffs(p0) - 1 : __ffs(p1) - 1;
+    const int kb = __shfl_sync(0xffffffffu, p0 ? key0 : key1, sb);
+    const bool b0 = has0 && key0 == kb, b1 = has1 && key1 == kb;
+    p0 &= ~__ballot_sync(0xffffffffu, b0);
+    p1 &= ~__ballot_sync(0xffffffffu, b1);
+    v[4] = v[5] = v[6] = v[7] = 0.0f;
+    if (b0) { v[4] = g0.x; v[5] = g0.y; v[6] = g0.z; v[7] = g0.w; }
+    if (b1) { v[4] += g1.x; v[5] += g1.y; v[6] += g1.z; v[7] += g1.w; }
+    const float r = warp_reduce8(v);
+    const int vi = lane >> 2;
+    if ((lane & 3) == 0 && r != 0.0f)
+      atomicAdd(A.v_edges + (long long)(-((vi < 4 ? ka : kb) + 2)) * 4 + (vi & 3), r);
+  }
+}
+
 __device__ __forceinline__ void flush_acc(const RasterArgs& A, int pid, int k, int c, float v) {
   if (v == 0.0f) return;
   if (c < 3) atomicAdd(A.v_colors + pid * 3 + c, v);
@@ -1393,8 +1452,8 @@ __device__ __forceinline__ bool backward_unit_direct(const RasterArgs& A, int un
     for (int u = 0; u < 2; ++u)
       bwd_pixel<false>(s[u], m, px[u], py, u ? v1 : v0, acc, collect, A.v_opac != nullptr,
                        A.v_inv != nullptr, eg[u], has_eg[u], contributed);
-    add_edge_grads(A, nullptr, 0, -(s[0].be + 2), has_eg[0], eg[0], -(s[1].be + 2), has_eg[1],
-                   eg[1]);
+    add_edge_grads_direct(A, -(s[0].be + 2), has_eg[0], eg[0], -(s[1].be + 2), has_eg[1],
+                          eg[1]);
     if (__any_sync(0xffffffffu, contributed)) {
       const int vi = (lane >> 3) & 3;
       const bool leader = (lane & 7) == 0;

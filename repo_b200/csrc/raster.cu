@@ -120,11 +120,8 @@ __device__ __forceinline__ UnitGeom unit_geom(const RasterArgs& A, int unit) {
   g.tile = (long long)g.ty * A.tbx + g.tx;
   g.rs = __ldg(A.bins + 2 * g.tile);
   g.re = __ldg(A.bins + 2 * g.tile + 1);
-  g.base = 0;
-  if (g.re > g.rs) {
-    const int2 dl = A.dlr[g.tile];
-    g.base = (long long)dl.x + (long long)g.st * dl.y;
-  }
+  const int2 dl = A.dlr[g.tile];  // loaded beside the ranges (every tile has an entry)
+  g.base = g.re > g.rs ? (long long)dl.x + (long long)g.st * dl.y : 0;
   return g;
 }
 
@@ -931,6 +928,16 @@ __device__ __forceinline__ void add_edge_grads(const RasterArgs& A, float4* dgra
   }
 }
 
+__device__ __forceinline__ void flush_acc(const RasterArgs& A, int pid, int k, int c, float v) {
+  if (v == 0.0f) return;
+  if (c < 3) atomicAdd(A.v_colors + pid * 3 + c, v);
+  else if (c == 3) { if (A.v_opac) atomicAdd(A.v_opac + pid, v); }
+  else if (c == 4) { if (A.v_inv) atomicAdd(A.v_inv + pid, v); }
+  else if (c == 5) atomicAdd(A.v_sw + pid, v);
+  else if (c < 9) { if (A.contrib) atomicAdd(A.contrib + pid * 3 + (c - 6), v); }
+  else if (A.icontrib) atomicAdd(A.icontrib + k, v);
+}
+
 // Sums over the warp of eight values at once: on return lane l holds the
 // total of value l / 4 (a reduce-scatter: four, two and one exchanged values,
 // then two butterfly steps).
@@ -953,10 +960,14 @@ __device__ __forceinline__ float warp_reduce8(const float v[8]) {
 // add_edge_grads for the direct backward (every sum goes to v_edges; key =
 // -(edge + 2)), two distinct winners per round when there are two: their
 // eight components share one reduce-scatter, so a visit with several winner
-// edges needs half the dependent shuffle rounds.
-__device__ __forceinline__ void add_edge_grads_direct(const RasterArgs& A, int key0, bool has0,
+// edges needs half the dependent shuffle rounds.  With `fold` (warp-uniform)
+// the visit's four per-primitive sums (colours, opacity) ride in the free half
+// of a last round that has a single winner, and the function returns true
+// once it has flushed them (else the caller reduces them itself).
+__device__ __forceinline__ bool add_edge_grads_direct(const RasterArgs& A, int key0, bool has0,
                                                       const float4& g0, int key1, bool has1,
-                                                      const float4& g1) {
+                                                      const float4& g1, bool fold,
+                                                      const float a4[4], int pid, int k) {
   const int lane = threadIdx.x & 31;
   unsigned p0 = __ballot_sync(0xffffffffu, has0), p1 = __ballot_sync(0xffffffffu, has1);
   while (p0 | p1) {  // every round clears at least the source lane's bit
@@ -969,11 +980,26 @@ __device__ __forceinline__ void add_edge_grads_direct(const RasterArgs& A, int k
     v[0] = v[1] = v[2] = v[3] = 0.0f;
     if (a0) { v[0] = g0.x; v[1] = g0.y; v[2] = g0.z; v[3] = g0.w; }
     if (a1) { v[0] += g1.x; v[1] += g1.y; v[2] += g1.z; v[3] += g1.w; }
-    if (!(p0 | p1)) {  // one winner left: the four-value butterfly
+    if (!(p0 | p1)) {  // one winner left
+      if (fold) {
+        v[4] = a4[0];
+        v[5] = a4[1];
+        v[6] = a4[2];
+        v[7] = a4[3];
+        const float r = warp_reduce8(v);
+        const int vi = lane >> 2;
+        if ((lane & 3) == 0 && r != 0.0f) {
+          if (vi < 4)
+            atomicAdd(A.v_edges + (long long)(-(ka + 2)) * 4 + vi, r);
+          else
+            flush_acc(A, pid, k, vi - 4, r);
+        }
+        return true;
+      }
       const float r = warp_reduce4(v[0], v[1], v[2], v[3]);
       if ((lane & 7) == 0 && r != 0.0f)
         atomicAdd(A.v_edges + (long long)(-(ka + 2)) * 4 + (lane >> 3), r);
-      break;
+      return false;
     }
     const int sb = p0 ? __ffs(p0) - 1 : __ffs(p1) - 1;
     const int kb = __shfl_sync(0xffffffffu, p0 ? key0 : key1, sb);
@@ -988,17 +1014,9 @@ __device__ __forceinline__ void add_edge_grads_direct(const RasterArgs& A, int k
     if ((lane & 3) == 0 && r != 0.0f)
       atomicAdd(A.v_edges + (long long)(-((vi < 4 ? ka : kb) + 2)) * 4 + (vi & 3), r);
   }
+  return false;
 }
 
-__device__ __forceinline__ void flush_acc(const RasterArgs& A, int pid, int k, int c, float v) {
-  if (v == 0.0f) return;
-  if (c < 3) atomicAdd(A.v_colors + pid * 3 + c, v);
-  else if (c == 3) { if (A.v_opac) atomicAdd(A.v_opac + pid, v); }
-  else if (c == 4) { if (A.v_inv) atomicAdd(A.v_inv + pid, v); }
-  else if (c == 5) atomicAdd(A.v_sw + pid, v);
-  else if (c < 9) { if (A.contrib) atomicAdd(A.contrib + pid * 3 + (c - 6), v); }
-  else if (A.icontrib) atomicAdd(A.icontrib + k, v);
-}
 
 // Per-pixel state of a backward strip: T, final_idx and the image gradient
 // (given, or the MSE gradient from the image and the target), with paired
@@ -1343,16 +1361,32 @@ __device__ __forceinline__ void prefetch_winners(const DEntry* dl, const IBatch&
 __device__ __forceinline__ bool backward_unit_direct(const RasterArgs& A, int unit, IBatch& ib,
                                                      DirectBuf& db) {
   const int lane = threadIdx.x & 31;
-  const UnitGeom g = unit_geom(A, unit);
-  const int rs = g.rs, re = g.re, st = g.st;
-  if (re <= rs) return true;
+  // the tile's intersect and record ranges and the strip's pixel state are
+  // loaded together: one memory round trip instead of three
+  UnitGeom g;
+  {
+    const int trel = unit / kStrips;
+    g.st = unit - trel * kStrips;
+    const int ry = trel / A.tbx;
+    g.tx = trel - ry * A.tbx;
+    g.ty = A.r0 + ry;
+    g.tile = (long long)g.ty * A.tbx + g.tx;
+  }
+  g.rs = __ldg(A.bins + 2 * g.tile);
+  g.re = __ldg(A.bins + 2 * g.tile + 1);
+  const int2 tdl = A.dlr[g.tile];
+  const int st = g.st;
   const int ly = st * kStripRows + (lane >> 3), lx = (lane & 7) * 2;
   const int i = g.ty * kTile + ly, j0 = g.tx * kTile + lx;
   const float py = (float)i + 0.5f;
   const float px[2] = {(float)j0 + 0.5f, (float)(j0 + 1) + 0.5f};
   const bool collect = (A.contrib != nullptr) | (A.icontrib != nullptr);
   BwdPix s[2];
-  const int kmax = bwd_setup(A, i, j0, re, s);
+  const int kall = bwd_setup(A, i, j0, INT_MAX, s);  // the warp's largest final_idx
+  const int rs = g.rs, re = g.re;
+  if (re <= rs) return true;
+  g.base = (long long)tdl.x + (long long)st * tdl.y;
+  const int kmax = min(kall, re - 1);
   if (kmax < rs) return true;
   const int* vl = A.visits + visit_base(g);
   const int cnt = vl[0];
@@ -1452,9 +1486,12 @@ __device__ __forceinline__ bool backward_unit_direct(const RasterArgs& A, int un
     for (int u = 0; u < 2; ++u)
       bwd_pixel<false>(s[u], m, px[u], py, u ? v1 : v0, acc, collect, A.v_opac != nullptr,
                        A.v_inv != nullptr, eg[u], has_eg[u], contributed);
-    add_edge_grads_direct(A, -(s[0].be + 2), has_eg[0], eg[0], -(s[1].be + 2), has_eg[1],
-                          eg[1]);
-    if (__any_sync(0xffffffffu, contributed)) {
+    const bool any_c = __any_sync(0xffffffffu, contributed);
+    const float a4[4] = {acc[0], acc[1], acc[2], A.v_opac ? acc[3] : 0.0f};
+    const bool folded = add_edge_grads_direct(A, -(s[0].be + 2), has_eg[0], eg[0],
+                                              -(s[1].be + 2), has_eg[1], eg[1],
+                                              any_c && !A.v_inv && !collect, a4, m.pid, k);
+    if (any_c && !folded) {
       const int vi = (lane >> 3) & 3;
       const bool leader = (lane & 7) == 0;
       float r = warp_reduce4(acc[0], acc[1], acc[2], A.v_opac ? acc[3] : 0.0f);

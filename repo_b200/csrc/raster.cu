@@ -211,14 +211,15 @@ __device__ __forceinline__ bool intersect_active(const int4& m0, const int4& m1,
 // batch entry j).
 template <bool STROKE>
 __device__ __forceinline__ unsigned load_batch(const RasterArgs& A, const int* lst, int k0, int n,
-                                               int st, int rs, int re, IBatch& b) {
+                                               int st, int rs, int re, IBatch& b,
+                                               bool have_id = false, int lane_id = 0) {
   const int lane = threadIdx.x & 31;
   bool act = false;
   __syncwarp();  // every lane is done with the previous batch
   if (lane < n) {
     int kid = k0 + lane;
     if (lst) {
-      kid = __ldg(lst + lane);
+      kid = have_id ? lane_id : __ldg(lst + lane);  // lane_id: lst[lane], loaded by the caller
       if (kid < rs || kid >= re) {  // not a list the forward wrote for this strip
         if (A.status) atomicExch(A.status, CS_ERR_ARG);
         kid = -1;
@@ -1309,7 +1310,8 @@ __device__ __forceinline__ bool backward_unit(const RasterArgs& A, int unit,
 // records of the current and the next visit.
 struct DirectBuf {
   unsigned short codes[32 * 32];
-  DEntry rec[2][32][2];
+  float4 ra[2][2][32];  // [slot][pixel][lane]: the records' two halves apart, so
+  float4 rb[2][2][32];  // that a warp's 16-byte reads hit consecutive addresses
 };
 
 // Starts the copies of the winner codes of batch positions 0 .. n - 1 (64
@@ -1321,7 +1323,7 @@ __device__ __forceinline__ void stage_codes(const unsigned short* src, int n, Di
 }
 
 // Starts the copies of this lane's two pixels' winning records of batch entry
-// j into db.rec[slot][lane]: pixels that the visit skips, codes that call for the
+// j into db.ra / db.rb [slot][pixel][lane]: pixels that the visit skips, codes that call for the
 // record walk and codes out of the intersect's range copy nothing (they are
 // handled, or reported, when the visit is evaluated).
 __device__ __forceinline__ void prefetch_winners(const DEntry* dl, const IBatch& ib, int j,
@@ -1335,8 +1337,8 @@ __device__ __forceinline__ void prefetch_winners(const DEntry* dl, const IBatch&
     const int win = (int)((wc >> (8 * u)) & 127u);
     if (rg.y > 0 && s[u].in && k <= s[u].fidx && win != kNoWinner && win < rg.y) {
       const DEntry* e = dl + rg.x + win;
-      cp_async16_ca(&db.rec[slot][lane][u].a, &e->a);
-      cp_async16_ca(&db.rec[slot][lane][u].b, &e->b);
+      cp_async16_ca(&db.ra[slot][u][lane], &e->a);
+      cp_async16_ca(&db.rb[slot][u][lane], &e->b);
     }
   }
   cp_async_commit();
@@ -1390,6 +1392,9 @@ __device__ __forceinline__ bool backward_unit_direct(const RasterArgs& A, int un
   if (kmax < rs) return true;
   const int* vl = A.visits + visit_base(g);
   const int cnt = vl[0];
+  // the list's first 32 ids come with its count (they are the only batch of a
+  // list of up to 32 visits; reads stay inside the strip's list region)
+  const int first_id = lane < re - rs ? __ldg(vl + 1 + lane) : -1;
   if (cnt < 0 || cnt > re - rs) {  // not a list the forward wrote for this strip
     if (lane == 0 && A.status) atomicExch(A.status, CS_ERR_ARG);
     return true;
@@ -1400,14 +1405,15 @@ __device__ __forceinline__ bool backward_unit_direct(const RasterArgs& A, int un
   int q = cnt - 1;      // next position (walking down)
   int qb = cnt;         // first position of the batch in shared memory
   unsigned amask = 0u;  // active intersects of the batch
-  int pf = -1;          // position whose winning records are in db.rec[slot]
+  int pf = -1;          // position whose winning records are in slot `slot`
   int slot = 0;
   while (q >= 0) {
     if (q < qb) {
       qb = max(0, q - 31);
       __syncwarp();  // every lane is done with the previous batch's codes
       stage_codes(A.winners + (wslot + qb) * 32, q - qb + 1, db);
-      amask = load_batch<false>(A, vl + qb, rs + qb, q - qb + 1, st, rs, re, ib);
+      amask = load_batch<false>(A, vl + qb, rs + qb, q - qb + 1, st, rs, re, ib, qb == 0,
+                                first_id);
       cp_async_wait_all();
       __syncwarp();  // the codes are visible to every lane
     }
@@ -1459,8 +1465,8 @@ __device__ __forceinline__ bool backward_unit_direct(const RasterArgs& A, int un
         if (A.status) atomicExch(A.status, CS_ERR_ARG);
         continue;
       } else {
-        EA = db.rec[slot][lane][u].a;
-        EB = db.rec[slot][lane][u].b;
+        EA = db.ra[slot][u][lane];
+        EB = db.rb[slot][u][lane];
       }
       s[u].md = seg_d2(px[u], py, py - EA.y, EA, EB, s[u].bp, s[u].bcx, s[u].bcy);
       s[u].be = __float_as_int(EB.w);

@@ -78,6 +78,9 @@ def parse_args(argv=None):
                     help="band exchange of the config-3 step: peer-memory kernels or NCCL")
     ap.add_argument("--no-strong", action="store_true",
                     help="skip the config-3 strong-scaling step of the default workload")
+    ap.add_argument("--host-profile", action="store_true",
+                    help="config 2 on one GPU: host time per phase of the drop-in API step and "
+                         "its device kernels (torch profiler); one JSON line")
     ap.add_argument("--band", default=None, metavar="K/N",
                     help="config3 on one GPU: only band K of the N-way tile-row split, no "
                          "exchange and no SSIM (the per-band compute of an N-GPU step)")
@@ -781,28 +784,44 @@ class E2EStep:
         self.h2d_bytes = int(self.target_host.numel() * 4)
         self.d2h_bytes = 8
 
-    def __call__(self):
+    def __call__(self, marks=None):
+        """One step; with a list `marks`, appends (phase, time.perf_counter())
+        after each phase (host-time profile)."""
         import torch
 
         import manbo
+
+        def mark(label):
+            if marks is not None:
+                marks.append((label, time.perf_counter()))
+
+        mark("start")
         main = torch.cuda.current_stream()
         self.copy_stream.wait_stream(main)  # last step's readers of the target are done
         with torch.cuda.stream(self.copy_stream):
             self.target_dev.copy_(self.target_host, non_blocking=True)
         self.opt.zero_grad(set_to_none=not self.capturable)
         cn = self.ring[:, self.gidx, :].reshape(-1, 4, 2) / self.half - 1.0
+        mark("user prep (copy, zero_grad, gather)")
         out = manbo.ops.render_cubic_fill_splat_tilelang(
             cn, self.offs, self.colors, self.opac, self.depths, self.h, self.w, 16, 16, self.bg,
             fill_rules=self.rules, aa_widths=self.aa, distance_samples=self.s)
+        mark("render forward (API)")
         img = torch.clamp(out, 0, 1).permute(2, 0, 1).unsqueeze(0).contiguous()
         main.wait_stream(self.copy_stream)
+        mark("user clamp/permute")
         loss = manbo.mse_loss_tilelang(img, self.target_dev)
+        mark("mse (API)")
         with torch.no_grad():
             sv = manbo.ssim(img.detach(), self.target_dev)
+        mark("ssim (API)")
         loss.backward()
+        mark("backward (autograd + API backward)")
         self.opt.step()
+        mark("torch Adam")
         self.loss_host[0:1].copy_(loss.detach().view(1), non_blocking=True)
         self.loss_host[1:2].copy_(sv.view(1), non_blocking=True)
+        mark("loss read-back (enqueue)")
 
 
 def run_e2e(scene, dev, args, flush, stream, world):
@@ -852,6 +871,52 @@ def run_e2e(scene, dev, args, flush, stream, world):
                       "d2h_bytes_per_step": gstep.d2h_bytes,
                       "path": "the same API calls captured once into a CUDA graph by the "
                               "caller (torch Adam capturable), replayed every step"}}
+
+
+def run_host_profile(args):
+    """Where the drop-in API step's time goes (config 2, one GPU): host time
+    per phase of the eager E2EStep (synchronised at the end of every step,
+    the wait counted as its own phase), and the device kernels of the step
+    from the torch profiler (CUDA activity, averaged per step)."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+
+    from repo_b200 import scenes
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    step = E2EStep(scenes.config2(), dev)
+    for _ in range(max(E2E_MIN_WARMUP, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    phases, walls = {}, []
+    for _ in range(args.steps):
+        marks = []
+        step(marks)
+        torch.cuda.current_stream().synchronize()
+        marks.append(("wait for the device (sync)", time.perf_counter()))
+        for (_, a), (label, b) in zip(marks, marks[1:]):
+            phases[label] = phases.get(label, 0.0) + (b - a)
+        walls.append(marks[-1][1] - marks[0][1])
+    n = args.steps
+    host = {k: round(v / n * 1e6, 1) for k, v in phases.items()}
+    prof_steps = 20
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(prof_steps):
+            step()
+        torch.cuda.synchronize()
+    kernels = []
+    for ev in prof.key_averages():
+        t = getattr(ev, "device_time_total", None)
+        if t is None:
+            t = getattr(ev, "cuda_time_total", 0.0)
+        if t and t > 0:
+            kernels.append({"name": ev.key[:120], "calls_per_step": round(ev.count / prof_steps, 2),
+                            "us_per_step": round(t / prof_steps, 1)})
+    kernels.sort(key=lambda k: -k["us_per_step"])
+    return {"metric": "drop-in API step (config 2): host time per phase and device kernels",
+            "steps": n, "wall_us_per_step": round(statistics.mean(walls) * 1e6, 1),
+            "host_us_per_step": host, "device_kernels_per_step": kernels[:25],
+            "profiled_steps": prof_steps}
 
 
 # --------------------------------------------------------------------------
@@ -1013,6 +1078,11 @@ def main(argv=None):
         res = run_reference(args, rank, world)
         if res is not None:
             print(json.dumps(res), flush=True)
+        return 0
+    if args.host_profile:
+        if world > 1:
+            raise SystemExit("--host-profile runs on one GPU")
+        print(json.dumps(run_host_profile(args)), flush=True)
         return 0
     import torch
     import torch.distributed as dist

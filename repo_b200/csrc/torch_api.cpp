@@ -477,8 +477,8 @@ std::tuple<Tensor, Tensor, Tensor> raster_forward(const FrameP& f, const Tensor&
 }
 
 // One forward of the drop-in renderer: clamped widths and 1/sigma^2, binning,
-// staging and the forward raster, with one read-back of the counts at the end
-// (none under graph capture).  Returns (out, final_Ts, final_idx, frame,
+// staging and the forward raster, with one read-back of the counts between
+// the binning and the raster (none under graph capture).  Returns (out, final_Ts, final_idx, frame,
 // widths, inv_sigma2s).
 std::tuple<Tensor, Tensor, Tensor, FrameP, Tensor, Tensor> render_forward(
     const Tensor& cubics_norm, const Tensor& offs, const Tensor& colors, const Tensor& opac,
@@ -515,16 +515,17 @@ std::tuple<Tensor, Tensor, Tensor, FrameP, Tensor, Tensor> render_forward(
     raster_forward_into(*f, bg, h, w, OptT(), out, fts, fidx);
     return {out, fts, fidx, f, widths, inv_s2};
   }
+  // The counts are read back as soon as the binning is done, before the
+  // raster launch: the host waits for the binning only, and the raster then
+  // runs while the caller's next operations are enqueued.
   FrameP f = bin_attempt(in, c.isect, c.dlist, false);
-  raster_forward_into(*f, bg, h, w, OptT(), out, fts, fidx);
   int64_t n = 0, nd = 0;
   if (!finish_frame(*f, in, n, nd)) {  // outgrew the cached capacity: bin again
     f = bin_attempt(in, size_class(n), size_class(nd), false);
-    raster_forward_into(*f, bg, h, w, OptT(), out, fts, fidx);
     if (!finish_frame(*f, in, n, nd)) check(CS_ERR_CAPACITY, "cs_bin_count");
   }
+  raster_forward_into(*f, bg, h, w, OptT(), out, fts, fidx);  // (background only if n == 0)
   remember(in, n, nd);
-  if (n == 0) fill_background(bg, out, fts, fidx);
   return {out, fts, fidx, f, widths, inv_s2};
 }
 

@@ -453,6 +453,17 @@ def run_b200(args, rank, world, local_rank):
     return result, tr
 
 
+def parse_band(spec: str):
+    """`--band K/N` -> (K, N): band K (0-based) of an N-way split."""
+    try:
+        k, n = (int(v) for v in spec.split("/"))
+    except ValueError:
+        raise ValueError(f"--band {spec}: expected K/N, e.g. 3/8") from None
+    if n < 1 or not 0 <= k < n:
+        raise ValueError(f"--band {spec}: K must be in [0, N) and N >= 1")
+    return k, n
+
+
 def run_bands(args, rank, world, local_rank):
     """Config 3: one large image across the ranks in tile-row bands."""
     import torch
@@ -467,9 +478,7 @@ def run_bands(args, rank, world, local_rank):
     scene = scenes.config3()
     nb, bi = world, rank
     if args.band and world == 1 and args.workload == "config3":
-        bi, nb = (int(v) for v in args.band.split("/"))
-        if not 0 <= bi < nb:
-            raise ValueError(f"--band {args.band}: K must be in [0, N)")
+        bi, nb = parse_band(args.band)
     split = bands.balanced_bands(bands.tile_row_work(scene, dev), nb)
     band = split[bi]
     collective = "none"

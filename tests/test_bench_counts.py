@@ -4,6 +4,7 @@ import os
 import sys
 
 import numpy as np
+import pytest
 
 sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 import bench  # noqa: E402
@@ -80,3 +81,13 @@ def test_profile_summaries_hold_the_traffic_bench_reports():
         t = bench.ncu_traffic(kernel, summary)
         assert isinstance(t, int) and t > 0, (kernel, summary)
     assert bench.ncu_traffic("raster_backward_kernel", "no_such_summary.md") is None
+
+
+def test_band_option_parses_and_rejects_bad_specs():
+    assert bench.parse_band("3/8") == (3, 8)
+    assert bench.parse_band("0/1") == (0, 1)
+    for bad in ("8/8", "-1/4", "3", "a/b", "1/0"):
+        with pytest.raises(ValueError):
+            bench.parse_band(bad)
+    args = bench.parse_args(["--workload", "config3", "--band", "2/4", "--host-profile"])
+    assert args.band == "2/4" and args.host_profile

@@ -39,6 +39,26 @@ def _align(n: int, a: int = 256) -> int:
     return (int(n) + a - 1) // a * a
 
 
+def buffer_layout(world: int, n_grad: int, halo_shape: Sequence[int]) -> dict:
+    """Byte offsets of the regions of one rank's symmetric buffer (flags,
+    gradients of even and odd steps, halo rows), each 256-byte aligned, and
+    its total size; the same on every rank."""
+    halo_elems = 1
+    for v in halo_shape:
+        halo_elems *= int(v)
+    off = 0
+    flags = off
+    off += _align(2 * int(world) * 4)
+    grads = []
+    for _ in range(2):
+        grads.append(off)
+        off += _align(int(n_grad) * 4)
+    halo = off
+    off += _align(halo_elems * 4)
+    return {"flags": flags, "grads": grads, "halo": halo, "halo_elems": halo_elems,
+            "nbytes": off}
+
+
 class PeerGroup:
     """One symmetric buffer per rank of `group` (collective: every rank
     constructs it with the same sizes)."""
@@ -53,19 +73,12 @@ class PeerGroup:
         self.world = dist.get_world_size(group)
         self.n_grad = int(n_grad)
         self.halo_shape = tuple(int(v) for v in halo_shape)
-        halo_elems = 1
-        for v in self.halo_shape:
-            halo_elems *= v
-        off = 0
-        self.off_flags = off
-        off += _align(2 * self.world * 4)
-        self.off_grads = []
-        for _ in range(2):
-            self.off_grads.append(off)
-            off += _align(self.n_grad * 4)
-        self.off_halo = off
-        off += _align(halo_elems * 4)
-        self.nbytes = off
+        lay = buffer_layout(self.world, self.n_grad, self.halo_shape)
+        halo_elems = lay["halo_elems"]
+        self.off_flags = lay["flags"]
+        self.off_grads = list(lay["grads"])
+        self.off_halo = lay["halo"]
+        self.nbytes = lay["nbytes"]
         self.buf = symm_mem.empty(self.nbytes, dtype=torch.uint8, device=self.device)
         self.buf.zero_()
         torch.cuda.synchronize(self.device)
@@ -118,4 +131,4 @@ class PeerGroup:
                            self.ws.data_ptr(), nat.stream(self.device)), "cs_allreduce_adam")
 
 
-__all__ = ["PeerGroup", "FLAG_GRADS", "FLAG_HALO", "SPIN_LIMIT"]
+__all__ = ["PeerGroup", "buffer_layout", "FLAG_GRADS", "FLAG_HALO", "SPIN_LIMIT"]

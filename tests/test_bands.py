@@ -167,3 +167,15 @@ def test_allgather_halo_returns_the_next_ranks_rows():
     for r in range(world - 1):
         np.testing.assert_array_equal(got[r], np.full((3, 10, 7), float(r + 1)) + np.arange(7.0))
     assert got[world - 1] is None
+
+
+def test_peer_buffer_layout_is_aligned_and_disjoint():
+    from repo_b200.peer import buffer_layout
+    for world, n, halo in ((2, 5, (3, 10, 7)), (8, 1_000_003, (3, 10, 2040)), (1, 0, (3, 0, 5))):
+        lay = buffer_layout(world, n, halo)
+        starts = [lay["flags"], *lay["grads"], lay["halo"]]
+        sizes = [2 * world * 4, n * 4, n * 4, lay["halo_elems"] * 4]
+        assert all(s % 256 == 0 for s in starts)
+        for (a, sa), (b, _) in zip(zip(starts, sizes), zip(starts[1:], sizes[1:])):
+            assert a + sa <= b  # regions in order, no overlap
+        assert starts[-1] + sizes[-1] <= lay["nbytes"] and lay["nbytes"] % 256 == 0

@@ -462,6 +462,7 @@ __device__ __forceinline__ void fwd_entries(const DEntry* __restrict__ buf, int 
                                             FwdPix& p1) {
   const float2 P = make_float2(px0, px1), NP = make_float2(-px0, -px1);
   const float2 npy = make_float2(-py, -py);
+#pragma unroll 2  // two records' distance arithmetic in flight (same order of updates)
   for (int d = lo; d < hi; ++d) {
     const float4 EA = buf[d - c0].a;
     const float4 EB = buf[d - c0].b;

@@ -38,6 +38,11 @@ per point.
 --impl reference times the reference algorithm's CPU implementation (the C
 oracle restating manbo/ops/cubic_splatting.py, all host threads) on the same
 workload; the reference has no CPU renderer of its own.
+
+Diagnostics (one GPU): --workload config3 --band K/N runs band K of the
+N-way tile-row split alone (no exchange, no SSIM: the per-band compute of an
+N-GPU step); --host-profile splits the drop-in API step's host time by phase
+and lists its device kernels (torch profiler).
 """
 from __future__ import annotations
 

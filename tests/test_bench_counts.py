@@ -91,3 +91,18 @@ def test_band_option_parses_and_rejects_bad_specs():
             bench.parse_band(bad)
     args = bench.parse_args(["--workload", "config3", "--band", "2/4", "--host-profile"])
     assert args.band == "2/4" and args.host_profile
+
+
+def test_reference_arm_line_keeps_the_contract():
+    """The reference arm (the C oracle on the host) prints the repo arm's
+    metric, unit and workload with impl, cpu_baseline and a copy-free e2e."""
+    args = bench.parse_args(["--impl", "reference", "--steps", "1", "--warmup", "0"])
+    res = bench.run_reference(args, 0, 1)
+    assert res["impl"] == "reference" and res["metric"] == bench.METRIC
+    assert res["unit"] == bench.UNIT and res["higher_is_better"] is True
+    assert res["config"]["workload"] == bench.WORKLOAD_CONFIG2
+    assert res["value"] > 0 and res["steps"] == 1
+    assert res["cpu_baseline"]["value"] == res["value"] and res["cpu_baseline"]["cores"] >= 1
+    assert res["e2e"] == {"value": res["value"], "unit": bench.UNIT,
+                          "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+    assert bench.run_reference(args, 1, 2) is None  # other ranks exit without work
